@@ -1,0 +1,312 @@
+"""Benchmark of the B200 tpt-infer backend's hot path.
+
+Workload (one "step"): the W8A8 GEMM of the standalone sweep at M = 4096,
+K = N = 4096 -- int8 activations (per-tensor scale) x int8 per-output-channel
+weights (W^T [N, K]), i32 accumulate, fused f32 dequant + bias epilogue.
+Inputs are seeded synthetic tensors with the sweep's distributions (W ~
+N(0, 0.02) quantised per output channel, A ~ N(0, 1) quantised per tensor,
+bias ~ N(0, 0.01)). The sweep's other M (1, 16, 256) are reported under
+"sweep" with their own roofline fractions.
+
+Timing: W warm-up steps, then K timed steps; L2 (126 MB) is flushed by a
+256 MB write before every timed step and each step is bracketed by CUDA
+events on the launching stream. Multi-GPU (torchrun): every rank runs the
+same step on its own GPU with no collective (independent batches, weak
+scaling); the time is the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_HEAD, N, K = 4096, 4096, 4096
+SWEEP_M = (1, 16, 256, 4096)
+METRIC = "W8A8 GEMM throughput (M=4096, K=N=4096, int8 x int8 -> i32 -> f32 + bias)"
+UNIT = "TOP/s"
+
+
+def ops(m):
+    return 2.0 * m * N * K
+
+
+def alg_bytes(m):
+    # A int8 + W int8 + scales + bias (f32 each) + Y f32
+    return m * K + N * K + 8 * N + 4 * m * N
+
+
+def peaks():
+    p = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        src = "measured"
+    except OSError:
+        src = "fallback"
+    hbm = float(p.get("hbm_gbs", 6650.0))
+    bf16 = float(p.get("bf16_tflops", 1590.0))
+    # dense INT8 tensor rate is twice the dense bf16 rate on B200
+    return {"hbm_gbs": hbm, "int8_tops": 2.0 * bf16, "src": src}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(m, seed=1000):
+    from oracle import oracle as O  # seeded generators and reference quantizers (input preparation only)
+
+    w = O.normal(K * N, seed, 0.0, 0.02).reshape(K, N)
+    wq, ws = O.quantize_i8_symmetric_per_channel(np.ascontiguousarray(w.T), N)
+    x = O.normal(m * K, seed + 1, 0.0, 1.0)
+    aq, sa = O.quantize_i8_symmetric(x)
+    bias = O.normal(N, seed + 2, 0.0, 0.01)
+    return aq, float(sa), wq, ws, bias
+
+
+def cpu_reference(m, threads, budget_s, aq, sa, wq, ws, bias):
+    """Times the reference's own loop (ptq.rs:312-319, B [k, n] strided) with the
+    per-channel + bias epilogue over a bounded sample of output rows."""
+    from oracle import oracle as O
+
+    b_kn = np.ascontiguousarray(wq.reshape(N, K).T)
+    t0 = time.perf_counter()
+    O.w8a8_gemm_refloop(aq, b_kn, m, N, K, sa, ws, bias, max(1, threads), threads)
+    per_round = time.perf_counter() - t0  # one row per thread
+    rounds = max(1, int(budget_s / max(per_round, 1e-9)))
+    rows = min(m, rounds * max(1, threads))
+    t0 = time.perf_counter()
+    O.w8a8_gemm_refloop(aq, b_kn, m, N, K, sa, ws, bias, rows, threads)
+    dt = time.perf_counter() - t0
+    return rows, dt, 2.0 * rows * N * K / dt / 1e12
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    aq, sa, wq, ws, bias = make_inputs(M_HEAD)
+    for _ in range(args.warmup):
+        cpu_reference(M_HEAD, threads, 0.2, aq, sa, wq, ws, bias)
+    vals = [cpu_reference(M_HEAD, threads, args.ref_budget, aq, sa, wq, ws, bias) for _ in range(args.steps)]
+    v = float(np.median([x[2] for x in vals]))
+    rows = vals[-1][0]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": float(np.median([x[1] for x in vals]) * 1e3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "w8a8_gemm", "M": M_HEAD, "N": N, "K": K, "sample_rows": rows},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} of {M_HEAD} output rows per step, the reference loop order "
+                                   f"(ptq.rs:312-319) with per-channel scale + bias, {threads} OpenMP threads"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-budget", type=float, default=3.0, help="seconds of CPU work per reference step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    from tpt_infer_b200 import CudaBackend
+
+    stream = torch.cuda.Stream()
+    be = CudaBackend.new(local, stream)
+    assert be is not None, "no sm_100 device"
+    pk = peaks()
+
+    aq, sa, wq, ws, bias = make_inputs(M_HEAD)
+    w = be.upload_i8(wq, ws, N, K)
+    dev = f"cuda:{local}"
+    a_dev = torch.from_numpy(aq).to(dev)
+    bias_dev = torch.from_numpy(bias).to(dev)
+    y_dev = torch.empty(M_HEAD * N, dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def timed(m, steps, warm):
+        with torch.cuda.stream(stream):
+            for _ in range(warm):
+                be.w8a8_gemm_dev(a_dev, m, sa, w, bias_dev, 0, y_dev)
+            stream.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            l0 = be.launch_count()
+            for s, e in evs:
+                flush.zero_()
+                s.record(stream)
+                be.w8a8_gemm_dev(a_dev, m, sa, w, bias_dev, 0, y_dev)
+                e.record(stream)
+            stream.synchronize()
+            launches = be.launch_count() - l0
+        be.sync()
+        return [s.elapsed_time(e) for s, e in evs], launches
+
+    # the rest of the sweep (informative)
+    sweep = []
+    for m in SWEEP_M:
+        ts, _ = timed(m, max(5, args.steps // 2), 3)
+        t = float(np.median(ts)) * 1e-3
+        entry = {"M": m, "us": t * 1e6, "TOP/s": ops(m) / t / 1e12, "GB/s": alg_bytes(m) / t / 1e9,
+                 "bound": "tensor" if m >= 1024 else "hbm"}
+        entry["frac_int8_peak"] = entry["TOP/s"] / pk["int8_tops"]
+        entry["frac_hbm"] = entry["GB/s"] / pk["hbm_gbs"]
+        sweep.append(entry)
+
+    # headline timed region, with clock sampling
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        times, launches = timed(M_HEAD, args.steps, args.warmup)
+    torch.cuda.synchronize()
+    total_s = sum(times) * 1e-3
+    if world > 1:
+        t = torch.tensor([total_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_s = float(t.item())
+        dist.barrier()
+    per_step = total_s / args.steps
+    value = world * ops(M_HEAD) / per_step / 1e12
+    kernel_s = float(np.mean(times)) * 1e-3
+
+    # e2e through the public host-buffer API: H2D of A, GEMM, D2H of Y every step
+    a_pin = torch.from_numpy(aq).pin_memory()
+    y_pin = torch.empty(M_HEAD * N, dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        be.w8a8_gemm(a_pin.numpy(), M_HEAD, K, sa, w, bias, 0, out=y_pin.numpy())
+    e2e_steps = max(3, args.steps // 4)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        be.w8a8_gemm(a_pin.numpy(), M_HEAD, K, sa, w, bias, 0, out=y_pin.numpy())
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rows, dt, v = cpu_reference(M_HEAD, threads, 10.0, aq, sa, wq, ws, bias)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{rows} of {M_HEAD} output rows of the same GEMM, the reference loop order "
+                         f"(ptq.rs:312-319) with per-channel scale + bias, {threads} OpenMP threads, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "w8a8_gemm", "M": M_HEAD, "N": N, "K": K, "bias": True,
+                       "l2": "flushed (256 MB write) before every timed step",
+                       "parallelism": f"independent GEMM per GPU x{world}"},
+            "roofline": {"bound": "tensor", "achieved": ops(M_HEAD) / kernel_s / 1e12,
+                         "peak": pk["int8_tops"], "unit": "TOP/s",
+                         "frac": ops(M_HEAD) / kernel_s / 1e12 / pk["int8_tops"],
+                         "traffic": None,
+                         "peak_note": f"2 x {pk['src']} dense bf16 burst (INT8 dense rate = 2x bf16 on B200)"},
+            "e2e": {"value": world * ops(M_HEAD) / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": M_HEAD * K,
+                    "d2h_bytes_per_step": M_HEAD * N * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "sweep": sweep,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    w.free()
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,232 @@
+/*
+ * tpt_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for tpt-infer.
+ *
+ * This is the boundary a tpt-infer `CudaBackend` binds through `extern "C"`:
+ * plain pointers and sizes, no CUDA or torch types in any signature. Every
+ * entry point names the reference interface it replaces (paths relative to the
+ * tpt-infer repository root).
+ *
+ * Conventions
+ *  - Every function returns a tpt_status. Validation happens before any device
+ *    work and follows the reference's checks in the reference's order, so a
+ *    call the reference rejects is rejected here with the same OpError
+ *    variant (crates/tpt-infer-ops/src/backend.rs:6-20, 149-284).
+ *    TPT_SIZE_MISMATCH additionally records (expected, actual), readable with
+ *    tpt_cuda_last_size_mismatch().
+ *  - Functions without a `_dev` suffix take HOST buffers (the `&[f32]` slices
+ *    of the Backend trait), stage them to the device on the context's stream
+ *    and return after the result is back in host memory. Pinned host memory
+ *    makes the copies faster but is not required.
+ *  - `_dev` functions take DEVICE pointers, enqueue on the context's stream and
+ *    return without synchronising (tpt_cuda_ctx_sync waits).
+ *  - Calls on one context are serialised on its stream. One context per GPU;
+ *    use one host thread per context for several GPUs.
+ *  - There is no CPU fallback: an op the CUDA path lacks returns
+ *    TPT_UNSUPPORTED.
+ */
+#ifndef TPT_CUDA_H
+#define TPT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 1-4 mirror OpError (crates/tpt-infer-ops/src/backend.rs:6-20):
+ * SizeMismatch{expected, actual}, ShapeMismatch, Unsupported, Invalid. */
+typedef enum tpt_status {
+    TPT_OK = 0,
+    TPT_SIZE_MISMATCH = 1,
+    TPT_SHAPE_MISMATCH = 2,
+    TPT_UNSUPPORTED = 3,
+    TPT_INVALID = 4,
+    TPT_CUDA_ERROR = 5,   /* a CUDA runtime/driver call failed (message: tpt_cuda_last_error) */
+    TPT_OUT_OF_MEMORY = 6,/* device arena or allocation exhausted (TensorError::OutOfMemory) */
+    TPT_TIMEOUT = 7,      /* a bounded device-side wait ran out; the kernel returned early */
+    TPT_NCCL_ERROR = 8,
+    TPT_DEVICE_CHECK = 9  /* a kernel's own bounds/alignment check recorded a violation */
+} tpt_status;
+
+/* Epilogue activation (the Relu / Gelu nodes of exec.rs:416-445, fused). */
+typedef enum tpt_act { TPT_ACT_NONE = 0, TPT_ACT_RELU = 1, TPT_ACT_GELU = 2 } tpt_act;
+
+typedef struct tpt_cuda_ctx tpt_cuda_ctx;
+typedef struct tpt_cuda_weights tpt_cuda_weights;
+
+/* ------------------------------------------------------------------ */
+/* Context                                                             */
+/* ------------------------------------------------------------------ */
+
+/* Creates a context on `device`. `stream` is a cudaStream_t passed as void*;
+ * NULL makes the context create and own a non-blocking stream. Replaces the
+ * zero-sized CPU backends' construction and WebGpuBackend::new() -> Option
+ * (crates/tpt-infer-ops/src/webgpu.rs:272); a machine without a usable sm_100
+ * device yields TPT_UNSUPPORTED. */
+int tpt_cuda_ctx_create(int device, void *stream, tpt_cuda_ctx **out);
+int tpt_cuda_ctx_destroy(tpt_cuda_ctx *ctx);
+/* Waits for the context's stream; reports device-side error words
+ * (TPT_TIMEOUT / TPT_DEVICE_CHECK) raised by earlier _dev launches. */
+int tpt_cuda_ctx_sync(tpt_cuda_ctx *ctx);
+/* The context's stream (cudaStream_t as void*). */
+void *tpt_cuda_ctx_stream(tpt_cuda_ctx *ctx);
+int tpt_cuda_ctx_device(tpt_cuda_ctx *ctx);
+/* Backend::name (crates/tpt-infer-ops/src/backend.rs:100): "cuda". */
+const char *tpt_cuda_backend_name(void);
+const char *tpt_cuda_status_str(int status);
+/* Text of the last CUDA error on this context ("" if none). */
+const char *tpt_cuda_last_error(tpt_cuda_ctx *ctx);
+/* (expected, actual) of the last TPT_SIZE_MISMATCH on this context. */
+void tpt_cuda_last_size_mismatch(tpt_cuda_ctx *ctx, size_t *expected, size_t *actual);
+/* Number of kernels this library launched on the context since creation. */
+uint64_t tpt_cuda_ctx_launch_count(tpt_cuda_ctx *ctx);
+
+/* ------------------------------------------------------------------ */
+/* Backend trait, host slices (crates/tpt-infer-ops/src/backend.rs:98-147) */
+/* ------------------------------------------------------------------ */
+
+/* Backend::matmul (backend.rs:106-113): out[m,n] = a[m,k] @ b[kb,n], f32.
+ * Validation = validate_matmul (backend.rs:149-183). Each output is summed in
+ * increasing k with separately rounded multiply and add, bit-identical to
+ * naive.rs:13-33 / avx512.rs:55-78 (never TF32). */
+int tpt_cuda_matmul(tpt_cuda_ctx *ctx, const float *a, size_t a_len, size_t m, size_t k,
+                    const float *b, size_t b_len, size_t kb, size_t n, float *out, size_t out_len);
+/* Backend::conv2d (backend.rs:119-127): NCHW input, OIHW weight, groups 1,
+ * no bias; Conv2dOptions (backend.rs:49-58) passed as four sizes.
+ * Validation = validate_conv2d (backend.rs:219-284). */
+int tpt_cuda_conv2d(tpt_cuda_ctx *ctx, const float *input, size_t in_len, const size_t in_shape[4],
+                    const float *weight, size_t w_len, const size_t w_shape[4], float *out,
+                    size_t out_len, size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w);
+/* Backend::elementwise_add (backend.rs:130) */
+int tpt_cuda_elementwise_add(tpt_cuda_ctx *ctx, const float *a, size_t a_len, const float *b,
+                             size_t b_len, float *out, size_t out_len);
+/* Backend::relu (backend.rs:133) */
+int tpt_cuda_relu(tpt_cuda_ctx *ctx, const float *a, size_t a_len, float *out, size_t out_len);
+/* Backend::softmax (backend.rs:139), rows of row_len */
+int tpt_cuda_softmax(tpt_cuda_ctx *ctx, const float *a, size_t a_len, float *out, size_t out_len,
+                     size_t row_len);
+/* Backend::sigmoid (backend.rs:142) */
+int tpt_cuda_sigmoid(tpt_cuda_ctx *ctx, const float *a, size_t a_len, float *out, size_t out_len);
+/* Backend::gelu (backend.rs:146), tanh approximation of naive.rs:137-146 */
+int tpt_cuda_gelu(tpt_cuda_ctx *ctx, const float *a, size_t a_len, float *out, size_t out_len);
+
+/* Device-pointer forms of the same ops (validated shapes, async). */
+int tpt_cuda_matmul_dev(tpt_cuda_ctx *ctx, const float *a, size_t m, size_t k, const float *b,
+                        size_t n, float *out);
+int tpt_cuda_conv2d_dev(tpt_cuda_ctx *ctx, const float *input, const size_t in_shape[4],
+                        const float *weight, const size_t w_shape[4], float *out,
+                        size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w);
+int tpt_cuda_elementwise_add_dev(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t n);
+int tpt_cuda_relu_dev(tpt_cuda_ctx *ctx, const float *a, float *out, size_t n);
+int tpt_cuda_softmax_dev(tpt_cuda_ctx *ctx, const float *a, float *out, size_t n, size_t row_len);
+int tpt_cuda_sigmoid_dev(tpt_cuda_ctx *ctx, const float *a, float *out, size_t n);
+int tpt_cuda_gelu_dev(tpt_cuda_ctx *ctx, const float *a, float *out, size_t n);
+
+/* ------------------------------------------------------------------ */
+/* Quantization (crates/tpt-infer-quantize/src/{quant,dequant,ptq}.rs)  */
+/* ------------------------------------------------------------------ */
+
+/* quantize_i8_symmetric (quant.rs:25-40): per-tensor, scale = max|x|/127
+ * (1.0 for an all-zero tensor), q = clamp(round_half_away(x/scale), -127, 127).
+ * Bit-exact with the reference. */
+int tpt_cuda_quantize_i8_symmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q,
+                                   float *scale);
+/* quantize_i8_symmetric_per_channel (quant.rs:95-107): one scale per row of
+ * a [rows, len/rows] view. len % rows != 0 or rows == 0 -> TPT_INVALID (the
+ * reference asserts). */
+int tpt_cuda_quantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const float *x, size_t len,
+                                               size_t rows, int8_t *q, float *scales);
+/* quantize_i8_asymmetric (quant.rs:45-90) */
+int tpt_cuda_quantize_i8_asymmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q,
+                                    float *scale, int32_t *zero_point);
+/* pack_i4 (quant.rs:123-140): low nibble first; out holds ceil(n/2) bytes.
+ * A value outside [-8, 7] -> TPT_INVALID (the reference panics). */
+int tpt_cuda_pack_i4(tpt_cuda_ctx *ctx, const int8_t *values, size_t n, uint8_t *out);
+/* unpack_i4 (quant.rs:143-157): writes min(n, 2*packed_len) values,
+ * count returned in *written. */
+int tpt_cuda_unpack_i4(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len, size_t n,
+                       int8_t *out, size_t *written);
+/* quantize_i4_symmetric (quant.rs:171-186): scale = max|x|/7, q in [-7, 7]. */
+int tpt_cuda_quantize_i4_symmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, uint8_t *packed,
+                                   float *scale);
+/* quantize_i4_symmetric_per_channel (quant.rs:192-204): rows padded to
+ * ceil(cols/2) bytes. */
+int tpt_cuda_quantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const float *x, size_t len,
+                                               size_t rows, uint8_t *packed, float *scales);
+/* dequantize_i8_symmetric (dequant.rs:13-15) */
+int tpt_cuda_dequantize_i8_symmetric(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale,
+                                     float *out);
+/* dequantize_i8_symmetric_per_channel (dequant.rs:26-37) */
+int tpt_cuda_dequantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const int8_t *q, size_t n,
+                                                 const float *scales, size_t n_scales, float *out);
+/* dequantize_i4_symmetric_per_channel (dequant.rs:56-71); n_scales rows of
+ * row_elems values, rows ceil(row_elems/2) bytes apart. */
+int tpt_cuda_dequantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const uint8_t *packed,
+                                                 size_t packed_len, size_t row_elems,
+                                                 const float *scales, size_t n_scales, float *out);
+/* quantized_matmul_i8 (crates/tpt-infer-quantize/src/ptq.rs:293-324), the
+ * reference contract as is: B is [kb, n], per-tensor b_scales[0] (1.0 when
+ * n_scales == 0), out = (float)acc * (a_scale * b_scale). Mismatched k ->
+ * TPT_SHAPE_MISMATCH, mismatched buffer sizes -> TPT_SIZE_MISMATCH (the
+ * reference's Err(String) cases). i32 accumulation, bit-exact. */
+int tpt_cuda_quantized_matmul_i8(tpt_cuda_ctx *ctx, const int8_t *a, size_t a_len, size_t m,
+                                 size_t k, float a_scale, const int8_t *b, size_t b_len, size_t kb,
+                                 size_t n, const float *b_scales, size_t n_scales, float *out,
+                                 size_t out_len);
+
+/* Device-pointer forms used by the device-resident plans. */
+/* quantize_i8_symmetric on device buffers; the per-tensor max-abs reduction
+ * goes through a cell of context scratch. The scale lands in *scale_dev. */
+int tpt_cuda_quantize_i8_symmetric_dev(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q,
+                                       float *scale_dev);
+/* q = clamp(round(x / scale), -127, 127) with a known (calibrated) scale. */
+int tpt_cuda_quantize_i8_static_dev(tpt_cuda_ctx *ctx, const float *x, size_t n, float scale,
+                                    int8_t *q);
+
+/* ------------------------------------------------------------------ */
+/* Packed quantized weights, uploaded once                              */
+/* ------------------------------------------------------------------ */
+
+/* Uploads an INT8 per-output-channel weight: `wt` is W^T as [n, k] row-major
+ * int8 -- exactly the `packed` bytes of a QuantizedTensor produced by
+ * quantize_i8_symmetric_per_channel(W^T, rows = n) (quant.rs:95-107,
+ * ptq.rs:77-86) -- with n scales. k must be a multiple of 16. */
+int tpt_cuda_weights_upload_i8(tpt_cuda_ctx *ctx, const int8_t *wt, const float *scales,
+                               size_t n, size_t k, tpt_cuda_weights **out);
+/* Uploads an INT4 per-output-channel weight: `packed` holds n rows of
+ * k/2 bytes, low nibble first along k, exactly the bytes of
+ * quantize_i4_symmetric_per_channel(W^T, rows = n) (quant.rs:192-204);
+ * k must be a multiple of 32. */
+int tpt_cuda_weights_upload_i4(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len,
+                               const float *scales, size_t n, size_t k, tpt_cuda_weights **out);
+int tpt_cuda_weights_free(tpt_cuda_weights *w);
+/* Shape of an uploaded weight (n output channels, k inputs). */
+int tpt_cuda_weights_shape(const tpt_cuda_weights *w, size_t *n, size_t *k);
+
+/* W8A8 GEMM with per-output-channel weights: the per-channel extension of
+ * quantized_matmul_i8 (ptq.rs:293-324). acc[m,n] = sum_k a[m,k]*wt[n,k] in
+ * i32, then y = (float)acc * (a_scale * w_scale[n]) + bias[n] (two roundings,
+ * no FMA; bias may be NULL), then `act`. Host buffers: a is [m, k] int8,
+ * out is [m, n] f32. */
+int tpt_cuda_w8a8_gemm(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, float a_scale,
+                       const tpt_cuda_weights *w, const float *bias, int act, float *out);
+/* Same on device pointers (async). */
+int tpt_cuda_w8a8_gemm_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, float a_scale,
+                           const tpt_cuda_weights *w, const float *bias, int act, float *out);
+/* Same, writing the raw i32 accumulators instead (bit-exactness checks). */
+int tpt_cuda_w8a8_gemm_acc_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m,
+                               const tpt_cuda_weights *w, int32_t *acc);
+
+/* W4 GEMM, f32 activations: y = x @ dequant(W4)^T + bias, then act -- the
+ * reference semantics of dequantize_i4_symmetric_per_channel (dequant.rs:56-71)
+ * followed by the f32 matmul. Host buffers x [m, k], out [m, n]. */
+int tpt_cuda_w4_gemm(tpt_cuda_ctx *ctx, const float *x, size_t m, size_t k,
+                     const tpt_cuda_weights *w, const float *bias, int act, float *out);
+int tpt_cuda_w4_gemm_dev(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w,
+                         const float *bias, int act, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPT_CUDA_H */

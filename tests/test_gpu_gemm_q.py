@@ -1,0 +1,156 @@
+"""GPU parity of the quantized GEMMs against the oracle.
+
+W8A8: the i32 accumulators are bit-exact, and so is the f32 output
+y = (float)acc * (a_scale * w_scale[n]) + bias[n] (two roundings, no FMA, in
+the oracle's order). Shapes cover the W8A8 sweep (M in {1, 16, 256, 4096},
+K = N = 4096) plus ragged ones; at M = 4096 the oracle checks a sample of rows.
+
+W4: the reference computes dequant -> f32 matmul; the device factors the
+channel scale out of the sum, so outputs match to rounding. Tolerance, per
+the spec: max-abs error <= 1e-3 x output scale, with the output scale read
+strictly as the symmetric INT8 quantisation step of the output,
+max|y| / 127.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def w8a8_case(m, n, k, seed=100, with_bias=True):
+    w = O.normal(k * n, seed, 0.0, 0.02).reshape(k, n)          # W [K, N]
+    wt = np.ascontiguousarray(w.T)                              # W^T [N, K]
+    wq, ws = O.quantize_i8_symmetric_per_channel(wt, n)          # per output channel
+    x = O.normal(m * k, seed + 1, 0.0, 1.0)
+    aq, sa = O.quantize_i8_symmetric(x)                          # per tensor
+    bias = O.normal(n, seed + 2, 0.0, 0.01) if with_bias else None
+    return aq, sa, wq, ws, bias
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (16, 4096, 4096), (256, 4096, 4096),
+                                   (3, 100, 48), (9, 33, 16), (130, 200, 64), (1, 10, 512),
+                                   (128, 256, 128), (300, 512, 256), (1000, 768, 768)])
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_w8a8_bit_exact(cuda, m, n, k, act):
+    if act and m * n * k > 1 << 26:
+        pytest.skip("activations covered at the smaller shapes")
+    aq, sa, wq, ws, bias = w8a8_case(m, n, k)
+    w = cuda.upload_i8(wq, ws, n, k)
+    y = cuda.w8a8_gemm(aq, m, k, sa, w, bias, act)
+    want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, act, threads=8)
+    if act == 2:  # CUDA tanhf vs libm tanhf: a few ulp
+        assert np.max(np.abs(y - want) / (1 + np.abs(want))) < 1e-6
+    else:
+        assert np.array_equal(y, want)
+    w.free()
+
+
+@pytest.mark.parametrize("m", [1, 16, 256, 4096])
+def test_w8a8_accumulators_bit_exact(cuda, m):
+    import torch
+
+    n = k = 4096
+    aq, sa, wq, ws, _ = w8a8_case(m, n, k, seed=200)
+    w = cuda.upload_i8(wq, ws, n, k)
+    a_dev = torch.from_numpy(aq).cuda()
+    acc = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    cuda.w8a8_gemm_acc_dev(a_dev, m, w, acc)
+    cuda.sync()
+    got = acc.cpu().numpy().reshape(m, n)
+    rows = np.unique(np.concatenate([[0, m - 1], np.random.default_rng(m).integers(0, m, 48)]))
+    want = O.i8_gemm_acc(aq.reshape(m, k)[rows].ravel(), wq, rows.size, n, k, threads=8).reshape(rows.size, n)
+    assert np.array_equal(got[rows], want)
+    w.free()
+
+
+def test_w8a8_full_m4096_sampled_rows(cuda):
+    m = n = k = 4096
+    aq, sa, wq, ws, bias = w8a8_case(m, n, k, seed=300)
+    w = cuda.upload_i8(wq, ws, n, k)
+    y = cuda.w8a8_gemm(aq, m, k, sa, w, bias, 0).reshape(m, n)
+    rows = np.unique(np.concatenate([[0, 127, 128, m - 1], np.random.default_rng(7).integers(0, m, 40)]))
+    want = O.w8a8_gemm(aq.reshape(m, k)[rows].ravel(), wq, rows.size, n, k, sa, ws, bias, 0,
+                       threads=8).reshape(rows.size, n)
+    assert np.array_equal(y[rows], want)
+    w.free()
+
+
+@pytest.mark.parametrize("m,k,n", [(4, 8, 4), (3, 17, 5), (64, 784, 10), (33, 100, 257)])
+def test_quantized_matmul_i8_reference_contract(cuda, m, k, n):
+    # ptq.rs:293-324 as is: B [k, n], per-tensor scale, no bias
+    a, b = O.lcg_sym(m * k, 301), O.lcg_sym(k * n, 302)
+    aq, sa = O.quantize_i8_symmetric(a)
+    bq, sb = O.quantize_i8_symmetric(b)
+    out = np.empty(m * n, np.float32)
+    cuda.quantized_matmul_i8(aq, (m, k), sa, bq, (k, n), [sb], out)
+    assert np.array_equal(out, O.quantized_matmul_i8(aq, (m, k), sa, bq, (k, n), [sb]))
+
+
+def test_quantized_matmul_i8_kat_and_errors(cuda):
+    from tpt_infer_b200 import OpError
+
+    # ptq.rs:409-436
+    m, k, n = 4, 8, 4
+    a = (np.sin(np.arange(m * k, dtype=np.float32)) * np.float32(0.5)).astype(np.float32)
+    b = (np.cos(np.arange(k * n, dtype=np.float32)) * np.float32(0.5)).astype(np.float32)
+    ref = O.matmul_naive(a, (m, k), b, (k, n))
+    aq, sa = cuda.quantize_i8_symmetric(a)
+    bq, sb = cuda.quantize_i8_symmetric(b)
+    out = np.empty(m * n, np.float32)
+    cuda.quantized_matmul_i8(aq, (m, k), sa, bq, (k, n), [sb], out)
+    assert np.all(np.abs(ref - out) < 0.05)
+    with pytest.raises(OpError) as e:
+        cuda.quantized_matmul_i8(aq, (m, k), sa, bq, (k + 1, n), [sb], out)
+    assert e.value.kind == "ShapeMismatch"
+    with pytest.raises(OpError) as e:
+        cuda.quantized_matmul_i8(aq[:-1], (m, k), sa, bq, (k, n), [sb], out)
+    assert e.value.kind == "SizeMismatch"
+
+
+def w4_case(m, n, k, seed=400):
+    w = O.normal(k * n, seed, 0.0, 0.02).reshape(k, n)
+    wt = np.ascontiguousarray(w.T)
+    p, s = O.quantize_i4_symmetric_per_channel(wt, n)
+    x = O.normal(m * k, seed + 1, 0.0, 1.0)
+    return x, p, s
+
+
+def w4_tol(want):
+    return 1e-3 * (np.max(np.abs(want)) / 127.0)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 11008, 4096), (2, 100, 64),
+                                   (5, 40, 96), (1, 8, 32)])
+def test_w4_gemm(cuda, m, n, k):
+    x, p, s = w4_case(m, n, k)
+    w = cuda.upload_i4(p, s, n, k)
+    y = cuda.w4_gemm(x, m, k, w)
+    want = O.w4_gemm(x, p, s, m, n, k, threads=8)
+    assert np.max(np.abs(y - want)) <= w4_tol(want)
+    w.free()
+
+
+def test_w4_gemm_m512_sampled(cuda):
+    m, n, k = 512, 11008, 4096
+    x, p, s = w4_case(m, n, k, seed=500)
+    w = cuda.upload_i4(p, s, n, k)
+    y = cuda.w4_gemm(x, m, k, w).reshape(m, n)
+    rows = np.unique(np.concatenate([[0, m - 1], np.random.default_rng(3).integers(0, m, 14)]))
+    want = O.w4_gemm(x.reshape(m, k)[rows].ravel(), p, s, rows.size, n, k, threads=8).reshape(rows.size, n)
+    assert np.max(np.abs(y[rows] - want)) <= w4_tol(want)
+    w.free()
+
+
+@pytest.mark.parametrize("act", [1, 2])
+def test_w4_bias_act(cuda, act):
+    m, n, k = 3, 64, 128
+    x, p, s = w4_case(m, n, k, seed=600)
+    bias = O.normal(n, 601, 0.0, 0.01)
+    w = cuda.upload_i4(p, s, n, k)
+    y = cuda.w4_gemm(x, m, k, w, bias, act)
+    want = O.w4_gemm(x, p, s, m, n, k, bias, act)
+    assert np.max(np.abs(y - want)) <= max(w4_tol(want), 1e-6)
+    w.free()

@@ -1,0 +1,81 @@
+"""ctypes binding of ``libtpt_cuda.so`` (declarations: include/tpt_cuda.h).
+
+The library is loaded from this package directory only. If it is missing the
+import fails loudly: there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libtpt_cuda.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is not built; run `python tpt_infer_b200/build.py` (the CUDA backend has no CPU fallback)")
+
+lib = C.CDLL(LIB_PATH)
+
+vp = C.c_void_p
+sz = C.c_size_t
+f32p = C.POINTER(C.c_float)
+i32p = C.POINTER(C.c_int32)
+szp = C.POINTER(C.c_size_t)
+ctxp = vp
+wp = vp
+
+# name -> (restype, argtypes); every symbol the header declares
+SIGNATURES = {
+    "tpt_cuda_ctx_create": (C.c_int, [C.c_int, vp, C.POINTER(vp)]),
+    "tpt_cuda_ctx_destroy": (C.c_int, [ctxp]),
+    "tpt_cuda_ctx_sync": (C.c_int, [ctxp]),
+    "tpt_cuda_ctx_stream": (vp, [ctxp]),
+    "tpt_cuda_ctx_device": (C.c_int, [ctxp]),
+    "tpt_cuda_backend_name": (C.c_char_p, []),
+    "tpt_cuda_status_str": (C.c_char_p, [C.c_int]),
+    "tpt_cuda_last_error": (C.c_char_p, [ctxp]),
+    "tpt_cuda_last_size_mismatch": (None, [ctxp, szp, szp]),
+    "tpt_cuda_ctx_launch_count": (C.c_uint64, [ctxp]),
+    "tpt_cuda_matmul": (C.c_int, [ctxp, vp, sz, sz, sz, vp, sz, sz, sz, vp, sz]),
+    "tpt_cuda_conv2d": (C.c_int, [ctxp, vp, sz, szp, vp, sz, szp, vp, sz, sz, sz, sz, sz]),
+    "tpt_cuda_elementwise_add": (C.c_int, [ctxp, vp, sz, vp, sz, vp, sz]),
+    "tpt_cuda_relu": (C.c_int, [ctxp, vp, sz, vp, sz]),
+    "tpt_cuda_softmax": (C.c_int, [ctxp, vp, sz, vp, sz, sz]),
+    "tpt_cuda_sigmoid": (C.c_int, [ctxp, vp, sz, vp, sz]),
+    "tpt_cuda_gelu": (C.c_int, [ctxp, vp, sz, vp, sz]),
+    "tpt_cuda_matmul_dev": (C.c_int, [ctxp, vp, sz, sz, vp, sz, vp]),
+    "tpt_cuda_conv2d_dev": (C.c_int, [ctxp, vp, szp, vp, szp, vp, sz, sz, sz, sz]),
+    "tpt_cuda_elementwise_add_dev": (C.c_int, [ctxp, vp, vp, vp, sz]),
+    "tpt_cuda_relu_dev": (C.c_int, [ctxp, vp, vp, sz]),
+    "tpt_cuda_softmax_dev": (C.c_int, [ctxp, vp, vp, sz, sz]),
+    "tpt_cuda_sigmoid_dev": (C.c_int, [ctxp, vp, vp, sz]),
+    "tpt_cuda_gelu_dev": (C.c_int, [ctxp, vp, vp, sz]),
+    "tpt_cuda_quantize_i8_symmetric": (C.c_int, [ctxp, vp, sz, vp, f32p]),
+    "tpt_cuda_quantize_i8_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, sz, vp, vp]),
+    "tpt_cuda_quantize_i8_asymmetric": (C.c_int, [ctxp, vp, sz, vp, f32p, i32p]),
+    "tpt_cuda_pack_i4": (C.c_int, [ctxp, vp, sz, vp]),
+    "tpt_cuda_unpack_i4": (C.c_int, [ctxp, vp, sz, sz, vp, szp]),
+    "tpt_cuda_quantize_i4_symmetric": (C.c_int, [ctxp, vp, sz, vp, f32p]),
+    "tpt_cuda_quantize_i4_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, sz, vp, vp]),
+    "tpt_cuda_dequantize_i8_symmetric": (C.c_int, [ctxp, vp, sz, C.c_float, vp]),
+    "tpt_cuda_dequantize_i8_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, vp, sz, vp]),
+    "tpt_cuda_dequantize_i4_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, sz, vp, sz, vp]),
+    "tpt_cuda_quantized_matmul_i8": (C.c_int, [ctxp, vp, sz, sz, sz, C.c_float, vp, sz, sz, sz, vp, sz, vp, sz]),
+    "tpt_cuda_quantize_i8_symmetric_dev": (C.c_int, [ctxp, vp, sz, vp, vp]),
+    "tpt_cuda_quantize_i8_static_dev": (C.c_int, [ctxp, vp, sz, C.c_float, vp]),
+    "tpt_cuda_weights_upload_i8": (C.c_int, [ctxp, vp, vp, sz, sz, C.POINTER(vp)]),
+    "tpt_cuda_weights_upload_i4": (C.c_int, [ctxp, vp, sz, vp, sz, sz, C.POINTER(vp)]),
+    "tpt_cuda_weights_free": (C.c_int, [wp]),
+    "tpt_cuda_weights_shape": (C.c_int, [wp, szp, szp]),
+    "tpt_cuda_w8a8_gemm": (C.c_int, [ctxp, vp, sz, sz, C.c_float, wp, vp, C.c_int, vp]),
+    "tpt_cuda_w8a8_gemm_dev": (C.c_int, [ctxp, vp, sz, C.c_float, wp, vp, C.c_int, vp]),
+    "tpt_cuda_w8a8_gemm_acc_dev": (C.c_int, [ctxp, vp, sz, wp, vp]),
+    "tpt_cuda_w4_gemm": (C.c_int, [ctxp, vp, sz, sz, wp, vp, C.c_int, vp]),
+    "tpt_cuda_w4_gemm_dev": (C.c_int, [ctxp, vp, sz, wp, vp, C.c_int, vp]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args

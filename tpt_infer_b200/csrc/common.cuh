@@ -1,0 +1,158 @@
+// common.cuh -- shared host/device plumbing of the tpt-infer B200 backend.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include <string>
+
+#include "../../include/tpt_cuda.h"
+
+// Device-side error words (one 32-bit word each), written by kernels whose
+// bounded waits ran out or whose own index checks failed. Read and cleared by
+// tpt_cuda_ctx_sync / the host-staged entry points.
+enum { TPT_FLAG_TIMEOUT = 0, TPT_FLAG_CHECK = 1, TPT_FLAG_WORDS = 4 };
+
+struct tpt_cuda_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    int sm_count = 0;
+    // growable device scratch used by host-staged calls and split reductions
+    char *scratch = nullptr;
+    size_t scratch_cap = 0;
+    // small persistent device words: error flags + reduction cells
+    unsigned *d_flags = nullptr;   // TPT_FLAG_WORDS words
+    unsigned *d_reduce = nullptr;  // 64 words of reduction scratch
+    size_t last_expected = 0, last_actual = 0;
+    std::string last_error;
+    uint64_t launches = 0;
+};
+
+struct tpt_cuda_weights {
+    tpt_cuda_ctx *ctx = nullptr;
+    int kind = 0;          // 8 = int8 [n,k]; 4 = int4 nibbles [n, k/2]
+    size_t n = 0, k = 0;
+    void *data = nullptr;  // device: packed weight bytes
+    float *scales = nullptr;  // device: n per-channel scales
+    size_t bytes = 0;
+    // TMA descriptor of the int8 weight (CUtensorMap, 128 bytes), built once
+    alignas(64) unsigned char tmap[128];
+    bool tmap_ok = false;
+};
+
+namespace tpt {
+
+int set_size_mismatch(tpt_cuda_ctx *ctx, size_t expected, size_t actual);
+int cuda_fail(tpt_cuda_ctx *ctx, cudaError_t e, const char *what);
+// Ensures the context scratch holds at least `bytes` (grows; never shrinks).
+int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes);
+// Waits for the stream, then reads and clears the device error words.
+int sync_and_check(tpt_cuda_ctx *ctx);
+// Returns TPT_CUDA_ERROR if the last launch failed, else TPT_OK; counts launches.
+int after_launch(tpt_cuda_ctx *ctx, const char *what, int n = 1);
+
+// Bump allocator over the context scratch for one host-staged call.
+struct Staging {
+    tpt_cuda_ctx *ctx;
+    size_t need = 0;
+    size_t off = 0;
+    explicit Staging(tpt_cuda_ctx *c) : ctx(c) {}
+    static size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+    // First pass: reserve sizes; second pass: hand out pointers.
+    void reserve(size_t bytes) { need += align_up(bytes); }
+    int commit() { return ensure_scratch(ctx, need); }
+    template <typename T> T *take(size_t count) {
+        T *p = reinterpret_cast<T *>(ctx->scratch + off);
+        off += align_up(count * sizeof(T));
+        return p;
+    }
+};
+
+int h2d(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+int d2h(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes);
+
+inline unsigned grid_1d(size_t n, unsigned block, unsigned cap = 148u * 16u) {
+    size_t g = (n + block - 1) / block;
+    if (g == 0) g = 1;
+    if (g > cap) g = cap;
+    return (unsigned)g;
+}
+
+bool checked_mul(size_t a, size_t b, size_t *r);
+
+// ---- launchers implemented across the .cu files (device pointers, async) ----
+int launch_add(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t n);
+int launch_unary(tpt_cuda_ctx *ctx, int op, const float *a, float *out, size_t n);  // 1 relu 2 sigmoid 3 gelu
+int launch_softmax(tpt_cuda_ctx *ctx, const float *a, float *out, size_t rows, size_t row_len);
+int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m,
+                      size_t k, size_t n);
+int launch_conv2d_f32(tpt_cuda_ctx *ctx, const float *in, const float *w, float *out, const size_t is[4],
+                      const size_t ws[4], size_t oh, size_t ow, size_t sh, size_t sw, size_t ph,
+                      size_t pw);
+int launch_quant_i8_sym(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, float *scale_dev,
+                        unsigned *cell);
+int launch_quant_i8_static(tpt_cuda_ctx *ctx, const float *x, size_t n, float scale, int8_t *q);
+int launch_quant_i8_rows(tpt_cuda_ctx *ctx, const float *x, size_t rows, size_t cols, int8_t *q,
+                         float *scales);
+int launch_quant_i8_asym(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, float *scale_dev,
+                         int32_t *zp_dev, unsigned *cells);
+int launch_pack_i4(tpt_cuda_ctx *ctx, const int8_t *v, size_t n, uint8_t *out, unsigned *bad);
+int launch_unpack_i4(tpt_cuda_ctx *ctx, const uint8_t *p, size_t count, int8_t *out);
+int launch_quant_i4_rows(tpt_cuda_ctx *ctx, const float *x, size_t rows, size_t cols, uint8_t *p,
+                         float *scales);
+int launch_dequant_i8_rows(tpt_cuda_ctx *ctx, const int8_t *q, size_t rows, size_t cols,
+                           const float *scales, float *out);
+int launch_dequant_i4_rows(tpt_cuda_ctx *ctx, const uint8_t *p, size_t rows, size_t row_elems,
+                           size_t packed_len, const float *scales, float *out);
+// i8 GEMM: y[m,n] (+bias, act) or raw i32 acc when acc != nullptr; W^T [n,k].
+int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w,
+                float a_scale, const float *bias, int act, float *y, int32_t *acc);
+int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w,
+              const float *bias, int act, float *y);
+
+}  // namespace tpt
+
+// ------------------------------------------------------------------ device helpers
+#ifdef __CUDACC__
+namespace tpt {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// GELU of crates/tpt-infer-ops/src/naive.rs:137-146, evaluated with explicit
+// round-to-nearest multiplies/adds in the reference's association order
+// (nvcc would otherwise contract them into FMAs).
+__device__ __forceinline__ float gelu_ref(float x) {
+    const float K = 0.7978846f, Cc = 0.044715f;
+    float cx = __fmul_rn(__fmul_rn(__fmul_rn(Cc, x), x), x);
+    float inner = __fmul_rn(K, __fadd_rn(x, cx));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ float apply_act(float y, int act) {
+    if (act == TPT_ACT_RELU) return y > 0.0f ? y : 0.0f;
+    if (act == TPT_ACT_GELU) return gelu_ref(y);
+    return y;
+}
+
+// Rust `f32::round(v).clamp(lo, hi) as i8`: half away from zero (roundf),
+// NaN -> 0 (saturating cast).
+__device__ __forceinline__ int8_t round_clamp_i8(float v, float lo, float hi) {
+    v = roundf(v);
+    if (isnan(v)) return 0;
+    v = fminf(fmaxf(v, lo), hi);
+    return (int8_t)(int)v;
+}
+
+}  // namespace tpt
+#endif

@@ -1,0 +1,604 @@
+// w8a8.cu -- INT8 weight x INT8 activation GEMMs with i32 accumulation and the
+// fused per-output-channel dequant epilogue: the per-channel extension of
+// quantized_matmul_i8 (crates/tpt-infer-quantize/src/ptq.rs:293-324),
+//   y[m,n] = (float)acc[m,n] * (a_scale * w_scale[n]) + bias[n], then act,
+// with the scale product formed first, and round-to-nearest multiply and add
+// kept separate (no FMA) so the f32 output is bit-exact with the oracle.
+//
+// Kernels here:
+//  - k_w8a8_gemv: small M (<= 8). One warp per output channel streams the
+//    K-contiguous weight row with 128-bit loads and dp4a; HBM-bound by design.
+//  - k_w8a8_simt: general shapes (ragged M/N, K % 16 == 0); dp4a tiles.
+//  - the tcgen05 tensor-core kernel for large M lives in w8a8_tc.cu.
+// Weight layout in HBM: W^T [n, k] int8 row-major (K-major B operand), which
+// is the byte layout quantize_i8_symmetric_per_channel(W^T, rows = n) emits.
+#include <string.h>
+
+#include <new>
+
+#include "common.cuh"
+
+namespace tpt {
+
+int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled);
+int build_weight_tmap(tpt_cuda_weights *w);
+
+namespace {
+
+__device__ __forceinline__ float w8a8_epilogue(int32_t acc, float a_scale, float ws, const float *bias, int n,
+                                               int act) {
+    float y = __fmul_rn((float)acc, __fmul_rn(a_scale, ws));
+    if (bias) y = __fadd_rn(y, __ldg(bias + n));
+    return apply_act(y, act);
+}
+
+__device__ __forceinline__ int dot16(int4 a, int4 b, int acc) {
+    acc = __dp4a(a.x, b.x, acc);
+    acc = __dp4a(a.y, b.y, acc);
+    acc = __dp4a(a.z, b.z, acc);
+    acc = __dp4a(a.w, b.w, acc);
+    return acc;
+}
+
+template <int MM>
+__global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
+                                                   const float *__restrict__ wscale, const float *__restrict__ bias,
+                                                   int M, int N, int K, float a_scale, int act,
+                                                   float *__restrict__ Y, int32_t *__restrict__ ACC) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int chunks = K >> 4;  // 16-byte chunks per row
+    for (int n = warp; n < N; n += nwarps) {
+        const int4 *wrow = reinterpret_cast<const int4 *>(Wt + (size_t)n * K);
+        int acc[MM];
+#pragma unroll
+        for (int i = 0; i < MM; i++) acc[i] = 0;
+        int c = lane;
+        for (; c + 96 < chunks; c += 128) {
+            int4 w0 = __ldcs(wrow + c), w1 = __ldcs(wrow + c + 32), w2 = __ldcs(wrow + c + 64),
+                 w3 = __ldcs(wrow + c + 96);
+#pragma unroll
+            for (int i = 0; i < MM; i++) {
+                if (i < M) {
+                    const int4 *arow = reinterpret_cast<const int4 *>(A + (size_t)i * K);
+                    acc[i] = dot16(__ldg(arow + c), w0, acc[i]);
+                    acc[i] = dot16(__ldg(arow + c + 32), w1, acc[i]);
+                    acc[i] = dot16(__ldg(arow + c + 64), w2, acc[i]);
+                    acc[i] = dot16(__ldg(arow + c + 96), w3, acc[i]);
+                }
+            }
+        }
+        for (; c < chunks; c += 32) {
+            int4 w0 = __ldcs(wrow + c);
+#pragma unroll
+            for (int i = 0; i < MM; i++)
+                if (i < M) acc[i] = dot16(__ldg(reinterpret_cast<const int4 *>(A + (size_t)i * K) + c), w0, acc[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < MM; i++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+        }
+        if (lane == 0) {
+            const float ws = __ldg(wscale + n);
+#pragma unroll
+            for (int i = 0; i < MM; i++) {
+                if (i < M) {
+                    if (ACC)
+                        ACC[(size_t)i * N + n] = acc[i];
+                    else
+                        Y[(size_t)i * N + n] = w8a8_epilogue(acc[i], a_scale, ws, bias, n, act);
+                }
+            }
+        }
+    }
+}
+
+// General dp4a tile GEMM: 128x128 outputs per CTA, 8x8 per thread, K in
+// 32-byte slices (K % 16 == 0; a trailing 16-byte half is zero-filled).
+__global__ void __launch_bounds__(256) k_w8a8_simt(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
+                                                   const float *__restrict__ wscale, const float *__restrict__ bias,
+                                                   int M, int N, int K, float a_scale, int act,
+                                                   float *__restrict__ Y, int32_t *__restrict__ ACC) {
+    __shared__ __align__(16) int As[2][8][128 + 4];
+    __shared__ __align__(16) int Bs[2][8][128 + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * 128, n0 = blockIdx.x * 128;
+    const int lr = tid >> 1, lh = tid & 1;  // loader: row lr, 16-byte half lh
+    int4 ra, rb;
+    auto load = [&](int k0) {
+        int kk = k0 + lh * 16;
+        ra = make_int4(0, 0, 0, 0);
+        rb = make_int4(0, 0, 0, 0);
+        if (m0 + lr < M && kk < K) ra = __ldg(reinterpret_cast<const int4 *>(A + (size_t)(m0 + lr) * K + kk));
+        if (n0 + lr < N && kk < K) rb = __ldg(reinterpret_cast<const int4 *>(Wt + (size_t)(n0 + lr) * K + kk));
+    };
+    auto store = [&](int buf) {
+        As[buf][lh * 4 + 0][lr] = ra.x;
+        As[buf][lh * 4 + 1][lr] = ra.y;
+        As[buf][lh * 4 + 2][lr] = ra.z;
+        As[buf][lh * 4 + 3][lr] = ra.w;
+        Bs[buf][lh * 4 + 0][lr] = rb.x;
+        Bs[buf][lh * 4 + 1][lr] = rb.y;
+        Bs[buf][lh * 4 + 2][lr] = rb.z;
+        Bs[buf][lh * 4 + 3][lr] = rb.w;
+    };
+    int acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0;
+    const int kt = (K + 31) / 32;
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int t = 0; t < kt; t++) {
+        const int buf = t & 1;
+        if (t + 1 < kt) load((t + 1) * 32);
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            int av[8], bv[8];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                av[i] = As[buf][w][ty * 4 + i];
+                av[4 + i] = As[buf][w][64 + ty * 4 + i];
+                bv[i] = Bs[buf][w][tx * 4 + i];
+                bv[4 + i] = Bs[buf][w][64 + tx * 4 + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = __dp4a(av[i], bv[j], acc[i][j]);
+        }
+        if (t + 1 < kt) store(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+            if (n >= N) continue;
+            if (ACC)
+                ACC[(size_t)m * N + n] = acc[i][j];
+            else
+                Y[(size_t)m * N + n] = w8a8_epilogue(acc[i][j], a_scale, __ldg(wscale + n), bias, n, act);
+        }
+    }
+}
+
+// [R, C] -> [C, R] byte transpose through 32x32 shared tiles.
+__global__ void k_transpose_i8(const int8_t *__restrict__ src, int8_t *__restrict__ dst, int R, int Ccols) {
+    __shared__ int8_t tile[32][33];
+    int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * 32 + threadIdx.y;
+    for (int j = 0; j < 32; j += 8)
+        if (x < Ccols && y + j < R) tile[threadIdx.y + j][threadIdx.x] = src[(size_t)(y + j) * Ccols + x];
+    __syncthreads();
+    x = blockIdx.y * 32 + threadIdx.x;
+    y = blockIdx.x * 32 + threadIdx.y;
+    for (int j = 0; j < 32; j += 8)
+        if (x < R && y + j < Ccols) dst[(size_t)(y + j) * R + x] = tile[threadIdx.x][threadIdx.y + j];
+}
+
+__global__ void k_fill_f32(float *p, size_t n, float v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+}  // namespace
+
+int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w, float a_scale,
+                const float *bias, int act, float *y, int32_t *acc) {
+    const size_t n = w->n;
+    if (m == 0 || n == 0) return TPT_OK;
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
+    const int8_t *wt = (const int8_t *)w->data;
+    if (m <= 8) {
+        unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
+#define TPT_GEMV(MM) \
+    k_w8a8_gemv<MM><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc)
+        if (m == 1)
+            TPT_GEMV(1);
+        else if (m == 2)
+            TPT_GEMV(2);
+        else if (m <= 4)
+            TPT_GEMV(4);
+        else
+            TPT_GEMV(8);
+#undef TPT_GEMV
+        return after_launch(ctx, "w8a8_gemv");
+    }
+    bool handled = false;
+    int st = launch_w8a8_tc(ctx, a, m, w, a_scale, bias, act, y, acc, &handled);
+    if (st || handled) return st;
+    dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 127) / 128));
+    if (grid.y > 65535) return TPT_UNSUPPORTED;
+    k_w8a8_simt<<<grid, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc);
+    return after_launch(ctx, "w8a8_simt");
+}
+
+}  // namespace tpt
+
+using namespace tpt;
+
+#define CHECK_CTX(c)                  \
+    do {                              \
+        if (!(c)) return TPT_INVALID; \
+        cudaSetDevice((c)->device);   \
+    } while (0)
+#define TRY(x)               \
+    do {                     \
+        int _st = (x);       \
+        if (_st) return _st; \
+    } while (0)
+
+extern "C" {
+
+int tpt_cuda_weights_upload_i8(tpt_cuda_ctx *ctx, const int8_t *wt, const float *scales, size_t n, size_t k,
+                               tpt_cuda_weights **out) {
+    CHECK_CTX(ctx);
+    if (!out || !wt || !scales || n == 0 || k == 0 || k % 16 != 0) return TPT_INVALID;
+    *out = nullptr;
+    size_t bytes;
+    if (!checked_mul(n, k, &bytes)) return TPT_INVALID;
+    tpt_cuda_weights *w = new (std::nothrow) tpt_cuda_weights();
+    if (!w) return TPT_OUT_OF_MEMORY;
+    w->ctx = ctx;
+    w->kind = 8;
+    w->n = n;
+    w->k = k;
+    w->bytes = bytes;
+    cudaError_t e = cudaMalloc(&w->data, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->scales, n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(w->data, wt, bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(w->scales, scales, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (w->data) cudaFree(w->data);
+        if (w->scales) cudaFree(w->scales);
+        delete w;
+        return cuda_fail(ctx, e, "weights upload");
+    }
+    build_weight_tmap(w);
+    *out = w;
+    return TPT_OK;
+}
+
+int tpt_cuda_weights_free(tpt_cuda_weights *w) {
+    if (!w) return TPT_INVALID;
+    cudaSetDevice(w->ctx->device);
+    cudaStreamSynchronize(w->ctx->stream);
+    if (w->data) cudaFree(w->data);
+    if (w->scales) cudaFree(w->scales);
+    delete w;
+    return TPT_OK;
+}
+
+int tpt_cuda_weights_shape(const tpt_cuda_weights *w, size_t *n, size_t *k) {
+    if (!w) return TPT_INVALID;
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    return TPT_OK;
+}
+
+int tpt_cuda_w8a8_gemm(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, float a_scale,
+                       const tpt_cuda_weights *w, const float *bias, int act, float *out) {
+    CHECK_CTX(ctx);
+    if (!w || w->kind != 8) return TPT_INVALID;
+    if (k != w->k) return TPT_SHAPE_MISMATCH;
+    if (act < 0 || act > 2) return TPT_INVALID;
+    size_t an, on;
+    if (!checked_mul(m, k, &an) || !checked_mul(m, w->n, &on)) return TPT_INVALID;
+    if (on == 0) return TPT_OK;
+    Staging st(ctx);
+    st.reserve(an);
+    st.reserve(on * 4);
+    st.reserve(bias ? w->n * 4 : 0);
+    TRY(st.commit());
+    int8_t *da = st.take<int8_t>(an);
+    float *dy = st.take<float>(on);
+    float *db = bias ? st.take<float>(w->n) : nullptr;
+    TRY(h2d(ctx, da, a, an));
+    if (bias) TRY(h2d(ctx, db, bias, w->n * 4));
+    TRY(launch_w8a8(ctx, da, m, k, w, a_scale, db, act, dy, nullptr));
+    TRY(d2h(ctx, out, dy, on * 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_w8a8_gemm_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, float a_scale, const tpt_cuda_weights *w,
+                           const float *bias, int act, float *out) {
+    CHECK_CTX(ctx);
+    if (!w || w->kind != 8 || act < 0 || act > 2) return TPT_INVALID;
+    return launch_w8a8(ctx, a, m, w->k, w, a_scale, bias, act, out, nullptr);
+}
+
+int tpt_cuda_w8a8_gemm_acc_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w,
+                               int32_t *acc) {
+    CHECK_CTX(ctx);
+    if (!w || w->kind != 8 || !acc) return TPT_INVALID;
+    return launch_w8a8(ctx, a, m, w->k, w, 1.0f, nullptr, 0, nullptr, acc);
+}
+
+// ptq.rs:293-324, the reference contract: B [kb, n], per-tensor b_scales[0].
+int tpt_cuda_quantized_matmul_i8(tpt_cuda_ctx *ctx, const int8_t *a, size_t a_len, size_t m, size_t k,
+                                 float a_scale, const int8_t *b, size_t b_len, size_t kb, size_t n,
+                                 const float *b_scales, size_t n_scales, float *out, size_t out_len) {
+    CHECK_CTX(ctx);
+    if (k != kb) return TPT_SHAPE_MISMATCH;
+    size_t e1, e2, e3;
+    if (!checked_mul(m, k, &e1) || !checked_mul(k, n, &e2) || !checked_mul(m, n, &e3)) return TPT_INVALID;
+    if (a_len != e1 || b_len != e2 || out_len != e3) return TPT_SIZE_MISMATCH;
+    if (e3 == 0) return TPT_OK;
+    if (k > INT32_MAX || n > INT32_MAX || m > INT32_MAX) return TPT_UNSUPPORTED;
+    const float b_scale = n_scales ? b_scales[0] : 1.0f;
+    // K padded to a multiple of 16 with zero bytes (a zero product leaves the
+    // i32 sum unchanged).
+    const size_t kp = (k + 15) & ~size_t(15);
+    Staging st(ctx);
+    st.reserve(m * kp);
+    st.reserve(k * n);   // B as given, [k, n]
+    st.reserve(n * k);   // B^T dense, [n, k]
+    st.reserve(n * kp);  // B^T with row pitch kp
+    st.reserve(n * 4);
+    st.reserve(e3 * 4);
+    TRY(st.commit());
+    int8_t *da = st.take<int8_t>(m * kp);
+    int8_t *db = st.take<int8_t>(k * n);
+    int8_t *dbt_dense = st.take<int8_t>(n * k);
+    int8_t *dbt = st.take<int8_t>(n * kp);
+    float *ds = st.take<float>(n);
+    float *dy = st.take<float>(e3);
+    cudaError_t ce = cudaSuccess;
+    if (kp != k) {
+        ce = cudaMemsetAsync(da, 0, m * kp, ctx->stream);
+        if (ce == cudaSuccess) ce = cudaMemsetAsync(dbt, 0, n * kp, ctx->stream);
+        if (ce == cudaSuccess) ce = cudaMemcpy2DAsync(da, kp, a, k, k, m, cudaMemcpyHostToDevice, ctx->stream);
+    } else {
+        ce = cudaMemcpyAsync(da, a, m * k, cudaMemcpyHostToDevice, ctx->stream);
+    }
+    if (ce != cudaSuccess) return cuda_fail(ctx, ce, "quantized_matmul_i8 staging");
+    TRY(h2d(ctx, db, b, k * n));
+    // transpose [k, n] -> [n, k], then lay the rows out at pitch kp
+    dim3 tgrid((unsigned)((n + 31) / 32), (unsigned)((k + 31) / 32));
+    if (tgrid.y > 65535) return TPT_UNSUPPORTED;
+    k_transpose_i8<<<tgrid, dim3(32, 8), 0, ctx->stream>>>(db, kp == k ? dbt : dbt_dense, (int)k, (int)n);
+    TRY(after_launch(ctx, "transpose_i8"));
+    if (kp != k) {
+        ce = cudaMemcpy2DAsync(dbt, kp, dbt_dense, k, k, n, cudaMemcpyDeviceToDevice, ctx->stream);
+        if (ce != cudaSuccess) return cuda_fail(ctx, ce, "quantized_matmul_i8 repitch");
+    }
+    k_fill_f32<<<grid_1d(n, 256), 256, 0, ctx->stream>>>(ds, n, b_scale);
+    TRY(after_launch(ctx, "fill"));
+    tpt_cuda_weights w;
+    w.ctx = ctx;
+    w.kind = 8;
+    w.n = n;
+    w.k = kp;
+    w.data = dbt;
+    w.scales = ds;
+    w.tmap_ok = false;  // transient weights: no tensor-map path
+    // out = (float)acc * (a_scale * b_scale): the per-channel epilogue with every
+    // channel scale equal to b_scale and no bias.
+    TRY(launch_w8a8(ctx, da, m, kp, &w, a_scale, nullptr, 0, dy, nullptr));
+    TRY(d2h(ctx, out, dy, e3 * 4));
+    return sync_and_check(ctx);
+}
+
+// ------------------------------------------------------------------ quantize entry points
+int tpt_cuda_quantize_i8_symmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, float *scale) {
+    CHECK_CTX(ctx);
+    if (!scale) return TPT_INVALID;
+    if (n == 0) {
+        *scale = 1.0f;  // max_abs of an empty slice is 0 -> scale 1.0
+        return TPT_OK;
+    }
+    Staging st(ctx);
+    st.reserve(n * 4);
+    st.reserve(n);
+    st.reserve(4);
+    TRY(st.commit());
+    float *dx = st.take<float>(n);
+    int8_t *dq = st.take<int8_t>(n);
+    float *ds = st.take<float>(1);
+    TRY(h2d(ctx, dx, x, n * 4));
+    TRY(launch_quant_i8_sym(ctx, dx, n, dq, ds, ctx->d_reduce));
+    TRY(d2h(ctx, q, dq, n));
+    TRY(d2h(ctx, scale, ds, 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_quantize_i8_symmetric_dev(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, float *scale_dev) {
+    CHECK_CTX(ctx);
+    if (n == 0) return TPT_OK;
+    return launch_quant_i8_sym(ctx, x, n, q, scale_dev, ctx->d_reduce);
+}
+
+int tpt_cuda_quantize_i8_static_dev(tpt_cuda_ctx *ctx, const float *x, size_t n, float scale, int8_t *q) {
+    CHECK_CTX(ctx);
+    if (n == 0) return TPT_OK;
+    return launch_quant_i8_static(ctx, x, n, scale, q);
+}
+
+int tpt_cuda_quantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const float *x, size_t len, size_t rows,
+                                               int8_t *q, float *scales) {
+    CHECK_CTX(ctx);
+    if (rows == 0 || len % rows != 0) return TPT_INVALID;  // quant.rs:96 assert
+    if (len == 0) {
+        for (size_t r = 0; r < rows; r++) scales[r] = 1.0f;
+        return TPT_OK;
+    }
+    const size_t cols = len / rows;
+    Staging st(ctx);
+    st.reserve(len * 4);
+    st.reserve(len);
+    st.reserve(rows * 4);
+    TRY(st.commit());
+    float *dx = st.take<float>(len);
+    int8_t *dq = st.take<int8_t>(len);
+    float *ds = st.take<float>(rows);
+    TRY(h2d(ctx, dx, x, len * 4));
+    TRY(launch_quant_i8_rows(ctx, dx, rows, cols, dq, ds));
+    TRY(d2h(ctx, q, dq, len));
+    TRY(d2h(ctx, scales, ds, rows * 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_quantize_i8_asymmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, float *scale,
+                                    int32_t *zero_point) {
+    CHECK_CTX(ctx);
+    if (!scale || !zero_point) return TPT_INVALID;
+    if (n == 0) {
+        // min/max fold over nothing -> (inf, -inf) -> (0, 0) -> scale 1, zp 0
+        *scale = 1.0f;
+        *zero_point = 0;
+        return TPT_OK;
+    }
+    Staging st(ctx);
+    st.reserve(n * 4);
+    st.reserve(n);
+    st.reserve(4);
+    st.reserve(4);
+    TRY(st.commit());
+    float *dx = st.take<float>(n);
+    int8_t *dq = st.take<int8_t>(n);
+    float *ds = st.take<float>(1);
+    int32_t *dz = st.take<int32_t>(1);
+    TRY(h2d(ctx, dx, x, n * 4));
+    TRY(launch_quant_i8_asym(ctx, dx, n, dq, ds, dz, ctx->d_reduce));
+    TRY(d2h(ctx, q, dq, n));
+    TRY(d2h(ctx, scale, ds, 4));
+    TRY(d2h(ctx, zero_point, dz, 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_pack_i4(tpt_cuda_ctx *ctx, const int8_t *values, size_t n, uint8_t *out) {
+    CHECK_CTX(ctx);
+    if (n == 0) return TPT_OK;
+    const size_t nb = (n + 1) / 2;
+    Staging st(ctx);
+    st.reserve(n);
+    st.reserve(nb);
+    TRY(st.commit());
+    int8_t *dv = st.take<int8_t>(n);
+    uint8_t *dp = st.take<uint8_t>(nb);
+    TRY(h2d(ctx, dv, values, n));
+    TRY(launch_pack_i4(ctx, dv, n, dp, ctx->d_reduce));
+    unsigned bad = 0;
+    TRY(d2h(ctx, &bad, ctx->d_reduce, 4));
+    TRY(sync_and_check(ctx));
+    if (bad) return TPT_INVALID;  // the reference panics: "i4 out of range"
+    TRY(d2h(ctx, out, dp, nb));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_unpack_i4(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len, size_t n, int8_t *out,
+                       size_t *written) {
+    CHECK_CTX(ctx);
+    const size_t count = n < 2 * packed_len ? n : 2 * packed_len;
+    if (written) *written = count;
+    if (count == 0) return TPT_OK;
+    const size_t nb = (count + 1) / 2;
+    Staging st(ctx);
+    st.reserve(nb);
+    st.reserve(count);
+    TRY(st.commit());
+    uint8_t *dp = st.take<uint8_t>(nb);
+    int8_t *dv = st.take<int8_t>(count);
+    TRY(h2d(ctx, dp, packed, nb));
+    TRY(launch_unpack_i4(ctx, dp, count, dv));
+    TRY(d2h(ctx, out, dv, count));
+    return sync_and_check(ctx);
+}
+
+static int quant_i4_host(tpt_cuda_ctx *ctx, const float *x, size_t len, size_t rows, uint8_t *packed,
+                         float *scales) {
+    const size_t cols = len / rows, rb = (cols + 1) / 2;
+    Staging st(ctx);
+    st.reserve(len * 4);
+    st.reserve(rows * rb);
+    st.reserve(rows * 4);
+    TRY(st.commit());
+    float *dx = st.take<float>(len);
+    uint8_t *dp = st.take<uint8_t>(rows * rb);
+    float *ds = st.take<float>(rows);
+    TRY(h2d(ctx, dx, x, len * 4));
+    TRY(launch_quant_i4_rows(ctx, dx, rows, cols, dp, ds));
+    TRY(d2h(ctx, packed, dp, rows * rb));
+    TRY(d2h(ctx, scales, ds, rows * 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_quantize_i4_symmetric(tpt_cuda_ctx *ctx, const float *x, size_t n, uint8_t *packed, float *scale) {
+    CHECK_CTX(ctx);
+    if (!scale) return TPT_INVALID;
+    if (n == 0) {
+        *scale = 1.0f;
+        return TPT_OK;
+    }
+    return quant_i4_host(ctx, x, n, 1, packed, scale);
+}
+
+int tpt_cuda_quantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const float *x, size_t len, size_t rows,
+                                               uint8_t *packed, float *scales) {
+    CHECK_CTX(ctx);
+    if (rows == 0 || len % rows != 0) return TPT_INVALID;  // quant.rs:193 assert
+    if (len == 0) {
+        for (size_t r = 0; r < rows; r++) scales[r] = 1.0f;
+        return TPT_OK;
+    }
+    return quant_i4_host(ctx, x, len, rows, packed, scales);
+}
+
+int tpt_cuda_dequantize_i8_symmetric(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale, float *out) {
+    return tpt_cuda_dequantize_i8_symmetric_per_channel(ctx, q, n, &scale, 1, out);
+}
+
+int tpt_cuda_dequantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, const float *scales,
+                                                 size_t n_scales, float *out) {
+    CHECK_CTX(ctx);
+    if (n_scales == 0 || n % n_scales != 0) return TPT_INVALID;  // dequant.rs:27-28 asserts
+    if (n == 0) return TPT_OK;
+    Staging st(ctx);
+    st.reserve(n);
+    st.reserve(n_scales * 4);
+    st.reserve(n * 4);
+    TRY(st.commit());
+    int8_t *dq = st.take<int8_t>(n);
+    float *ds = st.take<float>(n_scales);
+    float *dy = st.take<float>(n);
+    TRY(h2d(ctx, dq, q, n));
+    TRY(h2d(ctx, ds, scales, n_scales * 4));
+    TRY(launch_dequant_i8_rows(ctx, dq, n_scales, n / n_scales, ds, dy));
+    TRY(d2h(ctx, out, dy, n * 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_dequantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len,
+                                                 size_t row_elems, const float *scales, size_t n_scales,
+                                                 float *out) {
+    CHECK_CTX(ctx);
+    if (n_scales == 0) return TPT_INVALID;  // dequant.rs:61 assert
+    const size_t n = row_elems * n_scales;
+    if (n == 0) return TPT_OK;
+    Staging st(ctx);
+    st.reserve(packed_len ? packed_len : 1);
+    st.reserve(n_scales * 4);
+    st.reserve(n * 4);
+    TRY(st.commit());
+    uint8_t *dp = st.take<uint8_t>(packed_len ? packed_len : 1);
+    float *ds = st.take<float>(n_scales);
+    float *dy = st.take<float>(n);
+    TRY(h2d(ctx, dp, packed, packed_len));
+    TRY(h2d(ctx, ds, scales, n_scales * 4));
+    // values whose byte lies past packed_len are absent in the reference; the
+    // caller's buffer keeps its contents there: copy it in first
+    TRY(h2d(ctx, dy, out, n * 4));
+    TRY(launch_dequant_i4_rows(ctx, dp, n_scales, row_elems, packed_len, ds, dy));
+    TRY(d2h(ctx, out, dy, n * 4));
+    return sync_and_check(ctx);
+}
+
+}  // extern "C"
