@@ -1,18 +1,430 @@
-// w8a8_tc.cu -- tcgen05 (5th-gen tensor core) W8A8 GEMM for large M.
+// w8a8_tc.cu -- the large-M W8A8 GEMM on Blackwell's 5th-generation tensor
+// cores (tcgen05.mma kind::i8, i32 accumulators in tensor memory).
+//
+// Computes the per-channel extension of quantized_matmul_i8
+// (crates/tpt-infer-quantize/src/ptq.rs:293-324):
+//   acc[m,n] = sum_k A[m,k] * Wt[n,k]           (int8 x int8 -> i32, exact)
+//   y[m,n]   = (float)acc * (a_scale * w_scale[n]) + bias[n], then act
+// The epilogue rounds exactly like the oracle (separate RN multiply/add), so
+// the f32 output is bit-exact.
+//
+// Structure (one CTA per SM, persistent over output tiles of 128 x BN):
+//   warp 0      TMA producer: A tile [128 rows x 128 B] and B tile
+//               [BN rows x 128 B] per k-block into a STAGES-deep ring of
+//               128B-swizzled shared-memory buffers (K-major, the layout the
+//               MMA's shared-memory descriptors describe).
+//   warp 1      allocates tensor memory; one lane issues tcgen05.mma
+//               (M=128, N=BN, K=32 per instruction) and tcgen05.commit to free
+//               ring slots and to publish finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from the TMEM
+//               accumulator (each warp owns its 32-lane quarter), fused
+//               dequant + bias + activation, 128-bit stores.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the MMAs of tile i+1.
+//
+// Every mbarrier wait is bounded (TPT_WAIT_NS of wall time via %globaltimer).
+// A wait that runs out records TPT_FLAG_TIMEOUT in the context's device flag
+// words, raises a CTA-wide abort so every role leaves its loop, the producer
+// waits (bounded) for its own TMA copies still in flight, the MMA issuer waits
+// (bounded) for its MMAs, tensor memory is freed and the kernel returns.
+// No multicast loads are used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace tpt {
+namespace {
+
+constexpr int TC_BM = 128;       // output rows per tile (MMA M)
+constexpr int TC_BK = 128;       // k bytes per stage (one 128B swizzle row)
+constexpr int TC_THREADS = 192;  // 6 warps
+constexpr unsigned long long TPT_WAIT_NS = 1000000000ull;  // 1 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait. Returns false when the CTA is aborting or the wait ran out
+// (then the abort is raised and the global timeout flag recorded).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
+                                       bool honour_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (honour_abort && *abort_flag) return false;
+        if (globaltimer() - t0 > TPT_WAIT_NS) {
+            *abort_flag = 1;
+            if (gflags) atomicOr(gflags + TPT_FLAG_TIMEOUT, 1u);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets its lane's 32 values.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major, 128B-swizzled operand tile:
+// 8-row x 128-byte swizzle atoms stacked along M/N (stride 1024 B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address, bits 0-13
+    d |= (uint64_t)1 << 16;                     // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                     // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                     // swizzle mode: 128B
+    return d;
+}
+
+// Instruction descriptor, kind::i8: D = s32, A = B = signed 8-bit, both
+// K-major, N = BN, M = 128.
+template <int BN>
+__host__ __device__ constexpr uint32_t i8_idesc() {
+    return (2u << 4)            // D format: s32
+           | (1u << 7)          // A format: signed 8-bit
+           | (1u << 10)         // B format: signed 8-bit
+           | ((uint32_t)(BN >> 3) << 17)
+           | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+template <int BN>
+struct TcCfg {
+    static constexpr int A_BYTES = TC_BM * TC_BK;
+    static constexpr int B_BYTES = BN * TC_BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+    // ring + barriers (full, empty per stage; tfull, tempty per accumulator;
+    // one MMA-drain barrier) + TMEM address slot + 1 KB alignment slack
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
+};
+
+template <int BN, bool ACC_OUT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_w8a8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+              float a_scale, const float *__restrict__ wscale, const float *__restrict__ bias, int act,
+              float *__restrict__ Y, int32_t *__restrict__ ACC, unsigned *gflags) {
+    using Cfg = TcCfg<BN>;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int abort_flag;
+    __shared__ uint32_t tmem_slot;
+
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t ring = (raw + 1023u) & ~1023u;
+    const uint32_t bars = ring + S * Cfg::STAGE_BYTES;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+    auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
+    auto tempty_bar = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
+    const uint32_t drain_bar = bars + 8u * (2 * S + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + BN - 1) / BN;
+    const int ntiles = tiles_m * tiles_n;
+    const int kblocks = (K + TC_BK - 1) / TC_BK;
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 4 * 32);
+        }
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)Cfg::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int *abort_p = &abort_flag;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, last_phase = 0;  // per stage: issued?, parity of last issue
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int mt = t / tiles_n, nt = t - mt * tiles_n;
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t a_dst = ring + stage * Cfg::STAGE_BYTES;
+                    mbar_arrive_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
+                    tma_load_2d(a_dst, &tmA, full_bar(stage), kb * TC_BK, mt * TC_BM);
+                    tma_load_2d(a_dst + Cfg::A_BYTES, &tmB, full_bar(stage), kb * TC_BK, nt * BN);
+                    issued_mask |= 1u << stage;
+                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // our own copies in flight must land before the CTA can exit
+            for (int s = 0; s < S; s++)
+                if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (last_phase >> s) & 1u, abort_p, gflags, false);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = i8_idesc<BN>();
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = ring + stage * Cfg::STAGE_BYTES;
+                    const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 32; kk++)
+                        tc_mma_i8(d_tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), idesc,
+                                  (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(empty_bar(stage));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(tfull_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // drain: every MMA this thread issued completes before TMEM is freed
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_p, gflags, false);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            int okw = 0;
+            if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
+            okw = __shfl_sync(0xffffffffu, okw, 0);
+            if (!okw) break;
+            tc_fence_after();
+            const int mt = t / tiles_n, nt = t - mt * tiles_n;
+            const int m = mt * TC_BM + row;
+            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; c++) {
+                uint32_t v[32];
+                tmem_ld32(t_base + (uint32_t)(c * 32), v);
+                tmem_wait_ld();
+                const int n0 = nt * BN + c * 32;
+                if (m < M) {
+                    if (ACC_OUT) {
+                        int32_t *dst = ACC + (size_t)m * N + n0;
+                        if (n0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<int4 *>(dst + j) =
+                                    make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
+                        } else {
+                            for (int j = 0; j < 32 && n0 + j < N; j++) dst[j] = (int32_t)v[j];
+                        }
+                    } else {
+                        float o[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int n = n0 + j < N ? n0 + j : N - 1;
+                            float y = __fmul_rn(__int2float_rn((int)v[j]), __fmul_rn(a_scale, __ldg(wscale + n)));
+                            if (bias) y = __fadd_rn(y, __ldg(bias + n));
+                            o[j] = apply_act(y, act);
+                        }
+                        float *dst = Y + (size_t)m * N + n0;
+                        if (n0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4 *>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+                        } else {
+                            for (int j = 0; j < 32 && n0 + j < N; j++) dst[j] = o[j];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(tempty_bar(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"((uint32_t)Cfg::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// 2-D uint8 tensor [rows, k] (k contiguous), box [box_rows, 128 B], 128B swizzle,
+// out-of-range elements read as zero.
+bool make_tmap_i8(CUtensorMap *tm, const void *base, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    if (((uintptr_t)base & 15) || (k & 15)) return false;
+    cuuint64_t dims[2] = {k, rows};
+    cuuint64_t strides[1] = {k};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool ACC_OUT>
+int launch_tc(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
+              const float *ws, const float *bias, int act, float *y, int32_t *acc) {
+    using Cfg = TcCfg<BN>;
+    // the dynamic shared-memory opt-in is per device
+    static bool attr_done[64] = {};
+    auto kfn = k_w8a8_tc<BN, ACC_OUT>;
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "w8a8_tc smem attribute");
+        attr_done[dev] = true;
+    }
+    const int ntiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
+    const int grid = ntiles < ctx->sm_count ? ntiles : ctx->sm_count;
+    kfn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(ta, tb, M, N, K, a_scale, ws, bias, act, y, acc,
+                                                            ctx->d_flags);
+    return after_launch(ctx, "w8a8_tc");
+}
+
+}  // namespace
 
 int build_weight_tmap(tpt_cuda_weights *w) {
-    w->tmap_ok = false;
+    CUtensorMap *tm = reinterpret_cast<CUtensorMap *>(w->tmap);
+    w->tmap_ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff &&
+                 make_tmap_i8(tm, w->data, w->n, w->k, 256);
     return TPT_OK;
 }
 
+// Large-M shapes go to the tensor-core kernel: M >= 128, weights with a tensor
+// map (K % 16 == 0, 16-byte aligned), A 16-byte aligned.
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled) {
-    (void)ctx; (void)a; (void)m; (void)w; (void)a_scale; (void)bias; (void)act; (void)y; (void)acc;
     *handled = false;
-    return TPT_OK;
+    if (!w->tmap_ok || m < 128 || m > 0x7fffffff) return TPT_OK;
+    CUtensorMap ta;
+    if (!make_tmap_i8(&ta, a, m, w->k, TC_BM)) return TPT_OK;
+    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmap);
+    *handled = true;
+    if (acc) return launch_tc<256, true>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
+    return launch_tc<256, false>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
 }
 
 }  // namespace tpt
