@@ -181,6 +181,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-budget", type=float, default=3.0, help="seconds of CPU work per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="headline GEMM only (warm-up + steps), no sweep / e2e / CPU leg: the ncu capture case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -228,6 +230,15 @@ def main():
             launches = be.launch_count() - l0
         be.sync()
         return [s.elapsed_time(e) for s, e in evs], launches
+
+    if args.profile:
+        times, launches = timed(M_HEAD, args.steps, args.warmup)
+        if rank == 0:
+            print(json.dumps({"profile": True, "M": M_HEAD, "us": float(np.mean(times)) * 1e3,
+                              "launches": int(launches)}), flush=True)
+        w.free()
+        be.close()
+        return 0
 
     # the rest of the sweep (informative)
     sweep = []
