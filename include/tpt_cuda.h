@@ -226,6 +226,41 @@ int tpt_cuda_w4_gemm(tpt_cuda_ctx *ctx, const float *x, size_t m, size_t k,
 int tpt_cuda_w4_gemm_dev(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w,
                          const float *bias, int act, float *out);
 
+/* ------------------------------------------------------------------ */
+/* Allocation-free quantization                                         */
+/* ------------------------------------------------------------------ */
+
+/* Scratch of the allocation-free entry point below: TPT_NOALLOC_PARTIALS
+ * 32-bit words (128 KiB) in the library's device image, which bounds its input
+ * to TPT_NOALLOC_QUANT_MAX_ELEMS elements (2^28 floats, 1 GiB). */
+#define TPT_NOALLOC_PARTIALS 32768u
+#define TPT_NOALLOC_QUANT_MAX_ELEMS 268435456ull
+
+/* No counterpart in the reference: an extra entry point for callers that
+ * cannot allocate device memory -- code living inside another engine's memory
+ * budget, real-time paths that cannot afford cudaMalloc's implicit device
+ * synchronisation, and code that must not run out of memory halfway through.
+ * It needs no context (creating one allocates) and calls no cudaMalloc,
+ * cudaFree or other allocating routine.
+ *
+ * Same result as tpt_cuda_quantize_i8_symmetric_dev (quantize_i8_symmetric
+ * semantics, bit-exact): x, q and scale are DEVICE pointers (x: n floats,
+ * q: n int8, scale: one float written on the device), enqueued on `stream`
+ * (a cudaStream_t passed as void*, NULL = legacy default stream) on the
+ * current device; the call does not synchronise.
+ *
+ * Its reduction scratch is a fixed 128 KiB array that every GPU loading this
+ * library holds until the process exits. n > TPT_NOALLOC_QUANT_MAX_ELEMS is
+ * rejected with TPT_INVALID before any work is enqueued. The first call on a
+ * device looks up the scratch's device address (cudaGetSymbolAddress, with
+ * that device current) and caches it, so make that first call before any
+ * stream capture. All calls on a device share the scratch: calls whose
+ * kernels may overlap on the GPU (different streams without ordering) race
+ * on it. Nothing in the scratch needs to start at zero: a call only reads
+ * what it wrote itself earlier in stream order. */
+int tpt_cuda_quantize_i8_symmetric_noalloc(const float *x, size_t n, int8_t *q, float *scale,
+                                           void *stream);
+
 #ifdef __cplusplus
 }
 #endif

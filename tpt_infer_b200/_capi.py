@@ -73,6 +73,7 @@ SIGNATURES = {
     "tpt_cuda_w8a8_gemm_acc_dev": (C.c_int, [ctxp, vp, sz, wp, vp]),
     "tpt_cuda_w4_gemm": (C.c_int, [ctxp, vp, sz, sz, wp, vp, C.c_int, vp]),
     "tpt_cuda_w4_gemm_dev": (C.c_int, [ctxp, vp, sz, wp, vp, C.c_int, vp]),
+    "tpt_cuda_quantize_i8_symmetric_noalloc": (C.c_int, [vp, sz, vp, vp, vp]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():
