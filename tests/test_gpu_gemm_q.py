@@ -31,7 +31,8 @@ def w8a8_case(m, n, k, seed=100, with_bias=True):
 
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (16, 4096, 4096), (256, 4096, 4096),
                                    (3, 100, 48), (9, 33, 16), (130, 200, 64), (1, 10, 512),
-                                   (128, 256, 128), (300, 512, 256), (1000, 768, 768)])
+                                   (128, 256, 128), (300, 512, 256), (1000, 768, 768), (160, 203, 96),
+                                   (4097, 300, 128)])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_w8a8_bit_exact(cuda, m, n, k, act):
     if act and m * n * k > 1 << 26:

@@ -92,6 +92,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
         : "memory");
 }
 
+// 2-D bulk-tensor store of one 32 x 32 (4-byte) block from shared memory.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -152,16 +159,19 @@ struct TcCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 4 : 6;
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
-    // ring + barriers (full, empty per stage; tfull, tempty per accumulator;
-    // one MMA-drain barrier) + TMEM address slot + 1 KB alignment slack
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
+    // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B)
+    static constexpr int OUT_BYTES = 4 * 2 * 4096;
+    // ring + staging + barriers (full, empty per stage; tfull, tempty per
+    // accumulator; one MMA-drain barrier) + 1 KB alignment slack
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
 };
 
 template <int BN, bool ACC_OUT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    k_w8a8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-              float a_scale, const float *__restrict__ wscale, const float *__restrict__ bias, int act,
-              float *__restrict__ Y, int32_t *__restrict__ ACC, unsigned *gflags) {
+    k_w8a8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
+              const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
+              int32_t *__restrict__ ACC, unsigned *gflags) {
     using Cfg = TcCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -170,7 +180,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ring = (raw + 1023u) & ~1023u;
-    const uint32_t bars = ring + S * Cfg::STAGE_BYTES;
+    const uint32_t staging = ring + S * Cfg::STAGE_BYTES;  // 1 KB aligned
+    const uint32_t bars = staging + Cfg::OUT_BYTES;
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
@@ -283,8 +294,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        // Each warp owns TMEM lanes [32q, 32q+32) = tile rows [32q, 32q+32).
+        // Per 32-column chunk: tcgen05.ld (thread = row), dequant with the
+        // column's scale/bias broadcast by shuffle, then either a TMA store of
+        // the 32 x 32 block staged in 128B-swizzled shared memory (coalesced,
+        // clipped at ragged edges) or, when the output cannot be described by
+        // a tensor map, direct stores.
+        const int q = warp & 3;
         const int row = q * 32 + lane;
+        const uint32_t stage_s = staging + (uint32_t)(q * 8192);
+        uint8_t *stage_g = smem_raw + (stage_s - raw);
+        int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -302,34 +322,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
                 const int n0 = nt * BN + c * 32;
-                if (m < M) {
-                    if (ACC_OUT) {
-                        int32_t *dst = ACC + (size_t)m * N + n0;
-                        if (n0 + 32 <= N && (N & 3) == 0) {
+                if (!ACC_OUT) {
+                    const int nc = n0 + lane < N ? n0 + lane : N - 1;  // this lane's column
+                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nc));
+                    const float bi = bias ? __ldg(bias + nc) : 0.0f;
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<int4 *>(dst + j) =
-                                    make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
-                        } else {
-                            for (int j = 0; j < 32 && n0 + j < N; j++) dst[j] = (int32_t)v[j];
-                        }
+                    for (int j = 0; j < 32; j++) {
+                        float y = __fmul_rn(__int2float_rn((int)v[j]), __shfl_sync(0xffffffffu, sc, j));
+                        if (bias) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bi, j));
+                        v[j] = __float_as_uint(apply_act(y, act));
+                    }
+                }
+                if (tma_store) {
+                    // the store issued from this buffer two chunks ago must have read it
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    __syncwarp();
+                    uint8_t *sb = stage_g + buf * 4096 + lane * 128;
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++)
+                        *reinterpret_cast<uint4 *>(sb + ((cc ^ (lane & 7)) << 4)) =
+                            make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mt * TC_BM + q * 32);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                    buf ^= 1;
+                } else if (m < M) {
+                    uint32_t *dst = ACC_OUT ? reinterpret_cast<uint32_t *>(ACC) + (size_t)m * N + n0
+                                            : reinterpret_cast<uint32_t *>(Y) + (size_t)m * N + n0;
+                    if (n0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<uint4 *>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                     } else {
-                        float o[32];
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const int n = n0 + j < N ? n0 + j : N - 1;
-                            float y = __fmul_rn(__int2float_rn((int)v[j]), __fmul_rn(a_scale, __ldg(wscale + n)));
-                            if (bias) y = __fadd_rn(y, __ldg(bias + n));
-                            o[j] = apply_act(y, act);
-                        }
-                        float *dst = Y + (size_t)m * N + n0;
-                        if (n0 + 32 <= N && (N & 3) == 0) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4 *>(dst + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-                        } else {
-                            for (int j = 0; j < 32 && n0 + j < N; j++) dst[j] = o[j];
-                        }
+                        for (int j = 0; j < 32; j++)
+                            if (n0 + j < N) dst[j] = v[j];
                     }
                 }
             }
@@ -340,6 +370,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 acc_phase ^= 1u;
             }
         }
+        // every bulk store has finished reading this CTA's shared memory and
+        // written its block before the CTA exits
+        if (tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -366,6 +400,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
             cudaGetLastError();
     }
     return fn;
+}
+
+// 2-D 4-byte tensor [rows, cols] (f32 or i32, cols contiguous), box 32 x 32,
+// 128B swizzle: the epilogue's store map (stores are clipped to the tensor).
+bool make_tmap_out(CUtensorMap *tm, const void *base, uint64_t rows, uint64_t cols, bool is_int) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    if (((uintptr_t)base & 15) || (cols & 3)) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(tm, is_int ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 // 2-D uint8 tensor [rows, k] (k contiguous), box [box_rows, 128 B], 128B swizzle,
@@ -399,8 +449,11 @@ int launch_tc(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, i
     }
     const int ntiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
     const int grid = ntiles < ctx->sm_count ? ntiles : ctx->sm_count;
-    kfn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(ta, tb, M, N, K, a_scale, ws, bias, act, y, acc,
-                                                            ctx->d_flags);
+    CUtensorMap ty;
+    const bool tma_store = make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
+                                         (uint64_t)N, ACC_OUT);
+    kfn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0, M, N, K,
+                                                            a_scale, ws, bias, act, y, acc, ctx->d_flags);
     return after_launch(ctx, "w8a8_tc");
 }
 
