@@ -37,8 +37,10 @@ struct tpt_cuda_weights {
     void *data = nullptr;  // device: packed weight bytes
     float *scales = nullptr;  // device: n per-channel scales
     size_t bytes = 0;
-    // TMA descriptor of the int8 weight (CUtensorMap, 128 bytes), built once
+    // TMA descriptors of the int8 weight (CUtensorMap, 128 bytes each), built
+    // once: box of 256 rows (one-SM kernel) and of 128 rows (SM-pair kernel)
     alignas(64) unsigned char tmap[128];
+    alignas(64) unsigned char tmap128[128];
     bool tmap_ok = false;
 };
 

@@ -386,6 +386,298 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// SM-pair kernel: tcgen05.mma.cta_group::2, 256 x 256 output tiles per
+// cluster of two CTAs on two SMs. Each CTA loads its 128 rows of A and its 128
+// rows of B (its half of the tile's N) per k-block; the leader CTA (cluster
+// rank 0) issues the M=256 MMA, which reads both CTAs' shared memory, and
+// each CTA's tensor memory receives its own 128 x 256 accumulator. Per SM the
+// operand traffic is 8 KB per MMA instruction instead of 12 KB for the
+// one-SM 128 x 256 form, which is what lets the tensor pipe run at its rate.
+//   full[s]   (leader)  : completed by both CTAs' TMA bytes (2-SM loads)
+//   empty[s]  (each)    : leader's MMA commit, multicast to both CTAs
+//   tfull[b]  (each)    : leader's MMA commit, multicast to both CTAs
+//   tempty[b] (leader)  : one arrival per epilogue warp of both CTAs
+// 8 epilogue warps per CTA: two per TMEM lane quarter, each taking half of
+// the 256 accumulator columns.
+// ---------------------------------------------------------------------------
+constexpr int P_BN = 256;                 // tile N (MMA N)
+constexpr int P_BM = 256;                 // tile M (MMA M over the pair)
+constexpr int P_STAGES = 5;
+constexpr int P_EPI_WARPS = 8;
+constexpr int P_THREADS = (2 + P_EPI_WARPS) * 32;
+constexpr int P_A_BYTES = 128 * TC_BK;    // this CTA's 128 rows of A
+constexpr int P_B_BYTES = 128 * TC_BK;    // this CTA's 128 rows of B
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_OUT_BYTES = P_EPI_WARPS * 2 * 4096;
+constexpr int P_TMEM_COLS = 2 * P_BN;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + P_OUT_BYTES + (2 * P_STAGES + 5) * 8 + 16 + 1024;
+static_assert(P_SMEM_BYTES <= 232448, "dynamic shared memory per CTA");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-SM TMA load: data into this CTA's shared memory, transaction bytes
+// counted on the barrier at `bar_cluster` (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *tm, uint32_t bar_cluster, int x,
+                                                 int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tc2_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// commit the leader's MMAs to the barrier at `bar` in both CTAs of the pair
+__device__ __forceinline__ void tc2_commit_both(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+template <bool ACC_OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
+    k_w8a8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
+               const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
+               int32_t *__restrict__ ACC, unsigned *gflags) {
+    constexpr int S = P_STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int abort_flag;
+    __shared__ uint32_t tmem_slot;
+
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t ring = (raw + 1023u) & ~1023u;
+    const uint32_t staging = ring + S * P_STAGE_BYTES;
+    const uint32_t bars = staging + P_OUT_BYTES;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+    auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
+    auto tempty_bar = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
+    const uint32_t drain_bar = bars + 8u * (2 * S + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    const int tiles_m = (M + P_BM - 1) / P_BM, tiles_n = (N + P_BN - 1) / P_BN;
+    const int ntiles = tiles_m * tiles_n;
+    const int kblocks = (K + TC_BK - 1) / TC_BK;
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 2 * P_EPI_WARPS);
+        }
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)P_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int *abort_p = &abort_flag;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < ntiles && ok; t += nclusters) {
+                const int mt = t / tiles_n, nt = t - mt * tiles_n;
+                const int arow = mt * P_BM + (int)rank * 128, brow = nt * P_BN + (int)rank * 128;
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t a_dst = ring + stage * P_STAGE_BYTES;
+                    const uint32_t fb = map_to_rank(full_bar(stage), 0);
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * P_STAGE_BYTES);
+                    tma_load_2d_pair(a_dst, &tmA, fb, kb * TC_BK, arow);
+                    tma_load_2d_pair(a_dst + P_A_BYTES, &tmB, fb, kb * TC_BK, brow);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader CTA only) ----------------
+            constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(P_BN >> 3) << 17) |
+                                       ((uint32_t)(P_BM >> 4) << 24);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < ntiles && ok; t += nclusters) {
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * P_BN);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = ring + stage * P_STAGE_BYTES;
+                    const uint32_t b_addr = a_addr + P_A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 32; kk++)
+                        tc2_mma_i8(d_tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), idesc,
+                                   (kb | kk) != 0 ? 1u : 0u);
+                    tc2_commit_both(empty_bar(stage));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc2_commit_both(tfull_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // drain: every MMA issued completes before TMEM is freed
+            asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             drain_bar)
+                         : "memory");
+            mbar_wait(drain_bar, 0, abort_p, gflags, false);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
+        const int e = warp - 2;        // 0..7
+        const int q = warp & 3;        // TMEM lane quarter this warp may access
+        const int half = e >> 2;       // which 128 of the 256 columns
+        const int row = q * 32 + lane;
+        const uint32_t stage_s = staging + (uint32_t)(e * 8192);
+        uint8_t *stage_g = smem_raw + (stage_s - raw);
+        const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
+        const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
+        int buf = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = cluster; t < ntiles; t += nclusters) {
+            int okw = 0;
+            if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
+            okw = __shfl_sync(0xffffffffu, okw, 0);
+            if (!okw) break;
+            tc_fence_after();
+            const int mt = t / tiles_n, nt = t - mt * tiles_n;
+            const int mrow0 = mt * P_BM + (int)rank * 128 + q * 32;  // first row of this warp's block
+            const int m = mrow0 + lane;
+            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * P_BN + half * 128);
+#pragma unroll 1
+            for (int c = 0; c < 4; c++) {
+                uint32_t v[32];
+                tmem_ld32(t_base + (uint32_t)(c * 32), v);
+                tmem_wait_ld();
+                const int n0 = nt * P_BN + half * 128 + c * 32;
+                if (!ACC_OUT) {
+                    const int nc = n0 + lane < N ? n0 + lane : N - 1;
+                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nc));
+                    const float bi = bias ? __ldg(bias + nc) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        float y = __fmul_rn(__int2float_rn((int)v[j]), __shfl_sync(0xffffffffu, sc, j));
+                        if (bias) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bi, j));
+                        v[j] = __float_as_uint(apply_act(y, act));
+                    }
+                }
+                if (tma_store) {
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    __syncwarp();
+                    uint8_t *sb = stage_g + buf * 4096 + lane * 128;
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++)
+                        *reinterpret_cast<uint4 *>(sb + ((cc ^ (lane & 7)) << 4)) =
+                            make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mrow0);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                    buf ^= 1;
+                } else if (m < M) {
+                    uint32_t *dst = ACC_OUT ? reinterpret_cast<uint32_t *>(ACC) + (size_t)m * N + n0
+                                            : reinterpret_cast<uint32_t *>(Y) + (size_t)m * N + n0;
+                    if (n0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<uint4 *>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (n0 + j < N) dst[j] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc == 0 ? tempty_leader0 : tempty_leader1);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
+    }
+
+    // Both CTAs stay resident until neither needs the other: the leader's MMAs
+    // read the peer's shared memory, the peer's epilogue arrives on the
+    // leader's barriers, and both CTAs' TMA loads signal the leader.
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)P_TMEM_COLS)
+                     : "memory");
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static bool tried = false;
@@ -457,12 +749,55 @@ int launch_tc(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, i
     return after_launch(ctx, "w8a8_tc");
 }
 
+template <bool ACC_OUT>
+int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
+               const float *ws, const float *bias, int act, float *y, int32_t *acc) {
+    static bool attr_done[64] = {};
+    static int max_clusters[64] = {};
+    auto kfn = k_w8a8_tc2<ACC_OUT>;
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "w8a8_tc2 smem attribute");
+        // how many SM pairs can hold one cluster each at the same time (the
+        // persistent tile loop assumes every launched cluster is resident)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (ctx->sm_count / 2), 1, 1);
+        cfg.blockDim = dim3(P_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = ctx->sm_count / 2;
+        }
+        max_clusters[dev] = n;
+        attr_done[dev] = true;
+    }
+    const int ntiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+    const int pairs = max_clusters[dev];
+    const int clusters = ntiles < pairs ? ntiles : pairs;
+    CUtensorMap ty;
+    const bool tma_store = make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
+                                         (uint64_t)N, ACC_OUT);
+    kfn<<<2 * clusters, P_THREADS, P_SMEM_BYTES, ctx->stream>>>(ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0, M, N,
+                                                                 K, a_scale, ws, bias, act, y, acc, ctx->d_flags);
+    return after_launch(ctx, "w8a8_tc2");
+}
+
 }  // namespace
 
 int build_weight_tmap(tpt_cuda_weights *w) {
     CUtensorMap *tm = reinterpret_cast<CUtensorMap *>(w->tmap);
+    CUtensorMap *tm128 = reinterpret_cast<CUtensorMap *>(w->tmap128);
     w->tmap_ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff &&
-                 make_tmap_i8(tm, w->data, w->n, w->k, 256);
+                 make_tmap_i8(tm, w->data, w->n, w->k, 256) && make_tmap_i8(tm128, w->data, w->n, w->k, 128);
     return TPT_OK;
 }
 
@@ -474,8 +809,14 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     if (!w->tmap_ok || m < 128 || m > 0x7fffffff) return TPT_OK;
     CUtensorMap ta;
     if (!make_tmap_i8(&ta, a, m, w->k, TC_BM)) return TPT_OK;
-    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmap);
     *handled = true;
+    if (m >= 256) {
+        // SM-pair kernel (256 x 256 tiles); A and B tensor maps with 128-row boxes
+        const CUtensorMap &tb2 = *reinterpret_cast<const CUtensorMap *>(w->tmap128);
+        if (acc) return launch_tc2<true>(ctx, ta, tb2, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
+        return launch_tc2<false>(ctx, ta, tb2, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
+    }
+    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmap);
     if (acc) return launch_tc<256, true>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
     return launch_tc<256, false>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
 }
