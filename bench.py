@@ -116,14 +116,25 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_inputs(m, seed=1000):
-    from oracle import oracle as O  # seeded generators and reference quantizers (input preparation only)
+def make_inputs(m, seed=1000, be=None):
+    """Seeded W8A8 sweep inputs: W ~ N(0, 0.02) quantized per output channel (rows
+    of W^T), A ~ N(0, 1) quantized per tensor, bias ~ N(0, 0.01). Quantized by the
+    CUDA backend (``be``) on the GPU leg, by the oracle on the CPU-only legs; the
+    two are bit-identical."""
+    from tpt_infer_b200 import synth
 
-    w = O.normal(K * N, seed, 0.0, 0.02).reshape(K, N)
-    wq, ws = O.quantize_i8_symmetric_per_channel(np.ascontiguousarray(w.T), N)
-    x = O.normal(m * K, seed + 1, 0.0, 1.0)
-    aq, sa = O.quantize_i8_symmetric(x)
-    bias = O.normal(N, seed + 2, 0.0, 0.01)
+    w = synth.normal(K * N, seed, 0.0, 0.02).reshape(K, N)
+    x = synth.normal(m * K, seed + 1, 0.0, 1.0)
+    bias = synth.normal(N, seed + 2, 0.0, 0.01)
+    wt = np.ascontiguousarray(w.T)
+    if be is not None:
+        wq, ws = be.quantize_i8_symmetric_per_channel(wt, N)
+        aq, sa = be.quantize_i8_symmetric(x)
+    else:
+        from oracle import oracle as O
+
+        wq, ws = O.quantize_i8_symmetric_per_channel(wt, N)
+        aq, sa = O.quantize_i8_symmetric(x)
     return aq, float(sa), wq, ws, bias
 
 
@@ -205,7 +216,7 @@ def main():
     assert be is not None, "no sm_100 device"
     pk = peaks()
 
-    aq, sa, wq, ws, bias = make_inputs(M_HEAD)
+    aq, sa, wq, ws, bias = make_inputs(M_HEAD, be=be)
     w = be.upload_i8(wq, ws, N, K)
     dev = f"cuda:{local}"
     a_dev = torch.from_numpy(aq).to(dev)

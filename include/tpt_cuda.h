@@ -227,6 +227,71 @@ int tpt_cuda_w4_gemm_dev(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_
                          const float *bias, int act, float *out);
 
 /* ------------------------------------------------------------------ */
+/* Device-resident plans (execute_graph on the device)                  */
+/* ------------------------------------------------------------------ */
+
+/* The device counterpart of execute_graph / required_arena_bytes
+ * (crates/tpt-infer-runtime/src/exec.rs:117-131, 570-635): every activation
+ * tensor gets a disjoint offset in ONE device arena allocated at finalize
+ * (the reference's assign_offsets + single alloc_slice, exec.rs:276-294,595),
+ * constants are uploaded once, ops run in order on the context's stream, and
+ * host copies happen only at graph inputs and outputs (tpt_cuda_plan_run).
+ * INT8 activations carry a per-tensor scale; a quantization point either has a
+ * static scale (op.f0 > 0) or is calibrated: runs made with calibration on
+ * record max|x| per point, tpt_cuda_plan_freeze_scales sets
+ * scale = max / 127 (1.0 if max == 0), the quantize_i8_symmetric rule
+ * (crates/tpt-infer-quantize/src/quant.rs:25-31). */
+typedef struct tpt_cuda_plan tpt_cuda_plan;
+
+enum { TPT_DT_F32 = 0, TPT_DT_I8 = 1 };
+
+enum tpt_op_kind {
+    TPT_OP_QUANTIZE = 1,        /* in0 f32 [d0] -> out i8, per-tensor scale */
+    TPT_OP_LINEAR_W8A8 = 2,     /* in0 i8 [d0, w.k] x w -> out f32 [d0, w.n]; in1 bias (or -1); act */
+    TPT_OP_MATMUL_F32 = 3,      /* in0 [d0,d1] x in1 [d1,d2] -> out; in2 bias (or -1); act (Backend::matmul) */
+    TPT_OP_BIAS_ACT = 4,        /* out[d0,d1] = act(in0 + in1[d1]) (in1 may be -1) */
+    TPT_OP_ADD_ACT = 5,         /* out[d0] = act(in0 + in1) (residual add) */
+    TPT_OP_SOFTMAX = 6,         /* rows d0 of length d1 (Backend::softmax) */
+    TPT_OP_LAYERNORM = 7,       /* rows d0 of d1; in1 gamma, in2 beta; eps f0 */
+    TPT_OP_ATTENTION = 8,       /* in0 qkv [d0*d1, 3*d2*d3] -> out [d0*d1, d2*d3]; B=d0 S=d1 H=d2 D=d3; scale f0 */
+    TPT_OP_NCHW_TO_NHWC_Q8 = 9, /* in0 f32 NCHW [d0, d1, d2=H*W] -> out i8 NHWC, per-tensor scale */
+    TPT_OP_IM2COL = 10,         /* in0 i8 NHWC -> out i8 [N*OH*OW, Kp]; d0..d12 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW,Kp */
+    TPT_OP_MAXPOOL_NHWC = 11,   /* f32; d0..d11 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW */
+    TPT_OP_GAP_NHWC = 12        /* f32 [d0, d1=H*W, d2] -> [d0, d2] */
+};
+
+typedef struct tpt_plan_op {
+    int kind;
+    int in0, in1, in2, out;     /* tensor ids, -1 = unused */
+    const tpt_cuda_weights *w;  /* LINEAR_W8A8 */
+    int act;                    /* tpt_act */
+    float f0;                   /* static scale / eps / attention scale */
+    size_t dims[16];
+} tpt_plan_op;
+
+int tpt_cuda_plan_create(tpt_cuda_ctx *ctx, tpt_cuda_plan **out);
+int tpt_cuda_plan_destroy(tpt_cuda_plan *plan);
+/* an activation tensor in the arena (dtype TPT_DT_F32 / TPT_DT_I8) */
+int tpt_cuda_plan_add_tensor(tpt_cuda_plan *plan, int dtype, size_t numel, int *id);
+/* an f32 constant, uploaded now (weights of f32 MatMuls, biases, LN params) */
+int tpt_cuda_plan_add_const(tpt_cuda_plan *plan, const float *host, size_t numel, int *id);
+int tpt_cuda_plan_add_op(tpt_cuda_plan *plan, const tpt_plan_op *op);
+/* lays the arena out and allocates it (the only allocation of a run) */
+int tpt_cuda_plan_finalize(tpt_cuda_plan *plan);
+int tpt_cuda_plan_arena_bytes(tpt_cuda_plan *plan, size_t *bytes);
+int tpt_cuda_plan_tensor_ptr(tpt_cuda_plan *plan, int id, void **dev);
+int tpt_cuda_plan_set_calibration(tpt_cuda_plan *plan, int on);
+int tpt_cuda_plan_freeze_scales(tpt_cuda_plan *plan);
+/* The static scales of the quantization points, in op order (0 = none yet);
+ * *count receives the number of points. Lets a calibration be exported. */
+int tpt_cuda_plan_get_scales(tpt_cuda_plan *plan, float *scales, size_t n, size_t *count);
+/* ops only, inputs already resident (async) */
+int tpt_cuda_plan_run_device(tpt_cuda_plan *plan);
+/* H2D of the inputs, the ops, D2H of the outputs, then synchronise */
+int tpt_cuda_plan_run(tpt_cuda_plan *plan, const int *in_ids, const float *const *inputs, size_t n_in,
+                      const int *out_ids, float *const *outputs, size_t n_out);
+
+/* ------------------------------------------------------------------ */
 /* Allocation-free quantization                                         */
 /* ------------------------------------------------------------------ */
 

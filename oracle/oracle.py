@@ -101,6 +101,8 @@ _sig("tpto_w8a8_gemm", None, _i8p, _i8p, _sz, _sz, _sz, C.c_float, _f32p, C.c_vo
 _sig("tpto_w8a8_gemm_refloop", None, _i8p, _i8p, _sz, _sz, _sz, C.c_float, _f32p, C.c_void_p, _f32p,
      _sz, _sz, C.c_int)
 _sig("tpto_requant_i8", C.c_float, C.c_float, C.c_float, C.POINTER(C.c_int8))
+_sig("tpto_quantize_i8_static", None, _f32p, _sz, C.c_float, _i8p)
+_sig("tpto_absmax", C.c_float, _f32p, _sz)
 _sig("tpto_w4_gemm", None, _f32p, _u8p, _f32p, _sz, _sz, _sz, C.c_void_p, C.c_int, _f32p, C.c_int)
 _sig("tpto_max_pool2d", None, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _f32p, _sz, _sz)
 _sig("tpto_average_pool2d", None, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _f32p, _sz, _sz)
@@ -347,6 +349,24 @@ def w8a8_gemm_refloop(a, b_kn, m, n, k, a_scale, w_scales, bias, rows, threads):
     y = np.zeros(m * n, np.float32)
     _lib.tpto_w8a8_gemm_refloop(a, b_kn, m, n, k, a_scale, w_scales, _ptr_or_none(bias), y, 0, rows, threads)
     return y
+
+
+def quantize_i8_static(x, scale):
+    x = _f32(x).ravel()
+    q = np.empty(x.size, np.int8)
+    _lib.tpto_quantize_i8_static(x, x.size, np.float32(scale), q)
+    return q
+
+
+def absmax(x):
+    x = _f32(x).ravel()
+    return np.float32(_lib.tpto_absmax(x, x.size))
+
+
+def sym_scale(m):
+    """quantize_i8_symmetric's scale rule (quant.rs:27-31) for a max |x|."""
+    m = np.float32(m)
+    return np.float32(1.0) if m == 0 else np.float32(m / np.float32(127.0))
 
 
 def requant_i8(y, out_scale):

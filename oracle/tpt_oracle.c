@@ -504,6 +504,15 @@ void tpto_w8a8_gemm_refloop(const int8_t *a, const int8_t *b_kn, size_t m, size_
         }
 }
 
+/* q = clamp(round(x / scale), -127, 127) with a given (static) scale: the
+ * per-element rule of quant.rs:32-38. */
+void tpto_quantize_i8_static(const float *x, size_t n, float scale, int8_t *q) {
+    for (size_t i = 0; i < n; i++) q[i] = clamp_cast_i8(roundf(x[i] / scale), -127.0f, 127.0f);
+}
+
+/* max |x| (NaN ignored), the fold of quant.rs:26 */
+float tpto_absmax(const float *x, size_t n) { return max_abs(x, n); }
+
 /* Requantisation of an epilogue value for the next quantized op:
  * q = clamp(round(y / s), -127, 127), the rule of quant.rs:35-36. */
 float tpto_requant_i8(float y, float out_scale, int8_t *q) {

@@ -105,6 +105,8 @@ void tpto_w8a8_gemm_refloop(const int8_t *a, const int8_t *b_kn, size_t m, size_
                             float a_scale, const float *w_scales, const float *bias,
                             float *y, size_t row0, size_t row1, int threads);
 float tpto_requant_i8(float y, float out_scale, int8_t *q);
+void tpto_quantize_i8_static(const float *x, size_t n, float scale, int8_t *q);
+float tpto_absmax(const float *x, size_t n);
 /* W4 reference: dequantize_i4_symmetric_per_channel (dequant.rs:56-71) then the
  * f32 matmul of avx512.rs:55-78, with W^T nibble rows [N, ceil(K/2)]. */
 void tpto_w4_gemm(const float *x, const uint8_t *wt_packed, const float *w_scales,

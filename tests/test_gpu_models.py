@@ -1,0 +1,111 @@
+"""Model-level GPU parity: the device-resident plans against the oracle's
+node-by-node replay of the same graphs (oracle/models.py).
+
+MLP (f32): logits bit-exact (f32 MatMul is bit-identical to naive.rs), softmax
+within 1e-5*(1+|want|). MLP (INT8 PTQ) and the ResNet-18-shaped CNN: the
+calibrated activation scales and the logits are bit-exact -- every op on those
+paths (quantize, W8A8 GEMM, bias/ReLU, max pool, residual add, sequential
+global average pool, f32 MatMul) is exact. BERT-shaped encoder: attention and
+LayerNorm sum in a different order (and use CUDA expf/tanhf), so it is
+checked with the GPU's frozen scales given to the oracle, at relative L2
+error <= 5e-3 of the final hidden states.
+"""
+import numpy as np
+import pytest
+
+from oracle import models as OM
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _relerr(got, want):
+    return float(np.linalg.norm(got.astype(np.float64) - want) / max(np.linalg.norm(want.astype(np.float64)), 1e-30))
+
+
+def test_mlp_f32_plan(cuda):
+    from tpt_infer_b200 import graphs, synth
+
+    W = graphs.mlp_weights()
+    p, x, y, z = graphs.build_mlp_f32(cuda, 64, W)
+    xin = synth.uniform(64 * 784, 77)  # U[0,1)
+    got_y, got_z = p.run({x: xin}, [y, z])
+    h = O.matmul(xin, (64, 784), W.w1, (784, 512))
+    h = np.where(O.add_bias_rows(h, 64, 512, W.b1) > 0, O.add_bias_rows(h, 64, 512, W.b1), 0).astype(np.float32)
+    want_z = O.add_bias_rows(O.matmul(h, (64, 512), W.w2, (512, 10)), 64, 10, W.b2)
+    assert np.array_equal(got_z, want_z)
+    want_y = OM.mlp_f32(xin, W, 64)
+    assert np.all(np.abs(got_y - want_y) <= 1e-5 * (1 + np.abs(want_y)))
+    p.close()
+
+
+def test_mlp_int8_plan_calibration_and_parity(cuda):
+    from tpt_infer_b200 import graphs, synth
+
+    W = graphs.mlp_weights()
+    p, x, y, z, q = graphs.build_mlp_int8(cuda, 64, W)
+    # the device-quantized weights equal the oracle's per-channel quantization
+    q1o, s1o = O.quantize_i8_symmetric_per_channel(np.ascontiguousarray(W.w1.T), 512)
+    assert np.array_equal(q[0], q1o) and np.array_equal(q[1], s1o)
+    cal = [synth.uniform(64 * 784, 1000 + i) for i in range(4)]  # 256 seeded inputs
+    p.calibrate(True)
+    for xb in cal:
+        p.run({x: xb}, [y])
+    p.freeze()
+    want_scales = OM.mlp_int8_calibrate(cal, W, 64, q)
+    assert np.array_equal(p.scales(), np.array(want_scales, np.float32))
+    xin = synth.uniform(64 * 784, 77)
+    got_y, got_z = p.run({x: xin}, [y, z])
+    q1, s1, q2, s2 = q
+    a1, a2 = want_scales
+    hq = O.quantize_i8_static(O.w8a8_gemm(O.quantize_i8_static(xin, a1), q1, 64, 512, 784, a1, s1, W.b1,
+                                          O.ACT_RELU), a2)
+    want_z = O.w8a8_gemm(hq, q2, 64, 10, 512, a2, s2, W.b2, O.ACT_NONE)
+    assert np.array_equal(got_z, want_z)
+    want_y = OM.mlp_int8(xin, W, 64, q, want_scales)
+    assert np.all(np.abs(got_y - want_y) <= 1e-5 * (1 + np.abs(want_y)))
+    # and the INT8 classifier agrees with the f32 one on most rows
+    pf, xf, yf, _ = graphs.build_mlp_f32(cuda, 64, W)
+    f32_y, = pf.run({xf: xin}, [yf])
+    agree = np.mean(np.argmax(f32_y.reshape(64, 10), 1) == np.argmax(got_y.reshape(64, 10), 1))
+    assert agree >= 0.9
+    p.close()
+    pf.close()
+
+
+def test_resnet18_plan_bit_exact_batch2(cuda):
+    from tpt_infer_b200 import graphs, synth
+
+    spec = graphs.resnet18_weights(cuda)
+    p, x, logits = graphs.build_resnet18(cuda, 2, spec)
+    xcal = synth.normal(2 * 3 * 224 * 224, 31)
+    p.calibrate(True)
+    p.run({x: xcal}, [logits])
+    p.freeze()
+    cal = OM._Scales()
+    OM.resnet18(xcal, spec, 2, calib=cal)
+    assert np.array_equal(p.scales(), cal.frozen())
+    xin = synth.normal(2 * 3 * 224 * 224, 32)
+    got, = p.run({x: xin}, [logits])
+    want = OM.resnet18(xin, spec, 2, scales=cal.frozen())
+    assert np.array_equal(got, want), _relerr(got, want)
+    p.close()
+
+
+def test_bert_plan_two_layers(cuda):
+    from tpt_infer_b200 import graphs, synth
+
+    layers = graphs.bert_weights(cuda, layers=2)
+    p, x, out = graphs.build_bert(cuda, 2, 128, layers)
+    xcal = synth.normal(2 * 128 * 768, 41)
+    p.calibrate(True)
+    p.run({x: xcal}, [out])
+    p.freeze()
+    scales = p.scales()
+    assert scales.size == 8 and np.all(scales > 0)
+    xin = synth.normal(2 * 128 * 768, 42)
+    got, = p.run({x: xin}, [out])
+    want = OM.bert(xin, layers, 2, 128, scales=scales)
+    assert np.all(np.isfinite(got))
+    assert _relerr(got, want) <= 5e-3
+    p.close()

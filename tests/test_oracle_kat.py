@@ -322,3 +322,14 @@ def test_requant_rule():
     assert O.requant_i8(2.5, 1.0) == 3 and O.requant_i8(-2.5, 1.0) == -3
     assert O.requant_i8(1e9, 1.0) == 127 and O.requant_i8(-1e9, 1.0) == -127
     assert O.requant_i8(math.nan, 1.0) == 0
+
+
+def test_product_synth_matches_oracle_generators():
+    # tpt_infer_b200.synth restates the same LCG stream (bit-identical uniform)
+    # and Box-Muller (same formula; numpy vs libm transcendental last bits only)
+    from tpt_infer_b200 import synth
+
+    for n, seed in ((1, 3), (17, 4), (100001, 5)):
+        assert np.array_equal(synth.uniform(n, seed), O.lcg_uniform(n, seed))
+        a, b = synth.normal(n, seed, 0.5, 2.0), O.normal(n, seed, 0.5, 2.0)
+        assert np.max(np.abs(a - b)) <= 1e-6 * (1 + np.max(np.abs(b)))

@@ -74,7 +74,27 @@ SIGNATURES = {
     "tpt_cuda_w4_gemm": (C.c_int, [ctxp, vp, sz, sz, wp, vp, C.c_int, vp]),
     "tpt_cuda_w4_gemm_dev": (C.c_int, [ctxp, vp, sz, wp, vp, C.c_int, vp]),
     "tpt_cuda_quantize_i8_symmetric_noalloc": (C.c_int, [vp, sz, vp, vp, vp]),
+    "tpt_cuda_plan_create": (C.c_int, [ctxp, C.POINTER(vp)]),
+    "tpt_cuda_plan_destroy": (C.c_int, [vp]),
+    "tpt_cuda_plan_add_tensor": (C.c_int, [vp, C.c_int, sz, C.POINTER(C.c_int)]),
+    "tpt_cuda_plan_add_const": (C.c_int, [vp, vp, sz, C.POINTER(C.c_int)]),
+    "tpt_cuda_plan_add_op": (C.c_int, [vp, vp]),
+    "tpt_cuda_plan_finalize": (C.c_int, [vp]),
+    "tpt_cuda_plan_arena_bytes": (C.c_int, [vp, szp]),
+    "tpt_cuda_plan_tensor_ptr": (C.c_int, [vp, C.c_int, C.POINTER(vp)]),
+    "tpt_cuda_plan_set_calibration": (C.c_int, [vp, C.c_int]),
+    "tpt_cuda_plan_freeze_scales": (C.c_int, [vp]),
+    "tpt_cuda_plan_get_scales": (C.c_int, [vp, vp, sz, szp]),
+    "tpt_cuda_plan_run_device": (C.c_int, [vp]),
+    "tpt_cuda_plan_run": (C.c_int, [vp, vp, vp, sz, vp, vp, sz]),
 }
+
+
+class PlanOp(C.Structure):
+    """tpt_plan_op (include/tpt_cuda.h)."""
+
+    _fields_ = [("kind", C.c_int), ("in0", C.c_int), ("in1", C.c_int), ("in2", C.c_int), ("out", C.c_int),
+                ("w", C.c_void_p), ("act", C.c_int), ("f0", C.c_float), ("dims", C.c_size_t * 16)]
 
 for _name, (_res, _args) in SIGNATURES.items():
     _fn = getattr(lib, _name)

@@ -38,9 +38,9 @@ struct tpt_cuda_weights {
     float *scales = nullptr;  // device: n per-channel scales
     size_t bytes = 0;
     // TMA descriptors of the int8 weight (CUtensorMap, 128 bytes each), built
-    // once: box of 256 rows (one-SM kernel) and of 128 rows (SM-pair kernel)
-    alignas(64) unsigned char tmap[128];
-    alignas(64) unsigned char tmap128[128];
+    // once: boxes of 256 rows (one-SM kernel) and of 128 / 64 / 32 rows (the
+    // SM-pair kernel's B half-tiles for tile N = 256 / 128 / 64)
+    alignas(64) unsigned char tmaps[4][128];
     bool tmap_ok = false;
 };
 

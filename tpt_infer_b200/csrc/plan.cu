@@ -1,0 +1,332 @@
+// plan.cu -- device-resident execution plans: the device counterpart of
+// tpt-infer's execute_graph (crates/tpt-infer-runtime/src/exec.rs:570-635).
+//
+// The reference lays every non-input node's activation out at a disjoint
+// offset of one arena slice in topological order (assign_offsets,
+// exec.rs:276-294; one alloc_slice, exec.rs:595), runs the nodes in that order
+// and copies the marked outputs out at the end. A plan does the same on the
+// device: tensors get disjoint 256-byte-aligned offsets in ONE device
+// allocation made at finalize, constants (f32 weights, biases, LayerNorm
+// parameters) are uploaded once, ops run in order on the context's stream, and
+// host<->device copies happen only at graph inputs and outputs.
+//
+// INT8 activation quantization points carry a per-tensor scale. A plan in
+// calibration mode measures max|x| at every quantization point on each run
+// (the quantize_i8_symmetric rule, quant.rs:25-31, applied to the running
+// max); tpt_cuda_plan_freeze_scales turns the maxima into static scales.
+#include <string.h>
+
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+
+namespace tpt {
+int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
+                     size_t cols, float eps);
+int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale);
+int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
+int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act);
+int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, float scale);
+int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H, int W, int C, int KH, int KW, int sh,
+                  int sw, int ph, int pw, int OH, int OW, int Kp);
+int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
+                        int sw, int ph, int pw, int OH, int OW);
+int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, int C);
+int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell);
+}  // namespace tpt
+
+using namespace tpt;
+
+struct PlanTensor {
+    int dtype = TPT_DT_F32;
+    size_t numel = 0;
+    size_t offset = 0;      // arena offset (activations)
+    void *ptr = nullptr;    // device pointer (set at finalize / for constants)
+    bool is_const = false;
+    float scale = 0.0f;     // INT8 tensors: the per-tensor scale in effect
+};
+
+struct PlanOp {
+    tpt_plan_op op;
+    int cell = -1;          // calibration cell index (quantization points)
+    float frozen = 0.0f;    // static scale once frozen (or given)
+};
+
+struct tpt_cuda_plan {
+    tpt_cuda_ctx *ctx = nullptr;
+    std::vector<PlanTensor> tensors;
+    std::vector<PlanOp> ops;
+    char *arena = nullptr;
+    size_t arena_bytes = 0;
+    unsigned *cells = nullptr;  // device: one max-abs word per quantization point
+    std::vector<float> cal_max; // host: running max per quantization point
+    int n_cells = 0;
+    bool finalized = false;
+    bool calibrating = false;
+};
+
+namespace {
+
+size_t dt_size(int dt) { return dt == TPT_DT_I8 ? 1 : 4; }
+
+bool valid_id(tpt_cuda_plan *p, int id) { return id >= 0 && (size_t)id < p->tensors.size(); }
+
+float *F(tpt_cuda_plan *p, int id) { return id < 0 ? nullptr : static_cast<float *>(p->tensors[id].ptr); }
+int8_t *Q(tpt_cuda_plan *p, int id) { return id < 0 ? nullptr : static_cast<int8_t *>(p->tensors[id].ptr); }
+
+// Scale for a quantization point: frozen/static, or (calibrating) measured now.
+int point_scale(tpt_cuda_plan *p, PlanOp &po, const float *x, size_t n, float *scale) {
+    if (!p->calibrating) {
+        if (!(po.frozen > 0.0f)) return TPT_INVALID;  // not calibrated and no static scale given
+        *scale = po.frozen;
+        return TPT_OK;
+    }
+    tpt_cuda_ctx *ctx = p->ctx;
+    unsigned *cell = p->cells + po.cell;
+    cudaError_t e = cudaMemsetAsync(cell, 0, 4, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "calibration cell clear");
+    int st = launch_absmax_acc(ctx, x, n, cell);
+    if (st) return st;
+    unsigned bits = 0;
+    st = d2h(ctx, &bits, cell, 4);
+    if (st) return st;
+    st = sync_and_check(ctx);
+    if (st) return st;
+    float m;
+    memcpy(&m, &bits, 4);
+    if (m > p->cal_max[po.cell]) p->cal_max[po.cell] = m;
+    // quantize_i8_symmetric's rule (quant.rs:27-31) on this run's max
+    *scale = m == 0.0f ? 1.0f : m / 127.0f;
+    return TPT_OK;
+}
+
+int run_op(tpt_cuda_plan *p, PlanOp &po) {
+    tpt_cuda_ctx *ctx = p->ctx;
+    const tpt_plan_op &o = po.op;
+    const size_t *d = o.dims;
+    int st = TPT_OK;
+    switch (o.kind) {
+        case TPT_OP_QUANTIZE: {  // f32 [n] -> i8 [n], per-tensor scale
+            float s;
+            st = point_scale(p, po, F(p, o.in0), d[0], &s);
+            if (st) return st;
+            p->tensors[o.out].scale = s;
+            return launch_quant_i8_static(ctx, F(p, o.in0), d[0], s, Q(p, o.out));
+        }
+        case TPT_OP_NCHW_TO_NHWC_Q8: {  // f32 NCHW [N,C,HW] -> i8 NHWC
+            float s;
+            st = point_scale(p, po, F(p, o.in0), d[0] * d[1] * d[2], &s);
+            if (st) return st;
+            p->tensors[o.out].scale = s;
+            return launch_nchw_to_nhwc_q8(ctx, F(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], s);
+        }
+        case TPT_OP_LINEAR_W8A8: {  // i8 [rows, K] x W^T -> f32 [rows, N] (+bias, act)
+            const float sa = p->tensors[o.in0].scale;
+            return launch_w8a8(ctx, Q(p, o.in0), d[0], o.w->k, o.w, sa, F(p, o.in1), o.act, F(p, o.out), nullptr);
+        }
+        case TPT_OP_MATMUL_F32: {  // [m,k] x [k,n] (+bias, act)
+            st = launch_matmul_f32(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], d[1], d[2]);
+            if (st || (o.in2 < 0 && o.act == 0)) return st;
+            return launch_bias_act(ctx, F(p, o.out), F(p, o.in2), F(p, o.out), d[0], d[2], o.act);
+        }
+        case TPT_OP_BIAS_ACT:
+            return launch_bias_act(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], d[1], o.act);
+        case TPT_OP_ADD_ACT:
+            return launch_add_act(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], o.act);
+        case TPT_OP_SOFTMAX:
+            return launch_softmax(ctx, F(p, o.in0), F(p, o.out), d[0], d[1]);
+        case TPT_OP_LAYERNORM:
+            return launch_layernorm(ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), F(p, o.out), d[0], d[1], o.f0);
+        case TPT_OP_ATTENTION:
+            return launch_attention(ctx, F(p, o.in0), F(p, o.out), (int)d[0], (int)d[1], (int)d[2], (int)d[3], o.f0);
+        case TPT_OP_IM2COL:  // dims: N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW,Kp
+            p->tensors[o.out].scale = p->tensors[o.in0].scale;
+            return launch_im2col(ctx, Q(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], (int)d[3], (int)d[4],
+                                 (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10], (int)d[11],
+                                 (int)d[12]);
+        case TPT_OP_MAXPOOL_NHWC:
+            return launch_maxpool_nhwc(ctx, F(p, o.in0), F(p, o.out), (int)d[0], (int)d[1], (int)d[2], (int)d[3],
+                                       (int)d[4], (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10],
+                                       (int)d[11]);
+        case TPT_OP_GAP_NHWC:
+            return launch_gap_nhwc(ctx, F(p, o.in0), F(p, o.out), (int)d[0], (int)d[1], (int)d[2]);
+        default:
+            return TPT_UNSUPPORTED;
+    }
+}
+
+}  // namespace
+
+#define CHECK_PLAN(pl)                                  \
+    do {                                                \
+        if (!(pl) || !(pl)->ctx) return TPT_INVALID;    \
+        cudaSetDevice((pl)->ctx->device);               \
+    } while (0)
+
+extern "C" {
+
+int tpt_cuda_plan_create(tpt_cuda_ctx *ctx, tpt_cuda_plan **out) {
+    if (!ctx || !out) return TPT_INVALID;
+    tpt_cuda_plan *p = new (std::nothrow) tpt_cuda_plan();
+    if (!p) return TPT_OUT_OF_MEMORY;
+    p->ctx = ctx;
+    *out = p;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_destroy(tpt_cuda_plan *p) {
+    if (!p) return TPT_INVALID;
+    cudaSetDevice(p->ctx->device);
+    cudaStreamSynchronize(p->ctx->stream);
+    if (p->arena) cudaFree(p->arena);
+    if (p->cells) cudaFree(p->cells);
+    for (auto &t : p->tensors)
+        if (t.is_const && t.ptr) cudaFree(t.ptr);
+    delete p;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_add_tensor(tpt_cuda_plan *p, int dtype, size_t numel, int *id) {
+    CHECK_PLAN(p);
+    if (p->finalized || !id || (dtype != TPT_DT_F32 && dtype != TPT_DT_I8)) return TPT_INVALID;
+    PlanTensor t;
+    t.dtype = dtype;
+    t.numel = numel;
+    p->tensors.push_back(t);
+    *id = (int)p->tensors.size() - 1;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_add_const(tpt_cuda_plan *p, const float *host, size_t numel, int *id) {
+    CHECK_PLAN(p);
+    if (!id || (!host && numel)) return TPT_INVALID;
+    PlanTensor t;
+    t.numel = numel;
+    t.is_const = true;
+    cudaError_t e = cudaMalloc(&t.ptr, numel ? numel * 4 : 4);
+    if (e == cudaSuccess && numel) e = cudaMemcpy(t.ptr, host, numel * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (t.ptr) cudaFree(t.ptr);
+        return cuda_fail(p->ctx, e, "plan constant upload");
+    }
+    p->tensors.push_back(t);
+    *id = (int)p->tensors.size() - 1;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_add_op(tpt_cuda_plan *p, const tpt_plan_op *op) {
+    CHECK_PLAN(p);
+    if (!op || p->finalized) return TPT_INVALID;
+    if (!valid_id(p, op->in0) || !valid_id(p, op->out)) return TPT_INVALID;
+    if ((op->in1 >= 0 && !valid_id(p, op->in1)) || (op->in2 >= 0 && !valid_id(p, op->in2))) return TPT_INVALID;
+    if (op->kind == TPT_OP_LINEAR_W8A8 && (!op->w || op->w->kind != 8)) return TPT_INVALID;
+    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_GAP_NHWC) return TPT_UNSUPPORTED;
+    PlanOp po;
+    po.op = *op;
+    if (op->kind == TPT_OP_QUANTIZE || op->kind == TPT_OP_NCHW_TO_NHWC_Q8) {
+        po.cell = p->n_cells++;
+        po.frozen = op->f0;  // > 0: a static scale given by the caller
+    }
+    p->ops.push_back(po);
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
+    CHECK_PLAN(p);
+    if (p->finalized) return TPT_INVALID;
+    size_t off = 0;
+    for (auto &t : p->tensors) {
+        if (t.is_const) continue;
+        t.offset = off;
+        off += (t.numel * dt_size(t.dtype) + 255) & ~size_t(255);
+    }
+    p->arena_bytes = off;
+    cudaError_t e = cudaMalloc(&p->arena, off ? off : 256);
+    if (e == cudaSuccess) e = cudaMalloc(&p->cells, (size_t)(p->n_cells ? p->n_cells : 1) * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(p->ctx, e, "plan arena");
+    }
+    for (auto &t : p->tensors)
+        if (!t.is_const) t.ptr = p->arena + t.offset;
+    p->cal_max.assign(p->n_cells, 0.0f);
+    p->finalized = true;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_arena_bytes(tpt_cuda_plan *p, size_t *bytes) {
+    if (!p || !bytes) return TPT_INVALID;
+    *bytes = p->arena_bytes;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_tensor_ptr(tpt_cuda_plan *p, int id, void **dev) {
+    CHECK_PLAN(p);
+    if (!p->finalized || !valid_id(p, id) || !dev) return TPT_INVALID;
+    *dev = p->tensors[id].ptr;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_set_calibration(tpt_cuda_plan *p, int on) {
+    CHECK_PLAN(p);
+    p->calibrating = on != 0;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_freeze_scales(tpt_cuda_plan *p) {
+    CHECK_PLAN(p);
+    for (auto &po : p->ops)
+        if (po.cell >= 0 && !(po.op.f0 > 0.0f)) {
+            const float m = p->cal_max[po.cell];
+            po.frozen = m == 0.0f ? 1.0f : m / 127.0f;
+        }
+    p->calibrating = false;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_get_scales(tpt_cuda_plan *p, float *scales, size_t n, size_t *count) {
+    CHECK_PLAN(p);
+    size_t c = 0;
+    for (auto &po : p->ops)
+        if (po.cell >= 0) {
+            if (scales && c < n) scales[c] = po.frozen;
+            c++;
+        }
+    if (count) *count = c;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_run_device(tpt_cuda_plan *p) {
+    CHECK_PLAN(p);
+    if (!p->finalized) return TPT_INVALID;
+    for (auto &po : p->ops) {
+        int st = run_op(p, po);
+        if (st) return st;
+    }
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *inputs, size_t n_in,
+                      const int *out_ids, float *const *outputs, size_t n_out) {
+    CHECK_PLAN(p);
+    if (!p->finalized) return TPT_INVALID;
+    for (size_t i = 0; i < n_in; i++) {
+        if (!valid_id(p, in_ids[i])) return TPT_INVALID;
+        const PlanTensor &t = p->tensors[in_ids[i]];
+        int st = h2d(p->ctx, t.ptr, inputs[i], t.numel * dt_size(t.dtype));
+        if (st) return st;
+    }
+    int st = tpt_cuda_plan_run_device(p);
+    if (st) return st;
+    for (size_t i = 0; i < n_out; i++) {
+        if (!valid_id(p, out_ids[i])) return TPT_INVALID;
+        const PlanTensor &t = p->tensors[out_ids[i]];
+        st = d2h(p->ctx, outputs[i], t.ptr, t.numel * dt_size(t.dtype));
+        if (st) return st;
+    }
+    return sync_and_check(p->ctx);
+}
+
+}  // extern "C"

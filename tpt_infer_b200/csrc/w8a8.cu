@@ -6,7 +6,7 @@
 // kept separate (no FMA) so the f32 output is bit-exact with the oracle.
 //
 // Kernels here:
-//  - k_w8a8_gemv: small M (<= 8). One warp per output channel streams the
+//  - k_w8a8_gemv: small M (<= 16). One warp per output channel streams the
 //    K-contiguous weight row with 128-bit loads and dp4a; HBM-bound by design.
 //  - k_w8a8_simt: general shapes (ragged M/N, K % 16 == 0); dp4a tiles.
 //  - the tcgen05 tensor-core kernel for large M lives in w8a8_tc.cu.
@@ -196,7 +196,7 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     const int8_t *wt = (const int8_t *)w->data;
-    if (m <= 8) {
+    if (m <= 16) {
         unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
 #define TPT_GEMV(MM) \
     k_w8a8_gemv<MM><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc)
@@ -206,8 +206,10 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
             TPT_GEMV(2);
         else if (m <= 4)
             TPT_GEMV(4);
-        else
+        else if (m <= 8)
             TPT_GEMV(8);
+        else
+            TPT_GEMV(16);
 #undef TPT_GEMV
         return after_launch(ctx, "w8a8_gemv");
     }

@@ -402,18 +402,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // 8 epilogue warps per CTA: two per TMEM lane quarter, each taking half of
 // the 256 accumulator columns.
 // ---------------------------------------------------------------------------
-constexpr int P_BN = 256;                 // tile N (MMA N)
 constexpr int P_BM = 256;                 // tile M (MMA M over the pair)
-constexpr int P_STAGES = 5;
 constexpr int P_EPI_WARPS = 8;
 constexpr int P_THREADS = (2 + P_EPI_WARPS) * 32;
 constexpr int P_A_BYTES = 128 * TC_BK;    // this CTA's 128 rows of A
-constexpr int P_B_BYTES = 128 * TC_BK;    // this CTA's 128 rows of B
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_OUT_BYTES = P_EPI_WARPS * 2 * 4096;
-constexpr int P_TMEM_COLS = 2 * P_BN;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + P_OUT_BYTES + (2 * P_STAGES + 5) * 8 + 16 + 1024;
-static_assert(P_SMEM_BYTES <= 232448, "dynamic shared memory per CTA");
+
+// Tile N (the MMA's N) is a template parameter: 64, 128 or 256. Each CTA holds
+// BN/2 rows of B per stage; the ring is sized to ~160 KB.
+template <int BN>
+struct PairCfg {
+    static constexpr int B_BYTES = (BN / 2) * TC_BK;
+    static constexpr int STAGE_BYTES = P_A_BYTES + B_BYTES;
+    static constexpr int STAGES_RAW = 163840 / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + P_OUT_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
+    static_assert(SMEM_BYTES <= 232448, "dynamic shared memory per CTA");
+    static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -457,20 +464,21 @@ __device__ __forceinline__ void tc2_commit_both(uint32_t bar) {
         : "memory");
 }
 
-template <bool ACC_OUT>
+template <int BN, bool ACC_OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_w8a8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
                const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
                int32_t *__restrict__ ACC, unsigned *gflags) {
-    constexpr int S = P_STAGES;
+    using Cfg = PairCfg<BN>;
+    constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int abort_flag;
     __shared__ uint32_t tmem_slot;
 
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ring = (raw + 1023u) & ~1023u;
-    const uint32_t staging = ring + S * P_STAGE_BYTES;
+    const uint32_t staging = ring + S * Cfg::STAGE_BYTES;
     const uint32_t bars = staging + P_OUT_BYTES;
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
@@ -482,7 +490,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-    const int tiles_m = (M + P_BM - 1) / P_BM, tiles_n = (N + P_BN - 1) / P_BN;
+    const int tiles_m = (M + P_BM - 1) / P_BM, tiles_n = (N + BN - 1) / BN;
     const int ntiles = tiles_m * tiles_n;
     const int kblocks = (K + TC_BK - 1) / TC_BK;
 
@@ -503,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"((uint32_t)P_TMEM_COLS)
+                     "r"((uint32_t)Cfg::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
@@ -521,15 +529,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             bool ok = true;
             for (int t = cluster; t < ntiles && ok; t += nclusters) {
                 const int mt = t / tiles_n, nt = t - mt * tiles_n;
-                const int arow = mt * P_BM + (int)rank * 128, brow = nt * P_BN + (int)rank * 128;
+                const int arow = mt * P_BM + (int)rank * 128, brow = nt * BN + (int)rank * (BN / 2);
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
                         ok = false;
                         break;
                     }
-                    const uint32_t a_dst = ring + stage * P_STAGE_BYTES;
+                    const uint32_t a_dst = ring + stage * Cfg::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(full_bar(stage), 0);
-                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * P_STAGE_BYTES);
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::STAGE_BYTES);
                     tma_load_2d_pair(a_dst, &tmA, fb, kb * TC_BK, arow);
                     tma_load_2d_pair(a_dst + P_A_BYTES, &tmB, fb, kb * TC_BK, brow);
                     if (++stage == S) {
@@ -542,7 +550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             // ---------------- MMA issuer (leader CTA only) ----------------
-            constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(P_BN >> 3) << 17) |
+            constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                        ((uint32_t)(P_BM >> 4) << 24);
             int stage = 0;
             uint32_t phase = 0;
@@ -552,14 +560,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             for (int t = cluster; t < ntiles && ok; t += nclusters) {
                 if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)(acc * P_BN);
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(full_bar(stage), phase, abort_p, gflags, true)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = ring + stage * P_STAGE_BYTES;
+                    const uint32_t a_addr = ring + stage * Cfg::STAGE_BYTES;
                     const uint32_t b_addr = a_addr + P_A_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 32; kk++)
@@ -588,8 +596,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
         const int e = warp - 2;        // 0..7
         const int q = warp & 3;        // TMEM lane quarter this warp may access
-        const int half = e >> 2;       // which 128 of the 256 columns
-        const int row = q * 32 + lane;
+        const int half = e >> 2;       // which half of the BN accumulator columns
         const uint32_t stage_s = staging + (uint32_t)(e * 8192);
         uint8_t *stage_g = smem_raw + (stage_s - raw);
         const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
@@ -606,13 +613,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             const int mt = t / tiles_n, nt = t - mt * tiles_n;
             const int mrow0 = mt * P_BM + (int)rank * 128 + q * 32;  // first row of this warp's block
             const int m = mrow0 + lane;
-            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * P_BN + half * 128);
+            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + half * (BN / 2));
 #pragma unroll 1
-            for (int c = 0; c < 4; c++) {
+            for (int c = 0; c < BN / 64; c++) {
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
-                const int n0 = nt * P_BN + half * 128 + c * 32;
+                const int n0 = nt * BN + half * (BN / 2) + c * 32;
                 if (!ACC_OUT) {
                     const int nc = n0 + lane < N ? n0 + lane : N - 1;
                     const float sc = __fmul_rn(a_scale, __ldg(wscale + nc));
@@ -673,7 +680,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)P_TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)Cfg::TMEM_COLS)
                      : "memory");
     }
 }
@@ -749,12 +756,14 @@ int launch_tc(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, i
     return after_launch(ctx, "w8a8_tc");
 }
 
-template <bool ACC_OUT>
+template <int BN, bool ACC_OUT>
 int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
                const float *ws, const float *bias, int act, float *y, int32_t *acc) {
+    using Cfg = PairCfg<BN>;
+    constexpr int P_SMEM_BYTES = Cfg::SMEM_BYTES;
     static bool attr_done[64] = {};
     static int max_clusters[64] = {};
-    auto kfn = k_w8a8_tc2<ACC_OUT>;
+    auto kfn = k_w8a8_tc2<BN, ACC_OUT>;
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
@@ -780,7 +789,7 @@ int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, 
         max_clusters[dev] = n;
         attr_done[dev] = true;
     }
-    const int ntiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+    const int ntiles = ((M + P_BM - 1) / P_BM) * ((N + BN - 1) / BN);
     const int pairs = max_clusters[dev];
     const int clusters = ntiles < pairs ? ntiles : pairs;
     CUtensorMap ty;
@@ -794,10 +803,11 @@ int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, 
 }  // namespace
 
 int build_weight_tmap(tpt_cuda_weights *w) {
-    CUtensorMap *tm = reinterpret_cast<CUtensorMap *>(w->tmap);
-    CUtensorMap *tm128 = reinterpret_cast<CUtensorMap *>(w->tmap128);
-    w->tmap_ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff &&
-                 make_tmap_i8(tm, w->data, w->n, w->k, 256) && make_tmap_i8(tm128, w->data, w->n, w->k, 128);
+    bool ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff;
+    const uint32_t rows[4] = {256, 128, 64, 32};
+    for (int i = 0; i < 4 && ok; i++)
+        ok = make_tmap_i8(reinterpret_cast<CUtensorMap *>(w->tmaps[i]), w->data, w->n, w->k, rows[i]);
+    w->tmap_ok = ok;
     return TPT_OK;
 }
 
@@ -811,12 +821,21 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     if (!make_tmap_i8(&ta, a, m, w->k, TC_BM)) return TPT_OK;
     *handled = true;
     if (m >= 256) {
-        // SM-pair kernel (256 x 256 tiles); A and B tensor maps with 128-row boxes
-        const CUtensorMap &tb2 = *reinterpret_cast<const CUtensorMap *>(w->tmap128);
-        if (acc) return launch_tc2<true>(ctx, ta, tb2, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
-        return launch_tc2<false>(ctx, ta, tb2, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
+        // SM-pair kernel, 256 x BN tiles; each CTA's B box holds BN/2 rows
+        const int M = (int)m, N = (int)w->n, K = (int)w->k;
+        const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(w->tmaps);
+        if (N <= 64) {
+            return acc ? launch_tc2<64, true>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc)
+                       : launch_tc2<64, false>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc);
+        }
+        if (N <= 128) {
+            return acc ? launch_tc2<128, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc)
+                       : launch_tc2<128, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc);
+        }
+        return acc ? launch_tc2<256, true>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc)
+                   : launch_tc2<256, false>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc);
     }
-    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmap);
+    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmaps[0]);
     if (acc) return launch_tc<256, true>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
     return launch_tc<256, false>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
 }

@@ -1,0 +1,383 @@
+"""Device-resident plans for the model workloads, over the C ABI's plan API.
+
+``Plan`` wraps ``tpt_cuda_plan_*`` (the device counterpart of tpt-infer's
+``execute_graph``, crates/tpt-infer-runtime/src/exec.rs:570-635). The builders
+lay out the three model workloads the way tpt-infer's runtime would execute
+them node by node, with the quantized-weight path of tpt-infer-quantize:
+
+- ``mlp``: Gemm 784->512, ReLU, Gemm 512->10, Softmax, in f32 (the reference's
+  MatMul/Add/Relu/Softmax nodes) or with INT8 per-output-channel weights and
+  calibrated per-tensor activation scales.
+- ``resnet18``: a ResNet-18-shaped CNN in NHWC: INT8 convolutions as im2col +
+  W8A8 GEMM with fused bias (folded BatchNorm) and ReLU, max pool, residual
+  adds, global average pool, f32 Gemm 512->1000.
+- ``bert``: a BERT-base-shaped encoder: INT8 Q/K/V/O and FFN projections,
+  fused f32 attention, GELU, residual adds, post-LayerNorm.
+
+Weight tensors are synthesised with the seeded generators of ``synth`` and
+quantized on the device with the reference's quantizer rules
+(quantize_i8_symmetric_per_channel, per output channel = per row of W^T).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _capi, synth
+from ._capi import lib
+from .backend import ACT_GELU, ACT_NONE, ACT_RELU, CudaBackend, OpError
+
+F32, I8 = 0, 1
+OP_QUANTIZE, OP_LINEAR, OP_MATMUL, OP_BIAS_ACT, OP_ADD_ACT, OP_SOFTMAX, OP_LAYERNORM, OP_ATTENTION = range(1, 9)
+OP_NCHW_Q8, OP_IM2COL, OP_MAXPOOL, OP_GAP = 9, 10, 11, 12
+
+
+class Plan:
+    """A device-resident execution plan on one CudaBackend context."""
+
+    def __init__(self, be: CudaBackend):
+        self.be = be
+        h = C.c_void_p()
+        be._check(lib.tpt_cuda_plan_create(be.ctx, C.byref(h)))
+        self.h = h
+        self.weights = []  # keep uploaded weight handles alive
+        self.numel = {}
+        self.dtype = {}
+
+    def tensor(self, dtype, numel):
+        i = C.c_int()
+        self.be._check(lib.tpt_cuda_plan_add_tensor(self.h, dtype, int(numel), C.byref(i)))
+        self.numel[i.value] = int(numel)
+        self.dtype[i.value] = dtype
+        return i.value
+
+    def const(self, arr):
+        a = np.ascontiguousarray(arr, np.float32).ravel()
+        i = C.c_int()
+        self.be._check(lib.tpt_cuda_plan_add_const(self.h, a.ctypes.data_as(C.c_void_p), a.size, C.byref(i)))
+        self.numel[i.value] = a.size
+        self.dtype[i.value] = F32
+        return i.value
+
+    def op(self, kind, in0, out, in1=-1, in2=-1, w=None, act=ACT_NONE, f0=0.0, dims=()):
+        o = _capi.PlanOp()
+        o.kind, o.in0, o.in1, o.in2, o.out = kind, in0, in1, in2, out
+        o.w = w.handle if w is not None else None
+        o.act, o.f0 = act, f0
+        for j, d in enumerate(dims):
+            o.dims[j] = int(d)
+        self.be._check(lib.tpt_cuda_plan_add_op(self.h, C.byref(o)))
+
+    def finalize(self):
+        self.be._check(lib.tpt_cuda_plan_finalize(self.h))
+
+    def arena_bytes(self):
+        b = C.c_size_t()
+        lib.tpt_cuda_plan_arena_bytes(self.h, C.byref(b))
+        return b.value
+
+    def ptr(self, tid):
+        p = C.c_void_p()
+        self.be._check(lib.tpt_cuda_plan_tensor_ptr(self.h, tid, C.byref(p)))
+        return p.value
+
+    def calibrate(self, on=True):
+        self.be._check(lib.tpt_cuda_plan_set_calibration(self.h, 1 if on else 0))
+
+    def freeze(self):
+        self.be._check(lib.tpt_cuda_plan_freeze_scales(self.h))
+
+    def scales(self):
+        """Static scales of the quantization points, in op order."""
+        n = C.c_size_t()
+        lib.tpt_cuda_plan_get_scales(self.h, None, 0, C.byref(n))
+        out = np.zeros(n.value, np.float32)
+        lib.tpt_cuda_plan_get_scales(self.h, out.ctypes.data_as(C.c_void_p), n.value, C.byref(n))
+        return out
+
+    def run_device(self):
+        self.be._check(lib.tpt_cuda_plan_run_device(self.h))
+
+    def run(self, inputs: dict, outputs: list):
+        """H2D of ``inputs`` {tensor id: host array}, the ops, D2H of ``outputs``."""
+        ids = list(inputs)
+        arrs = [np.ascontiguousarray(inputs[i], np.float32).ravel() for i in ids]
+        for i, a in zip(ids, arrs):
+            if a.size != self.numel[i]:
+                raise OpError(1, self.numel[i], a.size)
+        outs = [np.empty(self.numel[o], np.float32) for o in outputs]
+        in_ids = (C.c_int * len(ids))(*ids)
+        in_p = (C.c_void_p * len(ids))(*[a.ctypes.data for a in arrs])
+        out_ids = (C.c_int * len(outputs))(*outputs)
+        out_p = (C.c_void_p * len(outputs))(*[a.ctypes.data for a in outs])
+        self.be._check(lib.tpt_cuda_plan_run(self.h, in_ids, in_p, len(ids), out_ids, out_p, len(outputs)))
+        return outs
+
+    def close(self):
+        if self.h:
+            lib.tpt_cuda_plan_destroy(self.h)
+            self.h = None
+        for w in self.weights:
+            w.free()
+        self.weights = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ weights
+@dataclass
+class QLinear:
+    """An INT8 per-output-channel weight: W^T [n, k] quantized row by row."""
+
+    n: int
+    k: int
+    q: np.ndarray        # int8 [n, k]
+    scales: np.ndarray   # f32 [n]
+    bias: np.ndarray     # f32 [n]
+
+
+def make_qlinear(be, n, k, seed, std, bias_std=0.0, kp=None):
+    """W ~ N(0, std) with W^T [n, k]; quantize_i8_symmetric_per_channel(W^T, rows=n)
+    (crates/tpt-infer-quantize/src/quant.rs:95-107) on the device. kp pads k with
+    zero columns."""
+    wt = synth.normal(n * k, seed, 0.0, std)
+    q, s = be.quantize_i8_symmetric_per_channel(wt, n)
+    q = q.reshape(n, k)
+    if kp is not None and kp != k:
+        qp = np.zeros((n, kp), np.int8)
+        qp[:, :k] = q
+        q = qp
+    b = synth.normal(n, seed + 7919, 0.0, bias_std) if bias_std > 0 else np.zeros(n, np.float32)
+    return QLinear(n, q.shape[1], np.ascontiguousarray(q), s, b)
+
+
+# ------------------------------------------------------------------ MLP
+@dataclass
+class MlpWeights:
+    w1: np.ndarray  # [784, 512]
+    b1: np.ndarray
+    w2: np.ndarray  # [512, 10]
+    b2: np.ndarray
+
+
+def mlp_weights(seed=10):
+    """The MLP workload: W1 ~ N(0, 0.036) [784,512], b1 = 0; W2 ~ N(0, 0.06) [512,10], b2 = 0."""
+    return MlpWeights(synth.normal(784 * 512, seed, 0.0, 0.036).reshape(784, 512), np.zeros(512, np.float32),
+                      synth.normal(512 * 10, seed + 1, 0.0, 0.06).reshape(512, 10), np.zeros(10, np.float32))
+
+
+def build_mlp_f32(be, batch, W: MlpWeights):
+    p = Plan(be)
+    x = p.tensor(F32, batch * 784)
+    h = p.tensor(F32, batch * 512)
+    z = p.tensor(F32, batch * 10)
+    y = p.tensor(F32, batch * 10)
+    w1, b1, w2, b2 = p.const(W.w1), p.const(W.b1), p.const(W.w2), p.const(W.b2)
+    p.op(OP_MATMUL, x, h, in1=w1, in2=b1, act=ACT_RELU, dims=(batch, 784, 512))
+    p.op(OP_MATMUL, h, z, in1=w2, in2=b2, dims=(batch, 512, 10))
+    p.op(OP_SOFTMAX, z, y, dims=(batch, 10))
+    p.finalize()
+    return p, x, y, z
+
+
+def build_mlp_int8(be, batch, W: MlpWeights):
+    """INT8 PTQ variant: W1, W2 per output channel (quantize W^T rows); activations
+    per tensor with calibrated static scales."""
+    p = Plan(be)
+    q1, s1 = be.quantize_i8_symmetric_per_channel(np.ascontiguousarray(W.w1.T), 512)
+    q2, s2 = be.quantize_i8_symmetric_per_channel(np.ascontiguousarray(W.w2.T), 10)
+    wh1 = be.upload_i8(q1, s1, 512, 784)  # K = 784 and 512 are multiples of 16
+    wh2 = be.upload_i8(q2, s2, 10, 512)
+    p.weights += [wh1, wh2]
+    x = p.tensor(F32, batch * 784)
+    xq = p.tensor(I8, batch * 784)
+    h = p.tensor(F32, batch * 512)
+    hq = p.tensor(I8, batch * 512)
+    z = p.tensor(F32, batch * 10)
+    y = p.tensor(F32, batch * 10)
+    b1, b2 = p.const(W.b1), p.const(W.b2)
+    p.op(OP_QUANTIZE, x, xq, dims=(batch * 784,))
+    p.op(OP_LINEAR, xq, h, in1=b1, w=wh1, act=ACT_RELU, dims=(batch,))
+    p.op(OP_QUANTIZE, h, hq, dims=(batch * 512,))
+    p.op(OP_LINEAR, hq, z, in1=b2, w=wh2, dims=(batch,))
+    p.op(OP_SOFTMAX, z, y, dims=(batch, 10))
+    p.finalize()
+    return p, x, y, z, (q1, s1, q2, s2)
+
+
+# ------------------------------------------------------------------ ResNet-18
+def _conv_out(h, k, s, pad):
+    return (h + 2 * pad - k) // s + 1
+
+
+@dataclass
+class ConvSpec:
+    cin: int
+    cout: int
+    k: int
+    stride: int
+    pad: int
+    qw: QLinear = None   # W [cout, cin*k*k] per-channel int8, columns in (ky, kx, c) order
+
+
+@dataclass
+class ResNetSpec:
+    convs: list = field(default_factory=list)
+    fc_w: np.ndarray = None   # [512, 1000]
+    fc_b: np.ndarray = None
+
+
+def resnet18_weights(be, seed=100):
+    """He-normal conv weights N(0, sqrt(2/fan_in)) in OIHW, quantized per output
+    channel (axis 0 of OIHW, quant.rs:95-107) on the device, then reordered to
+    (ky, kx, c) columns for NHWC im2col; BatchNorm folded into a bias ~ N(0, 0.01)."""
+    spec = ResNetSpec()
+    layers = [(3, 64, 7, 2, 3)]
+    cfg = [(64, 64, 1), (64, 64, 1), (64, 128, 2), (128, 128, 1), (128, 256, 2), (256, 256, 1), (256, 512, 2),
+           (512, 512, 1)]
+    for cin, cout, s in cfg:
+        layers.append((cin, cout, 3, s, 1))
+        layers.append((cout, cout, 3, 1, 1))
+        if s != 1 or cin != cout:
+            layers.append((cin, cout, 1, s, 0))
+    for i, (cin, cout, k, s, pad) in enumerate(layers):
+        fan_in = cin * k * k
+        w = synth.normal(cout * fan_in, seed + 17 * i, 0.0, float(np.sqrt(2.0 / fan_in)))  # OIHW
+        q, sc = be.quantize_i8_symmetric_per_channel(w, cout)
+        q = q.reshape(cout, cin, k, k).transpose(0, 2, 3, 1).reshape(cout, fan_in)  # (ky, kx, c)
+        kp = (fan_in + 15) // 16 * 16
+        qp = np.zeros((cout, kp), np.int8)
+        qp[:, :fan_in] = q
+        b = synth.normal(cout, seed + 17 * i + 5, 0.0, 0.01)
+        spec.convs.append(ConvSpec(cin, cout, k, s, pad, QLinear(cout, kp, qp, sc, b)))
+    spec.fc_w = synth.normal(512 * 1000, seed + 999, 0.0, float(np.sqrt(2.0 / 512))).reshape(512, 1000)
+    spec.fc_b = np.zeros(1000, np.float32)
+    return spec
+
+
+def build_resnet18(be, batch, spec: ResNetSpec):
+    p = Plan(be)
+    handles = []
+    for cv in spec.convs:
+        wh = be.upload_i8(cv.qw.q, cv.qw.scales, cv.qw.n, cv.qw.k)
+        handles.append(wh)
+    p.weights += handles
+    x = p.tensor(F32, batch * 3 * 224 * 224)
+    xq = p.tensor(I8, batch * 224 * 224 * 3)
+    p.op(OP_NCHW_Q8, x, xq, dims=(batch, 3, 224 * 224))
+
+    def conv(inp_q, H, W, ci, act):
+        cv = spec.convs[ci]
+        OH, OW = _conv_out(H, cv.k, cv.stride, cv.pad), _conv_out(W, cv.k, cv.stride, cv.pad)
+        M = batch * OH * OW
+        col = p.tensor(I8, M * cv.qw.k)
+        p.op(OP_IM2COL, inp_q, col, dims=(batch, H, W, cv.cin, cv.k, cv.k, cv.stride, cv.stride, cv.pad, cv.pad,
+                                         OH, OW, cv.qw.k))
+        out = p.tensor(F32, M * cv.cout)
+        p.op(OP_LINEAR, col, out, in1=p.const(cv.qw.bias), w=handles[ci], act=act, dims=(M,))
+        return out, OH, OW
+
+    y, H, W = conv(xq, 224, 224, 0, ACT_RELU)                      # stem 7x7/2 -> 112
+    OH, OW = _conv_out(H, 3, 2, 1), _conv_out(W, 3, 2, 1)
+    mp = p.tensor(F32, batch * OH * OW * 64)
+    p.op(OP_MAXPOOL, y, mp, dims=(batch, H, W, 64, 3, 3, 2, 2, 1, 1, OH, OW))
+    cur, H, W, C = mp, OH, OW, 64
+    ci = 1
+    for cin, cout, s in [(64, 64, 1), (64, 64, 1), (64, 128, 2), (128, 128, 1), (128, 256, 2), (256, 256, 1),
+                         (256, 512, 2), (512, 512, 1)]:
+        cq = p.tensor(I8, batch * H * W * C)
+        p.op(OP_QUANTIZE, cur, cq, dims=(batch * H * W * C,))
+        h1, OH, OW = conv(cq, H, W, ci, ACT_RELU)
+        h1q = p.tensor(I8, batch * OH * OW * cout)
+        p.op(OP_QUANTIZE, h1, h1q, dims=(batch * OH * OW * cout,))
+        h2, _, _ = conv(h1q, OH, OW, ci + 1, ACT_NONE)
+        ci += 2
+        if s != 1 or cin != cout:
+            sc, _, _ = conv(cq, H, W, ci, ACT_NONE)
+            ci += 1
+        else:
+            sc = cur
+        out = p.tensor(F32, batch * OH * OW * cout)
+        p.op(OP_ADD_ACT, h2, out, in1=sc, act=ACT_RELU, dims=(batch * OH * OW * cout,))
+        cur, H, W, C = out, OH, OW, cout
+    g = p.tensor(F32, batch * 512)
+    p.op(OP_GAP, cur, g, dims=(batch, H * W, 512))
+    logits = p.tensor(F32, batch * 1000)
+    p.op(OP_MATMUL, g, logits, in1=p.const(spec.fc_w), in2=p.const(spec.fc_b), dims=(batch, 512, 1000))
+    p.finalize()
+    return p, x, logits
+
+
+# ------------------------------------------------------------------ BERT-base
+@dataclass
+class BertLayerW:
+    qkv: QLinear   # [2304, 768]
+    o: QLinear     # [768, 768]
+    f1: QLinear    # [3072, 768]
+    f2: QLinear    # [768, 3072]
+    g1: np.ndarray
+    b1: np.ndarray
+    g2: np.ndarray
+    b2: np.ndarray
+
+
+def bert_weights(be, layers=12, seed=5000, hidden=768, ffn=3072):
+    """All weights and biases ~ N(0, 0.02); LayerNorm gamma = 1, beta = 0."""
+    out = []
+    for L in range(layers):
+        s = seed + 101 * L
+        out.append(BertLayerW(make_qlinear(be, 3 * hidden, hidden, s, 0.02, 0.02),
+                              make_qlinear(be, hidden, hidden, s + 1, 0.02, 0.02),
+                              make_qlinear(be, ffn, hidden, s + 2, 0.02, 0.02),
+                              make_qlinear(be, hidden, ffn, s + 3, 0.02, 0.02),
+                              np.ones(hidden, np.float32), np.zeros(hidden, np.float32),
+                              np.ones(hidden, np.float32), np.zeros(hidden, np.float32)))
+    return out
+
+
+def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-5):
+    p = Plan(be)
+    T = batch * seq
+    x = p.tensor(F32, T * hidden)
+    cur = x
+    for lw in layers_w:
+        hs = []
+        for ql in (lw.qkv, lw.o, lw.f1, lw.f2):
+            wh = be.upload_i8(ql.q, ql.scales, ql.n, ql.k)
+            p.weights.append(wh)
+            hs.append(wh)
+        xq = p.tensor(I8, T * hidden)
+        p.op(OP_QUANTIZE, cur, xq, dims=(T * hidden,))
+        qkv = p.tensor(F32, T * 3 * hidden)
+        p.op(OP_LINEAR, xq, qkv, in1=p.const(lw.qkv.bias), w=hs[0], dims=(T,))
+        ctx = p.tensor(F32, T * hidden)
+        p.op(OP_ATTENTION, qkv, ctx, f0=0.125, dims=(batch, seq, heads, hidden // heads))
+        cq = p.tensor(I8, T * hidden)
+        p.op(OP_QUANTIZE, ctx, cq, dims=(T * hidden,))
+        o = p.tensor(F32, T * hidden)
+        p.op(OP_LINEAR, cq, o, in1=p.const(lw.o.bias), w=hs[1], dims=(T,))
+        r1 = p.tensor(F32, T * hidden)
+        p.op(OP_ADD_ACT, o, r1, in1=cur, dims=(T * hidden,))
+        h1 = p.tensor(F32, T * hidden)
+        p.op(OP_LAYERNORM, r1, h1, in1=p.const(lw.g1), in2=p.const(lw.b1), f0=eps, dims=(T, hidden))
+        hq = p.tensor(I8, T * hidden)
+        p.op(OP_QUANTIZE, h1, hq, dims=(T * hidden,))
+        f = p.tensor(F32, T * ffn)
+        p.op(OP_LINEAR, hq, f, in1=p.const(lw.f1.bias), w=hs[2], act=ACT_GELU, dims=(T,))
+        fq = p.tensor(I8, T * ffn)
+        p.op(OP_QUANTIZE, f, fq, dims=(T * ffn,))
+        f2 = p.tensor(F32, T * hidden)
+        p.op(OP_LINEAR, fq, f2, in1=p.const(lw.f2.bias), w=hs[3], dims=(T,))
+        r2 = p.tensor(F32, T * hidden)
+        p.op(OP_ADD_ACT, f2, r2, in1=h1, dims=(T * hidden,))
+        h2 = p.tensor(F32, T * hidden)
+        p.op(OP_LAYERNORM, r2, h2, in1=p.const(lw.g2), in2=p.const(lw.b2), f0=eps, dims=(T, hidden))
+        cur = h2
+    p.finalize()
+    return p, x, cur
