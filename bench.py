@@ -155,6 +155,164 @@ def cpu_reference(m, threads, budget_s, aq, sa, wq, ws, bias):
     return rows, dt, 2.0 * rows * N * K / dt / 1e12
 
 
+def _time_device(stream, fn, steps, warm, flush=None):
+    """Mean device time (s) of fn() on `stream` over `steps` launches (CUDA events),
+    with an optional L2 flush before each timed launch."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            fn()
+        stream.synchronize()
+        ts = []
+        for _ in range(steps):
+            if flush is not None:
+                flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            ts.append((s, e))
+        stream.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in ts])) * 1e-3
+
+
+def run_configs(be, stream, flush, pk, local, world, rank, cpu=True):
+    """The W4 sweep and the model workloads, each a sub-result of the JSON line."""
+    import torch
+
+    from tpt_infer_b200 import graphs, synth
+
+    dev = f"cuda:{local}"
+    out = {}
+    threads = os.cpu_count() or 1
+
+    # ---- W4 GEMM sweep: K = 4096, N = 11008, M in {1, 8, 64, 512}, f32 activations
+    try:
+        Kw, Nw = 4096, 11008
+        wt = synth.normal(Nw * Kw, 2000, 0.0, 0.02)
+        pk4, s4 = be.quantize_i4_symmetric_per_channel(wt, Nw)
+        w4 = be.upload_i4(pk4, s4, Nw, Kw)
+        rows = []
+        for m in (1, 8, 64, 512):
+            x = torch.from_numpy(synth.normal(m * Kw, 2001 + m)).to(dev)
+            y = torch.empty(m * Nw, dtype=torch.float32, device=dev)
+            t = _time_device(stream, lambda: be.w4_gemm_dev(x, m, w4, None, 0, y), 10, 3, flush)
+            by = Kw * Nw / 2 + 4 * Nw + 4 * m * Kw + 4 * m * Nw
+            rows.append({"M": m, "us": t * 1e6, "TFLOP/s": 2.0 * m * Kw * Nw / t / 1e12, "GB/s": by / t / 1e9,
+                         "frac_hbm": by / t / 1e9 / pk["hbm_gbs"]})
+        w4.free()
+        out["w4_sweep"] = {"K": Kw, "N": Nw, "rows": rows, "l2": "flushed before each timed launch"}
+    except Exception as e:  # report, do not lose the headline
+        out["w4_sweep"] = {"error": repr(e)}
+
+    # ---- MLP [64,784] -> 512 -> ReLU -> 10 -> Softmax, f32 and INT8 PTQ
+    try:
+        W = graphs.mlp_weights()
+        xin = synth.uniform(64 * 784, 77)
+        pf, xf, yf, _ = graphs.build_mlp_f32(be, 64, W)
+        pf.run({xf: xin}, [yf])
+        tf = _time_device(stream, pf.run_device, 50, 5)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            pf.run({xf: xin}, [yf])
+        ef = (time.perf_counter() - t0) / 20
+        pq, xq, yq, _, _ = graphs.build_mlp_int8(be, 64, W)
+        pq.calibrate(True)
+        for i in range(4):
+            pq.run({xq: synth.uniform(64 * 784, 1000 + i)}, [yq])
+        pq.freeze()
+        pq.run({xq: xin}, [yq])
+        tq = _time_device(stream, pq.run_device, 50, 5)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            pq.run({xq: xin}, [yq])
+        eq = (time.perf_counter() - t0) / 20
+        mlp = {"batch": 64, "f32": {"us_per_forward": tf * 1e6, "inferences_per_s": 64 / tf,
+                                    "e2e_inferences_per_s": 64 / ef},
+               "int8": {"us_per_forward": tq * 1e6, "inferences_per_s": 64 / tq, "e2e_inferences_per_s": 64 / eq,
+                        "calibration": "256 seeded U[0,1) inputs"}}
+        if cpu:
+            from oracle import models as OM
+
+            t0 = time.perf_counter()
+            OM.mlp_f32(xin, W, 64)
+            c = time.perf_counter() - t0
+            mlp["cpu_baseline"] = {"value": 64 / c, "unit": "inferences/s", "cores": OM.TH, "kind": "port",
+                                   "sample": "one f32 forward of the batch of 64 (AVX matmul restatement)"}
+        pf.close()
+        pq.close()
+        out["mlp"] = mlp
+    except Exception as e:
+        out["mlp"] = {"error": repr(e)}
+
+    # ---- ResNet-18-shaped CNN, batch 256, INT8 convs
+    try:
+        B = 256
+        spec = graphs.resnet18_weights(be)
+        p, x, logits = graphs.build_resnet18(be, B, spec)
+        p.calibrate(True)
+        p.run({x: synth.normal(B * 3 * 224 * 224, 31)}, [logits])
+        p.freeze()
+        xin = synth.normal(B * 3 * 224 * 224, 32)
+        p.run({x: xin}, [logits])
+        t = _time_device(stream, p.run_device, 5, 2)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            p.run({x: xin}, [logits])
+        e2e = (time.perf_counter() - t0) / 3
+        gop = 3.628 * B
+        res = {"batch": B, "ms_per_batch": t * 1e3, "images_per_s": B / t, "int8_TOP/s": gop / t / 1e3,
+               "e2e_images_per_s": B / e2e, "arena_GB": p.arena_bytes() / 1e9,
+               "calibration": "one seeded batch of 256"}
+        if cpu:
+            from oracle import models as OM
+
+            x1 = xin[: 3 * 224 * 224]
+            t0 = time.perf_counter()
+            OM.resnet18(x1, spec, 1, scales=p.scales())
+            c = time.perf_counter() - t0
+            res["cpu_baseline"] = {"value": 1 / c, "unit": "images/s", "cores": OM.TH, "kind": "port",
+                                   "sample": "1 image through the oracle's INT8 node-by-node replay"}
+        p.close()
+        out["resnet18"] = res
+    except Exception as e:
+        out["resnet18"] = {"error": repr(e)}
+
+    # ---- BERT-base-shaped encoder, 12 layers, batch 64, seq 128
+    try:
+        B, S = 64, 128
+        layers = graphs.bert_weights(be, layers=12)
+        p, x, h = graphs.build_bert(be, B, S, layers)
+        p.calibrate(True)
+        p.run({x: synth.normal(B * S * 768, 41)}, [h])
+        p.freeze()
+        xin = synth.normal(B * S * 768, 42)
+        p.run({x: xin}, [h])
+        t = _time_device(stream, p.run_device, 5, 2)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            p.run({x: xin}, [h])
+        e2e = (time.perf_counter() - t0) / 3
+        bert = {"batch": B, "seq": S, "layers": 12, "ms_per_batch": t * 1e3, "sequences_per_s": B / t,
+                "int8_TOP/s": 1392.0 / t / 1e3, "e2e_sequences_per_s": B / e2e, "arena_GB": p.arena_bytes() / 1e9,
+                "calibration": "one seeded batch"}
+        if cpu:
+            from oracle import models as OM
+
+            x1 = xin[: S * 768]
+            t0 = time.perf_counter()
+            OM.bert(x1, layers[:1], 1, S, scales=p.scales()[:4])
+            c = time.perf_counter() - t0
+            bert["cpu_baseline"] = {"value": 1 / (12 * c), "unit": "sequences/s", "cores": OM.TH, "kind": "port",
+                                    "sample": "1 layer of 1 sequence through the oracle replay, x12 layers"}
+        p.close()
+        out["bert"] = bert
+    except Exception as e:
+        out["bert"] = {"error": repr(e)}
+    return out
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -192,6 +350,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-budget", type=float, default=3.0, help="seconds of CPU work per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the W4 sweep and the model workloads")
     ap.add_argument("--profile", action="store_true",
                     help="headline GEMM only (warm-up + steps), no sweep / e2e / CPU leg: the ncu capture case")
     args = ap.parse_args()
@@ -302,6 +461,10 @@ def main():
                "sample": f"{rows} of {M_HEAD} output rows of the same GEMM, the reference loop order "
                          f"(ptq.rs:312-319) with per-channel scale + bias, {threads} OpenMP threads, {dt:.1f} s"}
 
+    configs = None
+    if not args.no_configs:
+        configs = run_configs(be, stream, flush, pk, local, world, rank, cpu=(rank == 0 and world == 1))
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -321,6 +484,7 @@ def main():
             "clocks": clk.summary(),
             "sweep": sweep,
             "cpu_baseline": cpu,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
     w.free()
