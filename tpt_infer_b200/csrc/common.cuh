@@ -19,9 +19,13 @@ struct tpt_cuda_ctx {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     int sm_count = 0;
-    // growable device scratch used by host-staged calls and split reductions
+    // growable device scratch used by host-staged calls
     char *scratch = nullptr;
     size_t scratch_cap = 0;
+    // growable device workspace used inside launches (e.g. split activations);
+    // separate from `scratch` so a launch never moves a host-staged buffer
+    char *ws = nullptr;
+    size_t ws_cap = 0;
     // small persistent device words: error flags + reduction cells
     unsigned *d_flags = nullptr;   // TPT_FLAG_WORDS words
     unsigned *d_reduce = nullptr;  // 64 words of reduction scratch
@@ -50,6 +54,8 @@ int set_size_mismatch(tpt_cuda_ctx *ctx, size_t expected, size_t actual);
 int cuda_fail(tpt_cuda_ctx *ctx, cudaError_t e, const char *what);
 // Ensures the context scratch holds at least `bytes` (grows; never shrinks).
 int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes);
+// Same for the launch workspace.
+int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes);
 // Waits for the stream, then reads and clears the device error words.
 int sync_and_check(tpt_cuda_ctx *ctx);
 // Returns TPT_CUDA_ERROR if the last launch failed, else TPT_OK; counts launches.

@@ -55,6 +55,26 @@ int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes) {
     return TPT_OK;
 }
 
+int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes) {
+    if (bytes <= ctx->ws_cap) return TPT_OK;
+    size_t cap = ctx->ws_cap ? ctx->ws_cap : (size_t)1 << 20;
+    while (cap < bytes) cap *= 2;
+    if (ctx->ws) {
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "workspace sync");
+        cudaFree(ctx->ws);
+        ctx->ws = nullptr;
+        ctx->ws_cap = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->ws, cap);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(ctx, e, "workspace cudaMalloc");
+    }
+    ctx->ws_cap = cap;
+    return TPT_OK;
+}
+
 int h2d(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes) {
     if (!bytes) return TPT_OK;
     cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
@@ -166,6 +186,7 @@ int tpt_cuda_ctx_destroy(tpt_cuda_ctx *ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->d_flags) cudaFree(ctx->d_flags);
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

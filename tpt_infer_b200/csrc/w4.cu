@@ -23,6 +23,8 @@ namespace tpt {
 
 int launch_w4_simt(tpt_cuda_ctx *ctx, const float *x, const uint8_t *packed, const float *scales, const float *bias,
                    int act, float *y, size_t m, size_t n, size_t k);
+int launch_w4_tc(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias, int act,
+                 float *y, bool *handled);
 
 namespace {
 
@@ -117,6 +119,9 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
             k_w4_gemv<2><<<g, 256, 0, ctx->stream>>>(x, p, w->scales, bias, (int)m, (int)n, (int)k, act, y);
         return after_launch(ctx, "w4_gemv");
     }
+    bool handled = false;
+    int st = launch_w4_tc(ctx, x, m, w, bias, act, y, &handled);
+    if (st || handled) return st;
     return launch_w4_simt(ctx, x, p, w->scales, bias, act, y, m, n, k);
 }
 
