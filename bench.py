@@ -46,6 +46,11 @@ def alg_bytes(m):
     return m * K + N * K + 8 * N + 4 * m * N
 
 
+# DRAM bytes (read + write) of one k_w8a8_tc2<256,0> launch on this workload, from the
+# ncu capture summarised in profiles/k_w8a8_tc2_m4096_n4096_k4096.md.
+NCU_TRAFFIC_HEAD = 34.117888e6 + 19.930368e6
+
+
 def peaks():
     p = {}
     try:
@@ -476,7 +481,10 @@ def main():
             "roofline": {"bound": "tensor", "achieved": ops(M_HEAD) / kernel_s / 1e12,
                          "peak": pk["int8_tops"], "unit": "TOP/s",
                          "frac": ops(M_HEAD) / kernel_s / 1e12 / pk["int8_tops"],
-                         "traffic": None,
+                         "traffic": NCU_TRAFFIC_HEAD,
+                         "traffic_note": "ncu dram__bytes_read+write of one launch "
+                                         "(profiles/k_w8a8_tc2_m4096_n4096_k4096.md); algorithmic "
+                                         f"{alg_bytes(M_HEAD) / 1e6:.1f} MB, Y mostly still in L2 at kernel end",
                          "peak_note": f"2 x {pk['src']} dense bf16 burst (INT8 dense rate = 2x bf16 on B200)"},
             "e2e": {"value": world * ops(M_HEAD) / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": M_HEAD * K,
                     "d2h_bytes_per_step": M_HEAD * N * 4},
