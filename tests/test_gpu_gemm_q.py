@@ -32,7 +32,9 @@ def w8a8_case(m, n, k, seed=100, with_bias=True):
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (16, 4096, 4096), (256, 4096, 4096),
                                    (3, 100, 48), (9, 33, 16), (130, 200, 64), (1, 10, 512),
                                    (128, 256, 128), (300, 512, 256), (1000, 768, 768), (160, 203, 96),
-                                   (4097, 300, 128)])
+                                   (4097, 300, 128), (33, 300, 256), (64, 512, 784), (48, 4096, 4096),
+                                   (17, 4097, 4112), (65, 512, 256), (100, 1000, 1024), (2, 300, 8192),
+                                   (4, 257, 4160)])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_w8a8_bit_exact(cuda, m, n, k, act):
     if act and m * n * k > 1 << 26:
@@ -65,6 +67,31 @@ def test_w8a8_accumulators_bit_exact(cuda, m):
     want = O.i8_gemm_acc(aq.reshape(m, k)[rows].ravel(), wq, rows.size, n, k, threads=8).reshape(rows.size, n)
     assert np.array_equal(got[rows], want)
     w.free()
+
+
+def test_w8a8_small_m_back_to_back(cuda):
+    # the stream-K path combines partial tiles in a workspace that must be
+    # clean again after every launch: run several shapes back to back on the
+    # stream without a host sync in between and check every result
+    import torch
+
+    cases = []
+    for i, (m, n, k) in enumerate([(1, 4096, 4096), (16, 4096, 4096), (64, 512, 784), (1, 4096, 4096),
+                                   (40, 1000, 2048)]):
+        aq, sa, wq, ws, bias = w8a8_case(m, n, k, seed=400 + 10 * i)
+        w = cuda.upload_i8(wq, ws, n, k)
+        a_dev = torch.from_numpy(aq).cuda()
+        b_dev = torch.from_numpy(bias).cuda()
+        y_dev = torch.empty(m * n, dtype=torch.float32, device="cuda")
+        cases.append((m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev))
+    torch.cuda.synchronize()
+    for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in cases:
+        cuda.w8a8_gemm_dev(a_dev, m, sa, w, b_dev, 1, y_dev)
+    cuda.sync()
+    for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in cases:
+        want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, 1, threads=8)
+        assert np.array_equal(y_dev.cpu().numpy(), want), (m, n, k)
+        w.free()
 
 
 def test_w8a8_full_m4096_sampled_rows(cuda):
@@ -124,7 +151,8 @@ def w4_tol(want):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 11008, 4096), (2, 100, 64),
-                                   (5, 40, 96), (1, 8, 32)])
+                                   (5, 40, 96), (1, 8, 32), (24, 1000, 1024), (40, 300, 2048), (130, 300, 512),
+                                   (300, 129, 4096)])
 def test_w4_gemm(cuda, m, n, k):
     x, p, s = w4_case(m, n, k)
     w = cuda.upload_i4(p, s, n, k)
@@ -155,3 +183,19 @@ def test_w4_bias_act(cuda, act):
     want = O.w4_gemm(x, p, s, m, n, k, bias, act)
     assert np.max(np.abs(y - want)) <= max(w4_tol(want), 1e-6)
     w.free()
+
+
+def test_handles_outlive_context():
+    # weights and plans may be freed after the context they were made through
+    # has been destroyed (garbage collection order is not under the caller's
+    # control); freeing them must touch only their device
+    from tpt_infer_b200 import CudaBackend
+    from tpt_infer_b200.graphs import Plan
+
+    be = CudaBackend.new(0)
+    aq, sa, wq, ws, bias = w8a8_case(4, 256, 128, seed=700)
+    w = be.upload_i8(wq, ws, 256, 128)
+    p = Plan(be)
+    be.close()
+    w.free()
+    p.close()

@@ -26,6 +26,13 @@ struct tpt_cuda_ctx {
     // separate from `scratch` so a launch never moves a host-staged buffer
     char *ws = nullptr;
     size_t ws_cap = 0;
+    // stream-K reduction workspace (i32/f32 partial tiles + per-tile counters).
+    // All-zero between launches: the CTA that finishes a tile zeroes what it
+    // read. A launch that timed out may leave it dirty, so sk_dirty makes the
+    // next user clear it first.
+    char *sk = nullptr;
+    size_t sk_cap = 0;
+    bool sk_dirty = false;
     // small persistent device words: error flags + reduction cells
     unsigned *d_flags = nullptr;   // TPT_FLAG_WORDS words
     unsigned *d_reduce = nullptr;  // 64 words of reduction scratch
@@ -36,15 +43,17 @@ struct tpt_cuda_ctx {
 
 struct tpt_cuda_weights {
     tpt_cuda_ctx *ctx = nullptr;
+    int device = 0;  // freeing needs only the device: the context may be gone
     int kind = 0;          // 8 = int8 [n,k]; 4 = int4 nibbles [n, k/2]
     size_t n = 0, k = 0;
     void *data = nullptr;  // device: packed weight bytes
     float *scales = nullptr;  // device: n per-channel scales
     size_t bytes = 0;
     // TMA descriptors of the int8 weight (CUtensorMap, 128 bytes each), built
-    // once: boxes of 256 rows (one-SM kernel) and of 128 / 64 / 32 rows (the
-    // SM-pair kernel's B half-tiles for tile N = 256 / 128 / 64)
-    alignas(64) unsigned char tmaps[4][128];
+    // once: boxes of 128 / 64 / 32 rows x 128 bytes (the stream-K kernel's
+    // weight tile, and the SM-pair kernel's B half-tiles for tile N = 256 /
+    // 128 / 64)
+    alignas(64) unsigned char tmaps[3][128];
     bool tmap_ok = false;
 };
 
@@ -56,6 +65,13 @@ int cuda_fail(tpt_cuda_ctx *ctx, cudaError_t e, const char *what);
 int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes);
 // Same for the launch workspace.
 int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes);
+// Stream-K workspace layout: TPT_SK_COUNTERS tile counters at offset 0 (a
+// fixed region, so kernels with different tile counts never see each other's
+// partial tiles as counters), then the partial-tile slots.
+constexpr size_t TPT_SK_COUNTERS = 16384;
+constexpr size_t TPT_SK_SLOTS_OFFSET = TPT_SK_COUNTERS * sizeof(int);
+// Ensures room for `slot_bytes` of slots after the counter region.
+int ensure_sk(tpt_cuda_ctx *ctx, size_t slot_bytes);
 // Waits for the stream, then reads and clears the device error words.
 int sync_and_check(tpt_cuda_ctx *ctx);
 // Returns TPT_CUDA_ERROR if the last launch failed, else TPT_OK; counts launches.

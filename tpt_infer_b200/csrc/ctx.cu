@@ -75,6 +75,34 @@ int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes) {
     return TPT_OK;
 }
 
+int ensure_sk(tpt_cuda_ctx *ctx, size_t slot_bytes) {
+    const size_t bytes = TPT_SK_SLOTS_OFFSET + slot_bytes;
+    if (bytes > ctx->sk_cap) {
+        size_t cap = ctx->sk_cap ? ctx->sk_cap : (size_t)1 << 20;
+        while (cap < bytes) cap *= 2;
+        if (ctx->sk) {
+            cudaError_t e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "stream-K workspace sync");
+            cudaFree(ctx->sk);
+            ctx->sk = nullptr;
+            ctx->sk_cap = 0;
+        }
+        cudaError_t e = cudaMalloc(&ctx->sk, cap);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return cuda_fail(ctx, e, "stream-K workspace cudaMalloc");
+        }
+        ctx->sk_cap = cap;
+        ctx->sk_dirty = true;
+    }
+    if (ctx->sk_dirty) {
+        cudaError_t e = cudaMemsetAsync(ctx->sk, 0, ctx->sk_cap, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "stream-K workspace clear");
+        ctx->sk_dirty = false;
+    }
+    return TPT_OK;
+}
+
 int h2d(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes) {
     if (!bytes) return TPT_OK;
     cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
@@ -94,6 +122,7 @@ int sync_and_check(tpt_cuda_ctx *ctx) {
     e = cudaMemcpy(flags, ctx->d_flags, sizeof flags, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "flag read");
     if (flags[TPT_FLAG_TIMEOUT] || flags[TPT_FLAG_CHECK]) {
+        if (flags[TPT_FLAG_TIMEOUT]) ctx->sk_dirty = true;  // a stream-K launch may have stopped mid-tile
         cudaMemsetAsync(ctx->d_flags, 0, sizeof flags, ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         char buf[160];
@@ -187,6 +216,7 @@ int tpt_cuda_ctx_destroy(tpt_cuda_ctx *ctx) {
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->sk) cudaFree(ctx->sk);
     if (ctx->d_flags) cudaFree(ctx->d_flags);
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

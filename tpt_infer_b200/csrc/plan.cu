@@ -55,6 +55,7 @@ struct PlanOp {
 
 struct tpt_cuda_plan {
     tpt_cuda_ctx *ctx = nullptr;
+    int device = 0;  // destroying needs only the device: the context may be gone
     std::vector<PlanTensor> tensors;
     std::vector<PlanOp> ops;
     char *arena = nullptr;
@@ -171,14 +172,16 @@ int tpt_cuda_plan_create(tpt_cuda_ctx *ctx, tpt_cuda_plan **out) {
     tpt_cuda_plan *p = new (std::nothrow) tpt_cuda_plan();
     if (!p) return TPT_OUT_OF_MEMORY;
     p->ctx = ctx;
+    p->device = ctx->device;
     *out = p;
     return TPT_OK;
 }
 
+// cudaFree waits for work using the memory, so the context is not touched and
+// a plan may outlive it.
 int tpt_cuda_plan_destroy(tpt_cuda_plan *p) {
     if (!p) return TPT_INVALID;
-    cudaSetDevice(p->ctx->device);
-    cudaStreamSynchronize(p->ctx->stream);
+    cudaSetDevice(p->device);
     if (p->arena) cudaFree(p->arena);
     if (p->cells) cudaFree(p->cells);
     for (auto &t : p->tensors)

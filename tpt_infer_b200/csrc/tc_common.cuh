@@ -12,15 +12,13 @@
 namespace tpt {
 namespace tc {
 
-constexpr unsigned long long TPT_WAIT_NS = 1000000000ull;  // 1 s per wait
+// Bound of one wait in SM clock cycles: about 1 s at the B200's 1.965 GHz
+// boost clock (longer at lower clocks, never unbounded). The SM-local cycle
+// counter is read instead of %globaltimer, whose read is slow enough to add a
+// visible delay to every wait that does not succeed on its first poll.
+constexpr long long TPT_WAIT_CYCLES = 2000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -42,18 +40,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait. Returns false when the CTA is aborting or the wait ran out
-// (then the abort is raised and the global timeout flag recorded).
-static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
+// (then the abort is raised and the global timeout flag recorded). The abort
+// flag and the clock are checked every 16 polls.
+static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
                                        bool honour_abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
-    while (true) {
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (honour_abort && *abort_flag) return false;
-        if (globaltimer() - t0 > TPT_WAIT_NS) {
-            *abort_flag = 1;
-            if (gflags) atomicOr(gflags + TPT_FLAG_TIMEOUT, 1u);
-            return false;
+        if ((i & 15u) == 0) {
+            if (honour_abort && *abort_flag) return false;
+            if (clock64() - t0 > TPT_WAIT_CYCLES) {
+                *abort_flag = 1;
+                if (gflags) atomicOr(gflags + TPT_FLAG_TIMEOUT, 1u);
+                return false;
+            }
         }
     }
 }
@@ -93,6 +94,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
           "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
 }
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor of a K-major, 128B-swizzled operand tile:
@@ -114,6 +124,55 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, uint32_t src
                  : "memory");
 }
 
+// Named barrier over `count` threads (a multiple of 32) that also ANDs a
+// predicate across them: every participant gets the same answer.
+__device__ __forceinline__ bool bar_and(int id, int count, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.and.pred b, %2, %3, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Stream-K grids are at most this many CTAs (one per SM), so a split tile has
+// at most this many contributors.
+constexpr int TPT_SK_MAX_CTAS = 256;
+
+// The CTA whose stream-K unit range [U*c/G, U*(c+1)/G) holds unit u.
+__host__ __device__ inline int sk_cta_of_unit(long long u, long long units, int ctas) {
+    return (int)(((u + 1) * ctas + units - 1) / units) - 1;
+}
+// Partial-tile slot of CTA c for `tile`: only the first and the last segment
+// of a CTA's range can be partial, so they own slots 2c and 2c + 1 (the
+// workspace is bounded by the grid, not by the tile count). A split tile's
+// counter is indexed by its first contributor, which no other split tile has.
+__device__ inline int sk_slot(int c, int tile, long long units, int kblocks, int ctas) {
+    const long long u0 = units * c / ctas;
+    return 2 * c + ((int)(u0 / kblocks) == tile ? 0 : 1);
+}
+
+// Stream-K schedule: U = tiles x kblocks units split into gridDim equal
+// contiguous ranges; a CTA walks its range as segments (tile, [kb0, kb1)).
+struct SkRange {
+    long long u, u1;
+    int kblocks;
+    __device__ SkRange(long long units, int kb, int cta, int ctas)
+        : u(units * cta / ctas), u1(units * (cta + 1) / ctas), kblocks(kb) {}
+    __device__ bool next(int &tile, int &kb0, int &kb1) {
+        if (u >= u1) return false;
+        tile = (int)(u / kblocks);
+        kb0 = (int)(u - (long long)tile * kblocks);
+        const long long left = u1 - u;
+        kb1 = left < (long long)(kblocks - kb0) ? kb0 + (int)left : kblocks;
+        u += kb1 - kb0;
+        return true;
+    }
+};
 
 }  // namespace tc
 }  // namespace tpt

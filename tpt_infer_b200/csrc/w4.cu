@@ -13,8 +13,10 @@
 // bytes quantize_i4_symmetric_per_channel(W^T, rows = n) emits
 // (quant.rs:192-204), uploaded once, never repacked.
 //
-// k_w4_gemv (M <= 2): one warp streams 8 weight rows with 128-bit loads,
-// reusing each activation chunk (held in registers) across the 8 rows.
+// M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 64 == 0 and x is
+// 16-byte aligned. M <= 2 uses k_w4_gemv: one warp streams 8 weight rows with
+// 128-bit loads, reusing each activation chunk across the 8 rows. Other shapes
+// use the SIMT tile kernel.
 #include <new>
 
 #include "common.cuh"
@@ -110,6 +112,11 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     const uint8_t *p = (const uint8_t *)w->data;
+    if (m > 2) {
+        bool handled = false;
+        int st = launch_w4_tc(ctx, x, m, w, bias, act, y, &handled);
+        if (st || handled) return st;
+    }
     if (m <= 2 && ((uintptr_t)x & 15) == 0) {
         size_t warps = (n + W4_ROWS - 1) / W4_ROWS;
         unsigned g = grid_1d(warps * 32, 256, (unsigned)ctx->sm_count * 8);
@@ -119,9 +126,6 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
             k_w4_gemv<2><<<g, 256, 0, ctx->stream>>>(x, p, w->scales, bias, (int)m, (int)n, (int)k, act, y);
         return after_launch(ctx, "w4_gemv");
     }
-    bool handled = false;
-    int st = launch_w4_tc(ctx, x, m, w, bias, act, y, &handled);
-    if (st || handled) return st;
     return launch_w4_simt(ctx, x, p, w->scales, bias, act, y, m, n, k);
 }
 
@@ -153,6 +157,7 @@ int tpt_cuda_weights_upload_i4(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t 
     tpt_cuda_weights *w = new (std::nothrow) tpt_cuda_weights();
     if (!w) return TPT_OUT_OF_MEMORY;
     w->ctx = ctx;
+    w->device = ctx->device;
     w->kind = 4;
     w->n = n;
     w->k = k;

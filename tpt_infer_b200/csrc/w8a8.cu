@@ -6,10 +6,11 @@
 // kept separate (no FMA) so the f32 output is bit-exact with the oracle.
 //
 // Kernels here:
-//  - k_w8a8_gemv: small M (<= 16). One warp per output channel streams the
-//    K-contiguous weight row with 128-bit loads and dp4a; HBM-bound by design.
+//  - k_w8a8_gemv: M <= 4. One warp per output channel streams the K-contiguous
+//    weight row with 128-bit loads (all of a pass in flight) and dp4a.
 //  - k_w8a8_simt: general shapes (ragged M/N, K % 16 == 0); dp4a tiles.
-//  - the tcgen05 tensor-core kernel for large M lives in w8a8_tc.cu.
+//  - the tcgen05 tensor-core kernels: stream-K for M <= 64 in w8a8_sk.cu,
+//    one-SM and SM-pair tiles for larger M in w8a8_tc.cu.
 // Weight layout in HBM: W^T [n, k] int8 row-major (K-major B operand), which
 // is the byte layout quantize_i8_symmetric_per_channel(W^T, rows = n) emits.
 #include <string.h>
@@ -23,6 +24,8 @@ namespace tpt {
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled);
 int build_weight_tmap(tpt_cuda_weights *w);
+int launch_w8a8_sk(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled);
 
 namespace {
 
@@ -41,7 +44,14 @@ __device__ __forceinline__ int dot16(int4 a, int4 b, int acc) {
     return acc;
 }
 
-template <int MM>
+// One warp per output channel (grid-stride). Each lane owns 16-byte chunks
+// c = lane + 32 j of the row, j < 8, so a warp covers 4 KB of K per pass and
+// every load of the pass is issued before the first dp4a: a warp keeps 4 KB in
+// flight and the activations stay in registers (A_REG, M <= 2, K <= 4096) or in
+// L1 (reloaded per row, the lines are shared by every warp of the SM).
+constexpr int GEMV_CH = 8;  // 16-byte chunks per lane per pass
+
+template <int MM, bool A_REG>
 __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
                                                    const float *__restrict__ wscale, const float *__restrict__ bias,
                                                    int M, int N, int K, float a_scale, int act,
@@ -50,31 +60,44 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = K >> 4;  // 16-byte chunks per row
+    int4 ar[A_REG ? MM : 1][GEMV_CH];
+    if (A_REG) {
+#pragma unroll
+        for (int i = 0; i < MM; i++)
+#pragma unroll
+            for (int j = 0; j < GEMV_CH; j++) {
+                const int c = lane + 32 * j;
+                ar[i][j] = (i < M && c < chunks) ? __ldg(reinterpret_cast<const int4 *>(A + (size_t)i * K) + c)
+                                                 : make_int4(0, 0, 0, 0);
+            }
+    }
     for (int n = warp; n < N; n += nwarps) {
         const int4 *wrow = reinterpret_cast<const int4 *>(Wt + (size_t)n * K);
         int acc[MM];
 #pragma unroll
         for (int i = 0; i < MM; i++) acc[i] = 0;
-        int c = lane;
-        for (; c + 96 < chunks; c += 128) {
-            int4 w0 = __ldcs(wrow + c), w1 = __ldcs(wrow + c + 32), w2 = __ldcs(wrow + c + 64),
-                 w3 = __ldcs(wrow + c + 96);
+        for (int c0 = 0; c0 < chunks; c0 += 32 * GEMV_CH) {
+            int4 w[GEMV_CH];
+#pragma unroll
+            for (int j = 0; j < GEMV_CH; j++) {
+                const int c = c0 + lane + 32 * j;
+                w[j] = c < chunks ? __ldcs(wrow + c) : make_int4(0, 0, 0, 0);
+            }
 #pragma unroll
             for (int i = 0; i < MM; i++) {
-                if (i < M) {
-                    const int4 *arow = reinterpret_cast<const int4 *>(A + (size_t)i * K);
-                    acc[i] = dot16(__ldg(arow + c), w0, acc[i]);
-                    acc[i] = dot16(__ldg(arow + c + 32), w1, acc[i]);
-                    acc[i] = dot16(__ldg(arow + c + 64), w2, acc[i]);
-                    acc[i] = dot16(__ldg(arow + c + 96), w3, acc[i]);
+                if (i >= M) break;
+                const int4 *arow = reinterpret_cast<const int4 *>(A + (size_t)i * K);
+#pragma unroll
+                for (int j = 0; j < GEMV_CH; j++) {
+                    const int c = c0 + lane + 32 * j;
+                    int4 a;
+                    if (A_REG)
+                        a = ar[i][j];
+                    else
+                        a = c < chunks ? __ldg(arow + c) : make_int4(0, 0, 0, 0);
+                    acc[i] = dot16(a, w[j], acc[i]);
                 }
             }
-        }
-        for (; c < chunks; c += 32) {
-            int4 w0 = __ldcs(wrow + c);
-#pragma unroll
-            for (int i = 0; i < MM; i++)
-                if (i < M) acc[i] = dot16(__ldg(reinterpret_cast<const int4 *>(A + (size_t)i * K) + c), w0, acc[i]);
         }
 #pragma unroll
         for (int i = 0; i < MM; i++) {
@@ -196,24 +219,28 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     const int8_t *wt = (const int8_t *)w->data;
-    if (m <= 16) {
+    if (m <= 4) {
+        // decode-like: SIMT stream of the weight rows (HBM-bound)
         unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
-#define TPT_GEMV(MM) \
-    k_w8a8_gemv<MM><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc)
-        if (m == 1)
-            TPT_GEMV(1);
-        else if (m == 2)
-            TPT_GEMV(2);
-        else if (m <= 4)
-            TPT_GEMV(4);
-        else if (m <= 8)
-            TPT_GEMV(8);
+        const bool areg = k <= (size_t)GEMV_CH * 32 * 16;
+#define TPT_GEMV(MM, AR) \
+    k_w8a8_gemv<MM, AR><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc)
+        if (m == 1 && areg)
+            TPT_GEMV(1, true);
+        else if (m == 1)
+            TPT_GEMV(1, false);
+        else if (m == 2 && areg)
+            TPT_GEMV(2, true);
         else
-            TPT_GEMV(16);
+            TPT_GEMV(4, false);
 #undef TPT_GEMV
         return after_launch(ctx, "w8a8_gemv");
     }
     bool handled = false;
+    if (m <= 64) {
+        int st = launch_w8a8_sk(ctx, a, m, w, a_scale, bias, act, y, acc, &handled);
+        if (st || handled) return st;
+    }
     int st = launch_w8a8_tc(ctx, a, m, w, a_scale, bias, act, y, acc, &handled);
     if (st || handled) return st;
     dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 127) / 128));
@@ -249,6 +276,7 @@ int tpt_cuda_weights_upload_i8(tpt_cuda_ctx *ctx, const int8_t *wt, const float 
     tpt_cuda_weights *w = new (std::nothrow) tpt_cuda_weights();
     if (!w) return TPT_OUT_OF_MEMORY;
     w->ctx = ctx;
+    w->device = ctx->device;
     w->kind = 8;
     w->n = n;
     w->k = k;
@@ -269,10 +297,11 @@ int tpt_cuda_weights_upload_i8(tpt_cuda_ctx *ctx, const int8_t *wt, const float 
     return TPT_OK;
 }
 
+// Needs only the weight's device (cudaFree waits for work using the memory),
+// so a handle may outlive the context it was uploaded through.
 int tpt_cuda_weights_free(tpt_cuda_weights *w) {
     if (!w) return TPT_INVALID;
-    cudaSetDevice(w->ctx->device);
-    cudaStreamSynchronize(w->ctx->stream);
+    cudaSetDevice(w->device);
     if (w->data) cudaFree(w->data);
     if (w->scales) cudaFree(w->scales);
     delete w;

@@ -1,5 +1,6 @@
-// w8a8_tc.cu -- the large-M W8A8 GEMM on Blackwell's 5th-generation tensor
-// cores (tcgen05.mma kind::i8, i32 accumulators in tensor memory).
+// w8a8_tc.cu -- the W8A8 GEMM for M > 64 on Blackwell's 5th-generation tensor
+// cores (tcgen05.mma kind::i8, i32 accumulators in tensor memory), one output
+// tile per pair of SMs (cta_group::2).
 //
 // Computes the per-channel extension of quantized_matmul_i8
 // (crates/tpt-infer-quantize/src/ptq.rs:293-324):
@@ -8,21 +9,7 @@
 // The epilogue rounds exactly like the oracle (separate RN multiply/add), so
 // the f32 output is bit-exact.
 //
-// Structure (one CTA per SM, persistent over output tiles of 128 x BN):
-//   warp 0      TMA producer: A tile [128 rows x 128 B] and B tile
-//               [BN rows x 128 B] per k-block into a STAGES-deep ring of
-//               128B-swizzled shared-memory buffers (K-major, the layout the
-//               MMA's shared-memory descriptors describe).
-//   warp 1      allocates tensor memory; one lane issues tcgen05.mma
-//               (M=128, N=BN, K=32 per instruction) and tcgen05.commit to free
-//               ring slots and to publish finished accumulators.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from the TMEM
-//               accumulator (each warp owns its 32-lane quarter), fused
-//               dequant + bias + activation, 128-bit stores.
-// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
-// of tile i overlaps the MMAs of tile i+1.
-//
-// Every mbarrier wait is bounded (TPT_WAIT_NS of wall time via %globaltimer).
+// Every mbarrier wait is bounded (TPT_WAIT_CYCLES of the SM clock, about 1 s).
 // A wait that runs out records TPT_FLAG_TIMEOUT in the context's device flag
 // words, raises a CTA-wide abort so every role leaves its loop, the producer
 // waits (bounded) for its own TMA copies still in flight, the MMA issuer waits
@@ -34,254 +21,7 @@ namespace tpt {
 namespace {
 using namespace tc;
 
-constexpr int TC_BM = 128;       // output rows per tile (MMA M)
 constexpr int TC_BK = 128;       // k bytes per stage (one 128B swizzle row)
-constexpr int TC_THREADS = 192;  // 6 warps
-// Instruction descriptor, kind::i8: D = s32, A = B = signed 8-bit, both
-// K-major, N = BN, M = 128.
-template <int BN>
-__host__ __device__ constexpr uint32_t i8_idesc() {
-    return (2u << 4)            // D format: s32
-           | (1u << 7)          // A format: signed 8-bit
-           | (1u << 10)         // B format: signed 8-bit
-           | ((uint32_t)(BN >> 3) << 17)
-           | ((uint32_t)(TC_BM >> 4) << 24);
-}
-
-template <int BN>
-struct TcCfg {
-    static constexpr int A_BYTES = TC_BM * TC_BK;
-    static constexpr int B_BYTES = BN * TC_BK;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
-    static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
-    // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B)
-    static constexpr int OUT_BYTES = 4 * 2 * 4096;
-    // ring + staging + barriers (full, empty per stage; tfull, tempty per
-    // accumulator; one MMA-drain barrier) + 1 KB alignment slack
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
-};
-
-template <int BN, bool ACC_OUT>
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    k_w8a8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
-              const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
-              int32_t *__restrict__ ACC, unsigned *gflags) {
-    using Cfg = TcCfg<BN>;
-    constexpr int S = Cfg::STAGES;
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ int abort_flag;
-    __shared__ uint32_t tmem_slot;
-
-    const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t ring = (raw + 1023u) & ~1023u;
-    const uint32_t staging = ring + S * Cfg::STAGE_BYTES;  // 1 KB aligned
-    const uint32_t bars = staging + Cfg::OUT_BYTES;
-    auto full_bar = [&](int s) { return bars + 8u * s; };
-    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
-    auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
-    auto tempty_bar = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
-    const uint32_t drain_bar = bars + 8u * (2 * S + 4);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_m = (M + TC_BM - 1) / TC_BM, tiles_n = (N + BN - 1) / BN;
-    const int ntiles = tiles_m * tiles_n;
-    const int kblocks = (K + TC_BK - 1) / TC_BK;
-
-    if (threadIdx.x == 0) {
-        abort_flag = 0;
-        for (int s = 0; s < S; s++) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 1);
-        }
-        for (int b = 0; b < 2; b++) {
-            mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), 4 * 32);
-        }
-        mbar_init(drain_bar, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-    }
-    if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"((uint32_t)Cfg::TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_slot;
-    volatile int *abort_p = &abort_flag;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            // ---------------- TMA producer ----------------
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued_mask = 0, last_phase = 0;  // per stage: issued?, parity of last issue
-            bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int mt = t / tiles_n, nt = t - mt * tiles_n;
-                for (int kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t a_dst = ring + stage * Cfg::STAGE_BYTES;
-                    mbar_arrive_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
-                    tma_load_2d(a_dst, &tmA, full_bar(stage), kb * TC_BK, mt * TC_BM);
-                    tma_load_2d(a_dst + Cfg::A_BYTES, &tmB, full_bar(stage), kb * TC_BK, nt * BN);
-                    issued_mask |= 1u << stage;
-                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-            }
-            // our own copies in flight must land before the CTA can exit
-            for (int s = 0; s < S; s++)
-                if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (last_phase >> s) & 1u, abort_p, gflags, false);
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = i8_idesc<BN>();
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(full_bar(stage), phase, abort_p, gflags, true)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_addr = ring + stage * Cfg::STAGE_BYTES;
-                    const uint32_t b_addr = a_addr + Cfg::A_BYTES;
-#pragma unroll
-                    for (int kk = 0; kk < TC_BK / 32; kk++)
-                        tc_mma_i8(d_tmem, sw128_desc(a_addr + 32 * kk), sw128_desc(b_addr + 32 * kk), idesc,
-                                  (kb | kk) != 0 ? 1u : 0u);
-                    tc_commit(empty_bar(stage));
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                tc_commit(tfull_bar(acc));
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
-                }
-            }
-            // drain: every MMA this thread issued completes before TMEM is freed
-            tc_commit(drain_bar);
-            mbar_wait(drain_bar, 0, abort_p, gflags, false);
-        }
-    } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        // Each warp owns TMEM lanes [32q, 32q+32) = tile rows [32q, 32q+32).
-        // Per 32-column chunk: tcgen05.ld (thread = row), dequant with the
-        // column's scale/bias broadcast by shuffle, then either a TMA store of
-        // the 32 x 32 block staged in 128B-swizzled shared memory (coalesced,
-        // clipped at ragged edges) or, when the output cannot be described by
-        // a tensor map, direct stores.
-        const int q = warp & 3;
-        const int row = q * 32 + lane;
-        const uint32_t stage_s = staging + (uint32_t)(q * 8192);
-        uint8_t *stage_g = smem_raw + (stage_s - raw);
-        int buf = 0;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-            int okw = 0;
-            if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
-            okw = __shfl_sync(0xffffffffu, okw, 0);
-            if (!okw) break;
-            tc_fence_after();
-            const int mt = t / tiles_n, nt = t - mt * tiles_n;
-            const int m = mt * TC_BM + row;
-            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
-                uint32_t v[32];
-                tmem_ld32(t_base + (uint32_t)(c * 32), v);
-                tmem_wait_ld();
-                const int n0 = nt * BN + c * 32;
-                if (!ACC_OUT) {
-                    const int nc = n0 + lane < N ? n0 + lane : N - 1;  // this lane's column
-                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nc));
-                    const float bi = bias ? __ldg(bias + nc) : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        float y = __fmul_rn(__int2float_rn((int)v[j]), __shfl_sync(0xffffffffu, sc, j));
-                        if (bias) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bi, j));
-                        v[j] = __float_as_uint(apply_act(y, act));
-                    }
-                }
-                if (tma_store) {
-                    // the store issued from this buffer two chunks ago must have read it
-                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                    __syncwarp();
-                    uint8_t *sb = stage_g + buf * 4096 + lane * 128;
-#pragma unroll
-                    for (int cc = 0; cc < 8; cc++)
-                        *reinterpret_cast<uint4 *>(sb + ((cc ^ (lane & 7)) << 4)) =
-                            make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mt * TC_BM + q * 32);
-                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    }
-                    buf ^= 1;
-                } else if (m < M) {
-                    uint32_t *dst = ACC_OUT ? reinterpret_cast<uint32_t *>(ACC) + (size_t)m * N + n0
-                                            : reinterpret_cast<uint32_t *>(Y) + (size_t)m * N + n0;
-                    if (n0 + 32 <= N && (N & 3) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<uint4 *>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (n0 + j < N) dst[j] = v[j];
-                    }
-                }
-            }
-            tc_fence_before();
-            mbar_arrive(tempty_bar(acc));
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1u;
-            }
-        }
-        // every bulk store has finished reading this CTA's shared memory and
-        // written its block before the CTA exits
-        if (tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-        __syncwarp();
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"((uint32_t)Cfg::TMEM_COLS)
-                     : "memory");
-    }
-}
-
 
 // ---------------------------------------------------------------------------
 // SM-pair kernel: tcgen05.mma.cta_group::2, 256 x 256 output tiles per
@@ -528,20 +268,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                     }
                 }
                 if (tma_store) {
-                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                    __syncwarp();
-                    uint8_t *sb = stage_g + buf * 4096 + lane * 128;
+                    if (mrow0 < M) {  // a block entirely below the last row is not stored
+                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                        __syncwarp();
+                        uint8_t *sb = stage_g + buf * 4096 + lane * 128;
 #pragma unroll
-                    for (int cc = 0; cc < 8; cc++)
-                        *reinterpret_cast<uint4 *>(sb + ((cc ^ (lane & 7)) << 4)) =
-                            make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mrow0);
-                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        for (int cc = 0; cc < 8; cc++)
+                            *reinterpret_cast<uint4 *>(sb + ((cc ^ (lane & 7)) << 4)) =
+                                make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mrow0);
+                            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        }
+                        buf ^= 1;
                     }
-                    buf ^= 1;
                 } else if (m < M) {
                     uint32_t *dst = ACC_OUT ? reinterpret_cast<uint32_t *>(ACC) + (size_t)m * N + n0
                                             : reinterpret_cast<uint32_t *>(Y) + (size_t)m * N + n0;
@@ -630,29 +372,6 @@ bool make_tmap_i8(CUtensorMap *tm, const void *base, uint64_t rows, uint64_t k, 
 }
 
 template <int BN, bool ACC_OUT>
-int launch_tc(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
-              const float *ws, const float *bias, int act, float *y, int32_t *acc) {
-    using Cfg = TcCfg<BN>;
-    // the dynamic shared-memory opt-in is per device
-    static bool attr_done[64] = {};
-    auto kfn = k_w8a8_tc<BN, ACC_OUT>;
-    const int dev = ctx->device & 63;
-    if (!attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "w8a8_tc smem attribute");
-        attr_done[dev] = true;
-    }
-    const int ntiles = ((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
-    const int grid = ntiles < ctx->sm_count ? ntiles : ctx->sm_count;
-    CUtensorMap ty;
-    const bool tma_store = make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
-                                         (uint64_t)N, ACC_OUT);
-    kfn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0, M, N, K,
-                                                            a_scale, ws, bias, act, y, acc, ctx->d_flags);
-    return after_launch(ctx, "w8a8_tc");
-}
-
-template <int BN, bool ACC_OUT>
 int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
                const float *ws, const float *bias, int act, float *y, int32_t *acc) {
     using Cfg = PairCfg<BN>;
@@ -717,8 +436,8 @@ bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uin
 
 int build_weight_tmap(tpt_cuda_weights *w) {
     bool ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff;
-    const uint32_t rows[4] = {256, 128, 64, 32};
-    for (int i = 0; i < 4 && ok; i++)
+    const uint32_t rows[3] = {128, 64, 32};
+    for (int i = 0; i < 3 && ok; i++)
         ok = make_tmap_i8(reinterpret_cast<CUtensorMap *>(w->tmaps[i]), w->data, w->n, w->k, rows[i]);
     w->tmap_ok = ok;
     return TPT_OK;
@@ -726,31 +445,43 @@ int build_weight_tmap(tpt_cuda_weights *w) {
 
 // Large-M shapes go to the tensor-core kernel: M >= 128, weights with a tensor
 // map (K % 16 == 0, 16-byte aligned), A 16-byte aligned.
+// M > 64 with the weight's tensor maps available and A 16-byte aligned.
+// Tile N is the largest of 256 / 128 / 64 whose tile count still covers the SM
+// pairs in one pass, weighing a narrower tile's lower shared-memory efficiency
+// (an M=256 x N=64 MMA reads 5 KB of operands per 64 tensor-core cycles per SM
+// against 4 KB at N=256) with a per-width cost factor.
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled) {
     *handled = false;
-    if (!w->tmap_ok || m < 128 || m > 0x7fffffff) return TPT_OK;
+    if (!w->tmap_ok || m <= 64 || m > 0x7fffffff) return TPT_OK;
     CUtensorMap ta;
-    if (!make_tmap_i8(&ta, a, m, w->k, TC_BM)) return TPT_OK;
+    if (!make_tmap_i8(&ta, a, m, w->k, 128)) return TPT_OK;
     *handled = true;
-    if (m >= 256) {
-        // SM-pair kernel, 256 x BN tiles; each CTA's B box holds BN/2 rows
-        const int M = (int)m, N = (int)w->n, K = (int)w->k;
-        const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(w->tmaps);
-        if (N <= 64) {
-            return acc ? launch_tc2<64, true>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc)
-                       : launch_tc2<64, false>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc);
+    const int M = (int)m, N = (int)w->n, K = (int)w->k;
+    const long long pairs = ctx->sm_count / 2 > 0 ? ctx->sm_count / 2 : 1;
+    const long long mt = (M + P_BM - 1) / P_BM;
+    const int widths[3] = {256, 128, 64};
+    const double cost[3] = {1.0, 1.15, 1.5};
+    int bn = 256;
+    double best = 0.0;
+    for (int i = 0; i < 3; i++) {
+        const long long tiles = mt * ((N + widths[i] - 1) / widths[i]);
+        const double t = (double)((tiles + pairs - 1) / pairs) * widths[i] * cost[i];
+        if (i == 0 || t < best) {
+            best = t;
+            bn = widths[i];
         }
-        if (N <= 128) {
-            return acc ? launch_tc2<128, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc)
-                       : launch_tc2<128, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc);
-        }
-        return acc ? launch_tc2<256, true>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc)
-                   : launch_tc2<256, false>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc);
     }
-    const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->tmaps[0]);
-    if (acc) return launch_tc<256, true>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
-    return launch_tc<256, false>(ctx, ta, tb, (int)m, (int)w->n, (int)w->k, a_scale, w->scales, bias, act, y, acc);
+    // each CTA's B box holds BN/2 rows: tmaps[0..2] are the 128 / 64 / 32-row boxes
+    const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(w->tmaps);
+    if (bn == 64)
+        return acc ? launch_tc2<64, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc)
+                   : launch_tc2<64, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc);
+    if (bn == 128)
+        return acc ? launch_tc2<128, true>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc)
+                   : launch_tc2<128, false>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc);
+    return acc ? launch_tc2<256, true>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc)
+               : launch_tc2<256, false>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc);
 }
 
 }  // namespace tpt
