@@ -182,17 +182,54 @@ def _time_device(stream, fn, steps, warm, flush=None):
     return float(np.mean([a.elapsed_time(b) for a, b in ts])) * 1e-3
 
 
-def run_configs(be, stream, flush, pk, local, world, rank, cpu=True):
-    """The W4 sweep and the model workloads, each a sub-result of the JSON line."""
+def _gmax(v, world, dev):
+    """Max over the ranks (the slowest rank sets a multi-GPU time)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _shared_scales(plan, world, dev):
+    """Every rank calibrated on its own batch slice: adopt the max scale of each
+    quantization point over the ranks, so all ranks quantize identically."""
+    if world == 1:
+        return
+    import torch
+    import torch.distributed as dist
+
+    t = torch.from_numpy(plan.scales()).to(dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    plan.set_scales(t.cpu().numpy())
+
+
+def _run_host(plan, x, xin, y, reps):
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        plan.run({x: xin}, [y])
+    return (time.perf_counter() - t0) / reps
+
+
+def run_configs(be, stream, flush, pk, local, world, rank, cpu=True, comm=None):
+    """The W4 sweep and the model workloads, each a sub-result of the JSON line.
+    With world > 1 the model batches are sharded over the ranks (each rank runs
+    its contiguous slice; throughput = whole batch / slowest rank), and BERT
+    also runs with FFN1 column-sharded over the ranks (NCCL all-gather inside
+    the plan)."""
     import torch
 
     from tpt_infer_b200 import graphs, synth
+    from tpt_infer_b200.sharding import batch_shard
 
     dev = f"cuda:{local}"
     out = {}
-    threads = os.cpu_count() or 1
+    par = "single GPU" if world == 1 else f"batch sharded over {world} GPUs"
 
-    # ---- W4 GEMM sweep: K = 4096, N = 11008, M in {1, 8, 64, 512}, f32 activations
+    # ---- W4 GEMM sweep: K = 4096, N = 11008, M in {1, 8, 64, 512}, f32 activations (per GPU)
     try:
         Kw, Nw = 4096, 11008
         wt = synth.normal(Nw * Kw, 2000, 0.0, 0.02)
@@ -202,48 +239,47 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True):
         for m in (1, 8, 64, 512):
             x = torch.from_numpy(synth.normal(m * Kw, 2001 + m)).to(dev)
             y = torch.empty(m * Nw, dtype=torch.float32, device=dev)
-            t = _time_device(stream, lambda: be.w4_gemm_dev(x, m, w4, None, 0, y), 10, 3, flush)
+            t = _gmax(_time_device(stream, lambda: be.w4_gemm_dev(x, m, w4, None, 0, y), 10, 3, flush), world, dev)
             by = Kw * Nw / 2 + 4 * Nw + 4 * m * Kw + 4 * m * Nw
             rows.append({"M": m, "us": t * 1e6, "TFLOP/s": 2.0 * m * Kw * Nw / t / 1e12, "GB/s": by / t / 1e9,
                          "frac_hbm": by / t / 1e9 / pk["hbm_gbs"]})
         w4.free()
-        out["w4_sweep"] = {"K": Kw, "N": Nw, "rows": rows, "l2": "flushed before each timed launch"}
+        out["w4_sweep"] = {"K": Kw, "N": Nw, "rows": rows, "l2": "flushed before each timed launch",
+                           "per": "GPU (max over ranks)"}
     except Exception as e:  # report, do not lose the headline
         out["w4_sweep"] = {"error": repr(e)}
 
     # ---- MLP [64,784] -> 512 -> ReLU -> 10 -> Softmax, f32 and INT8 PTQ
     try:
+        B = 64
+        b0, bn = batch_shard(B, world, rank)
         W = graphs.mlp_weights()
-        xin = synth.uniform(64 * 784, 77)
-        pf, xf, yf, _ = graphs.build_mlp_f32(be, 64, W)
+        xall = synth.uniform(B * 784, 77)
+        xin = xall[b0 * 784:(b0 + bn) * 784]
+        pf, xf, yf, _ = graphs.build_mlp_f32(be, bn, W)
         pf.run({xf: xin}, [yf])
-        tf = _time_device(stream, pf.run_device, 50, 5)
-        t0 = time.perf_counter()
-        for _ in range(20):
-            pf.run({xf: xin}, [yf])
-        ef = (time.perf_counter() - t0) / 20
-        pq, xq, yq, _, _ = graphs.build_mlp_int8(be, 64, W)
+        tf = _gmax(_time_device(stream, pf.run_device, 50, 5), world, dev)
+        ef = _gmax(_run_host(pf, xf, xin, yf, 20), world, dev)
+        pq, xq, yq, _, _ = graphs.build_mlp_int8(be, bn, W)
         pq.calibrate(True)
         for i in range(4):
-            pq.run({xq: synth.uniform(64 * 784, 1000 + i)}, [yq])
+            pq.run({xq: synth.uniform(B * 784, 1000 + i)[b0 * 784:(b0 + bn) * 784]}, [yq])
         pq.freeze()
+        _shared_scales(pq, world, dev)
         pq.run({xq: xin}, [yq])
-        tq = _time_device(stream, pq.run_device, 50, 5)
-        t0 = time.perf_counter()
-        for _ in range(20):
-            pq.run({xq: xin}, [yq])
-        eq = (time.perf_counter() - t0) / 20
-        mlp = {"batch": 64, "f32": {"us_per_forward": tf * 1e6, "inferences_per_s": 64 / tf,
-                                    "e2e_inferences_per_s": 64 / ef},
-               "int8": {"us_per_forward": tq * 1e6, "inferences_per_s": 64 / tq, "e2e_inferences_per_s": 64 / eq,
+        tq = _gmax(_time_device(stream, pq.run_device, 50, 5), world, dev)
+        eq = _gmax(_run_host(pq, xq, xin, yq, 20), world, dev)
+        mlp = {"batch": B, "parallelism": par,
+               "f32": {"us_per_forward": tf * 1e6, "inferences_per_s": B / tf, "e2e_inferences_per_s": B / ef},
+               "int8": {"us_per_forward": tq * 1e6, "inferences_per_s": B / tq, "e2e_inferences_per_s": B / eq,
                         "calibration": "256 seeded U[0,1) inputs"}}
         if cpu:
             from oracle import models as OM
 
             t0 = time.perf_counter()
-            OM.mlp_f32(xin, W, 64)
+            OM.mlp_f32(xall, W, B)
             c = time.perf_counter() - t0
-            mlp["cpu_baseline"] = {"value": 64 / c, "unit": "inferences/s", "cores": OM.TH, "kind": "port",
+            mlp["cpu_baseline"] = {"value": B / c, "unit": "inferences/s", "cores": OM.TH, "kind": "port",
                                    "sample": "one f32 forward of the batch of 64 (AVX matmul restatement)"}
         pf.close()
         pq.close()
@@ -253,29 +289,28 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True):
 
     # ---- ResNet-18-shaped CNN, batch 256, INT8 convs
     try:
-        B = 256
+        B, IMG = 256, 3 * 224 * 224
+        b0, bn = batch_shard(B, world, rank)
         spec = graphs.resnet18_weights(be)
-        p, x, logits = graphs.build_resnet18(be, B, spec)
+        p, x, logits = graphs.build_resnet18(be, bn, spec)
         p.calibrate(True)
-        p.run({x: synth.normal(B * 3 * 224 * 224, 31)}, [logits])
+        p.run({x: synth.normal(B * IMG, 31)[b0 * IMG:(b0 + bn) * IMG]}, [logits])
         p.freeze()
-        xin = synth.normal(B * 3 * 224 * 224, 32)
+        _shared_scales(p, world, dev)
+        xall = synth.normal(B * IMG, 32)
+        xin = xall[b0 * IMG:(b0 + bn) * IMG]
         p.run({x: xin}, [logits])
-        t = _time_device(stream, p.run_device, 5, 2)
-        t0 = time.perf_counter()
-        for _ in range(3):
-            p.run({x: xin}, [logits])
-        e2e = (time.perf_counter() - t0) / 3
+        t = _gmax(_time_device(stream, p.run_device, 5, 2), world, dev)
+        e2e = _gmax(_run_host(p, x, xin, logits, 3), world, dev)
         gop = 3.628 * B
-        res = {"batch": B, "ms_per_batch": t * 1e3, "images_per_s": B / t, "int8_TOP/s": gop / t / 1e3,
-               "e2e_images_per_s": B / e2e, "arena_GB": p.arena_bytes() / 1e9,
+        res = {"batch": B, "parallelism": par, "ms_per_batch": t * 1e3, "images_per_s": B / t,
+               "int8_TOP/s": gop / t / 1e3, "e2e_images_per_s": B / e2e, "arena_GB_per_gpu": p.arena_bytes() / 1e9,
                "calibration": "one seeded batch of 256"}
         if cpu:
             from oracle import models as OM
 
-            x1 = xin[: 3 * 224 * 224]
             t0 = time.perf_counter()
-            OM.resnet18(x1, spec, 1, scales=p.scales())
+            OM.resnet18(xall[:IMG], spec, 1, scales=p.scales())
             c = time.perf_counter() - t0
             res["cpu_baseline"] = {"value": 1 / c, "unit": "images/s", "cores": OM.TH, "kind": "port",
                                    "sample": "1 image through the oracle's INT8 node-by-node replay"}
@@ -286,32 +321,44 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True):
 
     # ---- BERT-base-shaped encoder, 12 layers, batch 64, seq 128
     try:
-        B, S = 64, 128
+        B, S, H = 64, 128, 768
+        b0, bn = batch_shard(B, world, rank)
         layers = graphs.bert_weights(be, layers=12)
-        p, x, h = graphs.build_bert(be, B, S, layers)
+        p, x, h = graphs.build_bert(be, bn, S, layers)
         p.calibrate(True)
-        p.run({x: synth.normal(B * S * 768, 41)}, [h])
+        p.run({x: synth.normal(B * S * H, 41)[b0 * S * H:(b0 + bn) * S * H]}, [h])
         p.freeze()
-        xin = synth.normal(B * S * 768, 42)
+        _shared_scales(p, world, dev)
+        xall = synth.normal(B * S * H, 42)
+        xin = xall[b0 * S * H:(b0 + bn) * S * H]
         p.run({x: xin}, [h])
-        t = _time_device(stream, p.run_device, 5, 2)
-        t0 = time.perf_counter()
-        for _ in range(3):
-            p.run({x: xin}, [h])
-        e2e = (time.perf_counter() - t0) / 3
-        bert = {"batch": B, "seq": S, "layers": 12, "ms_per_batch": t * 1e3, "sequences_per_s": B / t,
-                "int8_TOP/s": 1392.0 / t / 1e3, "e2e_sequences_per_s": B / e2e, "arena_GB": p.arena_bytes() / 1e9,
-                "calibration": "one seeded batch"}
+        t = _gmax(_time_device(stream, p.run_device, 5, 2), world, dev)
+        e2e = _gmax(_run_host(p, x, xin, h, 3), world, dev)
+        bert = {"batch": B, "seq": S, "layers": 12, "parallelism": par, "ms_per_batch": t * 1e3,
+                "sequences_per_s": B / t, "int8_TOP/s": 1392.0 / t / 1e3, "e2e_sequences_per_s": B / e2e,
+                "arena_GB_per_gpu": p.arena_bytes() / 1e9, "calibration": "one seeded batch"}
         if cpu:
             from oracle import models as OM
 
-            x1 = xin[: S * 768]
             t0 = time.perf_counter()
-            OM.bert(x1, layers[:1], 1, S, scales=p.scales()[:4])
+            OM.bert(xall[:S * H], layers[:1], 1, S, scales=p.scales()[:4])
             c = time.perf_counter() - t0
             bert["cpu_baseline"] = {"value": 1 / (12 * c), "unit": "sequences/s", "cores": OM.TH, "kind": "port",
                                     "sample": "1 layer of 1 sequence through the oracle replay, x12 layers"}
         p.close()
+        if comm is not None and world > 1:
+            # every rank holds the whole batch; FFN1 is column-sharded and all-gathered (NCCL) per layer
+            p, x, h = graphs.build_bert(be, B, S, layers, ffn_shard=comm)
+            p.calibrate(True)
+            p.run({x: synth.normal(B * S * H, 41)}, [h])
+            p.freeze()
+            p.run({x: xall}, [h])
+            t = _gmax(_time_device(stream, p.run_device, 5, 2), world, dev)
+            bert["ffn_column_sharded"] = {
+                "ms_per_batch": t * 1e3, "sequences_per_s": B / t,
+                "parallelism": f"FFN1 split over {world} GPUs by output channel, int8 all-gather "
+                               f"({B * S * 3072 / 1e6:.0f} MB per layer) inside the plan; the rest replicated"}
+            p.close()
         out["bert"] = bert
     except Exception as e:
         out["bert"] = {"error": repr(e)}
@@ -468,7 +515,14 @@ def main():
 
     configs = None
     if not args.no_configs:
-        configs = run_configs(be, stream, flush, pk, local, world, rank, cpu=(rank == 0 and world == 1))
+        comm = None
+        if world > 1:
+            from tpt_infer_b200 import sharding
+
+            comm = sharding.Comm.create(be, world, rank, sharding.torch_broadcast)
+        configs = run_configs(be, stream, flush, pk, local, world, rank, cpu=(rank == 0 and world == 1), comm=comm)
+        if comm is not None:
+            comm.close()
 
     if rank == 0:
         line = {

@@ -246,7 +246,8 @@ typedef struct tpt_cuda_plan tpt_cuda_plan;
 enum { TPT_DT_F32 = 0, TPT_DT_I8 = 1 };
 
 enum tpt_op_kind {
-    TPT_OP_QUANTIZE = 1,        /* in0 f32 [d0] -> out i8, per-tensor scale */
+    TPT_OP_QUANTIZE = 1,        /* in0 f32 [d0] -> out i8, per-tensor scale; d1 != 0: the calibration max is
+                                   reduced over the plan's communicator (a column-sharded tensor) */
     TPT_OP_LINEAR_W8A8 = 2,     /* in0 i8 [d0, w.k] x w -> out f32 [d0, w.n]; in1 bias (or -1); act */
     TPT_OP_MATMUL_F32 = 3,      /* in0 [d0,d1] x in1 [d1,d2] -> out; in2 bias (or -1); act (Backend::matmul) */
     TPT_OP_BIAS_ACT = 4,        /* out[d0,d1] = act(in0 + in1[d1]) (in1 may be -1) */
@@ -257,7 +258,11 @@ enum tpt_op_kind {
     TPT_OP_NCHW_TO_NHWC_Q8 = 9, /* in0 f32 NCHW [d0, d1, d2=H*W] -> out i8 NHWC, per-tensor scale */
     TPT_OP_IM2COL = 10,         /* in0 i8 NHWC -> out i8 [N*OH*OW, Kp]; d0..d12 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW,Kp */
     TPT_OP_MAXPOOL_NHWC = 11,   /* f32; d0..d11 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW */
-    TPT_OP_GAP_NHWC = 12        /* f32 [d0, d1=H*W, d2] -> [d0, d2] */
+    TPT_OP_GAP_NHWC = 12,       /* f32 [d0, d1=H*W, d2] -> [d0, d2] */
+    TPT_OP_ALLGATHER = 13,      /* in0 [d0 elements] on every rank -> out [world * d0] in rank order (NCCL,
+                                   on the context stream; the plan needs a communicator) */
+    TPT_OP_PANELS_TO_ROWS = 14  /* i8 [d0 = P][d1 = T][d2 = C] -> i8 [T][P * C] (gathered column shards ->
+                                   the K-contiguous rows of the next GEMM) */
 };
 
 typedef struct tpt_plan_op {
@@ -285,11 +290,38 @@ int tpt_cuda_plan_freeze_scales(tpt_cuda_plan *plan);
 /* The static scales of the quantization points, in op order (0 = none yet);
  * *count receives the number of points. Lets a calibration be exported. */
 int tpt_cuda_plan_get_scales(tpt_cuda_plan *plan, float *scales, size_t n, size_t *count);
+/* Imports a calibration: n must equal the number of points, every scale > 0;
+ * the plan leaves calibration mode. (Batch-sharded ranks share one.) */
+int tpt_cuda_plan_set_scales(tpt_cuda_plan *plan, const float *scales, size_t n);
 /* ops only, inputs already resident (async) */
 int tpt_cuda_plan_run_device(tpt_cuda_plan *plan);
 /* H2D of the inputs, the ops, D2H of the outputs, then synchronise */
 int tpt_cuda_plan_run(tpt_cuda_plan *plan, const int *in_ids, const float *const *inputs, size_t n_in,
                       const int *out_ids, float *const *outputs, size_t n_out);
+
+/* ------------------------------------------------------------------ */
+/* Multi-GPU (one process per GPU on one node)                          */
+/* ------------------------------------------------------------------ */
+
+/* No counterpart in the reference (tpt-infer is single-process): the
+ * exchange step of the column-sharded configuration. An NCCL communicator is
+ * made from a unique id that rank 0 creates and the caller distributes to the
+ * other ranks over any out-of-band channel. Collectives are enqueued on the
+ * context's stream; every rank must issue the same ones in the same order.
+ * NCCL is loaded at run time (libnccl.so.2): TPT_UNSUPPORTED when absent;
+ * set-up that does not complete within 120 s returns TPT_NCCL_ERROR. Destroy a
+ * communicator before its context. */
+#define TPT_COMM_ID_BYTES 128
+typedef struct tpt_cuda_comm tpt_cuda_comm;
+int tpt_cuda_comm_unique_id(unsigned char *id, size_t id_bytes);
+int tpt_cuda_comm_create(tpt_cuda_ctx *ctx, const unsigned char *id, size_t id_bytes, int world, int rank,
+                         tpt_cuda_comm **out);
+int tpt_cuda_comm_destroy(tpt_cuda_comm *comm);
+int tpt_cuda_comm_size(const tpt_cuda_comm *comm, int *world, int *rank);
+/* out [world * bytes_per_rank] = the ranks' in [bytes_per_rank], rank order (device pointers, async) */
+int tpt_cuda_all_gather_dev(tpt_cuda_comm *comm, const void *in, void *out, size_t bytes_per_rank);
+/* The communicator of a plan's ALLGATHER ops and rank-global quantization points. */
+int tpt_cuda_plan_set_comm(tpt_cuda_plan *plan, tpt_cuda_comm *comm);
 
 /* ------------------------------------------------------------------ */
 /* Allocation-free quantization                                         */

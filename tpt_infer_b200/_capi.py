@@ -85,9 +85,19 @@ SIGNATURES = {
     "tpt_cuda_plan_set_calibration": (C.c_int, [vp, C.c_int]),
     "tpt_cuda_plan_freeze_scales": (C.c_int, [vp]),
     "tpt_cuda_plan_get_scales": (C.c_int, [vp, vp, sz, szp]),
+    "tpt_cuda_plan_set_scales": (C.c_int, [vp, vp, sz]),
     "tpt_cuda_plan_run_device": (C.c_int, [vp]),
     "tpt_cuda_plan_run": (C.c_int, [vp, vp, vp, sz, vp, vp, sz]),
+    # multi-GPU
+    "tpt_cuda_comm_unique_id": (C.c_int, [vp, sz]),
+    "tpt_cuda_comm_create": (C.c_int, [vp, vp, sz, C.c_int, C.c_int, C.POINTER(vp)]),
+    "tpt_cuda_comm_destroy": (C.c_int, [vp]),
+    "tpt_cuda_comm_size": (C.c_int, [vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "tpt_cuda_all_gather_dev": (C.c_int, [vp, vp, vp, sz]),
+    "tpt_cuda_plan_set_comm": (C.c_int, [vp, vp]),
 }
+
+COMM_ID_BYTES = 128
 
 
 class PlanOp(C.Structure):

@@ -327,6 +327,42 @@ int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, 
     return after_launch(ctx, "global_avgpool");
 }
 
+namespace {
+// [P][T][C] int8 panels (the all-gathered column shards) -> [T][P*C] rows, the
+// K-contiguous A operand of the next GEMM; 16 bytes per thread (C % 16 == 0).
+__global__ void k_panels_to_rows16(const int4 *__restrict__ in, int4 *__restrict__ out, int P, size_t T, int C16) {
+    const size_t total = (size_t)P * T * C16;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % C16);
+        const size_t pt = i / C16;
+        const size_t t = pt % T;
+        const int pp = (int)(pt / T);
+        out[(t * P + pp) * C16 + c] = __ldcs(in + i);
+    }
+}
+__global__ void k_panels_to_rows1(const int8_t *__restrict__ in, int8_t *__restrict__ out, int P, size_t T, int C) {
+    const size_t total = (size_t)P * T * C;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % C);
+        const size_t pt = i / C;
+        const size_t t = pt % T;
+        const int pp = (int)(pt / T);
+        out[(t * P + pp) * C + c] = in[i];
+    }
+}
+}  // namespace
+
+int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int P, size_t T, int C) {
+    const size_t total = (size_t)P * T * C;
+    if (C % 16 == 0 && ((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+        k_panels_to_rows16<<<grid_1d(total / 16, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const int4 *>(in), reinterpret_cast<int4 *>(out), P, T, C / 16);
+    } else {
+        k_panels_to_rows1<<<grid_1d(total, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(in, out, P, T, C);
+    }
+    return after_launch(ctx, "panels_to_rows");
+}
+
 int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell) {
     k_absmax_acc<<<grid_1d(n, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(x, n, cell);
     return after_launch(ctx, "absmax");

@@ -34,6 +34,9 @@ int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int 
                         int sw, int ph, int pw, int OH, int OW);
 int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, int C);
 int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell);
+int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int P, size_t T, int C);
+int comm_all_gather(tpt_cuda_comm *c, const void *in, void *out, size_t bytes_per_rank);
+int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
 }  // namespace tpt
 
 using namespace tpt;
@@ -55,6 +58,7 @@ struct PlanOp {
 
 struct tpt_cuda_plan {
     tpt_cuda_ctx *ctx = nullptr;
+    tpt_cuda_comm *comm = nullptr;  // multi-GPU plans: ALLGATHER and rank-global scales
     int device = 0;  // destroying needs only the device: the context may be gone
     std::vector<PlanTensor> tensors;
     std::vector<PlanOp> ops;
@@ -77,7 +81,10 @@ float *F(tpt_cuda_plan *p, int id) { return id < 0 ? nullptr : static_cast<float
 int8_t *Q(tpt_cuda_plan *p, int id) { return id < 0 ? nullptr : static_cast<int8_t *>(p->tensors[id].ptr); }
 
 // Scale for a quantization point: frozen/static, or (calibrating) measured now.
-int point_scale(tpt_cuda_plan *p, PlanOp &po, const float *x, size_t n, float *scale) {
+// A rank-global point (a column-sharded tensor that is all-gathered next)
+// takes the max over the plan's communicator, so every rank quantizes its
+// shard with the scale of the whole tensor.
+int point_scale(tpt_cuda_plan *p, PlanOp &po, const float *x, size_t n, float *scale, bool global = false) {
     if (!p->calibrating) {
         if (!(po.frozen > 0.0f)) return TPT_INVALID;  // not calibrated and no static scale given
         *scale = po.frozen;
@@ -89,6 +96,11 @@ int point_scale(tpt_cuda_plan *p, PlanOp &po, const float *x, size_t n, float *s
     if (e != cudaSuccess) return cuda_fail(ctx, e, "calibration cell clear");
     int st = launch_absmax_acc(ctx, x, n, cell);
     if (st) return st;
+    if (global) {
+        if (!p->comm) return TPT_INVALID;
+        st = comm_max_u32(p->comm, cell, 1);
+        if (st) return st;
+    }
     unsigned bits = 0;
     st = d2h(ctx, &bits, cell, 4);
     if (st) return st;
@@ -108,9 +120,9 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
     const size_t *d = o.dims;
     int st = TPT_OK;
     switch (o.kind) {
-        case TPT_OP_QUANTIZE: {  // f32 [n] -> i8 [n], per-tensor scale
+        case TPT_OP_QUANTIZE: {  // f32 [n] -> i8 [n], per-tensor scale (d1 != 0: rank-global)
             float s;
-            st = point_scale(p, po, F(p, o.in0), d[0], &s);
+            st = point_scale(p, po, F(p, o.in0), d[0], &s, d[1] != 0);
             if (st) return st;
             p->tensors[o.out].scale = s;
             return launch_quant_i8_static(ctx, F(p, o.in0), d[0], s, Q(p, o.out));
@@ -137,6 +149,15 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
             return launch_add_act(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], o.act);
         case TPT_OP_SOFTMAX:
             return launch_softmax(ctx, F(p, o.in0), F(p, o.out), d[0], d[1]);
+        case TPT_OP_ALLGATHER: {  // in0 [d0 elements] on every rank -> out [world * d0], rank order
+            if (!p->comm) return TPT_INVALID;
+            p->tensors[o.out].scale = p->tensors[o.in0].scale;
+            return comm_all_gather(p->comm, p->tensors[o.in0].ptr, p->tensors[o.out].ptr,
+                                   d[0] * dt_size(p->tensors[o.in0].dtype));
+        }
+        case TPT_OP_PANELS_TO_ROWS:  // i8 [d0 = P][d1 = T][d2 = C] -> i8 [T][P * C]
+            p->tensors[o.out].scale = p->tensors[o.in0].scale;
+            return launch_panels_to_rows(ctx, Q(p, o.in0), Q(p, o.out), (int)d[0], d[1], (int)d[2]);
         case TPT_OP_LAYERNORM:
             return launch_layernorm(ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), F(p, o.out), d[0], d[1], o.f0);
         case TPT_OP_ATTENTION:
@@ -225,7 +246,18 @@ int tpt_cuda_plan_add_op(tpt_cuda_plan *p, const tpt_plan_op *op) {
     if (!valid_id(p, op->in0) || !valid_id(p, op->out)) return TPT_INVALID;
     if ((op->in1 >= 0 && !valid_id(p, op->in1)) || (op->in2 >= 0 && !valid_id(p, op->in2))) return TPT_INVALID;
     if (op->kind == TPT_OP_LINEAR_W8A8 && (!op->w || op->w->kind != 8)) return TPT_INVALID;
-    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_GAP_NHWC) return TPT_UNSUPPORTED;
+    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_PANELS_TO_ROWS) return TPT_UNSUPPORTED;
+    if (op->kind == TPT_OP_ALLGATHER) {
+        const PlanTensor &a = p->tensors[op->in0], &b = p->tensors[op->out];
+        if (a.dtype != b.dtype || op->dims[0] > a.numel) return TPT_INVALID;
+    }
+    if (op->kind == TPT_OP_PANELS_TO_ROWS) {
+        const PlanTensor &a = p->tensors[op->in0], &b = p->tensors[op->out];
+        size_t n = 0;
+        if (a.dtype != TPT_DT_I8 || b.dtype != TPT_DT_I8 || op->dims[0] == 0 || op->dims[2] == 0 ||
+            !checked_mul(op->dims[0] * op->dims[2], op->dims[1], &n) || n > a.numel || n > b.numel)
+            return TPT_INVALID;
+    }
     PlanOp po;
     po.op = *op;
     if (op->kind == TPT_OP_QUANTIZE || op->kind == TPT_OP_NCHW_TO_NHWC_Q8) {
@@ -256,6 +288,12 @@ int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
         if (!t.is_const) t.ptr = p->arena + t.offset;
     p->cal_max.assign(p->n_cells, 0.0f);
     p->finalized = true;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_set_comm(tpt_cuda_plan *p, tpt_cuda_comm *comm) {
+    CHECK_PLAN(p);
+    p->comm = comm;
     return TPT_OK;
 }
 
@@ -298,6 +336,18 @@ int tpt_cuda_plan_get_scales(tpt_cuda_plan *p, float *scales, size_t n, size_t *
             c++;
         }
     if (count) *count = c;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_set_scales(tpt_cuda_plan *p, const float *scales, size_t n) {
+    CHECK_PLAN(p);
+    if (!scales || n != (size_t)p->n_cells) return TPT_INVALID;
+    for (size_t i = 0; i < n; i++)
+        if (!(scales[i] > 0.0f)) return TPT_INVALID;
+    size_t c = 0;
+    for (auto &po : p->ops)
+        if (po.cell >= 0) po.frozen = scales[c++];
+    p->calibrating = false;
     return TPT_OK;
 }
 

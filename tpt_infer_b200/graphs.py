@@ -32,6 +32,7 @@ from .backend import ACT_GELU, ACT_NONE, ACT_RELU, CudaBackend, OpError
 F32, I8 = 0, 1
 OP_QUANTIZE, OP_LINEAR, OP_MATMUL, OP_BIAS_ACT, OP_ADD_ACT, OP_SOFTMAX, OP_LAYERNORM, OP_ATTENTION = range(1, 9)
 OP_NCHW_Q8, OP_IM2COL, OP_MAXPOOL, OP_GAP = 9, 10, 11, 12
+OP_ALLGATHER, OP_PANELS_TO_ROWS = 13, 14
 
 
 class Plan:
@@ -70,6 +71,11 @@ class Plan:
             o.dims[j] = int(d)
         self.be._check(lib.tpt_cuda_plan_add_op(self.h, C.byref(o)))
 
+    def set_comm(self, comm):
+        """The communicator of the plan's ALLGATHER ops and rank-global scales."""
+        self.comm = comm
+        self.be._check(lib.tpt_cuda_plan_set_comm(self.h, comm.h))
+
     def finalize(self):
         self.be._check(lib.tpt_cuda_plan_finalize(self.h))
 
@@ -96,6 +102,11 @@ class Plan:
         out = np.zeros(n.value, np.float32)
         lib.tpt_cuda_plan_get_scales(self.h, out.ctypes.data_as(C.c_void_p), n.value, C.byref(n))
         return out
+
+    def set_scales(self, scales):
+        """Imports static scales (one per quantization point, op order)."""
+        a = np.ascontiguousarray(scales, np.float32)
+        self.be._check(lib.tpt_cuda_plan_set_scales(self.h, a.ctypes.data_as(C.c_void_p), a.size))
 
     def run_device(self):
         self.be._check(lib.tpt_cuda_plan_run_device(self.h))
@@ -341,14 +352,24 @@ def bert_weights(be, layers=12, seed=5000, hidden=768, ffn=3072):
     return out
 
 
-def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-5):
+def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-5, ffn_shard=None):
+    """``ffn_shard`` = a sharding.Comm: FFN1 column-sharded over its ranks and
+    reassembled by an all-gather inside the plan (see sharding.py)."""
+    from . import sharding
+
     p = Plan(be)
+    if ffn_shard is not None:
+        p.set_comm(ffn_shard)
     T = batch * seq
     x = p.tensor(F32, T * hidden)
     cur = x
     for lw in layers_w:
         hs = []
-        for ql in (lw.qkv, lw.o, lw.f1, lw.f2):
+        f1 = lw.f1
+        if ffn_shard is not None:
+            c0, cn = sharding.column_shard(ffn, ffn_shard.world, ffn_shard.rank)
+            f1 = sharding.slice_qlinear(lw.f1, c0, cn)
+        for ql in (lw.qkv, lw.o, f1, lw.f2):
             wh = be.upload_i8(ql.q, ql.scales, ql.n, ql.k)
             p.weights.append(wh)
             hs.append(wh)
@@ -368,10 +389,21 @@ def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-
         p.op(OP_LAYERNORM, r1, h1, in1=p.const(lw.g1), in2=p.const(lw.b1), f0=eps, dims=(T, hidden))
         hq = p.tensor(I8, T * hidden)
         p.op(OP_QUANTIZE, h1, hq, dims=(T * hidden,))
-        f = p.tensor(F32, T * ffn)
-        p.op(OP_LINEAR, hq, f, in1=p.const(lw.f1.bias), w=hs[2], act=ACT_GELU, dims=(T,))
-        fq = p.tensor(I8, T * ffn)
-        p.op(OP_QUANTIZE, f, fq, dims=(T * ffn,))
+        if ffn_shard is None:
+            f = p.tensor(F32, T * ffn)
+            p.op(OP_LINEAR, hq, f, in1=p.const(f1.bias), w=hs[2], act=ACT_GELU, dims=(T,))
+            fq = p.tensor(I8, T * ffn)
+            p.op(OP_QUANTIZE, f, fq, dims=(T * ffn,))
+        else:
+            P, cn = ffn_shard.world, f1.n
+            fs = p.tensor(F32, T * cn)  # this rank's output channels
+            p.op(OP_LINEAR, hq, fs, in1=p.const(f1.bias), w=hs[2], act=ACT_GELU, dims=(T,))
+            fsq = p.tensor(I8, T * cn)
+            p.op(OP_QUANTIZE, fs, fsq, dims=(T * cn, 1))  # scale of the whole [T, ffn] tensor
+            g = p.tensor(I8, P * T * cn)
+            p.op(OP_ALLGATHER, fsq, g, dims=(T * cn,))
+            fq = p.tensor(I8, T * ffn)
+            p.op(OP_PANELS_TO_ROWS, g, fq, dims=(P, T, cn))
         f2 = p.tensor(F32, T * hidden)
         p.op(OP_LINEAR, fq, f2, in1=p.const(lw.f2.bias), w=hs[3], dims=(T,))
         r2 = p.tensor(F32, T * hidden)
