@@ -92,20 +92,38 @@ def test_resnet18_plan_bit_exact_batch2(cuda):
     p.close()
 
 
-def test_bert_plan_two_layers(cuda):
+@pytest.mark.parametrize("B,S", [(2, 128), (3, 80)])
+def test_bert_plan_two_layers(cuda, B, S):
     from tpt_infer_b200 import graphs, synth
 
     layers = graphs.bert_weights(cuda, layers=2)
-    p, x, out = graphs.build_bert(cuda, 2, 128, layers)
-    xcal = synth.normal(2 * 128 * 768, 41)
+    p, x, out = graphs.build_bert(cuda, B, S, layers)
+    xcal = synth.normal(B * S * 768, 41)
     p.calibrate(True)
     p.run({x: xcal}, [out])
     p.freeze()
     scales = p.scales()
     assert scales.size == 8 and np.all(scales > 0)
-    xin = synth.normal(2 * 128 * 768, 42)
+    xin = synth.normal(B * S * 768, 42)
     got, = p.run({x: xin}, [out])
-    want = OM.bert(xin, layers, 2, 128, scales=scales)
+    want = OM.bert(xin, layers, B, S, scales=scales)
     assert np.all(np.isfinite(got))
     assert _relerr(got, want) <= 5e-3
     p.close()
+
+
+@pytest.mark.parametrize("B,S", [(2, 128), (1, 77)])
+def test_attention_op(cuda, B, S):
+    # the fused attention op alone against the oracle's MatMul / Softmax / MatMul
+    from tpt_infer_b200 import graphs, synth
+
+    qkv = synth.normal(B * S * 3 * 768, 45)
+    pa = graphs.Plan(cuda)
+    tq = pa.tensor(graphs.F32, qkv.size)
+    to = pa.tensor(graphs.F32, B * S * 768)
+    pa.op(graphs.OP_ATTENTION, tq, to, f0=0.125, dims=(B, S, 12, 64))
+    pa.finalize()
+    att = pa.run({tq: qkv}, [to])[0]
+    pa.close()
+    want = OM._attention(qkv, B, S, 12, 64, 0.125).ravel()
+    assert np.max(np.abs(att - want)) <= 1e-5 * (1 + np.max(np.abs(want)))

@@ -106,6 +106,14 @@ inline unsigned grid_1d(size_t n, unsigned block, unsigned cap = 148u * 16u) {
 
 bool checked_mul(size_t a, size_t b, size_t *r);
 
+// An int8 output for a W8A8 epilogue: y is requantized with the next
+// quantization point's static scale (clamp(roundf(y / scale)), exactly the
+// separate QUANTIZE op), so the f32 tensor is never written.
+struct Requant {
+    int8_t *q = nullptr;
+    float scale = 0.0f;
+};
+
 // ---- launchers implemented across the .cu files (device pointers, async) ----
 int launch_add(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t n);
 int launch_unary(tpt_cuda_ctx *ctx, int op, const float *a, float *out, size_t n);  // 1 relu 2 sigmoid 3 gelu
@@ -130,9 +138,10 @@ int launch_dequant_i8_rows(tpt_cuda_ctx *ctx, const int8_t *q, size_t rows, size
                            const float *scales, float *out);
 int launch_dequant_i4_rows(tpt_cuda_ctx *ctx, const uint8_t *p, size_t rows, size_t row_elems,
                            size_t packed_len, const float *scales, float *out);
-// i8 GEMM: y[m,n] (+bias, act) or raw i32 acc when acc != nullptr; W^T [n,k].
+// i8 GEMM: y[m,n] (+bias, act), raw i32 acc when acc != nullptr, or y
+// requantized to int8 when rq.q != nullptr; W^T [n,k].
 int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w,
-                float a_scale, const float *bias, int act, float *y, int32_t *acc);
+                float a_scale, const float *bias, int act, float *y, int32_t *acc, Requant rq = Requant{});
 int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w,
               const float *bias, int act, float *y);
 
@@ -176,6 +185,11 @@ __device__ __forceinline__ int8_t round_clamp_i8(float v, float lo, float hi) {
     if (isnan(v)) return 0;
     v = fminf(fmaxf(v, lo), hi);
     return (int8_t)(int)v;
+}
+
+// quantize_i8_static's rule for one value: clamp(roundf(y / scale), -127, 127)
+__device__ __forceinline__ int8_t requant_i8(float y, float scale) {
+    return round_clamp_i8(__fdiv_rn(y, scale), -127.0f, 127.0f);
 }
 
 }  // namespace tpt

@@ -163,6 +163,44 @@ __global__ void __launch_bounds__(NT) k_gemm_f32(const float *__restrict__ A, co
     }
 }
 
+// Small-output MatMul (MODE 0 arithmetic): 16x16 outputs per 256-thread CTA,
+// one output per thread, k-slices of 32 through shared memory. Used when the
+// 128x128 tiling would leave most SMs idle (e.g. [64,784]x[784,512]): the
+// outputs are latency-bound sequential chains, so more of them run at once;
+// the per-output RN multiply-then-add order is unchanged.
+constexpr int SB = 16, SK = 32;
+__global__ void __launch_bounds__(256) k_gemm_f32_small(const float *__restrict__ A, const float *__restrict__ B,
+                                                       float *__restrict__ Cout, int M, int N, int K) {
+    __shared__ float As[SK][SB + 1];
+    __shared__ float Bs[SK][SB + 1];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * SB, n0 = blockIdx.x * SB;
+    float acc = 0.0f;
+    for (int k0 = 0; k0 < K; k0 += SK) {
+        // A tile [16 rows][32 k] and B tile [32 k][16 cols]: 2 values per thread each
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int e = tid + 256 * i;
+            const int ar = e >> 5, ac = e & 31;
+            const int m = m0 + ar, ka = k0 + ac;
+            As[ac][ar] = (m < M && ka < K) ? A[(size_t)m * K + ka] : 0.0f;
+            const int br = e >> 4, bc = e & 15;
+            const int kb = k0 + br, n = n0 + bc;
+            Bs[br][bc] = (kb < K && n < N) ? B[(size_t)kb * N + n] : 0.0f;
+        }
+        __syncthreads();
+        if (K - k0 >= SK) {
+#pragma unroll
+            for (int kk = 0; kk < SK; kk++) acc = __fadd_rn(acc, __fmul_rn(As[kk][ty], Bs[kk][tx]));
+        } else {
+            for (int kk = 0; kk < K - k0; kk++) acc = __fadd_rn(acc, __fmul_rn(As[kk][ty], Bs[kk][tx]));
+        }
+        __syncthreads();
+    }
+    const int m = m0 + ty, n = n0 + tx;
+    if (m < M && n < N) Cout[(size_t)m * N + n] = acc;
+}
+
 }  // namespace
 
 int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m, size_t k,
@@ -173,6 +211,12 @@ int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *
         return e == cudaSuccess ? TPT_OK : cuda_fail(ctx, e, "matmul k=0 memset");
     }
     dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
+    if ((size_t)grid.x * grid.y < (size_t)ctx->sm_count) {
+        dim3 sg((unsigned)((n + SB - 1) / SB), (unsigned)((m + SB - 1) / SB));
+        if (sg.y > 65535) return TPT_UNSUPPORTED;
+        k_gemm_f32_small<<<sg, 256, 0, ctx->stream>>>(a, b, out, (int)m, (int)n, (int)k);
+        return after_launch(ctx, "matmul_f32_small");
+    }
     if (grid.y > 65535) return TPT_UNSUPPORTED;
     ConvGeom g{};
     k_gemm_f32<0><<<grid, NT, 0, ctx->stream>>>(a, b, out, (int)m, (int)n, (int)k, g, W4Epi{});

@@ -7,6 +7,8 @@
 // [N*H*W, C] and no transposes are needed between layers.
 #include <float.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tpt {
@@ -19,7 +21,7 @@ namespace {
 // the row held in registers (cols <= 32 * LN_MAX).
 constexpr int LN_MAX = 32;
 __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ b,
-                            float *__restrict__ y, int rows, int cols, float eps) {
+                            float *__restrict__ y, int rows, int cols, float eps, int8_t *__restrict__ qout, float qs) {
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -46,7 +48,11 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 #pragma unroll
         for (int i = 0; i < LN_MAX; i++) {
             const int c = lane + 32 * i;
-            if (c < cols) y[(size_t)r * cols + c] = (v[i] - mean) * inv * __ldg(g + c) + __ldg(b + c);
+            if (c < cols) {
+                const float o = (v[i] - mean) * inv * __ldg(g + c) + __ldg(b + c);
+                y[(size_t)r * cols + c] = o;
+                if (qout) qout[(size_t)r * cols + c] = requant_i8(o, qs);  // the next QUANTIZE, fused
+            }
         }
     }
 }
@@ -57,77 +63,133 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 // writing ctx [B*S, H*D]. One CTA per (batch, head, 64-query block); K and V of
 // the head are staged in shared memory; each thread owns one query row and
 // runs an online (streaming) softmax over key blocks of 16.
-constexpr int AT_D = 64;    // head dimension
-constexpr int AT_Q = 64;    // queries per CTA
-constexpr int AT_KB = 16;   // keys per online-softmax block
-__global__ void __launch_bounds__(AT_Q) k_attention(const float *__restrict__ qkv, float *__restrict__ out, int S,
-                                                    int H, float scale) {
-    extern __shared__ float sm[];
-    float *Ks = sm;                 // [S][AT_D]
-    float *Vs = sm + (size_t)S * AT_D;
-    const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * AT_Q;
+constexpr int AT_D = 64;     // head dimension
+constexpr int AT_S = 128;    // sequence length handled by the tiled kernel
+constexpr int AT_LD = AT_S + 4;  // padded row of the transposed tiles
+// Shared memory of k_attention: Q^T and K^T [D][S+4] (whose space P^T [S][S+4]
+// reuses once the scores are in registers) and V [S][D]: ~100 KB, 2 CTAs/SM.
+constexpr size_t AT_SMEM = (size_t)(2 * AT_D * AT_LD + AT_S * AT_D) * sizeof(float);
+static_assert(AT_S * AT_LD <= 2 * AT_D * AT_LD, "P^T fits in the Q^T/K^T space");
+
+// Attention for one (batch, head) per 256-thread CTA, S <= 128 (keys past S
+// masked out, queries past S not stored), D = 64, f32:
+//   S = scale * Q K^T            8x8 scores per thread (register tile)
+//   P = softmax(S) by rows       max-subtract, exp, sum, divide (naive.rs:104-125)
+//   O = P V                      8x4 outputs per thread
+// Q^T, K^T and P^T are held transposed in shared memory so every inner step
+// is two float4 loads feeding 32-64 FMAs. qkv rows are [q | k | v] of H*D each.
+__global__ void __launch_bounds__(256) k_attention(const float *__restrict__ qkv, float *__restrict__ out, int S,
+                                                   int H, float scale) {
+    extern __shared__ __align__(16) float sm[];
+    float *Qt = sm;                          // [D][LD]
+    float *Kt = Qt + AT_D * AT_LD;           // [D][LD]
+    float *Vs = Kt + AT_D * AT_LD;           // [S][D]
+    float *Pt = sm;                          // [S(key)][LD(query)], over Q^T/K^T after the scores
+    const int b = blockIdx.y, h = blockIdx.x, tid = threadIdx.x;
     const int ld = 3 * H * AT_D;
-    const float *base = qkv + (size_t)b * S * ld;
-    for (int i = threadIdx.x; i < S * (AT_D / 4); i += blockDim.x) {
-        const int j = i / (AT_D / 4), c4 = i - j * (AT_D / 4);
-        const float4 kv = *reinterpret_cast<const float4 *>(base + (size_t)j * ld + H * AT_D + h * AT_D + 4 * c4);
-        const float4 vv = *reinterpret_cast<const float4 *>(base + (size_t)j * ld + 2 * H * AT_D + h * AT_D + 4 * c4);
-        *reinterpret_cast<float4 *>(Ks + j * AT_D + 4 * c4) = kv;
-        *reinterpret_cast<float4 *>(Vs + j * AT_D + 4 * c4) = vv;
+    const float *base = qkv + (size_t)b * S * ld + h * AT_D;
+    // load: thread -> (row, 4 consecutive d); rows past S are zero
+    for (int i = tid; i < AT_S * (AT_D / 4); i += 256) {
+        const int r = i / (AT_D / 4), d4 = (i % (AT_D / 4)) * 4;
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 q = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + d4) : z;
+        const float4 k = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + H * AT_D + d4) : z;
+        const float4 v = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + 2 * H * AT_D + d4) : z;
+        Qt[(d4 + 0) * AT_LD + r] = q.x * scale;
+        Qt[(d4 + 1) * AT_LD + r] = q.y * scale;
+        Qt[(d4 + 2) * AT_LD + r] = q.z * scale;
+        Qt[(d4 + 3) * AT_LD + r] = q.w * scale;
+        Kt[(d4 + 0) * AT_LD + r] = k.x;
+        Kt[(d4 + 1) * AT_LD + r] = k.y;
+        Kt[(d4 + 2) * AT_LD + r] = k.z;
+        Kt[(d4 + 3) * AT_LD + r] = k.w;
+        *reinterpret_cast<float4 *>(Vs + r * AT_D + d4) = v;
     }
     __syncthreads();
-    const int qi = q0 + threadIdx.x;
-    if (qi >= S) return;
-    float q[AT_D], o[AT_D];
-    const float *qr = base + (size_t)qi * ld + h * AT_D;
+
+    // S = Q K^T: thread (ty, tx) owns queries ty*4 + {0..3} and 64 + ty*4 + {0..3},
+    // keys tx*4 + {0..3} and 64 + tx*4 + {0..3}
+    const int tx = tid & 15, ty = tid >> 4;
+    float acc[8][8];
 #pragma unroll
-    for (int d = 0; d < AT_D; d += 4) {
-        const float4 t = *reinterpret_cast<const float4 *>(qr + d);
-        q[d] = t.x * scale;
-        q[d + 1] = t.y * scale;
-        q[d + 2] = t.z * scale;
-        q[d + 3] = t.w * scale;
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+#pragma unroll 4
+    for (int d = 0; d < AT_D; d++) {
+        const float4 a0 = *reinterpret_cast<const float4 *>(Qt + d * AT_LD + ty * 4);
+        const float4 a1 = *reinterpret_cast<const float4 *>(Qt + d * AT_LD + 64 + ty * 4);
+        const float4 b0 = *reinterpret_cast<const float4 *>(Kt + d * AT_LD + tx * 4);
+        const float4 b1 = *reinterpret_cast<const float4 *>(Kt + d * AT_LD + 64 + tx * 4);
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();  // every thread has read Q^T/K^T: P^T may overwrite them
+    // scores to P^T [key][query]
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int q = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int k = j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4);
+            Pt[k * AT_LD + q] = k < S ? acc[i][j] : -INFINITY;
+        }
+    }
+    __syncthreads();
+
+    // softmax over keys for each query (a column of P^T): warp w owns queries
+    // w, w + 8, ...; lane covers keys lane + 32 c
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int q = warp; q < S; q += 8) {
+        float v[AT_S / 32];
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < AT_S / 32; c++) {
+            v[c] = Pt[(lane + 32 * c) * AT_LD + q];
+            m = fmaxf(m, v[c]);
+        }
+        m = warp_max(m);
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < AT_S / 32; c++) {
+            v[c] = expf(v[c] - m);
+            sum += v[c];
+        }
+        sum = warp_sum(sum);
+#pragma unroll
+        for (int c = 0; c < AT_S / 32; c++) Pt[(lane + 32 * c) * AT_LD + q] = __fdiv_rn(v[c], sum);
+    }
+    __syncthreads();
+
+    // O = P V: thread owns queries ty*4 + {0..3}, 64 + ty*4 + {0..3} and dims tx*4 + {0..3}
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[i][j] = 0.0f;
+#pragma unroll 4
+    for (int k = 0; k < AT_S; k++) {
+        const float4 p0 = *reinterpret_cast<const float4 *>(Pt + k * AT_LD + ty * 4);
+        const float4 p1 = *reinterpret_cast<const float4 *>(Pt + k * AT_LD + 64 + ty * 4);
+        const float4 vv = *reinterpret_cast<const float4 *>(Vs + k * AT_D + tx * 4);
+        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const float vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[i][j] = fmaf(pv[i], vw[j], o[i][j]);
     }
 #pragma unroll
-    for (int d = 0; d < AT_D; d++) o[d] = 0.0f;
-    float mrun = -INFINITY, lrun = 0.0f;
-    for (int j0 = 0; j0 < S; j0 += AT_KB) {
-        float sc[AT_KB];
-        float bm = -INFINITY;
-#pragma unroll
-        for (int jj = 0; jj < AT_KB; jj++) {
-            float a = -INFINITY;
-            if (j0 + jj < S) {
-                const float *kr = Ks + (j0 + jj) * AT_D;
-                a = 0.0f;
-#pragma unroll
-                for (int d = 0; d < AT_D; d++) a = fmaf(q[d], kr[d], a);
-            }
-            sc[jj] = a;
-            bm = fmaxf(bm, a);
-        }
-        const float mnew = fmaxf(mrun, bm);
-        const float corr = expf(mrun - mnew);
-        lrun *= corr;
-#pragma unroll
-        for (int d = 0; d < AT_D; d++) o[d] *= corr;
-#pragma unroll
-        for (int jj = 0; jj < AT_KB; jj++) {
-            if (j0 + jj < S) {
-                const float p = expf(sc[jj] - mnew);
-                lrun += p;
-                const float *vr = Vs + (j0 + jj) * AT_D;
-#pragma unroll
-                for (int d = 0; d < AT_D; d++) o[d] = fmaf(p, vr[d], o[d]);
-            }
-        }
-        mrun = mnew;
+    for (int i = 0; i < 8; i++) {
+        const int q = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
+        if (q >= S) continue;
+        float *orow = out + ((size_t)b * S + q) * (H * AT_D) + h * AT_D + tx * 4;
+        *reinterpret_cast<float4 *>(orow) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
     }
-    const float inv = __fdiv_rn(1.0f, lrun);
-    float *orow = out + ((size_t)b * S + qi) * (H * AT_D) + h * AT_D;
-#pragma unroll
-    for (int d = 0; d < AT_D; d += 4)
-        *reinterpret_cast<float4 *>(orow + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
 }
 
 // ---------------------------------------------------------------- adds
@@ -144,75 +206,101 @@ __global__ void k_bias_act(const float *__restrict__ x, const float *__restrict_
 }
 
 // y = act(a + b) element-wise (residual adds)
+// out = act(a + b); with q, also its int8 copy at the next quantization
+// point's scale (the following QUANTIZE op, fused)
 __global__ void k_add_act(const float4 *__restrict__ a, const float4 *__restrict__ b, float4 *__restrict__ y, size_t n4,
-                          int act) {
+                          int act, uint32_t *__restrict__ q, float qs) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const float4 x = a[i], z = b[i];
-        y[i] = make_float4(apply_act(x.x + z.x, act), apply_act(x.y + z.y, act), apply_act(x.z + z.z, act),
-                           apply_act(x.w + z.w, act));
+        const float4 o = make_float4(apply_act(x.x + z.x, act), apply_act(x.y + z.y, act), apply_act(x.z + z.z, act),
+                                     apply_act(x.w + z.w, act));
+        y[i] = o;
+        if (q)
+            q[i] = (uint32_t)(uint8_t)requant_i8(o.x, qs) | ((uint32_t)(uint8_t)requant_i8(o.y, qs) << 8) |
+                   ((uint32_t)(uint8_t)requant_i8(o.z, qs) << 16) | ((uint32_t)(uint8_t)requant_i8(o.w, qs) << 24);
     }
 }
 
 // ---------------------------------------------------------------- images
 // NCHW f32 -> NHWC int8 with a static per-tensor scale:
 // q = clamp(round(x / scale), -127, 127) (quant.rs:35-36)
-__global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restrict__ q, int N, int C, int HW,
+// NCHW f32 -> NHWC int8 with Cp >= C channels per pixel (channels [C, Cp) are
+// zero: a 3-channel image padded to 4 gives the stem 4-byte im2col chunks).
+__global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restrict__ q, int N, int C, int HW, int Cp,
                                   float scale) {
-    const size_t total = (size_t)N * C * HW;
+    const size_t total = (size_t)N * Cp * HW;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         // i indexes the NHWC output
-        const int c = (int)(i % C);
-        const size_t p = i / C;  // n*HW + hw
+        const int c = (int)(i % Cp);
+        const size_t p = i / Cp;  // n*HW + hw
         const size_t n = p / HW, hw = p - n * HW;
-        q[i] = round_clamp_i8(__fdiv_rn(x[(n * C + c) * HW + hw], scale), -127.0f, 127.0f);
+        q[i] = c < C ? round_clamp_i8(__fdiv_rn(x[(n * C + c) * HW + hw], scale), -127.0f, 127.0f) : (int8_t)0;
     }
 }
 
 // im2col of an NHWC int8 tensor: row m = (n, oy, ox), column (ky, kx, c),
-// zero for padded taps and for columns in [K, Kp).
-__global__ void k_im2col_nhwc(const int8_t *__restrict__ x, int8_t *__restrict__ col, int N, int H, int W, int C,
-                              int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW, int Kp) {
-    const int K = KH * KW * C;
-    if ((C & 15) == 0) {
-        // 16-byte chunks: one chunk = 16 channels of one tap
-        const int chunks = Kp >> 4;
-        const size_t total = (size_t)N * OH * OW * chunks;
-        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-            const int ch = (int)(i % chunks);
-            const size_t m = i / chunks;
-            const int kk = ch << 4;
-            int4 v = make_int4(0, 0, 0, 0);
+// zero for padded taps and for columns in [K, Kp). One warp per output row:
+// the row's pixel is decoded once (32-bit index math), lanes walk the row's
+// 16-byte (C % 16 == 0), 4-byte (C % 4 == 0) or 1-byte chunks, so loads of a
+// tap are contiguous channels and the row is written with coalesced stores.
+template <int VB>
+__global__ void __launch_bounds__(256) k_im2col_nhwc(const int8_t *__restrict__ x, int8_t *__restrict__ col, int N,
+                                                     int H, int W, int C, int KH, int KW, int sh, int sw, int ph,
+                                                     int pw, int OH, int OW, int Kp) {
+    using V = typename std::conditional<VB == 16, int4, typename std::conditional<VB == 4, int, int8_t>::type>::type;
+    const int lane = threadIdx.x & 31;
+    const int rows = N * OH * OW, K = KH * KW * C, chunks = Kp / VB;
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
+    for (int m = warp; m < rows; m += nwarps) {
+        const int ox = m % OW, t = m / OW, oy = t % OH, n = t / OH;
+        const int iy0 = oy * sh - ph, ix0 = ox * sw - pw;
+        const int8_t *img = x + (size_t)n * H * W * C;
+        V *dst = reinterpret_cast<V *>(col + (size_t)m * Kp);
+        for (int ch = lane; ch < chunks; ch += 32) {
+            const int kk = ch * VB;
+            V v{};
             if (kk < K) {
                 const int tap = kk / C, c = kk - tap * C;
                 const int ky = tap / KW, kx = tap - ky * KW;
-                const int ox = (int)(m % OW);
-                const size_t t2 = m / OW;
-                const int oy = (int)(t2 % OH);
-                const int n = (int)(t2 / OH);
-                const int iy = oy * sh + ky - ph, ix = ox * sw + kx - pw;
+                const int iy = iy0 + ky, ix = ix0 + kx;
                 if (iy >= 0 && iy < H && ix >= 0 && ix < W)
-                    v = *reinterpret_cast<const int4 *>(x + (((size_t)n * H + iy) * W + ix) * C + c);
+                    v = *reinterpret_cast<const V *>(img + ((size_t)iy * W + ix) * C + c);
             }
-            *reinterpret_cast<int4 *>(col + m * Kp + kk) = v;
+            dst[ch] = v;
         }
-    } else {
-        const size_t total = (size_t)N * OH * OW * Kp;
-        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-            const int kk = (int)(i % Kp);
-            const size_t m = i / Kp;
-            int8_t v = 0;
-            if (kk < K) {
-                const int tap = kk / C, c = kk - tap * C;
-                const int ky = tap / KW, kx = tap - ky * KW;
-                const int ox = (int)(m % OW);
-                const size_t t2 = m / OW;
-                const int oy = (int)(t2 % OH);
-                const int n = (int)(t2 / OH);
-                const int iy = oy * sh + ky - ph, ix = ox * sw + kx - pw;
-                if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = x[(((size_t)n * H + iy) * W + ix) * C + c];
-            }
-            col[i] = v;
+    }
+}
+
+// im2col for small, unaligned C (the 3-channel stem): lanes gather whole taps
+// (C bytes each) into a shared-memory copy of the row, which the warp then
+// writes with 16-byte stores. Kp <= IM2COL_ROW_MAX, Kp % 16 == 0.
+constexpr int IM2COL_ROW_MAX = 1024;
+__global__ void __launch_bounds__(256) k_im2col_nhwc_taps(const int8_t *__restrict__ x, int8_t *__restrict__ col,
+                                                          int N, int H, int W, int C, int KH, int KW, int sh, int sw,
+                                                          int ph, int pw, int OH, int OW, int Kp) {
+    __shared__ __align__(16) int8_t rowbuf[8][IM2COL_ROW_MAX];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    int8_t *rb = rowbuf[wib];
+    const int rows = N * OH * OW, taps = KH * KW, K = taps * C;
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int nwarps = (int)((gridDim.x * (size_t)blockDim.x) >> 5);
+    for (int kk = K + lane; kk < Kp; kk += 32) rb[kk] = 0;
+    for (int m = warp; m < rows; m += nwarps) {
+        const int ox = m % OW, t = m / OW, oy = t % OH, n = t / OH;
+        const int iy0 = oy * sh - ph, ix0 = ox * sw - pw;
+        const int8_t *img = x + (size_t)n * H * W * C;
+        for (int tap = lane; tap < taps; tap += 32) {
+            const int ky = tap / KW, kx = tap - ky * KW;
+            const int iy = iy0 + ky, ix = ix0 + kx;
+            const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+            const int8_t *src = img + ((size_t)iy * W + ix) * C;
+            for (int c = 0; c < C; c++) rb[tap * C + c] = in ? src[c] : (int8_t)0;
         }
+        __syncwarp();
+        int4 *dst = reinterpret_cast<int4 *>(col + (size_t)m * Kp);
+        for (int ch = lane; ch < Kp / 16; ch += 32) dst[ch] = reinterpret_cast<const int4 *>(rb)[ch];
+        __syncwarp();
     }
 }
 
@@ -236,6 +324,30 @@ __global__ void k_maxpool_nhwc(const float *__restrict__ x, float *__restrict__ 
                 if (ix < 0 || ix >= W) continue;
                 const float v = x[(((size_t)n * H + iy) * W + ix) * C + c];
                 if (v > best) best = v;
+            }
+        }
+        y[i] = best;
+    }
+}
+
+// Same, 4 channels per thread (C % 4 == 0, 16-byte aligned), 32-bit index math.
+__global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict__ y, int N, int H, int W, int C4,
+                                int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW) {
+    const int total = N * OH * OW * C4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int c = i % C4, t = i / C4, ox = t % OW, t2 = t / OW, oy = t2 % OH, n = t2 / OH;
+        float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        for (int ky = 0; ky < KH; ky++) {
+            const int iy = oy * sh + ky - ph;
+            if (iy < 0 || iy >= H) continue;
+            for (int kx = 0; kx < KW; kx++) {
+                const int ix = ox * sw + kx - pw;
+                if (ix < 0 || ix >= W) continue;
+                const float4 v = x[(((size_t)n * H + iy) * W + ix) * C4 + c];
+                if (v.x > best.x) best.x = v.x;
+                if (v.y > best.y) best.y = v.y;
+                if (v.z > best.z) best.z = v.z;
+                if (v.w > best.w) best.w = v.w;
             }
         }
         y[i] = best;
@@ -268,23 +380,23 @@ __global__ void k_absmax_acc(const float *__restrict__ x, size_t n, unsigned *ce
 }  // namespace
 
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
-                     size_t cols, float eps) {
+                     size_t cols, float eps, int8_t *q, float qs) {
     if (cols > 32 * LN_MAX || rows > INT32_MAX) return TPT_UNSUPPORTED;
     k_layernorm<<<grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(x, g, b, y, (int)rows,
-                                                                                              (int)cols, eps);
+                                                                                              (int)cols, eps, q, qs);
     return after_launch(ctx, "layernorm");
 }
 
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale) {
-    if (D != AT_D || S <= 0 || S > 256) return TPT_UNSUPPORTED;
-    const size_t smem = (size_t)2 * S * AT_D * sizeof(float);
+    if (D != AT_D || S <= 0 || S > AT_S || B <= 0 || H <= 0 || B > 65535 || (((uintptr_t)qkv | (uintptr_t)out) & 15))
+        return TPT_UNSUPPORTED;
     static bool attr[64] = {};
     if (!attr[ctx->device & 63]) {
-        cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 256 * AT_D * 4);
+        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
         attr[ctx->device & 63] = true;
     }
-    dim3 grid((unsigned)((S + AT_Q - 1) / AT_Q), (unsigned)H, (unsigned)B);
-    k_attention<<<grid, AT_Q, smem, ctx->stream>>>(qkv, out, S, H, scale);
+    k_attention<<<dim3((unsigned)H, (unsigned)B), 256, AT_SMEM, ctx->stream>>>(qkv, out, S, H, scale);
     return after_launch(ctx, "attention");
 }
 
@@ -294,30 +406,48 @@ int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float 
     return after_launch(ctx, "bias_act");
 }
 
-int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act) {
-    if (n % 4) return TPT_UNSUPPORTED;
+int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act, int8_t *q,
+                   float qs) {
+    if (n % 4 || ((uintptr_t)q & 3)) return TPT_UNSUPPORTED;
     k_add_act<<<grid_1d(n / 4, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
-        (const float4 *)a, (const float4 *)b, (float4 *)y, n / 4, act);
+        (const float4 *)a, (const float4 *)b, (float4 *)y, n / 4, act, reinterpret_cast<uint32_t *>(q), qs);
     return after_launch(ctx, "add_act");
 }
 
-int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, float scale) {
-    k_nchw_to_nhwc_q8<<<grid_1d((size_t)N * C * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
-        x, q, N, C, HW, scale);
+int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int Cp,
+                           float scale) {
+    k_nchw_to_nhwc_q8<<<grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
+        x, q, N, C, HW, Cp, scale);
     return after_launch(ctx, "nchw_to_nhwc_q8");
 }
 
 int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H, int W, int C, int KH, int KW, int sh,
                   int sw, int ph, int pw, int OH, int OW, int Kp) {
-    const size_t work = (size_t)N * OH * OW * ((C & 15) == 0 ? Kp / 16 : Kp);
-    k_im2col_nhwc<<<grid_1d(work, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW,
-                                                                                           sh, sw, ph, pw, OH, OW, Kp);
+    const size_t rows = (size_t)N * OH * OW;
+    if (rows > 0x7fffffff || (size_t)H * W * C > 0x7fffffff) return TPT_UNSUPPORTED;
+    const unsigned g = grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16);
+    const bool a16 = ((uintptr_t)x & 15) == 0 && ((uintptr_t)col & 15) == 0;
+    if ((C & 15) == 0 && (Kp & 15) == 0 && a16)
+        k_im2col_nhwc<16><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+    else if ((C & 3) == 0 && (Kp & 3) == 0 && a16)
+        k_im2col_nhwc<4><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+    else if ((Kp & 15) == 0 && Kp <= IM2COL_ROW_MAX && ((uintptr_t)col & 15) == 0)
+        k_im2col_nhwc_taps<<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+    else
+        k_im2col_nhwc<1><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
     return after_launch(ctx, "im2col");
 }
 
 int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
                         int sw, int ph, int pw, int OH, int OW) {
-    k_maxpool_nhwc<<<grid_1d((size_t)N * OH * OW * C, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(
+    const size_t total = (size_t)N * OH * OW * C;
+    if (C % 4 == 0 && total / 4 < 0x7fffffff && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
+        k_maxpool_nhwc4<<<grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw, ph, pw,
+            OH, OW);
+        return after_launch(ctx, "maxpool");
+    }
+    k_maxpool_nhwc<<<grid_1d(total, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(
         x, y, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW);
     return after_launch(ctx, "maxpool");
 }

@@ -23,11 +23,13 @@
 
 namespace tpt {
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
-                     size_t cols, float eps);
+                     size_t cols, float eps, int8_t *q = nullptr, float qs = 0.0f);
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale);
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
-int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act);
-int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, float scale);
+int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act,
+                   int8_t *q = nullptr, float qs = 0.0f);
+int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int Cp,
+                           float scale);
 int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H, int W, int C, int KH, int KW, int sh,
                   int sw, int ph, int pw, int OH, int OW, int Kp);
 int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
@@ -48,6 +50,7 @@ struct PlanTensor {
     void *ptr = nullptr;    // device pointer (set at finalize / for constants)
     bool is_const = false;
     float scale = 0.0f;     // INT8 tensors: the per-tensor scale in effect
+    int readers = 0;        // ops reading this tensor (set at finalize)
 };
 
 struct PlanOp {
@@ -127,12 +130,13 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
             p->tensors[o.out].scale = s;
             return launch_quant_i8_static(ctx, F(p, o.in0), d[0], s, Q(p, o.out));
         }
-        case TPT_OP_NCHW_TO_NHWC_Q8: {  // f32 NCHW [N,C,HW] -> i8 NHWC
+        case TPT_OP_NCHW_TO_NHWC_Q8: {  // f32 NCHW [N,C,HW] -> i8 NHWC with d3 (>= C, or 0 = C) channels
             float s;
             st = point_scale(p, po, F(p, o.in0), d[0] * d[1] * d[2], &s);
             if (st) return st;
             p->tensors[o.out].scale = s;
-            return launch_nchw_to_nhwc_q8(ctx, F(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], s);
+            const int cp = d[3] > d[1] ? (int)d[3] : (int)d[1];
+            return launch_nchw_to_nhwc_q8(ctx, F(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], cp, s);
         }
         case TPT_OP_LINEAR_W8A8: {  // i8 [rows, K] x W^T -> f32 [rows, N] (+bias, act)
             const float sa = p->tensors[o.in0].scale;
@@ -287,6 +291,12 @@ int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
     for (auto &t : p->tensors)
         if (!t.is_const) t.ptr = p->arena + t.offset;
     p->cal_max.assign(p->n_cells, 0.0f);
+    for (auto &t : p->tensors) t.readers = 0;
+    for (auto &po : p->ops) {
+        const tpt_plan_op &o = po.op;
+        for (int id : {o.in0, o.in1, o.in2})
+            if (id >= 0) p->tensors[id].readers++;
+    }
     p->finalized = true;
     return TPT_OK;
 }
@@ -351,14 +361,68 @@ int tpt_cuda_plan_set_scales(tpt_cuda_plan *p, const float *scales, size_t n) {
     return TPT_OK;
 }
 
-int tpt_cuda_plan_run_device(tpt_cuda_plan *p) {
-    CHECK_PLAN(p);
-    if (!p->finalized) return TPT_INVALID;
-    for (auto &po : p->ops) {
+namespace {
+bool is_output(const int *out_ids, size_t n_out, int id) {
+    for (size_t i = 0; i < n_out; i++)
+        if (out_ids[i] == id) return true;
+    return false;
+}
+
+// With frozen scales, LINEAR_W8A8 -> QUANTIZE of its f32 output (read by no
+// other op and not fetched by the caller) runs as one launch whose epilogue
+// writes the int8 tensor (clamp(roundf(y / s)), the QUANTIZE op's arithmetic):
+// the f32 tensor is neither written nor read back.
+int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
+    for (size_t i = 0; i < p->ops.size(); i++) {
+        PlanOp &po = p->ops[i];
+        const tpt_plan_op &o = po.op;
+        if (!p->calibrating && o.kind == TPT_OP_LINEAR_W8A8 && i + 1 < p->ops.size()) {
+            PlanOp &nq = p->ops[i + 1];
+            const tpt_plan_op &q = nq.op;
+            const PlanTensor &t = p->tensors[o.out];
+            if (q.kind == TPT_OP_QUANTIZE && q.in0 == o.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                t.readers == 1 && q.dims[0] == t.numel && !is_output(out_ids, n_out, o.out)) {
+                Requant rq;
+                rq.q = Q(p, q.out);
+                rq.scale = nq.frozen;
+                p->tensors[q.out].scale = nq.frozen;
+                int st = launch_w8a8(p->ctx, Q(p, o.in0), o.dims[0], o.w->k, o.w, p->tensors[o.in0].scale,
+                                     F(p, o.in1), o.act, nullptr, nullptr, rq);
+                if (st) return st;
+                i++;
+                continue;
+            }
+        }
+        // ADD_ACT / LAYERNORM -> QUANTIZE of its output: one pass writes the f32
+        // tensor (still read later, e.g. by a residual) and its int8 copy
+        if (!p->calibrating && (o.kind == TPT_OP_ADD_ACT || o.kind == TPT_OP_LAYERNORM) && i + 1 < p->ops.size()) {
+            PlanOp &nq = p->ops[i + 1];
+            const tpt_plan_op &q = nq.op;
+            const PlanTensor &t = p->tensors[o.out];
+            if (q.kind == TPT_OP_QUANTIZE && q.in0 == o.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                q.dims[0] == t.numel) {
+                p->tensors[q.out].scale = nq.frozen;
+                int st = o.kind == TPT_OP_ADD_ACT
+                             ? launch_add_act(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), o.dims[0], o.act,
+                                              Q(p, q.out), nq.frozen)
+                             : launch_layernorm(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), F(p, o.out), o.dims[0],
+                                                o.dims[1], o.f0, Q(p, q.out), nq.frozen);
+                if (st) return st;
+                i++;
+                continue;
+            }
+        }
         int st = run_op(p, po);
         if (st) return st;
     }
     return TPT_OK;
+}
+}  // namespace
+
+int tpt_cuda_plan_run_device(tpt_cuda_plan *p) {
+    CHECK_PLAN(p);
+    if (!p->finalized) return TPT_INVALID;
+    return run_ops(p, nullptr, 0);
 }
 
 int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *inputs, size_t n_in,
@@ -371,7 +435,7 @@ int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *i
         int st = h2d(p->ctx, t.ptr, inputs[i], t.numel * dt_size(t.dtype));
         if (st) return st;
     }
-    int st = tpt_cuda_plan_run_device(p);
+    int st = run_ops(p, out_ids, n_out);
     if (st) return st;
     for (size_t i = 0; i < n_out; i++) {
         if (!valid_id(p, out_ids[i])) return TPT_INVALID;

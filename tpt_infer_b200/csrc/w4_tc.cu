@@ -460,7 +460,8 @@ int launch_w4_tc_bn(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap 
     const int kblocks = K / W4_KB;
     const long long units = (long long)tiles * kblocks;
     const int ctas = ctx->sm_count < tc::TPT_SK_MAX_CTAS ? ctx->sm_count : tc::TPT_SK_MAX_CTAS;
-    const int grid = units < ctas ? (int)units : ctas;
+    // fewer than two units per SM: whole tiles per CTA, no cross-CTA reduction
+    const int grid = units < 2LL * ctas ? (tiles < ctas ? tiles : ctas) : ctas;
     int st = ensure_sk(ctx, (size_t)2 * grid * BN * W4_TM * sizeof(float));
     if (st) return st;
     int *cnt = reinterpret_cast<int *>(ctx->sk);

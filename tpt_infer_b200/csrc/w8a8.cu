@@ -22,10 +22,10 @@
 namespace tpt {
 
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
-                   const float *bias, int act, float *y, int32_t *acc, bool *handled);
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
 int build_weight_tmap(tpt_cuda_weights *w);
 int launch_w8a8_sk(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
-                   const float *bias, int act, float *y, int32_t *acc, bool *handled);
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
 
 namespace {
 
@@ -55,7 +55,8 @@ template <int MM, bool A_REG>
 __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
                                                    const float *__restrict__ wscale, const float *__restrict__ bias,
                                                    int M, int N, int K, float a_scale, int act,
-                                                   float *__restrict__ Y, int32_t *__restrict__ ACC) {
+                                                   float *__restrict__ Y, int32_t *__restrict__ ACC,
+                                                   int8_t *__restrict__ Q, float q_scale) {
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -111,6 +112,8 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                 if (i < M) {
                     if (ACC)
                         ACC[(size_t)i * N + n] = acc[i];
+                    else if (Q)
+                        Q[(size_t)i * N + n] = requant_i8(w8a8_epilogue(acc[i], a_scale, ws, bias, n, act), q_scale);
                     else
                         Y[(size_t)i * N + n] = w8a8_epilogue(acc[i], a_scale, ws, bias, n, act);
                 }
@@ -124,7 +127,8 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
 __global__ void __launch_bounds__(256) k_w8a8_simt(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
                                                    const float *__restrict__ wscale, const float *__restrict__ bias,
                                                    int M, int N, int K, float a_scale, int act,
-                                                   float *__restrict__ Y, int32_t *__restrict__ ACC) {
+                                                   float *__restrict__ Y, int32_t *__restrict__ ACC,
+                                                   int8_t *__restrict__ Q, float q_scale) {
     __shared__ __align__(16) int As[2][8][128 + 4];
     __shared__ __align__(16) int Bs[2][8][128 + 4];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -188,6 +192,9 @@ __global__ void __launch_bounds__(256) k_w8a8_simt(const int8_t *__restrict__ A,
             if (n >= N) continue;
             if (ACC)
                 ACC[(size_t)m * N + n] = acc[i][j];
+            else if (Q)
+                Q[(size_t)m * N + n] =
+                    requant_i8(w8a8_epilogue(acc[i][j], a_scale, __ldg(wscale + n), bias, n, act), q_scale);
             else
                 Y[(size_t)m * N + n] = w8a8_epilogue(acc[i][j], a_scale, __ldg(wscale + n), bias, n, act);
         }
@@ -214,7 +221,7 @@ __global__ void k_fill_f32(float *p, size_t n, float v) {
 }  // namespace
 
 int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w, float a_scale,
-                const float *bias, int act, float *y, int32_t *acc) {
+                const float *bias, int act, float *y, int32_t *acc, Requant rq) {
     const size_t n = w->n;
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
@@ -224,7 +231,8 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
         unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
         const bool areg = k <= (size_t)GEMV_CH * 32 * 16;
 #define TPT_GEMV(MM, AR) \
-    k_w8a8_gemv<MM, AR><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc)
+    k_w8a8_gemv<MM, AR><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc, \
+                                                    rq.q, rq.scale)
         if (m == 1 && areg)
             TPT_GEMV(1, true);
         else if (m == 1)
@@ -238,14 +246,15 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     }
     bool handled = false;
     if (m <= 64) {
-        int st = launch_w8a8_sk(ctx, a, m, w, a_scale, bias, act, y, acc, &handled);
+        int st = launch_w8a8_sk(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);
         if (st || handled) return st;
     }
-    int st = launch_w8a8_tc(ctx, a, m, w, a_scale, bias, act, y, acc, &handled);
+    int st = launch_w8a8_tc(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);
     if (st || handled) return st;
     dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 127) / 128));
     if (grid.y > 65535) return TPT_UNSUPPORTED;
-    k_w8a8_simt<<<grid, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc);
+    k_w8a8_simt<<<grid, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc,
+                                               rq.q, rq.scale);
     return after_launch(ctx, "w8a8_simt");
 }
 
@@ -334,7 +343,7 @@ int tpt_cuda_w8a8_gemm(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, f
     float *db = bias ? st.take<float>(w->n) : nullptr;
     TRY(h2d(ctx, da, a, an));
     if (bias) TRY(h2d(ctx, db, bias, w->n * 4));
-    TRY(launch_w8a8(ctx, da, m, k, w, a_scale, db, act, dy, nullptr));
+    TRY(launch_w8a8(ctx, da, m, k, w, a_scale, db, act, dy, nullptr, Requant{}));
     TRY(d2h(ctx, out, dy, on * 4));
     return sync_and_check(ctx);
 }
@@ -343,14 +352,14 @@ int tpt_cuda_w8a8_gemm_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, float a
                            const float *bias, int act, float *out) {
     CHECK_CTX(ctx);
     if (!w || w->kind != 8 || act < 0 || act > 2) return TPT_INVALID;
-    return launch_w8a8(ctx, a, m, w->k, w, a_scale, bias, act, out, nullptr);
+    return launch_w8a8(ctx, a, m, w->k, w, a_scale, bias, act, out, nullptr, Requant{});
 }
 
 int tpt_cuda_w8a8_gemm_acc_dev(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w,
                                int32_t *acc) {
     CHECK_CTX(ctx);
     if (!w || w->kind != 8 || !acc) return TPT_INVALID;
-    return launch_w8a8(ctx, a, m, w->k, w, 1.0f, nullptr, 0, nullptr, acc);
+    return launch_w8a8(ctx, a, m, w->k, w, 1.0f, nullptr, 0, nullptr, acc, Requant{});
 }
 
 // ptq.rs:293-324, the reference contract: B [kb, n], per-tensor b_scales[0].
@@ -413,7 +422,7 @@ int tpt_cuda_quantized_matmul_i8(tpt_cuda_ctx *ctx, const int8_t *a, size_t a_le
     w.tmap_ok = false;  // transient weights: no tensor-map path
     // out = (float)acc * (a_scale * b_scale): the per-channel epilogue with every
     // channel scale equal to b_scale and no bias.
-    TRY(launch_w8a8(ctx, da, m, kp, &w, a_scale, nullptr, 0, dy, nullptr));
+    TRY(launch_w8a8(ctx, da, m, kp, &w, a_scale, nullptr, 0, dy, nullptr, Requant{}));
     TRY(d2h(ctx, out, dy, e3 * 4));
     return sync_and_check(ctx);
 }

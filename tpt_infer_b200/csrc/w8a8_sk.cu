@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     k_w8a8_sk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA, int M, int N, int K,
               float a_scale, const float *__restrict__ wscale, const float *__restrict__ bias, int act,
               float *__restrict__ Y, int32_t *__restrict__ ACC, int32_t *__restrict__ part,
-              int *__restrict__ cnt, unsigned *gflags) {
+              int *__restrict__ cnt, unsigned *gflags, int8_t *__restrict__ Q, float q_scale) {
     using Cfg = SkCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -244,7 +244,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
                 } else {
                     float y = __fmul_rn(__int2float_rn(a), sc);
                     if (bias) y = __fadd_rn(y, bi);
-                    Y[o] = apply_act(y, act);
+                    y = apply_act(y, act);
+                    if (Q)
+                        Q[o] = requant_i8(y, q_scale);
+                    else
+                        Y[o] = y;
                 }
             };
             if (kb0 == 0 && kb1 == kblocks) {
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
 
 template <int BN, bool ACC_OUT>
 int launch_sk(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap &ta, int M, int N, int K, float a_scale,
-              const float *ws, const float *bias, int act, float *y, int32_t *acc) {
+              const float *ws, const float *bias, int act, float *y, int32_t *acc, Requant rq) {
     using Cfg = SkCfg<BN>;
     static bool attr_done[64] = {};
     auto kfn = k_w8a8_sk<BN, ACC_OUT>;
@@ -329,13 +333,14 @@ int launch_sk(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap &ta, i
     const int tiles = ((N + SK_TM - 1) / SK_TM) * ((M + BN - 1) / BN);
     const long long units = (long long)tiles * ((K + SK_BK - 1) / SK_BK);
     const int ctas = ctx->sm_count < tc::TPT_SK_MAX_CTAS ? ctx->sm_count : tc::TPT_SK_MAX_CTAS;
-    const int grid = units < ctas ? (int)units : ctas;
+    // fewer than two units per SM: whole tiles per CTA, no cross-CTA reduction
+    const int grid = units < 2LL * ctas ? (tiles < ctas ? tiles : ctas) : ctas;
     int st = ensure_sk(ctx, (size_t)2 * grid * BN * SK_TM * sizeof(int32_t));
     if (st) return st;
     int *cnt = reinterpret_cast<int *>(ctx->sk);
     int32_t *part = reinterpret_cast<int32_t *>(ctx->sk + TPT_SK_SLOTS_OFFSET);
     kfn<<<grid, SK_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(tw, ta, M, N, K, a_scale, ws, bias, act, y, acc, part, cnt,
-                                                            ctx->d_flags);
+                                                            ctx->d_flags, rq.q, rq.scale);
     return after_launch(ctx, "w8a8_sk");
 }
 
@@ -344,7 +349,7 @@ int launch_sk(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap &ta, i
 // M <= 64 with the weight's tensor maps available and A 16-byte aligned;
 // returns handled = false otherwise (the caller falls back to the GEMV).
 int launch_w8a8_sk(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
-                   const float *bias, int act, float *y, int32_t *acc, bool *handled) {
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq) {
     *handled = false;
     if (!w->tmap_ok || m == 0 || m > 64 || w->k == 0) return TPT_OK;
     const int BN = m <= 16 ? 16 : m <= 32 ? 32 : 64;
@@ -356,8 +361,8 @@ int launch_w8a8_sk(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     const CUtensorMap &tw = *reinterpret_cast<const CUtensorMap *>(w->tmaps[0]);  // 128-row box
     const int M = (int)m, N = (int)w->n, K = (int)w->k;
 #define TPT_SK(BNV)                                                                                         \
-    return acc ? launch_sk<BNV, true>(ctx, tw, ta, M, N, K, a_scale, w->scales, bias, act, y, acc)          \
-               : launch_sk<BNV, false>(ctx, tw, ta, M, N, K, a_scale, w->scales, bias, act, y, acc)
+    return acc ? launch_sk<BNV, true>(ctx, tw, ta, M, N, K, a_scale, w->scales, bias, act, y, acc, rq)      \
+               : launch_sk<BNV, false>(ctx, tw, ta, M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
     if (BN == 16) TPT_SK(16);
     if (BN == 32) TPT_SK(32);
     TPT_SK(64);

@@ -105,7 +105,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_w8a8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
                const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
-               int32_t *__restrict__ ACC, unsigned *gflags) {
+               int32_t *__restrict__ ACC, unsigned *gflags, int8_t *__restrict__ Q, float q_scale) {
     using Cfg = PairCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -267,7 +267,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                         v[j] = __float_as_uint(apply_act(y, act));
                     }
                 }
-                if (tma_store) {
+                if (!ACC_OUT && Q) {
+                    // int8 output requantized with the next point's scale: this
+                    // lane's row gets 32 consecutive bytes
+                    if (m < M) {
+                        uint32_t b[8];
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            b[j / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j]), q_scale) |
+                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 1]), q_scale) << 8) |
+                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 2]), q_scale) << 16) |
+                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 3]), q_scale) << 24);
+                        int8_t *dst = Q + (size_t)m * N + n0;
+                        if (n0 + 32 <= N && (N & 15) == 0) {
+                            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
+                            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(b[4], b[5], b[6], b[7]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                if (n0 + j < N) dst[j] = (int8_t)(b[j / 4] >> (8 * (j % 4)));
+                        }
+                    }
+                } else if (tma_store) {
                     if (mrow0 < M) {  // a block entirely below the last row is not stored
                         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                         __syncwarp();
@@ -373,7 +394,7 @@ bool make_tmap_i8(CUtensorMap *tm, const void *base, uint64_t rows, uint64_t k, 
 
 template <int BN, bool ACC_OUT>
 int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
-               const float *ws, const float *bias, int act, float *y, int32_t *acc) {
+               const float *ws, const float *bias, int act, float *y, int32_t *acc, Requant rq) {
     using Cfg = PairCfg<BN>;
     constexpr int P_SMEM_BYTES = Cfg::SMEM_BYTES;
     static bool attr_done[64] = {};
@@ -408,10 +429,10 @@ int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, 
     const int pairs = max_clusters[dev];
     const int clusters = ntiles < pairs ? ntiles : pairs;
     CUtensorMap ty;
-    const bool tma_store = make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
-                                         (uint64_t)N, ACC_OUT);
+    const bool tma_store = !rq.q && make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
+                                                  (uint64_t)N, ACC_OUT);
     kfn<<<2 * clusters, P_THREADS, P_SMEM_BYTES, ctx->stream>>>(ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0, M, N,
-                                                                 K, a_scale, ws, bias, act, y, acc, ctx->d_flags);
+                                                                 K, a_scale, ws, bias, act, y, acc, ctx->d_flags, rq.q, rq.scale);
     return after_launch(ctx, "w8a8_tc2");
 }
 
@@ -451,7 +472,7 @@ int build_weight_tmap(tpt_cuda_weights *w) {
 // (an M=256 x N=64 MMA reads 5 KB of operands per 64 tensor-core cycles per SM
 // against 4 KB at N=256) with a per-width cost factor.
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
-                   const float *bias, int act, float *y, int32_t *acc, bool *handled) {
+                   const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq) {
     *handled = false;
     if (!w->tmap_ok || m <= 64 || m > 0x7fffffff) return TPT_OK;
     CUtensorMap ta;
@@ -475,13 +496,13 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     // each CTA's B box holds BN/2 rows: tmaps[0..2] are the 128 / 64 / 32-row boxes
     const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(w->tmaps);
     if (bn == 64)
-        return acc ? launch_tc2<64, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc)
-                   : launch_tc2<64, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc);
+        return acc ? launch_tc2<64, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
+                   : launch_tc2<64, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc, rq);
     if (bn == 128)
-        return acc ? launch_tc2<128, true>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc)
-                   : launch_tc2<128, false>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc);
-    return acc ? launch_tc2<256, true>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc)
-               : launch_tc2<256, false>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc);
+        return acc ? launch_tc2<128, true>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
+                   : launch_tc2<128, false>(ctx, ta, maps[1], M, N, K, a_scale, w->scales, bias, act, y, acc, rq);
+    return acc ? launch_tc2<256, true>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
+               : launch_tc2<256, false>(ctx, ta, maps[0], M, N, K, a_scale, w->scales, bias, act, y, acc, rq);
 }
 
 }  // namespace tpt

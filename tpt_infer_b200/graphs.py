@@ -272,24 +272,47 @@ def resnet18_weights(be, seed=100):
     return spec
 
 
+def _pad_channels(cv, cp):
+    """The conv's (ky, kx, c) weight columns with c padded from cin to cp by
+    zero weights: the same int32 sums on an input whose extra channels are 0."""
+    taps = cv.k * cv.k
+    q = cv.qw.q[:, :taps * cv.cin].reshape(cv.cout, taps, cv.cin)
+    qp = np.zeros((cv.cout, taps, cp), np.int8)
+    qp[:, :, :cv.cin] = q
+    kp = (taps * cp + 15) // 16 * 16
+    out = np.zeros((cv.cout, kp), np.int8)
+    out[:, :taps * cp] = qp.reshape(cv.cout, taps * cp)
+    return out
+
+
 def build_resnet18(be, batch, spec: ResNetSpec):
+    """The stem input is held as NHWC with 4 channels (the 4th zero) and the stem
+    weights padded to match, so its im2col moves 4-byte chunks; outputs are
+    unchanged."""
     p = Plan(be)
     handles = []
-    for cv in spec.convs:
-        wh = be.upload_i8(cv.qw.q, cv.qw.scales, cv.qw.n, cv.qw.k)
+    STEM_C = 4
+    cins = []
+    for i, cv in enumerate(spec.convs):
+        q, cin = cv.qw.q, cv.cin
+        if i == 0:
+            q, cin = _pad_channels(cv, STEM_C), STEM_C
+        wh = be.upload_i8(np.ascontiguousarray(q), cv.qw.scales, cv.qw.n, q.shape[1])
         handles.append(wh)
+        cins.append(cin)
     p.weights += handles
     x = p.tensor(F32, batch * 3 * 224 * 224)
-    xq = p.tensor(I8, batch * 224 * 224 * 3)
-    p.op(OP_NCHW_Q8, x, xq, dims=(batch, 3, 224 * 224))
+    xq = p.tensor(I8, batch * 224 * 224 * STEM_C)
+    p.op(OP_NCHW_Q8, x, xq, dims=(batch, 3, 224 * 224, STEM_C))
 
     def conv(inp_q, H, W, ci, act):
         cv = spec.convs[ci]
         OH, OW = _conv_out(H, cv.k, cv.stride, cv.pad), _conv_out(W, cv.k, cv.stride, cv.pad)
         M = batch * OH * OW
-        col = p.tensor(I8, M * cv.qw.k)
-        p.op(OP_IM2COL, inp_q, col, dims=(batch, H, W, cv.cin, cv.k, cv.k, cv.stride, cv.stride, cv.pad, cv.pad,
-                                         OH, OW, cv.qw.k))
+        kp = handles[ci].k
+        col = p.tensor(I8, M * kp)
+        p.op(OP_IM2COL, inp_q, col, dims=(batch, H, W, cins[ci], cv.k, cv.k, cv.stride, cv.stride, cv.pad, cv.pad,
+                                         OH, OW, kp))
         out = p.tensor(F32, M * cv.cout)
         p.op(OP_LINEAR, col, out, in1=p.const(cv.qw.bias), w=handles[ci], act=act, dims=(M,))
         return out, OH, OW
