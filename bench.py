@@ -48,7 +48,7 @@ def alg_bytes(m):
 
 # DRAM bytes (read + write) of one k_w8a8_tc2<256,0> launch on this workload, from the
 # ncu capture summarised in profiles/k_w8a8_tc2_m4096_n4096_k4096.md.
-NCU_TRAFFIC_HEAD = 34.117888e6 + 19.930368e6
+NCU_TRAFFIC_HEAD = 34.148864e6 + 21.071360e6
 
 
 def peaks():
@@ -365,6 +365,52 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True, comm=None):
     return out
 
 
+def profile_kernels(args):
+    """One case per main kernel, args.warmup + args.steps launches each, in this
+    order: W8A8 M=1 (GEMV), M=16 (stream-K), M=4096 (SM pair) at K=N=4096; W4 M=1
+    (GEMV) and M=8 (tensor core) at K=4096, N=11008; BERT attention 64x128x12."""
+    import torch
+
+    from tpt_infer_b200 import CudaBackend, graphs, synth
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    be = CudaBackend.new(0, stream)
+    dev = "cuda:0"
+    reps = args.warmup + args.steps
+    out = {}
+    aq, sa, wq, ws, bias = make_inputs(M_HEAD, be=be)
+    w = be.upload_i8(wq, ws, N, K)
+    bias_dev = torch.from_numpy(bias).to(dev)
+    for m in (1, 16, M_HEAD):
+        a = torch.from_numpy(aq[:m * K]).to(dev)
+        y = torch.empty(m * N, dtype=torch.float32, device=dev)
+        out[f"w8a8_m{m}_us"] = _time_device(stream, lambda: be.w8a8_gemm_dev(a, m, sa, w, bias_dev, 0, y), args.steps,
+                                            args.warmup) * 1e6
+    w.free()
+    Kw, Nw = 4096, 11008
+    pk4, s4 = be.quantize_i4_symmetric_per_channel(synth.normal(Nw * Kw, 2000, 0.0, 0.02), Nw)
+    w4 = be.upload_i4(pk4, s4, Nw, Kw)
+    for m in (1, 8):
+        x = torch.from_numpy(synth.normal(m * Kw, 2001 + m)).to(dev)
+        y = torch.empty(m * Nw, dtype=torch.float32, device=dev)
+        out[f"w4_m{m}_us"] = _time_device(stream, lambda: be.w4_gemm_dev(x, m, w4, None, 0, y), args.steps,
+                                          args.warmup) * 1e6
+    w4.free()
+    B, S = 64, 128
+    pa = graphs.Plan(be)
+    tq = pa.tensor(graphs.F32, B * S * 3 * 768)
+    to = pa.tensor(graphs.F32, B * S * 768)
+    pa.op(graphs.OP_ATTENTION, tq, to, f0=0.125, dims=(B, S, 12, 64))
+    pa.finalize()
+    pa.run({tq: synth.normal(B * S * 3 * 768, 45)}, [to])
+    out["attention_64x128x12_us"] = _time_device(stream, pa.run_device, args.steps, args.warmup) * 1e6
+    pa.close()
+    be.close()
+    print(json.dumps({"profile_kernels": True, "launches_each": reps, **out}), flush=True)
+    return 0
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -405,10 +451,15 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the W4 sweep and the model workloads")
     ap.add_argument("--profile", action="store_true",
                     help="headline GEMM only (warm-up + steps), no sweep / e2e / CPU leg: the ncu capture case")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="each main kernel on one case, `--steps` launches each after warm-up: the ncu capture case "
+                         "for the per-kernel summaries")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_kernels:
+        return profile_kernels(args)
 
     import torch
     import torch.distributed as dist

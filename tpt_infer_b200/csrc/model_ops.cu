@@ -57,6 +57,50 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
     }
 }
 
+// Same arithmetic, cols % 128 == 0 (each lane owns float4 groups c = 4 (lane + 32 i)):
+// 16-byte loads and stores and a 4-byte store of the int8 copy.
+template <int G>
+__global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restrict__ g, const float4 *__restrict__ b,
+                             float4 *__restrict__ y, int rows, float eps, uint32_t *__restrict__ qout, float qs) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    constexpr int cols4 = 32 * G;
+    const float n = (float)(4 * cols4);
+    for (int r = warp; r < rows; r += nwarps) {
+        const float4 *xr = x + (size_t)r * cols4;
+        float4 v[G];
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            v[i] = xr[lane + 32 * i];
+            s += v[i].x + v[i].y + v[i].z + v[i].w;
+        }
+        const float mean = __fdiv_rn(warp_sum(s), n);
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
+            q += dx * dx + dy * dy + dz * dz + dw * dw;
+        }
+        const float var = __fdiv_rn(warp_sum(q), n);
+        const float inv = __fdiv_rn(1.0f, sqrtf(var + eps));
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            const int c = lane + 32 * i;
+            const float4 gg = __ldg(g + c), bb = __ldg(b + c);
+            const float4 o = make_float4((v[i].x - mean) * inv * gg.x + bb.x, (v[i].y - mean) * inv * gg.y + bb.y,
+                                         (v[i].z - mean) * inv * gg.z + bb.z, (v[i].w - mean) * inv * gg.w + bb.w);
+            y[(size_t)r * cols4 + c] = o;
+            if (qout)
+                qout[(size_t)r * cols4 + c] = (uint32_t)(uint8_t)requant_i8(o.x, qs) |
+                                             ((uint32_t)(uint8_t)requant_i8(o.y, qs) << 8) |
+                                             ((uint32_t)(uint8_t)requant_i8(o.z, qs) << 16) |
+                                             ((uint32_t)(uint8_t)requant_i8(o.w, qs) << 24);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- attention
 // Fused softmax(Q K^T * scale) V per (batch, head) on f32, reading Q, K, V from
 // the packed projection output qkv [B*S, 3*H*D] (Q | K | V along columns) and
@@ -79,7 +123,7 @@ static_assert(AT_S * AT_LD <= 2 * AT_D * AT_LD, "P^T fits in the Q^T/K^T space")
 // Q^T, K^T and P^T are held transposed in shared memory so every inner step
 // is two float4 loads feeding 32-64 FMAs. qkv rows are [q | k | v] of H*D each.
 __global__ void __launch_bounds__(256) k_attention(const float *__restrict__ qkv, float *__restrict__ out, int S,
-                                                   int H, float scale) {
+                                                   int H, float scale, int8_t *__restrict__ qout, float qs) {
     extern __shared__ __align__(16) float sm[];
     float *Qt = sm;                          // [D][LD]
     float *Kt = Qt + AT_D * AT_LD;           // [D][LD]
@@ -187,8 +231,13 @@ __global__ void __launch_bounds__(256) k_attention(const float *__restrict__ qkv
     for (int i = 0; i < 8; i++) {
         const int q = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
         if (q >= S) continue;
-        float *orow = out + ((size_t)b * S + q) * (H * AT_D) + h * AT_D + tx * 4;
-        *reinterpret_cast<float4 *>(orow) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+        const size_t off = ((size_t)b * S + q) * (H * AT_D) + h * AT_D + tx * 4;
+        if (qout)  // the following QUANTIZE, fused: the f32 context is not written
+            *reinterpret_cast<uint32_t *>(qout + off) =
+                (uint32_t)(uint8_t)requant_i8(o[i][0], qs) | ((uint32_t)(uint8_t)requant_i8(o[i][1], qs) << 8) |
+                ((uint32_t)(uint8_t)requant_i8(o[i][2], qs) << 16) | ((uint32_t)(uint8_t)requant_i8(o[i][3], qs) << 24);
+        else
+            *reinterpret_cast<float4 *>(out + off) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
     }
 }
 
@@ -382,13 +431,21 @@ __global__ void k_absmax_acc(const float *__restrict__ x, size_t n, unsigned *ce
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
                      size_t cols, float eps, int8_t *q, float qs) {
     if (cols > 32 * LN_MAX || rows > INT32_MAX) return TPT_UNSUPPORTED;
-    k_layernorm<<<grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(x, g, b, y, (int)rows,
-                                                                                              (int)cols, eps, q, qs);
+    const unsigned grid = grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16);
+    const bool a16 = ((((uintptr_t)x | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) & 15) == 0) && ((uintptr_t)q & 3) == 0;
+    if (a16 && cols == 768) {  // the BERT hidden size
+        k_layernorm4<6><<<grid, 256, 0, ctx->stream>>>((const float4 *)x, (const float4 *)g, (const float4 *)b,
+                                                       (float4 *)y, (int)rows, eps, (uint32_t *)q, qs);
+        return after_launch(ctx, "layernorm");
+    }
+    k_layernorm<<<grid, 256, 0, ctx->stream>>>(x, g, b, y, (int)rows, (int)cols, eps, q, qs);
     return after_launch(ctx, "layernorm");
 }
 
-int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale) {
-    if (D != AT_D || S <= 0 || S > AT_S || B <= 0 || H <= 0 || B > 65535 || (((uintptr_t)qkv | (uintptr_t)out) & 15))
+int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                     int8_t *q, float qs) {
+    if (D != AT_D || S <= 0 || S > AT_S || B <= 0 || H <= 0 || B > 65535 ||
+        (((uintptr_t)qkv | (uintptr_t)out) & 15) || ((uintptr_t)q & 3))
         return TPT_UNSUPPORTED;
     static bool attr[64] = {};
     if (!attr[ctx->device & 63]) {
@@ -396,7 +453,7 @@ int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int
         if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
         attr[ctx->device & 63] = true;
     }
-    k_attention<<<dim3((unsigned)H, (unsigned)B), 256, AT_SMEM, ctx->stream>>>(qkv, out, S, H, scale);
+    k_attention<<<dim3((unsigned)H, (unsigned)B), 256, AT_SMEM, ctx->stream>>>(qkv, out, S, H, scale, q, qs);
     return after_launch(ctx, "attention");
 }
 

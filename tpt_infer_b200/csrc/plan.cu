@@ -24,7 +24,8 @@
 namespace tpt {
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
                      size_t cols, float eps, int8_t *q = nullptr, float qs = 0.0f);
-int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale);
+int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                     int8_t *q = nullptr, float qs = 0.0f);
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
 int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act,
                    int8_t *q = nullptr, float qs = 0.0f);
@@ -388,6 +389,21 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
                 p->tensors[q.out].scale = nq.frozen;
                 int st = launch_w8a8(p->ctx, Q(p, o.in0), o.dims[0], o.w->k, o.w, p->tensors[o.in0].scale,
                                      F(p, o.in1), o.act, nullptr, nullptr, rq);
+                if (st) return st;
+                i++;
+                continue;
+            }
+        }
+        // ATTENTION -> QUANTIZE of a context read by nothing else: int8 straight from the kernel
+        if (!p->calibrating && o.kind == TPT_OP_ATTENTION && i + 1 < p->ops.size()) {
+            PlanOp &nq = p->ops[i + 1];
+            const tpt_plan_op &q = nq.op;
+            const PlanTensor &t = p->tensors[o.out];
+            if (q.kind == TPT_OP_QUANTIZE && q.in0 == o.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                t.readers == 1 && q.dims[0] == t.numel && !is_output(out_ids, n_out, o.out)) {
+                p->tensors[q.out].scale = nq.frozen;
+                int st = launch_attention(p->ctx, F(p, o.in0), F(p, o.out), (int)o.dims[0], (int)o.dims[1],
+                                          (int)o.dims[2], (int)o.dims[3], o.f0, Q(p, q.out), nq.frozen);
                 if (st) return st;
                 i++;
                 continue;

@@ -13,7 +13,7 @@
 // bytes quantize_i4_symmetric_per_channel(W^T, rows = n) emits
 // (quant.rs:192-204), uploaded once, never repacked.
 //
-// M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 64 == 0 and x is
+// M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 128 == 0 and x is
 // 16-byte aligned. M <= 2 uses k_w4_gemv: one warp streams 8 weight rows with
 // 128-bit loads, reusing each activation chunk across the 8 rows. Other shapes
 // use the SIMT tile kernel.

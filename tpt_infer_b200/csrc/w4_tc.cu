@@ -22,7 +22,7 @@
 // side BN = 16/32/64/128 activation rows, so a decode-like M still runs
 // full-height MMAs and each weight byte is unpacked once per BN activation rows.
 //
-// Stream-K. The (tile, 64-k block) units are split into one equal contiguous
+// Stream-K. The (tile, 128-k block) units are split into one equal contiguous
 // range per CTA, so all SMs share the nibble stream and the unpacking. A CTA
 // covering a whole tile writes the output directly; otherwise it stores its
 // f32 partial tile in its own slot of the tile (plain coalesced stores; slot =
@@ -31,8 +31,8 @@
 // the epilogue. Nothing waits on another CTA.
 //
 // Roles (480 threads, one CTA per SM):
-//   warp 0       TMA: nibbles [128 rows x 32 B] (64 k) into a deep ring (HBM)
-//   warp 14      TMA: x_hi, x_lo [BN rows x 64 fp16] into their own deep ring
+//   warp 0       TMA: nibbles [128 rows x 64 B] (128 k) into a ring (HBM)
+//   warp 14      TMA: x_hi, x_lo [BN rows x 64 fp16] x 2 sub-tiles into their own ring
 //                (L2 hits; freed by the MMA commit, so they run ahead of it)
 //   warps 6..13  unpack: thread = (weight row, half of the 32 B), 8 nibbles per
 //                32-bit word -> 8 fp16 with one LOP3 and one fp16 subtract per
@@ -56,20 +56,24 @@ namespace {
 using namespace tc;
 
 constexpr int W4_TM = 128;                      // weight rows per tile (MMA M)
-constexpr int W4_KB = 64;                       // k per block (one 128-byte fp16 row)
-constexpr int NIB_BYTES = W4_TM * (W4_KB / 2);  // 4 KB of nibbles per block
-constexpr int W16_BYTES = W4_TM * W4_KB * 2;    // 16 KB fp16 weight tile per block
+constexpr int W4_KB = 128;                      // k per block (two 64-k sub-tiles)
+constexpr int W4_SUBK = 64;                     // k of one 128B-swizzled fp16 sub-tile
+constexpr int NIB_BYTES = W4_TM * (W4_KB / 2);  // 8 KB of nibbles per block
+constexpr int W16_SUB = W4_TM * W4_SUBK * 2;    // 16 KB: one fp16 weight sub-tile
+constexpr int W16_BYTES = 2 * W16_SUB;          // 32 KB fp16 weight tile per block
 constexpr int W4_UNPACK_WARPS = 8;
 constexpr int W4_THREADS = 15 * 32;
 constexpr int W4_EPI = 128;
 
 template <int BN>
 struct W4Cfg {
-    static constexpr int X_BYTES = BN * W4_KB * 2;  // one of x_hi / x_lo
-    static constexpr int XSTG_BYTES = 2 * X_BYTES;  // activation stage (hi, lo), multiple of 1024
-    static constexpr int NS = BN >= 64 ? 8 : 16;    // nibble stages (HBM latency)
-    static constexpr int XS = BN == 16 ? 16 : BN == 32 ? 8 : BN == 64 ? 6 : 3;  // activation stages (L2 latency)
-    static constexpr int WS = BN == 128 ? 3 : 4;    // fp16 weight stages (unpack -> MMA)
+    static constexpr int X_BYTES = BN * W4_SUBK * 2;  // one of x_hi / x_lo for one 64-k sub-tile
+    // activation stage: [x_hi; x_lo] of sub-tile 0, then of sub-tile 1 (each pair
+    // is the MMA's 2 x BN-row B operand), multiple of 1024
+    static constexpr int XSTG_BYTES = 4 * X_BYTES;
+    static constexpr int NS = BN == 16 ? 8 : BN == 128 ? 4 : 6;  // nibble stages (HBM latency)
+    static constexpr int XS = BN == 16 ? 4 : BN == 32 ? 4 : 2;   // activation stages (L2 latency)
+    static constexpr int WS = BN == 128 ? 2 : 3;                 // fp16 weight stages (unpack -> MMA)
     static constexpr int SUBS = BN <= 32 ? 4 : BN == 64 ? 2 : 1;
     static constexpr int ACC_STRIDE = 2 * BN;             // columns of one sub-accumulator (hi | lo)
     static constexpr int TMEM_COLS = 2 * SUBS * ACC_STRIDE;  // double-buffered
@@ -148,8 +152,9 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
     const uint32_t nib = xst + XS * Cfg::XSTG_BYTES;
     const uint32_t bars = nib + NS * NIB_BYTES;
     auto w16_s = [&](int s) { return w16 + (uint32_t)(s * W16_BYTES); };
-    auto xh_s = [&](int s) { return xst + (uint32_t)(s * Cfg::XSTG_BYTES); };
-    auto xl_s = [&](int s) { return xh_s(s) + Cfg::X_BYTES; };
+    // x_hi / x_lo of 64-k sub-tile j of activation stage s
+    auto xh_s = [&](int s, int j) { return xst + (uint32_t)(s * Cfg::XSTG_BYTES + j * 2 * Cfg::X_BYTES); };
+    auto xl_s = [&](int s, int j) { return xh_s(s, j) + Cfg::X_BYTES; };
     auto nib_s = [&](int s) { return nib + (uint32_t)(s * NIB_BYTES); };
     auto full_nib = [&](int s) { return bars + 8u * s; };
     auto empty_nib = [&](int s) { return bars + 8u * (NS + s); };
@@ -224,9 +229,12 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
                         mbar_arrive_expect_tx(fb, NIB_BYTES);
                         tma_load_2d(nib_s(stage), &tmW, fb, kb * (W4_KB / 2), wt * W4_TM);
                     } else {
-                        mbar_arrive_expect_tx(fb, 2 * Cfg::X_BYTES);
-                        tma_load_2d(xh_s(stage), &tmXh, fb, kb * W4_KB, xt * BN);
-                        tma_load_2d(xl_s(stage), &tmXl, fb, kb * W4_KB, xt * BN);
+                        mbar_arrive_expect_tx(fb, Cfg::XSTG_BYTES);
+#pragma unroll
+                        for (int j = 0; j < 2; j++) {
+                            tma_load_2d(xh_s(stage, j), &tmXh, fb, kb * W4_KB + j * W4_SUBK, xt * BN);
+                            tma_load_2d(xl_s(stage, j), &tmXl, fb, kb * W4_KB + j * W4_SUBK, xt * BN);
+                        }
                     }
                     issued_mask |= 1u << stage;
                     last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
@@ -264,9 +272,11 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
                     }
                     tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < W4_KB / 16; kk++)  // B = [x_hi; x_lo], 2 x BN rows
-                        tc_mma_f16(d_tmem, sw128_desc(w16_s(ws) + 32 * kk), sw128_desc(xh_s(xs) + 32 * kk), idesc,
-                                   (i >= SUBS || kk != 0) ? 1u : 0u);
+                    for (int kk = 0; kk < W4_KB / 16; kk++) {  // B = [x_hi; x_lo], 2 x BN rows
+                        const int j = kk / (W4_SUBK / 16), k16 = kk % (W4_SUBK / 16);
+                        tc_mma_f16(d_tmem, sw128_desc(w16_s(ws) + j * W16_SUB + 32 * k16),
+                                   sw128_desc(xh_s(xs, j) + 32 * k16), idesc, (i >= SUBS || kk != 0) ? 1u : 0u);
+                    }
                     tc_commit(empty_x(xs));
                     tc_commit(empty_w16(ws));
                     if (++xs == XS) {
@@ -303,16 +313,17 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
                     ok = false;
                     break;
                 }
-                const uint4 p = *reinterpret_cast<const uint4 *>(smem_raw + (nib_s(ns) - raw) + r * 32 + half * 16);
+                // this thread: row r, k-half `half` (= fp16 sub-tile) of the block's 64 nibble bytes
+                const uint8_t *src = smem_raw + (nib_s(ns) - raw) + r * 64 + half * 32;
+                const uint4 p0 = *reinterpret_cast<const uint4 *>(src);
+                const uint4 p1 = *reinterpret_cast<const uint4 *>(src + 16);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty_nib(ns));
-                uint8_t *dst = smem_raw + (w16_s(ws) - raw) + r * 128;
-                const uint32_t words[4] = {p.x, p.y, p.z, p.w};
+                uint8_t *dst = smem_raw + (w16_s(ws) - raw) + half * W16_SUB + r * 128;
+                const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int c = half * 4 + j;  // 16-byte chunk of the 128-byte fp16 row
-                    *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = unpack8(words[j]);
-                }
+                for (int c = 0; c < 8; c++)  // 16-byte chunk c of the sub-tile's 128-byte fp16 row
+                    *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = unpack8(words[c]);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(wready(ws));
@@ -473,7 +484,7 @@ int launch_w4_tc_bn(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap 
 
 }  // namespace
 
-// Tensor-core W4 for K % 64 == 0 and a 16-byte aligned x; returns handled =
+// Tensor-core W4 for K % 128 == 0 and a 16-byte aligned x; returns handled =
 // false otherwise (the caller falls back to the SIMT kernel).
 int launch_w4_tc(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias, int act,
                  float *y, bool *handled) {
@@ -488,8 +499,8 @@ int launch_w4_tc(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_wei
     const int BN = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, n, k / 2, 1, W4_KB / 2, W4_TM,
                       CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tmap_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hi, m, k, 2, W4_KB, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lo, m, k, 2, W4_KB, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        !make_tmap_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hi, m, k, 2, W4_SUBK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lo, m, k, 2, W4_SUBK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
         return TPT_OK;
     *handled = true;
     const size_t groups = m * k / 8;
