@@ -114,6 +114,21 @@ int tpt_cuda_gelu(tpt_cuda_ctx *ctx, const float *a, size_t a_len, float *out, s
 /* Device-pointer forms of the same ops (validated shapes, async). */
 int tpt_cuda_matmul_dev(tpt_cuda_ctx *ctx, const float *a, size_t m, size_t k, const float *b,
                         size_t n, float *out);
+
+/* ONNX Gemm: Y = alpha * op(A) op(B) + beta * C. tpt-infer's ONNX loader maps
+ * "Gemm" to a plain MatMul and drops transA/transB/alpha/beta/C
+ * (crates/tpt-infer-onnx/src/registry.rs:21, load.rs:410-445); this is the full
+ * semantics. op(A) is A [m,k], or A^T of a stored [k,m] when trans_a; op(B) is
+ * B [k,n], or B^T of a stored [n,k] when trans_b. C is [n] (broadcast over rows)
+ * or [m,n]; c_len = 0 (c may be NULL) means no C term. Sequential k with a
+ * separately rounded multiply and add per term (the MatMul arithmetic), then
+ * alpha*acc + beta*c, each product and the sum rounded separately. Errors:
+ * SIZE_MISMATCH for a_len, b_len, out_len; SHAPE_MISMATCH for another c_len. */
+int tpt_cuda_gemm(tpt_cuda_ctx *ctx, const float *a, size_t a_len, size_t m, size_t k, int trans_a,
+                  const float *b, size_t b_len, size_t n, int trans_b, const float *c, size_t c_len,
+                  float alpha, float beta, float *out, size_t out_len);
+int tpt_cuda_gemm_dev(tpt_cuda_ctx *ctx, const float *a, size_t m, size_t k, int trans_a, const float *b,
+                      size_t n, int trans_b, const float *c, size_t c_len, float alpha, float beta, float *out);
 int tpt_cuda_conv2d_dev(tpt_cuda_ctx *ctx, const float *input, const size_t in_shape[4],
                         const float *weight, const size_t w_shape[4], float *out,
                         size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w);
@@ -262,8 +277,11 @@ enum tpt_op_kind {
     TPT_OP_GAP_NHWC = 12,       /* f32 [d0, d1=H*W, d2] -> [d0, d2] */
     TPT_OP_ALLGATHER = 13,      /* in0 [d0 elements] on every rank -> out [world * d0] in rank order (NCCL,
                                    on the context stream; the plan needs a communicator) */
-    TPT_OP_PANELS_TO_ROWS = 14  /* i8 [d0 = P][d1 = T][d2 = C] -> i8 [T][P * C] (gathered column shards ->
+    TPT_OP_PANELS_TO_ROWS = 14, /* i8 [d0 = P][d1 = T][d2 = C] -> i8 [T][P * C] (gathered column shards ->
                                    the K-contiguous rows of the next GEMM) */
+    TPT_OP_GEMM_F32 = 15        /* ONNX Gemm: out [d0=m, d2=n] = f0 * op(in0) op(in1) + C; in0 [m,k] (d3: stored
+                                   [k,m]), in1 [d1=k, n] (d4: stored [n,k]), in2 C [n] or [m,n] already scaled
+                                   by beta, or -1 */
 };
 
 typedef struct tpt_plan_op {

@@ -76,6 +76,8 @@ _sig("tpto_lcg_sym", None, _f32p, _sz, C.c_uint32)
 _sig("tpto_lcg_uniform", None, _f32p, _sz, C.c_uint32)
 _sig("tpto_normal", None, _f32p, _sz, C.c_uint32, C.c_float, C.c_float)
 _sig("tpto_matmul_naive", C.c_int, _f32p, _sz, _sz, _sz, _f32p, _sz, _sz, _sz, _f32p, _sz)
+_sig("tpto_gemm", C.c_int, _f32p, _sz, _sz, _sz, C.c_int, _f32p, _sz, _sz, C.c_int, C.c_void_p, _sz, C.c_float,
+     C.c_float, _f32p, _sz)
 _sig("tpto_matmul_avx", C.c_int, _f32p, _sz, _sz, _sz, _f32p, _sz, _sz, _sz, _f32p, _sz, C.c_int)
 _sig("tpto_conv2d", C.c_int, _f32p, _sz, _szp, _f32p, _sz, _szp, _f32p, _sz, _sz, _sz, _sz, _sz, C.c_int)
 _sig("tpto_elementwise_add", C.c_int, _f32p, _sz, _f32p, _sz, _f32p, _sz)
@@ -155,6 +157,16 @@ def matmul_naive(a, a_shape, b, b_shape, out_len=None):
     kb, n = b_shape
     out = np.empty(m * n if out_len is None else out_len, np.float32)
     _check(_lib.tpto_matmul_naive(a, a.size, m, k, b, b.size, kb, n, out, out.size))
+    return out
+
+
+def gemm(a, m, k, b, n, c=None, alpha=1.0, beta=1.0, trans_a=False, trans_b=False, out_len=None):
+    """ONNX Gemm (tpto_gemm): Y = alpha * op(A) op(B) + beta * C."""
+    a, b = _f32(a).ravel(), _f32(b).ravel()
+    cc = None if c is None else _f32(c).ravel()
+    out = np.empty(m * n if out_len is None else out_len, np.float32)
+    _check(_lib.tpto_gemm(a, a.size, m, k, int(trans_a), b, b.size, n, int(trans_b), _ptr_or_none(cc),
+                          0 if cc is None else cc.size, alpha, beta, out, out.size))
     return out
 
 

@@ -116,6 +116,43 @@ int tpto_matmul_naive(const float *a, size_t a_len, size_t m, size_t k,
     return TPTO_OK;
 }
 
+/* ONNX Gemm, Y = alpha * op(A) op(B) + beta * C: the semantics tpt-infer's
+ * loader drops when it maps "Gemm" to a plain MatMul (crates/tpt-infer-onnx/
+ * src/registry.rs:21; the transA/transB/alpha/beta attributes fall through the
+ * attribute match in load.rs:410-445). Defined here, restated by the device
+ * kernel: op(A) = A [m,k] or A^T of a stored [k,m]; op(B) = B [k,n] or B^T of a
+ * stored [n,k]; the sum runs in increasing k with a separate multiply and add
+ * (as naive.rs:13-33); then y = alpha*acc, plus beta*C when C is given, each
+ * product and the sum rounded separately. C is [n] (broadcast over rows) or
+ * [m,n]; c_len = 0 means no C. */
+int tpto_gemm(const float *a, size_t a_len, size_t m, size_t k, int trans_a,
+              const float *b, size_t b_len, size_t n, int trans_b,
+              const float *c, size_t c_len, float alpha, float beta,
+              float *out, size_t out_len) {
+    if (a_len != m * k) return TPTO_SIZE_MISMATCH;
+    if (b_len != k * n) return TPTO_SIZE_MISMATCH;
+    if (c_len != 0 && c_len != n && c_len != m * n) return TPTO_SHAPE_MISMATCH;
+    if (out_len != m * n) return TPTO_SIZE_MISMATCH;
+    for (size_t i = 0; i < m; i++)
+        for (size_t j = 0; j < n; j++) {
+            float acc = 0.0f;
+            for (size_t kk = 0; kk < k; kk++) {
+                const float av = trans_a ? a[kk * m + i] : a[i * k + kk];
+                const float bv = trans_b ? b[j * k + kk] : b[kk * n + j];
+                const float p = av * bv;
+                acc = acc + p;
+            }
+            float y = alpha * acc;
+            if (c_len) {
+                const float cv = c_len == n ? c[j] : c[i * n + j];
+                const float t = beta * cv;
+                y = y + t;
+            }
+            out[i * n + j] = y;
+        }
+    return TPTO_OK;
+}
+
 /* crates/tpt-infer-ops/src/avx512.rs:55-78 (and avx2.rs:47-66): out.fill(0);
  * for i, kk: out[i, :] = out[i, :] + a[i,kk]*b[kk, :] with a separate mul and
  * add. Bit-identical to naive (same k order, same two roundings). The j loop

@@ -49,6 +49,10 @@ void tpto_normal(float *out, size_t n, uint32_t seed, float mean, float std); /*
 int tpto_matmul_naive(const float *a, size_t a_len, size_t m, size_t k,
                       const float *b, size_t b_len, size_t kb, size_t n,
                       float *out, size_t out_len);
+int tpto_gemm(const float *a, size_t a_len, size_t m, size_t k, int trans_a,
+              const float *b, size_t b_len, size_t n, int trans_b,
+              const float *c, size_t c_len, float alpha, float beta,
+              float *out, size_t out_len);
 int tpto_matmul_avx(const float *a, size_t a_len, size_t m, size_t k,
                     const float *b, size_t b_len, size_t kb, size_t n,
                     float *out, size_t out_len, int threads);

@@ -28,6 +28,10 @@ def cases():
     b = O.lcg_sym(31 * 23, 102)
     c["matmul"] = dict(in_a=a, in_b=b, in_shape=np.array([17, 31, 23]),
                        out_y=O.matmul_naive(a, (17, 31), b, (31, 23)))
+    # ONNX Gemm (the semantics the loader drops, registry.rs:21): alpha A B^T + beta C[n]
+    ga, gb, gc = O.lcg_sym(9 * 20, 121), O.lcg_sym(13 * 20, 122), O.lcg_sym(13, 123)
+    c["gemm"] = dict(in_a=ga, in_b=gb, in_c=gc, in_shape=np.array([9, 20, 13]),
+                     out_y=O.gemm(ga, 9, 20, gb, 13, c=gc, alpha=0.5, beta=2.0, trans_b=True))
     # Conv2d (naive.rs:36-92), stride 2, pad 1
     x = O.lcg_sym(2 * 3 * 9 * 9, 103)
     w = O.lcg_sym(4 * 3 * 3 * 3, 104)

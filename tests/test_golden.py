@@ -45,6 +45,11 @@ def test_golden_backend_ops(cuda):
     cuda.matmul(g["in_a"], (m, k), g["in_b"], (k, n), y)
     assert np.array_equal(y, g["out_y"])
 
+    g = GOLD["gemm"]
+    m, k, n = (int(v) for v in g["in_shape"])
+    y = cuda.gemm(g["in_a"], m, k, g["in_b"], n, c=g["in_c"], alpha=0.5, beta=2.0, trans_b=True)
+    assert np.array_equal(y, g["out_y"])
+
     from tpt_infer_b200 import Conv2dOptions
     g = GOLD["conv2d"]
     bn, c, h, w, co, kh, kw, sh, sw, ph, pw = (int(v) for v in g["in_shape"])

@@ -163,3 +163,25 @@ def test_add_length_check(cuda):
 
 def test_backend_name(cuda):
     assert cuda.name() == "cuda"
+
+
+@pytest.mark.parametrize("m,k,n", [(3, 4, 5), (64, 784, 512), (129, 70, 33)])
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("cmode", [0, 1, 2])
+def test_gemm_onnx_bit_exact(cuda, m, k, n, ta, tb, cmode):
+    a = O.lcg_sym(m * k, 91)
+    b = O.lcg_sym(k * n, 92)
+    c = None if cmode == 0 else O.lcg_sym(n if cmode == 1 else m * n, 93)
+    got = cuda.gemm(a, m, k, b, n, c=c, alpha=1.5, beta=-0.75, trans_a=ta, trans_b=tb)
+    want = O.gemm(a, m, k, b, n, c=c, alpha=1.5, beta=-0.75, trans_a=ta, trans_b=tb)
+    assert np.array_equal(got, want)
+
+
+def test_gemm_onnx_errors(cuda):
+    from tpt_infer_b200 import OpError
+    with pytest.raises(OpError) as e:
+        cuda.gemm(np.ones(5), 2, 3, np.ones(9), 3)
+    assert (e.value.kind, e.value.expected, e.value.actual) == ("SizeMismatch", 6, 5)
+    with pytest.raises(OpError) as e:
+        cuda.gemm(np.ones(6), 2, 3, np.ones(9), 3, c=np.ones(4))
+    assert e.value.kind == "ShapeMismatch"

@@ -127,3 +127,49 @@ def test_attention_op(cuda, B, S):
     pa.close()
     want = OM._attention(qkv, B, S, 12, 64, 0.125).ravel()
     assert np.max(np.abs(att - want)) <= 1e-5 * (1 + np.max(np.abs(want)))
+
+
+def test_plan_fusion_rules(cuda):
+    # LINEAR -> QUANTIZE runs as one requantizing launch only when the f32
+    # tensor is not fetched; fetched or not, the int8 result is the same, and both
+    # match the oracle's separate quantize.
+    import torch
+
+    from tpt_infer_b200 import graphs, synth
+
+    m, k, n = 96, 512, 384
+    x = synth.normal(m * k, 61)
+    wq, ws = cuda.quantize_i8_symmetric_per_channel(synth.normal(n * k, 62, 0.0, 0.05), n)
+    bias = synth.normal(n, 63, 0.0, 0.1)
+    p = graphs.Plan(cuda)
+    w = cuda.upload_i8(wq, ws, n, k)
+    p.weights.append(w)
+    tx, tq = p.tensor(graphs.F32, m * k), p.tensor(graphs.I8, m * k)
+    ty, tyq = p.tensor(graphs.F32, m * n), p.tensor(graphs.I8, m * n)
+    p.op(graphs.OP_QUANTIZE, tx, tq, dims=(m * k,))
+    p.op(graphs.OP_LINEAR, tq, ty, in1=p.const(bias), w=w, act=graphs.ACT_RELU, dims=(m,))
+    p.op(graphs.OP_QUANTIZE, ty, tyq, dims=(m * n,))
+    p.finalize()
+    p.calibrate(True)
+    p.run({tx: x}, [ty])
+    p.freeze()
+    sx, sy = p.scales()
+
+    class _Dev:  # a view of a plan tensor for torch
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|i1", "data": (ptr, False), "version": 3}
+
+    def read_q():
+        torch.cuda.synchronize()
+        return torch.as_tensor(_Dev(p.ptr(tyq), m * n), device="cuda").cpu().numpy().copy()
+
+    y_unfused = p.run({tx: x}, [ty])[0]  # the f32 tensor is fetched: separate QUANTIZE
+    q_unfused = read_q()
+    p.run({tx: x}, [])                   # not fetched: requantizing epilogue
+    q_fused = read_q()
+    assert np.array_equal(q_unfused, q_fused)
+    xq = O.quantize_i8_static(x, sx)
+    want_y = O.w8a8_gemm(xq, wq, m, n, k, sx, ws, bias, O.ACT_RELU)
+    assert np.array_equal(y_unfused, want_y)
+    assert np.array_equal(q_fused, O.quantize_i8_static(want_y, sy))
+    p.close()

@@ -333,3 +333,24 @@ def test_product_synth_matches_oracle_generators():
         assert np.array_equal(synth.uniform(n, seed), O.lcg_uniform(n, seed))
         a, b = synth.normal(n, seed, 0.5, 2.0), O.normal(n, seed, 0.5, 2.0)
         assert np.max(np.abs(a - b)) <= 1e-6 * (1 + np.max(np.abs(b)))
+
+
+# ---------------------------------------------------------------- ONNX Gemm (defined here)
+def test_gemm_known_values():
+    # the loader maps Gemm to MatMul (registry.rs:21); the oracle states the full
+    # semantics: alpha * A B^T + beta * C with C broadcast over rows
+    y = O.gemm([1, 2, 3, 4], 2, 2, [5, 6, 7, 8], 2, c=[1, 2], alpha=2.0, beta=0.5, trans_b=True)
+    assert y.tolist() == [34.5, 47.0, 78.5, 107.0]
+    # no C, no transposes, alpha = 1: MatMul (naive.rs:212-219)
+    assert O.gemm([1, 2, 3, 4], 2, 2, [5, 6, 7, 8], 2).tolist() == [19.0, 22.0, 43.0, 50.0]
+    # trans_a: A stored [k, m]
+    assert O.gemm([1, 3, 2, 4], 2, 2, [5, 6, 7, 8], 2, trans_a=True).tolist() == [19.0, 22.0, 43.0, 50.0]
+
+
+def test_gemm_errors():
+    with pytest.raises(O.OracleError) as e:
+        O.gemm(np.ones(5), 2, 3, np.ones(9), 3)
+    assert e.value.code == O.SIZE_MISMATCH
+    with pytest.raises(O.OracleError) as e:
+        O.gemm(np.ones(6), 2, 3, np.ones(9), 3, c=np.ones(4))
+    assert e.value.code == O.SHAPE_MISMATCH

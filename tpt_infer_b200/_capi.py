@@ -76,6 +76,9 @@ SIGNATURES = {
     "tpt_cuda_quantize_i8_symmetric_noalloc": (C.c_int, [vp, sz, vp, vp, vp]),
     "tpt_cuda_plan_create": (C.c_int, [ctxp, C.POINTER(vp)]),
     "tpt_cuda_plan_destroy": (C.c_int, [vp]),
+    "tpt_cuda_gemm": (C.c_int, [vp, vp, sz, sz, sz, C.c_int, vp, sz, sz, C.c_int, vp, sz, C.c_float, C.c_float,
+                                vp, sz]),
+    "tpt_cuda_gemm_dev": (C.c_int, [vp, vp, sz, sz, C.c_int, vp, sz, C.c_int, vp, sz, C.c_float, C.c_float, vp]),
     "tpt_cuda_plan_add_tensor": (C.c_int, [vp, C.c_int, sz, C.POINTER(C.c_int)]),
     "tpt_cuda_plan_add_const": (C.c_int, [vp, vp, sz, C.POINTER(C.c_int)]),
     "tpt_cuda_plan_add_op": (C.c_int, [vp, vp]),

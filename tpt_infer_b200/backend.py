@@ -169,6 +169,17 @@ class CudaBackend:
         raise OpError(st, detail=detail)
 
     # ------------------------------------------------------------ trait methods
+    def gemm(self, a, m, k, b, n, c=None, alpha=1.0, beta=1.0, trans_a=False, trans_b=False, out=None):
+        """ONNX Gemm, Y = alpha * op(A) op(B) + beta * C (the attributes tpt-infer's
+        loader drops, crates/tpt-infer-onnx/src/registry.rs:21); C is [n] or [m, n]."""
+        a, b = _host(a, np.float32).ravel(), _host(b, np.float32).ravel()
+        cc = None if c is None else _host(c, np.float32).ravel()
+        y = np.empty(m * n, np.float32) if out is None else _out(out, np.float32)
+        self._check(lib.tpt_cuda_gemm(self._ctx, _ptr(a), a.size, m, k, int(trans_a), _ptr(b), b.size, n,
+                                      int(trans_b), _ptr(cc), 0 if cc is None else cc.size, float(alpha),
+                                      float(beta), _ptr(y), y.size))
+        return y
+
     def matmul(self, a, a_shape, b, b_shape, out):
         """Backend::matmul (backend.rs:106-113): out[m,n] = a[m,k] @ b[k,n]."""
         a, b, out = _host(a, np.float32).ravel(), _host(b, np.float32).ravel(), _out(out, np.float32)

@@ -142,6 +142,9 @@ int launch_dequant_i4_rows(tpt_cuda_ctx *ctx, const uint8_t *p, size_t rows, siz
 // requantized to int8 when rq.q != nullptr; W^T [n,k].
 int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w,
                 float a_scale, const float *bias, int act, float *y, int32_t *acc, Requant rq = Requant{});
+// ONNX Gemm: y = alpha * op(a) op(b) + beta * c; c_mode 0 none, 1 [n], 2 [m,n]
+int launch_gemm_onnx(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *c, int c_mode, float alpha,
+                     float beta, float *y, size_t m, size_t k, size_t n, bool ta, bool tb);
 int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w,
               const float *bias, int act, float *y);
 

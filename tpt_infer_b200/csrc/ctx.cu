@@ -274,6 +274,59 @@ int tpt_cuda_matmul_dev(tpt_cuda_ctx *ctx, const float *a, size_t m, size_t k, c
     return launch_matmul_f32(ctx, a, b, out, m, k, n);
 }
 
+// ------------------------------------------------------------------ ONNX Gemm
+// Checks: a_len = m*k, b_len = k*n (size mismatches report expected/actual),
+// c_len in {0, n, m*n} (else ShapeMismatch), out_len = m*n.
+static int validate_gemm(tpt_cuda_ctx *ctx, size_t a_len, size_t m, size_t k, size_t b_len, size_t n, const float *c,
+                         size_t c_len, size_t out_len, int *c_mode) {
+    size_t e, mn;
+    if (!checked_mul(m, k, &e)) return TPT_INVALID;
+    if (a_len != e) return set_size_mismatch(ctx, e, a_len);
+    if (!checked_mul(k, n, &e)) return TPT_INVALID;
+    if (b_len != e) return set_size_mismatch(ctx, e, b_len);
+    if (!checked_mul(m, n, &mn)) return TPT_INVALID;
+    if (c_len != 0 && c_len != n && c_len != mn) return TPT_SHAPE_MISMATCH;
+    if (c_len && !c) return TPT_INVALID;
+    if (out_len != mn) return set_size_mismatch(ctx, mn, out_len);
+    *c_mode = c_len == 0 ? 0 : (c_len == n ? 1 : 2);
+    return TPT_OK;
+}
+
+int tpt_cuda_gemm(tpt_cuda_ctx *ctx, const float *a, size_t a_len, size_t m, size_t k, int trans_a, const float *b,
+                  size_t b_len, size_t n, int trans_b, const float *c, size_t c_len, float alpha, float beta,
+                  float *out, size_t out_len) {
+    CHECK_CTX(ctx);
+    int c_mode = 0;
+    TRY(validate_gemm(ctx, a_len, m, k, b_len, n, c, c_len, out_len, &c_mode));
+    if (out_len == 0) return TPT_OK;
+    Staging st(ctx);
+    st.reserve(a_len * 4);
+    st.reserve(b_len * 4);
+    st.reserve(c_len * 4);
+    st.reserve(out_len * 4);
+    TRY(st.commit());
+    float *da = st.take<float>(a_len), *db = st.take<float>(b_len);
+    float *dcm = c_len ? st.take<float>(c_len) : nullptr;
+    float *dy = st.take<float>(out_len);
+    TRY(h2d(ctx, da, a, a_len * 4));
+    TRY(h2d(ctx, db, b, b_len * 4));
+    if (c_len) TRY(h2d(ctx, dcm, c, c_len * 4));
+    TRY(launch_gemm_onnx(ctx, da, db, dcm, c_mode, alpha, beta, dy, m, k, n, trans_a != 0, trans_b != 0));
+    TRY(d2h(ctx, out, dy, out_len * 4));
+    return sync_and_check(ctx);
+}
+
+int tpt_cuda_gemm_dev(tpt_cuda_ctx *ctx, const float *a, size_t m, size_t k, int trans_a, const float *b, size_t n,
+                      int trans_b, const float *c, size_t c_len, float alpha, float beta, float *out) {
+    CHECK_CTX(ctx);
+    size_t e;
+    int c_mode = 0;
+    if (!checked_mul(m, k, &e) || !checked_mul(k, n, &e) || !checked_mul(m, n, &e)) return TPT_INVALID;
+    TRY(validate_gemm(ctx, m * k, m, k, k * n, n, c, c_len, m * n, &c_mode));
+    if (m * n == 0) return TPT_OK;
+    return launch_gemm_onnx(ctx, a, b, c, c_mode, alpha, beta, out, m, k, n, trans_a != 0, trans_b != 0);
+}
+
 // ------------------------------------------------------------------ Backend::conv2d
 static int validate_conv2d(tpt_cuda_ctx *ctx, size_t in_len, const size_t is[4], size_t w_len,
                            const size_t ws[4], size_t out_len, size_t sh, size_t sw, size_t ph,

@@ -201,7 +201,76 @@ __global__ void __launch_bounds__(256) k_gemm_f32_small(const float *__restrict_
     if (m < M && n < N) Cout[(size_t)m * N + n] = acc;
 }
 
+// ONNX Gemm, Y = alpha * op(A) op(B) + beta * C (C: none, [N] broadcast, or
+// [M,N]): the small-tile structure above with transposable operands (each tile
+// load walks the operand's contiguous dimension with consecutive threads), the
+// same per-output sequential RN multiply-then-add, and an epilogue that rounds
+// alpha*acc, beta*c and their sum separately.
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(256) k_gemm_onnx(const float *__restrict__ A, const float *__restrict__ B,
+                                                  const float *__restrict__ Cm, int c_mode, float alpha, float beta,
+                                                  float *__restrict__ Y, int M, int N, int K) {
+    __shared__ float As[SK][SB + 1];
+    __shared__ float Bs[SK][SB + 1];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * SB, n0 = blockIdx.x * SB;
+    float acc = 0.0f;
+    for (int k0 = 0; k0 < K; k0 += SK) {
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int e = tid + 256 * i;
+            {
+                const int r = TA ? (e & 15) : (e >> 5), c = TA ? (e >> 4) : (e & 31);
+                const int m = m0 + r, ka = k0 + c;
+                float v = 0.0f;
+                if (m < M && ka < K) v = TA ? A[(size_t)ka * M + m] : A[(size_t)m * K + ka];
+                As[c][r] = v;
+            }
+            {
+                const int kr = TB ? (e & 31) : (e >> 4), nc = TB ? (e >> 5) : (e & 15);
+                const int kb = k0 + kr, n = n0 + nc;
+                float v = 0.0f;
+                if (kb < K && n < N) v = TB ? B[(size_t)n * K + kb] : B[(size_t)kb * N + n];
+                Bs[kr][nc] = v;
+            }
+        }
+        __syncthreads();
+        if (K - k0 >= SK) {
+#pragma unroll
+            for (int kk = 0; kk < SK; kk++) acc = __fadd_rn(acc, __fmul_rn(As[kk][ty], Bs[kk][tx]));
+        } else {
+            for (int kk = 0; kk < K - k0; kk++) acc = __fadd_rn(acc, __fmul_rn(As[kk][ty], Bs[kk][tx]));
+        }
+        __syncthreads();
+    }
+    const int m = m0 + ty, n = n0 + tx;
+    if (m < M && n < N) {
+        float y = __fmul_rn(alpha, acc);
+        if (c_mode) y = __fadd_rn(y, __fmul_rn(beta, c_mode == 1 ? Cm[n] : Cm[(size_t)m * N + n]));
+        Y[(size_t)m * N + n] = y;
+    }
+}
+
 }  // namespace
+
+int launch_gemm_onnx(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *c, int c_mode, float alpha,
+                     float beta, float *y, size_t m, size_t k, size_t n, bool ta, bool tb) {
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
+    dim3 g((unsigned)((n + SB - 1) / SB), (unsigned)((m + SB - 1) / SB));
+    if (g.y > 65535) return TPT_UNSUPPORTED;
+#define TPT_ONNX(TA_, TB_)                                                                                     \
+    k_gemm_onnx<TA_, TB_><<<g, 256, 0, ctx->stream>>>(a, b, c, c_mode, alpha, beta, y, (int)m, (int)n, (int)k)
+    if (ta && tb)
+        TPT_ONNX(true, true);
+    else if (ta)
+        TPT_ONNX(true, false);
+    else if (tb)
+        TPT_ONNX(false, true);
+    else
+        TPT_ONNX(false, false);
+#undef TPT_ONNX
+    return after_launch(ctx, "gemm_onnx");
+}
 
 int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m, size_t k,
                       size_t n) {

@@ -160,6 +160,11 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
             return comm_all_gather(p->comm, p->tensors[o.in0].ptr, p->tensors[o.out].ptr,
                                    d[0] * dt_size(p->tensors[o.in0].dtype));
         }
+        case TPT_OP_GEMM_F32: {  // ONNX Gemm, beta folded into the constant C
+            const int c_mode = o.in2 < 0 ? 0 : (p->tensors[o.in2].numel == d[2] ? 1 : 2);
+            return launch_gemm_onnx(ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), c_mode, o.f0, 1.0f, F(p, o.out), d[0],
+                                    d[1], d[2], d[3] != 0, d[4] != 0);
+        }
         case TPT_OP_PANELS_TO_ROWS:  // i8 [d0 = P][d1 = T][d2 = C] -> i8 [T][P * C]
             p->tensors[o.out].scale = p->tensors[o.in0].scale;
             return launch_panels_to_rows(ctx, Q(p, o.in0), Q(p, o.out), (int)d[0], d[1], (int)d[2]);
@@ -251,7 +256,15 @@ int tpt_cuda_plan_add_op(tpt_cuda_plan *p, const tpt_plan_op *op) {
     if (!valid_id(p, op->in0) || !valid_id(p, op->out)) return TPT_INVALID;
     if ((op->in1 >= 0 && !valid_id(p, op->in1)) || (op->in2 >= 0 && !valid_id(p, op->in2))) return TPT_INVALID;
     if (op->kind == TPT_OP_LINEAR_W8A8 && (!op->w || op->w->kind != 8)) return TPT_INVALID;
-    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_PANELS_TO_ROWS) return TPT_UNSUPPORTED;
+    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_GEMM_F32) return TPT_UNSUPPORTED;
+    if (op->kind == TPT_OP_GEMM_F32) {
+        size_t mk = 0, kn = 0, mn = 0;
+        const size_t m = op->dims[0], k = op->dims[1], n = op->dims[2];
+        if (!checked_mul(m, k, &mk) || !checked_mul(k, n, &kn) || !checked_mul(m, n, &mn) ||
+            p->tensors[op->in0].numel != mk || p->tensors[op->in1].numel != kn || p->tensors[op->out].numel != mn)
+            return TPT_INVALID;
+        if (op->in2 >= 0 && p->tensors[op->in2].numel != n && p->tensors[op->in2].numel != mn) return TPT_INVALID;
+    }
     if (op->kind == TPT_OP_ALLGATHER) {
         const PlanTensor &a = p->tensors[op->in0], &b = p->tensors[op->out];
         if (a.dtype != b.dtype || op->dims[0] > a.numel) return TPT_INVALID;

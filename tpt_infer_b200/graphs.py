@@ -32,7 +32,7 @@ from .backend import ACT_GELU, ACT_NONE, ACT_RELU, CudaBackend, OpError
 F32, I8 = 0, 1
 OP_QUANTIZE, OP_LINEAR, OP_MATMUL, OP_BIAS_ACT, OP_ADD_ACT, OP_SOFTMAX, OP_LAYERNORM, OP_ATTENTION = range(1, 9)
 OP_NCHW_Q8, OP_IM2COL, OP_MAXPOOL, OP_GAP = 9, 10, 11, 12
-OP_ALLGATHER, OP_PANELS_TO_ROWS = 13, 14
+OP_ALLGATHER, OP_PANELS_TO_ROWS, OP_GEMM = 13, 14, 15
 
 
 class Plan:
