@@ -482,7 +482,7 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     const long long pairs = ctx->sm_count / 2 > 0 ? ctx->sm_count / 2 : 1;
     const long long mt = (M + P_BM - 1) / P_BM;
     const int widths[3] = {256, 128, 64};
-    const double cost[3] = {1.0, 1.15, 1.5};
+    const double cost[3] = {1.0, 1.6, 2.6};
     int bn = 256;
     double best = 0.0;
     for (int i = 0; i < 3; i++) {
