@@ -82,6 +82,27 @@ void tpt_cuda_last_size_mismatch(tpt_cuda_ctx *ctx, size_t *expected, size_t *ac
 /* Number of kernels this library launched on the context since creation. */
 uint64_t tpt_cuda_ctx_launch_count(tpt_cuda_ctx *ctx);
 
+/* CUDA graphs of device-pointer calls. The reference runtime walks the graph
+ * node by node on every call (crates/tpt-infer-runtime/src/exec.rs:570-635);
+ * on the device a fixed sequence of launches is recorded once and replayed
+ * with one launch. tpt_cuda_capture_begin starts recording what is issued on
+ * the context's stream; tpt_cuda_capture_end ends it (always call it once
+ * begin succeeded) and returns the graph. Only device-pointer (_dev) entry
+ * points and tpt_cuda_plan_run_device can be recorded: a call that would
+ * synchronise or grow a context workspace returns TPT_INVALID while
+ * recording, so run each call once before recording it. A graph keeps the
+ * context's workspace addresses: once a later call grows a workspace,
+ * tpt_cuda_graph_launch returns TPT_INVALID and the graph must be recorded
+ * again. */
+typedef struct tpt_cuda_graph tpt_cuda_graph;
+int tpt_cuda_capture_begin(tpt_cuda_ctx *ctx);
+int tpt_cuda_capture_end(tpt_cuda_ctx *ctx, tpt_cuda_graph **graph);
+/* enqueues one replay on the context's stream (async) */
+int tpt_cuda_graph_launch(tpt_cuda_ctx *ctx, tpt_cuda_graph *graph);
+/* kernels one replay launches */
+uint64_t tpt_cuda_graph_kernels(const tpt_cuda_graph *graph);
+int tpt_cuda_graph_destroy(tpt_cuda_graph *graph);
+
 /* ------------------------------------------------------------------ */
 /* Backend trait, host slices (crates/tpt-infer-ops/src/backend.rs:98-147) */
 /* ------------------------------------------------------------------ */
@@ -312,6 +333,11 @@ int tpt_cuda_plan_get_scales(tpt_cuda_plan *plan, float *scales, size_t n, size_
 /* Imports a calibration: n must equal the number of points, every scale > 0;
  * the plan leaves calibration mode. (Batch-sharded ranks share one.) */
 int tpt_cuda_plan_set_scales(tpt_cuda_plan *plan, const float *scales, size_t n);
+/* With graphs on (default off), a run with frozen scales records the op
+ * sequence once (after one direct run that sizes the workspaces) and replays
+ * it from then on; calibration, new scales, a different output set or a moved
+ * workspace make it record again. Plans with a communicator run directly. */
+int tpt_cuda_plan_set_graph(tpt_cuda_plan *plan, int on);
 /* ops only, inputs already resident (async) */
 int tpt_cuda_plan_run_device(tpt_cuda_plan *plan);
 /* H2D of the inputs, the ops, D2H of the outputs, then synchronise */

@@ -34,7 +34,7 @@ def w8a8_case(m, n, k, seed=100, with_bias=True):
                                    (128, 256, 128), (300, 512, 256), (1000, 768, 768), (160, 203, 96),
                                    (4097, 300, 128), (33, 300, 256), (64, 512, 784), (48, 4096, 4096),
                                    (17, 4097, 4112), (65, 512, 256), (100, 1000, 1024), (2, 300, 8192),
-                                   (4, 257, 4160)])
+                                   (4, 257, 4160), (16, 1024, 4096), (64, 2048, 2048), (5, 200, 384)])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_w8a8_bit_exact(cuda, m, n, k, act):
     if act and m * n * k > 1 << 26:
@@ -91,6 +91,34 @@ def test_w8a8_small_m_back_to_back(cuda):
     for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in cases:
         want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, 1, threads=8)
         assert np.array_equal(y_dev.cpu().numpy(), want), (m, n, k)
+        w.free()
+
+
+def test_w8a8_large_m_back_to_back(cuda):
+    # SM-pair launches of several shapes and tile widths queued back to back
+    # on the stream (twice) with no host sync in between, every result checked
+    import torch
+
+    cases = []
+    for i, (m, n, k) in enumerate([(256, 4096, 4096), (1000, 768, 768), (8192, 768, 3072), (300, 512, 256),
+                                   (256, 4096, 4096), (2048, 1000, 1024)]):
+        aq, sa, wq, ws, bias = w8a8_case(m, n, k, seed=600 + 10 * i)
+        w = cuda.upload_i8(wq, ws, n, k)
+        a_dev = torch.from_numpy(aq).cuda()
+        b_dev = torch.from_numpy(bias).cuda()
+        y_dev = torch.empty(m * n, dtype=torch.float32, device="cuda")
+        cases.append((m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev))
+    torch.cuda.synchronize()
+    for _ in range(2):
+        for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in cases:
+            cuda.w8a8_gemm_dev(a_dev, m, sa, w, b_dev, 0, y_dev)
+    cuda.sync()
+    for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in cases:
+        got = y_dev.cpu().numpy().reshape(m, n)
+        rows = np.unique(np.concatenate([[0, m - 1], np.random.default_rng(m + n).integers(0, m, 64)]))
+        want = O.w8a8_gemm(aq.reshape(m, k)[rows].ravel(), wq, rows.size, n, k, sa, ws, bias, 0,
+                           threads=8).reshape(rows.size, n)
+        assert np.array_equal(got[rows], want), (m, n, k)
         w.free()
 
 

@@ -37,6 +37,11 @@ SIGNATURES = {
     "tpt_cuda_last_error": (C.c_char_p, [ctxp]),
     "tpt_cuda_last_size_mismatch": (None, [ctxp, szp, szp]),
     "tpt_cuda_ctx_launch_count": (C.c_uint64, [ctxp]),
+    "tpt_cuda_capture_begin": (C.c_int, [ctxp]),
+    "tpt_cuda_capture_end": (C.c_int, [ctxp, C.POINTER(C.c_void_p)]),
+    "tpt_cuda_graph_launch": (C.c_int, [ctxp, vp]),
+    "tpt_cuda_graph_kernels": (C.c_uint64, [vp]),
+    "tpt_cuda_graph_destroy": (C.c_int, [vp]),
     "tpt_cuda_matmul": (C.c_int, [ctxp, vp, sz, sz, sz, vp, sz, sz, sz, vp, sz]),
     "tpt_cuda_conv2d": (C.c_int, [ctxp, vp, sz, szp, vp, sz, szp, vp, sz, sz, sz, sz, sz]),
     "tpt_cuda_elementwise_add": (C.c_int, [ctxp, vp, sz, vp, sz, vp, sz]),
@@ -90,6 +95,7 @@ SIGNATURES = {
     "tpt_cuda_plan_get_scales": (C.c_int, [vp, vp, sz, szp]),
     "tpt_cuda_plan_set_scales": (C.c_int, [vp, vp, sz]),
     "tpt_cuda_plan_run_device": (C.c_int, [vp]),
+    "tpt_cuda_plan_set_graph": (C.c_int, [vp, C.c_int]),
     "tpt_cuda_plan_run": (C.c_int, [vp, vp, vp, sz, vp, vp, sz]),
     # multi-GPU
     "tpt_cuda_comm_unique_id": (C.c_int, [vp, sz]),

@@ -108,6 +108,31 @@ class Weights:
             pass
 
 
+class Graph:
+    """A recorded launch sequence (tpt_cuda_capture_begin/_end)."""
+
+    def __init__(self, be, handle):
+        self.be, self.h = be, handle
+
+    @property
+    def kernels(self) -> int:
+        return int(lib.tpt_cuda_graph_kernels(self.h))
+
+    def launch(self):
+        self.be._check(lib.tpt_cuda_graph_launch(self.be.ctx, self.h))
+
+    def close(self):
+        if self.h:
+            lib.tpt_cuda_graph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class CudaBackend:
     """The CUDA implementation of the Backend trait on one B200."""
 
@@ -153,6 +178,24 @@ class CudaBackend:
 
     def sync(self):
         self._check(lib.tpt_cuda_ctx_sync(self._ctx))
+
+    def capture(self, fn):
+        """Records the device-pointer calls ``fn()`` issues on this context into a
+        CUDA graph (run ``fn`` once before, so every workspace is sized)."""
+        self._check(lib.tpt_cuda_capture_begin(self._ctx))
+        err = None
+        try:
+            fn()
+        except Exception as e:  # the recording must still be closed
+            err = e
+        h = C.c_void_p()
+        st = lib.tpt_cuda_capture_end(self._ctx, C.byref(h))
+        if err is not None:
+            if h.value:
+                lib.tpt_cuda_graph_destroy(h)
+            raise err
+        self._check(st)
+        return Graph(self, h)
 
     def name(self) -> str:
         """Backend::name (backend.rs:100)."""

@@ -39,6 +39,12 @@ struct tpt_cuda_ctx {
     size_t last_expected = 0, last_actual = 0;
     std::string last_error;
     uint64_t launches = 0;
+    // CUDA graph recording: while `capturing`, nothing may allocate or wait.
+    // `ws_gen` counts workspace moves; a graph recorded at another generation
+    // holds stale workspace addresses and is refused at launch.
+    bool capturing = false;
+    uint64_t capture_launches0 = 0;
+    uint64_t ws_gen = 0;
 };
 
 struct tpt_cuda_weights {
@@ -50,7 +56,7 @@ struct tpt_cuda_weights {
     float *scales = nullptr;  // device: n per-channel scales
     size_t bytes = 0;
     // TMA descriptors of the int8 weight (CUtensorMap, 128 bytes each), built
-    // once: boxes of 128 / 64 / 32 rows x 128 bytes (the stream-K kernel's
+    // once: boxes of 128 / 64 / 32 rows x 128 bytes (the small-M kernel's
     // weight tile, and the SM-pair kernel's B half-tiles for tile N = 256 /
     // 128 / 64)
     alignas(64) unsigned char tmaps[3][128];

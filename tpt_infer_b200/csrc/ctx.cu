@@ -35,8 +35,17 @@ int after_launch(tpt_cuda_ctx *ctx, const char *what, int n) {
     return TPT_OK;
 }
 
+// Workspaces cannot move while a graph is being recorded: the graph would
+// keep the old address. The caller runs the call once before recording it.
+static int refuse_in_capture(tpt_cuda_ctx *ctx, const char *what) {
+    ctx->last_error = std::string(what) + " while a graph is being recorded (run the call once before recording)";
+    return TPT_INVALID;
+}
+
 int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes) {
     if (bytes <= ctx->scratch_cap) return TPT_OK;
+    if (ctx->capturing) return refuse_in_capture(ctx, "scratch grows");
+    ctx->ws_gen++;
     size_t cap = ctx->scratch_cap ? ctx->scratch_cap : (size_t)1 << 20;
     while (cap < bytes) cap *= 2;
     if (ctx->scratch) {
@@ -57,6 +66,8 @@ int ensure_scratch(tpt_cuda_ctx *ctx, size_t bytes) {
 
 int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes) {
     if (bytes <= ctx->ws_cap) return TPT_OK;
+    if (ctx->capturing) return refuse_in_capture(ctx, "workspace grows");
+    ctx->ws_gen++;
     size_t cap = ctx->ws_cap ? ctx->ws_cap : (size_t)1 << 20;
     while (cap < bytes) cap *= 2;
     if (ctx->ws) {
@@ -78,6 +89,8 @@ int ensure_ws(tpt_cuda_ctx *ctx, size_t bytes) {
 int ensure_sk(tpt_cuda_ctx *ctx, size_t slot_bytes) {
     const size_t bytes = TPT_SK_SLOTS_OFFSET + slot_bytes;
     if (bytes > ctx->sk_cap) {
+        if (ctx->capturing) return refuse_in_capture(ctx, "stream-K workspace grows");
+        ctx->ws_gen++;
         size_t cap = ctx->sk_cap ? ctx->sk_cap : (size_t)1 << 20;
         while (cap < bytes) cap *= 2;
         if (ctx->sk) {
@@ -96,6 +109,7 @@ int ensure_sk(tpt_cuda_ctx *ctx, size_t slot_bytes) {
         ctx->sk_dirty = true;
     }
     if (ctx->sk_dirty) {
+        if (ctx->capturing) return refuse_in_capture(ctx, "stream-K workspace clear");
         cudaError_t e = cudaMemsetAsync(ctx->sk, 0, ctx->sk_cap, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "stream-K workspace clear");
         ctx->sk_dirty = false;
@@ -116,6 +130,7 @@ int d2h(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes) {
 }
 
 int sync_and_check(tpt_cuda_ctx *ctx) {
+    if (ctx->capturing) return refuse_in_capture(ctx, "a synchronising call");
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "stream sync");
     unsigned flags[TPT_FLAG_WORDS];
@@ -237,6 +252,82 @@ void tpt_cuda_last_size_mismatch(tpt_cuda_ctx *ctx, size_t *expected, size_t *ac
     if (actual) *actual = ctx->last_actual;
 }
 uint64_t tpt_cuda_ctx_launch_count(tpt_cuda_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+// ---- CUDA graphs of device-pointer calls ----
+
+struct tpt_cuda_graph {
+    int device = 0;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t kernels = 0;  // kernel launches recorded (added to the launch count per replay)
+    uint64_t ws_gen = 0;   // workspace generation the recorded addresses belong to
+};
+
+int tpt_cuda_capture_begin(tpt_cuda_ctx *ctx) {
+    CHECK_CTX(ctx);
+    if (ctx->capturing) return TPT_INVALID;
+    if (ctx->sk_dirty && ctx->sk) {  // clear a timed-out launch's leftovers outside the graph
+        int st = ensure_sk(ctx, 0);
+        if (st) return st;
+    }
+    cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "begin capture");
+    ctx->capturing = true;
+    ctx->capture_launches0 = ctx->launches;
+    return TPT_OK;
+}
+
+int tpt_cuda_capture_end(tpt_cuda_ctx *ctx, tpt_cuda_graph **out) {
+    CHECK_CTX(ctx);
+    if (!ctx->capturing || !out) return TPT_INVALID;
+    *out = nullptr;
+    ctx->capturing = false;
+    const uint64_t kernels = ctx->launches - ctx->capture_launches0;
+    ctx->launches = ctx->capture_launches0;  // recorded, not run
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return cuda_fail(ctx, e, "end capture");
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "graph instantiate");
+    tpt_cuda_graph *gr = new (std::nothrow) tpt_cuda_graph();
+    if (!gr) {
+        cudaGraphExecDestroy(exec);
+        return TPT_OUT_OF_MEMORY;
+    }
+    gr->device = ctx->device;
+    gr->exec = exec;
+    gr->kernels = kernels;
+    gr->ws_gen = ctx->ws_gen;
+    *out = gr;
+    return TPT_OK;
+}
+
+int tpt_cuda_graph_launch(tpt_cuda_ctx *ctx, tpt_cuda_graph *g) {
+    CHECK_CTX(ctx);
+    if (!g || ctx->capturing || g->device != ctx->device) return TPT_INVALID;
+    if (g->ws_gen != ctx->ws_gen) {
+        ctx->last_error = "a workspace moved since the graph was recorded (record it again)";
+        return TPT_INVALID;
+    }
+    cudaError_t e = cudaGraphLaunch(g->exec, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "graph launch");
+    ctx->launches += g->kernels;
+    return TPT_OK;
+}
+
+uint64_t tpt_cuda_graph_kernels(const tpt_cuda_graph *g) { return g ? g->kernels : 0; }
+
+int tpt_cuda_graph_destroy(tpt_cuda_graph *g) {
+    if (!g) return TPT_INVALID;
+    cudaSetDevice(g->device);
+    cudaGraphExecDestroy(g->exec);
+    delete g;
+    return TPT_OK;
+}
 
 // ------------------------------------------------------------------ Backend::matmul
 int tpt_cuda_matmul(tpt_cuda_ctx *ctx, const float *a, size_t a_len, size_t m, size_t k,

@@ -73,11 +73,21 @@ struct tpt_cuda_plan {
     int n_cells = 0;
     bool finalized = false;
     bool calibrating = false;
+    // recorded replay of run_ops (tpt_cuda_plan_set_graph) and the output set it was recorded for
+    bool use_graph = false;
+    tpt_cuda_graph *graph = nullptr;
+    std::vector<int> graph_out;
 };
 
 namespace {
 
 size_t dt_size(int dt) { return dt == TPT_DT_I8 ? 1 : 4; }
+
+void drop_graph(tpt_cuda_plan *p) {
+    if (p->graph) tpt_cuda_graph_destroy(p->graph);
+    p->graph = nullptr;
+    p->graph_out.clear();
+}
 
 bool valid_id(tpt_cuda_plan *p, int id) { return id >= 0 && (size_t)id < p->tensors.size(); }
 
@@ -213,6 +223,7 @@ int tpt_cuda_plan_create(tpt_cuda_ctx *ctx, tpt_cuda_plan **out) {
 int tpt_cuda_plan_destroy(tpt_cuda_plan *p) {
     if (!p) return TPT_INVALID;
     cudaSetDevice(p->device);
+    drop_graph(p);
     if (p->arena) cudaFree(p->arena);
     if (p->cells) cudaFree(p->cells);
     for (auto &t : p->tensors)
@@ -317,6 +328,7 @@ int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
 
 int tpt_cuda_plan_set_comm(tpt_cuda_plan *p, tpt_cuda_comm *comm) {
     CHECK_PLAN(p);
+    drop_graph(p);
     p->comm = comm;
     return TPT_OK;
 }
@@ -336,7 +348,15 @@ int tpt_cuda_plan_tensor_ptr(tpt_cuda_plan *p, int id, void **dev) {
 
 int tpt_cuda_plan_set_calibration(tpt_cuda_plan *p, int on) {
     CHECK_PLAN(p);
+    drop_graph(p);
     p->calibrating = on != 0;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_set_graph(tpt_cuda_plan *p, int on) {
+    CHECK_PLAN(p);
+    drop_graph(p);
+    p->use_graph = on != 0;
     return TPT_OK;
 }
 
@@ -347,6 +367,7 @@ int tpt_cuda_plan_freeze_scales(tpt_cuda_plan *p) {
             const float m = p->cal_max[po.cell];
             po.frozen = m == 0.0f ? 1.0f : m / 127.0f;
         }
+    drop_graph(p);
     p->calibrating = false;
     return TPT_OK;
 }
@@ -371,6 +392,7 @@ int tpt_cuda_plan_set_scales(tpt_cuda_plan *p, const float *scales, size_t n) {
     size_t c = 0;
     for (auto &po : p->ops)
         if (po.cell >= 0) po.frozen = scales[c++];
+    drop_graph(p);
     p->calibrating = false;
     return TPT_OK;
 }
@@ -446,12 +468,41 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
     }
     return TPT_OK;
 }
+
+// run_ops, or its recorded replay. The first run after a change goes direct
+// (sizing every workspace the ops use), then the same sequence is recorded;
+// later runs launch the recording.
+int run_plan(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
+    if (!p->use_graph || p->calibrating || p->comm) return run_ops(p, out_ids, n_out);
+    tpt_cuda_ctx *ctx = p->ctx;
+    const std::vector<int> key(out_ids, out_ids + n_out);
+    if (p->graph && key == p->graph_out) {
+        if (tpt_cuda_graph_launch(ctx, p->graph) == TPT_OK) return TPT_OK;
+        drop_graph(p);  // a workspace moved: record again below
+    }
+    drop_graph(p);
+    int st = run_ops(p, out_ids, n_out);
+    if (st) return st;
+    st = tpt_cuda_capture_begin(ctx);
+    if (st) return st;
+    const int st_ops = run_ops(p, out_ids, n_out);
+    tpt_cuda_graph *g = nullptr;
+    st = tpt_cuda_capture_end(ctx, &g);
+    if (st_ops) {
+        if (g) tpt_cuda_graph_destroy(g);
+        return st_ops;
+    }
+    if (st) return st;
+    p->graph = g;
+    p->graph_out = key;
+    return TPT_OK;
+}
 }  // namespace
 
 int tpt_cuda_plan_run_device(tpt_cuda_plan *p) {
     CHECK_PLAN(p);
     if (!p->finalized) return TPT_INVALID;
-    return run_ops(p, nullptr, 0);
+    return run_plan(p, nullptr, 0);
 }
 
 int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *inputs, size_t n_in,
@@ -464,7 +515,7 @@ int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *i
         int st = h2d(p->ctx, t.ptr, inputs[i], t.numel * dt_size(t.dtype));
         if (st) return st;
     }
-    int st = run_ops(p, out_ids, n_out);
+    int st = run_plan(p, out_ids, n_out);
     if (st) return st;
     for (size_t i = 0; i < n_out; i++) {
         if (!valid_id(p, out_ids[i])) return TPT_INVALID;

@@ -9,8 +9,8 @@
 //  - k_w8a8_gemv: M <= 4. One warp per output channel streams the K-contiguous
 //    weight row with 128-bit loads (all of a pass in flight) and dp4a.
 //  - k_w8a8_simt: general shapes (ragged M/N, K % 16 == 0); dp4a tiles.
-//  - the tcgen05 tensor-core kernels: stream-K for M <= 64 in w8a8_sk.cu,
-//    one-SM and SM-pair tiles for larger M in w8a8_tc.cu.
+//  - the tcgen05 tensor-core kernels: K split over a thread-block cluster
+//    for 4 < M <= 64 in w8a8_ck.cu, SM-pair tiles for larger M in w8a8_tc.cu.
 // Weight layout in HBM: W^T [n, k] int8 row-major (K-major B operand), which
 // is the byte layout quantize_i8_symmetric_per_channel(W^T, rows = n) emits.
 #include <string.h>
@@ -24,7 +24,7 @@ namespace tpt {
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
 int build_weight_tmap(tpt_cuda_weights *w);
-int launch_w8a8_sk(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
+int launch_w8a8_ck(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
 
 namespace {
@@ -246,7 +246,7 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     }
     bool handled = false;
     if (m <= 64) {
-        int st = launch_w8a8_sk(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);
+        int st = launch_w8a8_ck(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);
         if (st || handled) return st;
     }
     int st = launch_w8a8_tc(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);

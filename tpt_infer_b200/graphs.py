@@ -108,6 +108,10 @@ class Plan:
         a = np.ascontiguousarray(scales, np.float32)
         self.be._check(lib.tpt_cuda_plan_set_scales(self.h, a.ctypes.data_as(C.c_void_p), a.size))
 
+    def set_graph(self, on=True):
+        """Replays a recorded launch sequence once scales are frozen (CUDA graph)."""
+        self.be._check(lib.tpt_cuda_plan_set_graph(self.h, int(bool(on))))
+
     def run_device(self):
         self.be._check(lib.tpt_cuda_plan_run_device(self.h))
 
