@@ -112,7 +112,7 @@ def test_bert_plan_two_layers(cuda, B, S):
     p.close()
 
 
-@pytest.mark.parametrize("B,S", [(2, 128), (1, 77)])
+@pytest.mark.parametrize("B,S", [(2, 128), (1, 77), (3, 40), (1, 1)])
 def test_attention_op(cuda, B, S):
     # the fused attention op alone against the oracle's MatMul / Softmax / MatMul
     from tpt_infer_b200 import graphs, synth

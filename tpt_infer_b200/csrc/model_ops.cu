@@ -1,5 +1,6 @@
 // model_ops.cu -- device ops the model plans need besides the GEMMs:
-// LayerNorm, fused attention, bias/residual adds, NHWC INT8 conv plumbing
+// LayerNorm, bias/residual adds, NHWC INT8 conv plumbing (the fused attention
+// is in attention_tc.cu)
 // (layout change + quantize, im2col), pooling, per-tensor max-abs.
 //
 // Layout inside a plan: activations are row-major [rows, channels] (NHWC for
@@ -98,146 +99,6 @@ __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restr
                                              ((uint32_t)(uint8_t)requant_i8(o.z, qs) << 16) |
                                              ((uint32_t)(uint8_t)requant_i8(o.w, qs) << 24);
         }
-    }
-}
-
-// ---------------------------------------------------------------- attention
-// Fused softmax(Q K^T * scale) V per (batch, head) on f32, reading Q, K, V from
-// the packed projection output qkv [B*S, 3*H*D] (Q | K | V along columns) and
-// writing ctx [B*S, H*D]. One CTA per (batch, head, 64-query block); K and V of
-// the head are staged in shared memory; each thread owns one query row and
-// runs an online (streaming) softmax over key blocks of 16.
-constexpr int AT_D = 64;     // head dimension
-constexpr int AT_S = 128;    // sequence length handled by the tiled kernel
-constexpr int AT_LD = AT_S + 4;  // padded row of the transposed tiles
-// Shared memory of k_attention: Q^T and K^T [D][S+4] (whose space P^T [S][S+4]
-// reuses once the scores are in registers) and V [S][D]: ~100 KB, 2 CTAs/SM.
-constexpr size_t AT_SMEM = (size_t)(2 * AT_D * AT_LD + AT_S * AT_D) * sizeof(float);
-static_assert(AT_S * AT_LD <= 2 * AT_D * AT_LD, "P^T fits in the Q^T/K^T space");
-
-// Attention for one (batch, head) per 256-thread CTA, S <= 128 (keys past S
-// masked out, queries past S not stored), D = 64, f32:
-//   S = scale * Q K^T            8x8 scores per thread (register tile)
-//   P = softmax(S) by rows       max-subtract, exp, sum, divide (naive.rs:104-125)
-//   O = P V                      8x4 outputs per thread
-// Q^T, K^T and P^T are held transposed in shared memory so every inner step
-// is two float4 loads feeding 32-64 FMAs. qkv rows are [q | k | v] of H*D each.
-__global__ void __launch_bounds__(256) k_attention(const float *__restrict__ qkv, float *__restrict__ out, int S,
-                                                   int H, float scale, int8_t *__restrict__ qout, float qs) {
-    extern __shared__ __align__(16) float sm[];
-    float *Qt = sm;                          // [D][LD]
-    float *Kt = Qt + AT_D * AT_LD;           // [D][LD]
-    float *Vs = Kt + AT_D * AT_LD;           // [S][D]
-    float *Pt = sm;                          // [S(key)][LD(query)], over Q^T/K^T after the scores
-    const int b = blockIdx.y, h = blockIdx.x, tid = threadIdx.x;
-    const int ld = 3 * H * AT_D;
-    const float *base = qkv + (size_t)b * S * ld + h * AT_D;
-    // load: thread -> (row, 4 consecutive d); rows past S are zero
-    for (int i = tid; i < AT_S * (AT_D / 4); i += 256) {
-        const int r = i / (AT_D / 4), d4 = (i % (AT_D / 4)) * 4;
-        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        const float4 q = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + d4) : z;
-        const float4 k = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + H * AT_D + d4) : z;
-        const float4 v = r < S ? *reinterpret_cast<const float4 *>(base + (size_t)r * ld + 2 * H * AT_D + d4) : z;
-        Qt[(d4 + 0) * AT_LD + r] = q.x * scale;
-        Qt[(d4 + 1) * AT_LD + r] = q.y * scale;
-        Qt[(d4 + 2) * AT_LD + r] = q.z * scale;
-        Qt[(d4 + 3) * AT_LD + r] = q.w * scale;
-        Kt[(d4 + 0) * AT_LD + r] = k.x;
-        Kt[(d4 + 1) * AT_LD + r] = k.y;
-        Kt[(d4 + 2) * AT_LD + r] = k.z;
-        Kt[(d4 + 3) * AT_LD + r] = k.w;
-        *reinterpret_cast<float4 *>(Vs + r * AT_D + d4) = v;
-    }
-    __syncthreads();
-
-    // S = Q K^T: thread (ty, tx) owns queries ty*4 + {0..3} and 64 + ty*4 + {0..3},
-    // keys tx*4 + {0..3} and 64 + tx*4 + {0..3}
-    const int tx = tid & 15, ty = tid >> 4;
-    float acc[8][8];
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-#pragma unroll 4
-    for (int d = 0; d < AT_D; d++) {
-        const float4 a0 = *reinterpret_cast<const float4 *>(Qt + d * AT_LD + ty * 4);
-        const float4 a1 = *reinterpret_cast<const float4 *>(Qt + d * AT_LD + 64 + ty * 4);
-        const float4 b0 = *reinterpret_cast<const float4 *>(Kt + d * AT_LD + tx * 4);
-        const float4 b1 = *reinterpret_cast<const float4 *>(Kt + d * AT_LD + 64 + tx * 4);
-        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-#pragma unroll
-            for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-    }
-    __syncthreads();  // every thread has read Q^T/K^T: P^T may overwrite them
-    // scores to P^T [key][query]
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int q = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int k = j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4);
-            Pt[k * AT_LD + q] = k < S ? acc[i][j] : -INFINITY;
-        }
-    }
-    __syncthreads();
-
-    // softmax over keys for each query (a column of P^T): warp w owns queries
-    // w, w + 8, ...; lane covers keys lane + 32 c
-    const int lane = tid & 31, warp = tid >> 5;
-    for (int q = warp; q < S; q += 8) {
-        float v[AT_S / 32];
-        float m = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < AT_S / 32; c++) {
-            v[c] = Pt[(lane + 32 * c) * AT_LD + q];
-            m = fmaxf(m, v[c]);
-        }
-        m = warp_max(m);
-        float sum = 0.0f;
-#pragma unroll
-        for (int c = 0; c < AT_S / 32; c++) {
-            v[c] = expf(v[c] - m);
-            sum += v[c];
-        }
-        sum = warp_sum(sum);
-#pragma unroll
-        for (int c = 0; c < AT_S / 32; c++) Pt[(lane + 32 * c) * AT_LD + q] = __fdiv_rn(v[c], sum);
-    }
-    __syncthreads();
-
-    // O = P V: thread owns queries ty*4 + {0..3}, 64 + ty*4 + {0..3} and dims tx*4 + {0..3}
-    float o[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) o[i][j] = 0.0f;
-#pragma unroll 4
-    for (int k = 0; k < AT_S; k++) {
-        const float4 p0 = *reinterpret_cast<const float4 *>(Pt + k * AT_LD + ty * 4);
-        const float4 p1 = *reinterpret_cast<const float4 *>(Pt + k * AT_LD + 64 + ty * 4);
-        const float4 vv = *reinterpret_cast<const float4 *>(Vs + k * AT_D + tx * 4);
-        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        const float vw[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) o[i][j] = fmaf(pv[i], vw[j], o[i][j]);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int q = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-        if (q >= S) continue;
-        const size_t off = ((size_t)b * S + q) * (H * AT_D) + h * AT_D + tx * 4;
-        if (qout)  // the following QUANTIZE, fused: the f32 context is not written
-            *reinterpret_cast<uint32_t *>(qout + off) =
-                (uint32_t)(uint8_t)requant_i8(o[i][0], qs) | ((uint32_t)(uint8_t)requant_i8(o[i][1], qs) << 8) |
-                ((uint32_t)(uint8_t)requant_i8(o[i][2], qs) << 16) | ((uint32_t)(uint8_t)requant_i8(o[i][3], qs) << 24);
-        else
-            *reinterpret_cast<float4 *>(out + off) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
     }
 }
 
@@ -442,19 +303,12 @@ int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const fl
     return after_launch(ctx, "layernorm");
 }
 
+int launch_attention_tc(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                        int8_t *q, float qs);
+
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
                      int8_t *q, float qs) {
-    if (D != AT_D || S <= 0 || S > AT_S || B <= 0 || H <= 0 || B > 65535 ||
-        (((uintptr_t)qkv | (uintptr_t)out) & 15) || ((uintptr_t)q & 3))
-        return TPT_UNSUPPORTED;
-    static bool attr[64] = {};
-    if (!attr[ctx->device & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
-        attr[ctx->device & 63] = true;
-    }
-    k_attention<<<dim3((unsigned)H, (unsigned)B), 256, AT_SMEM, ctx->stream>>>(qkv, out, S, H, scale, q, qs);
-    return after_launch(ctx, "attention");
+    return launch_attention_tc(ctx, qkv, out, B, S, H, D, scale, q, qs);
 }
 
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act) {

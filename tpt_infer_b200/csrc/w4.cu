@@ -111,7 +111,10 @@ __global__ void __launch_bounds__(256) k_w4_gemv(const float *__restrict__ X, co
 // 8 independent 16-byte loads per lane in flight, each nibble decoded with
 // one LOP3 + FADD (the bits (u ^ 8) | 0x4B000000 are exactly 2^23 + v + 8), one
 // FFMA per activation row; warp sums go through shared memory and are added in
-// warp order, so the result does not depend on the launch shape.
+// warp order, so the result does not depend on the launch shape. The grid is a
+// few blocks per SM, each streaming a run of row groups with the next group's
+// loads issued before the current group's arithmetic (a two-deep register
+// pipeline), so the nibble stream and the decode overlap.
 constexpr int W4V_ROWS = 8;
 template <int MM>
 __global__ void __launch_bounds__(256) k_w4_gemv2(const float *__restrict__ X, const uint8_t *__restrict__ Wp,
@@ -142,18 +145,24 @@ __global__ void __launch_bounds__(256) k_w4_gemv2(const float *__restrict__ X, c
 #pragma unroll
         for (int j = 0; j < 32; j++) asm volatile("" : "+f"(xr[i][j]));
     const int groups = (N + W4V_ROWS - 1) / W4V_ROWS;
-    for (int gi = blockIdx.x; gi < groups; gi += gridDim.x) {
-        const int n0 = gi * W4V_ROWS;
-        uint4 w[W4V_ROWS];
+    auto load_group = [&](int g, uint4 (&dst)[W4V_ROWS]) {
 #pragma unroll
         for (int r = 0; r < W4V_ROWS; r++) {
-            const int n = n0 + r < N ? n0 + r : N - 1;
-            w[r] = __ldcs(reinterpret_cast<const uint4 *>(Wp + (size_t)n * row_bytes + (kbase >> 1)));
+            const int n = g * W4V_ROWS + r < N ? g * W4V_ROWS + r : N - 1;
+            dst[r] = __ldcs(reinterpret_cast<const uint4 *>(Wp + (size_t)n * row_bytes + (kbase >> 1)));
         }
-        // all eight loads are issued before the first decode (the compiler would
+        // all eight loads are issued before any use (the compiler would
         // otherwise interleave them with the arithmetic, one load in flight)
 #pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++) asm volatile("" ::"r"(w[r].x), "r"(w[r].y), "r"(w[r].z), "r"(w[r].w));
+        for (int r = 0; r < W4V_ROWS; r++)
+            asm volatile("" : "+r"(dst[r].x), "+r"(dst[r].y), "+r"(dst[r].z), "+r"(dst[r].w));
+    };
+    uint4 w[W4V_ROWS];
+    if ((int)blockIdx.x < groups) load_group(blockIdx.x, w);
+    for (int gi = blockIdx.x; gi < groups; gi += gridDim.x) {
+        const int n0 = gi * W4V_ROWS;
+        uint4 wn[W4V_ROWS];
+        if (gi + (int)gridDim.x < groups) load_group(gi + gridDim.x, wn);
         float acc[MM][W4V_ROWS];
 #pragma unroll
         for (int r = 0; r < W4V_ROWS; r++) {
@@ -199,6 +208,8 @@ __global__ void __launch_bounds__(256) k_w4_gemv2(const float *__restrict__ X, c
             }
         }
         __syncthreads();
+#pragma unroll
+        for (int r = 0; r < W4V_ROWS; r++) w[r] = wn[r];
     }
 }
 
@@ -218,7 +229,8 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
     if (m <= 2 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)p & 15) == 0 && k % 1024 == 0 && k <= 8192) {
         const int kw = (int)(k / 1024);
         const size_t groups = (n + W4V_ROWS - 1) / W4V_ROWS;
-        const unsigned g = (unsigned)(groups < (size_t)ctx->sm_count * 8 ? groups : (size_t)ctx->sm_count * 8);
+        const size_t per_sm = m == 1 ? 3 : 2;  // blocks that fit one SM at the kernel's register count
+        const unsigned g = (unsigned)(groups < (size_t)ctx->sm_count * per_sm ? groups : (size_t)ctx->sm_count * per_sm);
         if (m == 1)
             k_w4_gemv2<1><<<g, 32 * kw, 0, ctx->stream>>>(x, p, w->scales, bias, (int)m, (int)n, (int)k, act, y);
         else
