@@ -1,0 +1,70 @@
+"""The implicit-GEMM INT8 convolution (IM2COL -> LINEAR fused inside a plan).
+
+A plan runs QUANTIZE (static scale) -> IM2COL -> LINEAR_W8A8 (+bias, act)
+[-> QUANTIZE]. Fetching only the conv output lets the plan replace the two ops
+by one implicit-GEMM launch; fetching the im2col rows as well forces the
+separate im2col + GEMM. Both must equal the oracle (its im2col restatement
+and W8A8 GEMM) bit for bit, f32 and requantized int8 outputs alike, over
+ragged shapes, strides, padding, 1x1 kernels and output-channel counts that
+are not tile multiples.
+"""
+import numpy as np
+import pytest
+
+from oracle import models as OM
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CASES = [  # N, H, W, C, OC, k, stride, pad
+    (3, 13, 11, 32, 48, 3, 1, 1),
+    (2, 9, 9, 64, 64, 3, 2, 1),
+    (2, 16, 16, 16, 200, 1, 2, 0),
+    (1, 7, 7, 128, 512, 3, 1, 1),
+    (2, 10, 12, 64, 130, 3, 1, 1),
+    (4, 20, 20, 64, 64, 3, 1, 1),
+]
+
+
+@pytest.mark.parametrize("N,H,W,C,OC,k,s,pad", CASES)
+@pytest.mark.parametrize("requant", [False, True])
+def test_conv_implicit_gemm_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requant):
+    from tpt_infer_b200 import graphs
+
+    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    M, K = N * OH * OW, k * k * C
+    seed = 7000 + N * 131 + C + OC + k
+    x = O.normal(N * H * W * C, seed)
+    sx = np.float32(O.sym_scale(O.absmax(x)))
+    wq, ws = O.quantize_i8_symmetric_per_channel(O.normal(OC * K, seed + 1, 0.0, 0.05), OC)
+    bias = O.normal(OC, seed + 2, 0.0, 0.1)
+    p = graphs.Plan(cuda)
+    w = cuda.upload_i8(wq, ws, OC, K)
+    p.weights.append(w)
+    tx, txq = p.tensor(graphs.F32, x.size), p.tensor(graphs.I8, x.size)
+    col, ty = p.tensor(graphs.I8, M * K), p.tensor(graphs.F32, M * OC)
+    p.op(graphs.OP_QUANTIZE, tx, txq, f0=float(sx), dims=(x.size,))
+    p.op(graphs.OP_IM2COL, txq, col, dims=(N, H, W, C, k, k, s, s, pad, pad, OH, OW, K))
+    p.op(graphs.OP_LINEAR, col, ty, in1=p.const(bias), w=w, act=graphs.ACT_RELU, dims=(M,))
+    sy = np.float32(0.05)
+    if requant:
+        tyq = p.tensor(graphs.I8, M * OC)
+        p.op(graphs.OP_QUANTIZE, ty, tyq, f0=float(sy), dims=(M * OC,))
+    p.finalize()
+
+    xq = O.quantize_i8_static(x, sx).reshape(N, H, W, C)
+    col_o, _, _ = OM._im2col(xq, k, s, pad, K)
+    want = O.w8a8_gemm(col_o, wq, M, OC, K, sx, ws, bias, O.ACT_RELU, threads=8)
+    if requant:
+        want_q = O.quantize_i8_static(want, sy)
+        fused = p.run({tx: x}, [tyq])[0]                    # implicit GEMM with the requantizing epilogue
+        split = p.run({tx: x}, [col, tyq])[1]               # im2col rows fetched: separate ops
+        for got in (fused, split):
+            assert np.array_equal(np.frombuffer(got.tobytes()[:M * OC], np.int8), want_q)
+    else:
+        fused = p.run({tx: x}, [ty])[0]
+        got_col, split = p.run({tx: x}, [col, ty])
+        assert np.array_equal(np.frombuffer(got_col.tobytes()[:M * K], np.int8), col_o.ravel())
+        assert np.array_equal(fused, want)
+        assert np.array_equal(split, want)
+    p.close()

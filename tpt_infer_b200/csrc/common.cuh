@@ -187,6 +187,62 @@ __device__ __forceinline__ float apply_act(float y, int act) {
     return y;
 }
 
+template <int ACT>
+__device__ __forceinline__ float act_t(float y) {
+    if constexpr (ACT == TPT_ACT_RELU) return y > 0.0f ? y : 0.0f;
+    else if constexpr (ACT == TPT_ACT_GELU) return gelu_ref(y);
+    else return y;
+}
+
+// The W8A8 epilogue of one 32-column chunk of one row, in place: i32
+// accumulators of columns n0 .. n0+31 become the f32 bits of
+// act((float)acc * (a_scale * ws[n]) + bias[n]) (the product of the scales
+// first, separately rounded multiply and add). Every lane of a warp passes the
+// same n0: the 32 channel scales and biases are broadcast loads, 128-bit when
+// aligned and in range.
+template <int ACT>
+__device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
+                                           const float *bias) {
+    float sc[32], bi[32];
+    if (n0 + 32 <= N && ((reinterpret_cast<uintptr_t>(ws + n0) | reinterpret_cast<uintptr_t>(bias + n0)) & 15) == 0) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(ws + n0) + c);
+            sc[4 * c] = w4.x;
+            sc[4 * c + 1] = w4.y;
+            sc[4 * c + 2] = w4.z;
+            sc[4 * c + 3] = w4.w;
+            const float4 b4 = bias ? __ldg(reinterpret_cast<const float4 *>(bias + n0) + c) : make_float4(0, 0, 0, 0);
+            bi[4 * c] = b4.x;
+            bi[4 * c + 1] = b4.y;
+            bi[4 * c + 2] = b4.z;
+            bi[4 * c + 3] = b4.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int n = n0 + j < N ? n0 + j : N - 1;
+            sc[j] = __ldg(ws + n);
+            bi[j] = bias ? __ldg(bias + n) : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+        float y = __fmul_rn(__int2float_rn((int)v[j]), __fmul_rn(a_scale, sc[j]));
+        if (bias) y = __fadd_rn(y, bi[j]);
+        v[j] = __float_as_uint(act_t<ACT>(y));
+    }
+}
+__device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
+                                           const float *bias, int act) {
+    if (act == TPT_ACT_RELU)
+        w8a8_epi32<TPT_ACT_RELU>(v, n0, N, a_scale, ws, bias);
+    else if (act == TPT_ACT_GELU)
+        w8a8_epi32<TPT_ACT_GELU>(v, n0, N, a_scale, ws, bias);
+    else
+        w8a8_epi32<TPT_ACT_NONE>(v, n0, N, a_scale, ws, bias);
+}
+
 // Rust `f32::round(v).clamp(lo, hi) as i8`: half away from zero (roundf),
 // NaN -> 0 (saturating cast).
 __device__ __forceinline__ int8_t round_clamp_i8(float v, float lo, float hi) {

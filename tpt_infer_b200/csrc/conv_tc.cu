@@ -1,0 +1,433 @@
+// conv_tc.cu -- INT8 convolution of an NHWC tensor as an implicit GEMM on the
+// tcgen05 tensor cores (kind::i8, i32 accumulators in tensor memory).
+//
+// The same arithmetic as im2col followed by the W8A8 GEMM (the reference's
+// Conv2d, crates/tpt-infer-ops/src/naive.rs:36-83, on quantized operands, with
+// the per-channel epilogue of quantized_matmul_i8, crates/tpt-infer-quantize/
+// src/ptq.rs:293-324): GEMM row m = output pixel (n, oy, ox), column k =
+// (ky, kx, c) of the tap-major, channel-minor weight rows Wt [OC, Kw],
+//   acc[m, oc] = sum_k x[n, oy*sh - ph + ky, ox*sw - pw + kx, c] * Wt[oc, k]
+// with taps outside the image (and k >= KH*KW*C) contributing zero, then
+//   y = (float)acc * (a_scale * w_scale[oc]) + bias[oc], act, and optionally
+// the int8 requantization of the next quantization point. The rows of the
+// im2col matrix are gathered straight from the activation tensor into shared
+// memory instead of being written to and read back from HBM.
+//
+// Tile: 128 output pixels (MMA M) x BN = 64/128/256 output channels (MMA N),
+// 128-byte k-blocks (one 3x3 tap of 128 channels, two taps of 64, ..., 32
+// taps of the 4-channel stem). The gather moves VB-byte chunks, VB = 16 when
+// C % 16 == 0 and 4 when C % 4 == 0, so a chunk never straddles two taps.
+// Roles (320 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA: weight tile [BN rows x 128 B], 128B-swizzled
+//   warp 1      TMEM allocation; one lane issues tcgen05.mma (M=128, N=BN,
+//               K=32) and the commits
+//   warps 2..5  epilogue, thread = output pixel (TMEM lane); f32 rows through
+//               a swizzled staging tile and bulk-tensor stores, or int8 rows
+//   warps 6..9  gather: at each tile the 128 rows' first input pixel goes to a
+//               shared table; lane = (chunk of the k-block, pixel row);
+//               cp.async with zero fill for padding taps, S - 2 k-blocks in
+//               flight per thread; a warp arrives on the stage's barrier
+//               after its copies landed and were fenced for the tensor core
+// Every wait is bounded (about 1 s); a timeout raises the CTA abort and the
+// device timeout flag.
+#include "tc_common.cuh"
+
+namespace tpt {
+
+bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uint64_t rows, uint64_t cols,
+                  uint32_t elem_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
+
+namespace {
+using namespace tc;
+
+constexpr int CV_BM = 128;                  // output pixels per tile (MMA M)
+constexpr int CV_BK = 128;                  // k bytes per stage
+constexpr int CV_THREADS = 320;
+constexpr int CV_A_BYTES = CV_BM * CV_BK;   // 16 KB
+constexpr int CV_OUT_BYTES = 4 * 2 * 4096;  // epilogue staging: 4 warps x 2 buffers of 32 x 32 f32
+
+struct ConvShape {
+    int N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW;
+    int K;  // KH*KW*C: columns past it are zero
+    int Kw; // the weight rows' length (>= K)
+};
+
+template <int BN>
+struct ConvCfg {
+    static constexpr int B_BYTES = BN * CV_BK;
+    static constexpr int STAGE_BYTES = CV_A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 64 ? 8 : BN == 128 ? 6 : 4;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + CV_OUT_BYTES + (2 * STAGES + 5) * 8 + 1024;
+    static_assert(SMEM_BYTES + 3 * CV_BM * 4 + 16 <= 232448, "shared memory (dynamic + the static gather table)");
+    static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
+};
+
+template <int VB>
+__device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void *src, bool valid) {
+    if constexpr (VB == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                     : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0)
+                     : "memory");
+}
+// waits until at most n (0..7) of this thread's cp.async groups are pending
+__device__ __forceinline__ void cp_async_wait_upto(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+    }
+}
+
+template <int BN, int VB>
+__global__ void __launch_bounds__(CV_THREADS, 1)
+    k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmY, int tma_store,
+                const int8_t *__restrict__ X, ConvShape cs, int OC, float a_scale, const float *__restrict__ wscale,
+                const float *__restrict__ bias, int act, float *__restrict__ Y, int8_t *__restrict__ Q,
+                float q_scale, unsigned *gflags) {
+    using Cfg = ConvCfg<BN>;
+    constexpr int S = Cfg::STAGES;
+    constexpr int INFLIGHT = S - 2;  // k-blocks a gather thread keeps in flight
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int abort_flag;
+    __shared__ uint32_t tmem_slot;
+    // gather table of the tile: image offset, first input row / column of each pixel
+    __shared__ int row_base[CV_BM], row_iy[CV_BM], row_ix[CV_BM];
+
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t ring = (raw + 1023u) & ~1023u;
+    const uint32_t staging = ring + S * Cfg::STAGE_BYTES;
+    const uint32_t bars = staging + CV_OUT_BYTES;
+    auto a_s = [&](int s) { return ring + (uint32_t)(s * Cfg::STAGE_BYTES); };
+    auto b_s = [&](int s) { return a_s(s) + (uint32_t)CV_A_BYTES; };
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+    auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
+    auto tempty_bar = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
+    const uint32_t drain_bar = bars + 8u * (2 * S + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = cs.N * cs.OH * cs.OW;
+    const int tiles_n = (OC + BN - 1) / BN;
+    const int ntiles = ((M + CV_BM - 1) / CV_BM) * tiles_n;
+    const int kblocks = (cs.Kw + CV_BK - 1) / CV_BK;
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1 + 4);  // the weight TMA + the 4 gather warps
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 4);
+        }
+        mbar_init(drain_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)Cfg::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int *abort_p = &abort_flag;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- weight TMA ----------------
+            int stage = 0;
+            uint32_t phase = 0, issued_mask = 0, last_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int nt = t % tiles_n;
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), Cfg::B_BYTES);
+                    tma_load_2d(b_s(stage), &tmW, full_bar(stage), kb * CV_BK, nt * BN);
+                    issued_mask |= 1u << stage;
+                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // our own copies in flight land before the CTA can exit (the
+            // stage's barrier also waits for the gather warps)
+            for (int s = 0; s < S; s++)
+                if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (last_phase >> s) & 1u, abort_p, gflags, false);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                       ((uint32_t)(CV_BM >> 4) << 24);
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_p, gflags, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < CV_BK / 32; kk++)
+                        tc_mma_i8(d_tmem, sw128_desc(a_s(stage) + 32 * kk), sw128_desc(b_s(stage) + 32 * kk), idesc,
+                                  (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(empty_bar(stage));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(tfull_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_p, gflags, false);
+        }
+    } else if (warp >= 6) {
+        // ---------------- gather ----------------
+        // VB = 16: lane = (chunk j of 8, row r of a 4-row group), 8 rows per thread;
+        // VB = 4:  lane = chunk j of 32, one row per warp step, 32 rows per thread
+        constexpr int CPR = CV_BK / VB;               // chunks per row
+        constexpr int RPW = 32 / CPR;                 // rows a warp covers per step
+        constexpr int STEPS = CV_BM / (4 * RPW);      // steps per k-block
+        const int gt = threadIdx.x - 192, gw = gt >> 5, j = lane % CPR, rr = lane / CPR;
+        const int HWo = cs.OH * cs.OW;
+        int stage = 0;
+        uint32_t phase = 0;
+        int pend_stage[S] = {};  // stages whose copies are in flight, oldest first
+        int npend = 0;
+        bool ok = true;
+        auto retire = [&](int keep) {
+            // this thread's copies of the oldest stage landed: fence them for the
+            // tensor core, and the warp arrives once for the stage
+            cp_async_wait_upto(keep);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_bar(pend_stage[0]));
+            for (int i = 0; i < npend - 1; i++) pend_stage[i] = pend_stage[i + 1];
+            npend--;
+        };
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            const int mt = t / tiles_n;
+            // the 4 gather warps stop together (they share the named barriers), and
+            // every gather thread is done reading the previous tile's table
+            if (!bar_and(1, 128, ok)) break;
+            {
+                const int m = mt * CV_BM + gt;
+                if (m < M) {
+                    const int n = m / HWo, rem = m - n * HWo, oy = rem / cs.OW, ox = rem - oy * cs.OW;
+                    row_base[gt] = n * cs.H * cs.W * cs.C;
+                    row_iy[gt] = oy * cs.sh - cs.ph;
+                    row_ix[gt] = ox * cs.sw - cs.pw;
+                } else {
+                    row_base[gt] = 0;
+                    row_iy[gt] = -(1 << 28);  // every tap outside: zeros
+                    row_ix[gt] = 0;
+                }
+            }
+            bar_sync(1, 128);
+            for (int kb = 0; kb < kblocks; kb++) {
+                if (!ok) continue;  // stopped: issue nothing more, meet the others at the next tile
+                int okw = 1;
+                if (lane == 0) okw = mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true) ? 1 : 0;
+                okw = __shfl_sync(0xffffffffu, okw, 0);
+                if (!okw) {
+                    ok = false;
+                    continue;
+                }
+                const int k = kb * CV_BK + j * VB;
+                const bool kin = k < cs.K;
+                const int tap = kin ? k / cs.C : 0, c = kin ? k - tap * cs.C : 0;
+                const int ky = tap / cs.KW, kx = tap - ky * cs.KW;
+                const uint32_t chunk_off = (uint32_t)(((j * VB) >> 4) << 4), in16 = (uint32_t)((j * VB) & 15);
+#pragma unroll 8
+                for (int i = 0; i < STEPS; i++) {
+                    const int ml = (i * 4 + gw) * RPW + rr;
+                    const int iy = row_iy[ml] + ky, ix = row_ix[ml] + kx;
+                    const bool v = kin && iy >= 0 && iy < cs.H && ix >= 0 && ix < cs.W;
+                    const int8_t *src = v ? X + row_base[ml] + (iy * cs.W + ix) * cs.C + c : X;
+                    cp_async_zfill<VB>(a_s(stage) + (uint32_t)(ml * 128) + ((chunk_off ^ ((ml & 7) << 4))) + in16,
+                                       src, v);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                pend_stage[npend++] = stage;
+                if (npend > INFLIGHT) retire(INFLIGHT);
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        while (npend > 0) retire(npend - 1);
+    } else {
+        // ---------------- epilogue (warps 2..5): thread = output pixel ----------------
+        const int q = warp & 3;  // TMEM lane quarter
+        const int e = warp - 2;
+        const uint32_t stage_s = staging + (uint32_t)(e * 8192);
+        uint8_t *stage_g = smem_raw + (stage_s - raw);
+        int buf = 0, acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            int okw = 0;
+            if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
+            okw = __shfl_sync(0xffffffffu, okw, 0);
+            if (!okw) break;
+            tc_fence_after();
+            const int mt = t / tiles_n, nt = t - mt * tiles_n;
+            const int mrow0 = mt * CV_BM + q * 32, m = mrow0 + lane;
+            const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; cc++) {
+                const int n0 = nt * BN + cc * 32;
+                if (n0 >= OC) break;
+                uint32_t v[32];
+                tmem_ld32(t_base + (uint32_t)(cc * 32), v);
+                tmem_wait_ld();
+                w8a8_epi32(v, n0, OC, a_scale, wscale, bias, act);
+                if (Q) {
+                    if (m < M) {
+                        uint32_t b[8];
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj += 4)
+                            b[jj / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj]), q_scale) |
+                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 1]), q_scale) << 8) |
+                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 2]), q_scale) << 16) |
+                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 3]), q_scale) << 24);
+                        int8_t *dst = Q + (size_t)m * OC + n0;
+                        if (n0 + 32 <= OC && (OC & 15) == 0) {
+                            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
+                            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(b[4], b[5], b[6], b[7]);
+                        } else {
+                            for (int jj = 0; jj < 32; jj++)
+                                if (n0 + jj < OC) dst[jj] = (int8_t)(b[jj / 4] >> (8 * (jj % 4)));
+                        }
+                    }
+                } else if (tma_store) {
+                    if (mrow0 < M) {  // a block entirely below the last row is not stored
+                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                        __syncwarp();
+                        uint8_t *sb = stage_g + buf * 4096 + lane * 128;
+#pragma unroll
+                        for (int c4 = 0; c4 < 8; c4++)
+                            *reinterpret_cast<uint4 *>(sb + ((c4 ^ (lane & 7)) << 4)) =
+                                make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mrow0);
+                            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        }
+                        buf ^= 1;
+                    }
+                } else if (m < M) {
+                    float *dst = Y + (size_t)m * OC + n0;
+                    for (int jj = 0; jj < 32; jj++)
+                        if (n0 + jj < OC) dst[jj] = __uint_as_float(v[jj]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)Cfg::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <int BN, int VB>
+int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const tpt_cuda_weights *w, float a_scale,
+                const float *bias, int act, float *y, Requant rq) {
+    using Cfg = ConvCfg<BN>;
+    static bool attr_done[64] = {};
+    auto kfn = k_conv_w8a8<BN, VB>;
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "conv smem attribute");
+        attr_done[dev] = true;
+    }
+    const int OC = (int)w->n;
+    CUtensorMap tw, ty;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->n, w->k, 1, CV_BK, BN,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+        return TPT_UNSUPPORTED;
+    const long long M = (long long)cs.N * cs.OH * cs.OW;
+    const bool tma_store = !rq.q && make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, (uint64_t)M, (uint64_t)OC, 4,
+                                                 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    const long long ntiles = ((M + CV_BM - 1) / CV_BM) * ((OC + BN - 1) / BN);
+    const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);
+    kfn<<<grid, CV_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(tw, tma_store ? ty : tw, tma_store ? 1 : 0, x, cs, OC,
+                                                           a_scale, w->scales, bias, act, y, rq.q, rq.scale,
+                                                           ctx->d_flags);
+    return after_launch(ctx, "conv_w8a8");
+}
+
+}  // namespace
+
+// INT8 NHWC convolution as an implicit GEMM. Needs C % 4 == 0, a 16-byte
+// aligned input, int8 weights [OC, Kw] with Kw >= KH*KW*C and a tensor map
+// (Kw % 16 == 0); returns *handled = false otherwise (the caller runs im2col +
+// GEMM instead).
+int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
+                     int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
+                     int act, float *y, bool *handled, Requant rq) {
+    *handled = false;
+    if (w->kind != 8 || !w->tmap_ok || C % 4 != 0 || ((uintptr_t)x & 15) || w->k < (size_t)KH * KW * C ||
+        w->n > 0x7fffffff || w->k > 0x7fffffff || (!rq.q && ((uintptr_t)y & 15)))
+        return TPT_OK;
+    const long long M = (long long)N * OH * OW, xin = (long long)N * H * W * C;
+    if (M <= 0 || M > 0x7fffffffLL || xin > 0x7fffffffLL) return TPT_OK;  // 32-bit pixel offsets
+    ConvShape cs{N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, KH * KW * C, (int)w->k};
+    *handled = true;
+    const size_t oc = w->n;
+    if (C % 16 == 0) {
+        if (oc <= 64) return launch_conv<64, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+        if (oc <= 128) return launch_conv<128, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+        return launch_conv<256, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+    }
+    if (oc <= 64) return launch_conv<64, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+    if (oc <= 128) return launch_conv<128, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+    return launch_conv<256, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+}
+
+}  // namespace tpt

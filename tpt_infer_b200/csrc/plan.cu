@@ -39,6 +39,9 @@ int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, 
 int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell);
 int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int P, size_t T, int C);
 int comm_all_gather(tpt_cuda_comm *c, const void *in, void *out, size_t bytes_per_rank);
+int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
+                     int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
+                     int act, float *y, bool *handled, Requant rq);
 int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
 }  // namespace tpt
 
@@ -412,6 +415,44 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
     for (size_t i = 0; i < p->ops.size(); i++) {
         PlanOp &po = p->ops[i];
         const tpt_plan_op &o = po.op;
+        // IM2COL -> LINEAR_W8A8 of its rows (read by no other op, not fetched):
+        // one implicit-GEMM convolution launch gathers the rows from the NHWC
+        // tensor instead of writing and re-reading them; a QUANTIZE of the f32
+        // result folds into its epilogue as for a plain LINEAR.
+        if (o.kind == TPT_OP_IM2COL && i + 1 < p->ops.size()) {
+            const tpt_plan_op &l = p->ops[i + 1].op;
+            const PlanTensor &col = p->tensors[o.out];
+            if (l.kind == TPT_OP_LINEAR_W8A8 && l.in0 == o.out && col.readers == 1 &&
+                !is_output(out_ids, n_out, o.out)) {
+                const float sa = p->tensors[o.in0].scale;
+                p->tensors[o.out].scale = sa;
+                Requant rq;
+                size_t fused = 1;
+                if (!p->calibrating && i + 2 < p->ops.size()) {
+                    PlanOp &nq = p->ops[i + 2];
+                    const tpt_plan_op &q = nq.op;
+                    const PlanTensor &t = p->tensors[l.out];
+                    if (q.kind == TPT_OP_QUANTIZE && q.in0 == l.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                        t.readers == 1 && q.dims[0] == t.numel && !is_output(out_ids, n_out, l.out)) {
+                        rq.q = Q(p, q.out);
+                        rq.scale = nq.frozen;
+                        fused = 2;
+                    }
+                }
+                const size_t *d = o.dims;
+                bool handled = false;
+                int st = launch_conv_w8a8(p->ctx, Q(p, o.in0), (int)d[0], (int)d[1], (int)d[2], (int)d[3], (int)d[4],
+                                          (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10],
+                                          (int)d[11], l.w, sa, F(p, l.in1), l.act, rq.q ? nullptr : F(p, l.out),
+                                          &handled, rq);
+                if (st) return st;
+                if (handled) {
+                    if (rq.q) p->tensors[p->ops[i + 2].op.out].scale = rq.scale;
+                    i += fused;
+                    continue;
+                }
+            }
+        }
         if (!p->calibrating && o.kind == TPT_OP_LINEAR_W8A8 && i + 1 < p->ops.size()) {
             PlanOp &nq = p->ops[i + 1];
             const tpt_plan_op &q = nq.op;

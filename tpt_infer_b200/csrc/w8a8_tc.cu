@@ -239,17 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
                 const int n0 = nt * BN + half * (BN / 2) + c * 32;
-                if (!ACC_OUT) {
-                    const int nc = n0 + lane < N ? n0 + lane : N - 1;
-                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nc));
-                    const float bi = bias ? __ldg(bias + nc) : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        float y = __fmul_rn(__int2float_rn((int)v[j]), __shfl_sync(0xffffffffu, sc, j));
-                        if (bias) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bi, j));
-                        v[j] = __float_as_uint(apply_act(y, act));
-                    }
-                }
+                if (!ACC_OUT) w8a8_epi32(v, n0, N, a_scale, wscale, bias, act);
                 if (!ACC_OUT && Q) {
                     // int8 output requantized with the next point's scale: this
                     // lane's row gets 32 consecutive bytes
