@@ -6,7 +6,8 @@ by one implicit-GEMM launch; fetching the im2col rows as well forces the
 separate im2col + GEMM. Both must equal the oracle (its im2col restatement
 and W8A8 GEMM) bit for bit, f32 and requantized int8 outputs alike, over
 ragged shapes, strides, padding, 1x1 kernels and output-channel counts that
-are not tile multiples.
+are not tile multiples, in both ways of loading the activation tiles (cp.async
+gathers for small inputs, TMA im2col for inputs of 128 KB and more).
 """
 import numpy as np
 import pytest
@@ -23,6 +24,12 @@ CASES = [  # N, H, W, C, OC, k, stride, pad
     (1, 7, 7, 128, 512, 3, 1, 1),
     (2, 10, 12, 64, 130, 3, 1, 1),
     (4, 20, 20, 64, 64, 3, 1, 1),
+    # inputs of 128 KB and more: the activation tiles come from TMA im2col loads
+    (2, 40, 40, 64, 64, 3, 1, 1),
+    (2, 32, 32, 128, 128, 3, 2, 1),
+    (3, 24, 24, 128, 256, 1, 2, 0),
+    (3, 30, 26, 64, 130, 3, 1, 1),
+    (1, 20, 20, 512, 512, 3, 1, 1),
 ]
 
 

@@ -13,17 +13,24 @@
 // im2col matrix are gathered straight from the activation tensor into shared
 // memory instead of being written to and read back from HBM.
 //
-// Tile: 128 output pixels (MMA M) x BN = 64/128/256 output channels (MMA N),
-// 128-byte k-blocks (one 3x3 tap of 128 channels, two taps of 64, ..., 32
-// taps of the 4-channel stem). The gather moves VB-byte chunks, VB = 16 when
-// C % 16 == 0 and 4 when C % 4 == 0, so a chunk never straddles two taps.
-// Roles (320 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA: weight tile [BN rows x 128 B], 128B-swizzled
+// Tile: 128 output pixels (MMA M) x BN = 64/128/256 output channels (MMA N).
+// Two ways to fill the activation operand:
+//  - TMA im2col (C % 64 == 0, input >= 128 KB): the tensor unit walks the 128
+//    output pixels' windows itself (cp.async.bulk.tensor.4d ... .im2col: the
+//    window starts of the tile's first pixel, the tap as the im2col offset,
+//    padding read as zeros from outside the tensor's bounding box). A k-block
+//    is one tap x KB channels, KB = 128 (128B swizzle) or 64 (C == 64, 64B
+//    swizzle, two MMA k-steps).
+//  - gather (otherwise, e.g. the 4-channel stem): 128-byte k-blocks (two taps
+//    of 64 channels, ..., 32 taps of 4), VB-byte cp.async chunks, VB = 16 when
+//    C % 16 == 0 and 4 when C % 4 == 0, so a chunk never straddles two taps.
+// Roles (one CTA per SM, persistent over tiles):
+//   warp 0      TMA: weight tile [BN rows x KB B] (and the im2col tile)
 //   warp 1      TMEM allocation; one lane issues tcgen05.mma (M=128, N=BN,
 //               K=32) and the commits
 //   warps 2..5  epilogue, thread = output pixel (TMEM lane); f32 rows through
 //               a swizzled staging tile and bulk-tensor stores, or int8 rows
-//   warps 6..9  gather: at each tile the 128 rows' first input pixel goes to a
+//   warps 6..9  (gather mode) at each tile the 128 rows' first input pixel goes to a
 //               shared table; lane = (chunk of the k-block, pixel row);
 //               cp.async with zero fill for padding taps, S - 2 k-blocks in
 //               flight per thread; a warp arrives on the stage's barrier
@@ -41,10 +48,13 @@ namespace {
 using namespace tc;
 
 constexpr int CV_BM = 128;                  // output pixels per tile (MMA M)
-constexpr int CV_BK = 128;                  // k bytes per stage
-constexpr int CV_THREADS = 320;
-constexpr int CV_A_BYTES = CV_BM * CV_BK;   // 16 KB
 constexpr int CV_OUT_BYTES = 4 * 2 * 4096;  // epilogue staging: 4 warps x 2 buffers of 32 x 32 f32
+// activation operand modes: gather with 16- or 4-byte chunks (128-byte
+// k-blocks), TMA im2col with 128- or 64-byte k-blocks
+enum { CV_GATHER16 = 0, CV_GATHER4 = 1, CV_IM2COL128 = 2, CV_IM2COL64 = 3 };
+__host__ __device__ constexpr bool cv_tma(int mode) { return mode >= CV_IM2COL128; }
+__host__ __device__ constexpr int cv_kb(int mode) { return mode == CV_IM2COL64 ? 64 : 128; }
+__host__ __device__ constexpr int cv_threads(int mode) { return cv_tma(mode) ? 192 : 320; }
 
 struct ConvShape {
     int N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW;
@@ -52,16 +62,50 @@ struct ConvShape {
     int Kw; // the weight rows' length (>= K)
 };
 
-template <int BN>
+template <int BN, int MODE>
 struct ConvCfg {
-    static constexpr int B_BYTES = BN * CV_BK;
-    static constexpr int STAGE_BYTES = CV_A_BYTES + B_BYTES;
-    static constexpr int STAGES = BN == 64 ? 8 : BN == 128 ? 6 : 4;
+    static constexpr int KB = cv_kb(MODE);  // k bytes per stage
+    static constexpr int A_BYTES = CV_BM * KB;
+    static constexpr int B_BYTES = BN * KB;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_FIT = (232448 - CV_OUT_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + CV_OUT_BYTES + (2 * STAGES + 5) * 8 + 1024;
     static_assert(SMEM_BYTES + 3 * CV_BM * 4 + 16 <= 232448, "shared memory (dynamic + the static gather table)");
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
+    static_assert(STAGES >= 3, "stages");
 };
+
+// Shared-memory matrix descriptor of a K-major operand tile with 64-byte
+// rows, 64B swizzle (8-row groups 512 B apart)
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;  // swizzle mode: 64B
+    return d;
+}
+template <int KB>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+    if constexpr (KB == 64)
+        return sw64_desc(saddr);
+    else
+        return sw128_desc(saddr);
+}
+
+// 4-D im2col load: 128 window positions starting at {c, w, h, n} (input
+// coordinates of the first output pixel's window), tap offsets {ow, oh}
+__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int c, int w,
+                                                   int h, int n, uint16_t ow, uint16_t oh) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(ow), "h"(oh)
+        : "memory");
+}
 
 template <int VB>
 __device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void *src, bool valid) {
@@ -86,14 +130,18 @@ __device__ __forceinline__ void cp_async_wait_upto(int n) {
     }
 }
 
-template <int BN, int VB>
-__global__ void __launch_bounds__(CV_THREADS, 1)
-    k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmY, int tma_store,
+template <int BN, int MODE>
+__global__ void __launch_bounds__(cv_threads(MODE), 1)
+    k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                const __grid_constant__ CUtensorMap tmY, int tma_store,
                 const int8_t *__restrict__ X, ConvShape cs, int OC, float a_scale, const float *__restrict__ wscale,
                 const float *__restrict__ bias, int act, float *__restrict__ Y, int8_t *__restrict__ Q,
                 float q_scale, unsigned *gflags) {
-    using Cfg = ConvCfg<BN>;
+    using Cfg = ConvCfg<BN, MODE>;
     constexpr int S = Cfg::STAGES;
+    constexpr bool TMA_A = cv_tma(MODE);
+    constexpr int KB = Cfg::KB;
+    constexpr int VB = MODE == CV_GATHER4 ? 4 : 16;
     constexpr int INFLIGHT = S - 2;  // k-blocks a gather thread keeps in flight
     extern __shared__ uint8_t smem_raw[];
     __shared__ int abort_flag;
@@ -106,7 +154,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
     const uint32_t staging = ring + S * Cfg::STAGE_BYTES;
     const uint32_t bars = staging + CV_OUT_BYTES;
     auto a_s = [&](int s) { return ring + (uint32_t)(s * Cfg::STAGE_BYTES); };
-    auto b_s = [&](int s) { return a_s(s) + (uint32_t)CV_A_BYTES; };
+    auto b_s = [&](int s) { return a_s(s) + (uint32_t)Cfg::A_BYTES; };
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
@@ -117,12 +165,13 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
     const int M = cs.N * cs.OH * cs.OW;
     const int tiles_n = (OC + BN - 1) / BN;
     const int ntiles = ((M + CV_BM - 1) / CV_BM) * tiles_n;
-    const int kblocks = (cs.Kw + CV_BK - 1) / CV_BK;
+    const int kblocks = (cs.Kw + KB - 1) / KB;
+    const int HWo = cs.OH * cs.OW;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
         for (int s = 0; s < S; s++) {
-            mbar_init(full_bar(s), 1 + 4);  // the weight TMA + the 4 gather warps
+            mbar_init(full_bar(s), TMA_A ? 1 : 1 + 4);  // the TMA producer (+ the 4 gather warps)
             mbar_init(empty_bar(s), 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -132,6 +181,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
         mbar_init(drain_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+        if (TMA_A) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -147,19 +197,29 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- weight TMA ----------------
+            // ---------------- TMA: weight tile (and the im2col activation tile) ----------------
             int stage = 0;
             uint32_t phase = 0, issued_mask = 0, last_phase = 0;
             bool ok = true;
+            const int cblocks = TMA_A ? cs.C / KB : 1;  // k-blocks per tap
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int nt = t % tiles_n;
+                const int nt = t % tiles_n, m0 = (t / tiles_n) * CV_BM;
+                const int n0 = m0 / HWo, r0 = m0 - n0 * HWo, oy0 = r0 / cs.OW, ox0 = r0 - oy0 * cs.OW;
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_p, gflags, true)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_bar(stage), Cfg::B_BYTES);
-                    tma_load_2d(b_s(stage), &tmW, full_bar(stage), kb * CV_BK, nt * BN);
+                    if (TMA_A) {
+                        const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB;
+                        const int ky = tap / cs.KW, kx = tap - ky * cs.KW;
+                        mbar_arrive_expect_tx(full_bar(stage), Cfg::A_BYTES + Cfg::B_BYTES);
+                        tma_load_im2col_4d(a_s(stage), &tmX, full_bar(stage), c0, ox0 * cs.sw - cs.pw,
+                                           oy0 * cs.sh - cs.ph, n0, (uint16_t)kx, (uint16_t)ky);
+                    } else {
+                        mbar_arrive_expect_tx(full_bar(stage), Cfg::B_BYTES);
+                    }
+                    tma_load_2d(b_s(stage), &tmW, full_bar(stage), kb * KB, nt * BN);
                     issued_mask |= 1u << stage;
                     last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -192,9 +252,9 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
                     }
                     tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < CV_BK / 32; kk++)
-                        tc_mma_i8(d_tmem, sw128_desc(a_s(stage) + 32 * kk), sw128_desc(b_s(stage) + 32 * kk), idesc,
-                                  (kb | kk) != 0 ? 1u : 0u);
+                    for (int kk = 0; kk < KB / 32; kk++)
+                        tc_mma_i8(d_tmem, kmajor_desc<KB>(a_s(stage) + 32 * kk), kmajor_desc<KB>(b_s(stage) + 32 * kk),
+                                  idesc, (kb | kk) != 0 ? 1u : 0u);
                     tc_commit(empty_bar(stage));
                     if (++stage == S) {
                         stage = 0;
@@ -211,15 +271,14 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
             tc_commit(drain_bar);
             mbar_wait(drain_bar, 0, abort_p, gflags, false);
         }
-    } else if (warp >= 6) {
+    } else if (!TMA_A && warp >= 6) {
         // ---------------- gather ----------------
         // VB = 16: lane = (chunk j of 8, row r of a 4-row group), 8 rows per thread;
         // VB = 4:  lane = chunk j of 32, one row per warp step, 32 rows per thread
-        constexpr int CPR = CV_BK / VB;               // chunks per row
+        constexpr int CPR = 128 / VB;                 // chunks per row
         constexpr int RPW = 32 / CPR;                 // rows a warp covers per step
         constexpr int STEPS = CV_BM / (4 * RPW);      // steps per k-block
         const int gt = threadIdx.x - 192, gw = gt >> 5, j = lane % CPR, rr = lane / CPR;
-        const int HWo = cs.OH * cs.OW;
         int stage = 0;
         uint32_t phase = 0;
         int pend_stage[S] = {};  // stages whose copies are in flight, oldest first
@@ -263,7 +322,7 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
                     ok = false;
                     continue;
                 }
-                const int k = kb * CV_BK + j * VB;
+                const int k = kb * 128 + j * VB;
                 const bool kin = k < cs.K;
                 const int tap = kin ? k / cs.C : 0, c = kin ? k - tap * cs.C : 0;
                 const int ky = tap / cs.KW, kx = tap - ky * cs.KW;
@@ -374,12 +433,47 @@ __global__ void __launch_bounds__(CV_THREADS, 1)
     }
 }
 
-template <int BN, int VB>
-int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const tpt_cuda_weights *w, float a_scale,
-                const float *bias, int act, float *y, Requant rq) {
-    using Cfg = ConvCfg<BN>;
+PFN_cuTensorMapEncodeIm2col_v12000 im2col_encode_fn() {
+    static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// im2col tensor map of the NHWC int8 input [N, H, W, C]: the bounding box of
+// window starts runs from -pad to (extent + pad - kernel) per spatial
+// dimension with the conv stride as the traversal stride; 128 window
+// positions per load, KB channels each, swizzled like the MMA operand.
+bool make_tmap_im2col(CUtensorMap *tm, const int8_t *x, const ConvShape &cs, int kb) {
+    auto fn = im2col_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)cs.C, (cuuint64_t)cs.W, (cuuint64_t)cs.H, (cuuint64_t)cs.N};
+    cuuint64_t strides[3] = {(cuuint64_t)cs.C, (cuuint64_t)cs.W * cs.C, (cuuint64_t)cs.H * cs.W * cs.C};
+    int lower[2] = {-cs.pw, -cs.ph};
+    int upper[2] = {cs.pw - (cs.KW - 1), cs.ph - (cs.KH - 1)};
+    cuuint32_t estr[4] = {1, (cuuint32_t)cs.sw, (cuuint32_t)cs.sh, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(x), dims, strides, lower, upper,
+                    (cuuint32_t)kb, CV_BM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    kb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int MODE>
+int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
+                const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq) {
+    using Cfg = ConvCfg<BN, MODE>;
     static bool attr_done[64] = {};
-    auto kfn = k_conv_w8a8<BN, VB>;
+    auto kfn = k_conv_w8a8<BN, MODE>;
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
@@ -388,18 +482,26 @@ int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const t
     }
     const int OC = (int)w->n;
     CUtensorMap tw, ty;
-    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->n, w->k, 1, CV_BK, BN,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->n, w->k, 1, Cfg::KB, BN,
+                      Cfg::KB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
         return TPT_UNSUPPORTED;
     const long long M = (long long)cs.N * cs.OH * cs.OW;
     const bool tma_store = !rq.q && make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, (uint64_t)M, (uint64_t)OC, 4,
                                                  32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const long long ntiles = ((M + CV_BM - 1) / CV_BM) * ((OC + BN - 1) / BN);
     const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);
-    kfn<<<grid, CV_THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(tw, tma_store ? ty : tw, tma_store ? 1 : 0, x, cs, OC,
-                                                           a_scale, w->scales, bias, act, y, rq.q, rq.scale,
-                                                           ctx->d_flags);
+    kfn<<<grid, cv_threads(MODE), Cfg::SMEM_BYTES, ctx->stream>>>(tw, tx ? *tx : tw, tma_store ? ty : tw,
+                                                                 tma_store ? 1 : 0, x, cs, OC, a_scale, w->scales,
+                                                                 bias, act, y, rq.q, rq.scale, ctx->d_flags);
     return after_launch(ctx, "conv_w8a8");
+}
+
+template <int MODE>
+int launch_conv_bn(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
+                   const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq) {
+    if (w->n <= 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
+    if (w->n <= 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
+    return launch_conv<256, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
 }
 
 }  // namespace
@@ -419,15 +521,18 @@ int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, in
     if (M <= 0 || M > 0x7fffffffLL || xin > 0x7fffffffLL) return TPT_OK;  // 32-bit pixel offsets
     ConvShape cs{N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, KH * KW * C, (int)w->k};
     *handled = true;
-    const size_t oc = w->n;
-    if (C % 16 == 0) {
-        if (oc <= 64) return launch_conv<64, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
-        if (oc <= 128) return launch_conv<128, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
-        return launch_conv<256, 16>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+    // TMA im2col needs channel blocks of 64 or 128 bytes and k-blocks that are
+    // whole taps (Kw == K); inputs under 128 KB take the gather instead (the
+    // im2col descriptor of a tensor that small is not used on this driver)
+    if (C % 64 == 0 && (size_t)KH * KW * C == w->k && xin >= 131072) {
+        CUtensorMap tx;
+        const int kb = C % 128 == 0 ? 128 : 64;
+        if (make_tmap_im2col(&tx, x, cs, kb))
+            return kb == 128 ? launch_conv_bn<CV_IM2COL128>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq)
+                             : launch_conv_bn<CV_IM2COL64>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq);
     }
-    if (oc <= 64) return launch_conv<64, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
-    if (oc <= 128) return launch_conv<128, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
-    return launch_conv<256, 4>(ctx, x, cs, w, a_scale, bias, act, y, rq);
+    if (C % 16 == 0) return launch_conv_bn<CV_GATHER16>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq);
+    return launch_conv_bn<CV_GATHER4>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq);
 }
 
 }  // namespace tpt
