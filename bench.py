@@ -427,10 +427,37 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True, comm=None):
     return out
 
 
+def _conv_plan(be, N, H, W, C, OC, k, s, pad, seed):
+    """QUANTIZE (static scale) -> IM2COL -> LINEAR (+ReLU): one implicit-GEMM conv
+    launch per run after the quantize."""
+    from tpt_infer_b200 import graphs, synth
+
+    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    M, Kc = N * OH * OW, k * k * C
+    Kp = (Kc + 15) // 16 * 16  # weight rows padded with zero columns to a 16-byte multiple
+    wq, ws = be.quantize_i8_symmetric_per_channel(synth.normal(OC * Kc, seed, 0.0, 0.05), OC)
+    wp = np.zeros((OC, Kp), np.int8)
+    wp[:, :Kc] = np.asarray(wq).reshape(OC, Kc)
+    w = be.upload_i8(wp, ws, OC, Kp)
+    p = graphs.Plan(be)
+    p.weights.append(w)
+    tx, txq = p.tensor(graphs.F32, N * H * W * C), p.tensor(graphs.I8, N * H * W * C)
+    col, ty = p.tensor(graphs.I8, M * Kp), p.tensor(graphs.F32, M * OC)
+    p.op(graphs.OP_QUANTIZE, tx, txq, f0=0.02, dims=(N * H * W * C,))
+    p.op(graphs.OP_IM2COL, txq, col, dims=(N, H, W, C, k, k, s, s, pad, pad, OH, OW, Kp))
+    p.op(graphs.OP_LINEAR, col, ty, in1=p.const(np.zeros(OC, np.float32)), w=w, act=graphs.ACT_RELU, dims=(M,))
+    p.finalize()
+    p.run({tx: synth.normal(N * H * W * C, seed + 1)}, [ty])
+    return p
+
+
 def profile_kernels(args):
     """One case per main kernel, args.warmup + args.steps launches each, in this
-    order: W8A8 M=1 (GEMV), M=16 (stream-K), M=4096 (SM pair) at K=N=4096; W4 M=1
-    (GEMV) and M=8 (tensor core) at K=4096, N=11008; BERT attention 64x128x12."""
+    order: W8A8 M=1 (GEMV), M=16 (cluster split-K), M=4096 (SM pair) at
+    K=N=4096; W4 M=1 (GEMV) and M=8 (tensor core) at K=4096, N=11008; BERT
+    attention 64x128x12; INT8 convs of ResNet-18 at batch 64: a stage-1 3x3
+    (64 -> 64 channels at 56x56, TMA im2col) and the 7x7/2 stem (4 -> 64
+    channels at 224x224, cp.async gathers)."""
     import torch
 
     from tpt_infer_b200 import CudaBackend, graphs, synth
@@ -469,6 +496,10 @@ def profile_kernels(args):
     pa.run({tq: synth.normal(B * S * 3 * 768, 45)}, [to])
     out["attention_64x128x12_us"] = _time_device(stream, pa.run_device, args.steps, args.warmup, flush) * 1e6
     pa.close()
+    for name, shape in (("conv_stage1_b64", (64, 56, 56, 64, 64, 3, 1, 1)), ("conv_stem_b64", (64, 224, 224, 4, 64, 7, 2, 3))):
+        pc = _conv_plan(be, *shape, seed=3100)
+        out[f"{name}_us_with_quantize"] = _time_device(stream, pc.run_device, args.steps, args.warmup, flush) * 1e6
+        pc.close()
     be.close()
     print(json.dumps({"profile_kernels": True, "launches_each": reps, **out}), flush=True)
     return 0
