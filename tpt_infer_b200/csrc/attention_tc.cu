@@ -113,6 +113,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
 
+    pdl_wait();  // the previous kernel's output (qkv) is complete from here on
+    pdl_trigger();
+
     // ---- load and split: item = (row r, 4 consecutive d at 4*c4); rows past S
     // are zero. A warp's 32 items are 8 consecutive rows x 4 consecutive chunks
     // (64-byte global segments; the transposed V stores spread over the banks).
@@ -296,7 +299,7 @@ int launch_attention_tc(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, 
         if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
         attr[ctx->device & 63] = true;
     }
-    k_attention_tc<<<dim3((unsigned)H, (unsigned)B), AT_THREADS, AT_TC_SMEM, ctx->stream>>>(qkv, out, S, H, scale, q,
+    launch_pdl(k_attention_tc, dim3((unsigned)H, (unsigned)B), AT_THREADS, AT_TC_SMEM, ctx->stream, qkv, out, S, H, scale, q,
                                                                                            qs, ctx->d_flags);
     return after_launch(ctx, "attention_tc");
 }

@@ -65,6 +65,23 @@ struct tpt_cuda_weights {
 
 namespace tpt {
 
+// Launches `kern` on `st` with programmatic stream serialization (see
+// pdl_wait); a launch error is left for after_launch's cudaGetLastError.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 int set_size_mismatch(tpt_cuda_ctx *ctx, size_t expected, size_t actual);
 int cuda_fail(tpt_cuda_ctx *ctx, cudaError_t e, const char *what);
 // Ensures the context scratch holds at least `bytes` (grows; never shrinks).
@@ -186,6 +203,17 @@ __device__ __forceinline__ float apply_act(float y, int act) {
     if (act == TPT_ACT_GELU) return gelu_ref(y);
     return y;
 }
+
+// Programmatic dependent launch. A kernel launched with launch_pdl may start
+// while the previous kernel on the stream is still finishing: pdl_wait()
+// blocks until that kernel has completed and its memory is visible, so every
+// read of a predecessor's output (and every write) comes after it; each such
+// kernel calls it unconditionally, before any early exit, so it cannot
+// complete ahead of its predecessor. pdl_trigger() then lets the next kernel
+// be scheduled while this one runs (its own pdl_wait still waits for this
+// kernel's completion).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <int ACT>
 __device__ __forceinline__ float act_t(float y) {

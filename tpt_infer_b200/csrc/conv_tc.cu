@@ -192,6 +192,8 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_wait();  // the previous kernel's output (the input tensor) is complete from here on
+    pdl_trigger();
     const uint32_t tmem = tmem_slot;
     volatile int *abort_p = &abort_flag;
 
@@ -490,7 +492,7 @@ int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const C
                                                  32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const long long ntiles = ((M + CV_BM - 1) / CV_BM) * ((OC + BN - 1) / BN);
     const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);
-    kfn<<<grid, cv_threads(MODE), Cfg::SMEM_BYTES, ctx->stream>>>(tw, tx ? *tx : tw, tma_store ? ty : tw,
+    launch_pdl(kfn, grid, cv_threads(MODE), Cfg::SMEM_BYTES, ctx->stream, tw, tx ? *tx : tw, tma_store ? ty : tw,
                                                                  tma_store ? 1 : 0, x, cs, OC, a_scale, w->scales,
                                                                  bias, act, y, rq.q, rq.scale, ctx->d_flags);
     return after_launch(ctx, "conv_w8a8");

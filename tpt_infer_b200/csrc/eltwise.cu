@@ -15,6 +15,8 @@ __device__ __forceinline__ float unary_op(int op, float x) {
 
 __global__ void k_add_vec(const float4 *__restrict__ a, const float4 *__restrict__ b,
                           float4 *__restrict__ o, size_t n4) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
          i += (size_t)gridDim.x * blockDim.x) {
         float4 x = __ldg(a + i), y = __ldg(b + i);
@@ -24,6 +26,8 @@ __global__ void k_add_vec(const float4 *__restrict__ a, const float4 *__restrict
 
 __global__ void k_add(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ o,
                       size_t n) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         o[i] = a[i] + b[i];
@@ -31,6 +35,8 @@ __global__ void k_add(const float *__restrict__ a, const float *__restrict__ b, 
 
 template <int OP>
 __global__ void k_unary_vec(const float4 *__restrict__ a, float4 *__restrict__ o, size_t n4) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
          i += (size_t)gridDim.x * blockDim.x) {
         float4 x = __ldg(a + i);
@@ -40,6 +46,8 @@ __global__ void k_unary_vec(const float4 *__restrict__ a, float4 *__restrict__ o
 
 template <int OP>
 __global__ void k_unary(const float *__restrict__ a, float *__restrict__ o, size_t n) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         o[i] = unary_op(OP, a[i]);
@@ -49,6 +57,8 @@ __global__ void k_unary(const float *__restrict__ a, float *__restrict__ o, size
 // exp(v - max), warp-tree sum, then an IEEE divide by the sum.
 __global__ void k_softmax_warp(const float *__restrict__ a, float *__restrict__ o, size_t rows,
                                size_t L) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     size_t row = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
     const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -72,6 +82,8 @@ __global__ void k_softmax_warp(const float *__restrict__ a, float *__restrict__ 
 // One block per row for long rows.
 __global__ void k_softmax_block(const float *__restrict__ a, float *__restrict__ o, size_t rows,
                                 size_t L) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
     for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -109,10 +121,10 @@ int launch_add(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, si
     const unsigned bs = 256;
     unsigned cap = (unsigned)ctx->sm_count * 8;
     if (n % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out)) {
-        k_add_vec<<<grid_1d(n / 4, bs, cap), bs, 0, ctx->stream>>>((const float4 *)a, (const float4 *)b,
+        launch_pdl(k_add_vec, grid_1d(n / 4, bs, cap), bs, 0, ctx->stream, (const float4 *)a, (const float4 *)b,
                                                                     (float4 *)out, n / 4);
     } else {
-        k_add<<<grid_1d(n, bs, cap), bs, 0, ctx->stream>>>(a, b, out, n);
+        launch_pdl(k_add, grid_1d(n, bs, cap), bs, 0, ctx->stream, a, b, out, n);
     }
     return after_launch(ctx, "add");
 }
@@ -124,9 +136,9 @@ int launch_unary(tpt_cuda_ctx *ctx, int op, const float *a, float *out, size_t n
     unsigned g = grid_1d(vec ? n / 4 : n, bs, cap);
 #define TPT_UNARY(OPN)                                                                                 \
     if (vec)                                                                                           \
-        k_unary_vec<OPN><<<g, bs, 0, ctx->stream>>>((const float4 *)a, (float4 *)out, n / 4);          \
+        launch_pdl(k_unary_vec<OPN>, g, bs, 0, ctx->stream, (const float4 *)a, (float4 *)out, n / 4);          \
     else                                                                                               \
-        k_unary<OPN><<<g, bs, 0, ctx->stream>>>(a, out, n);
+        launch_pdl(k_unary<OPN>, g, bs, 0, ctx->stream, a, out, n);
     if (op == 1) {
         TPT_UNARY(1)
     } else if (op == 2) {
@@ -142,10 +154,10 @@ int launch_softmax(tpt_cuda_ctx *ctx, const float *a, float *out, size_t rows, s
     if (row_len <= 2048) {
         const unsigned bs = 256;
         unsigned g = grid_1d(rows * 32, bs, (unsigned)ctx->sm_count * 16);
-        k_softmax_warp<<<g, bs, 0, ctx->stream>>>(a, out, rows, row_len);
+        launch_pdl(k_softmax_warp, g, bs, 0, ctx->stream, a, out, rows, row_len);
     } else {
         unsigned g = (unsigned)(rows < (size_t)ctx->sm_count * 8 ? rows : (size_t)ctx->sm_count * 8);
-        k_softmax_block<<<g, 512, 0, ctx->stream>>>(a, out, rows, row_len);
+        launch_pdl(k_softmax_block, g, 512, 0, ctx->stream, a, out, rows, row_len);
     }
     return after_launch(ctx, "softmax");
 }

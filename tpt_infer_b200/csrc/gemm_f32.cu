@@ -42,6 +42,8 @@ template <int MODE>
 __global__ void __launch_bounds__(NT) k_gemm_f32(const float *__restrict__ A, const float *__restrict__ B,
                                                  float *__restrict__ Cout, int M, int N, int K,
                                                  ConvGeom g, W4Epi epi) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
     const int tid = threadIdx.x;
@@ -171,6 +173,8 @@ __global__ void __launch_bounds__(NT) k_gemm_f32(const float *__restrict__ A, co
 constexpr int SB = 16, SK = 32;
 __global__ void __launch_bounds__(256) k_gemm_f32_small(const float *__restrict__ A, const float *__restrict__ B,
                                                        float *__restrict__ Cout, int M, int N, int K) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float As[SK][SB + 1];
     __shared__ float Bs[SK][SB + 1];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -210,6 +214,8 @@ template <bool TA, bool TB>
 __global__ void __launch_bounds__(256) k_gemm_onnx(const float *__restrict__ A, const float *__restrict__ B,
                                                   const float *__restrict__ Cm, int c_mode, float alpha, float beta,
                                                   float *__restrict__ Y, int M, int N, int K) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float As[SK][SB + 1];
     __shared__ float Bs[SK][SB + 1];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -259,7 +265,7 @@ int launch_gemm_onnx(tpt_cuda_ctx *ctx, const float *a, const float *b, const fl
     dim3 g((unsigned)((n + SB - 1) / SB), (unsigned)((m + SB - 1) / SB));
     if (g.y > 65535) return TPT_UNSUPPORTED;
 #define TPT_ONNX(TA_, TB_)                                                                                     \
-    k_gemm_onnx<TA_, TB_><<<g, 256, 0, ctx->stream>>>(a, b, c, c_mode, alpha, beta, y, (int)m, (int)n, (int)k)
+    launch_pdl(k_gemm_onnx<TA_, TB_>, g, 256, 0, ctx->stream, a, b, c, c_mode, alpha, beta, y, (int)m, (int)n, (int)k)
     if (ta && tb)
         TPT_ONNX(true, true);
     else if (ta)
@@ -283,12 +289,12 @@ int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *
     if ((size_t)grid.x * grid.y < (size_t)ctx->sm_count) {
         dim3 sg((unsigned)((n + SB - 1) / SB), (unsigned)((m + SB - 1) / SB));
         if (sg.y > 65535) return TPT_UNSUPPORTED;
-        k_gemm_f32_small<<<sg, 256, 0, ctx->stream>>>(a, b, out, (int)m, (int)n, (int)k);
+        launch_pdl(k_gemm_f32_small, sg, 256, 0, ctx->stream, a, b, out, (int)m, (int)n, (int)k);
         return after_launch(ctx, "matmul_f32_small");
     }
     if (grid.y > 65535) return TPT_UNSUPPORTED;
     ConvGeom g{};
-    k_gemm_f32<0><<<grid, NT, 0, ctx->stream>>>(a, b, out, (int)m, (int)n, (int)k, g, W4Epi{});
+    launch_pdl(k_gemm_f32<0>, grid, NT, 0, ctx->stream, a, b, out, (int)m, (int)n, (int)k, g, W4Epi{});
     return after_launch(ctx, "matmul_f32");
 }
 
@@ -306,7 +312,7 @@ int launch_conv2d_f32(tpt_cuda_ctx *ctx, const float *in, const float *w, float 
                (int)sh, (int)sw, (int)ph, (int)pw, (int)ws[0]};
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
     if (grid.y > 65535) return TPT_UNSUPPORTED;
-    k_gemm_f32<1><<<grid, NT, 0, ctx->stream>>>(in, w, out, (int)M, (int)N, (int)K, g, W4Epi{});
+    launch_pdl(k_gemm_f32<1>, grid, NT, 0, ctx->stream, in, w, out, (int)M, (int)N, (int)K, g, W4Epi{});
     return after_launch(ctx, "conv2d_f32");
 }
 
@@ -316,7 +322,7 @@ int launch_w4_simt(tpt_cuda_ctx *ctx, const float *x, const uint8_t *packed, con
     dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
     if (grid.y > 65535) return TPT_UNSUPPORTED;
     ConvGeom g{};
-    k_gemm_f32<2><<<grid, NT, 0, ctx->stream>>>(x, reinterpret_cast<const float *>(packed), y, (int)m, (int)n,
+    launch_pdl(k_gemm_f32<2>, grid, NT, 0, ctx->stream, x, reinterpret_cast<const float *>(packed), y, (int)m, (int)n,
                                                 (int)k, g, W4Epi{scales, bias, act});
     return after_launch(ctx, "w4_simt");
 }

@@ -23,6 +23,8 @@ namespace {
 constexpr int LN_MAX = 32;
 __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ b,
                             float *__restrict__ y, int rows, int cols, float eps, int8_t *__restrict__ qout, float qs) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -63,6 +65,8 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 template <int G>
 __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restrict__ g, const float4 *__restrict__ b,
                              float4 *__restrict__ y, int rows, float eps, uint32_t *__restrict__ qout, float qs) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -107,6 +111,8 @@ __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restr
 // crates/tpt-infer-runtime/src/kernels.rs:150-178, plus a fused activation)
 __global__ void k_bias_act(const float *__restrict__ x, const float *__restrict__ bias, float *__restrict__ y,
                            size_t rows, int cols, int act) {
+    pdl_wait();
+    pdl_trigger();
     const size_t n = rows * (size_t)cols;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         float v = x[i];
@@ -120,6 +126,8 @@ __global__ void k_bias_act(const float *__restrict__ x, const float *__restrict_
 // point's scale (the following QUANTIZE op, fused)
 __global__ void k_add_act(const float4 *__restrict__ a, const float4 *__restrict__ b, float4 *__restrict__ y, size_t n4,
                           int act, uint32_t *__restrict__ q, float qs) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const float4 x = a[i], z = b[i];
         const float4 o = make_float4(apply_act(x.x + z.x, act), apply_act(x.y + z.y, act), apply_act(x.z + z.z, act),
@@ -138,6 +146,8 @@ __global__ void k_add_act(const float4 *__restrict__ a, const float4 *__restrict
 // zero: a 3-channel image padded to 4 gives the stem 4-byte im2col chunks).
 __global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restrict__ q, int N, int C, int HW, int Cp,
                                   float scale) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = (size_t)N * Cp * HW;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         // i indexes the NHWC output
@@ -157,6 +167,8 @@ template <int VB>
 __global__ void __launch_bounds__(256) k_im2col_nhwc(const int8_t *__restrict__ x, int8_t *__restrict__ col, int N,
                                                      int H, int W, int C, int KH, int KW, int sh, int sw, int ph,
                                                      int pw, int OH, int OW, int Kp) {
+    pdl_wait();
+    pdl_trigger();
     using V = typename std::conditional<VB == 16, int4, typename std::conditional<VB == 4, int, int8_t>::type>::type;
     const int lane = threadIdx.x & 31;
     const int rows = N * OH * OW, K = KH * KW * C, chunks = Kp / VB;
@@ -189,6 +201,8 @@ constexpr int IM2COL_ROW_MAX = 1024;
 __global__ void __launch_bounds__(256) k_im2col_nhwc_taps(const int8_t *__restrict__ x, int8_t *__restrict__ col,
                                                           int N, int H, int W, int C, int KH, int KW, int sh, int sw,
                                                           int ph, int pw, int OH, int OW, int Kp) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) int8_t rowbuf[8][IM2COL_ROW_MAX];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     int8_t *rb = rowbuf[wib];
@@ -217,6 +231,8 @@ __global__ void __launch_bounds__(256) k_im2col_nhwc_taps(const int8_t *__restri
 // max pool on NHWC f32, padding as -inf (kernels.rs:271-325)
 __global__ void k_maxpool_nhwc(const float *__restrict__ x, float *__restrict__ y, int N, int H, int W, int C, int KH,
                                int KW, int sh, int sw, int ph, int pw, int OH, int OW) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = (size_t)N * OH * OW * C;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % C);
@@ -243,6 +259,8 @@ __global__ void k_maxpool_nhwc(const float *__restrict__ x, float *__restrict__ 
 // Same, 4 channels per thread (C % 4 == 0, 16-byte aligned), 32-bit index math.
 __global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict__ y, int N, int H, int W, int C4,
                                 int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW) {
+    pdl_wait();
+    pdl_trigger();
     const int total = N * OH * OW * C4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int c = i % C4, t = i / C4, ox = t % OW, t2 = t / OW, oy = t2 % OH, n = t2 / OH;
@@ -267,6 +285,8 @@ __global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict
 // global average pool NHWC f32 [N, HW, C] -> [N, C]: sequential sum over the
 // window, then divide by the count (kernels.rs:335-390 with kernel = spatial)
 __global__ void k_gap_nhwc(const float *__restrict__ x, float *__restrict__ y, int N, int HW, int C) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = (size_t)N * C;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % C);
@@ -280,6 +300,8 @@ __global__ void k_gap_nhwc(const float *__restrict__ x, float *__restrict__ y, i
 // max |x| folded into *cell (non-negative float bits; atomicMax), used to
 // calibrate static activation scales
 __global__ void k_absmax_acc(const float *__restrict__ x, size_t n, unsigned *cell) {
+    pdl_wait();
+    pdl_trigger();
     float m = 0.0f;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         m = fmaxf(m, fabsf(x[i]));
@@ -295,11 +317,11 @@ int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const fl
     const unsigned grid = grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16);
     const bool a16 = ((((uintptr_t)x | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) & 15) == 0) && ((uintptr_t)q & 3) == 0;
     if (a16 && cols == 768) {  // the BERT hidden size
-        k_layernorm4<6><<<grid, 256, 0, ctx->stream>>>((const float4 *)x, (const float4 *)g, (const float4 *)b,
+        launch_pdl(k_layernorm4<6>, grid, 256, 0, ctx->stream, (const float4 *)x, (const float4 *)g, (const float4 *)b,
                                                        (float4 *)y, (int)rows, eps, (uint32_t *)q, qs);
         return after_launch(ctx, "layernorm");
     }
-    k_layernorm<<<grid, 256, 0, ctx->stream>>>(x, g, b, y, (int)rows, (int)cols, eps, q, qs);
+    launch_pdl(k_layernorm, grid, 256, 0, ctx->stream, x, g, b, y, (int)rows, (int)cols, eps, q, qs);
     return after_launch(ctx, "layernorm");
 }
 
@@ -312,7 +334,7 @@ int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int
 }
 
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act) {
-    k_bias_act<<<grid_1d(rows * cols, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(x, bias, y, rows,
+    launch_pdl(k_bias_act, grid_1d(rows * cols, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, x, bias, y, rows,
                                                                                               (int)cols, act);
     return after_launch(ctx, "bias_act");
 }
@@ -320,15 +342,13 @@ int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float 
 int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act, int8_t *q,
                    float qs) {
     if (n % 4 || ((uintptr_t)q & 3)) return TPT_UNSUPPORTED;
-    k_add_act<<<grid_1d(n / 4, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
-        (const float4 *)a, (const float4 *)b, (float4 *)y, n / 4, act, reinterpret_cast<uint32_t *>(q), qs);
+    launch_pdl(k_add_act, grid_1d(n / 4, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, (const float4 *)a, (const float4 *)b, (float4 *)y, n / 4, act, reinterpret_cast<uint32_t *>(q), qs);
     return after_launch(ctx, "add_act");
 }
 
 int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int Cp,
                            float scale) {
-    k_nchw_to_nhwc_q8<<<grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
-        x, q, N, C, HW, Cp, scale);
+    launch_pdl(k_nchw_to_nhwc_q8, grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, x, q, N, C, HW, Cp, scale);
     return after_launch(ctx, "nchw_to_nhwc_q8");
 }
 
@@ -339,13 +359,13 @@ int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H,
     const unsigned g = grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16);
     const bool a16 = ((uintptr_t)x & 15) == 0 && ((uintptr_t)col & 15) == 0;
     if ((C & 15) == 0 && (Kp & 15) == 0 && a16)
-        k_im2col_nhwc<16><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+        launch_pdl(k_im2col_nhwc<16>, g, 256, 0, ctx->stream, x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
     else if ((C & 3) == 0 && (Kp & 3) == 0 && a16)
-        k_im2col_nhwc<4><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+        launch_pdl(k_im2col_nhwc<4>, g, 256, 0, ctx->stream, x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
     else if ((Kp & 15) == 0 && Kp <= IM2COL_ROW_MAX && ((uintptr_t)col & 15) == 0)
-        k_im2col_nhwc_taps<<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+        launch_pdl(k_im2col_nhwc_taps, g, 256, 0, ctx->stream, x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
     else
-        k_im2col_nhwc<1><<<g, 256, 0, ctx->stream>>>(x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
+        launch_pdl(k_im2col_nhwc<1>, g, 256, 0, ctx->stream, x, col, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW, Kp);
     return after_launch(ctx, "im2col");
 }
 
@@ -353,18 +373,16 @@ int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int 
                         int sw, int ph, int pw, int OH, int OW) {
     const size_t total = (size_t)N * OH * OW * C;
     if (C % 4 == 0 && total / 4 < 0x7fffffff && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
-        k_maxpool_nhwc4<<<grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw, ph, pw,
+        launch_pdl(k_maxpool_nhwc4, grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream, reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw, ph, pw,
             OH, OW);
         return after_launch(ctx, "maxpool");
     }
-    k_maxpool_nhwc<<<grid_1d(total, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream>>>(
-        x, y, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW);
+    launch_pdl(k_maxpool_nhwc, grid_1d(total, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream, x, y, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW);
     return after_launch(ctx, "maxpool");
 }
 
 int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, int C) {
-    k_gap_nhwc<<<grid_1d((size_t)N * C, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(x, y, N, HW, C);
+    launch_pdl(k_gap_nhwc, grid_1d((size_t)N * C, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, x, y, N, HW, C);
     return after_launch(ctx, "global_avgpool");
 }
 
@@ -372,6 +390,8 @@ namespace {
 // [P][T][C] int8 panels (the all-gathered column shards) -> [T][P*C] rows, the
 // K-contiguous A operand of the next GEMM; 16 bytes per thread (C % 16 == 0).
 __global__ void k_panels_to_rows16(const int4 *__restrict__ in, int4 *__restrict__ out, int P, size_t T, int C16) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = (size_t)P * T * C16;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % C16);
@@ -382,6 +402,8 @@ __global__ void k_panels_to_rows16(const int4 *__restrict__ in, int4 *__restrict
     }
 }
 __global__ void k_panels_to_rows1(const int8_t *__restrict__ in, int8_t *__restrict__ out, int P, size_t T, int C) {
+    pdl_wait();
+    pdl_trigger();
     const size_t total = (size_t)P * T * C;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % C);
@@ -396,16 +418,15 @@ __global__ void k_panels_to_rows1(const int8_t *__restrict__ in, int8_t *__restr
 int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int P, size_t T, int C) {
     const size_t total = (size_t)P * T * C;
     if (C % 16 == 0 && ((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0) {
-        k_panels_to_rows16<<<grid_1d(total / 16, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const int4 *>(in), reinterpret_cast<int4 *>(out), P, T, C / 16);
+        launch_pdl(k_panels_to_rows16, grid_1d(total / 16, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, reinterpret_cast<const int4 *>(in), reinterpret_cast<int4 *>(out), P, T, C / 16);
     } else {
-        k_panels_to_rows1<<<grid_1d(total, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(in, out, P, T, C);
+        launch_pdl(k_panels_to_rows1, grid_1d(total, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, in, out, P, T, C);
     }
     return after_launch(ctx, "panels_to_rows");
 }
 
 int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell) {
-    k_absmax_acc<<<grid_1d(n, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream>>>(x, n, cell);
+    launch_pdl(k_absmax_acc, grid_1d(n, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, x, n, cell);
     return after_launch(ctx, "absmax");
 }
 

@@ -70,6 +70,8 @@ __global__ void k_quant_i8_from_cell(const float *__restrict__ x, size_t n, cons
 }
 
 __global__ void k_quant_i8_static(const float *__restrict__ x, size_t n, float scale, int8_t *__restrict__ q) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         q[i] = round_clamp_i8(__fdiv_rn(x[i], scale), -127.0f, 127.0f);
 }
@@ -77,6 +79,8 @@ __global__ void k_quant_i8_static(const float *__restrict__ x, size_t n, float s
 // Same, 16 elements per thread: four 16-byte loads, one 16-byte store
 // (x and q 16-byte aligned, n % 16 == 0).
 __global__ void k_quant_i8_static16(const float4 *__restrict__ x, size_t n16, float scale, int4 *__restrict__ q) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
         uint32_t w[4];
 #pragma unroll
@@ -95,6 +99,8 @@ __global__ void k_quant_i8_static16(const float4 *__restrict__ x, size_t n16, fl
 // quant.rs:95-107: one CTA per row of [rows, cols]
 __global__ void k_quant_i8_rows(const float *__restrict__ x, size_t rows, size_t cols, int8_t *__restrict__ q,
                                 float *__restrict__ scales) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const float *xr = x + r * cols;
         float m = 0.0f;
@@ -261,17 +267,16 @@ int launch_quant_i8_sym(tpt_cuda_ctx *ctx, const float *x, size_t n, int8_t *q, 
 
 int launch_quant_i8_static(tpt_cuda_ctx *ctx, const float *x, size_t n, float scale, int8_t *q) {
     if (n % 16 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)q & 15) == 0) {
-        k_quant_i8_static16<<<grid_1d(n / 16, 256, cap_grid(ctx)), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float4 *>(x), n / 16, scale, reinterpret_cast<int4 *>(q));
+        launch_pdl(k_quant_i8_static16, grid_1d(n / 16, 256, cap_grid(ctx)), 256, 0, ctx->stream, reinterpret_cast<const float4 *>(x), n / 16, scale, reinterpret_cast<int4 *>(q));
         return after_launch(ctx, "quantize_i8_static");
     }
-    k_quant_i8_static<<<grid_1d(n, 256, cap_grid(ctx)), 256, 0, ctx->stream>>>(x, n, scale, q);
+    launch_pdl(k_quant_i8_static, grid_1d(n, 256, cap_grid(ctx)), 256, 0, ctx->stream, x, n, scale, q);
     return after_launch(ctx, "quantize_i8_static");
 }
 
 int launch_quant_i8_rows(tpt_cuda_ctx *ctx, const float *x, size_t rows, size_t cols, int8_t *q, float *scales) {
     unsigned g = (unsigned)(rows < (size_t)ctx->sm_count * 16 ? rows : (size_t)ctx->sm_count * 16);
-    k_quant_i8_rows<<<g ? g : 1, 256, 0, ctx->stream>>>(x, rows, cols, q, scales);
+    launch_pdl(k_quant_i8_rows, g ? g : 1, 256, 0, ctx->stream, x, rows, cols, q, scales);
     return after_launch(ctx, "quantize_i8_per_channel");
 }
 

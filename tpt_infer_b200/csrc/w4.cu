@@ -40,6 +40,8 @@ template <int MM>
 __global__ void __launch_bounds__(256) k_w4_gemv(const float *__restrict__ X, const uint8_t *__restrict__ Wp,
                                                  const float *__restrict__ scales, const float *__restrict__ bias,
                                                  int M, int N, int K, int act, float *__restrict__ Y) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -120,6 +122,8 @@ template <int MM>
 __global__ void __launch_bounds__(256) k_w4_gemv2(const float *__restrict__ X, const uint8_t *__restrict__ Wp,
                                                   const float *__restrict__ scales, const float *__restrict__ bias,
                                                   int M, int N, int K, int act, float *__restrict__ Y) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float part[8][MM][W4V_ROWS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int KW = K >> 10;  // warps along K (blockDim.x / 32 == KW)

@@ -204,6 +204,8 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_wait();  // the previous kernel's output (x_hi / x_lo) is complete from here on
+    pdl_trigger();
     const uint32_t tmem = tmem_slot;
     volatile int *abort_p = &abort_flag;
     SkRange range(units, kblocks, blockIdx.x, gridDim.x);
@@ -442,6 +444,8 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
 // x f32 [M, K] -> hi, lo fp16 [M, K]; inside each group of 8 the k order is
 // (0, 4, 1, 5, 2, 6, 3, 7), the order the unpacker produces for the weights.
 __global__ void k_split_f16(const float *__restrict__ x, __half *__restrict__ hi, __half *__restrict__ lo, size_t groups) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
         const float4 a = __ldg(reinterpret_cast<const float4 *>(x) + 2 * g);
         const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + 2 * g + 1);

@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                                                    int M, int N, int K, float a_scale, int act,
                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
                                                    int8_t *__restrict__ Q, float q_scale) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -129,6 +131,8 @@ __global__ void __launch_bounds__(256) k_w8a8_simt(const int8_t *__restrict__ A,
                                                    int M, int N, int K, float a_scale, int act,
                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
                                                    int8_t *__restrict__ Q, float q_scale) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) int As[2][8][128 + 4];
     __shared__ __align__(16) int Bs[2][8][128 + 4];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -231,7 +235,7 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
         unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
         const bool areg = k <= (size_t)GEMV_CH * 32 * 16;
 #define TPT_GEMV(MM, AR) \
-    k_w8a8_gemv<MM, AR><<<g, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc, \
+    launch_pdl(k_w8a8_gemv<MM, AR>, g, 256, 0, ctx->stream, a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc, \
                                                     rq.q, rq.scale)
         if (m == 1 && areg)
             TPT_GEMV(1, true);
@@ -253,7 +257,7 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     if (st || handled) return st;
     dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 127) / 128));
     if (grid.y > 65535) return TPT_UNSUPPORTED;
-    k_w8a8_simt<<<grid, 256, 0, ctx->stream>>>(a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc,
+    launch_pdl(k_w8a8_simt, grid, 256, 0, ctx->stream, a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc,
                                                rq.q, rq.scale);
     return after_launch(ctx, "w8a8_simt");
 }

@@ -138,6 +138,8 @@ __global__ void __launch_bounds__(CK_THREADS, 1)
     tc_fence_before();
     cluster_sync();  // every CTA's barriers exist before any partial is sent
     tc_fence_after();
+    pdl_wait();  // the previous kernel's output (A) is complete from here on
+    pdl_trigger();
     const uint32_t tmem = tmem_slot;
     volatile int *abort_p = &abort_flag;
 
@@ -302,13 +304,15 @@ int launch_ck(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const CUtensorMap &ta, i
     cfg.blockDim = dim3(CK_THREADS, 1, 1);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
     cfg.stream = ctx->stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = (unsigned)ks;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, tw, ta, M, N, K, a_scale, ws, bias, act, y, acc, ctx->d_flags, rq.q,
                                        rq.scale);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "w8a8_ck launch");

@@ -137,6 +137,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     tc_fence_before();
     cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
+    pdl_wait();  // the previous kernel's output (A) is complete from here on
+    pdl_trigger();
     const uint32_t tmem = tmem_slot;
     volatile int *abort_p = &abort_flag;
 
@@ -404,8 +406,8 @@ int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, 
     CUtensorMap ty;
     const bool tma_store = !rq.q && make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
                                                   (uint64_t)N, ACC_OUT);
-    kfn<<<2 * clusters, P_THREADS, P_SMEM_BYTES, ctx->stream>>>(ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0, M, N,
-                                                                 K, a_scale, ws, bias, act, y, acc, ctx->d_flags, rq.q, rq.scale);
+    launch_pdl(kfn, 2 * clusters, P_THREADS, P_SMEM_BYTES, ctx->stream, ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0,
+               M, N, K, a_scale, ws, bias, act, y, acc, ctx->d_flags, rq.q, rq.scale);
     return after_launch(ctx, "w8a8_tc2");
 }
 
