@@ -427,12 +427,12 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True, comm=None):
     return out
 
 
-def _conv_plan(be, N, H, W, C, OC, k, s, pad, seed):
+def _conv_plan(be, N, H, W, C, OC, k, s, pad, seed, out_hw=None):
     """QUANTIZE (static scale) -> IM2COL -> LINEAR (+ReLU): one implicit-GEMM conv
     launch per run after the quantize."""
     from tpt_infer_b200 import graphs, synth
 
-    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    OH, OW = out_hw or ((H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1)
     M, Kc = N * OH * OW, k * k * C
     Kp = (Kc + 15) // 16 * 16  # weight rows padded with zero columns to a 16-byte multiple
     wq, ws = be.quantize_i8_symmetric_per_channel(synth.normal(OC * Kc, seed, 0.0, 0.05), OC)
@@ -456,8 +456,9 @@ def profile_kernels(args):
     order: W8A8 M=1 (GEMV), M=16 (cluster split-K), M=4096 (SM pair) at
     K=N=4096; W4 M=1 (GEMV) and M=8 (tensor core) at K=4096, N=11008; BERT
     attention 64x128x12; INT8 convs of ResNet-18 at batch 64: a stage-1 3x3
-    (64 -> 64 channels at 56x56, TMA im2col) and the 7x7/2 stem (4 -> 64
-    channels at 224x224, cp.async gathers)."""
+    (64 -> 64 channels at 56x56, TMA im2col) and the stem in its space-to-depth
+    form (the 7x7/2 conv as a 4x4/1 conv over [112, 112, 16], cp.async
+    gathers)."""
     import torch
 
     from tpt_infer_b200 import CudaBackend, graphs, synth
@@ -496,8 +497,9 @@ def profile_kernels(args):
     pa.run({tq: synth.normal(B * S * 3 * 768, 45)}, [to])
     out["attention_64x128x12_us"] = _time_device(stream, pa.run_device, args.steps, args.warmup, flush) * 1e6
     pa.close()
-    for name, shape in (("conv_stage1_b64", (64, 56, 56, 64, 64, 3, 1, 1)), ("conv_stem_b64", (64, 224, 224, 4, 64, 7, 2, 3))):
-        pc = _conv_plan(be, *shape, seed=3100)
+    for name, shape, ohw in (("conv_stage1_b64", (64, 56, 56, 64, 64, 3, 1, 1), None),
+                             ("conv_stem_b64", (64, 112, 112, 16, 64, 4, 1, 2), (112, 112))):
+        pc = _conv_plan(be, *shape, seed=3100, out_hw=ohw)
         out[f"{name}_us_with_quantize"] = _time_device(stream, pc.run_device, args.steps, args.warmup, flush) * 1e6
         pc.close()
     be.close()

@@ -292,7 +292,8 @@ enum tpt_op_kind {
     TPT_OP_LAYERNORM = 7,       /* rows d0 of d1; in1 gamma, in2 beta; eps f0 */
     TPT_OP_ATTENTION = 8,       /* in0 qkv [d0*d1, 3*d2*d3] -> out [d0*d1, d2*d3]; B=d0 S=d1 H=d2 D=d3; scale f0 */
     TPT_OP_NCHW_TO_NHWC_Q8 = 9, /* in0 f32 NCHW [d0, d1, d2=H*W] -> out i8 NHWC with d3 channels (d3 > d1:
-                                   zero-padded; 0: d1), per-tensor scale */
+                                   zero-padded; 0: d1), per-tensor scale. d5 = 2 (with d4 = W): space-to-depth,
+                                   out [d0, H/2, W/2, 4*d3], channel (dy*2 + dx)*d3 + c */
     TPT_OP_IM2COL = 10,         /* in0 i8 NHWC -> out i8 [N*OH*OW, Kp]; d0..d12 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW,Kp */
     TPT_OP_MAXPOOL_NHWC = 11,   /* f32; d0..d11 = N,H,W,C,KH,KW,sh,sw,ph,pw,OH,OW */
     TPT_OP_GAP_NHWC = 12,       /* f32 [d0, d1=H*W, d2] -> [d0, d2] */

@@ -141,19 +141,28 @@ __global__ void k_add_act(const float4 *__restrict__ a, const float4 *__restrict
 
 // ---------------------------------------------------------------- images
 // NCHW f32 -> NHWC int8 with a static per-tensor scale:
-// q = clamp(round(x / scale), -127, 127) (quant.rs:35-36)
-// NCHW f32 -> NHWC int8 with Cp >= C channels per pixel (channels [C, Cp) are
-// zero: a 3-channel image padded to 4 gives the stem 4-byte im2col chunks).
-__global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restrict__ q, int N, int C, int HW, int Cp,
-                                  float scale) {
+// q = clamp(round(x / scale), -127, 127) (quant.rs:35-36), Cp >= C channels
+// per pixel (channels [C, Cp) are zero). With s2d = 2 the pixels are also
+// regrouped space-to-depth: output pixel (y, x) of an [H/2, W/2] grid holds the
+// 2x2 input pixels (2y + dy, 2x + dx) as channels ((dy * 2 + dx) * Cp + c). A
+// stride-2 convolution then runs as a stride-1 one on 16-byte pixels (a
+// 3-channel image padded to 4: the stem's gathers move 16-byte chunks).
+__global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restrict__ q, int N, int C, int HW, int W,
+                                  int Cp, int s2d, float scale) {
     pdl_wait();
     pdl_trigger();
     const size_t total = (size_t)N * Cp * HW;
+    const int cpp = Cp * s2d * s2d;  // output channels per pixel
+    const int Wo = W / s2d;
+    const size_t HWo = (size_t)HW / ((size_t)s2d * s2d);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        // i indexes the NHWC output
-        const int c = (int)(i % Cp);
-        const size_t p = i / Cp;  // n*HW + hw
-        const size_t n = p / HW, hw = p - n * HW;
+        // i indexes the output
+        const int oc = (int)(i % cpp);
+        const size_t p = i / cpp;  // n * HWo + output pixel
+        const size_t n = p / HWo, hwo = p - n * HWo;
+        const int sub = oc / Cp, c = oc - sub * Cp;
+        const int oy = (int)(hwo / Wo), ox = (int)(hwo - (size_t)oy * Wo);
+        const size_t hw = (size_t)(oy * s2d + sub / s2d) * W + (ox * s2d + sub % s2d);
         q[i] = c < C ? round_clamp_i8(__fdiv_rn(x[(n * C + c) * HW + hw], scale), -127.0f, 127.0f) : (int8_t)0;
     }
 }
@@ -346,9 +355,13 @@ int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, 
     return after_launch(ctx, "add_act");
 }
 
-int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int Cp,
+int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int W, int Cp, int s2d,
                            float scale) {
-    launch_pdl(k_nchw_to_nhwc_q8, grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream, x, q, N, C, HW, Cp, scale);
+    if (s2d < 1) s2d = 1;
+    if (W <= 0) W = HW;  // no width given: only s2d = 1 is possible
+    if (s2d > 2 || HW % W || (W % s2d) || ((HW / W) % s2d)) return TPT_UNSUPPORTED;
+    launch_pdl(k_nchw_to_nhwc_q8, grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream,
+               x, q, N, C, HW, W, Cp, s2d, scale);
     return after_launch(ctx, "nchw_to_nhwc_q8");
 }
 

@@ -29,7 +29,7 @@ int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
 int launch_add_act(tpt_cuda_ctx *ctx, const float *a, const float *b, float *y, size_t n, int act,
                    int8_t *q = nullptr, float qs = 0.0f);
-int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int Cp,
+int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, int C, int HW, int W, int Cp, int s2d,
                            float scale);
 int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H, int W, int C, int KH, int KW, int sh,
                   int sw, int ph, int pw, int OH, int OW, int Kp);
@@ -144,13 +144,15 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
             p->tensors[o.out].scale = s;
             return launch_quant_i8_static(ctx, F(p, o.in0), d[0], s, Q(p, o.out));
         }
-        case TPT_OP_NCHW_TO_NHWC_Q8: {  // f32 NCHW [N,C,HW] -> i8 NHWC with d3 (>= C, or 0 = C) channels
+        case TPT_OP_NCHW_TO_NHWC_Q8: {  // f32 NCHW [N,C,HW] -> i8 NHWC with d3 (>= C, or 0 = C) channels;
+                                        // d4 = W, d5 = 2: space-to-depth 2x2
             float s;
             st = point_scale(p, po, F(p, o.in0), d[0] * d[1] * d[2], &s);
             if (st) return st;
             p->tensors[o.out].scale = s;
             const int cp = d[3] > d[1] ? (int)d[3] : (int)d[1];
-            return launch_nchw_to_nhwc_q8(ctx, F(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], cp, s);
+            return launch_nchw_to_nhwc_q8(ctx, F(p, o.in0), Q(p, o.out), (int)d[0], (int)d[1], (int)d[2], (int)d[4], cp,
+                                          (int)d[5], s);
         }
         case TPT_OP_LINEAR_W8A8: {  // i8 [rows, K] x W^T -> f32 [rows, N] (+bias, act)
             const float sa = p->tensors[o.in0].scale;

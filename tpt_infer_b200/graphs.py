@@ -276,23 +276,35 @@ def resnet18_weights(be, seed=100):
     return spec
 
 
-def _pad_channels(cv, cp):
-    """The conv's (ky, kx, c) weight columns with c padded from cin to cp by
-    zero weights: the same int32 sums on an input whose extra channels are 0."""
-    taps = cv.k * cv.k
-    q = cv.qw.q[:, :taps * cv.cin].reshape(cv.cout, taps, cv.cin)
-    qp = np.zeros((cv.cout, taps, cp), np.int8)
-    qp[:, :, :cv.cin] = q
-    kp = (taps * cp + 15) // 16 * 16
-    out = np.zeros((cv.cout, kp), np.int8)
-    out[:, :taps * cp] = qp.reshape(cv.cout, taps * cp)
-    return out
+def _stem_s2d(cv, cp):
+    """The stem's 7x7 stride-2 pad-3 weights as a 4x4 stride-1 pad-2 conv over the
+    2x2 space-to-depth input (channels (dy*2 + dx)*cp + c, c padded from cin to cp):
+    tap (ty, tx) with sub-pixel (dy, dx) is the original tap (2ty + dy - 1,
+    2tx + dx - 1), zero outside the 7x7 window. Output pixel (oy, ox) then reads
+    s2d pixels (oy - 2 + ty, ox - 2 + tx): exactly the original window, so every
+    int32 sum is unchanged."""
+    k = cv.k
+    q = cv.qw.q[:, :k * k * cv.cin].reshape(cv.cout, k, k, cv.cin)
+    out = np.zeros((cv.cout, 4, 4, 2, 2, cp), np.int8)
+    for ty in range(4):
+        for dy in range(2):
+            ky = 2 * ty + dy - 1
+            if not 0 <= ky < k:
+                continue
+            for tx in range(4):
+                for dx in range(2):
+                    kx = 2 * tx + dx - 1
+                    if 0 <= kx < k:
+                        out[:, ty, tx, dy, dx, :cv.cin] = q[:, ky, kx, :]
+    return out.reshape(cv.cout, 4 * 4 * 4 * cp)
 
 
 def build_resnet18(be, batch, spec: ResNetSpec):
-    """The stem input is held as NHWC with 4 channels (the 4th zero) and the stem
-    weights padded to match, so its im2col moves 4-byte chunks; outputs are
-    unchanged."""
+    """The stem input is held as 2x2 space-to-depth NHWC of the image padded to 4
+    channels ([112, 112, 16]); the 7x7/2 stem runs as the equivalent 4x4/1 conv
+    on it, so its gathers move 16-byte pixels. Outputs are unchanged (the same
+    integer sums)."""
+    assert spec.convs[0].k == 7 and spec.convs[0].stride == 2 and spec.convs[0].pad == 3
     p = Plan(be)
     handles = []
     STEM_C = 4
@@ -300,23 +312,25 @@ def build_resnet18(be, batch, spec: ResNetSpec):
     for i, cv in enumerate(spec.convs):
         q, cin = cv.qw.q, cv.cin
         if i == 0:
-            q, cin = _pad_channels(cv, STEM_C), STEM_C
+            q, cin = _stem_s2d(cv, STEM_C), 4 * STEM_C
         wh = be.upload_i8(np.ascontiguousarray(q), cv.qw.scales, cv.qw.n, q.shape[1])
         handles.append(wh)
         cins.append(cin)
     p.weights += handles
     x = p.tensor(F32, batch * 3 * 224 * 224)
     xq = p.tensor(I8, batch * 224 * 224 * STEM_C)
-    p.op(OP_NCHW_Q8, x, xq, dims=(batch, 3, 224 * 224, STEM_C))
+    p.op(OP_NCHW_Q8, x, xq, dims=(batch, 3, 224 * 224, STEM_C, 224, 2))
 
     def conv(inp_q, H, W, ci, act):
         cv = spec.convs[ci]
         OH, OW = _conv_out(H, cv.k, cv.stride, cv.pad), _conv_out(W, cv.k, cv.stride, cv.pad)
+        k, s, pad, ih, iw = cv.k, cv.stride, cv.pad, H, W
+        if ci == 0:  # the space-to-depth form of the stem
+            k, s, pad, ih, iw = 4, 1, 2, H // 2, W // 2
         M = batch * OH * OW
         kp = handles[ci].k
         col = p.tensor(I8, M * kp)
-        p.op(OP_IM2COL, inp_q, col, dims=(batch, H, W, cins[ci], cv.k, cv.k, cv.stride, cv.stride, cv.pad, cv.pad,
-                                         OH, OW, kp))
+        p.op(OP_IM2COL, inp_q, col, dims=(batch, ih, iw, cins[ci], k, k, s, s, pad, pad, OH, OW, kp))
         out = p.tensor(F32, M * cv.cout)
         p.op(OP_LINEAR, col, out, in1=p.const(cv.qw.bias), w=handles[ci], act=act, dims=(M,))
         return out, OH, OW
