@@ -180,7 +180,10 @@ def w4_tol(want):
 
 @pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 11008, 4096), (2, 100, 64),
                                    (5, 40, 96), (1, 8, 32), (24, 1000, 1024), (40, 300, 2048), (130, 300, 512),
-                                   (300, 129, 4096)])
+                                   (300, 129, 4096),
+                                   # decode GEMV: ragged groups, 3 / 11 / 12 K-slices, K beyond the ring
+                                   (2, 1001, 4096), (1, 4096, 11008), (2, 4096, 11008), (1, 77, 3072),
+                                   (2, 300, 12288), (1, 64, 16384)])
 def test_w4_gemm(cuda, m, n, k):
     x, p, s = w4_case(m, n, k)
     w = cuda.upload_i4(p, s, n, k)
@@ -198,6 +201,21 @@ def test_w4_gemm_m512_sampled(cuda):
     rows = np.unique(np.concatenate([[0, m - 1], np.random.default_rng(3).integers(0, m, 14)]))
     want = O.w4_gemm(x.reshape(m, k)[rows].ravel(), p, s, rows.size, n, k, threads=8).reshape(rows.size, n)
     assert np.max(np.abs(y[rows] - want)) <= w4_tol(want)
+    w.free()
+
+
+def test_w4_gemv_non_finite(cuda):
+    """inf / NaN activations propagate as in the reference's f32 matmul."""
+    m, n, k = 2, 300, 4096
+    x, p, s = w4_case(m, n, k, seed=700)
+    x[5] = np.inf
+    x[k + 100] = np.nan
+    w = cuda.upload_i4(p, s, n, k)
+    y = cuda.w4_gemm(x, m, k, w)
+    want = O.w4_gemm(x, p, s, m, n, k)
+    assert np.array_equal(np.isnan(y), np.isnan(want))
+    assert np.array_equal(np.isposinf(y), np.isposinf(want)) and np.array_equal(np.isneginf(y), np.isneginf(want))
+    assert np.isnan(want[n:]).all() and np.isinf(want[:n]).any()
     w.free()
 
 

@@ -213,6 +213,14 @@ __device__ __forceinline__ float apply_act(float y, int act) {
 // be scheduled while this one runs (its own pdl_wait still waits for this
 // kernel's completion).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Starts pulling [p, p + bytes) into L2 (the bulk copy unit, no registers, no
+// completion to wait for); p 16-byte aligned, bytes a multiple of 16. A hint
+// only: L2 is coherent with every write, so this may be issued before
+// pdl_wait() for buffers the predecessor could still be writing. Used for
+// weights before pdl_wait(), so their HBM stream overlaps the previous kernel.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <int ACT>

@@ -93,6 +93,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
         : "memory");
 }
 
+// Pulls the box at {x, y} of the tensor map into L2 (no shared memory, no
+// completion); a hint, coherent with every write, so it may run before
+// pdl_wait() for constant operands (weights).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *tm, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tm)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 

@@ -14,9 +14,10 @@
 // (quant.rs:192-204), uploaded once, never repacked.
 //
 // M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 128 == 0 and x is
-// 16-byte aligned. M <= 2 uses k_w4_gemv: one warp streams 8 weight rows with
-// 128-bit loads, reusing each activation chunk across the 8 rows. Other shapes
-// use the SIMT tile kernel.
+// 16-byte aligned. M <= 2 uses the bulk-copy ring GEMV with integer digit
+// planes (w4_gemv.cu) for K <= 12288, else k_w4_gemv: one warp streams 8
+// weight rows with 128-bit loads, reusing each activation chunk across the 8
+// rows. Other shapes use the SIMT tile kernel.
 #include <new>
 
 #include "common.cuh"
@@ -27,6 +28,8 @@ int launch_w4_simt(tpt_cuda_ctx *ctx, const float *x, const uint8_t *packed, con
                    int act, float *y, size_t m, size_t n, size_t k);
 int launch_w4_tc(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias, int act,
                  float *y, bool *handled);
+int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
+                       int act, float *y, bool *handled);
 
 namespace {
 
@@ -106,117 +109,6 @@ __global__ void __launch_bounds__(256) k_w4_gemv(const float *__restrict__ X, co
     }
 }
 
-// W4 GEMV v2 (M <= 2, K % 1024 == 0, K <= 8192): the K range is split over the
-// block's KW = K / 1024 warps; lane l of warp w owns the 16 nibble bytes
-// [w*512 + 16 l, +16) of every row (32 k) and keeps its 32 activations (per
-// activation row) in registers across all rows. A block takes 8 rows per step:
-// 8 independent 16-byte loads per lane in flight, each nibble decoded with
-// one LOP3 + FADD (the bits (u ^ 8) | 0x4B000000 are exactly 2^23 + v + 8), one
-// FFMA per activation row; warp sums go through shared memory and are added in
-// warp order, so the result does not depend on the launch shape. The grid is a
-// few blocks per SM, each streaming a run of row groups with the next group's
-// loads issued before the current group's arithmetic (a two-deep register
-// pipeline), so the nibble stream and the decode overlap.
-constexpr int W4V_ROWS = 8;
-template <int MM>
-__global__ void __launch_bounds__(256) k_w4_gemv2(const float *__restrict__ X, const uint8_t *__restrict__ Wp,
-                                                  const float *__restrict__ scales, const float *__restrict__ bias,
-                                                  int M, int N, int K, int act, float *__restrict__ Y) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ float part[8][MM][W4V_ROWS];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int KW = K >> 10;  // warps along K (blockDim.x / 32 == KW)
-    const size_t row_bytes = (size_t)K >> 1;
-    const int kbase = warp * 1024 + lane * 32;  // this lane's first k
-    float xr[MM][32];
-#pragma unroll
-    for (int i = 0; i < MM; i++) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (i < M) t = __ldg(reinterpret_cast<const float4 *>(X + (size_t)i * K + kbase + j));
-            xr[i][j] = t.x;
-            xr[i][j + 1] = t.y;
-            xr[i][j + 2] = t.z;
-            xr[i][j + 3] = t.w;
-        }
-    }
-    // keep the activations in registers for the whole kernel (otherwise they
-    // are re-read from L1 next to every FMA)
-#pragma unroll
-    for (int i = 0; i < MM; i++)
-#pragma unroll
-        for (int j = 0; j < 32; j++) asm volatile("" : "+f"(xr[i][j]));
-    const int groups = (N + W4V_ROWS - 1) / W4V_ROWS;
-    auto load_group = [&](int g, uint4 (&dst)[W4V_ROWS]) {
-#pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++) {
-            const int n = g * W4V_ROWS + r < N ? g * W4V_ROWS + r : N - 1;
-            dst[r] = __ldcs(reinterpret_cast<const uint4 *>(Wp + (size_t)n * row_bytes + (kbase >> 1)));
-        }
-        // all eight loads are issued before any use (the compiler would
-        // otherwise interleave them with the arithmetic, one load in flight)
-#pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++)
-            asm volatile("" : "+r"(dst[r].x), "+r"(dst[r].y), "+r"(dst[r].z), "+r"(dst[r].w));
-    };
-    uint4 w[W4V_ROWS];
-    if ((int)blockIdx.x < groups) load_group(blockIdx.x, w);
-    for (int gi = blockIdx.x; gi < groups; gi += gridDim.x) {
-        const int n0 = gi * W4V_ROWS;
-        uint4 wn[W4V_ROWS];
-        if (gi + (int)gridDim.x < groups) load_group(gi + gridDim.x, wn);
-        float acc[MM][W4V_ROWS];
-#pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++) {
-#pragma unroll
-            for (int i = 0; i < MM; i++) acc[i][r] = 0.0f;
-            const uint32_t words[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                // (v + 8) per nibble; even / odd nibbles of the 4 bytes as byte planes
-                const uint32_t u = words[q] ^ 0x88888888u;
-                const uint32_t even = u & 0x0F0F0F0Fu, odd = (u >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                for (int bb = 0; bb < 4; bb++) {  // byte bb holds k = 8q + 2bb (low) and 8q + 2bb + 1 (high)
-                    // bytes [plane byte bb, 0, 0, 0x4B]: the float 2^23 + v + 8, exactly
-                    const float v0 = __uint_as_float(__byte_perm(even, 0x4B000000u, 0x7440 + bb)) - 8388616.0f;
-                    const float v1 = __uint_as_float(__byte_perm(odd, 0x4B000000u, 0x7440 + bb)) - 8388616.0f;
-#pragma unroll
-                    for (int i = 0; i < MM; i++) {
-                        acc[i][r] = fmaf(xr[i][8 * q + 2 * bb], v0, acc[i][r]);
-                        acc[i][r] = fmaf(xr[i][8 * q + 2 * bb + 1], v1, acc[i][r]);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++)
-#pragma unroll
-            for (int i = 0; i < MM; i++) acc[i][r] = warp_sum(acc[i][r]);
-        if (lane == 0)
-#pragma unroll
-            for (int r = 0; r < W4V_ROWS; r++)
-#pragma unroll
-                for (int i = 0; i < MM; i++) part[warp][i][r] = acc[i][r];
-        __syncthreads();
-        if ((int)threadIdx.x < W4V_ROWS * MM) {
-            const int r = threadIdx.x % W4V_ROWS, i = threadIdx.x / W4V_ROWS, n = n0 + r;
-            if (n < N && i < M) {
-                float s = 0.0f;
-                for (int ww = 0; ww < KW; ww++) s += part[ww][i][r];
-                float y = s * __ldg(scales + n);
-                if (bias) y += __ldg(bias + n);
-                Y[(size_t)i * N + n] = apply_act(y, act);
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < W4V_ROWS; r++) w[r] = wn[r];
-    }
-}
-
 }  // namespace
 
 int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias, int act,
@@ -230,16 +122,10 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
         int st = launch_w4_tc(ctx, x, m, w, bias, act, y, &handled);
         if (st || handled) return st;
     }
-    if (m <= 2 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)p & 15) == 0 && k % 1024 == 0 && k <= 8192) {
-        const int kw = (int)(k / 1024);
-        const size_t groups = (n + W4V_ROWS - 1) / W4V_ROWS;
-        const size_t per_sm = m == 1 ? 3 : 2;  // blocks that fit one SM at the kernel's register count
-        const unsigned g = (unsigned)(groups < (size_t)ctx->sm_count * per_sm ? groups : (size_t)ctx->sm_count * per_sm);
-        if (m == 1)
-            k_w4_gemv2<1><<<g, 32 * kw, 0, ctx->stream>>>(x, p, w->scales, bias, (int)m, (int)n, (int)k, act, y);
-        else
-            k_w4_gemv2<2><<<g, 32 * kw, 0, ctx->stream>>>(x, p, w->scales, bias, (int)m, (int)n, (int)k, act, y);
-        return after_launch(ctx, "w4_gemv");
+    if (m <= 2) {
+        bool handled = false;
+        int st = launch_w4_gemv_tma(ctx, x, m, w, bias, act, y, &handled);
+        if (st || handled) return st;
     }
     if (m <= 2 && ((uintptr_t)x & 15) == 0) {
         size_t warps = (n + W4_ROWS - 1) / W4_ROWS;

@@ -1,0 +1,379 @@
+// w4_gemv.cu -- INT4-weight GEMV for decode-like M <= 2: the nibble stream is
+// moved by the bulk-copy unit into a shared-memory ring and multiplied in
+// integer arithmetic against activation digit planes.
+//
+// Reference semantics: dequantize_i4_symmetric_per_channel then the f32 matmul
+// (crates/tpt-infer-quantize/src/dequant.rs:56-71, crates/tpt-infer-ops/src/
+// avx512.rs:55-78): y[m,n] = sum_k x[m,k] * (q[n,k] * s[n]) + bias[n], then act.
+//
+// Numerics. Each activation row is split, per slice of 512 k, into three signed
+// 8-bit digit planes:
+//   x_k = s (d0_k + d1_k / 128 + d2_k / 16384) (1 + e),  s = max_slice |x| / 127,
+//   t = x * (127 / max|x|), d0 = rint(t), d1 = rint((t - d0) 128),
+//   d2 = rint(((t - d0) 128 - d1) 128)
+// (both residual steps are exact in f32), so each activation is represented to
+// s / 32768 plus one f32 rounding. The weights enter as q + 8 in [0, 15]
+// (unsigned bytes); the sums sum_k (q_k + 8) d_p,k are exact in i32 and start
+// from -8 sum_k d_p,k, which removes the +8. Per row and slice the three plane
+// sums A_p are combined as s (A0 + (A1 + A2 / 128) / 128) in f32 (A0 is below
+// 2^24, exact). Against the f32 dot product this differs by the digit error (at
+// most 8 * 512 * s / 32768 per slice, far inside the 1e-3 x output-step bound)
+// and f32 rounding. A slice holding a non-finite activation is computed as the
+// f32 dot product instead, so inf and NaN propagate as in the reference.
+//
+// The integer products run on mma.sync m16n8k32 (u8 x s8 -> s32): one
+// instruction multiplies 16 weight rows x 32 k by the 8 columns {3 digit planes
+// per activation row, zeros}, i.e. 1.5 k multiply-adds of useful work, where a
+// dp4a does 4. A weight word (8 nibbles, low first) becomes the two A-fragment
+// words of its row with one LOP3 each (even k, odd k); the digit words are
+// packed in the same even / odd order, so B's k order matches. The tcgen05 MMA
+// is not used here: at N = 8 its per-instruction cost, not the arithmetic,
+// would bound an HBM-speed GEMV, while the register-fragment MMA issues from
+// the warps that decode the nibbles.
+//
+// Data movement. A CTA takes a contiguous run of 16-row groups. Before its
+// dependency wait it has set up its barriers; then one producer thread streams
+// the groups with cp.async.bulk (one copy per row, no multicast) into an
+// S-stage ring guarded by full / empty mbarriers, each row padded by 16 bytes
+// so that the fragment loads (8 rows x 4 words per warp) hit 32 distinct banks.
+// Consumer warp w owns k slice w (512 k) of every row: per stage 16 MMAs, then
+// the plane sums are combined and the row's slice sum goes to a shared buffer;
+// the buffered groups are combined (slice sums added in slice order, so the
+// result does not depend on the launch shape, then scale, bias, act) once per
+// P groups, normally once per CTA. All waits are bounded.
+#include "tc_common.cuh"
+
+namespace tpt {
+
+namespace {
+using namespace tc;
+
+constexpr int WG_ROWS = 16;    // weight rows per group (one ring stage; the MMA's M)
+constexpr int WG_SLICE = 512;  // k per consumer warp
+constexpr int WG_MAX_KW = 16;  // K <= 8192
+constexpr int WG_RING_BUDGET = 160 * 1024;
+constexpr int WG_PART_BUDGET = 12 * 1024;
+constexpr int WG_SMEM_MAX = 200 * 1024;
+constexpr int WG_MAX_THREADS = 32 * (WG_MAX_KW + 1);
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// D += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulate
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int MM>
+__global__ void __launch_bounds__(WG_MAX_THREADS, 1)
+    k_w4_gemv_tma(const float *__restrict__ X, const uint8_t *__restrict__ Wp, const float *__restrict__ scales,
+                  const float *__restrict__ bias, int M, int N, int K, int act, float *__restrict__ Y, int S, int P,
+                  unsigned *gflags) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int KW = (K + WG_SLICE - 1) / WG_SLICE;  // consumer warps; warp KW is the producer
+    const uint32_t row_bytes = (uint32_t)K >> 1, row_pitch = row_bytes + 16u, stage_bytes = WG_ROWS * row_pitch;
+    const int groups = (N + WG_ROWS - 1) / WG_ROWS;
+    const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
+    const int g1 = (int)((long long)(blockIdx.x + 1) * groups / gridDim.x);
+    const uint32_t ring = smem_u32(smem);
+    // per consumer warp: digit words [MM][3 planes][32 chunks][4 words]
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (size_t)S * stage_bytes);
+    float *part = reinterpret_cast<float *>(tab + KW * MM * 3 * 32 * 4);  // [P][MM][KW][16]
+    const uint32_t bars = smem_u32(part + P * MM * KW * WG_ROWS);
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), (uint32_t)KW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_wait();  // X (the previous kernel's output) is complete from here on
+    pdl_trigger();
+    volatile int *abort_p = &abort_flag;
+
+    if (warp == KW) {
+        if (lane == 0) {
+            // ---------------- bulk-copy producer ----------------
+            int s = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            for (int g = g0; g < g1; g++) {
+                if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_p, gflags, true)) break;
+                const int rows = min(WG_ROWS, N - g * WG_ROWS);
+                mbar_arrive_expect_tx(full_bar(s), (uint32_t)rows * row_bytes);
+                const uint8_t *src = Wp + (size_t)g * WG_ROWS * row_bytes;
+                for (int r = 0; r < rows; r++)
+                    bulk_load(ring + (uint32_t)s * stage_bytes + (uint32_t)r * row_pitch, src + (size_t)r * row_bytes,
+                              row_bytes, full_bar(s));
+                issued |= 1u << s;
+                last_ph = (last_ph & ~(1u << s)) | (ph << s);
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+            // our copies in flight land before the CTA can exit
+            for (int t = 0; t < S; t++)
+                if (issued & (1u << t)) mbar_wait(full_bar(t), (last_ph >> t) & 1u, abort_p, gflags, false);
+        }
+        return;
+    }
+    if (warp > KW) return;
+
+    // ---------------- consumers: warp = k slice ----------------
+    const int ncons = KW * 32;
+    const int gq = lane >> 2, tq = lane & 3;  // MMA fragment group / thread in group
+    const int kslice = warp * WG_SLICE;
+    const int ksteps = min(WG_SLICE, K - kslice) / 32;
+    uint32_t *mytab = tab + warp * MM * 3 * 32 * 4;
+    // Digits of this slice: lane c splits k [kslice + 16 c, +16) of each row.
+    float sx[MM];  // slice scale (NaN: the slice holds a non-finite activation)
+    int corr[MM][3];
+#pragma unroll
+    for (int i = 0; i < MM; i++) {
+        const int kb = kslice + 16 * lane;
+        float xv[16];
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < M && kb < K) t = __ldg(reinterpret_cast<const float4 *>(X + (size_t)i * K + kb + j));
+            xv[j] = t.x;
+            xv[j + 1] = t.y;
+            xv[j + 2] = t.z;
+            xv[j + 3] = t.w;
+        }
+        float amax = 0.0f;
+        bool fin = true;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const float a = fabsf(xv[j]);
+            fin = fin && a <= 3.402823466e38f;  // false for inf and NaN
+            amax = fmaxf(amax, a);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        fin = __all_sync(0xffffffffu, fin);
+        const float s = __fdiv_rn(amax, 127.0f), inv = __fdiv_rn(127.0f, amax);
+        const bool live = fin && s > 0.0f && inv <= 3.402823466e38f;
+        sx[i] = !fin ? __int_as_float(0x7fc00000) : live ? s : 0.0f;
+        // Rounding by an addend of 1.5 * 2^23: t + 1.5 * 2^23 lands in
+        // [2^23, 2^24), whose ulp is 1, so it rounds t to the nearest integer
+        // (ties to even, as rint), its low mantissa byte is that integer mod
+        // 256 (the digit as a signed byte), and subtracting the addend back
+        // gives rint(t) exactly.
+        constexpr float RND = 12582912.0f;
+        uint32_t bits[3][16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const float t = live ? xv[j] * inv : 0.0f;
+            const float f0 = t + RND;
+            const float r1 = (t - (f0 - RND)) * 128.0f;
+            const float f1 = r1 + RND;
+            const float f2 = (r1 - (f1 - RND)) * 128.0f + RND;
+            bits[0][j] = __float_as_uint(f0);
+            bits[1][j] = __float_as_uint(f1);
+            bits[2][j] = __float_as_uint(f2);
+        }
+        // chunk word 2q (+1 for odd): the digits of k = 8q + 2bb (+1), bb = 0..3
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            uint32_t wd[4];
+            int sum = 0;
+#pragma unroll
+            for (int wi = 0; wi < 4; wi++) {
+                const int j0 = 8 * (wi >> 1) + (wi & 1);
+                const uint32_t lo = __byte_perm(bits[p][j0], bits[p][j0 + 2], 0x0040);
+                const uint32_t hi = __byte_perm(bits[p][j0 + 4], bits[p][j0 + 6], 0x0040);
+                wd[wi] = __byte_perm(lo, hi, 0x5410);
+                sum = __dp4a((int)wd[wi], 0x01010101, sum);
+            }
+            *reinterpret_cast<uint4 *>(mytab + ((i * 3 + p) * 32 + lane) * 4) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            corr[i][p] = -8 * sum;
+        }
+    }
+    __syncwarp();
+    // B fragments of the 16 k-steps: column gq = (activation row, plane) or
+    // zero; k-step j, word t of B = chunk 2j + t/2, quad t%2 (even, odd word)
+    uint32_t bf[16][2];
+    const int bi = gq / 3, bp = gq - 3 * (gq / 3);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        bf[j][0] = bf[j][1] = 0u;
+        if (gq < 3 * MM) {
+            const uint32_t *src = mytab + ((bi * 3 + bp) * 32 + 2 * j + (tq >> 1)) * 4 + 2 * (tq & 1);
+            bf[j][0] = src[0];
+            bf[j][1] = src[1];
+        }
+    }
+    // accumulator init: column 2 tq + e holds -8 sum_k d of its (row, plane)
+    int cinit[2];
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int col = 2 * tq + e;
+        int v = 0;
+#pragma unroll
+        for (int i = 0; i < MM; i++)
+#pragma unroll
+            for (int p = 0; p < 3; p++)
+                if (col == 3 * i + p) v = corr[i][p];
+        cinit[e] = v;
+    }
+    const bool slow = isnan(sx[0]) || (MM > 1 && isnan(sx[MM - 1]));
+
+    // Row sums are buffered per group in part[P][MM][KW][16] and combined P
+    // groups at a time (all scale / bias loads of a flush in flight together,
+    // no per-group barrier).
+    int s = 0, gl = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int g = g0; g < g1; g++) {
+        if (ok) ok = mbar_wait(full_bar(s), ph, abort_p, gflags, true);
+        int d[4] = {cinit[0], cinit[1], cinit[0], cinit[1]};
+        const uint32_t base = ring + (uint32_t)s * stage_bytes + (uint32_t)gq * row_pitch + (uint32_t)(kslice >> 1) +
+                              4u * tq;
+        if (ok) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                if (j < ksteps) {
+                    const uint32_t w0 = lds32(base + 16u * j), w1 = lds32(base + 8u * row_pitch + 16u * j);
+                    uint32_t a[4];
+                    a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq, even k: q + 8
+                    a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq + 8, even k
+                    a[2] = ((w0 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq, odd k
+                    a[3] = ((w1 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq + 8, odd k
+                    mma_u8s8(d, a, bf[j][0], bf[j][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(empty_bar(s));
+        // d: rows gq (d0, d1) and gq + 8 (d2, d3), columns 2 tq, 2 tq + 1.
+        // Activation row 0 = columns 0..2 (tq 0: A0 A1; tq 1: A2 in d0 / d2),
+        // row 1 = columns 3..5 (tq 1: A0 in d1 / d3; tq 2: A1 A2).
+        const int nx0 = __shfl_down_sync(0xffffffffu, d[0], 1), nx2 = __shfl_down_sync(0xffffffffu, d[2], 1);
+        const int px1 = __shfl_up_sync(0xffffffffu, d[1], 1), px3 = __shfl_up_sync(0xffffffffu, d[3], 1);
+        float v[2] = {0.0f, 0.0f};
+        int vi = -1;
+        if (tq == 0) {
+            vi = 0;
+            v[0] = sx[0] * fmaf(fmaf((float)nx0, 0.0078125f, (float)d[1]), 0.0078125f, (float)d[0]);
+            v[1] = sx[0] * fmaf(fmaf((float)nx2, 0.0078125f, (float)d[3]), 0.0078125f, (float)d[2]);
+        } else if (MM > 1 && tq == 2) {
+            vi = 1;
+            v[0] = sx[MM - 1] * fmaf(fmaf((float)d[1], 0.0078125f, (float)d[0]), 0.0078125f, (float)px1);
+            v[1] = sx[MM - 1] * fmaf(fmaf((float)d[3], 0.0078125f, (float)d[2]), 0.0078125f, (float)px3);
+        }
+        if (slow && vi >= 0 && isnan(sx[vi])) {  // non-finite activations: the slice's f32 dot product
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t rowp = ring + (uint32_t)s * stage_bytes + (uint32_t)(gq + 8 * h) * row_pitch +
+                                      (uint32_t)(kslice >> 1);
+                float acc = 0.0f;
+                if (vi < M && ok)
+                    for (int kk = 0; kk < ksteps * 32; kk++) {
+                        const uint32_t wd = lds32(rowp + 4u * (kk >> 3));
+                        const int nb = (int)((wd >> (4 * (kk & 7))) & 0xFu);
+                        acc = fmaf(__ldg(X + (size_t)vi * K + kslice + kk), (float)(nb - ((nb & 8) << 1)), acc);
+                    }
+                v[h] = acc;
+            }
+        }
+        if (vi >= 0) {
+            float *dst = part + ((gl * MM + vi) * KW + warp) * WG_ROWS;
+            dst[gq] = v[0];
+            dst[gq + 8] = v[1];
+        }
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+        }
+        if (++gl == P || g + 1 == g1) {  // flush: combine the buffered groups
+            ok = bar_and(1, ncons, ok);   // every consumer's sums are in part
+            if (ok) {
+                const int gb = g + 1 - gl;  // first buffered group
+                for (int idx = (int)threadIdx.x; idx < gl * WG_ROWS * MM; idx += ncons) {
+                    const int r = idx % WG_ROWS, i = (idx / WG_ROWS) % MM, gi = idx / (WG_ROWS * MM);
+                    const int n = (gb + gi) * WG_ROWS + r;
+                    if (n >= N || i >= M) continue;
+                    float acc = 0.0f;
+                    for (int sl = 0; sl < KW; sl++) acc += part[((gi * MM + i) * KW + sl) * WG_ROWS + r];
+                    float y = acc * __ldg(scales + n);
+                    if (bias) y += __ldg(bias + n);
+                    Y[(size_t)i * N + n] = apply_act(y, act);
+                }
+            }
+            bar_sync(1, ncons);  // part is free again
+            gl = 0;
+        }
+    }
+}
+
+template <int MM>
+int launch_one(tpt_cuda_ctx *ctx, const float *x, const uint8_t *p, const float *scales, const float *bias, int act,
+               float *y, int n, int k, int S, int P, size_t smem) {
+    static bool attr_done[64] = {};
+    auto kfn = k_w4_gemv_tma<MM>;
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, WG_SMEM_MAX + 1024);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "w4_gemv smem attribute");
+        attr_done[dev] = true;
+    }
+    const int kw = (k + WG_SLICE - 1) / WG_SLICE, groups = (n + WG_ROWS - 1) / WG_ROWS;
+    const unsigned grid = (unsigned)(groups < ctx->sm_count ? groups : ctx->sm_count);  // one CTA per SM
+    launch_pdl(kfn, grid, 32 * (kw + 1), smem, ctx->stream, x, p, scales, bias, MM, n, k, act, y, S, P, ctx->d_flags);
+    return after_launch(ctx, "w4_gemv_tma");
+}
+
+}  // namespace
+
+// M <= 2, K % 32 == 0, K <= 8192, x and the nibbles 16-byte aligned; returns
+// handled = false otherwise.
+int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
+                       int act, float *y, bool *handled) {
+    *handled = false;
+    const size_t n = w->n, k = w->k;
+    const uint8_t *p = (const uint8_t *)w->data;
+    if (m == 0 || m > 2 || k % 32 != 0 || k > (size_t)WG_MAX_KW * WG_SLICE || n > INT32_MAX) return TPT_OK;
+    if (((uintptr_t)x & 15) != 0 || ((uintptr_t)p & 15) != 0) return TPT_OK;
+    const int kw = (int)((k + WG_SLICE - 1) / WG_SLICE);
+    const int MM = (int)m;
+    const size_t stage = WG_ROWS * (k / 2 + 16), table = (size_t)kw * MM * 3 * 32 * 16;
+    const size_t ring = WG_RING_BUDGET < WG_SMEM_MAX - table - WG_PART_BUDGET ? WG_RING_BUDGET
+                                                                              : WG_SMEM_MAX - table - WG_PART_BUDGET;
+    const int S = (int)(ring / stage < 8 ? ring / stage : 8);
+    if (S < 2) return TPT_OK;
+    // groups buffered between flushes: all of a CTA's run when they fit
+    const size_t per_group = (size_t)MM * kw * WG_ROWS * 4;
+    const size_t groups = (n + WG_ROWS - 1) / WG_ROWS;
+    const size_t ctas = groups < (size_t)ctx->sm_count ? groups : (size_t)ctx->sm_count;
+    const size_t run = (groups + ctas - 1) / ctas;
+    const int P = (int)(run < WG_PART_BUDGET / per_group ? run : WG_PART_BUDGET / per_group);
+    const size_t smem = (size_t)S * stage + table + (size_t)P * per_group + (size_t)2 * S * 8;
+    *handled = true;
+    return MM == 1 ? launch_one<1>(ctx, x, p, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
+                   : launch_one<2>(ctx, x, p, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
+}
+
+}  // namespace tpt

@@ -57,12 +57,17 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                                                    int M, int N, int K, float a_scale, int act,
                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
                                                    int8_t *__restrict__ Q, float q_scale) {
-    pdl_wait();
-    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = K >> 4;  // 16-byte chunks per row
+    // this warp's weight rows start streaming into L2 while the previous
+    // kernel on the stream finishes (the grid is small enough to be resident
+    // beside it); the loads below then hit L2
+    for (int n = warp + lane * nwarps; n < N; n += 32 * nwarps)
+        for (int c = 0; c < K; c += 32768) prefetch_l2_bulk(Wt + (size_t)n * K + c, (uint32_t)min(K - c, 32768));
+    pdl_wait();
+    pdl_trigger();
     int4 ar[A_REG ? MM : 1][GEMV_CH];
     if (A_REG) {
 #pragma unroll
@@ -232,7 +237,9 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     const int8_t *wt = (const int8_t *)w->data;
     if (m <= 4) {
         // decode-like: SIMT stream of the weight rows (HBM-bound)
-        unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 8);
+        // two 8-warp blocks per SM: the next launch's blocks fit beside them
+        // and prefetch their weights while this one runs
+        unsigned g = grid_1d(n * 32, 256, (unsigned)ctx->sm_count * 2);
         const bool areg = k <= (size_t)GEMV_CH * 32 * 16;
 #define TPT_GEMV(MM, AR) \
     launch_pdl(k_w8a8_gemv<MM, AR>, g, 256, 0, ctx->stream, a, wt, w->scales, bias, (int)m, (int)n, (int)k, a_scale, act, y, acc, \

@@ -52,7 +52,9 @@ struct CkCfg {
     static constexpr int W_BYTES = CK_TM * CK_BK;
     static constexpr int A_BYTES = BN * CK_BK;
     static constexpr int STAGE_BYTES = W_BYTES + A_BYTES;  // multiple of 1024
-    static constexpr int STAGES = 8;
+    // BN <= 32: small enough for two CTAs per SM, so the next launch's CTAs
+    // are resident early and pull their weights into L2 during this one
+    static constexpr int STAGES = BN == 16 ? 5 : BN == 32 ? 4 : 8;
     static constexpr int RECV_BYTES = CK_TM * BN * 4;      // KS partials of 128/KS rows each
     static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + RECV_BYTES + (2 * STAGES + 3) * 8 + 1024;
@@ -128,6 +130,9 @@ __global__ void __launch_bounds__(CK_THREADS, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        // this CTA's weight boxes start streaming into L2 while the previous
+        // kernel finishes; the ring's loads below then come from L2
+        for (int kb = kb0; kb < kb1; kb++) tma_prefetch_l2_2d(&tmW, kb * CK_BK, wt * CK_TM);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
