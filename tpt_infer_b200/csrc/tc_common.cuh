@@ -10,6 +10,9 @@
 #include "common.cuh"
 
 namespace tpt {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();  // null when the driver lacks it
+
 namespace tc {
 
 // Bound of one wait in SM clock cycles: about 1 s at the B200's 1.965 GHz

@@ -14,8 +14,8 @@
 // (quant.rs:192-204), uploaded once, never repacked.
 //
 // M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 128 == 0 and x is
-// 16-byte aligned. M <= 2 uses the bulk-copy ring GEMV with integer digit
-// planes (w4_gemv.cu) for K <= 12288, else k_w4_gemv: one warp streams 8
+// 16-byte aligned. M <= 2 uses the TMA-ring GEMV with integer digit planes
+// (w4_gemv.cu) for K % 256 == 0, K <= 8192, else k_w4_gemv: one warp streams 8
 // weight rows with 128-bit loads, reusing each activation chunk across the 8
 // rows. Other shapes use the SIMT tile kernel.
 #include <new>

@@ -1,6 +1,6 @@
 // w4_gemv.cu -- INT4-weight GEMV for decode-like M <= 2: the nibble stream is
-// moved by the bulk-copy unit into a shared-memory ring and multiplied in
-// integer arithmetic against activation digit planes.
+// moved by the TMA unit into a shared-memory ring and multiplied in integer
+// arithmetic against activation digit planes.
 //
 // Reference semantics: dequantize_i4_symmetric_per_channel then the f32 matmul
 // (crates/tpt-infer-quantize/src/dequant.rs:56-71, crates/tpt-infer-ops/src/
@@ -29,18 +29,22 @@
 // packed in the same even / odd order, so B's k order matches. The tcgen05 MMA
 // is not used here: at N = 8 its per-instruction cost, not the arithmetic,
 // would bound an HBM-speed GEMV, while the register-fragment MMA issues from
-// the warps that decode the nibbles.
+// the warps that decode the nibbles. Four independent accumulator sets keep
+// four MMAs in flight per warp (their i32 sums are added exactly).
 //
-// Data movement. A CTA takes a contiguous run of 16-row groups. Before its
-// dependency wait it has set up its barriers; then one producer thread streams
-// the groups with cp.async.bulk (one copy per row, no multicast) into an
-// S-stage ring guarded by full / empty mbarriers, each row padded by 16 bytes
-// so that the fragment loads (8 rows x 4 words per warp) hit 32 distinct banks.
-// Consumer warp w owns k slice w (512 k) of every row: per stage 16 MMAs, then
-// the plane sums are combined and the row's slice sum goes to a shared buffer;
-// the buffered groups are combined (slice sums added in slice order, so the
-// result does not depend on the launch shape, then scale, bias, act) once per
-// P groups, normally once per CTA. All waits are bounded.
+// Data movement. A CTA takes a contiguous run of 16-row groups; one producer
+// thread streams them, one TMA tensor load per group (a 3-D view of the nibble
+// matrix: 16 rows x 128 bytes per 128-byte column, 128B-swizzled, no
+// multicast), into an S-stage ring guarded by full / empty mbarriers, the first
+// S groups before the kernel's dependency wait (two CTAs fit one SM, so under
+// programmatic dependent launch the next GEMV's first stages arrive while this
+// one computes). The swizzle puts the 8 rows of a fragment load (8 rows x 4
+// words per warp) in 32 distinct banks. Consumer warp w owns k slice w (512 k)
+// of every row: per stage 16 MMAs, then the plane sums are combined and the
+// row's slice sum goes to a shared buffer; the buffered groups are combined
+// (slice sums added in slice order, so the result does not depend on the
+// launch shape, then scale, bias, act) once per P groups, normally once per
+// CTA. All waits are bounded.
 #include "tc_common.cuh"
 
 namespace tpt {
@@ -51,15 +55,26 @@ using namespace tc;
 constexpr int WG_ROWS = 16;    // weight rows per group (one ring stage; the MMA's M)
 constexpr int WG_SLICE = 512;  // k per consumer warp
 constexpr int WG_MAX_KW = 16;  // K <= 8192
-constexpr int WG_RING_BUDGET = 160 * 1024;
 constexpr int WG_PART_BUDGET = 12 * 1024;
+constexpr int WG_SMEM_PAIR = 112 * 1024;  // two CTAs per SM: the next launch's CTA streams beside this one
 constexpr int WG_SMEM_MAX = 200 * 1024;
 constexpr int WG_MAX_THREADS = 32 * (WG_MAX_KW + 1);
 
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
+// One stage: rows [y, y + 16) x all K/2 bytes, as 16-row x 128-byte boxes per
+// 128-byte column (3-D view {128 B, rows, columns}), 128B-swizzled.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(0), "r"(y), "r"(0)
+        : "memory");
+}
+
+// byte offset of (row, byte b of the row) in a stage: column b / 128 holds 16
+// rows of 128 bytes; the 16-byte unit u of row r sits at u ^ (r & 7)
+__device__ __forceinline__ uint32_t stage_off(int row, uint32_t b) {
+    return (b >> 7) * (WG_ROWS * 128u) + (uint32_t)row * 128u + ((((b >> 4) & 7u) ^ (uint32_t)(row & 7)) << 4) +
+           (b & 15u);
 }
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
@@ -79,22 +94,23 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
 
 template <int MM>
 __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
-    k_w4_gemv_tma(const float *__restrict__ X, const uint8_t *__restrict__ Wp, const float *__restrict__ scales,
-                  const float *__restrict__ bias, int M, int N, int K, int act, float *__restrict__ Y, int S, int P,
-                  unsigned *gflags) {
+    k_w4_gemv_tma(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
+                  const float *__restrict__ scales, const float *__restrict__ bias, int M, int N, int K, int act,
+                  float *__restrict__ Y, int S, int P, unsigned *gflags) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int abort_flag;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int KW = (K + WG_SLICE - 1) / WG_SLICE;  // consumer warps; warp KW is the producer
-    const uint32_t row_bytes = (uint32_t)K >> 1, row_pitch = row_bytes + 16u, stage_bytes = WG_ROWS * row_pitch;
+    const uint32_t stage_bytes = (uint32_t)K * 8u;   // 16 rows x K/2 bytes
     const int groups = (N + WG_ROWS - 1) / WG_ROWS;
     const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
     const int g1 = (int)((long long)(blockIdx.x + 1) * groups / gridDim.x);
-    const uint32_t ring = smem_u32(smem);
-    // per consumer warp: digit words [MM][3 planes][32 chunks][4 words]
-    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (size_t)S * stage_bytes);
-    float *part = reinterpret_cast<float *>(tab + KW * MM * 3 * 32 * 4);  // [P][MM][KW][16]
-    const uint32_t bars = smem_u32(part + P * MM * KW * WG_ROWS);
+    const uint32_t raw = smem_u32(smem), ring = (raw + 1023u) & ~1023u;  // 128B swizzle: 1 KB aligned
+    // per consumer warp: digit words [MM][3 planes][32 chunks][4 words]; the
+    // same bytes later hold the slice sums part[P][MM][KW][16]
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (ring - raw) + (size_t)S * stage_bytes);
+    float *part = reinterpret_cast<float *>(tab);
+    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * 4, P * MM * KW * WG_ROWS));
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
 
@@ -105,31 +121,38 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
             mbar_init(empty_bar(s), (uint32_t)KW);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
     }
     __syncthreads();
-    pdl_wait();  // X (the previous kernel's output) is complete from here on
-    pdl_trigger();
     volatile int *abort_p = &abort_flag;
 
     if (warp == KW) {
         if (lane == 0) {
-            // ---------------- bulk-copy producer ----------------
+            // ---------------- TMA producer ----------------
+            // The first S groups are requested before the dependency wait: the
+            // nibbles are constants (written only by host uploads, which a
+            // programmatic launch never overlaps), so they stream while the
+            // previous kernel finishes.
             int s = 0;
             uint32_t ph = 0, issued = 0, last_ph = 0;
             for (int g = g0; g < g1; g++) {
+                if (g == g0 + S) {
+                    pdl_wait();
+                    pdl_trigger();
+                }
                 if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_p, gflags, true)) break;
-                const int rows = min(WG_ROWS, N - g * WG_ROWS);
-                mbar_arrive_expect_tx(full_bar(s), (uint32_t)rows * row_bytes);
-                const uint8_t *src = Wp + (size_t)g * WG_ROWS * row_bytes;
-                for (int r = 0; r < rows; r++)
-                    bulk_load(ring + (uint32_t)s * stage_bytes + (uint32_t)r * row_pitch, src + (size_t)r * row_bytes,
-                              row_bytes, full_bar(s));
+                mbar_arrive_expect_tx(full_bar(s), stage_bytes);  // the whole box, rows past N read as 0
+                tma_load_3d(ring + (uint32_t)s * stage_bytes, &tmW, full_bar(s), g * WG_ROWS);
                 issued |= 1u << s;
                 last_ph = (last_ph & ~(1u << s)) | (ph << s);
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
                 }
+            }
+            if (g1 - g0 <= S) {
+                pdl_wait();
+                pdl_trigger();
             }
             // our copies in flight land before the CTA can exit
             for (int t = 0; t < S; t++)
@@ -138,6 +161,8 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         return;
     }
     if (warp > KW) return;
+    pdl_wait();  // X (the previous kernel's output) is complete from here on
+    pdl_trigger();
 
     // ---------------- consumers: warp = k slice ----------------
     const int ncons = KW * 32;
@@ -240,6 +265,18 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         cinit[e] = v;
     }
     const bool slow = isnan(sx[0]) || (MM > 1 && isnan(sx[MM - 1]));
+    // When one flush covers the CTA's run and every output has a thread, each
+    // thread's channel scale and bias are loaded now, off the flush's path.
+    const bool one_flush = P >= g1 - g0 && (g1 - g0) * WG_ROWS * MM <= ncons;
+    float my_sc = 0.0f, my_bi = 0.0f;
+    if (one_flush) {
+        const int idx = (int)threadIdx.x, n = (g0 + idx / (WG_ROWS * MM)) * WG_ROWS + idx % WG_ROWS;
+        if (idx < (g1 - g0) * WG_ROWS * MM && n < N) {
+            my_sc = __ldg(scales + n);
+            if (bias) my_bi = __ldg(bias + n);
+        }
+    }
+    bar_sync(1, ncons);  // every warp has its B fragments: the table becomes part
 
     // Row sums are buffered per group in part[P][MM][KW][16] and combined P
     // groups at a time (all scale / bias loads of a flush in flight together,
@@ -249,22 +286,30 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     bool ok = true;
     for (int g = g0; g < g1; g++) {
         if (ok) ok = mbar_wait(full_bar(s), ph, abort_p, gflags, true);
+        // four independent accumulator sets (k-step j -> set j % 4) keep four
+        // MMAs in flight; their i32 sums are added exactly afterwards
         int d[4] = {cinit[0], cinit[1], cinit[0], cinit[1]};
-        const uint32_t base = ring + (uint32_t)s * stage_bytes + (uint32_t)gq * row_pitch + (uint32_t)(kslice >> 1) +
-                              4u * tq;
+        int e[3][4] = {};
+        const uint32_t base = ring + (uint32_t)s * stage_bytes;
         if (ok) {
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 if (j < ksteps) {
-                    const uint32_t w0 = lds32(base + 16u * j), w1 = lds32(base + 8u * row_pitch + 16u * j);
+                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq);
+                    const uint32_t w0 = lds32(base + off), w1 = lds32(base + off + 8u * 128u);
                     uint32_t a[4];
                     a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq, even k: q + 8
                     a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq + 8, even k
                     a[2] = ((w0 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq, odd k
                     a[3] = ((w1 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq + 8, odd k
-                    mma_u8s8(d, a, bf[j][0], bf[j][1]);
+                    if (j % 4 == 0)
+                        mma_u8s8(d, a, bf[j][0], bf[j][1]);
+                    else
+                        mma_u8s8(e[j % 4 - 1], a, bf[j][0], bf[j][1]);
                 }
             }
+#pragma unroll
+            for (int c = 0; c < 4; c++) d[c] += e[0][c] + e[1][c] + e[2][c];
         }
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(empty_bar(s));
@@ -287,12 +332,11 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         if (slow && vi >= 0 && isnan(sx[vi])) {  // non-finite activations: the slice's f32 dot product
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                const uint32_t rowp = ring + (uint32_t)s * stage_bytes + (uint32_t)(gq + 8 * h) * row_pitch +
-                                      (uint32_t)(kslice >> 1);
                 float acc = 0.0f;
                 if (vi < M && ok)
                     for (int kk = 0; kk < ksteps * 32; kk++) {
-                        const uint32_t wd = lds32(rowp + 4u * (kk >> 3));
+                        const uint32_t wd =
+                            lds32(base + stage_off(gq + 8 * h, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)));
                         const int nb = (int)((wd >> (4 * (kk & 7))) & 0xFu);
                         acc = fmaf(__ldg(X + (size_t)vi * K + kslice + kk), (float)(nb - ((nb & 8) << 1)), acc);
                     }
@@ -318,8 +362,8 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
                     if (n >= N || i >= M) continue;
                     float acc = 0.0f;
                     for (int sl = 0; sl < KW; sl++) acc += part[((gi * MM + i) * KW + sl) * WG_ROWS + r];
-                    float y = acc * __ldg(scales + n);
-                    if (bias) y += __ldg(bias + n);
+                    float y = acc * (one_flush ? my_sc : __ldg(scales + n));
+                    if (bias) y += one_flush ? my_bi : __ldg(bias + n);
                     Y[(size_t)i * N + n] = apply_act(y, act);
                 }
             }
@@ -330,8 +374,8 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
 }
 
 template <int MM>
-int launch_one(tpt_cuda_ctx *ctx, const float *x, const uint8_t *p, const float *scales, const float *bias, int act,
-               float *y, int n, int k, int S, int P, size_t smem) {
+int launch_one(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const float *x, const float *scales, const float *bias,
+               int act, float *y, int n, int k, int S, int P, size_t smem) {
     static bool attr_done[64] = {};
     auto kfn = k_w4_gemv_tma<MM>;
     const int dev = ctx->device & 63;
@@ -342,38 +386,57 @@ int launch_one(tpt_cuda_ctx *ctx, const float *x, const uint8_t *p, const float 
     }
     const int kw = (k + WG_SLICE - 1) / WG_SLICE, groups = (n + WG_ROWS - 1) / WG_ROWS;
     const unsigned grid = (unsigned)(groups < ctx->sm_count ? groups : ctx->sm_count);  // one CTA per SM
-    launch_pdl(kfn, grid, 32 * (kw + 1), smem, ctx->stream, x, p, scales, bias, MM, n, k, act, y, S, P, ctx->d_flags);
+    launch_pdl(kfn, grid, 32 * (kw + 1), smem, ctx->stream, tw, x, scales, bias, MM, n, k, act, y, S, P, ctx->d_flags);
     return after_launch(ctx, "w4_gemv_tma");
+}
+
+// The nibble matrix [n rows, K/2 bytes] as the 3-D tensor {128 B, n rows, K/256
+// columns of 128 B} with box {128, 16, K/256} and 128B swizzle; rows past n
+// read as zero, and every address stays inside the matrix.
+bool make_tmap_nibbles(CUtensorMap *tm, const void *base, uint64_t n, uint64_t k) {
+    auto fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15) || (k % 256) || k / 256 > 256) return false;
+    cuuint64_t dims[3] = {128, n, k / 256};
+    cuuint64_t strides[2] = {k / 2, 128};
+    cuuint32_t box[3] = {128, (cuuint32_t)WG_ROWS, (cuuint32_t)(k / 256)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 }  // namespace
 
-// M <= 2, K % 32 == 0, K <= 8192, x and the nibbles 16-byte aligned; returns
-// handled = false otherwise.
+// M <= 2, K % 256 == 0, K <= 8192, x 16-byte aligned; returns handled = false
+// otherwise.
 int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
                        int act, float *y, bool *handled) {
     *handled = false;
     const size_t n = w->n, k = w->k;
-    const uint8_t *p = (const uint8_t *)w->data;
-    if (m == 0 || m > 2 || k % 32 != 0 || k > (size_t)WG_MAX_KW * WG_SLICE || n > INT32_MAX) return TPT_OK;
-    if (((uintptr_t)x & 15) != 0 || ((uintptr_t)p & 15) != 0) return TPT_OK;
+    if (m == 0 || m > 2 || k % 256 != 0 || k > (size_t)WG_MAX_KW * WG_SLICE || n > INT32_MAX) return TPT_OK;
+    if (((uintptr_t)x & 15) != 0) return TPT_OK;
+    CUtensorMap tw;
+    if (!make_tmap_nibbles(&tw, w->data, n, k)) return TPT_OK;
     const int kw = (int)((k + WG_SLICE - 1) / WG_SLICE);
     const int MM = (int)m;
-    const size_t stage = WG_ROWS * (k / 2 + 16), table = (size_t)kw * MM * 3 * 32 * 16;
-    const size_t ring = WG_RING_BUDGET < WG_SMEM_MAX - table - WG_PART_BUDGET ? WG_RING_BUDGET
-                                                                              : WG_SMEM_MAX - table - WG_PART_BUDGET;
-    const int S = (int)(ring / stage < 8 ? ring / stage : 8);
-    if (S < 2) return TPT_OK;
+    const size_t stage = WG_ROWS * (k / 2), table = (size_t)kw * MM * 3 * 32 * 16;
     // groups buffered between flushes: all of a CTA's run when they fit
     const size_t per_group = (size_t)MM * kw * WG_ROWS * 4;
     const size_t groups = (n + WG_ROWS - 1) / WG_ROWS;
     const size_t ctas = groups < (size_t)ctx->sm_count ? groups : (size_t)ctx->sm_count;
     const size_t run = (groups + ctas - 1) / ctas;
     const int P = (int)(run < WG_PART_BUDGET / per_group ? run : WG_PART_BUDGET / per_group);
-    const size_t smem = (size_t)S * stage + table + (size_t)P * per_group + (size_t)2 * S * 8;
+    const size_t shared = table > (size_t)P * per_group ? table : (size_t)P * per_group;  // table, then part
+    // two CTAs per SM when three stages fit beside each other, else one
+    size_t budget = WG_SMEM_PAIR - shared - 1024 - 128;
+    if (budget / stage < 3) budget = WG_SMEM_MAX - shared - 1024 - 128;
+    const int S = (int)(budget / stage < 8 ? budget / stage : 8);
+    if (S < 2) return TPT_OK;
+    const size_t smem = 1024 + (size_t)S * stage + shared + (size_t)2 * S * 8;
     *handled = true;
-    return MM == 1 ? launch_one<1>(ctx, x, p, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
-                   : launch_one<2>(ctx, x, p, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
+    return MM == 1 ? launch_one<1>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
+                   : launch_one<2>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
 }
 
 }  // namespace tpt
