@@ -183,7 +183,7 @@ def w4_tol(want):
                                    (300, 129, 4096),
                                    # decode GEMV: ragged groups, 3 / 11 / 12 K-slices, K beyond the ring
                                    (2, 1001, 4096), (1, 4096, 11008), (2, 4096, 11008), (1, 77, 3072),
-                                   (2, 300, 12288), (1, 64, 16384)])
+                                   (2, 300, 12288), (1, 64, 16384), (1, 200, 8192), (2, 72, 6144)])
 def test_w4_gemm(cuda, m, n, k):
     x, p, s = w4_case(m, n, k)
     w = cuda.upload_i4(p, s, n, k)

@@ -53,8 +53,7 @@ namespace {
 using namespace tc;
 
 constexpr int WG_ROWS = 16;    // weight rows per group (one ring stage; the MMA's M)
-constexpr int WG_SLICE = 512;  // k per consumer warp
-constexpr int WG_MAX_KW = 16;  // K <= 8192
+constexpr int WG_MAX_KW = 16;  // consumer warps: K <= 16 x 512
 constexpr int WG_PART_BUDGET = 12 * 1024;
 constexpr int WG_SMEM_PAIR = 112 * 1024;  // two CTAs per SM: the next launch's CTA streams beside this one
 constexpr int WG_SMEM_MAX = 200 * 1024;
@@ -77,22 +76,19 @@ __device__ __forceinline__ uint32_t stage_off(int row, uint32_t b) {
            (b & 15u);
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-
-// D += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulate
+// D += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulate. Not
+// volatile: a pure function of its registers, so the compiler may hoist the
+// fragment loads of later k-steps above it.
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int MM>
+// CH = k per lane (8 or 16): a consumer warp's slice is 32 CH k, CH MMA k-steps.
+template <int MM, int CH>
 __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     k_w4_gemv_tma(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
                   const float *__restrict__ scales, const float *__restrict__ bias, int M, int N, int K, int act,
@@ -100,7 +96,8 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int abort_flag;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int KW = (K + WG_SLICE - 1) / WG_SLICE;  // consumer warps; warp KW is the producer
+    constexpr int SL = 32 * CH;           // k per consumer warp
+    const int KW = (K + SL - 1) / SL;     // consumer warps; warp KW is the producer
     const uint32_t stage_bytes = (uint32_t)K * 8u;   // 16 rows x K/2 bytes
     const int groups = (N + WG_ROWS - 1) / WG_ROWS;
     const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
@@ -110,7 +107,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     // same bytes later hold the slice sums part[P][MM][KW][16]
     uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (ring - raw) + (size_t)S * stage_bytes);
     float *part = reinterpret_cast<float *>(tab);
-    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * 4, P * MM * KW * WG_ROWS));
+    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * (CH / 4), P * MM * KW * WG_ROWS));
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
 
@@ -167,18 +164,18 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     // ---------------- consumers: warp = k slice ----------------
     const int ncons = KW * 32;
     const int gq = lane >> 2, tq = lane & 3;  // MMA fragment group / thread in group
-    const int kslice = warp * WG_SLICE;
-    const int ksteps = min(WG_SLICE, K - kslice) / 32;
-    uint32_t *mytab = tab + warp * MM * 3 * 32 * 4;
+    const int kslice = warp * SL;
+    const int ksteps = min(SL, K - kslice) / 32;
+    uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
     // Digits of this slice: lane c splits k [kslice + 16 c, +16) of each row.
     float sx[MM];  // slice scale (NaN: the slice holds a non-finite activation)
     int corr[MM][3];
 #pragma unroll
     for (int i = 0; i < MM; i++) {
-        const int kb = kslice + 16 * lane;
-        float xv[16];
+        const int kb = kslice + CH * lane;
+        float xv[CH];
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
+        for (int j = 0; j < CH; j += 4) {
             float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (i < M && kb < K) t = __ldg(reinterpret_cast<const float4 *>(X + (size_t)i * K + kb + j));
             xv[j] = t.x;
@@ -189,7 +186,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         float amax = 0.0f;
         bool fin = true;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < CH; j++) {
             const float a = fabsf(xv[j]);
             fin = fin && a <= 3.402823466e38f;  // false for inf and NaN
             amax = fmaxf(amax, a);
@@ -206,9 +203,9 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         // 256 (the digit as a signed byte), and subtracting the addend back
         // gives rint(t) exactly.
         constexpr float RND = 12582912.0f;
-        uint32_t bits[3][16];
+        uint32_t bits[3][CH];
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < CH; j++) {
             const float t = live ? xv[j] * inv : 0.0f;
             const float f0 = t + RND;
             const float r1 = (t - (f0 - RND)) * 128.0f;
@@ -221,32 +218,35 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         // chunk word 2q (+1 for odd): the digits of k = 8q + 2bb (+1), bb = 0..3
 #pragma unroll
         for (int p = 0; p < 3; p++) {
-            uint32_t wd[4];
+            uint32_t wd[CH / 4];
             int sum = 0;
 #pragma unroll
-            for (int wi = 0; wi < 4; wi++) {
+            for (int wi = 0; wi < CH / 4; wi++) {
                 const int j0 = 8 * (wi >> 1) + (wi & 1);
                 const uint32_t lo = __byte_perm(bits[p][j0], bits[p][j0 + 2], 0x0040);
                 const uint32_t hi = __byte_perm(bits[p][j0 + 4], bits[p][j0 + 6], 0x0040);
                 wd[wi] = __byte_perm(lo, hi, 0x5410);
                 sum = __dp4a((int)wd[wi], 0x01010101, sum);
             }
-            *reinterpret_cast<uint4 *>(mytab + ((i * 3 + p) * 32 + lane) * 4) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+#pragma unroll
+            for (int wi = 0; wi < CH / 4; wi++) mytab[((i * 3 + p) * 32 + lane) * (CH / 4) + wi] = wd[wi];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             corr[i][p] = -8 * sum;
         }
     }
     __syncwarp();
-    // B fragments of the 16 k-steps: column gq = (activation row, plane) or
-    // zero; k-step j, word t of B = chunk 2j + t/2, quad t%2 (even, odd word)
-    uint32_t bf[16][2];
+    // B fragments of the CH k-steps: column gq = (activation row, plane) or
+    // zero; k-step j, word t of B = the 8 k at 32 j + 8 t: chunk (32 j + 8 t) / CH,
+    // quad ((32 j + 8 t) % CH) / 8 (even, odd word)
+    uint32_t bf[CH][2];
     const int bi = gq / 3, bp = gq - 3 * (gq / 3);
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
+    for (int j = 0; j < CH; j++) {
         bf[j][0] = bf[j][1] = 0u;
         if (gq < 3 * MM) {
-            const uint32_t *src = mytab + ((bi * 3 + bp) * 32 + 2 * j + (tq >> 1)) * 4 + 2 * (tq & 1);
+            const int k8 = 32 * j + 8 * tq;
+            const uint32_t *src = mytab + ((bi * 3 + bp) * 32 + k8 / CH) * (CH / 4) + 2 * ((k8 % CH) / 8);
             bf[j][0] = src[0];
             bf[j][1] = src[1];
         }
@@ -291,12 +291,15 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         int d[4] = {cinit[0], cinit[1], cinit[0], cinit[1]};
         int e[3][4] = {};
         const uint32_t base = ring + (uint32_t)s * stage_bytes;
+        // plain loads (ordered after the barrier wait by its memory clobber),
+        // free to be issued all at once ahead of the MMAs
+        const uint32_t *stg = reinterpret_cast<const uint32_t *>(smem + (base - raw));
         if (ok) {
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
+            for (int j = 0; j < CH; j++) {
                 if (j < ksteps) {
-                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq);
-                    const uint32_t w0 = lds32(base + off), w1 = lds32(base + off + 8u * 128u);
+                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq) >> 2;
+                    const uint32_t w0 = stg[off], w1 = stg[off + 256u];
                     uint32_t a[4];
                     a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq, even k: q + 8
                     a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq + 8, even k
@@ -335,8 +338,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
                 float acc = 0.0f;
                 if (vi < M && ok)
                     for (int kk = 0; kk < ksteps * 32; kk++) {
-                        const uint32_t wd =
-                            lds32(base + stage_off(gq + 8 * h, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)));
+                        const uint32_t wd = stg[stage_off(gq + 8 * h, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)) >> 2];
                         const int nb = (int)((wd >> (4 * (kk & 7))) & 0xFu);
                         acc = fmaf(__ldg(X + (size_t)vi * K + kslice + kk), (float)(nb - ((nb & 8) << 1)), acc);
                     }
@@ -373,18 +375,18 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     }
 }
 
-template <int MM>
+template <int MM, int CH>
 int launch_one(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const float *x, const float *scales, const float *bias,
                int act, float *y, int n, int k, int S, int P, size_t smem) {
     static bool attr_done[64] = {};
-    auto kfn = k_w4_gemv_tma<MM>;
+    auto kfn = k_w4_gemv_tma<MM, CH>;
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, WG_SMEM_MAX + 1024);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "w4_gemv smem attribute");
         attr_done[dev] = true;
     }
-    const int kw = (k + WG_SLICE - 1) / WG_SLICE, groups = (n + WG_ROWS - 1) / WG_ROWS;
+    const int kw = (k + 32 * CH - 1) / (32 * CH), groups = (n + WG_ROWS - 1) / WG_ROWS;
     const unsigned grid = (unsigned)(groups < ctx->sm_count ? groups : ctx->sm_count);  // one CTA per SM
     launch_pdl(kfn, grid, 32 * (kw + 1), smem, ctx->stream, tw, x, scales, bias, MM, n, k, act, y, S, P, ctx->d_flags);
     return after_launch(ctx, "w4_gemv_tma");
@@ -414,13 +416,15 @@ int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cu
                        int act, float *y, bool *handled) {
     *handled = false;
     const size_t n = w->n, k = w->k;
-    if (m == 0 || m > 2 || k % 256 != 0 || k > (size_t)WG_MAX_KW * WG_SLICE || n > INT32_MAX) return TPT_OK;
+    if (m == 0 || m > 2 || k % 256 != 0 || k > (size_t)WG_MAX_KW * 512 || n > INT32_MAX) return TPT_OK;
     if (((uintptr_t)x & 15) != 0) return TPT_OK;
     CUtensorMap tw;
     if (!make_tmap_nibbles(&tw, w->data, n, k)) return TPT_OK;
-    const int kw = (int)((k + WG_SLICE - 1) / WG_SLICE);
+    // slices of 256 k (16 consumer warps at K = 4096) while they fit, else 512
+    const int ch = k <= (size_t)WG_MAX_KW * 256 ? 8 : 16;
+    const int kw = (int)((k + 32 * ch - 1) / (32 * ch));
     const int MM = (int)m;
-    const size_t stage = WG_ROWS * (k / 2), table = (size_t)kw * MM * 3 * 32 * 16;
+    const size_t stage = WG_ROWS * (k / 2), table = (size_t)kw * MM * 3 * 32 * ch;
     // groups buffered between flushes: all of a CTA's run when they fit
     const size_t per_group = (size_t)MM * kw * WG_ROWS * 4;
     const size_t groups = (n + WG_ROWS - 1) / WG_ROWS;
@@ -435,8 +439,11 @@ int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cu
     if (S < 2) return TPT_OK;
     const size_t smem = 1024 + (size_t)S * stage + shared + (size_t)2 * S * 8;
     *handled = true;
-    return MM == 1 ? launch_one<1>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
-                   : launch_one<2>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
+    if (ch == 8)
+        return MM == 1 ? launch_one<1, 8>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
+                       : launch_one<2, 8>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
+    return MM == 1 ? launch_one<1, 16>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
+                   : launch_one<2, 16>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
 }
 
 }  // namespace tpt
