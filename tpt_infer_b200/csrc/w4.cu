@@ -13,8 +13,9 @@
 // bytes quantize_i4_symmetric_per_channel(W^T, rows = n) emits
 // (quant.rs:192-204), uploaded once, never repacked.
 //
-// M >= 3 goes to the tensor-core kernel (w4_tc.cu) when K % 128 == 0 and x is
-// 16-byte aligned. M <= 2 uses the TMA-ring GEMV with integer digit planes
+// 3 <= M <= 8 with K % 256 == 0, K <= 4096 goes to the small-batch kernel of
+// w4_gemv.cu; other M >= 3 to the tensor-core kernel (w4_tc.cu) when
+// K % 128 == 0 and x is 16-byte aligned. M <= 2 uses the TMA-ring GEMV with integer digit planes
 // (w4_gemv.cu) for K % 256 == 0, K <= 8192, else k_w4_gemv: one warp streams 8
 // weight rows with 128-bit loads, reusing each activation chunk across the 8
 // rows. Other shapes use the SIMT tile kernel.
@@ -30,6 +31,8 @@ int launch_w4_tc(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_wei
                  float *y, bool *handled);
 int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
                        int act, float *y, bool *handled);
+int launch_w4_small(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
+                    int act, float *y, bool *handled);
 
 namespace {
 
@@ -117,6 +120,11 @@ int launch_w4(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weight
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     const uint8_t *p = (const uint8_t *)w->data;
+    if (m > 2 && m <= 8) {
+        bool handled = false;
+        int st = launch_w4_small(ctx, x, m, w, bias, act, y, &handled);
+        if (st || handled) return st;
+    }
     if (m > 2) {
         bool handled = false;
         int st = launch_w4_tc(ctx, x, m, w, bias, act, y, &handled);

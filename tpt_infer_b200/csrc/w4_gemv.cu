@@ -6,8 +6,8 @@
 // (crates/tpt-infer-quantize/src/dequant.rs:56-71, crates/tpt-infer-ops/src/
 // avx512.rs:55-78): y[m,n] = sum_k x[m,k] * (q[n,k] * s[n]) + bias[n], then act.
 //
-// Numerics. Each activation row is split, per slice of 512 k, into three signed
-// 8-bit digit planes:
+// Numerics. Each activation row is split, per slice of SL = 256 k (K <= 4096)
+// or 512 k (K <= 8192), into three signed 8-bit digit planes:
 //   x_k = s (d0_k + d1_k / 128 + d2_k / 16384) (1 + e),  s = max_slice |x| / 127,
 //   t = x * (127 / max|x|), d0 = rint(t), d1 = rint((t - d0) 128),
 //   d2 = rint(((t - d0) 128 - d1) 128)
@@ -17,7 +17,7 @@
 // from -8 sum_k d_p,k, which removes the +8. Per row and slice the three plane
 // sums A_p are combined as s (A0 + (A1 + A2 / 128) / 128) in f32 (A0 is below
 // 2^24, exact). Against the f32 dot product this differs by the digit error (at
-// most 8 * 512 * s / 32768 per slice, far inside the 1e-3 x output-step bound)
+// most 8 * SL * s / 32768 per slice, far inside the 1e-3 x output-step bound)
 // and f32 rounding. A slice holding a non-finite activation is computed as the
 // f32 dot product instead, so inf and NaN propagate as in the reference.
 //
@@ -39,8 +39,8 @@
 // S groups before the kernel's dependency wait (two CTAs fit one SM, so under
 // programmatic dependent launch the next GEMV's first stages arrive while this
 // one computes). The swizzle puts the 8 rows of a fragment load (8 rows x 4
-// words per warp) in 32 distinct banks. Consumer warp w owns k slice w (512 k)
-// of every row: per stage 16 MMAs, then the plane sums are combined and the
+// words per warp) in 32 distinct banks. Consumer warp w owns k slice w (SL k)
+// of every row: per stage SL / 32 MMAs, then the plane sums are combined and the
 // row's slice sum goes to a shared buffer; the buffered groups are combined
 // (slice sums added in slice order, so the result does not depend on the
 // launch shape, then scale, bias, act) once per P groups, normally once per
@@ -87,89 +87,48 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// CH = k per lane (8 or 16): a consumer warp's slice is 32 CH k, CH MMA k-steps.
-template <int MM, int CH>
-__global__ void __launch_bounds__(WG_MAX_THREADS, 1)
-    k_w4_gemv_tma(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
-                  const float *__restrict__ scales, const float *__restrict__ bias, int M, int N, int K, int act,
-                  float *__restrict__ Y, int S, int P, unsigned *gflags) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int abort_flag;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int SL = 32 * CH;           // k per consumer warp
-    const int KW = (K + SL - 1) / SL;     // consumer warps; warp KW is the producer
-    const uint32_t stage_bytes = (uint32_t)K * 8u;   // 16 rows x K/2 bytes
-    const int groups = (N + WG_ROWS - 1) / WG_ROWS;
-    const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
-    const int g1 = (int)((long long)(blockIdx.x + 1) * groups / gridDim.x);
-    const uint32_t raw = smem_u32(smem), ring = (raw + 1023u) & ~1023u;  // 128B swizzle: 1 KB aligned
-    // per consumer warp: digit words [MM][3 planes][32 chunks][4 words]; the
-    // same bytes later hold the slice sums part[P][MM][KW][16]
-    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (ring - raw) + (size_t)S * stage_bytes);
-    float *part = reinterpret_cast<float *>(tab);
-    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * (CH / 4), P * MM * KW * WG_ROWS));
+// ---------------- TMA producer (one thread) ----------------
+// The first S groups are requested before the dependency wait: the nibbles are
+// constants (written only by host uploads, which a programmatic launch never
+// overlaps), so they stream while the previous kernel finishes.
+__device__ __forceinline__ void produce(const CUtensorMap &tmW, uint32_t ring, uint32_t stage_bytes, uint32_t bars,
+                                        int S, int g0, int g1, volatile int *abort_p, unsigned *gflags) {
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
-
-    if (threadIdx.x == 0) {
-        abort_flag = 0;
-        for (int s = 0; s < S; s++) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), (uint32_t)KW);
+    int s = 0;
+    uint32_t ph = 0, issued = 0, last_ph = 0;
+    for (int g = g0; g < g1; g++) {
+        if (g == g0 + S) {
+            pdl_wait();
+            pdl_trigger();
         }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-    }
-    __syncthreads();
-    volatile int *abort_p = &abort_flag;
-
-    if (warp == KW) {
-        if (lane == 0) {
-            // ---------------- TMA producer ----------------
-            // The first S groups are requested before the dependency wait: the
-            // nibbles are constants (written only by host uploads, which a
-            // programmatic launch never overlaps), so they stream while the
-            // previous kernel finishes.
-            int s = 0;
-            uint32_t ph = 0, issued = 0, last_ph = 0;
-            for (int g = g0; g < g1; g++) {
-                if (g == g0 + S) {
-                    pdl_wait();
-                    pdl_trigger();
-                }
-                if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_p, gflags, true)) break;
-                mbar_arrive_expect_tx(full_bar(s), stage_bytes);  // the whole box, rows past N read as 0
-                tma_load_3d(ring + (uint32_t)s * stage_bytes, &tmW, full_bar(s), g * WG_ROWS);
-                issued |= 1u << s;
-                last_ph = (last_ph & ~(1u << s)) | (ph << s);
-                if (++s == S) {
-                    s = 0;
-                    ph ^= 1u;
-                }
-            }
-            if (g1 - g0 <= S) {
-                pdl_wait();
-                pdl_trigger();
-            }
-            // our copies in flight land before the CTA can exit
-            for (int t = 0; t < S; t++)
-                if (issued & (1u << t)) mbar_wait(full_bar(t), (last_ph >> t) & 1u, abort_p, gflags, false);
+        if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_p, gflags, true)) break;
+        mbar_arrive_expect_tx(full_bar(s), stage_bytes);  // the whole box, rows past N read as 0
+        tma_load_3d(ring + (uint32_t)s * stage_bytes, &tmW, full_bar(s), g * WG_ROWS);
+        issued |= 1u << s;
+        last_ph = (last_ph & ~(1u << s)) | (ph << s);
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
         }
-        return;
     }
-    if (warp > KW) return;
-    pdl_wait();  // X (the previous kernel's output) is complete from here on
-    pdl_trigger();
+    if (g1 - g0 <= S) {
+        pdl_wait();
+        pdl_trigger();
+    }
+    // our copies in flight land before the CTA can exit
+    for (int t = 0; t < S; t++)
+        if (issued & (1u << t)) mbar_wait(full_bar(t), (last_ph >> t) & 1u, abort_p, gflags, false);
+}
 
-    // ---------------- consumers: warp = k slice ----------------
-    const int ncons = KW * 32;
-    const int gq = lane >> 2, tq = lane & 3;  // MMA fragment group / thread in group
-    const int kslice = warp * SL;
-    const int ksteps = min(SL, K - kslice) / 32;
-    uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
-    // Digits of this slice: lane c splits k [kslice + 16 c, +16) of each row.
-    float sx[MM];  // slice scale (NaN: the slice holds a non-finite activation)
-    int corr[MM][3];
+// Digits of one warp's slice [kslice, kslice + 32 CH) for activation rows
+// 0..MM-1 (rows >= M read as zero): lane c splits k [kslice + CH c, +CH) and
+// writes its words to tab[(i * 3 + p) * 32 + c][CH / 4]; every lane gets the
+// slice scale sx[i] (NaN when the slice holds a non-finite activation) and
+// corr[i][p] = -8 sum_k d_p,k over the slice.
+template <int MM, int CH>
+__device__ __forceinline__ void split_slice(const float *__restrict__ X, int M, int K, int kslice, int lane,
+                                            uint32_t *tab, float (&sx)[MM], int (&corr)[MM][3]) {
 #pragma unroll
     for (int i = 0; i < MM; i++) {
         const int kb = kslice + CH * lane;
@@ -229,12 +188,67 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
                 sum = __dp4a((int)wd[wi], 0x01010101, sum);
             }
 #pragma unroll
-            for (int wi = 0; wi < CH / 4; wi++) mytab[((i * 3 + p) * 32 + lane) * (CH / 4) + wi] = wd[wi];
+            for (int wi = 0; wi < CH / 4; wi++) tab[((i * 3 + p) * 32 + lane) * (CH / 4) + wi] = wd[wi];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             corr[i][p] = -8 * sum;
         }
     }
+}
+
+// CH = k per lane (8 or 16): a consumer warp's slice is 32 CH k, CH MMA k-steps.
+template <int MM, int CH>
+__global__ void __launch_bounds__(WG_MAX_THREADS, 1)
+    k_w4_gemv_tma(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
+                  const float *__restrict__ scales, const float *__restrict__ bias, int M, int N, int K, int act,
+                  float *__restrict__ Y, int S, int P, unsigned *gflags) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int SL = 32 * CH;           // k per consumer warp
+    const int KW = (K + SL - 1) / SL;     // consumer warps; warp KW is the producer
+    const uint32_t stage_bytes = (uint32_t)K * 8u;   // 16 rows x K/2 bytes
+    const int groups = (N + WG_ROWS - 1) / WG_ROWS;
+    const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
+    const int g1 = (int)((long long)(blockIdx.x + 1) * groups / gridDim.x);
+    const uint32_t raw = smem_u32(smem), ring = (raw + 1023u) & ~1023u;  // 128B swizzle: 1 KB aligned
+    // per consumer warp: digit words [MM][3 planes][32 chunks][4 words]; the
+    // same bytes later hold the slice sums part[P][MM][KW][16]
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (ring - raw) + (size_t)S * stage_bytes);
+    float *part = reinterpret_cast<float *>(tab);
+    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * (CH / 4), P * MM * KW * WG_ROWS));
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), (uint32_t)KW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    }
+    __syncthreads();
+    volatile int *abort_p = &abort_flag;
+
+    if (warp == KW) {
+        if (lane == 0) produce(tmW, ring, stage_bytes, bars, S, g0, g1, abort_p, gflags);
+        return;
+    }
+    if (warp > KW) return;
+    pdl_wait();  // X (the previous kernel's output) is complete from here on
+    pdl_trigger();
+
+    // ---------------- consumers: warp = k slice ----------------
+    const int ncons = KW * 32;
+    const int gq = lane >> 2, tq = lane & 3;  // MMA fragment group / thread in group
+    const int kslice = warp * SL;
+    const int ksteps = min(SL, K - kslice) / 32;
+    uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
+    float sx[MM];  // slice scale (NaN: the slice holds a non-finite activation)
+    int corr[MM][3];
+    split_slice<MM, CH>(X, M, K, kslice, lane, mytab, sx, corr);
     __syncwarp();
     // B fragments of the CH k-steps: column gq = (activation row, plane) or
     // zero; k-step j, word t of B = the 8 k at 32 j + 8 t: chunk (32 j + 8 t) / CH,
@@ -375,6 +389,202 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     }
 }
 
+// Small batches (3 <= M <= MM, MM = 4 or 8; K <= 4096, CH = 8): the same
+// ring, digit split and weight fragments, with T = ceil(3 MM / 8) MMA column
+// tiles per k-step (column 3 i + p = plane p of activation row i). The plane
+// sums go through a per-warp shared scratch [16 rows][8 T columns] and each
+// lane combines (row, activation row) pairs.
+template <int MM>
+__global__ void __launch_bounds__(WG_MAX_THREADS, 1)
+    k_w4_small(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X, const float *__restrict__ scales,
+               const float *__restrict__ bias, int M, int N, int K, int act, float *__restrict__ Y, int S, int P,
+               unsigned *gflags) {
+    constexpr int CH = 8, SL = 32 * CH, T = (3 * MM + 7) / 8, SC = 8 * T;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int KW = (K + SL - 1) / SL;  // consumer warps; warp KW is the producer
+    const uint32_t stage_bytes = (uint32_t)K * 8u;
+    const int groups = (N + WG_ROWS - 1) / WG_ROWS;
+    const int g0 = (int)((long long)blockIdx.x * groups / gridDim.x);
+    const int g1 = (int)((long long)(blockIdx.x + 1) * groups / gridDim.x);
+    const uint32_t raw = smem_u32(smem), ring = (raw + 1023u) & ~1023u;
+    // digit table [KW][MM][3][32][CH/4] words; afterwards the same bytes hold
+    // part[P][MM][KW][16] and the per-warp scratch [KW][16][SC]
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + (ring - raw) + (size_t)S * stage_bytes);
+    float *part = reinterpret_cast<float *>(tab);
+    int *scr = reinterpret_cast<int *>(part + P * MM * KW * WG_ROWS);
+    const uint32_t bars = smem_u32(tab + max(KW * MM * 3 * 32 * (CH / 4), P * MM * KW * WG_ROWS + KW * 16 * SC));
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), (uint32_t)KW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    }
+    __syncthreads();
+    volatile int *abort_p = &abort_flag;
+    if (warp == KW) {
+        if (lane == 0) produce(tmW, ring, stage_bytes, bars, S, g0, g1, abort_p, gflags);
+        return;
+    }
+    if (warp > KW) return;
+    pdl_wait();  // X (the previous kernel's output) is complete from here on
+    pdl_trigger();
+
+    const int ncons = KW * 32;
+    const int gq = lane >> 2, tq = lane & 3;
+    const int kslice = warp * SL;
+    const int ksteps = min(SL, K - kslice) / 32;
+    uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
+    float sx[MM];
+    int corr[MM][3];
+    split_slice<MM, CH>(X, M, K, kslice, lane, mytab, sx, corr);
+    __syncwarp();
+    // B fragments: tile tt, column gq -> c = 8 tt + gq = (row c / 3, plane c % 3)
+    uint32_t bf[T][CH][2];
+#pragma unroll
+    for (int tt = 0; tt < T; tt++) {
+        const int c = 8 * tt + gq;
+#pragma unroll
+        for (int j = 0; j < CH; j++) {
+            bf[tt][j][0] = bf[tt][j][1] = 0u;
+            if (c < 3 * MM) {
+                const int k8 = 32 * j + 8 * tq;
+                const uint32_t *src = mytab + (c * 32 + k8 / CH) * (CH / 4) + 2 * ((k8 % CH) / 8);
+                bf[tt][j][0] = src[0];
+                bf[tt][j][1] = src[1];
+            }
+        }
+    }
+    int cinit[T][2];
+#pragma unroll
+    for (int tt = 0; tt < T; tt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int c = 8 * tt + 2 * tq + e;
+            int v = 0;
+#pragma unroll
+            for (int i = 0; i < MM; i++)
+#pragma unroll
+                for (int p = 0; p < 3; p++)
+                    if (c == 3 * i + p) v = corr[i][p];
+            cinit[tt][e] = v;
+        }
+    bool slow = false;
+#pragma unroll
+    for (int i = 0; i < MM; i++) slow = slow || isnan(sx[i]);
+    bar_sync(1, ncons);  // every warp has its B fragments: the table becomes part + scratch
+    int *mysc = scr + warp * 16 * SC;
+
+    int s = 0, gl = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int g = g0; g < g1; g++) {
+        if (ok) ok = mbar_wait(full_bar(s), ph, abort_p, gflags, true);
+        int d[T][4];
+#pragma unroll
+        for (int tt = 0; tt < T; tt++) {
+            d[tt][0] = d[tt][2] = cinit[tt][0];
+            d[tt][1] = d[tt][3] = cinit[tt][1];
+        }
+        const uint32_t base = ring + (uint32_t)s * stage_bytes;
+        const uint32_t *stg = reinterpret_cast<const uint32_t *>(smem + (base - raw));
+        if (ok) {
+#pragma unroll
+            for (int j = 0; j < CH; j++) {
+                if (j < ksteps) {
+                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq) >> 2;
+                    const uint32_t w0 = stg[off], w1 = stg[off + 256u];
+                    uint32_t a[4];
+                    a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;
+                    a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;
+                    a[2] = ((w0 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
+                    a[3] = ((w1 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int tt = 0; tt < T; tt++) mma_u8s8(d[tt], a, bf[tt][j][0], bf[tt][j][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(empty_bar(s));
+        // plane sums -> scratch [row][column]
+#pragma unroll
+        for (int tt = 0; tt < T; tt++) {
+            const int c = 8 * tt + 2 * tq;
+            mysc[gq * SC + c] = d[tt][0];
+            mysc[gq * SC + c + 1] = d[tt][1];
+            mysc[(gq + 8) * SC + c] = d[tt][2];
+            mysc[(gq + 8) * SC + c + 1] = d[tt][3];
+        }
+        __syncwarp();
+        // lane -> (weight row r = lane % 16, activation row i = 2 u + lane / 16)
+#pragma unroll
+        for (int u = 0; u < MM / 2; u++) {
+            const int r = lane & 15, i = 2 * u + (lane >> 4);
+            const float si = (lane >> 4) ? sx[2 * u + 1] : sx[2 * u];
+            const int *row = mysc + r * SC + 3 * i;
+            float v = si * fmaf(fmaf((float)row[2], 0.0078125f, (float)row[1]), 0.0078125f, (float)row[0]);
+            if (slow && isnan(si)) {  // non-finite activations: the slice's f32 dot product
+                float acc = 0.0f;
+                if (i < M && ok)
+                    for (int kk = 0; kk < ksteps * 32; kk++) {
+                        const uint32_t wd = stg[stage_off(r, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)) >> 2];
+                        const int nb = (int)((wd >> (4 * (kk & 7))) & 0xFu);
+                        acc = fmaf(__ldg(X + (size_t)i * K + kslice + kk), (float)(nb - ((nb & 8) << 1)), acc);
+                    }
+                v = acc;
+            }
+            part[((gl * MM + i) * KW + warp) * WG_ROWS + r] = v;
+        }
+        __syncwarp();  // the scratch is read before the next stage overwrites it
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+        }
+        if (++gl == P || g + 1 == g1) {  // flush: combine the buffered groups
+            ok = bar_and(1, ncons, ok);
+            if (ok) {
+                const int gb = g + 1 - gl;
+                for (int idx = (int)threadIdx.x; idx < gl * WG_ROWS * MM; idx += ncons) {
+                    const int r = idx % WG_ROWS, i = (idx / WG_ROWS) % MM, gi = idx / (WG_ROWS * MM);
+                    const int n = (gb + gi) * WG_ROWS + r;
+                    if (n >= N || i >= M) continue;
+                    float acc = 0.0f;
+                    for (int sl = 0; sl < KW; sl++) acc += part[((gi * MM + i) * KW + sl) * WG_ROWS + r];
+                    float y = acc * __ldg(scales + n);
+                    if (bias) y += __ldg(bias + n);
+                    Y[(size_t)i * N + n] = apply_act(y, act);
+                }
+            }
+            bar_sync(1, ncons);
+            gl = 0;
+        }
+    }
+}
+
+template <int MM>
+int launch_small(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const float *x, const float *scales, const float *bias,
+                 int act, float *y, int m, int n, int k, int S, int P, size_t smem) {
+    static bool attr_done[64] = {};
+    auto kfn = k_w4_small<MM>;
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, WG_SMEM_MAX + 1024);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "w4_small smem attribute");
+        attr_done[dev] = true;
+    }
+    const int kw = (k + 255) / 256, groups = (n + WG_ROWS - 1) / WG_ROWS;
+    const unsigned grid = (unsigned)(groups < ctx->sm_count ? groups : ctx->sm_count);
+    launch_pdl(kfn, grid, 32 * (kw + 1), smem, ctx->stream, tw, x, scales, bias, m, n, k, act, y, S, P, ctx->d_flags);
+    return after_launch(ctx, "w4_small");
+}
+
 template <int MM, int CH>
 int launch_one(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const float *x, const float *scales, const float *bias,
                int act, float *y, int n, int k, int S, int P, size_t smem) {
@@ -444,6 +654,36 @@ int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cu
                        : launch_one<2, 8>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
     return MM == 1 ? launch_one<1, 16>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem)
                    : launch_one<2, 16>(ctx, tw, x, w->scales, bias, act, y, (int)n, (int)k, S, P, smem);
+}
+
+// 3 <= M <= 8, K % 256 == 0, K <= 4096, x 16-byte aligned; returns handled =
+// false otherwise.
+int launch_w4_small(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_weights *w, const float *bias,
+                    int act, float *y, bool *handled) {
+    *handled = false;
+    const size_t n = w->n, k = w->k;
+    if (m < 3 || m > 8 || k % 256 != 0 || k > (size_t)WG_MAX_KW * 256 || n > INT32_MAX) return TPT_OK;
+    if (((uintptr_t)x & 15) != 0) return TPT_OK;
+    CUtensorMap tw;
+    if (!make_tmap_nibbles(&tw, w->data, n, k)) return TPT_OK;
+    const int MM = m <= 4 ? 4 : 8, T = (3 * MM + 7) / 8;
+    const int kw = (int)((k + 255) / 256);
+    const size_t stage = WG_ROWS * (k / 2), table = (size_t)kw * MM * 3 * 32 * 8;
+    const size_t per_group = (size_t)MM * kw * WG_ROWS * 4, scratch = (size_t)kw * 16 * 8 * T * 4;
+    const size_t groups = (n + WG_ROWS - 1) / WG_ROWS;
+    const size_t ctas = groups < (size_t)ctx->sm_count ? groups : (size_t)ctx->sm_count;
+    const size_t run = (groups + ctas - 1) / ctas;
+    const size_t pmax = (4 * WG_PART_BUDGET) / per_group;
+    const int P = (int)(run < pmax ? run : pmax);
+    if (P < 1) return TPT_OK;
+    const size_t shared = table > (size_t)P * per_group + scratch ? table : (size_t)P * per_group + scratch;
+    const size_t budget = WG_SMEM_MAX - shared - 1024 - 128;
+    const int S = (int)(budget / stage < 8 ? budget / stage : 8);
+    if (S < 2) return TPT_OK;
+    const size_t smem = 1024 + (size_t)S * stage + shared + (size_t)2 * S * 8;
+    *handled = true;
+    return MM == 4 ? launch_small<4>(ctx, tw, x, w->scales, bias, act, y, (int)m, (int)n, (int)k, S, P, smem)
+                   : launch_small<8>(ctx, tw, x, w->scales, bias, act, y, (int)m, (int)n, (int)k, S, P, smem);
 }
 
 }  // namespace tpt
