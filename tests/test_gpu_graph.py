@@ -72,23 +72,25 @@ def test_recording_refuses_workspace_growth_and_stale_replay():
     K4, N4 = 4096, 256
     pk, s4 = O.quantize_i4_symmetric_per_channel(O.normal(N4 * K4, 411, 0.0, 0.02), N4)
     w4 = be.upload_i4(pk, s4, N4, K4)
-    xs = {m: torch.from_numpy(O.normal(m * K4, 412 + m)).cuda() for m in (8, 512)}
-    ys = {m: torch.empty(m * N4, dtype=torch.float32, device="cuda") for m in (8, 512)}
+    # M = 16 runs on the tensor-core kernel, whose split activations live in the
+    # context workspace
+    xs = {m: torch.from_numpy(O.normal(m * K4, 412 + m)).cuda() for m in (16, 512)}
+    ys = {m: torch.empty(m * N4, dtype=torch.float32, device="cuda") for m in (16, 512)}
     torch.cuda.synchronize()
     call = lambda m: be.w4_gemm_dev(xs[m], m, w4, None, 0, ys[m])  # noqa: E731
     # a fresh context: the launch workspace for the split activations does not exist yet
     with pytest.raises(OpError):
-        be.capture(lambda: call(8))
+        be.capture(lambda: call(16))
     # once sized, the same call records and replays
-    call(8)
+    call(16)
     be.sync()
-    want = ys[8].cpu().numpy().copy()
-    g = be.capture(lambda: call(8))
-    ys[8].zero_()
+    want = ys[16].cpu().numpy().copy()
+    g = be.capture(lambda: call(16))
+    ys[16].zero_()
     torch.cuda.synchronize()
     g.launch()
     be.sync()
-    assert np.array_equal(ys[8].cpu().numpy(), want)
+    assert np.array_equal(ys[16].cpu().numpy(), want)
     # a larger M needs a larger workspace: it moves, and the recording is stale
     call(512)
     be.sync()
