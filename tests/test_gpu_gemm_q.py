@@ -34,7 +34,10 @@ def w8a8_case(m, n, k, seed=100, with_bias=True):
                                    (128, 256, 128), (300, 512, 256), (1000, 768, 768), (160, 203, 96),
                                    (4097, 300, 128), (33, 300, 256), (64, 512, 784), (48, 4096, 4096),
                                    (17, 4097, 4112), (65, 512, 256), (100, 1000, 1024), (2, 300, 8192),
-                                   (4, 257, 4160), (16, 1024, 4096), (64, 2048, 2048), (5, 200, 384)])
+                                   (4, 257, 4160), (16, 1024, 4096), (64, 2048, 2048), (5, 200, 384),
+                                   # the small-batch MMA kernel: 1, 2 and 4 activation tiles
+                                   (3, 4096, 4096), (8, 1000, 1024), (12, 130, 512), (24, 500, 2048),
+                                   (32, 4096, 4096), (20, 17, 256)])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_w8a8_bit_exact(cuda, m, n, k, act):
     if act and m * n * k > 1 << 26:
@@ -50,7 +53,7 @@ def test_w8a8_bit_exact(cuda, m, n, k, act):
     w.free()
 
 
-@pytest.mark.parametrize("m", [1, 16, 256, 4096])
+@pytest.mark.parametrize("m", [1, 16, 30, 256, 4096])
 def test_w8a8_accumulators_bit_exact(cuda, m):
     import torch
 

@@ -129,15 +129,16 @@ def test_attention_op(cuda, B, S):
     assert np.max(np.abs(att - want)) <= 1e-5 * (1 + np.max(np.abs(want)))
 
 
-def test_plan_fusion_rules(cuda):
+@pytest.mark.parametrize("m", [96, 12])
+def test_plan_fusion_rules(cuda, m):
     # LINEAR -> QUANTIZE runs as one requantizing launch only when the f32
     # tensor is not fetched; fetched or not, the int8 result is the same, and both
-    # match the oracle's separate quantize.
+    # match the oracle's separate quantize (M = 12: the small-batch MMA kernel).
     import torch
 
     from tpt_infer_b200 import graphs, synth
 
-    m, k, n = 96, 512, 384
+    k, n = 512, 384
     x = synth.normal(m * k, 61)
     wq, ws = cuda.quantize_i8_symmetric_per_channel(synth.normal(n * k, 62, 0.0, 0.05), n)
     bias = synth.normal(n, 63, 0.0, 0.1)

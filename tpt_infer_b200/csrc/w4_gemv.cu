@@ -45,36 +45,19 @@
 // (slice sums added in slice order, so the result does not depend on the
 // launch shape, then scale, bias, act) once per P groups, normally once per
 // CTA. All waits are bounded.
-#include "tc_common.cuh"
+#include "ring.cuh"
 
 namespace tpt {
 
 namespace {
 using namespace tc;
+using namespace ring;
 
-constexpr int WG_ROWS = 16;    // weight rows per group (one ring stage; the MMA's M)
 constexpr int WG_MAX_KW = 16;  // consumer warps: K <= 16 x 512
 constexpr int WG_PART_BUDGET = 12 * 1024;
 constexpr int WG_SMEM_PAIR = 112 * 1024;  // two CTAs per SM: the next launch's CTA streams beside this one
 constexpr int WG_SMEM_MAX = 200 * 1024;
 constexpr int WG_MAX_THREADS = 32 * (WG_MAX_KW + 1);
-
-// One stage: rows [y, y + 16) x all K/2 bytes, as 16-row x 128-byte boxes per
-// 128-byte column (3-D view {128 B, rows, columns}), 128B-swizzled.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
-        "[%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(0), "r"(y), "r"(0)
-        : "memory");
-}
-
-// byte offset of (row, byte b of the row) in a stage: column b / 128 holds 16
-// rows of 128 bytes; the 16-byte unit u of row r sits at u ^ (r & 7)
-__device__ __forceinline__ uint32_t stage_off(int row, uint32_t b) {
-    return (b >> 7) * (WG_ROWS * 128u) + (uint32_t)row * 128u + ((((b >> 4) & 7u) ^ (uint32_t)(row & 7)) << 4) +
-           (b & 15u);
-}
 
 // D += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulate. Not
 // volatile: a pure function of its registers, so the compiler may hoist the
@@ -85,40 +68,6 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], ui
         "{%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// ---------------- TMA producer (one thread) ----------------
-// The first S groups are requested before the dependency wait: the nibbles are
-// constants (written only by host uploads, which a programmatic launch never
-// overlaps), so they stream while the previous kernel finishes.
-__device__ __forceinline__ void produce(const CUtensorMap &tmW, uint32_t ring, uint32_t stage_bytes, uint32_t bars,
-                                        int S, int g0, int g1, volatile int *abort_p, unsigned *gflags) {
-    auto full_bar = [&](int s) { return bars + 8u * s; };
-    auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
-    int s = 0;
-    uint32_t ph = 0, issued = 0, last_ph = 0;
-    for (int g = g0; g < g1; g++) {
-        if (g == g0 + S) {
-            pdl_wait();
-            pdl_trigger();
-        }
-        if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_p, gflags, true)) break;
-        mbar_arrive_expect_tx(full_bar(s), stage_bytes);  // the whole box, rows past N read as 0
-        tma_load_3d(ring + (uint32_t)s * stage_bytes, &tmW, full_bar(s), g * WG_ROWS);
-        issued |= 1u << s;
-        last_ph = (last_ph & ~(1u << s)) | (ph << s);
-        if (++s == S) {
-            s = 0;
-            ph ^= 1u;
-        }
-    }
-    if (g1 - g0 <= S) {
-        pdl_wait();
-        pdl_trigger();
-    }
-    // our copies in flight land before the CTA can exit
-    for (int t = 0; t < S; t++)
-        if (issued & (1u << t)) mbar_wait(full_bar(t), (last_ph >> t) & 1u, abort_p, gflags, false);
 }
 
 // Digits of one warp's slice [kslice, kslice + 32 CH) for activation rows
@@ -602,22 +551,6 @@ int launch_one(tpt_cuda_ctx *ctx, const CUtensorMap &tw, const float *x, const f
     return after_launch(ctx, "w4_gemv_tma");
 }
 
-// The nibble matrix [n rows, K/2 bytes] as the 3-D tensor {128 B, n rows, K/256
-// columns of 128 B} with box {128, 16, K/256} and 128B swizzle; rows past n
-// read as zero, and every address stays inside the matrix.
-bool make_tmap_nibbles(CUtensorMap *tm, const void *base, uint64_t n, uint64_t k) {
-    auto fn = encode_fn();
-    if (!fn || ((uintptr_t)base & 15) || (k % 256) || k / 256 > 256) return false;
-    cuuint64_t dims[3] = {128, n, k / 256};
-    cuuint64_t strides[2] = {k / 2, 128};
-    cuuint32_t box[3] = {128, (cuuint32_t)WG_ROWS, (cuuint32_t)(k / 256)};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 // M <= 2, K % 256 == 0, K <= 8192, x 16-byte aligned; returns handled = false
@@ -629,7 +562,7 @@ int launch_w4_gemv_tma(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cu
     if (m == 0 || m > 2 || k % 256 != 0 || k > (size_t)WG_MAX_KW * 512 || n > INT32_MAX) return TPT_OK;
     if (((uintptr_t)x & 15) != 0) return TPT_OK;
     CUtensorMap tw;
-    if (!make_tmap_nibbles(&tw, w->data, n, k)) return TPT_OK;
+    if (!make_tmap_rows3d(&tw, w->data, n, k / 2)) return TPT_OK;
     // slices of 256 k (16 consumer warps at K = 4096) while they fit, else 512
     const int ch = k <= (size_t)WG_MAX_KW * 256 ? 8 : 16;
     const int kw = (int)((k + 32 * ch - 1) / (32 * ch));
@@ -665,7 +598,7 @@ int launch_w4_small(tpt_cuda_ctx *ctx, const float *x, size_t m, const tpt_cuda_
     if (m < 3 || m > 8 || k % 256 != 0 || k > (size_t)WG_MAX_KW * 256 || n > INT32_MAX) return TPT_OK;
     if (((uintptr_t)x & 15) != 0) return TPT_OK;
     CUtensorMap tw;
-    if (!make_tmap_nibbles(&tw, w->data, n, k)) return TPT_OK;
+    if (!make_tmap_rows3d(&tw, w->data, n, k / 2)) return TPT_OK;
     const int MM = m <= 4 ? 4 : 8, T = (3 * MM + 7) / 8;
     const int kw = (int)((k + 255) / 256);
     const size_t stage = WG_ROWS * (k / 2), table = (size_t)kw * MM * 3 * 32 * 8;

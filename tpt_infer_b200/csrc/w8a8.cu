@@ -9,6 +9,8 @@
 //  - k_w8a8_gemv: M <= 4. One warp per output channel streams the K-contiguous
 //    weight row with 128-bit loads (all of a pass in flight) and dp4a.
 //  - k_w8a8_simt: general shapes (ragged M/N, K % 16 == 0); dp4a tiles.
+//  - 3 <= M <= 32 (uploaded weights, K <= 4096): the TMA-ring mma.sync kernel
+//    of w8a8_mma.cu;
 //  - the tcgen05 tensor-core kernels: K split over a thread-block cluster
 //    for 4 < M <= 64 in w8a8_ck.cu, SM-pair tiles for larger M in w8a8_tc.cu.
 // Weight layout in HBM: W^T [n, k] int8 row-major (K-major B operand), which
@@ -26,6 +28,8 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
 int build_weight_tmap(tpt_cuda_weights *w);
 int launch_w8a8_ck(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
+int launch_w8a8_mma(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
+                    const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq);
 
 namespace {
 
@@ -235,6 +239,11 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
     if (m == 0 || n == 0) return TPT_OK;
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     const int8_t *wt = (const int8_t *)w->data;
+    if (m >= 3 && m <= 32) {
+        bool handled = false;
+        int st = launch_w8a8_mma(ctx, a, m, w, a_scale, bias, act, y, acc, &handled, rq);
+        if (st || handled) return st;
+    }
     if (m <= 4) {
         // decode-like: SIMT stream of the weight rows (HBM-bound)
         // two 8-warp blocks per SM: the next launch's blocks fit beside them
