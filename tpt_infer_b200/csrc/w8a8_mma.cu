@@ -99,6 +99,18 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
         }
     }
 
+    // When one flush covers the CTA's run and every output has a thread, each
+    // thread's channel scale and bias are loaded now, off the flush's path.
+    const bool one_flush = P >= g1 - g0 && (g1 - g0) * WG_ROWS * M <= ncons;
+    float my_sc = 0.0f, my_bi = 0.0f;
+    if (one_flush && !ACC) {
+        const int idx = (int)threadIdx.x, n = (g0 + idx / (WG_ROWS * M)) * WG_ROWS + idx % WG_ROWS;
+        if (idx < (g1 - g0) * WG_ROWS * M && n < N) {
+            my_sc = __ldg(wscale + n);
+            if (bias) my_bi = __ldg(bias + n);
+        }
+    }
+
     int s = 0, gl = 0;
     uint32_t ph = 0;
     bool ok = true;
@@ -148,8 +160,9 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
                     if (ACC) {
                         ACC[o] = acc;
                     } else {
-                        float y = __fmul_rn(__int2float_rn(acc), __fmul_rn(a_scale, __ldg(wscale + n)));
-                        if (bias) y = __fadd_rn(y, __ldg(bias + n));
+                        const float sc = one_flush ? my_sc : __ldg(wscale + n);
+                        float y = __fmul_rn(__int2float_rn(acc), __fmul_rn(a_scale, sc));
+                        if (bias) y = __fadd_rn(y, one_flush ? my_bi : __ldg(bias + n));
                         y = apply_act(y, act);
                         if (Q)
                             Q[o] = requant_i8(y, q_scale);
