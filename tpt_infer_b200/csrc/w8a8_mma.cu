@@ -84,18 +84,25 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
     const int gq = lane >> 2, tq = lane & 3;
     const int kslice = warp * SL;
     const int ksteps = min(SL, K - kslice) / 32;
-    // activation fragments: tile tt, column gq = activation row 8 tt + gq;
-    // k-step j: k [32 j + 4 tq, +4) and [32 j + 16 + 4 tq, +4) of the slice
+    // The MMA's k positions 4 tq..4 tq+3 and 16+4 tq..16+4 tq+3 of k-step j are
+    // given the 8 consecutive k [32 j + 8 tq, +8) of the slice, identically in
+    // both operands (the sum over k is unchanged), so each fragment pair is one
+    // 8-byte load. Fragment row g is weight row pr = 2 (g & 3) + (g >> 2) (and
+    // pr + 8): the 4 rows of a half-warp then differ in swizzle bits 1-2 and
+    // its 8-byte loads hit 16 distinct banks pairs.
+    const int pr = ((gq & 3) << 1) | (gq >> 2);
+    // activation fragments: tile tt, column gq = activation row 8 tt + gq
     uint32_t bf[MT][CH][2];
 #pragma unroll
     for (int tt = 0; tt < MT; tt++) {
         const int m = 8 * tt + gq;
-        const int8_t *arow = A + (size_t)m * K + kslice + 4 * tq;
+        const int8_t *arow = A + (size_t)m * K + kslice + 8 * tq;
 #pragma unroll
         for (int j = 0; j < CH; j++) {
-            const bool v = m < M && j < ksteps;
-            bf[tt][j][0] = v ? __ldg(reinterpret_cast<const uint32_t *>(arow + 32 * j)) : 0u;
-            bf[tt][j][1] = v ? __ldg(reinterpret_cast<const uint32_t *>(arow + 32 * j + 16)) : 0u;
+            const uint2 v = (m < M && j < ksteps) ? __ldg(reinterpret_cast<const uint2 *>(arow + 32 * j))
+                                                  : make_uint2(0u, 0u);
+            bf[tt][j][0] = v.x;
+            bf[tt][j][1] = v.y;
         }
     }
 
@@ -119,14 +126,14 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
         int d[MT][4] = {};
         const uint32_t base = ring + (uint32_t)s * stage_bytes;
         // plain loads (ordered after the barrier wait by its memory clobber)
-        const uint32_t *stg = reinterpret_cast<const uint32_t *>(smem + (base - raw));
+        const uint2 *stg2 = reinterpret_cast<const uint2 *>(smem + (base - raw));
         if (ok) {
 #pragma unroll
             for (int j = 0; j < CH; j++) {
                 if (j < ksteps) {
-                    const uint32_t b = (uint32_t)kslice + 32u * j + 4u * tq;
-                    const uint32_t o0 = stage_off(gq, b) >> 2, o1 = stage_off(gq, b + 16u) >> 2;
-                    const uint32_t a[4] = {stg[o0], stg[o0 + 256u], stg[o1], stg[o1 + 256u]};  // rows gq, gq + 8
+                    const uint32_t o = stage_off(pr, (uint32_t)kslice + 32u * j + 8u * tq) >> 3;
+                    const uint2 r0 = stg2[o], r1 = stg2[o + 128u];  // weight rows pr, pr + 8
+                    const uint32_t a[4] = {r0.x, r1.x, r0.y, r1.y};
 #pragma unroll
                     for (int tt = 0; tt < MT; tt++) mma_s8(d[tt], a, bf[tt][j][0], bf[tt][j][1]);
                 }
@@ -134,12 +141,12 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
         }
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(empty_bar(s));
-        // d[tt]: weight rows gq (0, 1) and gq + 8 (2, 3), activation rows 8 tt + 2 tq (+1)
+        // d[tt]: weight rows pr (0, 1) and pr + 8 (2, 3), activation rows 8 tt + 2 tq (+1)
 #pragma unroll
         for (int tt = 0; tt < MT; tt++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const int m = 8 * tt + 2 * tq + (e & 1), r = gq + 8 * (e >> 1);
+                const int m = 8 * tt + 2 * tq + (e & 1), r = pr + 8 * (e >> 1);
                 part[((gl * MP + m) * KW + warp) * WG_ROWS + r] = d[tt][e];
             }
         if (++s == S) {
