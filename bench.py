@@ -453,7 +453,7 @@ def _conv_plan(be, N, H, W, C, OC, k, s, pad, seed, out_hw=None):
 
 def profile_kernels(args):
     """One case per main kernel, args.warmup + args.steps launches each, in this
-    order: W8A8 M=1 (GEMV), M=16 (cluster split-K), M=4096 (SM pair) at
+    order: W8A8 M=1 (GEMV), M=16 (small-batch MMA ring), M=4096 (SM pair) at
     K=N=4096; W4 M=1 (GEMV) and M=8 (small-batch digit-plane kernel) at K=4096,
     N=11008; BERT
     attention 64x128x12; INT8 convs of ResNet-18 at batch 64: a stage-1 3x3
