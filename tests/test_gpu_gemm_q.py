@@ -72,6 +72,24 @@ def test_w8a8_accumulators_bit_exact(cuda, m):
     w.free()
 
 
+def test_w8a8_pinned_host_buffers_pipelined(cuda):
+    """Page-locked host buffers with a large output take the chunked path (H2D,
+    GEMM and D2H of row chunks overlapped): the same bits, on two calls in a row."""
+    import torch
+
+    m, n, k = 1024, 4096, 1024  # 16 MB of f32 output: four row chunks
+    aq, sa, wq, ws, bias = w8a8_case(m, n, k, seed=900)
+    w = cuda.upload_i8(wq, ws, n, k)
+    a_pin = torch.from_numpy(aq).pin_memory()
+    y_pin = torch.empty(m * n, dtype=torch.float32).pin_memory()
+    want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, 1, threads=8)
+    for _ in range(2):
+        y_pin.zero_()
+        cuda.w8a8_gemm(a_pin.numpy(), m, k, sa, w, bias, 1, out=y_pin.numpy())
+        assert np.array_equal(y_pin.numpy(), want)
+    w.free()
+
+
 def test_w8a8_small_m_back_to_back(cuda):
     # the stream-K path combines partial tiles in a workspace that must be
     # clean again after every launch: run several shapes back to back on the

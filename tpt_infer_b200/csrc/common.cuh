@@ -45,6 +45,10 @@ struct tpt_cuda_ctx {
     bool capturing = false;
     uint64_t capture_launches0 = 0;
     uint64_t ws_gen = 0;
+    // copy streams and events of the pipelined host-buffer calls (created on
+    // first use): H2D on copy_in, D2H on copy_out, compute on `stream`
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    cudaEvent_t pipe_ev[2 * 8 + 2] = {};
 };
 
 struct tpt_cuda_weights {
@@ -97,6 +101,10 @@ constexpr size_t TPT_SK_SLOTS_OFFSET = TPT_SK_COUNTERS * sizeof(int);
 int ensure_sk(tpt_cuda_ctx *ctx, size_t slot_bytes);
 // Waits for the stream, then reads and clears the device error words.
 int sync_and_check(tpt_cuda_ctx *ctx);
+// copy streams + events of the pipelined host-buffer calls, created once
+int ensure_copy_streams(tpt_cuda_ctx *ctx);
+// true when p lies in page-locked (pinned or registered) host memory
+bool is_pinned_host(const void *p);
 // Returns TPT_CUDA_ERROR if the last launch failed, else TPT_OK; counts launches.
 int after_launch(tpt_cuda_ctx *ctx, const char *what, int n = 1);
 

@@ -129,6 +129,25 @@ int d2h(tpt_cuda_ctx *ctx, void *dst, const void *src, size_t bytes) {
     return e == cudaSuccess ? TPT_OK : cuda_fail(ctx, e, "D2H copy");
 }
 
+int ensure_copy_streams(tpt_cuda_ctx *ctx) {
+    if (ctx->copy_in) return TPT_OK;
+    cudaError_t e = cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking);
+    for (int i = 0; e == cudaSuccess && i < (int)(sizeof(ctx->pipe_ev) / sizeof(ctx->pipe_ev[0])); i++)
+        e = cudaEventCreateWithFlags(&ctx->pipe_ev[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "copy streams");
+    return TPT_OK;
+}
+
+bool is_pinned_host(const void *p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
 int sync_and_check(tpt_cuda_ctx *ctx) {
     if (ctx->capturing) return refuse_in_capture(ctx, "a synchronising call");
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
@@ -233,6 +252,14 @@ int tpt_cuda_ctx_destroy(tpt_cuda_ctx *ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->sk) cudaFree(ctx->sk);
     if (ctx->d_flags) cudaFree(ctx->d_flags);
+    if (ctx->copy_in) {
+        cudaStreamSynchronize(ctx->copy_in);
+        cudaStreamSynchronize(ctx->copy_out);
+        for (cudaEvent_t ev : ctx->pipe_ev)
+            if (ev) cudaEventDestroy(ev);
+        cudaStreamDestroy(ctx->copy_in);
+        cudaStreamDestroy(ctx->copy_out);
+    }
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return TPT_OK;

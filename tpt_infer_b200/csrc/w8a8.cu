@@ -344,6 +344,8 @@ int tpt_cuda_weights_shape(const tpt_cuda_weights *w, size_t *n, size_t *k) {
     return TPT_OK;
 }
 
+constexpr int PIPE_CHUNKS = 4;  // row chunks of a pipelined host-buffer call
+
 int tpt_cuda_w8a8_gemm(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, float a_scale,
                        const tpt_cuda_weights *w, const float *bias, int act, float *out) {
     CHECK_CTX(ctx);
@@ -361,8 +363,37 @@ int tpt_cuda_w8a8_gemm(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, f
     int8_t *da = st.take<int8_t>(an);
     float *dy = st.take<float>(on);
     float *db = bias ? st.take<float>(w->n) : nullptr;
-    TRY(h2d(ctx, da, a, an));
     if (bias) TRY(h2d(ctx, db, bias, w->n * 4));
+    // Large outputs from and to page-locked memory: row chunks pipelined, the
+    // H2D of chunk c + 1, the GEMM of chunk c and the D2H of chunk c - 1 in
+    // flight together (the two copy engines and the SMs), so the call costs
+    // about the larger of the two transfers instead of their sum.
+    const size_t rows = ((m + PIPE_CHUNKS - 1) / PIPE_CHUNKS + 127) / 128 * 128;
+    if (on * 4 >= ((size_t)16 << 20) && rows < m && !ctx->capturing && is_pinned_host(a) && is_pinned_host(out)) {
+        TRY(ensure_copy_streams(ctx));
+        cudaEvent_t start = ctx->pipe_ev[2 * PIPE_CHUNKS], fin = ctx->pipe_ev[2 * PIPE_CHUNKS + 1];
+        cudaError_t e = cudaEventRecord(start, ctx->stream);  // staging is free: prior work on the stream is done
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->copy_in, start, 0);
+        for (int c = 0; e == cudaSuccess && (size_t)c * rows < m; c++) {
+            const size_t r0 = (size_t)c * rows, rc = m - r0 < rows ? m - r0 : rows;
+            cudaEvent_t in_done = ctx->pipe_ev[2 * c], gemm_done = ctx->pipe_ev[2 * c + 1];
+            e = cudaMemcpyAsync(da + r0 * k, a + r0 * k, rc * k, cudaMemcpyHostToDevice, ctx->copy_in);
+            if (e == cudaSuccess) e = cudaEventRecord(in_done, ctx->copy_in);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, in_done, 0);
+            if (e != cudaSuccess) break;
+            TRY(launch_w8a8(ctx, da + r0 * k, rc, k, w, a_scale, db, act, dy + r0 * w->n, nullptr, Requant{}));
+            e = cudaEventRecord(gemm_done, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->copy_out, gemm_done, 0);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(out + r0 * w->n, dy + r0 * w->n, rc * w->n * 4, cudaMemcpyDeviceToHost,
+                                    ctx->copy_out);
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(fin, ctx->copy_out);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, fin, 0);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "pipelined w8a8_gemm");
+        return sync_and_check(ctx);
+    }
+    TRY(h2d(ctx, da, a, an));
     TRY(launch_w8a8(ctx, da, m, k, w, a_scale, db, act, dy, nullptr, Requant{}));
     TRY(d2h(ctx, out, dy, on * 4));
     return sync_and_check(ctx);
