@@ -192,6 +192,12 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     // ---------------- consumers: warp = k slice ----------------
     const int ncons = KW * 32;
     const int gq = lane >> 2, tq = lane & 3;  // MMA fragment group / thread in group
+    // Fragment row g is weight row pr = 2 (g & 3) + (g >> 2) (and pr + 8), and
+    // MMA k positions 4 tq.. / 16 + 4 tq.. of k-step j hold the 8 consecutive k
+    // 64 (j / 2) + 16 tq + 8 (j % 2) (identically in both operands, so the sums
+    // are unchanged): a lane's nibbles of a k-step pair are one 8-byte load and
+    // a half-warp's rows differ in swizzle bits 1-2 (conflict-free).
+    const int pr = ((gq & 3) << 1) | (gq >> 2);
     const int kslice = warp * SL;
     const int ksteps = min(SL, K - kslice) / 32;
     uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
     for (int j = 0; j < CH; j++) {
         bf[j][0] = bf[j][1] = 0u;
         if (gq < 3 * MM) {
-            const int k8 = 32 * j + 8 * tq;
+            const int k8 = 64 * (j >> 1) + 16 * tq + 8 * (j & 1);
             const uint32_t *src = mytab + ((bi * 3 + bp) * 32 + k8 / CH) * (CH / 4) + 2 * ((k8 % CH) / 8);
             bf[j][0] = src[0];
             bf[j][1] = src[1];
@@ -257,17 +263,23 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         // plain loads (ordered after the barrier wait by its memory clobber),
         // free to be issued all at once ahead of the MMAs
         const uint32_t *stg = reinterpret_cast<const uint32_t *>(smem + (base - raw));
+        const uint2 *stg2 = reinterpret_cast<const uint2 *>(stg);
+        uint2 r0 = make_uint2(0u, 0u), r1 = make_uint2(0u, 0u);
         if (ok) {
 #pragma unroll
             for (int j = 0; j < CH; j++) {
                 if (j < ksteps) {
-                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq) >> 2;
-                    const uint32_t w0 = stg[off], w1 = stg[off + 256u];
+                    if ((j & 1) == 0) {  // the nibbles of k-steps j and j + 1, rows pr and pr + 8
+                        const uint32_t o = stage_off(pr, (uint32_t)(kslice >> 1) + 16u * j + 8u * tq) >> 3;
+                        r0 = stg2[o];
+                        r1 = stg2[o + 128u];
+                    }
+                    const uint32_t w0 = (j & 1) ? r0.y : r0.x, w1 = (j & 1) ? r1.y : r1.x;
                     uint32_t a[4];
-                    a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq, even k: q + 8
-                    a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row gq + 8, even k
-                    a[2] = ((w0 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq, odd k
-                    a[3] = ((w1 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row gq + 8, odd k
+                    a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row pr, even k: q + 8
+                    a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;          // row pr + 8, even k
+                    a[2] = ((w0 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row pr, odd k
+                    a[3] = ((w1 >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;   // row pr + 8, odd k
                     if (j % 4 == 0)
                         mma_u8s8(d, a, bf[j][0], bf[j][1]);
                     else
@@ -279,7 +291,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         }
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(empty_bar(s));
-        // d: rows gq (d0, d1) and gq + 8 (d2, d3), columns 2 tq, 2 tq + 1.
+        // d: rows pr (d0, d1) and pr + 8 (d2, d3), columns 2 tq, 2 tq + 1.
         // Activation row 0 = columns 0..2 (tq 0: A0 A1; tq 1: A2 in d0 / d2),
         // row 1 = columns 3..5 (tq 1: A0 in d1 / d3; tq 2: A1 A2).
         const int nx0 = __shfl_down_sync(0xffffffffu, d[0], 1), nx2 = __shfl_down_sync(0xffffffffu, d[2], 1);
@@ -301,7 +313,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
                 float acc = 0.0f;
                 if (vi < M && ok)
                     for (int kk = 0; kk < ksteps * 32; kk++) {
-                        const uint32_t wd = stg[stage_off(gq + 8 * h, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)) >> 2];
+                        const uint32_t wd = stg[stage_off(pr + 8 * h, (uint32_t)(kslice >> 1) + 4u * (kk >> 3)) >> 2];
                         const int nb = (int)((wd >> (4 * (kk & 7))) & 0xFu);
                         acc = fmaf(__ldg(X + (size_t)vi * K + kslice + kk), (float)(nb - ((nb & 8) << 1)), acc);
                     }
@@ -310,8 +322,8 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         }
         if (vi >= 0) {
             float *dst = part + ((gl * MM + vi) * KW + warp) * WG_ROWS;
-            dst[gq] = v[0];
-            dst[gq + 8] = v[1];
+            dst[pr] = v[0];
+            dst[pr + 8] = v[1];
         }
         if (++s == S) {
             s = 0;
@@ -388,6 +400,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
 
     const int ncons = KW * 32;
     const int gq = lane >> 2, tq = lane & 3;
+    const int pr = ((gq & 3) << 1) | (gq >> 2);  // weight row of fragment row gq (see the GEMV)
     const int kslice = warp * SL;
     const int ksteps = min(SL, K - kslice) / 32;
     uint32_t *mytab = tab + warp * MM * 3 * 32 * (CH / 4);
@@ -404,7 +417,7 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         for (int j = 0; j < CH; j++) {
             bf[tt][j][0] = bf[tt][j][1] = 0u;
             if (c < 3 * MM) {
-                const int k8 = 32 * j + 8 * tq;
+                const int k8 = 64 * (j >> 1) + 16 * tq + 8 * (j & 1);
                 const uint32_t *src = mytab + (c * 32 + k8 / CH) * (CH / 4) + 2 * ((k8 % CH) / 8);
                 bf[tt][j][0] = src[0];
                 bf[tt][j][1] = src[1];
@@ -444,12 +457,18 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
         }
         const uint32_t base = ring + (uint32_t)s * stage_bytes;
         const uint32_t *stg = reinterpret_cast<const uint32_t *>(smem + (base - raw));
+        const uint2 *stg2 = reinterpret_cast<const uint2 *>(stg);
+        uint2 r0 = make_uint2(0u, 0u), r1 = make_uint2(0u, 0u);
         if (ok) {
 #pragma unroll
             for (int j = 0; j < CH; j++) {
                 if (j < ksteps) {
-                    const uint32_t off = stage_off(gq, (uint32_t)(kslice >> 1) + 16u * j + 4u * tq) >> 2;
-                    const uint32_t w0 = stg[off], w1 = stg[off + 256u];
+                    if ((j & 1) == 0) {  // the nibbles of k-steps j and j + 1, rows pr and pr + 8
+                        const uint32_t o = stage_off(pr, (uint32_t)(kslice >> 1) + 16u * j + 8u * tq) >> 3;
+                        r0 = stg2[o];
+                        r1 = stg2[o + 128u];
+                    }
+                    const uint32_t w0 = (j & 1) ? r0.y : r0.x, w1 = (j & 1) ? r1.y : r1.x;
                     uint32_t a[4];
                     a[0] = (w0 ^ 0x88888888u) & 0x0F0F0F0Fu;
                     a[1] = (w1 ^ 0x88888888u) & 0x0F0F0F0Fu;
@@ -466,10 +485,10 @@ __global__ void __launch_bounds__(WG_MAX_THREADS, 1)
 #pragma unroll
         for (int tt = 0; tt < T; tt++) {
             const int c = 8 * tt + 2 * tq;
-            mysc[gq * SC + c] = d[tt][0];
-            mysc[gq * SC + c + 1] = d[tt][1];
-            mysc[(gq + 8) * SC + c] = d[tt][2];
-            mysc[(gq + 8) * SC + c + 1] = d[tt][3];
+            mysc[pr * SC + c] = d[tt][0];
+            mysc[pr * SC + c + 1] = d[tt][1];
+            mysc[(pr + 8) * SC + c] = d[tt][2];
+            mysc[(pr + 8) * SC + c + 1] = d[tt][3];
         }
         __syncwarp();
         // lane -> (weight row r = lane % 16, activation row i = 2 u + lane / 16)
