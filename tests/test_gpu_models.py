@@ -112,6 +112,39 @@ def test_bert_plan_two_layers(cuda, B, S):
     p.close()
 
 
+@pytest.mark.parametrize("rows,cols", [(300, 768), (37, 500)])
+def test_plan_add_layernorm_fusion(cuda, rows, cols):
+    # ADD_ACT -> LAYERNORM (-> QUANTIZE) runs as one residual layernorm when the
+    # sum is not fetched: the LayerNorm output and its int8 copy are the same
+    # bits as the separate ops give (the sum fetched), for the 768-wide and the
+    # generic kernel
+    from tpt_infer_b200 import graphs, synth
+
+    a, r = synth.normal(rows * cols, 71), synth.normal(rows * cols, 72)
+    g, b = synth.normal(cols, 73, 1.0, 0.1), synth.normal(cols, 74, 0.0, 0.1)
+    p = graphs.Plan(cuda)
+    ta, tr = p.tensor(graphs.F32, rows * cols), p.tensor(graphs.F32, rows * cols)
+    ts, th = p.tensor(graphs.F32, rows * cols), p.tensor(graphs.F32, rows * cols)
+    tq = p.tensor(graphs.I8, rows * cols)
+    p.op(graphs.OP_ADD_ACT, ta, ts, in1=tr, dims=(rows * cols,))
+    p.op(graphs.OP_LAYERNORM, ts, th, in1=p.const(g), in2=p.const(b), f0=1e-5, dims=(rows, cols))
+    p.op(graphs.OP_QUANTIZE, th, tq, dims=(rows * cols,))
+    p.finalize()
+    p.calibrate(True)
+    p.run({ta: a, tr: r}, [th])
+    p.freeze()
+    s_sep, h_sep, q_sep = p.run({ta: a, tr: r}, [ts, th, tq])  # the sum fetched: separate ops
+    h_fused, q_fused = p.run({ta: a, tr: r}, [th, tq])         # fused
+    assert np.array_equal(s_sep, (a + r).astype(np.float32))
+    assert np.array_equal(h_fused, h_sep)
+    n = rows * cols  # int8 outputs come back as raw bytes at the front of the buffer
+    assert np.array_equal(np.frombuffer(q_fused.tobytes()[:n], np.int8), np.frombuffer(q_sep.tobytes()[:n], np.int8))
+    x = (a + r).astype(np.float64).reshape(rows, cols)
+    ref = (x - x.mean(1, keepdims=True)) / np.sqrt(x.var(1, keepdims=True) + 1e-5) * g + b
+    assert np.max(np.abs(h_fused.reshape(rows, cols) - ref)) < 1e-4
+    p.close()
+
+
 @pytest.mark.parametrize("B,S", [(2, 128), (1, 77), (3, 40), (1, 1)])
 def test_attention_op(cuda, B, S):
     # the fused attention op alone against the oracle's MatMul / Softmax / MatMul

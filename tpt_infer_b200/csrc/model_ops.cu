@@ -22,7 +22,8 @@ namespace {
 // the row held in registers (cols <= 32 * LN_MAX).
 constexpr int LN_MAX = 32;
 __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ b,
-                            float *__restrict__ y, int rows, int cols, float eps, int8_t *__restrict__ qout, float qs) {
+                            float *__restrict__ y, int rows, int cols, float eps, int8_t *__restrict__ qout, float qs,
+                            const float *__restrict__ res) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -35,7 +36,7 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 #pragma unroll
         for (int i = 0; i < LN_MAX; i++) {
             const int c = lane + 32 * i;
-            v[i] = c < cols ? xr[c] : 0.0f;
+            v[i] = c < cols ? (res ? xr[c] + res[(size_t)r * cols + c] : xr[c]) : 0.0f;
             s += v[i];
         }
         const float mean = __fdiv_rn(warp_sum(s), (float)cols);
@@ -64,7 +65,8 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 // 16-byte loads and stores and a 4-byte store of the int8 copy.
 template <int G>
 __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restrict__ g, const float4 *__restrict__ b,
-                             float4 *__restrict__ y, int rows, float eps, uint32_t *__restrict__ qout, float qs) {
+                             float4 *__restrict__ y, int rows, float eps, uint32_t *__restrict__ qout, float qs,
+                             const float4 *__restrict__ res) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -79,6 +81,10 @@ __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restr
 #pragma unroll
         for (int i = 0; i < G; i++) {
             v[i] = xr[lane + 32 * i];
+            if (res) {  // LayerNorm(x + res): the residual add of the ADD_ACT it replaces, same rounding
+                const float4 z = res[(size_t)r * cols4 + lane + 32 * i];
+                v[i] = make_float4(v[i].x + z.x, v[i].y + z.y, v[i].z + z.z, v[i].w + z.w);
+            }
             s += v[i].x + v[i].y + v[i].z + v[i].w;
         }
         const float mean = __fdiv_rn(warp_sum(s), n);
@@ -321,16 +327,18 @@ __global__ void k_absmax_acc(const float *__restrict__ x, size_t n, unsigned *ce
 }  // namespace
 
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
-                     size_t cols, float eps, int8_t *q, float qs) {
+                     size_t cols, float eps, int8_t *q, float qs, const float *res) {
     if (cols > 32 * LN_MAX || rows > INT32_MAX) return TPT_UNSUPPORTED;
     const unsigned grid = grid_1d(rows * 32, 256, (unsigned)ctx->sm_count * 16);
-    const bool a16 = ((((uintptr_t)x | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) & 15) == 0) && ((uintptr_t)q & 3) == 0;
+    const bool a16 = ((((uintptr_t)x | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y | (uintptr_t)res) & 15) == 0) &&
+                     ((uintptr_t)q & 3) == 0;
     if (a16 && cols == 768) {  // the BERT hidden size
         launch_pdl(k_layernorm4<6>, grid, 256, 0, ctx->stream, (const float4 *)x, (const float4 *)g, (const float4 *)b,
-                                                       (float4 *)y, (int)rows, eps, (uint32_t *)q, qs);
+                                                       (float4 *)y, (int)rows, eps, (uint32_t *)q, qs,
+                   (const float4 *)res);
         return after_launch(ctx, "layernorm");
     }
-    launch_pdl(k_layernorm, grid, 256, 0, ctx->stream, x, g, b, y, (int)rows, (int)cols, eps, q, qs);
+    launch_pdl(k_layernorm, grid, 256, 0, ctx->stream, x, g, b, y, (int)rows, (int)cols, eps, q, qs, res);
     return after_launch(ctx, "layernorm");
 }
 

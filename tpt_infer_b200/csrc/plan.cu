@@ -23,7 +23,7 @@
 
 namespace tpt {
 int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const float *b, float *y, size_t rows,
-                     size_t cols, float eps, int8_t *q = nullptr, float qs = 0.0f);
+                     size_t cols, float eps, int8_t *q = nullptr, float qs = 0.0f, const float *res = nullptr);
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
                      int8_t *q = nullptr, float qs = 0.0f);
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
@@ -484,6 +484,36 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
                                           (int)o.dims[2], (int)o.dims[3], o.f0, Q(p, q.out), nq.frozen);
                 if (st) return st;
                 i++;
+                continue;
+            }
+        }
+        // ADD_ACT (no activation) -> LAYERNORM of the sum (read by no other op,
+        // not fetched): the layernorm adds its two inputs itself (the same f32
+        // add), so the sum is neither written nor read back; a QUANTIZE of the
+        // layernorm's output folds in as below.
+        if (o.kind == TPT_OP_ADD_ACT && o.act == 0 && i + 1 < p->ops.size()) {
+            const tpt_plan_op &l = p->ops[i + 1].op;
+            const PlanTensor &t = p->tensors[o.out];
+            if (l.kind == TPT_OP_LAYERNORM && l.in0 == o.out && t.readers == 1 && !is_output(out_ids, n_out, o.out) &&
+                l.dims[0] * l.dims[1] == o.dims[0]) {
+                int8_t *qo = nullptr;
+                float qs = 0.0f;
+                size_t fused = 1;
+                if (!p->calibrating && i + 2 < p->ops.size()) {
+                    PlanOp &nq = p->ops[i + 2];
+                    const tpt_plan_op &q = nq.op;
+                    if (q.kind == TPT_OP_QUANTIZE && q.in0 == l.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                        q.dims[0] == p->tensors[l.out].numel) {
+                        qo = Q(p, q.out);
+                        qs = nq.frozen;
+                        p->tensors[q.out].scale = qs;
+                        fused = 2;
+                    }
+                }
+                int st = launch_layernorm(p->ctx, F(p, o.in0), F(p, l.in1), F(p, l.in2), F(p, l.out), l.dims[0],
+                                          l.dims[1], l.f0, qo, qs, F(p, o.in1));
+                if (st) return st;
+                i += fused;
                 continue;
             }
         }
