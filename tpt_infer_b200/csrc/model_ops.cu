@@ -173,6 +173,36 @@ __global__ void k_nchw_to_nhwc_q8(const float *__restrict__ x, int8_t *__restric
     }
 }
 
+// The ResNet stem's form of the same conversion (2x2 space-to-depth, C <= 4
+// channels padded to Cp = 4): one thread per output pixel, its 16 bytes as one
+// 16-byte store; the 2 x 2 input pixels of each channel are two 8-byte loads
+// (x even, W even), consecutive threads reading consecutive pairs.
+__global__ void k_nchw_to_nhwc_q8_s2d4(const float *__restrict__ x, uint4 *__restrict__ q, int N, int C, int H, int W,
+                                       float scale) {
+    pdl_wait();
+    pdl_trigger();
+    const int Ho = H >> 1, Wo = W >> 1;
+    const int total = N * Ho * Wo;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < total; p += gridDim.x * blockDim.x) {
+        const int n = p / (Ho * Wo), r = p - n * (Ho * Wo), oy = r / Wo, ox = r - oy * Wo;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};  // word sub = dy * 2 + dx, byte c
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            if (c >= C) break;
+#pragma unroll
+            for (int dy = 0; dy < 2; dy++) {
+                const float2 v = __ldg(reinterpret_cast<const float2 *>(
+                    x + (((size_t)n * C + c) * H + 2 * oy + dy) * W + 2 * ox));
+                const uint32_t b0 = (uint8_t)round_clamp_i8(__fdiv_rn(v.x, scale), -127.0f, 127.0f);
+                const uint32_t b1 = (uint8_t)round_clamp_i8(__fdiv_rn(v.y, scale), -127.0f, 127.0f);
+                w[2 * dy] |= b0 << (8 * c);
+                w[2 * dy + 1] |= b1 << (8 * c);
+            }
+        }
+        q[p] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // im2col of an NHWC int8 tensor: row m = (n, oy, ox), column (ky, kx, c),
 // zero for padded taps and for columns in [K, Kp). One warp per output row:
 // the row's pixel is decoded once (32-bit index math), lanes walk the row's
@@ -368,6 +398,12 @@ int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, 
     if (s2d < 1) s2d = 1;
     if (W <= 0) W = HW;  // no width given: only s2d = 1 is possible
     if (s2d > 2 || HW % W || (W % s2d) || ((HW / W) % s2d)) return TPT_UNSUPPORTED;
+    if (s2d == 2 && Cp == 4 && C <= 4 && ((uintptr_t)x & 7) == 0 && ((uintptr_t)q & 15) == 0 &&
+        (size_t)N * HW / 4 < 0x7fffffff) {
+        launch_pdl(k_nchw_to_nhwc_q8_s2d4, grid_1d((size_t)N * HW / 4, 256, (unsigned)ctx->sm_count * 8), 256, 0,
+                   ctx->stream, x, reinterpret_cast<uint4 *>(q), N, C, HW / W, W, scale);
+        return after_launch(ctx, "nchw_to_nhwc_q8");
+    }
     launch_pdl(k_nchw_to_nhwc_q8, grid_1d((size_t)N * Cp * HW, 256, (unsigned)ctx->sm_count * 8), 256, 0, ctx->stream,
                x, q, N, C, HW, W, Cp, s2d, scale);
     return after_launch(ctx, "nchw_to_nhwc_q8");
