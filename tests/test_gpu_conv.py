@@ -75,3 +75,54 @@ def test_conv_implicit_gemm_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requant):
         assert np.array_equal(fused, want)
         assert np.array_equal(split, want)
     p.close()
+
+
+@pytest.mark.parametrize("N,H,W,C,OC,k,s,pad", [CASES[i] for i in (0, 2, 4, 7, 9)])
+@pytest.mark.parametrize("requant", [False, True])
+@pytest.mark.parametrize("res_first", [False, True])
+def test_conv_residual_epilogue_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requant, res_first):
+    # IM2COL -> LINEAR -> ADD_ACT(relu) with a residual [-> QUANTIZE of the sum]:
+    # with the conv output not fetched the residual add folds into the conv
+    # epilogue (the sum, and its int8 copy, from one launch); fetching the conv
+    # output keeps the separate ADD_ACT. Both equal the oracle's conv plus a
+    # float32 add and ReLU, bit for bit, with the residual as either input.
+    from tpt_infer_b200 import graphs
+
+    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    M, K = N * OH * OW, k * k * C
+    seed = 7500 + N * 131 + C + OC + k
+    x = O.normal(N * H * W * C, seed)
+    r = O.normal(M * OC, seed + 3)
+    sx = np.float32(O.sym_scale(O.absmax(x)))
+    wq, ws = O.quantize_i8_symmetric_per_channel(O.normal(OC * K, seed + 1, 0.0, 0.05), OC)
+    bias = O.normal(OC, seed + 2, 0.0, 0.1)
+    p = graphs.Plan(cuda)
+    w = cuda.upload_i8(wq, ws, OC, K)
+    p.weights.append(w)
+    tx, txq = p.tensor(graphs.F32, x.size), p.tensor(graphs.I8, x.size)
+    col, ty = p.tensor(graphs.I8, M * K), p.tensor(graphs.F32, M * OC)
+    tr, ts = p.tensor(graphs.F32, M * OC), p.tensor(graphs.F32, M * OC)
+    p.op(graphs.OP_QUANTIZE, tx, txq, f0=float(sx), dims=(x.size,))
+    p.op(graphs.OP_IM2COL, txq, col, dims=(N, H, W, C, k, k, s, s, pad, pad, OH, OW, K))
+    p.op(graphs.OP_LINEAR, col, ty, in1=p.const(bias), w=w, act=graphs.ACT_NONE, dims=(M,))
+    a0, a1 = (tr, ty) if res_first else (ty, tr)
+    p.op(graphs.OP_ADD_ACT, a0, ts, in1=a1, act=graphs.ACT_RELU, dims=(M * OC,))
+    sy = np.float32(0.05)
+    tsq = p.tensor(graphs.I8, M * OC)
+    if requant:
+        p.op(graphs.OP_QUANTIZE, ts, tsq, f0=float(sy), dims=(M * OC,))
+    p.finalize()
+
+    xq = O.quantize_i8_static(x, sx).reshape(N, H, W, C)
+    col_o, _, _ = OM._im2col(xq, k, s, pad, K)
+    conv = O.w8a8_gemm(col_o, wq, M, OC, K, sx, ws, bias, O.ACT_NONE, threads=8)
+    want = np.maximum(conv + r, np.float32(0.0)).astype(np.float32)
+    outs = [ts, tsq] if requant else [ts]
+    fused = p.run({tx: x, tr: r}, outs)
+    split = p.run({tx: x, tr: r}, [ty] + outs)
+    assert np.array_equal(split[0], conv)
+    for got in (fused, split[1:]):
+        assert np.array_equal(got[0], want)
+        if requant:
+            assert np.array_equal(np.frombuffer(got[1].tobytes()[:M * OC], np.int8), O.quantize_i8_static(want, sy))
+    p.close()

@@ -145,6 +145,13 @@ struct Requant {
     float scale = 0.0f;
 };
 
+// A residual folded into an epilogue: y = act(y + r[row, col]), r f32 with the
+// output's shape (the ADD_ACT op's arithmetic)
+struct Residual {
+    const float *r = nullptr;
+    int act = 0;
+};
+
 // ---- launchers implemented across the .cu files (device pointers, async) ----
 int launch_add(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t n);
 int launch_unary(tpt_cuda_ctx *ctx, int op, const float *a, float *out, size_t n);  // 1 relu 2 sigmoid 3 gelu
@@ -299,6 +306,50 @@ __device__ __forceinline__ int8_t round_clamp_i8(float v, float lo, float hi) {
 // quantize_i8_static's rule for one value: clamp(roundf(y / scale), -127, 127)
 __device__ __forceinline__ int8_t requant_i8(float y, float scale) {
     return round_clamp_i8(__fdiv_rn(y, scale), -127.0f, 127.0f);
+}
+
+// The same rule without a division, for scales in [2^-40, 2^40] (requant_fast_ok).
+// rs = RN(1 / s) (__frcp_rn). q1 = y * rs is within a few ulps of y / s; one
+// residual step (r = y - s q by FMA, q += r rs) makes it faithful, and a second
+// is Markstein's correction step (P. Markstein, IBM J. Res. Dev. 34(1), 1990),
+// which turns a faithful quotient into the correctly rounded one, the IEEE
+// quotient, whenever the residual is exact. The residual can be inexact only
+// when it underflows, for quotients far below 0.5 that round to 0 either way;
+// |y| > 2^80 clamps to +-127 whatever the quotient, and NaN gives 0. Rounding
+// is half away from zero (roundf) on the value clamped to [-128, 128], with no
+// branch, so the 32 values of an epilogue chunk interleave.
+__device__ __forceinline__ bool requant_fast_ok(float s) { return s >= 0x1p-40f && s <= 0x1p40f; }
+__device__ __forceinline__ int8_t requant_i8_fast(float y, float s, float rs) {
+    const float q1 = __fmul_rn(y, rs);
+    const float q2 = __fmaf_rn(__fmaf_rn(-s, q1, y), rs, q1);
+    float q = __fmaf_rn(__fmaf_rn(-s, q2, y), rs, q2);
+    q = fabsf(y) <= 0x1p80f ? q : y;
+    const float c = fminf(fmaxf(q, -128.0f), 128.0f);
+    const float t = truncf(c);
+    const float f = __fsub_rn(c, t);  // exact, the sign of c
+    int n = (int)t + (f >= 0.5f ? 1 : 0) - (f <= -0.5f ? 1 : 0);
+    n = n > 127 ? 127 : (n < -127 ? -127 : n);
+    return isnan(q) ? (int8_t)0 : (int8_t)n;
+}
+
+// requant_i8 of 32 values (f32 bits) packed 4 to a word, low byte first
+__device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s, float rs, bool fast,
+                                               uint32_t (&qb)[8]) {
+    if (fast) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            qb[j / 4] = (uint32_t)(uint8_t)requant_i8_fast(__uint_as_float(v[j]), s, rs) |
+                        ((uint32_t)(uint8_t)requant_i8_fast(__uint_as_float(v[j + 1]), s, rs) << 8) |
+                        ((uint32_t)(uint8_t)requant_i8_fast(__uint_as_float(v[j + 2]), s, rs) << 16) |
+                        ((uint32_t)(uint8_t)requant_i8_fast(__uint_as_float(v[j + 3]), s, rs) << 24);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            qb[j / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j]), s) |
+                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 1]), s) << 8) |
+                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 2]), s) << 16) |
+                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 3]), s) << 24);
+    }
 }
 
 }  // namespace tpt

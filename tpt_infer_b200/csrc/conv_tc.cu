@@ -48,7 +48,8 @@ namespace {
 using namespace tc;
 
 constexpr int CV_BM = 128;                  // output pixels per tile (MMA M)
-constexpr int CV_OUT_BYTES = 4 * 2 * 4096;  // epilogue staging: 4 warps x 2 buffers of 32 x 32 f32
+constexpr int CV_WARP_OUT = 3 * 4096 + 2 * 1024;  // epilogue staging per warp: 3 f32 + 2 int8 32 x 32 tiles
+constexpr int CV_OUT_BYTES = 4 * CV_WARP_OUT;
 // activation operand modes: gather with 16- or 4-byte chunks (128-byte
 // k-blocks), TMA im2col with 128- or 64-byte k-blocks
 enum { CV_GATHER16 = 0, CV_GATHER4 = 1, CV_IM2COL128 = 2, CV_IM2COL64 = 3 };
@@ -71,7 +72,7 @@ struct ConvCfg {
     static constexpr int STAGES_FIT = (232448 - CV_OUT_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + CV_OUT_BYTES + (2 * STAGES + 5) * 8 + 1024;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + CV_OUT_BYTES + (2 * STAGES + 5 + 12) * 8 + 1024;
     static_assert(SMEM_BYTES + 3 * CV_BM * 4 + 16 <= 232448, "shared memory (dynamic + the static gather table)");
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
     static_assert(STAGES >= 3, "stages");
@@ -133,10 +134,11 @@ __device__ __forceinline__ void cp_async_wait_upto(int n) {
 template <int BN, int MODE>
 __global__ void __launch_bounds__(cv_threads(MODE), 1)
     k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                const __grid_constant__ CUtensorMap tmY, int tma_store,
+                const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmQ,
+                const __grid_constant__ CUtensorMap tmR, int tma_store, int tma_q, int tma_r,
                 const int8_t *__restrict__ X, ConvShape cs, int OC, float a_scale, const float *__restrict__ wscale,
                 const float *__restrict__ bias, int act, float *__restrict__ Y, int8_t *__restrict__ Q,
-                float q_scale, unsigned *gflags) {
+                float q_scale, const float *__restrict__ R, int ract, unsigned *gflags) {
     using Cfg = ConvCfg<BN, MODE>;
     constexpr int S = Cfg::STAGES;
     constexpr bool TMA_A = cv_tma(MODE);
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
             mbar_init(tempty_bar(b), 4);
         }
         mbar_init(drain_bar, 1);
+        for (int b = 0; b < 12; b++) mbar_init(bars + 8u * (2 * S + 5 + b), 1);  // residual tiles, 3 per epilogue warp
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         if (TMA_A) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
@@ -350,13 +353,43 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
         while (npend > 0) retire(npend - 1);
     } else {
         // ---------------- epilogue (warps 2..5): thread = output pixel ----------------
+        // Per warp: a ring of three 32 x 32 f32 tiles (128B swizzle) and two
+        // 32 x 32 int8 tiles (32B swizzle). A chunk's residual block arrives in
+        // its f32 tile by TMA two chunks ahead; the result is written back in
+        // place and leaves, with its int8 copy, as one bulk store group.
         const int q = warp & 3;  // TMEM lane quarter
         const int e = warp - 2;
-        const uint32_t stage_s = staging + (uint32_t)(e * 8192);
-        uint8_t *stage_g = smem_raw + (stage_s - raw);
-        int buf = 0, acc = 0;
-        uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const uint32_t ys = staging + (uint32_t)(e * CV_WARP_OUT), qs = ys + 3u * 4096u;
+        uint8_t *yg = smem_raw + (ys - raw);
+        auto rbar = [&](int b) { return bars + 8u * (2 * S + 5 + 3 * e + b); };
+        const bool bulk = (Y && tma_store) || (Q && tma_q);
+        const float q_rs = __frcp_rn(q_scale);
+        const bool q_fast = requant_fast_ok(q_scale);
+        int acc = 0, k = 0;
+        uint32_t acc_phase = 0, rphase = 0, rpend = 0;
+        int pt = blockIdx.x, pcc = 0, pk = 0;  // residual prefetch cursor: tile, chunk, sequence number
+        auto issue_r = [&]() {
+            if (pt >= ntiles) return;
+            const int mt = pt / tiles_n, nt = pt - mt * tiles_n, mrow0 = mt * CV_BM + q * 32, b = pk % 3;
+            if (mrow0 < M) {  // blocks entirely below the last row are neither loaded nor stored
+                rpend |= 1u << b;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(rbar(b), 4096);
+                    tma_load_2d(ys + (uint32_t)(b * 4096), &tmR, rbar(b), nt * BN + pcc * 32, mrow0);
+                }
+            }
+            pk++;
+            if (++pcc == BN / 32 || nt * BN + pcc * 32 >= OC) {
+                pcc = 0;
+                pt += gridDim.x;
+            }
+        };
+        if (tma_r) {
+            issue_r();
+            issue_r();
+        }
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             int okw = 0;
             if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
             okw = __shfl_sync(0xffffffffu, okw, 0);
@@ -364,56 +397,98 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
             tc_fence_after();
             const int mt = t / tiles_n, nt = t - mt * tiles_n;
             const int mrow0 = mt * CV_BM + q * 32, m = mrow0 + lane;
+            const bool live = mrow0 < M;
             const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; cc++) {
+            for (int cc = 0; cc < BN / 32; cc++, k++) {
                 const int n0 = nt * BN + cc * 32;
                 if (n0 >= OC) break;
+                const int b = k % 3;
+                uint8_t *sb = yg + b * 4096 + lane * 128;
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(cc * 32), v);
                 tmem_wait_ld();
                 w8a8_epi32(v, n0, OC, a_scale, wscale, bias, act);
-                if (Q) {
-                    if (m < M) {
-                        uint32_t b[8];
+                if (R && tma_r) {  // residual: y = ract(conv + r), the ADD_ACT op's f32 add
+                    if (live) {
+                        int okr = 0;
+                        if (lane == 0) okr = mbar_wait(rbar(b), (rphase >> b) & 1u, abort_p, gflags, true) ? 1 : 0;
+                        okr = __shfl_sync(0xffffffffu, okr, 0);
+                        __syncwarp();  // lane 0's completed wait orders the tile's bytes for the warp
+                        if (!okr) {
+                            ok = false;
+                            break;
+                        }
+                        rphase ^= 1u << b;
+                        rpend &= ~(1u << b);
 #pragma unroll
-                        for (int jj = 0; jj < 32; jj += 4)
-                            b[jj / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj]), q_scale) |
-                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 1]), q_scale) << 8) |
-                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 2]), q_scale) << 16) |
-                                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[jj + 3]), q_scale) << 24);
-                        int8_t *dst = Q + (size_t)m * OC + n0;
-                        if (n0 + 32 <= OC && (OC & 15) == 0) {
-                            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
-                            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(b[4], b[5], b[6], b[7]);
-                        } else {
-                            for (int jj = 0; jj < 32; jj++)
-                                if (n0 + jj < OC) dst[jj] = (int8_t)(b[jj / 4] >> (8 * (jj % 4)));
+                        for (int c4 = 0; c4 < 8; c4++) {
+                            const float4 r = *reinterpret_cast<const float4 *>(sb + ((c4 ^ (lane & 7)) << 4));
+                            v[4 * c4] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4]) + r.x, ract));
+                            v[4 * c4 + 1] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 1]) + r.y, ract));
+                            v[4 * c4 + 2] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 2]) + r.z, ract));
+                            v[4 * c4 + 3] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 3]) + r.w, ract));
                         }
                     }
-                } else if (tma_store) {
-                    if (mrow0 < M) {  // a block entirely below the last row is not stored
-                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                        __syncwarp();
-                        uint8_t *sb = stage_g + buf * 4096 + lane * 128;
+                } else if (R && m < M) {
+                    const float *src = R + (size_t)m * OC + n0;
+                    for (int jj = 0; jj < 32; jj++)
+                        if (n0 + jj < OC) v[jj] = __float_as_uint(apply_act(__uint_as_float(v[jj]) + src[jj], ract));
+                }
+                if (Q && live) {
+                    uint32_t qb[8];
+                    requant_pack32(v, q_scale, q_rs, q_fast, qb);
+                    if (tma_q) {  // 32B swizzle: half h of row `lane` sits at h ^ bit 2 of the row
+                        uint8_t *qrow = yg + 3 * 4096 + (k & 1) * 1024 + lane * 32;
+                        const int sw = (lane >> 2) & 1;
+                        *reinterpret_cast<uint4 *>(qrow + (sw << 4)) = make_uint4(qb[0], qb[1], qb[2], qb[3]);
+                        *reinterpret_cast<uint4 *>(qrow + ((sw ^ 1) << 4)) = make_uint4(qb[4], qb[5], qb[6], qb[7]);
+                    } else if (m < M) {
+                        int8_t *dst = Q + (size_t)m * OC + n0;
+                        if (n0 + 32 <= OC && (OC & 15) == 0) {
+                            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(qb[0], qb[1], qb[2], qb[3]);
+                            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(qb[4], qb[5], qb[6], qb[7]);
+                        } else {
+                            for (int jj = 0; jj < 32; jj++)
+                                if (n0 + jj < OC) dst[jj] = (int8_t)(qb[jj / 4] >> (8 * (jj % 4)));
+                        }
+                    }
+                }
+                if (Y && tma_store) {
+                    if (live) {
 #pragma unroll
                         for (int c4 = 0; c4 < 8; c4++)
                             *reinterpret_cast<uint4 *>(sb + ((c4 ^ (lane & 7)) << 4)) =
                                 make_uint4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(&tmY, stage_s + (uint32_t)(buf * 4096), n0, mrow0);
-                            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                        }
-                        buf ^= 1;
                     }
-                } else if (m < M) {
+                } else if (Y && m < M) {
                     float *dst = Y + (size_t)m * OC + n0;
                     for (int jj = 0; jj < 32; jj++)
                         if (n0 + jj < OC) dst[jj] = __uint_as_float(v[jj]);
                 }
+                if (bulk) {
+                    if (live) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (Y && tma_store) tma_store_2d(&tmY, ys + (uint32_t)(b * 4096), n0, mrow0);
+                            if (Q && tma_q) tma_store_2d(&tmQ, qs + (uint32_t)((k & 1) * 1024), n0, mrow0);
+                        }
+                    }
+                    // one group per chunk; after the wait only this chunk's stores may
+                    // still read their tiles, so the next chunks' tiles are free
+                    if (lane == 0) {
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    }
+                    __syncwarp();
+                }
+                if (tma_r) {  // two chunks ahead, into the tile of chunk k - 1 (read by every lane by now)
+                    __syncwarp();
+                    issue_r();
+                }
             }
+            if (!ok) break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -422,7 +497,11 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
                 acc_phase ^= 1u;
             }
         }
-        if (tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        // residual loads still in flight (an abort) land before the CTA exits
+        if (lane == 0)
+            for (int b = 0; b < 3; b++)
+                if (rpend & (1u << b)) mbar_wait(rbar(b), (rphase >> b) & 1u, abort_p, gflags, false);
+        if (bulk && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
         __syncwarp();
     }
 
@@ -472,7 +551,8 @@ bool make_tmap_im2col(CUtensorMap *tm, const int8_t *x, const ConvShape &cs, int
 
 template <int BN, int MODE>
 int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
-                const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq) {
+                const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq,
+                const Residual &res) {
     using Cfg = ConvCfg<BN, MODE>;
     static bool attr_done[64] = {};
     auto kfn = k_conv_w8a8<BN, MODE>;
@@ -483,27 +563,33 @@ int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const C
         attr_done[dev] = true;
     }
     const int OC = (int)w->n;
-    CUtensorMap tw, ty;
+    CUtensorMap tw, ty, tq, tr;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->n, w->k, 1, Cfg::KB, BN,
                       Cfg::KB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
         return TPT_UNSUPPORTED;
     const long long M = (long long)cs.N * cs.OH * cs.OW;
-    const bool tma_store = !rq.q && make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, (uint64_t)M, (uint64_t)OC, 4,
+    const bool tma_store = y && make_tmap_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, (uint64_t)M, (uint64_t)OC, 4,
                                                  32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    // int8 output rows of 32 bytes (32B swizzle) and residual rows like the f32 output
+    const bool tma_q = rq.q && make_tmap_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, rq.q, (uint64_t)M, (uint64_t)OC, 1,
+                                            32, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+    const bool tma_r = res.r && make_tmap_2d(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, res.r, (uint64_t)M, (uint64_t)OC,
+                                             4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const long long ntiles = ((M + CV_BM - 1) / CV_BM) * ((OC + BN - 1) / BN);
     const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);
     launch_pdl(kfn, grid, cv_threads(MODE), Cfg::SMEM_BYTES, ctx->stream, tw, tx ? *tx : tw, tma_store ? ty : tw,
-                                                                 tma_store ? 1 : 0, x, cs, OC, a_scale, w->scales,
-                                                                 bias, act, y, rq.q, rq.scale, ctx->d_flags);
+               tma_q ? tq : tw, tma_r ? tr : tw, tma_store ? 1 : 0, tma_q ? 1 : 0, tma_r ? 1 : 0, x, cs, OC, a_scale,
+               w->scales, bias, act, y, rq.q, rq.scale, res.r, res.act, ctx->d_flags);
     return after_launch(ctx, "conv_w8a8");
 }
 
 template <int MODE>
 int launch_conv_bn(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
-                   const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq) {
-    if (w->n <= 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
-    if (w->n <= 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
-    return launch_conv<256, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq);
+                   const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq,
+                   const Residual &res) {
+    if (w->n <= 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
+    if (w->n <= 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
+    return launch_conv<256, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
 }
 
 }  // namespace
@@ -514,10 +600,10 @@ int launch_conv_bn(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, cons
 // GEMM instead).
 int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
                      int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
-                     int act, float *y, bool *handled, Requant rq) {
+                     int act, float *y, bool *handled, Requant rq, Residual res) {
     *handled = false;
     if (w->kind != 8 || !w->tmap_ok || C % 4 != 0 || ((uintptr_t)x & 15) || w->k < (size_t)KH * KW * C ||
-        w->n > 0x7fffffff || w->k > 0x7fffffff || (!rq.q && ((uintptr_t)y & 15)))
+        w->n > 0x7fffffff || w->k > 0x7fffffff || (!y && !rq.q) || ((uintptr_t)y & 15))
         return TPT_OK;
     const long long M = (long long)N * OH * OW, xin = (long long)N * H * W * C;
     if (M <= 0 || M > 0x7fffffffLL || xin > 0x7fffffffLL) return TPT_OK;  // 32-bit pixel offsets
@@ -530,11 +616,11 @@ int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, in
         CUtensorMap tx;
         const int kb = C % 128 == 0 ? 128 : 64;
         if (make_tmap_im2col(&tx, x, cs, kb))
-            return kb == 128 ? launch_conv_bn<CV_IM2COL128>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq)
-                             : launch_conv_bn<CV_IM2COL64>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq);
+            return kb == 128 ? launch_conv_bn<CV_IM2COL128>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq, res)
+                             : launch_conv_bn<CV_IM2COL64>(ctx, x, cs, &tx, w, a_scale, bias, act, y, rq, res);
     }
-    if (C % 16 == 0) return launch_conv_bn<CV_GATHER16>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq);
-    return launch_conv_bn<CV_GATHER4>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq);
+    if (C % 16 == 0) return launch_conv_bn<CV_GATHER16>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq, res);
+    return launch_conv_bn<CV_GATHER4>(ctx, x, cs, nullptr, w, a_scale, bias, act, y, rq, res);
 }
 
 }  // namespace tpt

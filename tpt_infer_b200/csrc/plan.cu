@@ -41,7 +41,7 @@ int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int 
 int comm_all_gather(tpt_cuda_comm *c, const void *in, void *out, size_t bytes_per_rank);
 int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
                      int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
-                     int act, float *y, bool *handled, Requant rq);
+                     int act, float *y, bool *handled, Requant rq, Residual res = Residual());
 int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
 }  // namespace tpt
 
@@ -420,7 +420,11 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
         // IM2COL -> LINEAR_W8A8 of its rows (read by no other op, not fetched):
         // one implicit-GEMM convolution launch gathers the rows from the NHWC
         // tensor instead of writing and re-reading them; a QUANTIZE of the f32
-        // result folds into its epilogue as for a plain LINEAR.
+        // result folds into its epilogue as for a plain LINEAR. An ADD_ACT of
+        // the result (read by nothing else) and another tensor (a residual)
+        // folds in too: the epilogue adds the residual, applies the activation
+        // and writes the sum (and, with a QUANTIZE of the sum after it, also
+        // its int8 copy), so the conv output is neither written nor read back.
         if (o.kind == TPT_OP_IM2COL && i + 1 < p->ops.size()) {
             const tpt_plan_op &l = p->ops[i + 1].op;
             const PlanTensor &col = p->tensors[o.out];
@@ -429,27 +433,45 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
                 const float sa = p->tensors[o.in0].scale;
                 p->tensors[o.out].scale = sa;
                 Requant rq;
+                Residual res;
+                float *y = F(p, l.out);
+                int q_op = -1;
                 size_t fused = 1;
-                if (!p->calibrating && i + 2 < p->ops.size()) {
-                    PlanOp &nq = p->ops[i + 2];
+                const PlanTensor &t = p->tensors[l.out];
+                const bool private_out = t.readers == 1 && !is_output(out_ids, n_out, l.out);
+                if (private_out && i + 2 < p->ops.size()) {
+                    const tpt_plan_op &a = p->ops[i + 2].op;
+                    if (a.kind == TPT_OP_ADD_ACT && (a.in0 == l.out) != (a.in1 == l.out) && a.dims[0] == t.numel) {
+                        res.r = F(p, a.in0 == l.out ? a.in1 : a.in0);
+                        res.act = a.act;
+                        y = F(p, a.out);
+                        fused = 2;
+                    }
+                }
+                const size_t qi = i + 1 + fused;  // the op after the conv (and its residual add)
+                if (!p->calibrating && qi < p->ops.size()) {
+                    PlanOp &nq = p->ops[qi];
                     const tpt_plan_op &q = nq.op;
-                    const PlanTensor &t = p->tensors[l.out];
-                    if (q.kind == TPT_OP_QUANTIZE && q.in0 == l.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
-                        t.readers == 1 && q.dims[0] == t.numel && !is_output(out_ids, n_out, l.out)) {
+                    const int src = fused == 2 ? p->ops[i + 2].op.out : l.out;
+                    // without a residual the f32 output is dropped, so it must be private;
+                    // the residual sum is still written (a later op reads it)
+                    if (q.kind == TPT_OP_QUANTIZE && q.in0 == src && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                        q.dims[0] == p->tensors[src].numel && (fused == 2 || private_out)) {
                         rq.q = Q(p, q.out);
                         rq.scale = nq.frozen;
-                        fused = 2;
+                        if (fused == 1) y = nullptr;
+                        q_op = (int)qi;
+                        fused++;
                     }
                 }
                 const size_t *d = o.dims;
                 bool handled = false;
                 int st = launch_conv_w8a8(p->ctx, Q(p, o.in0), (int)d[0], (int)d[1], (int)d[2], (int)d[3], (int)d[4],
                                           (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10],
-                                          (int)d[11], l.w, sa, F(p, l.in1), l.act, rq.q ? nullptr : F(p, l.out),
-                                          &handled, rq);
+                                          (int)d[11], l.w, sa, F(p, l.in1), l.act, y, &handled, rq, res);
                 if (st) return st;
                 if (handled) {
-                    if (rq.q) p->tensors[p->ops[i + 2].op.out].scale = rq.scale;
+                    if (q_op >= 0) p->tensors[p->ops[q_op].op.out].scale = rq.scale;
                     i += fused;
                     continue;
                 }

@@ -81,15 +81,17 @@ __global__ void k_quant_i8_static(const float *__restrict__ x, size_t n, float s
 __global__ void k_quant_i8_static16(const float4 *__restrict__ x, size_t n16, float scale, int4 *__restrict__ q) {
     pdl_wait();
     pdl_trigger();
+    const float rs = __frcp_rn(scale);
+    const bool fast = requant_fast_ok(scale);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const float4 v = __ldcs(x + 4 * i + j);
-            const uint32_t b0 = (uint8_t)round_clamp_i8(__fdiv_rn(v.x, scale), -127.0f, 127.0f);
-            const uint32_t b1 = (uint8_t)round_clamp_i8(__fdiv_rn(v.y, scale), -127.0f, 127.0f);
-            const uint32_t b2 = (uint8_t)round_clamp_i8(__fdiv_rn(v.z, scale), -127.0f, 127.0f);
-            const uint32_t b3 = (uint8_t)round_clamp_i8(__fdiv_rn(v.w, scale), -127.0f, 127.0f);
+            const uint32_t b0 = (uint8_t)(fast ? requant_i8_fast(v.x, scale, rs) : requant_i8(v.x, scale));
+            const uint32_t b1 = (uint8_t)(fast ? requant_i8_fast(v.y, scale, rs) : requant_i8(v.y, scale));
+            const uint32_t b2 = (uint8_t)(fast ? requant_i8_fast(v.z, scale, rs) : requant_i8(v.z, scale));
+            const uint32_t b3 = (uint8_t)(fast ? requant_i8_fast(v.w, scale, rs) : requant_i8(v.w, scale));
             w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
         }
         q[i] = make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);

@@ -266,12 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                     // lane's row gets 32 consecutive bytes
                     if (m < M) {
                         uint32_t b[8];
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            b[j / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j]), q_scale) |
-                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 1]), q_scale) << 8) |
-                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 2]), q_scale) << 16) |
-                                       ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 3]), q_scale) << 24);
+                        requant_pack32(v, q_scale, __frcp_rn(q_scale), requant_fast_ok(q_scale), b);
                         int8_t *dst = Q + (size_t)m * N + n0;
                         if (n0 + 32 <= N && (N & 15) == 0) {
                             reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
