@@ -284,6 +284,18 @@ __device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, flo
         v[j] = __float_as_uint(act_t<ACT>(y));
     }
 }
+// The activation of 32 values (f32 bits) in place, for epilogues that keep
+// their code small: ReLU as a select, GELU through an out-of-line call.
+static __device__ __noinline__ float gelu_outline(float y) { return gelu_ref(y); }
+__device__ __forceinline__ void act32(uint32_t (&v)[32], int act) {
+    if (act == TPT_ACT_RELU) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __float_as_uint(act_t<TPT_ACT_RELU>(__uint_as_float(v[j])));
+    } else if (act == TPT_ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __float_as_uint(gelu_outline(__uint_as_float(v[j])));
+    }
+}
 __device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
                                            const float *bias, int act) {
     if (act == TPT_ACT_RELU)
@@ -324,13 +336,14 @@ __device__ __forceinline__ int8_t requant_i8_fast(float y, float s, float rs) {
     const float q2 = __fmaf_rn(__fmaf_rn(-s, q1, y), rs, q1);
     float q = __fmaf_rn(__fmaf_rn(-s, q2, y), rs, q2);
     q = fabsf(y) <= 0x1p80f ? q : y;
-    const float c = fminf(fmaxf(q, -128.0f), 128.0f);
-    const float t = truncf(c);
-    const float f = __fsub_rn(c, t);  // exact, the sign of c
-    int n = (int)t + (f >= 0.5f ? 1 : 0) - (f <= -0.5f ? 1 : 0);
+    const float f = __fsub_rn(q, truncf(q));  // exact, the sign of q; NaN for NaN and +-inf
+    // truncation saturates to the int32 range and takes NaN to 0 (cvt.rzi.s32.f32)
+    int n = __float2int_rz(q) + (f >= 0.5f ? 1 : 0) - (f <= -0.5f ? 1 : 0);
     n = n > 127 ? 127 : (n < -127 ? -127 : n);
-    return isnan(q) ? (int8_t)0 : (int8_t)n;
+    return (int8_t)n;
 }
+// out of line: the dividing path of the wide epilogues (scales outside the fast range)
+static __device__ __noinline__ int8_t requant_i8_outline(float y, float s) { return requant_i8(y, s); }
 
 // requant_i8 of 32 values (f32 bits) packed 4 to a word, low byte first
 __device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s, float rs, bool fast,
@@ -345,10 +358,10 @@ __device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s,
     } else {
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-            qb[j / 4] = (uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j]), s) |
-                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 1]), s) << 8) |
-                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 2]), s) << 16) |
-                        ((uint32_t)(uint8_t)requant_i8(__uint_as_float(v[j + 3]), s) << 24);
+            qb[j / 4] = (uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j]), s) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 1]), s) << 8) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 2]), s) << 16) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 3]), s) << 24);
     }
 }
 

@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(cc * 32), v);
                 tmem_wait_ld();
-                w8a8_epi32(v, n0, OC, a_scale, wscale, bias, act);
+                w8a8_epi32<TPT_ACT_NONE>(v, n0, OC, a_scale, wscale, bias);
+                act32(v, act);
                 if (R && tma_r) {  // residual: y = ract(conv + r), the ADD_ACT op's f32 add
                     if (live) {
                         int okr = 0;
@@ -424,16 +425,19 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
 #pragma unroll
                         for (int c4 = 0; c4 < 8; c4++) {
                             const float4 r = *reinterpret_cast<const float4 *>(sb + ((c4 ^ (lane & 7)) << 4));
-                            v[4 * c4] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4]) + r.x, ract));
-                            v[4 * c4 + 1] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 1]) + r.y, ract));
-                            v[4 * c4 + 2] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 2]) + r.z, ract));
-                            v[4 * c4 + 3] = __float_as_uint(apply_act(__uint_as_float(v[4 * c4 + 3]) + r.w, ract));
+                            v[4 * c4] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4]), r.x));
+                            v[4 * c4 + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 1]), r.y));
+                            v[4 * c4 + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 2]), r.z));
+                            v[4 * c4 + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 3]), r.w));
                         }
+                        act32(v, ract);
                     }
                 } else if (R && m < M) {
                     const float *src = R + (size_t)m * OC + n0;
+#pragma unroll
                     for (int jj = 0; jj < 32; jj++)
-                        if (n0 + jj < OC) v[jj] = __float_as_uint(apply_act(__uint_as_float(v[jj]) + src[jj], ract));
+                        if (n0 + jj < OC) v[jj] = __float_as_uint(__fadd_rn(__uint_as_float(v[jj]), src[jj]));
+                    act32(v, ract);
                 }
                 if (Q && live) {
                     uint32_t qb[8];
