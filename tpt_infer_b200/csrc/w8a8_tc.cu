@@ -102,11 +102,13 @@ __device__ __forceinline__ void tc2_commit_both(uint32_t bar) {
         : "memory");
 }
 
-template <int BN, bool ACC_OUT>
+// ACT: the activation, a compile-time choice so that each instantiation's
+// epilogue holds only its own code
+template <int BN, bool ACC_OUT, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     k_w8a8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmY, int tma_store, int M, int N, int K, float a_scale,
-               const float *__restrict__ wscale, const float *__restrict__ bias, int act, float *__restrict__ Y,
+               const float *__restrict__ wscale, const float *__restrict__ bias, float *__restrict__ Y,
                int32_t *__restrict__ ACC, unsigned *gflags, int8_t *__restrict__ Q, float q_scale) {
     using Cfg = PairCfg<BN>;
     constexpr int S = Cfg::STAGES;
@@ -260,7 +262,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
                 const int n0 = nt * BN + half * (BN / 2) + c * 32;
-                if (!ACC_OUT) w8a8_epi32(v, n0, N, a_scale, wscale, bias, act);
+                if (!ACC_OUT) w8a8_epi32<ACT>(v, n0, N, a_scale, wscale, bias);
                 if (!ACC_OUT && Q) {
                     // int8 output requantized with the next point's scale: this
                     // lane's row gets 32 consecutive bytes
@@ -365,14 +367,14 @@ bool make_tmap_i8(CUtensorMap *tm, const void *base, uint64_t rows, uint64_t k, 
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool ACC_OUT>
-int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
-               const float *ws, const float *bias, int act, float *y, int32_t *acc, Requant rq) {
+template <int BN, bool ACC_OUT, int ACT>
+int launch_tc2_act(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
+                   float a_scale, const float *ws, const float *bias, float *y, int32_t *acc, Requant rq) {
     using Cfg = PairCfg<BN>;
     constexpr int P_SMEM_BYTES = Cfg::SMEM_BYTES;
     static bool attr_done[64] = {};
     static int max_clusters[64] = {};
-    auto kfn = k_w8a8_tc2<BN, ACC_OUT>;
+    auto kfn = k_w8a8_tc2<BN, ACC_OUT, ACT>;
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
@@ -405,8 +407,18 @@ int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, 
     const bool tma_store = !rq.q && make_tmap_out(&ty, ACC_OUT ? (const void *)acc : (const void *)y, (uint64_t)M,
                                                   (uint64_t)N, ACC_OUT);
     launch_pdl(kfn, 2 * clusters, P_THREADS, P_SMEM_BYTES, ctx->stream, ta, tb, tma_store ? ty : ta, tma_store ? 1 : 0,
-               M, N, K, a_scale, ws, bias, act, y, acc, ctx->d_flags, rq.q, rq.scale);
+               M, N, K, a_scale, ws, bias, y, acc, ctx->d_flags, rq.q, rq.scale);
     return after_launch(ctx, "w8a8_tc2");
+}
+
+template <int BN, bool ACC_OUT>
+int launch_tc2(tpt_cuda_ctx *ctx, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, float a_scale,
+               const float *ws, const float *bias, int act, float *y, int32_t *acc, Requant rq) {
+    if (ACC_OUT || act == TPT_ACT_NONE)  // raw accumulators take no epilogue
+        return launch_tc2_act<BN, ACC_OUT, TPT_ACT_NONE>(ctx, ta, tb, M, N, K, a_scale, ws, bias, y, acc, rq);
+    if (act == TPT_ACT_RELU)
+        return launch_tc2_act<BN, false, TPT_ACT_RELU>(ctx, ta, tb, M, N, K, a_scale, ws, bias, y, acc, rq);
+    return launch_tc2_act<BN, false, TPT_ACT_GELU>(ctx, ta, tb, M, N, K, a_scale, ws, bias, y, acc, rq);
 }
 
 }  // namespace
