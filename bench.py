@@ -459,7 +459,8 @@ def profile_kernels(args):
     attention 64x128x12; INT8 convs of ResNet-18 at batch 64: a stage-1 3x3
     (64 -> 64 channels at 56x56, TMA im2col) and the stem in its space-to-depth
     form (the 7x7/2 conv as a 4x4/1 conv over [112, 112, 16], cp.async
-    gathers)."""
+    gathers); then the whole ResNet-18 plan at batch 64 (two direct runs, then
+    graph replays: 20 conv launches per forward)."""
     import torch
 
     from tpt_infer_b200 import CudaBackend, graphs, synth
@@ -503,6 +504,16 @@ def profile_kernels(args):
         pc = _conv_plan(be, *shape, seed=3100, out_hw=ohw)
         out[f"{name}_us_with_quantize"] = _time_device(stream, pc.run_device, args.steps, args.warmup, flush) * 1e6
         pc.close()
+    # the ResNet-18 plan at batch 64 (calibrated on one batch, scales frozen, then
+    # replayed): 20 conv launches per forward, int8 outputs and folded residual adds
+    Bn, IMG = 64, 3 * 224 * 224
+    pr, xr, logits = graphs.build_resnet18(be, Bn, graphs.resnet18_weights(be))
+    pr.calibrate(True)
+    pr.run({xr: synth.normal(Bn * IMG, 31)}, [logits])
+    pr.freeze()
+    pr.run({xr: synth.normal(Bn * IMG, 32)}, [logits])
+    out["resnet18_b64_forward_us"] = _time_device(stream, pr.run_device, args.steps, args.warmup, flush) * 1e6
+    pr.close()
     be.close()
     print(json.dumps({"profile_kernels": True, "launches_each": reps, **out}), flush=True)
     return 0
