@@ -126,3 +126,26 @@ def test_conv_residual_epilogue_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requa
         if requant:
             assert np.array_equal(np.frombuffer(got[1].tobytes()[:M * OC], np.int8), O.quantize_i8_static(want, sy))
     p.close()
+
+
+@pytest.mark.parametrize("N,H,W,C,k,s,pad", [(2, 17, 15, 64, 3, 2, 1), (3, 8, 8, 16, 3, 1, 1), (2, 12, 10, 8, 2, 2, 0)])
+def test_maxpool_op_bit_exact(cuda, N, H, W, C, k, s, pad):
+    # the plan's NHWC MAXPOOL (the 3x3 window compiled in, others generic)
+    # against the oracle's NCHW max_pool2d, bit for bit, with signed zeros and
+    # NaN among the inputs
+    from tpt_infer_b200 import graphs
+
+    OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
+    x = O.normal(N * H * W * C, 9100 + H + C).reshape(N, H, W, C)
+    x.ravel()[::37] = 0.0
+    x.ravel()[5::41] = -0.0
+    x.ravel()[11::997] = np.nan
+    p = graphs.Plan(cuda)
+    tx, ty = p.tensor(graphs.F32, x.size), p.tensor(graphs.F32, N * OH * OW * C)
+    p.op(graphs.OP_MAXPOOL, tx, ty, dims=(N, H, W, C, k, k, s, s, pad, pad, OH, OW))
+    p.finalize()
+    got = p.run({tx: x}, [ty])[0].reshape(N, OH, OW, C)
+    p.close()
+    want = O.max_pool2d(np.ascontiguousarray(x.transpose(0, 3, 1, 2)), N, C, H, W, (k, k), (s, s), (pad, pad))
+    want = want.reshape(N, C, OH, OW).transpose(0, 2, 3, 1)
+    assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(want).view(np.uint32))

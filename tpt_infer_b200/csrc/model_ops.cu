@@ -302,21 +302,28 @@ __global__ void k_maxpool_nhwc(const float *__restrict__ x, float *__restrict__ 
 }
 
 // Same, 4 channels per thread (C % 4 == 0, 16-byte aligned), 32-bit index math.
+// KT > 0: a KT x KT window known at compile time, so its loads are issued
+// together; taps outside the input are skipped as in the generic loop, and
+// the taps are compared in the same order (row by row), so ties between
+// signed zeros and NaN inputs resolve the same way.
+template <int KT>
 __global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict__ y, int N, int H, int W, int C4,
                                 int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW) {
     pdl_wait();
     pdl_trigger();
+    if (KT > 0) KH = KW = KT;
     const int total = N * OH * OW * C4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int c = i % C4, t = i / C4, ox = t % OW, t2 = t / OW, oy = t2 % OH, n = t2 / OH;
         float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        for (int ky = 0; ky < KH; ky++) {
+#pragma unroll
+        for (int ky = 0; ky < (KT > 0 ? KT : KH); ky++) {
             const int iy = oy * sh + ky - ph;
-            if (iy < 0 || iy >= H) continue;
-            for (int kx = 0; kx < KW; kx++) {
+#pragma unroll
+            for (int kx = 0; kx < (KT > 0 ? KT : KW); kx++) {
                 const int ix = ox * sw + kx - pw;
-                if (ix < 0 || ix >= W) continue;
-                const float4 v = x[(((size_t)n * H + iy) * W + ix) * C4 + c];
+                if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+                const float4 v = __ldg(x + ((n * H + iy) * W + ix) * C4 + c);
                 if (v.x > best.x) best.x = v.x;
                 if (v.y > best.y) best.y = v.y;
                 if (v.z > best.z) best.z = v.z;
@@ -429,9 +436,12 @@ int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H,
 int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
                         int sw, int ph, int pw, int OH, int OW) {
     const size_t total = (size_t)N * OH * OW * C;
-    if (C % 4 == 0 && total / 4 < 0x7fffffff && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
-        launch_pdl(k_maxpool_nhwc4, grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream, reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw, ph, pw,
-            OH, OW);
+    if (C % 4 == 0 && total / 4 < 0x7fffffff && (size_t)N * H * W * C / 4 < 0x7fffffff && ((uintptr_t)x & 15) == 0 &&
+        ((uintptr_t)y & 15) == 0) {
+        auto kfn = KH == 3 && KW == 3 ? k_maxpool_nhwc4<3> : k_maxpool_nhwc4<0>;
+        launch_pdl(kfn, grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream,
+                   reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw,
+                   ph, pw, OH, OW);
         return after_launch(ctx, "maxpool");
     }
     launch_pdl(k_maxpool_nhwc, grid_1d(total, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream, x, y, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW);
