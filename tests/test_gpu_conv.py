@@ -132,7 +132,8 @@ def test_conv_residual_epilogue_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requa
 def test_maxpool_op_bit_exact(cuda, N, H, W, C, k, s, pad):
     # the plan's NHWC MAXPOOL (the 3x3 window compiled in, others generic)
     # against the oracle's NCHW max_pool2d, bit for bit, with signed zeros and
-    # NaN among the inputs
+    # NaN among the inputs; a QUANTIZE of the pooled tensor runs inside the
+    # pool's pass (its int8 copy) and must equal the oracle's quantizer
     from tpt_infer_b200 import graphs
 
     OH, OW = (H + 2 * pad - k) // s + 1, (W + 2 * pad - k) // s + 1
@@ -142,10 +143,16 @@ def test_maxpool_op_bit_exact(cuda, N, H, W, C, k, s, pad):
     x.ravel()[11::997] = np.nan
     p = graphs.Plan(cuda)
     tx, ty = p.tensor(graphs.F32, x.size), p.tensor(graphs.F32, N * OH * OW * C)
+    tq = p.tensor(graphs.I8, N * OH * OW * C)
     p.op(graphs.OP_MAXPOOL, tx, ty, dims=(N, H, W, C, k, k, s, s, pad, pad, OH, OW))
+    sq = np.float32(0.02)
+    p.op(graphs.OP_QUANTIZE, ty, tq, f0=float(sq), dims=(N * OH * OW * C,))
     p.finalize()
-    got = p.run({tx: x}, [ty])[0].reshape(N, OH, OW, C)
+    got, gq = p.run({tx: x}, [ty, tq])
+    got = got.reshape(N, OH, OW, C)
     p.close()
     want = O.max_pool2d(np.ascontiguousarray(x.transpose(0, 3, 1, 2)), N, C, H, W, (k, k), (s, s), (pad, pad))
-    want = want.reshape(N, C, OH, OW).transpose(0, 2, 3, 1)
-    assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(want).view(np.uint32))
+    want = np.ascontiguousarray(want.reshape(N, C, OH, OW).transpose(0, 2, 3, 1))
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    n = want.size
+    assert np.array_equal(np.frombuffer(gq.tobytes()[:n], np.int8), O.quantize_i8_static(want, sq))

@@ -306,9 +306,12 @@ __global__ void k_maxpool_nhwc(const float *__restrict__ x, float *__restrict__ 
 // together; taps outside the input are skipped as in the generic loop, and
 // the taps are compared in the same order (row by row), so ties between
 // signed zeros and NaN inputs resolve the same way.
+// q != nullptr: also the int8 copy of the output, clamp(roundf(y / qs)) (the
+// QUANTIZE op's rule), 4 bytes per thread.
 template <int KT>
 __global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict__ y, int N, int H, int W, int C4,
-                                int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW) {
+                                int KH, int KW, int sh, int sw, int ph, int pw, int OH, int OW,
+                                uint32_t *__restrict__ q, float qs) {
     pdl_wait();
     pdl_trigger();
     if (KT > 0) KH = KW = KT;
@@ -331,6 +334,12 @@ __global__ void k_maxpool_nhwc4(const float4 *__restrict__ x, float4 *__restrict
             }
         }
         y[i] = best;
+        if (q) {
+            const bool fast = requant_fast_ok(qs);
+            const float rs = __frcp_rn(qs);
+            auto rq = [&](float v) { return (uint32_t)(uint8_t)(fast ? requant_i8_fast(v, qs, rs) : requant_i8(v, qs)); };
+            q[i] = rq(best.x) | (rq(best.y) << 8) | (rq(best.z) << 16) | (rq(best.w) << 24);
+        }
     }
 }
 
@@ -434,16 +443,17 @@ int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H,
 }
 
 int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
-                        int sw, int ph, int pw, int OH, int OW) {
+                        int sw, int ph, int pw, int OH, int OW, int8_t *q, float qs) {
     const size_t total = (size_t)N * OH * OW * C;
     if (C % 4 == 0 && total / 4 < 0x7fffffff && (size_t)N * H * W * C / 4 < 0x7fffffff && ((uintptr_t)x & 15) == 0 &&
-        ((uintptr_t)y & 15) == 0) {
+        ((uintptr_t)y & 15) == 0 && ((uintptr_t)q & 3) == 0) {
         auto kfn = KH == 3 && KW == 3 ? k_maxpool_nhwc4<3> : k_maxpool_nhwc4<0>;
         launch_pdl(kfn, grid_1d(total / 4, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream,
                    reinterpret_cast<const float4 *>(x), reinterpret_cast<float4 *>(y), N, H, W, C / 4, KH, KW, sh, sw,
-                   ph, pw, OH, OW);
+                   ph, pw, OH, OW, reinterpret_cast<uint32_t *>(q), qs);
         return after_launch(ctx, "maxpool");
     }
+    if (q) return TPT_UNSUPPORTED;  // the int8 copy needs the 4-channel kernel
     launch_pdl(k_maxpool_nhwc, grid_1d(total, 256, (unsigned)ctx->sm_count * 16), 256, 0, ctx->stream, x, y, N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW);
     return after_launch(ctx, "maxpool");
 }

@@ -34,7 +34,8 @@ int launch_nchw_to_nhwc_q8(tpt_cuda_ctx *ctx, const float *x, int8_t *q, int N, 
 int launch_im2col(tpt_cuda_ctx *ctx, const int8_t *x, int8_t *col, int N, int H, int W, int C, int KH, int KW, int sh,
                   int sw, int ph, int pw, int OH, int OW, int Kp);
 int launch_maxpool_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int H, int W, int C, int KH, int KW, int sh,
-                        int sw, int ph, int pw, int OH, int OW);
+                        int sw, int ph, int pw, int OH, int OW, int8_t *q = nullptr,
+                        float qs = 0.0f);
 int launch_gap_nhwc(tpt_cuda_ctx *ctx, const float *x, float *y, int N, int HW, int C);
 int launch_absmax_acc(tpt_cuda_ctx *ctx, const float *x, size_t n, unsigned *cell);
 int launch_panels_to_rows(tpt_cuda_ctx *ctx, const int8_t *in, int8_t *out, int P, size_t T, int C);
@@ -539,20 +540,28 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
                 continue;
             }
         }
-        // ADD_ACT / LAYERNORM -> QUANTIZE of its output: one pass writes the f32
-        // tensor (still read later, e.g. by a residual) and its int8 copy
-        if (!p->calibrating && (o.kind == TPT_OP_ADD_ACT || o.kind == TPT_OP_LAYERNORM) && i + 1 < p->ops.size()) {
+        // ADD_ACT / LAYERNORM / MAXPOOL -> QUANTIZE of its output: one pass writes
+        // the f32 tensor (still read later, e.g. by a residual) and its int8 copy
+        if (!p->calibrating &&
+            (o.kind == TPT_OP_ADD_ACT || o.kind == TPT_OP_LAYERNORM ||
+             (o.kind == TPT_OP_MAXPOOL_NHWC && o.dims[3] % 4 == 0)) &&
+            i + 1 < p->ops.size()) {
             PlanOp &nq = p->ops[i + 1];
             const tpt_plan_op &q = nq.op;
             const PlanTensor &t = p->tensors[o.out];
             if (q.kind == TPT_OP_QUANTIZE && q.in0 == o.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
                 q.dims[0] == t.numel) {
                 p->tensors[q.out].scale = nq.frozen;
+                const size_t *d = o.dims;
                 int st = o.kind == TPT_OP_ADD_ACT
-                             ? launch_add_act(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), o.dims[0], o.act,
+                             ? launch_add_act(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], o.act,
                                               Q(p, q.out), nq.frozen)
-                             : launch_layernorm(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), F(p, o.out), o.dims[0],
-                                                o.dims[1], o.f0, Q(p, q.out), nq.frozen);
+                         : o.kind == TPT_OP_LAYERNORM
+                             ? launch_layernorm(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), F(p, o.out), d[0], d[1],
+                                                o.f0, Q(p, q.out), nq.frozen)
+                             : launch_maxpool_nhwc(p->ctx, F(p, o.in0), F(p, o.out), (int)d[0], (int)d[1], (int)d[2],
+                                                   (int)d[3], (int)d[4], (int)d[5], (int)d[6], (int)d[7], (int)d[8],
+                                                   (int)d[9], (int)d[10], (int)d[11], Q(p, q.out), nq.frozen);
                 if (st) return st;
                 i++;
                 continue;
