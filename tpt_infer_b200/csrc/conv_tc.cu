@@ -49,13 +49,19 @@ using namespace tc;
 
 constexpr int CV_BM = 128;                  // output pixels per tile (MMA M)
 constexpr int CV_WARP_OUT = 3 * 4096 + 2 * 1024;  // epilogue staging per warp: 3 f32 + 2 int8 32 x 32 tiles
-constexpr int CV_OUT_BYTES = 4 * CV_WARP_OUT;
 // activation operand modes: gather with 16- or 4-byte chunks (128-byte
 // k-blocks), TMA im2col with 128- or 64-byte k-blocks
 enum { CV_GATHER16 = 0, CV_GATHER4 = 1, CV_IM2COL128 = 2, CV_IM2COL64 = 3 };
 __host__ __device__ constexpr bool cv_tma(int mode) { return mode >= CV_IM2COL128; }
 __host__ __device__ constexpr int cv_kb(int mode) { return mode == CV_IM2COL64 ? 64 : 128; }
-__host__ __device__ constexpr int cv_threads(int mode) { return cv_tma(mode) ? 192 : 320; }
+// epilogue warps: two per TMEM lane quarter (each takes every other 32-column
+// chunk) for 128-wide tiles with TMA operands, else one (64-wide tiles have two
+// chunks per tile, and 256-wide ones lack the shared memory for the staging)
+__host__ __device__ constexpr int cv_epi_warps(int mode, int bn) { return cv_tma(mode) && bn == 128 ? 8 : 4; }
+// warp 0 TMA, warp 1 MMA, then the epilogue warps, then (gather modes) 4 gather warps
+__host__ __device__ constexpr int cv_threads(int mode, int bn) {
+    return 64 + 32 * cv_epi_warps(mode, bn) + (cv_tma(mode) ? 0 : 128);
+}
 
 struct ConvShape {
     int N, H, W, C, KH, KW, sh, sw, ph, pw, OH, OW;
@@ -69,10 +75,12 @@ struct ConvCfg {
     static constexpr int A_BYTES = CV_BM * KB;
     static constexpr int B_BYTES = BN * KB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_FIT = (232448 - CV_OUT_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
+    static constexpr int EPI = cv_epi_warps(MODE, BN);
+    static constexpr int OUT_BYTES = EPI * CV_WARP_OUT;
+    static constexpr int STAGES_FIT = (232448 - OUT_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + CV_OUT_BYTES + (2 * STAGES + 5 + 12) * 8 + 1024;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + (2 * STAGES + 5 + 3 * EPI) * 8 + 1024;
     static_assert(SMEM_BYTES + 3 * CV_BM * 4 + 16 <= 232448, "shared memory (dynamic + the static gather table)");
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
     static_assert(STAGES >= 3, "stages");
@@ -132,7 +140,7 @@ __device__ __forceinline__ void cp_async_wait_upto(int n) {
 }
 
 template <int BN, int MODE>
-__global__ void __launch_bounds__(cv_threads(MODE), 1)
+__global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
     k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmR, int tma_store, int tma_q, int tma_r,
@@ -145,6 +153,8 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
     constexpr int KB = Cfg::KB;
     constexpr int VB = MODE == CV_GATHER4 ? 4 : 16;
     constexpr int INFLIGHT = S - 2;  // k-blocks a gather thread keeps in flight
+    constexpr int EPI = Cfg::EPI;
+    constexpr int GATHER0 = 2 + EPI;  // first gather warp
     extern __shared__ uint8_t smem_raw[];
     __shared__ int abort_flag;
     __shared__ uint32_t tmem_slot;
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ring = (raw + 1023u) & ~1023u;
     const uint32_t staging = ring + S * Cfg::STAGE_BYTES;
-    const uint32_t bars = staging + CV_OUT_BYTES;
+    const uint32_t bars = staging + Cfg::OUT_BYTES;
     auto a_s = [&](int s) { return ring + (uint32_t)(s * Cfg::STAGE_BYTES); };
     auto b_s = [&](int s) { return a_s(s) + (uint32_t)Cfg::A_BYTES; };
     auto full_bar = [&](int s) { return bars + 8u * s; };
@@ -178,10 +188,10 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), 4);
+            mbar_init(tempty_bar(b), EPI);
         }
         mbar_init(drain_bar, 1);
-        for (int b = 0; b < 12; b++) mbar_init(bars + 8u * (2 * S + 5 + b), 1);  // residual tiles, 3 per epilogue warp
+        for (int b = 0; b < 3 * EPI; b++) mbar_init(bars + 8u * (2 * S + 5 + b), 1);  // residual tiles, 3 per epilogue warp
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         if (TMA_A) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
@@ -276,14 +286,14 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
             tc_commit(drain_bar);
             mbar_wait(drain_bar, 0, abort_p, gflags, false);
         }
-    } else if (!TMA_A && warp >= 6) {
+    } else if (!TMA_A && warp >= GATHER0) {
         // ---------------- gather ----------------
         // VB = 16: lane = (chunk j of 8, row r of a 4-row group), 8 rows per thread;
         // VB = 4:  lane = chunk j of 32, one row per warp step, 32 rows per thread
         constexpr int CPR = 128 / VB;                 // chunks per row
         constexpr int RPW = 32 / CPR;                 // rows a warp covers per step
         constexpr int STEPS = CV_BM / (4 * RPW);      // steps per k-block
-        const int gt = threadIdx.x - 192, gw = gt >> 5, j = lane % CPR, rr = lane / CPR;
+        const int gt = threadIdx.x - GATHER0 * 32, gw = gt >> 5, j = lane % CPR, rr = lane / CPR;
         int stage = 0;
         uint32_t phase = 0;
         int pend_stage[S] = {};  // stages whose copies are in flight, oldest first
@@ -352,13 +362,16 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
         }
         while (npend > 0) retire(npend - 1);
     } else {
-        // ---------------- epilogue (warps 2..5): thread = output pixel ----------------
+        // ---------------- epilogue (warps 2 .. 2 + EPI): thread = output pixel ----------------
         // Per warp: a ring of three 32 x 32 f32 tiles (128B swizzle) and two
         // 32 x 32 int8 tiles (32B swizzle). A chunk's residual block arrives in
         // its f32 tile by TMA two chunks ahead; the result is written back in
-        // place and leaves, with its int8 copy, as one bulk store group.
+        // place and leaves, with its int8 copy, as one bulk store group. With 8
+        // epilogue warps, the two warps of a lane quarter take alternate chunks.
+        constexpr int CSTEP = EPI / 4;
         const int q = warp & 3;  // TMEM lane quarter
         const int e = warp - 2;
+        const int c0 = e >> 2;   // this warp's first chunk of a tile
         const uint32_t ys = staging + (uint32_t)(e * CV_WARP_OUT), qs = ys + 3u * 4096u;
         uint8_t *yg = smem_raw + (ys - raw);
         auto rbar = [&](int b) { return bars + 8u * (2 * S + 5 + 3 * e + b); };
@@ -367,8 +380,12 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
         const bool q_fast = requant_fast_ok(q_scale);
         int acc = 0, k = 0;
         uint32_t acc_phase = 0, rphase = 0, rpend = 0;
-        int pt = blockIdx.x, pcc = 0, pk = 0;  // residual prefetch cursor: tile, chunk, sequence number
+        int pt = blockIdx.x, pcc = c0, pk = 0;  // residual prefetch cursor: tile, chunk, sequence number
         auto issue_r = [&]() {
+            while (pt < ntiles && (pt % tiles_n) * BN + pcc * 32 >= OC) {  // no chunk of this warp left in the tile
+                pcc = c0;
+                pt += gridDim.x;
+            }
             if (pt >= ntiles) return;
             const int mt = pt / tiles_n, nt = pt - mt * tiles_n, mrow0 = mt * CV_BM + q * 32, b = pk % 3;
             if (mrow0 < M) {  // blocks entirely below the last row are neither loaded nor stored
@@ -379,8 +396,9 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
                 }
             }
             pk++;
-            if (++pcc == BN / 32 || nt * BN + pcc * 32 >= OC) {
-                pcc = 0;
+            pcc += CSTEP;
+            if (pcc >= BN / 32) {
+                pcc = c0;
                 pt += gridDim.x;
             }
         };
@@ -400,7 +418,7 @@ __global__ void __launch_bounds__(cv_threads(MODE), 1)
             const bool live = mrow0 < M;
             const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; cc++, k++) {
+            for (int cc = c0; cc < BN / 32; cc += CSTEP, k++) {
                 const int n0 = nt * BN + cc * 32;
                 if (n0 >= OC) break;
                 const int b = k % 3;
@@ -581,7 +599,7 @@ int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const C
                                              4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const long long ntiles = ((M + CV_BM - 1) / CV_BM) * ((OC + BN - 1) / BN);
     const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);
-    launch_pdl(kfn, grid, cv_threads(MODE), Cfg::SMEM_BYTES, ctx->stream, tw, tx ? *tx : tw, tma_store ? ty : tw,
+    launch_pdl(kfn, grid, cv_threads(MODE, BN), Cfg::SMEM_BYTES, ctx->stream, tw, tx ? *tx : tw, tma_store ? ty : tw,
                tma_q ? tq : tw, tma_r ? tr : tw, tma_store ? 1 : 0, tma_q ? 1 : 0, tma_r ? 1 : 0, x, cs, OC, a_scale,
                w->scales, bias, act, y, rq.q, rq.scale, res.r, res.act, ctx->d_flags);
     return after_launch(ctx, "conv_w8a8");
