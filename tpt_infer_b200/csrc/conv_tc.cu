@@ -9,7 +9,9 @@
 //   acc[m, oc] = sum_k x[n, oy*sh - ph + ky, ox*sw - pw + kx, c] * Wt[oc, k]
 // with taps outside the image (and k >= KH*KW*C) contributing zero, then
 //   y = (float)acc * (a_scale * w_scale[oc]) + bias[oc], act, and optionally
-// the int8 requantization of the next quantization point. The rows of the
+// the int8 requantization of the next quantization point, and optionally a
+// residual added after the activation with a second activation (the plan's
+// ADD_ACT folded in: out = act2(y + r)). The rows of the
 // im2col matrix are gathered straight from the activation tensor into shared
 // memory instead of being written to and read back from HBM.
 //
@@ -28,9 +30,13 @@
 //   warp 0      TMA: weight tile [BN rows x KB B] (and the im2col tile)
 //   warp 1      TMEM allocation; one lane issues tcgen05.mma (M=128, N=BN,
 //               K=32) and the commits
-//   warps 2..5  epilogue, thread = output pixel (TMEM lane); f32 rows through
-//               a swizzled staging tile and bulk-tensor stores, or int8 rows
-//   warps 6..9  (gather mode) at each tile the 128 rows' first input pixel goes to a
+//   warps 2..    epilogue, thread = output pixel (TMEM lane): 4 warps, or 8
+//               for 128-wide tiles with TMA operands (two per TMEM lane quarter,
+//               alternate 32-column chunks). f32 and int8 rows leave through
+//               swizzled staging tiles and bulk-tensor stores; a residual
+//               (a folded ADD_ACT) arrives by TMA two chunks ahead; the int8
+//               requantization has no division (requant_i8_fast)
+//   last 4 warps (gather mode) at each tile the 128 rows' first input pixel goes to a
 //               shared table; lane = (chunk of the k-block, pixel row);
 //               cp.async with zero fill for padding taps, S - 2 k-blocks in
 //               flight per thread; a warp arrives on the stage's barrier
