@@ -30,6 +30,8 @@ CASES = [  # N, H, W, C, OC, k, stride, pad
     (3, 24, 24, 128, 256, 1, 2, 0),
     (3, 30, 26, 64, 130, 3, 1, 1),
     (1, 20, 20, 512, 512, 3, 1, 1),
+    # a 128-wide tile with TMA operands (eight epilogue warps) and a ragged last chunk
+    (2, 40, 40, 64, 100, 3, 1, 1),
 ]
 
 
@@ -77,7 +79,7 @@ def test_conv_implicit_gemm_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requant):
     p.close()
 
 
-@pytest.mark.parametrize("N,H,W,C,OC,k,s,pad", [CASES[i] for i in (0, 2, 4, 7, 9)])
+@pytest.mark.parametrize("N,H,W,C,OC,k,s,pad", [CASES[i] for i in (0, 2, 4, 7, 9, 11)])
 @pytest.mark.parametrize("requant", [False, True])
 @pytest.mark.parametrize("res_first", [False, True])
 def test_conv_residual_epilogue_bit_exact(cuda, N, H, W, C, OC, k, s, pad, requant, res_first):
