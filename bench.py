@@ -50,8 +50,8 @@ def alg_bytes(m):
     return m * K + N * K + 8 * N + 4 * m * N
 
 
-# DRAM bytes (read + write) of one k_w8a8_tc2<256,0> launch on this workload, from the
-# ncu capture summarised in profiles/k_w8a8_tc2_m4096_n4096_k4096.md.
+# DRAM bytes (read + write) of one k_w8a8_tc2<256,0> launch on this workload, from an
+# ncu capture of `python bench.py --profile` (dram__bytes_read.sum + dram__bytes_write.sum).
 NCU_TRAFFIC_HEAD = 34.148864e6 + 21.071360e6
 
 
@@ -125,13 +125,24 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _synth():
+    """tpt_infer_b200/synth.py loaded by its file path: the seeded generators
+    without the package's __init__, which loads the CUDA library (the CPU
+    reference arm must not load it)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_tpt_bench_synth", os.path.join(ROOT, "tpt_infer_b200", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def make_inputs(m, seed=1000, be=None):
     """Seeded W8A8 sweep inputs: W ~ N(0, 0.02) quantized per output channel (rows
     of W^T), A ~ N(0, 1) quantized per tensor, bias ~ N(0, 0.01). Quantized by the
     CUDA backend (``be``) on the GPU leg, by the oracle on the CPU-only legs; the
     two are bit-identical."""
-    from tpt_infer_b200 import synth
-
+    synth = _synth()
     w = synth.normal(K * N, seed, 0.0, 0.02).reshape(K, N)
     x = synth.normal(m * K, seed + 1, 0.0, 1.0)
     bias = synth.normal(N, seed + 2, 0.0, 0.01)
@@ -147,17 +158,29 @@ def make_inputs(m, seed=1000, be=None):
     return aq, float(sa), wq, ws, bias
 
 
-def cpu_reference(m, threads, budget_s, aq, sa, wq, ws, bias):
+def headline_config(world):
+    """The workload both arms report (the reference arm runs the same GEMM)."""
+    return {"workload": "w8a8_gemm", "M": M_HEAD, "N": N, "K": K, "bias": True,
+            "l2": "flushed before every timed GPU step (256 MB written, then read back)",
+            "parallelism": f"independent GEMM per GPU x{world}"}
+
+
+def cpu_reference(m, threads, budget_s, aq, sa, wq, ws, bias, b_kn=None):
     """Times the reference's own loop (ptq.rs:312-319, B [k, n] strided) with the
-    per-channel + bias epilogue over a bounded sample of output rows."""
+    per-channel + bias epilogue over a bounded sample of output rows (all m rows
+    when budget_s is None)."""
     from oracle import oracle as O
 
-    b_kn = np.ascontiguousarray(wq.reshape(N, K).T)
-    t0 = time.perf_counter()
-    O.w8a8_gemm_refloop(aq, b_kn, m, N, K, sa, ws, bias, max(1, threads), threads)
-    per_round = time.perf_counter() - t0  # one row per thread
-    rounds = max(1, int(budget_s / max(per_round, 1e-9)))
-    rows = min(m, rounds * max(1, threads))
+    if b_kn is None:
+        b_kn = np.ascontiguousarray(wq.reshape(N, K).T)
+    if budget_s is None:
+        rows = m
+    else:
+        t0 = time.perf_counter()
+        O.w8a8_gemm_refloop(aq, b_kn, m, N, K, sa, ws, bias, max(1, threads), threads)
+        per_round = time.perf_counter() - t0  # one row per thread
+        rounds = max(1, int(budget_s / max(per_round, 1e-9)))
+        rows = min(m, rounds * max(1, threads))
     t0 = time.perf_counter()
     O.w8a8_gemm_refloop(aq, b_kn, m, N, K, sa, ws, bias, rows, threads)
     dt = time.perf_counter() - t0
@@ -524,23 +547,29 @@ def dist_env():
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU loop for the headline GEMM
+    (quantized_matmul_i8, ptq.rs:312-319, with the per-channel scale + bias
+    epilogue), restated in C, on all host threads. Every timed step is the whole
+    M = 4096 GEMM; warm-up steps run a few rows. Loads neither the CUDA library
+    nor the tpt_infer_b200 package."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     aq, sa, wq, ws, bias = make_inputs(M_HEAD)
+    b_kn = np.ascontiguousarray(wq.reshape(N, K).T)
     for _ in range(args.warmup):
-        cpu_reference(M_HEAD, threads, 0.2, aq, sa, wq, ws, bias)
-    vals = [cpu_reference(M_HEAD, threads, args.ref_budget, aq, sa, wq, ws, bias) for _ in range(args.steps)]
-    v = float(np.median([x[2] for x in vals]))
-    rows = vals[-1][0]
+        cpu_reference(threads, threads, None, aq, sa, wq, ws, bias, b_kn)
+    vals = [cpu_reference(M_HEAD, threads, None, aq, sa, wq, ws, bias, b_kn) for _ in range(args.steps)]
+    total = sum(x[1] for x in vals)
+    v = args.steps * ops(M_HEAD) / total / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": float(np.median([x[1] for x in vals]) * 1e3),
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "w8a8_gemm", "M": M_HEAD, "N": N, "K": K, "sample_rows": rows},
+        "config": headline_config(world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{rows} of {M_HEAD} output rows per step, the reference loop order "
+                         "sample": f"the whole {M_HEAD}x{N}x{K} GEMM every step, the reference loop order "
                                    f"(ptq.rs:312-319) with per-channel scale + bias, {threads} OpenMP threads"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -699,16 +728,15 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "w8a8_gemm", "M": M_HEAD, "N": N, "K": K, "bias": True,
-                       "l2": "flushed before every timed step (256 MB written, then read back)",
-                       "parallelism": f"independent GEMM per GPU x{world}"},
+            "config": headline_config(world),
             "roofline": {"bound": "tensor", "achieved": ops(M_HEAD) / kernel_s / 1e12,
                          "peak": pk["int8_tops"], "unit": "TOP/s",
                          "frac": ops(M_HEAD) / kernel_s / 1e12 / pk["int8_tops"],
                          "traffic": NCU_TRAFFIC_HEAD,
-                         "traffic_note": "ncu dram__bytes_read+write of one launch "
-                                         "(profiles/k_w8a8_tc2_m4096_n4096_k4096.md); algorithmic "
-                                         f"{alg_bytes(M_HEAD) / 1e6:.1f} MB, Y mostly still in L2 at kernel end",
+                         "traffic_note": "ncu dram__bytes_read+write of one launch; algorithmic "
+                                         f"{alg_bytes(M_HEAD) / 1e6:.1f} MB. The 67 MB f32 Y is mostly still "
+                                         "in L2 when the kernel ends: its write-back to HBM lands in the L2 "
+                                         "flush between steps, outside the timed region",
                          "peak_note": f"2 x {pk['src']} dense bf16 burst (INT8 dense rate = 2x bf16 on B200)"},
             "e2e": {"value": world * ops(M_HEAD) / e2e_s / 1e12, "unit": UNIT, "h2d_bytes_per_step": M_HEAD * K,
                     "d2h_bytes_per_step": M_HEAD * N * 4},

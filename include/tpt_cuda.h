@@ -193,9 +193,18 @@ int tpt_cuda_quantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const float *x
 /* dequantize_i8_symmetric (dequant.rs:13-15) */
 int tpt_cuda_dequantize_i8_symmetric(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale,
                                      float *out);
+/* dequantize_i8_asymmetric (dequant.rs:18-22): out = (q - zero_point) * scale,
+ * the QuantParams of quantize_i8_asymmetric (quant.rs:6-12) passed as two values. */
+int tpt_cuda_dequantize_i8_asymmetric(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale,
+                                      int32_t zero_point, float *out);
 /* dequantize_i8_symmetric_per_channel (dequant.rs:26-37) */
 int tpt_cuda_dequantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const int8_t *q, size_t n,
                                                  const float *scales, size_t n_scales, float *out);
+/* dequantize_i4_symmetric (dequant.rs:45-50): unpack_i4(packed, n) (quant.rs:143-157)
+ * times one per-tensor scale; writes min(n, 2*packed_len) values, the count
+ * returned in *written. */
+int tpt_cuda_dequantize_i4_symmetric(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len, size_t n,
+                                     float scale, float *out, size_t *written);
 /* dequantize_i4_symmetric_per_channel (dequant.rs:56-71); n_scales rows of
  * row_elems values, rows ceil(row_elems/2) bytes apart. */
 int tpt_cuda_dequantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const uint8_t *packed,

@@ -136,6 +136,32 @@ def test_dequantize_bit_exact(cuda, rows, cols):
                           O.dequantize_i4_symmetric_per_channel(p, cols, s4))
 
 
+@pytest.mark.parametrize("n", [1, 7, 4096, 100003])
+def test_dequantize_asymmetric_and_i4_per_tensor_bit_exact(cuda, n):
+    # dequantize_i8_asymmetric (dequant.rs:18-22) on the reference quantizer's
+    # own (scale, zero_point), including the pinned-zero-point branches (all
+    # positive, all negative), and per-tensor dequantize_i4_symmetric
+    # (dequant.rs:45-50) with short packed buffers (unpack_i4 stops early)
+    for x in (O.normal(n, 95), np.abs(O.normal(n, 96)) + 0.5, -np.abs(O.normal(n, 97)) - 0.5):
+        x = x.astype(np.float32)
+        q, s, zp = O.quantize_i8_asymmetric(x)
+        got = cuda.dequantize_i8_asymmetric(q, s, zp)
+        assert np.array_equal(got, O.dequantize_i8_asymmetric(q, s, zp))
+    p, s4 = O.quantize_i4_symmetric(O.normal(n, 98))
+    for plen in sorted({p.size, (n + 1) // 2, n // 3, 0}):
+        got = cuda.dequantize_i4_symmetric(p[:plen], n, s4)
+        want = O.dequantize_i4_symmetric(p[:plen], n, s4)
+        assert got.size == min(n, 2 * plen) and np.array_equal(got, want)
+
+
+def test_dequantize_asymmetric_kat(cuda):
+    # dequant.rs:87-95: the asymmetric round trip of [1, 2, 3, 4] within 0.01
+    data = np.array([1.0, 2.0, 3.0, 4.0], np.float32)
+    q, s, zp = cuda.quantize_i8_asymmetric(data)
+    d = cuda.dequantize_i8_asymmetric(q, s, zp)
+    assert np.all(np.abs(d - data) < 0.01)
+
+
 def test_ptq_roundtrip_kats(cuda):
     # ptq.rs:358-391 on the device quantizers
     w = (np.arange(32, dtype=np.float32) / np.float32(32.0) - np.float32(0.5)).astype(np.float32)

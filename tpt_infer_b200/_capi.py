@@ -66,6 +66,8 @@ SIGNATURES = {
     "tpt_cuda_dequantize_i8_symmetric": (C.c_int, [ctxp, vp, sz, C.c_float, vp]),
     "tpt_cuda_dequantize_i8_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, vp, sz, vp]),
     "tpt_cuda_dequantize_i4_symmetric_per_channel": (C.c_int, [ctxp, vp, sz, sz, vp, sz, vp]),
+    "tpt_cuda_dequantize_i8_asymmetric": (C.c_int, [ctxp, vp, sz, C.c_float, C.c_int32, vp]),
+    "tpt_cuda_dequantize_i4_symmetric": (C.c_int, [ctxp, vp, sz, sz, C.c_float, vp, szp]),
     "tpt_cuda_quantized_matmul_i8": (C.c_int, [ctxp, vp, sz, sz, sz, C.c_float, vp, sz, sz, sz, vp, sz, vp, sz]),
     "tpt_cuda_quantize_i8_symmetric_dev": (C.c_int, [ctxp, vp, sz, vp, vp]),
     "tpt_cuda_quantize_i8_static_dev": (C.c_int, [ctxp, vp, sz, C.c_float, vp]),

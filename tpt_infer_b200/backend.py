@@ -341,6 +341,23 @@ class CudaBackend:
                                                                      _ptr(out)))
         return out
 
+    def dequantize_i8_asymmetric(self, q, scale, zero_point):
+        """dequantize_i8_asymmetric (dequant.rs:18-22): (q - zero_point) * scale."""
+        q = _host(q, np.int8).ravel()
+        out = np.empty(q.size, np.float32)
+        self._check(lib.tpt_cuda_dequantize_i8_asymmetric(self._ctx, _ptr(q), q.size, float(scale), int(zero_point),
+                                                          _ptr(out)))
+        return out
+
+    def dequantize_i4_symmetric(self, packed, n, scale):
+        """dequantize_i4_symmetric (dequant.rs:45-50): min(n, 2 * len(packed)) values."""
+        p = _host(packed, np.uint8).ravel()
+        out = np.empty(max(min(n, 2 * p.size), 1), np.float32)
+        w = C.c_size_t()
+        self._check(lib.tpt_cuda_dequantize_i4_symmetric(self._ctx, _ptr(p), p.size, n, float(scale), _ptr(out),
+                                                         C.byref(w)))
+        return out[:w.value]
+
     def dequantize_i4_symmetric_per_channel(self, packed, row_elems, scales):
         """dequantize_i4_symmetric_per_channel (dequant.rs:56-71)."""
         p, s = _host(packed, np.uint8).ravel(), _host(scales, np.float32).ravel()

@@ -176,6 +176,7 @@ int launch_dequant_i8_rows(tpt_cuda_ctx *ctx, const int8_t *q, size_t rows, size
                            const float *scales, float *out);
 int launch_dequant_i4_rows(tpt_cuda_ctx *ctx, const uint8_t *p, size_t rows, size_t row_elems,
                            size_t packed_len, const float *scales, float *out);
+int launch_dequant_i8_asym(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale, int32_t zp, float *out);
 // i8 GEMM: y[m,n] (+bias, act), raw i32 acc when acc != nullptr, or y
 // requantized to int8 when rq.q != nullptr; W^T [n,k].
 int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tpt_cuda_weights *w,

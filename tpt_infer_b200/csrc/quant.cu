@@ -240,6 +240,15 @@ __global__ void k_dequant_i8_rows(const int8_t *__restrict__ q, size_t rows, siz
         out[i] = __fmul_rn((float)q[i], scales[i / cols]);
 }
 
+// dequant.rs:18-22: out = (q as f32 - zero_point as f32) * scale (both
+// conversions exact, the difference of two small integers exact, one rounding)
+__global__ void k_dequant_i8_asym(const int8_t *__restrict__ q, size_t n, float scale, int32_t zp,
+                                  float *__restrict__ out) {
+    const float z = (float)zp;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __fmul_rn(__fsub_rn((float)q[i], z), scale);
+}
+
 // dequant.rs:56-71: rows of ceil(row_elems/2) bytes; values past packed_len absent
 __global__ void k_dequant_i4_rows(const uint8_t *__restrict__ p, size_t rows, size_t row_elems, size_t packed_len,
                                   const float *__restrict__ scales, float *__restrict__ out) {
@@ -323,6 +332,11 @@ int launch_dequant_i8_rows(tpt_cuda_ctx *ctx, const int8_t *q, size_t rows, size
                            float *out) {
     k_dequant_i8_rows<<<grid_1d(rows * cols, 256, cap_grid(ctx)), 256, 0, ctx->stream>>>(q, rows, cols, scales, out);
     return after_launch(ctx, "dequantize_i8");
+}
+
+int launch_dequant_i8_asym(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale, int32_t zp, float *out) {
+    k_dequant_i8_asym<<<grid_1d(n, 256, cap_grid(ctx)), 256, 0, ctx->stream>>>(q, n, scale, zp, out);
+    return after_launch(ctx, "dequantize_i8_asymmetric");
 }
 
 int launch_dequant_i4_rows(tpt_cuda_ctx *ctx, const uint8_t *p, size_t rows, size_t row_elems, size_t packed_len,

@@ -667,6 +667,48 @@ int tpt_cuda_dequantize_i8_symmetric_per_channel(tpt_cuda_ctx *ctx, const int8_t
     return sync_and_check(ctx);
 }
 
+int tpt_cuda_dequantize_i8_asymmetric(tpt_cuda_ctx *ctx, const int8_t *q, size_t n, float scale, int32_t zero_point,
+                                      float *out) {
+    CHECK_CTX(ctx);
+    if (n == 0) return TPT_OK;
+    if (!q || !out) return TPT_INVALID;
+    Staging st(ctx);
+    st.reserve(n);
+    st.reserve(n * 4);
+    TRY(st.commit());
+    int8_t *dq = st.take<int8_t>(n);
+    float *dy = st.take<float>(n);
+    TRY(h2d(ctx, dq, q, n));
+    TRY(launch_dequant_i8_asym(ctx, dq, n, scale, zero_point, dy));
+    TRY(d2h(ctx, out, dy, n * 4));
+    return sync_and_check(ctx);
+}
+
+// dequantize_i4_symmetric (dequant.rs:45-50) = unpack_i4(packed, n) (quant.rs:143-157: min(n, 2 * packed_len)
+// values) scaled: one row of n values with a single scale.
+int tpt_cuda_dequantize_i4_symmetric(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len, size_t n,
+                                     float scale, float *out, size_t *written) {
+    CHECK_CTX(ctx);
+    const size_t cnt = n < 2 * packed_len ? n : 2 * packed_len;
+    if (written) *written = cnt;
+    if (cnt == 0) return TPT_OK;
+    if (!packed || !out) return TPT_INVALID;
+    const size_t pb = (cnt + 1) / 2;  // the bytes holding the cnt values
+    Staging st(ctx);
+    st.reserve(pb);
+    st.reserve(4);
+    st.reserve(cnt * 4);
+    TRY(st.commit());
+    uint8_t *dp = st.take<uint8_t>(pb);
+    float *ds = st.take<float>(1);
+    float *dy = st.take<float>(cnt);
+    TRY(h2d(ctx, dp, packed, pb));
+    TRY(h2d(ctx, ds, &scale, 4));
+    TRY(launch_dequant_i4_rows(ctx, dp, 1, cnt, pb, ds, dy));
+    TRY(d2h(ctx, out, dy, cnt * 4));
+    return sync_and_check(ctx);
+}
+
 int tpt_cuda_dequantize_i4_symmetric_per_channel(tpt_cuda_ctx *ctx, const uint8_t *packed, size_t packed_len,
                                                  size_t row_elems, const float *scales, size_t n_scales,
                                                  float *out) {
