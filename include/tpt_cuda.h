@@ -406,10 +406,13 @@ int tpt_cuda_plan_set_comm(tpt_cuda_plan *plan, tpt_cuda_comm *comm);
  * rejected with TPT_INVALID before any work is enqueued. The first call on a
  * device looks up the scratch's device address (cudaGetSymbolAddress, with
  * that device current) and caches it, so make that first call before any
- * stream capture. All calls on a device share the scratch: calls whose
- * kernels may overlap on the GPU (different streams without ordering) race
- * on it. Nothing in the scratch needs to start at zero: a call only reads
- * what it wrote itself earlier in stream order. */
+ * stream capture. The cached address belongs to the device's primary context:
+ * after cudaDeviceReset on that device the library's device image may be
+ * loaded at another address, so do not use this entry point in a process that
+ * resets a device it has already been called on. All calls on a device share
+ * the scratch: calls whose kernels may overlap on the GPU (different streams
+ * without ordering) race on it. Nothing in the scratch needs to start at
+ * zero: a call only reads what it wrote itself earlier in stream order. */
 int tpt_cuda_quantize_i8_symmetric_noalloc(const float *x, size_t n, int8_t *q, float *scale,
                                            void *stream);
 

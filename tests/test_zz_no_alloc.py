@@ -55,6 +55,35 @@ def test_noalloc_quantize_matches_context_entry_point_on_two_calls(cuda):
         assert torch.equal(q_na, q_ref)
 
 
+@pytest.mark.parametrize("n,special", [(3 * 8192, False), (3 * 8192 + 1, False), (8192, False), (40_000, True)])
+def test_noalloc_quantize_tile_edges_and_non_finite(cuda, n, special):
+    # n an exact multiple of the 8192-element reduction tile (the last tile
+    # full) and one past it (a one-element last tile); an input holding NaN and
+    # +-Inf, where both entry points must ignore NaN in the max and agree on the
+    # resulting scale and codes bit for bit
+    import torch
+
+    from tpt_infer_b200._capi import lib
+
+    h = O.normal(n, 21, 0.0, 1.0)
+    if special:
+        h[5], h[777], h[n - 1] = np.nan, np.inf, -np.inf
+    x = torch.from_numpy(h).cuda()
+    for _ in range(2):
+        q_na = torch.empty(n, dtype=torch.int8, device="cuda")
+        s_na = torch.empty(1, dtype=torch.float32, device="cuda")
+        q_ref = torch.empty(n, dtype=torch.int8, device="cuda")
+        s_ref = torch.empty(1, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        st = lib.tpt_cuda_quantize_i8_symmetric_noalloc(_p(x), n, _p(q_na), _p(s_na), None)
+        assert st == 0
+        torch.cuda.synchronize()
+        cuda.quantize_i8_symmetric_dev(x, q_ref, s_ref)
+        cuda.sync()
+        assert s_na.view(torch.int32).item() == s_ref.view(torch.int32).item()
+        assert torch.equal(q_na, q_ref)
+
+
 def test_noalloc_quantize_edge_sizes(cuda):
     import torch
 
