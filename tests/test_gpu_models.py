@@ -207,3 +207,30 @@ def test_plan_fusion_rules(cuda, m):
     assert np.array_equal(y_unfused, want_y)
     assert np.array_equal(q_fused, O.quantize_i8_static(want_y, sy))
     p.close()
+
+
+def test_resnet18_plan_bit_exact_batch256(cuda):
+    # the benchmarked shape: batch 256 (TMA-im2col operands, several persistent
+    # tile rounds per conv, every run-time fusion). The calibration over the whole
+    # batch and the logits of all 256 images are bit-exact against the oracle's
+    # replay of the same graph.
+    from tpt_infer_b200 import graphs, synth
+
+    B, IMG = 256, 3 * 224 * 224
+    spec = graphs.resnet18_weights(cuda)
+    p, x, logits = graphs.build_resnet18(cuda, B, spec)
+    xcal = synth.normal(B * IMG, 31)
+    p.calibrate(True)
+    p.run({x: xcal}, [logits])
+    p.freeze()
+    cal = OM._Scales()
+    OM.resnet18(xcal, spec, B, calib=cal)
+    del xcal
+    assert np.array_equal(p.scales(), cal.frozen())
+    xin = synth.normal(B * IMG, 32)
+    got, = p.run({x: xin}, [logits])
+    p.close()
+    for b0 in range(0, B, 64):
+        want = OM.resnet18(xin[b0 * IMG:(b0 + 64) * IMG], spec, 64, scales=cal.frozen())
+        g = got[b0 * 1000:(b0 + 64) * 1000]
+        assert np.array_equal(g, want), (b0, _relerr(g, want))
