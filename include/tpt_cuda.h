@@ -312,7 +312,24 @@ enum tpt_op_kind {
                                    the K-contiguous rows of the next GEMM) */
     TPT_OP_GEMM_F32 = 15        /* ONNX Gemm: out [d0=m, d2=n] = f0 * op(in0) op(in1) + C; in0 [m,k] (d3: stored
                                    [k,m]), in1 [d1=k, n] (d4: stored [n,k]), in2 C [n] or [m,n] already scaled
-                                   by beta, or -1 */
+                                   by beta, or -1 */,
+    /* The rest of the reference runtime's dispatch table (exec.rs:347-533), f32, bit-exact with its kernels.
+       Shapes are padded to rank 8 (MAX_RANK, crates/tpt-infer-core/src/shape.rs:4) with leading 1s. */
+    TPT_OP_BINARY = 16,         /* out = in0 op in1, numpy broadcasting (kernels.rs:92-137); act = 0 add, 1 sub,
+                                   2 mul, 3 div; d0..d7 out dims; d8 / d9: masks of the dims where in0 / in1 is 1 */
+    TPT_OP_UNARY = 17,          /* act = 1 relu, 2 sigmoid, 3 gelu (Backend::relu/sigmoid/gelu); d0 = n */
+    TPT_OP_POOL_NCHW = 18,      /* act = 0 max (kernels.rs:271-325), 1 average (count_include_pad 0, :335-390);
+                                   d0..d11 = N,C,H,W,KH,KW,sh,sw,ph,pw,OH,OW */
+    TPT_OP_BATCHNORM = 19,      /* in1 = [scale|bias|mean|var] (d1 values each), eps f0 (kernels.rs:425-476);
+                                   d0 = numel, d2 = 1: channel mode with d3 = H*W, 0: element mode */
+    TPT_OP_TRANSPOSE = 20,      /* d0..d7 input dims, d8..d15 perm (out axis i reads input axis perm[i]) */
+    TPT_OP_CONCAT_COPY = 21,    /* one Concat input into out (concat_copy_one, kernels.rs:548-588): d0 outer,
+                                   d1 source block, d2 output block, d3 offset (elements) */
+    TPT_OP_CONV2D_F32 = 22,     /* Backend::conv2d NCHW f32, in1 OIHW weight; d0..d10 = N,C,H,W,OC,KH,KW,sh,sw,
+                                   ph,pw */
+    TPT_OP_BATCHED_MATMUL = 23  /* in0 [batch.., m, k] x in1 [batch.., k, n] -> [batch.., m, n] (shapes.rs:163-186);
+                                   d0..d5 output batch dims, d6 / d7 masks of the batch dims where in0 / in1 is 1,
+                                   d8 m, d9 k, d10 n */
 };
 
 typedef struct tpt_plan_op {

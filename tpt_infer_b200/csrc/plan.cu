@@ -44,6 +44,17 @@ int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, in
                      int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
                      int act, float *y, bool *handled, Requant rq, Residual res = Residual());
 int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
+int launch_binary(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, const size_t od[8], unsigned amask,
+                  unsigned bmask, int op, size_t n);
+int launch_pool_nchw(tpt_cuda_ctx *ctx, const float *x, float *y, int avg, size_t NC, int H, int W, int KH, int KW,
+                     int sh, int sw, int ph, int pw, int OH, int OW);
+int launch_batchnorm(tpt_cuda_ctx *ctx, const float *x, const float *prm, float *y, size_t n, size_t plen, size_t hw,
+                     int channel_mode, float eps);
+int launch_transpose(tpt_cuda_ctx *ctx, const float *x, float *y, const size_t xd[8], const size_t perm[8], size_t n);
+int launch_concat_copy(tpt_cuda_ctx *ctx, const float *src, float *dst, size_t outer, size_t src_block,
+                       size_t out_block, size_t offset);
+int launch_bmm(tpt_cuda_ctx *ctx, const float *a, const float *b, float *c, const size_t bd[6], unsigned amask,
+               unsigned bmask, size_t m, size_t k, size_t n);
 }  // namespace tpt
 
 using namespace tpt;
@@ -199,11 +210,131 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
                                        (int)d[11]);
         case TPT_OP_GAP_NHWC:
             return launch_gap_nhwc(ctx, F(p, o.in0), F(p, o.out), (int)d[0], (int)d[1], (int)d[2]);
+        case TPT_OP_BINARY: {
+            size_t n = 1;
+            for (int i = 0; i < 8; i++) n *= d[i];
+            return launch_binary(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d, (unsigned)d[8], (unsigned)d[9], o.act,
+                                 n);
+        }
+        case TPT_OP_UNARY:
+            return launch_unary(ctx, o.act, F(p, o.in0), F(p, o.out), d[0]);
+        case TPT_OP_POOL_NCHW:
+            return launch_pool_nchw(ctx, F(p, o.in0), F(p, o.out), o.act, d[0] * d[1], (int)d[2], (int)d[3],
+                                    (int)d[4], (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10],
+                                    (int)d[11]);
+        case TPT_OP_BATCHNORM:
+            return launch_batchnorm(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], d[1], d[3], (int)d[2], o.f0);
+        case TPT_OP_TRANSPOSE:
+            return launch_transpose(ctx, F(p, o.in0), F(p, o.out), d, d + 8, p->tensors[o.in0].numel);
+        case TPT_OP_CONCAT_COPY:
+            return launch_concat_copy(ctx, F(p, o.in0), F(p, o.out), d[0], d[1], d[2], d[3]);
+        case TPT_OP_CONV2D_F32: {
+            const size_t is[4] = {d[0], d[1], d[2], d[3]}, ws[4] = {d[4], d[1], d[5], d[6]};
+            const size_t oh = (d[2] + 2 * d[9] - d[5]) / d[7] + 1, ow = (d[3] + 2 * d[10] - d[6]) / d[8] + 1;
+            return launch_conv2d_f32(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), is, ws, oh, ow, d[7], d[8], d[9],
+                                     d[10]);
+        }
+        case TPT_OP_BATCHED_MATMUL:
+            return launch_bmm(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d, (unsigned)d[6], (unsigned)d[7], d[8],
+                              d[9], d[10]);
         default:
             return TPT_UNSUPPORTED;
     }
 }
 
+}  // namespace
+
+namespace {
+// Sizes of the graph-level ops checked against their tensors at add time, so a
+// launch can never index outside a tensor. Invalid geometry (a zero stride, a
+// non-permutation, a shape that does not broadcast) is TPT_INVALID.
+size_t numel_of(tpt_cuda_plan *p, int id) { return p->tensors[id].numel; }
+bool prod_ok(const size_t *d, int n, size_t *out) {
+    size_t r = 1;
+    for (int i = 0; i < n; i++)
+        if (!checked_mul(r, d[i], &r)) return false;
+    *out = r;
+    return true;
+}
+int validate_graph_op(tpt_cuda_plan *p, const tpt_plan_op &o) {
+    const size_t *d = o.dims;
+    const bool f32 = p->tensors[o.in0].dtype == TPT_DT_F32 && p->tensors[o.out].dtype == TPT_DT_F32 &&
+                     (o.in1 < 0 || p->tensors[o.in1].dtype == TPT_DT_F32);
+    if (!f32) return TPT_INVALID;
+    switch (o.kind) {
+        case TPT_OP_BINARY: {
+            if (o.in1 < 0 || o.act < 0 || o.act > 3 || d[8] > 255 || d[9] > 255) return TPT_INVALID;
+            size_t n, na = 1, nb = 1;
+            if (!prod_ok(d, 8, &n) || n != numel_of(p, o.out)) return TPT_INVALID;
+            for (int i = 0; i < 8; i++) {
+                if (!(d[8] >> i & 1)) na *= d[i];
+                if (!(d[9] >> i & 1)) nb *= d[i];
+            }
+            return na == numel_of(p, o.in0) && nb == numel_of(p, o.in1) ? TPT_OK : TPT_INVALID;
+        }
+        case TPT_OP_UNARY:
+            return o.act >= 1 && o.act <= 3 && d[0] <= numel_of(p, o.in0) && d[0] <= numel_of(p, o.out) ? TPT_OK
+                                                                                                      : TPT_INVALID;
+        case TPT_OP_POOL_NCHW: {
+            size_t a, b;
+            const size_t in_d[4] = {d[0], d[1], d[2], d[3]}, out_d[4] = {d[0], d[1], d[10], d[11]};
+            if (o.act < 0 || o.act > 1 || d[4] == 0 || d[5] == 0 || d[6] == 0 || d[7] == 0) return TPT_INVALID;
+            for (int i = 2; i < 12; i++)
+                if (d[i] > INT32_MAX) return TPT_INVALID;
+            if (!prod_ok(in_d, 4, &a) || !prod_ok(out_d, 4, &b)) return TPT_INVALID;
+            return a == numel_of(p, o.in0) && b == numel_of(p, o.out) ? TPT_OK : TPT_INVALID;
+        }
+        case TPT_OP_BATCHNORM: {
+            size_t four;
+            if (o.in1 < 0 || d[1] == 0 || !checked_mul(d[1], 4, &four) || four != numel_of(p, o.in1)) return TPT_INVALID;
+            if (d[0] != numel_of(p, o.in0) || d[0] != numel_of(p, o.out)) return TPT_INVALID;
+            if (d[2]) return d[3] && d[0] % (d[1] * d[3]) == 0 ? TPT_OK : TPT_INVALID;
+            return d[1] == d[0] ? TPT_OK : TPT_INVALID;
+        }
+        case TPT_OP_TRANSPOSE: {
+            size_t n;
+            unsigned seen = 0;
+            for (int i = 0; i < 8; i++) {
+                if (d[8 + i] > 7 || (seen >> d[8 + i] & 1)) return TPT_INVALID;
+                seen |= 1u << d[8 + i];
+            }
+            if (!prod_ok(d, 8, &n)) return TPT_INVALID;
+            return n == numel_of(p, o.in0) && n == numel_of(p, o.out) ? TPT_OK : TPT_INVALID;
+        }
+        case TPT_OP_CONCAT_COPY: {
+            size_t n, last;
+            if (d[0] == 0 || d[1] == 0) return TPT_INVALID;
+            if (!checked_mul(d[0], d[1], &n) || n > numel_of(p, o.in0)) return TPT_INVALID;
+            if (!checked_mul(d[0] - 1, d[2], &last) || d[3] + d[1] > d[2]) return TPT_INVALID;
+            return last + d[2] <= numel_of(p, o.out) ? TPT_OK : TPT_INVALID;
+        }
+        case TPT_OP_CONV2D_F32: {
+            size_t a, w, y;
+            if (o.in1 < 0 || d[7] == 0 || d[8] == 0) return TPT_INVALID;
+            if (d[2] + 2 * d[9] < d[5] || d[3] + 2 * d[10] < d[6]) return TPT_INVALID;
+            const size_t oh = (d[2] + 2 * d[9] - d[5]) / d[7] + 1, ow = (d[3] + 2 * d[10] - d[6]) / d[8] + 1;
+            const size_t xd[4] = {d[0], d[1], d[2], d[3]}, wd[4] = {d[4], d[1], d[5], d[6]}, yd[4] = {d[0], d[4], oh, ow};
+            if (!prod_ok(xd, 4, &a) || !prod_ok(wd, 4, &w) || !prod_ok(yd, 4, &y)) return TPT_INVALID;
+            return a == numel_of(p, o.in0) && w == numel_of(p, o.in1) && y == numel_of(p, o.out) ? TPT_OK
+                                                                                                 : TPT_INVALID;
+        }
+        case TPT_OP_BATCHED_MATMUL: {
+            if (o.in1 < 0 || d[6] > 63 || d[7] > 63) return TPT_INVALID;
+            size_t bo, ba = 1, bb = 1, mk, kn, mn, t;
+            if (!prod_ok(d, 6, &bo)) return TPT_INVALID;
+            for (int i = 0; i < 6; i++) {
+                if (!(d[6] >> i & 1)) ba *= d[i];
+                if (!(d[7] >> i & 1)) bb *= d[i];
+            }
+            if (!checked_mul(d[8], d[9], &mk) || !checked_mul(d[9], d[10], &kn) || !checked_mul(d[8], d[10], &mn))
+                return TPT_INVALID;
+            if (!checked_mul(ba, mk, &t) || t != numel_of(p, o.in0)) return TPT_INVALID;
+            if (!checked_mul(bb, kn, &t) || t != numel_of(p, o.in1)) return TPT_INVALID;
+            return checked_mul(bo, mn, &t) && t == numel_of(p, o.out) ? TPT_OK : TPT_INVALID;
+        }
+    }
+    return TPT_OK;
+}
 }  // namespace
 
 #define CHECK_PLAN(pl)                                  \
@@ -273,7 +404,11 @@ int tpt_cuda_plan_add_op(tpt_cuda_plan *p, const tpt_plan_op *op) {
     if (!valid_id(p, op->in0) || !valid_id(p, op->out)) return TPT_INVALID;
     if ((op->in1 >= 0 && !valid_id(p, op->in1)) || (op->in2 >= 0 && !valid_id(p, op->in2))) return TPT_INVALID;
     if (op->kind == TPT_OP_LINEAR_W8A8 && (!op->w || op->w->kind != 8)) return TPT_INVALID;
-    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_GEMM_F32) return TPT_UNSUPPORTED;
+    if (op->kind < TPT_OP_QUANTIZE || op->kind > TPT_OP_BATCHED_MATMUL) return TPT_UNSUPPORTED;
+    if (op->kind >= TPT_OP_BINARY) {
+        const int st = validate_graph_op(p, *op);
+        if (st) return st;
+    }
     if (op->kind == TPT_OP_GEMM_F32) {
         size_t mk = 0, kn = 0, mn = 0;
         const size_t m = op->dims[0], k = op->dims[1], n = op->dims[2];
