@@ -111,6 +111,10 @@ _sig("tpto_average_pool2d", None, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz,
 _sig("tpto_add_bias_nchw", None, _f32p, _sz, _sz, _sz, _f32p)
 _sig("tpto_add_bias_rows", None, _f32p, _sz, _sz, _f32p)
 _sig("tpto_layernorm", None, _f32p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
+_sig("tpto_binary", None, C.c_int, _f32p, _szp, _sz, _f32p, _szp, _sz, _f32p, _szp, _sz)
+_sig("tpto_batch_norm", None, _f32p, _sz, _f32p, _f32p, _f32p, _f32p, _sz, _sz, C.c_float, _f32p)
+_sig("tpto_transpose", None, _f32p, _szp, _sz, _szp, _f32p)
+_sig("tpto_concat_copy_one", None, _f32p, _sz, _sz, _sz, _sz, _f32p, _sz)
 
 
 def _check(st):
@@ -434,3 +438,68 @@ def layernorm(x, rows, cols, gamma, beta, eps=1e-5):
     y = np.empty(rows * cols, np.float32)
     _lib.tpto_layernorm(x, rows, cols, _f32(gamma).ravel(), _f32(beta).ravel(), eps, y)
     return y
+
+
+# ------------------------------------------------------------------ runtime dispatch table
+BIN_ADD, BIN_SUB, BIN_MUL, BIN_DIV = 0, 1, 2, 3
+
+
+def _dims(d):
+    return np.ascontiguousarray(np.asarray(d, np.uintp).ravel())
+
+
+def broadcast_shape(ad, bd):
+    """numpy broadcasting of two shapes, or None (kernels.rs:43-58 check_broadcast)."""
+    r = max(len(ad), len(bd))
+    a = [1] * (r - len(ad)) + list(ad)
+    b = [1] * (r - len(bd)) + list(bd)
+    out = []
+    for x, y in zip(a, b):
+        if x != y and x != 1 and y != 1:
+            return None
+        out.append(max(x, y))
+    return out
+
+
+def binary(op, a, ad, b, bd, od=None):
+    """kernels::binary (crates/tpt-infer-runtime/src/kernels.rs:92-137)."""
+    od = list(od if od is not None else broadcast_shape(ad, bd))
+    a, b = _f32(a).ravel(), _f32(b).ravel()
+    out = np.empty(int(np.prod(od, dtype=np.int64)), np.float32)
+    _lib.tpto_binary(op, a, _dims(ad), len(ad), b, _dims(bd), len(bd), out, _dims(od), len(od))
+    return out
+
+
+def batch_norm(x, x_dims, scale, bias, mean, var, eps):
+    """kernels::batch_norm (kernels.rs:425-476): channel mode for rank-4 x with one
+    parameter per channel, else element mode."""
+    x = _f32(x).ravel()
+    scale, bias, mean, var = (_f32(v).ravel() for v in (scale, bias, mean, var))
+    hw = int(x_dims[2] * x_dims[3]) if len(x_dims) == 4 and scale.size == x_dims[1] else 0
+    out = np.empty(x.size, np.float32)
+    _lib.tpto_batch_norm(x, x.size, scale, bias, mean, var, scale.size, hw, eps, out)
+    return out
+
+
+def transpose(x, x_dims, perm):
+    """kernels::transpose (kernels.rs:484-532)."""
+    x = _f32(x).ravel()
+    out = np.empty(x.size, np.float32)
+    _lib.tpto_transpose(x, _dims(x_dims), len(x_dims), _dims(perm), out)
+    return out
+
+
+def concat(inputs, dims_list, axis):
+    """Concat of the runtime (exec.rs:471-513) through concat_copy_one (kernels.rs:548-588)."""
+    rank = len(dims_list[0])
+    ax = axis + rank if axis < 0 else axis
+    od = list(dims_list[0])
+    od[ax] = sum(d[ax] for d in dims_list)
+    inner = int(np.prod(od[ax + 1:], dtype=np.int64))
+    out = np.empty(int(np.prod(od, dtype=np.int64)), np.float32)
+    off = 0
+    for x, d in zip(inputs, dims_list):
+        x = _f32(x).ravel()
+        _lib.tpto_concat_copy_one(out, od[ax], off, d[ax], inner, x, x.size)
+        off += d[ax]
+    return out, od

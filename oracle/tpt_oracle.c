@@ -664,3 +664,98 @@ void tpto_layernorm(const float *x, size_t rows, size_t cols, const float *gamma
         for (size_t j = 0; j < cols; j++) y[r * cols + j] = (xr[j] - mean) * inv * gamma[j] + beta[j];
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* The rest of the runtime's dispatch table (exec.rs:347-533)          */
+/* ------------------------------------------------------------------ */
+
+/* kernels::binary (crates/tpt-infer-runtime/src/kernels.rs:92-137): numpy
+ * broadcasting over dims padded to rank 8 (pad, :33-41; map_coord, :60-66),
+ * out[i] = a[ai] op b[bi], op 0 add 1 sub 2 mul 3 div. Shapes were checked by
+ * the caller (check_broadcast, :43-58). */
+void tpto_binary(int op, const float *a, const size_t *ad, size_t ar, const float *b, const size_t *bd, size_t br,
+                 float *out, const size_t *od, size_t orank) {
+    size_t A[8], B[8], O[8], n = 1;
+    for (int d = 0; d < 8; d++) A[d] = B[d] = O[d] = 1;
+    for (size_t d = 0; d < ar; d++) A[8 - ar + d] = ad[d];
+    for (size_t d = 0; d < br; d++) B[8 - br + d] = bd[d];
+    for (size_t d = 0; d < orank; d++) O[8 - orank + d] = od[d];
+    for (int d = 0; d < 8; d++) n *= O[d];
+    for (size_t i = 0; i < n; i++) {
+        size_t rem = i, ai = 0, bi = 0, as = 1, bs = 1;
+        for (int d = 7; d >= 0; d--) {
+            size_t c = rem % O[d];
+            rem /= O[d];
+            ai += (A[d] == 1 ? 0 : c) * as;
+            as *= A[d];
+            bi += (B[d] == 1 ? 0 : c) * bs;
+            bs *= B[d];
+        }
+        float x = a[ai], y = b[bi];
+        out[i] = op == 0 ? x + y : op == 1 ? x - y : op == 2 ? x * y : x / y;
+    }
+}
+
+/* sqrt_f32 (kernels.rs:397-411): the exponent halved through the bits, four
+ * Newton steps. */
+static float sqrt_ref(float x) {
+    if (x != x || x < 0.0f) return NAN;
+    if (x == 0.0f || isinf(x)) return x;
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u = (u >> 1) + (1u << 29);
+    float y;
+    memcpy(&y, &u, 4);
+    for (int i = 0; i < 4; i++) y = 0.5f * (y + x / y);
+    return y;
+}
+
+/* kernels::batch_norm (kernels.rs:425-476), channel mode (x [N, C, H, W],
+ * plen = C: hw = H*W) or element mode (hw = 0, plen = n). */
+void tpto_batch_norm(const float *x, size_t n, const float *scale, const float *bias, const float *mean,
+                     const float *var, size_t plen, size_t hw, float eps, float *out) {
+    if (hw) {
+        size_t c = plen, nb = n / (c * hw);
+        for (size_t ni = 0; ni < nb; ni++)
+            for (size_t ci = 0; ci < c; ci++) {
+                float inv = 1.0f / sqrt_ref(var[ci] + eps);
+                float f = scale[ci] * inv;
+                float g = bias[ci] - mean[ci] * f;
+                size_t base = (ni * c + ci) * hw;
+                for (size_t i = base; i < base + hw; i++) out[i] = x[i] * f + g;
+            }
+    } else {
+        for (size_t i = 0; i < n; i++) {
+            float inv = 1.0f / sqrt_ref(var[i] + eps);
+            float f = scale[i] * inv;
+            out[i] = (x[i] - mean[i]) * f + bias[i];
+        }
+    }
+}
+
+/* kernels::transpose (kernels.rs:484-532): out axis d reads input axis perm[d]. */
+void tpto_transpose(const float *x, const size_t *xd, size_t rank, const size_t *perm, float *out) {
+    size_t od[8], xs[8], n = 1, s = 1;
+    for (size_t d = 0; d < rank; d++) od[d] = xd[perm[d]];
+    for (size_t d = rank; d-- > 0;) {
+        xs[d] = s;
+        s *= xd[d];
+    }
+    for (size_t d = 0; d < rank; d++) n *= od[d];
+    for (size_t i = 0; i < n; i++) {
+        size_t rem = i, xi = 0;
+        for (size_t d = rank; d-- > 0;) {
+            size_t c = rem % od[d];
+            rem /= od[d];
+            xi += c * xs[perm[d]];
+        }
+        out[i] = x[xi];
+    }
+}
+
+/* kernels::concat_copy_one (kernels.rs:548-588) */
+void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_src, size_t inner, const float *src,
+                          size_t src_len) {
+    size_t sb = c_src * inner, ob = c_total * inner, outer = src_len / sb;
+    for (size_t o = 0; o < outer; o++) memcpy(out + o * ob + c_offset * inner, src + o * sb, sb * 4);
+}

@@ -131,6 +131,15 @@ void tpto_add_bias_rows(float *out, size_t rows, size_t cols, const float *bias)
 void tpto_layernorm(const float *x, size_t rows, size_t cols, const float *gamma,
                     const float *beta, float eps, float *y);
 
+/* The rest of the runtime's dispatch table (kernels.rs) */
+void tpto_binary(int op, const float *a, const size_t *ad, size_t ar, const float *b, const size_t *bd, size_t br,
+                 float *out, const size_t *od, size_t orank);
+void tpto_batch_norm(const float *x, size_t n, const float *scale, const float *bias, const float *mean,
+                     const float *var, size_t plen, size_t hw, float eps, float *out);
+void tpto_transpose(const float *x, const size_t *xd, size_t rank, const size_t *perm, float *out);
+void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_src, size_t inner, const float *src,
+                          size_t src_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -354,3 +354,73 @@ def test_gemm_errors():
     with pytest.raises(O.OracleError) as e:
         O.gemm(np.ones(6), 2, 3, np.ones(9), 3, c=np.ones(4))
     assert e.value.code == O.SHAPE_MISMATCH
+
+
+# ---------------------------------------------------------------- runtime kernels (kernels.rs tests)
+def test_runtime_binary_kats():
+    # kernels.rs:592-625: broadcast add, equal-shape mul/sub/div
+    assert O.binary(O.BIN_ADD, [1, 2], [2, 1], [10, 20, 30], [1, 3]).tolist() == [11, 21, 31, 12, 22, 32]
+    assert O.binary(O.BIN_MUL, [1, 4], [2], [3, 2], [2]).tolist() == [3, 8]
+    assert O.binary(O.BIN_SUB, [1, 4], [2], [3, 2], [2]).tolist() == [-2, 2]
+    d = O.binary(O.BIN_DIV, [1, 4], [2], [3, 2], [2])
+    assert abs(d[0] - 1 / 3) < 1e-6 and d[1] == 2.0
+    # add_inplace_broadcast_bias (:627-632)
+    assert O.binary(O.BIN_ADD, [1, 2, 3, 4, 5, 6], [2, 3], [10, 20], [2, 1]).tolist() == [11, 12, 13, 24, 25, 26]
+    assert O.broadcast_shape([3], [4]) is None  # binary_incompatible_broadcast_errors
+
+
+def test_runtime_pool_batchnorm_transpose_concat_kats():
+    assert O.max_pool2d(np.arange(16, dtype=np.float32), 1, 1, 4, 4, (2, 2), (2, 2), (0, 0)).tolist() == \
+        [5, 7, 13, 15]
+    g = O.average_pool2d([1, 2, 3, 6], 1, 1, 2, 2, (2, 2), (1, 1), (0, 0))
+    assert abs(g[0] - 3.0) < 1e-6
+    # batch_norm_channel_mode (kernels.rs:676-695)
+    y = O.batch_norm([1, 2, 3, 4], [1, 2, 1, 2], [2, 1], [0, 10], [1, 3], [1, 1], 0.0)
+    assert y.tolist() == [0, 2, 10, 11]
+    # transpose_swaps_axes (:706-711)
+    assert O.transpose([1, 2, 3, 4, 5, 6], [2, 3], [1, 0]).tolist() == [1, 4, 2, 5, 3, 6]
+    # concat_streams_operands (:718-727): two [1,1,2] on axis 1
+    out, od = O.concat([[1, 2], [3, 4]], [[1, 1, 2], [1, 1, 2]], 1)
+    assert out.tolist() == [1, 2, 3, 4] and od == [1, 2, 2]
+
+
+def test_runtime_dispatch_coverage_graph_kats():
+    # crates/tpt-infer-runtime/src/tests.rs:209-260 (dispatch_operator_coverage),
+    # replayed through the oracle's graph executor
+    from oracle import graph_exec
+    from tpt_infer_b200 import lowering as L
+
+    g = L.ComputationGraph()
+    x = g.add_input([1, 1, 4, 4], "x")
+    mp = g.add_node(L.Operator.max_pool2d([2, 2], [2, 2], [0, 0]), [x], [1, 1, 2, 2])
+    cat = g.add_node(L.Operator.concat(1), [mp, mp], [1, 2, 2, 2])
+    flat = g.add_node(L.Operator.flatten(1), [cat], [1, 8])
+    tr = g.add_node(L.Operator.transpose([0, 1, 3, 2]), [mp], [1, 1, 2, 2])
+    outs = [flat, tr]
+    for k in ("sub", "mul", "div", "sigmoid", "gelu"):
+        op = getattr(L.Operator, k)()
+        ins = [mp, mp] if k in ("sub", "mul", "div") else [mp]
+        outs.append(g.add_node(op, ins, [1, 1, 2, 2]))
+    for o in outs:
+        g.mark_output(o)
+    r = graph_exec.execute_graph(g, [np.arange(16, dtype=np.float32)])
+    assert r[0].ravel().tolist() == [5, 7, 13, 15, 5, 7, 13, 15]
+    assert r[1].ravel().tolist() == [5, 13, 7, 15]
+    assert r[2].ravel().tolist() == [0, 0, 0, 0]
+    mpv = np.array([5, 7, 13, 15], np.float32)
+    assert np.all(np.abs(r[3].ravel() - mpv * mpv) < 1e-4) and np.all(np.abs(r[4].ravel() - 1) < 1e-5)
+    assert np.all((r[5] >= 0) & (r[5] <= 1)) and np.all(np.isfinite(r[6]))
+
+
+def test_runtime_conv_bias_kat():
+    # tests.rs:294-322 (conv_bias_is_added): 3x3 input of ones * [[1,0],[0,-1]] + bias 1 = ones
+    from oracle import graph_exec
+    from tpt_infer_b200 import lowering as L
+
+    g = L.ComputationGraph()
+    x = g.add_input([1, 1, 3, 3], "x")
+    w = g.add_weight("w", [1, 1, 2, 2], [1.0, 0.0, 0.0, -1.0])
+    b = g.add_weight("b", [1], [1.0])
+    y = g.add_node(L.Operator.conv2d([1, 1], [0, 0]), [x, w, b], [1, 1, 2, 2])
+    g.mark_output(y)
+    assert graph_exec.execute_graph(g, [np.ones(9, np.float32)])[0].ravel().tolist() == [1, 1, 1, 1]

@@ -33,6 +33,7 @@ F32, I8 = 0, 1
 OP_QUANTIZE, OP_LINEAR, OP_MATMUL, OP_BIAS_ACT, OP_ADD_ACT, OP_SOFTMAX, OP_LAYERNORM, OP_ATTENTION = range(1, 9)
 OP_NCHW_Q8, OP_IM2COL, OP_MAXPOOL, OP_GAP = 9, 10, 11, 12
 OP_ALLGATHER, OP_PANELS_TO_ROWS, OP_GEMM = 13, 14, 15
+OP_BINARY, OP_UNARY, OP_POOL_NCHW, OP_BATCHNORM, OP_TRANSPOSE, OP_CONCAT, OP_CONV2D, OP_BATCHED_MATMUL = range(16, 24)
 
 
 class Plan:
