@@ -1,0 +1,113 @@
+"""ONNX loader and writer (tpt_infer_b200/onnx.py), on the CPU.
+
+- The reference's own committed fixtures, when the reference tree is present:
+  the structural assertions of crates/tpt-infer-onnx/tests/
+  real_model_fixtures.rs:16-60 and :185-230, and an execution through the
+  oracle's graph walk (finite outputs of the declared shape).
+- Writer -> loader round trips of generated graphs reproduce the graph and its
+  oracle outputs bit for bit.
+- Malformed bytes raise OnnxError (load.rs decode / invalid-model errors).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import graph_exec
+
+FIX = "/root/reference/crates/tpt-infer-onnx/tests/fixtures"
+
+
+def _kinds(g, kind):
+    return sum(1 for n in g.nodes if n.op.kind == kind)
+
+
+@pytest.mark.skipif(not os.path.isdir(FIX), reason="reference fixtures not present")
+def test_reference_mobilenet_fixture():
+    from tpt_infer_b200 import onnx
+
+    g = onnx.load(os.path.join(FIX, "mobilenet_v2_style.onnx"))
+    assert len(g.nodes) >= 20
+    assert len(g.initializers) == 12
+    assert _kinds(g, "Input") == 1 + 12
+    x = [n for n in g.nodes if n.name == "x"]
+    assert x and x[0].dims == (1, 3, 16, 16)
+    assert len(g.outputs) == 1 and g.nodes[g.outputs[0]].dims == (1, 10)
+    for k in ("Conv2d", "BatchNorm", "Relu", "Add", "AveragePool2d", "MatMul"):
+        assert _kinds(g, k) >= 1, k
+    out = graph_exec.execute_graph(g, [np.linspace(-1, 1, 3 * 16 * 16, dtype=np.float32)])[0]
+    assert out.shape == (1, 10) and np.all(np.isfinite(out))
+
+
+@pytest.mark.skipif(not os.path.isdir(FIX), reason="reference fixtures not present")
+def test_reference_bert_tiny_fixture():
+    from tpt_infer_b200 import onnx
+
+    g = onnx.load(os.path.join(FIX, "bert_tiny_style.onnx"))
+    assert len(g.nodes) >= 15
+    assert len(g.initializers) == 10
+    x = [n for n in g.nodes if n.name == "x"]
+    assert x and x[0].dims == (1, 8)
+    assert len(g.outputs) == 1 and g.nodes[g.outputs[0]].dims == (1, 8)
+    assert _kinds(g, "MatMul") >= 5 and _kinds(g, "Add") >= 4
+    assert _kinds(g, "Softmax") == 1 and _kinds(g, "BatchNorm") == 1 and _kinds(g, "Relu") == 1
+    out = graph_exec.execute_graph(g, [np.linspace(-1, 1, 8, dtype=np.float32)])[0]
+    assert out.shape == (1, 8) and np.all(np.isfinite(out))
+
+
+def _sample_graph(L):
+    r = np.random.default_rng(3)
+    g = L.ComputationGraph()
+    x = g.add_input([2, 4, 8, 8], "img")
+    c = g.add_node(L.Operator.conv2d([2, 2], [1, 1]), [x, g.add_weight("w", [6, 4, 3, 3], r.normal(0, .2, 216)),
+                                                       g.add_weight("b", [1, 6, 1, 1], r.normal(0, .1, 6))],
+                   [2, 6, 4, 4])
+    bn = g.add_node(L.Operator.batch_norm(1e-4), [c] + [g.add_weight(f"p{i}", [6], v) for i, v in enumerate(
+        (r.normal(1, .1, 6), r.normal(0, .1, 6), r.normal(0, .1, 6), r.uniform(.5, 1.5, 6)))], [2, 6, 4, 4])
+    rl = g.add_node(L.Operator.relu(), [bn], [2, 6, 4, 4])
+    mp = g.add_node(L.Operator.max_pool2d([2, 2], [2, 2], [0, 0]), [rl], [2, 6, 2, 2])
+    tr = g.add_node(L.Operator.transpose([0, 2, 3, 1]), [mp], [2, 2, 2, 6])
+    rs = g.add_node(L.Operator.reshape([2, 24]), [tr], [2, 24])
+    gm = g.add_node(L.Operator.gemm(1.5, 0.5, False, True), [rs, g.add_weight("gw", [5, 24], r.normal(0, .2, 120)),
+                                                             g.add_weight("gc", [5], r.normal(0, 1, 5))], [2, 5])
+    ln = g.add_node(L.Operator.layer_norm(1e-5), [gm, g.add_weight("lg", [5], np.ones(5)),
+                                                  g.add_weight("lb", [5], np.zeros(5))], [2, 5])
+    sm = g.add_node(L.Operator.softmax(-1), [ln], [2, 5])
+    g.mark_output(sm)
+    g.mark_output(mp)
+    return g
+
+
+def test_writer_loader_round_trip():
+    from tpt_infer_b200 import lowering as L
+    from tpt_infer_b200 import onnx
+
+    g = _sample_graph(L)
+    g2 = onnx.load_from_bytes(onnx.save_bytes(g))
+    assert [n.op.kind for n in g2.nodes if n.op.kind != "Input"] == \
+        [n.op.kind for n in g.nodes if n.op.kind != "Input"]
+    assert set(g2.initializers) >= set(g.initializers)
+    for name, init in g.initializers.items():
+        assert np.array_equal(g2.initializers[name].data, init.data)
+    for a, b in zip([n for n in g.nodes if n.op.kind != "Input"], [n for n in g2.nodes if n.op.kind != "Input"]):
+        assert a.dims == b.dims
+        for k, v in a.op.attrs.items():
+            assert b.op.attrs[k] == pytest.approx(v) if isinstance(v, float) else tuple(np.ravel(b.op.attrs[k])) == \
+                tuple(np.ravel(v)), (a.op.kind, k)
+    x = np.random.default_rng(4).normal(0, 1, 2 * 4 * 8 * 8).astype(np.float32)
+    for u, v in zip(graph_exec.execute_graph(g, [x]), graph_exec.execute_graph(g2, [x])):
+        assert np.array_equal(u, v)
+
+
+def test_loader_rejects_malformed_bytes():
+    from tpt_infer_b200 import onnx
+
+    with pytest.raises(onnx.OnnxError):
+        onnx.load_from_bytes(b"\x3a\xff\xff")  # truncated length-delimited graph field
+    with pytest.raises(onnx.OnnxError):
+        onnx.load_from_bytes(b"\x08\x08")  # a model with no graph
+    with pytest.raises(onnx.OnnxError):  # opset beyond the supported version (load.rs:168-175)
+        from tpt_infer_b200 import lowering as L
+
+        good = onnx.save_bytes(_sample_graph(L))
+        onnx.load_from_bytes(good[:-1] + bytes([99]))

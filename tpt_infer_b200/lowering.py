@@ -39,6 +39,10 @@ from .backend import OpError
 
 SIZE_MISMATCH, SHAPE_MISMATCH, UNSUPPORTED, INVALID = 1, 2, 3, 4
 MAX_RANK = 8  # crates/tpt-infer-core/src/shape.rs:4
+# Operator kinds with a CUDA lowering (everything else raises UnsupportedOp)
+SUPPORTED = frozenset({"Input", "MatMul", "Conv2d", "Add", "Sub", "Mul", "Div", "Relu", "Sigmoid", "Gelu", "Softmax",
+                       "Reshape", "Flatten", "MaxPool2d", "AveragePool2d", "BatchNorm", "Concat", "Transpose",
+                       "LayerNorm", "Gemm"})
 
 
 class UnsupportedOp(OpError):
