@@ -138,18 +138,10 @@ def resnet18(x_nchw, spec, batch, scales=None, calib=None):
 
 # ------------------------------------------------------------------ BERT-shaped encoder
 def _attention(qkv, batch, seq, heads, d, scale):
-    hid = heads * d
-    qkv = qkv.reshape(batch, seq, 3 * hid)
-    out = np.empty((batch, seq, hid), np.float32)
-    for b in range(batch):
-        for h in range(heads):
-            q = np.ascontiguousarray(qkv[b, :, h * d:(h + 1) * d] * np.float32(scale))
-            k = np.ascontiguousarray(qkv[b, :, hid + h * d:hid + (h + 1) * d].T)
-            v = np.ascontiguousarray(qkv[b, :, 2 * hid + h * d:2 * hid + (h + 1) * d])
-            s = O.matmul(q, (seq, d), k, (d, seq))
-            p = O.softmax(s, seq)
-            out[b, :, h * d:(h + 1) * d] = O.matmul(p, (seq, seq), v, (seq, d)).reshape(seq, d)
-    return out.reshape(batch * seq, hid)
+    """The plan's fused attention, in the device's evaluation order
+    (tpto_attention_det; D = 64)."""
+    assert d == 64
+    return O.attention_det(qkv, batch, seq, heads, scale).reshape(batch * seq, heads * d)
 
 
 def bert(x, layers_w, batch, seq, scales=None, calib=None, heads=12, hidden=768, ffn=3072, eps=1e-5):

@@ -111,6 +111,10 @@ _sig("tpto_average_pool2d", None, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz,
 _sig("tpto_add_bias_nchw", None, _f32p, _sz, _sz, _sz, _f32p)
 _sig("tpto_add_bias_rows", None, _f32p, _sz, _sz, _f32p)
 _sig("tpto_layernorm", None, _f32p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
+_sig("tpto_gelu_det_array", None, _f32p, _sz, _f32p)
+_sig("tpto_exp_det_array", None, _f32p, _sz, _f32p)
+_sig("tpto_attention_det", None, _f32p, _sz, _sz, _sz, C.c_float, _f32p, _sz, _sz)
+_sig("tpto_layernorm_res", None, _f32p, C.c_void_p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
 _sig("tpto_binary", None, C.c_int, _f32p, _szp, _sz, _f32p, _szp, _sz, _f32p, _szp, _sz)
 _sig("tpto_batch_norm", None, _f32p, _sz, _f32p, _f32p, _f32p, _f32p, _sz, _sz, C.c_float, _f32p)
 _sig("tpto_transpose", None, _f32p, _szp, _sz, _szp, _f32p)
@@ -503,3 +507,39 @@ def concat(inputs, dims_list, axis):
         _lib.tpto_concat_copy_one(out, od[ax], off, d[ax], inner, x, x.size)
         off += d[ax]
     return out, od
+
+
+def gelu_det(a):
+    """The device's deterministic GELU (det_math.cuh), bit-exact restatement."""
+    a = _f32(a).ravel()
+    out = np.empty(a.size, np.float32)
+    _lib.tpto_gelu_det_array(a, a.size, out)
+    return out
+
+
+def exp_det(a):
+    """The device's deterministic exp (det_math.cuh), bit-exact restatement."""
+    a = _f32(a).ravel()
+    out = np.empty(a.size, np.float32)
+    _lib.tpto_exp_det_array(a, a.size, out)
+    return out
+
+
+def attention_det(qkv, batch, seq, heads, scale, b0=0, b1=None):
+    """The device's fused attention (attention_det.cu order), bit-exact; rows of
+    batches [b0, b1) are filled (the rest of the output stays zero)."""
+    qkv = _f32(qkv).ravel()
+    b1 = batch if b1 is None else b1
+    out = np.zeros(batch * seq * heads * 64, np.float32)
+    _lib.tpto_attention_det(qkv, batch, seq, heads, scale, out, b0, b1)
+    return out
+
+
+def layernorm_res(x, res, rows, cols, gamma, beta, eps=1e-5):
+    """LayerNorm(x + res) in the device order (the fused residual layernorm)."""
+    x = _f32(x).ravel()
+    r = _f32(res).ravel()
+    y = np.empty(rows * cols, np.float32)
+    _lib.tpto_layernorm_res(x, r.ctypes.data_as(C.c_void_p), rows, cols, _f32(gamma).ravel(), _f32(beta).ravel(),
+                            eps, y)
+    return y

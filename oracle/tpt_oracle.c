@@ -10,6 +10,7 @@
 #include <float.h>
 #include <math.h>
 #include <string.h>
+#include <stdlib.h>
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -286,6 +287,56 @@ static float gelu1(float x) {
     return 0.5f * x * (1.0f + tanhf(inner));
 }
 
+/* The device's deterministic exp / reciprocal / GELU (tpt_infer_b200/csrc/
+ * det_math.cuh), restated with the same correctly rounded operations in the
+ * same order: Cody-Waite reduction + degree-7 Taylor polynomial for exp,
+ * three Newton steps from 48/17 - 32/17 h for 1/d on [1, 2], and
+ * GELU = x w / (1 + t) with t = exp(-2 |inner|). Used by the W8A8 epilogue's
+ * GELU and the attention softmax, which this backend defines. */
+float tpto_exp_det(float x) {
+    if (!(x >= -87.0f)) return x != x ? x : 0.0f;
+    if (x > 88.0f) return INFINITY;
+    const float n = rintf(x * 1.44269504f);
+    float r = fmaf(n, -0.693145751953125f, x);
+    r = fmaf(n, -1.42860676533018720e-06f, r);
+    float p = 0.000198412701f;
+    p = fmaf(p, r, 0.00138888892f);
+    p = fmaf(p, r, 0.00833333377f);
+    p = fmaf(p, r, 0.0416666679f);
+    p = fmaf(p, r, 0.166666672f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    uint32_t eb = (uint32_t)((int)n + 127) << 23;
+    float sc;
+    memcpy(&sc, &eb, 4);
+    return p * sc;
+}
+
+static float recip12_det(float d) {
+    const float h = d * 0.5f;
+    float r = fmaf(h, -1.88235295f, 2.82352948f);
+    for (int i = 0; i < 3; i++) r = fmaf(r, fmaf(-h, r, 1.0f), r);
+    return r * 0.5f;
+}
+
+float tpto_gelu_det(float x) {
+    const float K = 0.7978846f, C = 0.044715f;
+    const float cx = ((C * x) * x) * x;
+    const float inner = K * (x + cx);
+    const float t = tpto_exp_det(-2.0f * fabsf(inner));
+    const float w = inner >= 0.0f ? 1.0f : t;
+    return (x * w) * recip12_det(1.0f + t);
+}
+
+void tpto_gelu_det_array(const float *a, size_t n, float *out) {
+    for (size_t i = 0; i < n; i++) out[i] = tpto_gelu_det(a[i]);
+}
+
+void tpto_exp_det_array(const float *a, size_t n, float *out) {
+    for (size_t i = 0; i < n; i++) out[i] = tpto_exp_det(a[i]);
+}
+
 int tpto_gelu(const float *a, size_t a_len, float *out, size_t out_len) {
     if (out_len != a_len) return size_mismatch(a_len, out_len);
     for (size_t i = 0; i < a_len; i++) out[i] = gelu1(a[i]);
@@ -500,9 +551,18 @@ void tpto_i8_gemm_acc(const int8_t *a, const int8_t *wt, size_t m, size_t n, siz
         }
 }
 
-static float apply_act(float y, int act) {
+/* The reference's activation nodes (naive.rs:95-101, :137-146): the W4 path's
+ * semantics is dequant -> f32 MatMul -> bias add -> the activation node. */
+static float apply_act_ref(float y, int act) {
     if (act == TPTO_ACT_RELU) return y > 0.0f ? y : 0.0f;
     if (act == TPTO_ACT_GELU) return gelu1(y);
+    return y;
+}
+
+/* The W8A8 epilogue's activation: ReLU, or this backend's deterministic GELU. */
+static float apply_act(float y, int act) {
+    if (act == TPTO_ACT_RELU) return y > 0.0f ? y : 0.0f;
+    if (act == TPTO_ACT_GELU) return tpto_gelu_det(y);  /* the device epilogue's GELU */
     return y;
 }
 
@@ -576,7 +636,7 @@ void tpto_w4_gemm(const float *x, const uint8_t *wt_packed, const float *w_scale
                 acc = acc + xr[kk] * w;
             }
             if (bias) acc = acc + bias[j];
-            y[i * n + j] = apply_act(acc, act);
+            y[i * n + j] = apply_act_ref(acc, act);
         }
 }
 
@@ -644,25 +704,75 @@ void tpto_add_bias_rows(float *out, size_t rows, size_t cols, const float *bias)
         for (size_t j = 0; j < cols; j++) out[r * cols + j] += bias[j];
 }
 
-/* LayerNormalization (ONNX, axis = -1), which the reference runtime lacks
- * (ONNX LayerNormalization maps to Custom in crates/tpt-infer-onnx/src/registry.rs:62):
- * mean = sum(x)/C, var = sum((x-mean)^2)/C (biased), y = (x-mean)/sqrt(var+eps)*g + b,
- * all f32 with sequential sums. */
-void tpto_layernorm(const float *x, size_t rows, size_t cols, const float *gamma,
-                    const float *beta, float eps, float *y) {
+/* LayerNorm as this backend defines it (the reference has none:
+ * crates/tpt-infer-onnx/src/registry.rs:62 maps LayerNormalization to Custom):
+ * ONNX semantics over the last axis, biased variance, evaluated in the device
+ * kernels' order (tpt_infer_b200/csrc/model_ops.cu k_layernorm / k_layernorm4):
+ * 32 lanes, lane l owning columns l + 32 i (cols != 768) or the float4 groups
+ * 4 (l + 32 i) .. +3 (cols == 768); sequential partial sums per lane, a xor
+ * butterfly (o = 16, 8, 4, 2, 1) across lanes, mean = s / cols, variance by
+ * fmaf(d, d, q) in the same order, inv = 1 / sqrtf(var + eps),
+ * y = fmaf((x - mean) * inv, gamma, beta). res (may be NULL) is added first. */
+static float ln_butterfly(float p[32]) {
+    float t[32];
+    for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; l++) t[l] = p[l] + p[l ^ o];
+        memcpy(p, t, sizeof t);
+    }
+    return p[0];
+}
+
+void tpto_layernorm_res(const float *x, const float *res, size_t rows, size_t cols, const float *gamma,
+                        const float *beta, float eps, float *y) {
+    const int vec4 = cols == 768;
+    float *v = malloc(cols * sizeof(float));
     for (size_t r = 0; r < rows; r++) {
         const float *xr = x + r * cols;
-        float s = 0.0f;
-        for (size_t j = 0; j < cols; j++) s += xr[j];
-        float mean = s / (float)cols;
-        float v = 0.0f;
-        for (size_t j = 0; j < cols; j++) {
-            float d = xr[j] - mean;
-            v += d * d;
+        for (size_t c = 0; c < cols; c++) v[c] = res ? xr[c] + res[r * cols + c] : xr[c];
+        float p[32], q[32];
+        for (int l = 0; l < 32; l++) {
+            float s = 0.0f;
+            if (vec4) {
+                for (size_t gi = (size_t)l; gi < cols / 4; gi += 32) {
+                    const float *e = v + 4 * gi;
+                    s = s + (((e[0] + e[1]) + e[2]) + e[3]);
+                }
+            } else {
+                for (size_t i = 0; i < 32; i++) {
+                    size_t c = (size_t)l + 32 * i;
+                    s = s + (c < cols ? v[c] : 0.0f);
+                }
+            }
+            p[l] = s;
         }
-        float inv = 1.0f / sqrtf(v / (float)cols + eps);
-        for (size_t j = 0; j < cols; j++) y[r * cols + j] = (xr[j] - mean) * inv * gamma[j] + beta[j];
+        const float mean = ln_butterfly(p) / (float)cols;
+        for (int l = 0; l < 32; l++) {
+            float a = 0.0f;
+            if (vec4) {
+                for (size_t gi = (size_t)l; gi < cols / 4; gi += 32)
+                    for (int j = 0; j < 4; j++) {
+                        float d = v[4 * gi + j] - mean;
+                        a = fmaf(d, d, a);
+                    }
+            } else {
+                for (size_t i = 0; i < 32; i++) {
+                    size_t c = (size_t)l + 32 * i;
+                    float d = c < cols ? v[c] - mean : 0.0f;
+                    a = fmaf(d, d, a);
+                }
+            }
+            q[l] = a;
+        }
+        const float var = ln_butterfly(q) / (float)cols;
+        const float inv = 1.0f / sqrtf(var + eps);
+        for (size_t c = 0; c < cols; c++) y[r * cols + c] = fmaf((v[c] - mean) * inv, gamma[c], beta[c]);
     }
+    free(v);
+}
+
+void tpto_layernorm(const float *x, size_t rows, size_t cols, const float *gamma, const float *beta, float eps,
+                    float *y) {
+    tpto_layernorm_res(x, NULL, rows, cols, gamma, beta, eps, y);
 }
 
 /* ------------------------------------------------------------------ */
@@ -758,4 +868,60 @@ void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_
                           size_t src_len) {
     size_t sb = c_src * inner, ob = c_total * inner, outer = src_len / sb;
     for (size_t o = 0; o < outer; o++) memcpy(out + o * ob + c_offset * inner, src + o * sb, sb * 4);
+}
+
+/* The fused attention of the encoder plans as this backend defines it
+ * (tpt_infer_b200/csrc/attention_det.cu; the reference has no attention
+ * operator): per (batch, head), q' = q * scale; s_c = fmaf over d in order;
+ * m = max over the S keys; e_c = exp_det(s_c - m) (0 for the padding slots
+ * c >= S up to 128); the 128 slots summed per t = c mod 16 in increasing
+ * c / 16, the 16 partials combined by the xor butterfly (o = 8, 4, 2, 1);
+ * p_c = e_c * (1 / sum); o_d = fmaf over the 128 slots in order (padding
+ * p = 0, v = 0). qkv [B*S, 3*H*D], out [B*S, H*D], D = 64, S <= 128. Rows of
+ * the batch range [b0, b1) only. */
+void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
+                        size_t b1) {
+    (void)B;
+    const size_t D = 64, ld = 3 * H * D;
+    float q[64], sc[128], p[128];
+#pragma omp parallel for collapse(2) private(q, sc, p) schedule(static)
+    for (size_t b = b0; b < b1; b++)
+        for (size_t h = 0; h < H; h++) {
+            const float *base = qkv + b * S * ld + h * D;
+            for (size_t r = 0; r < S; r++) {
+                for (size_t d = 0; d < D; d++) q[d] = base[r * ld + d] * scale;
+                float m = -INFINITY;
+                for (size_t c = 0; c < 128; c++) {
+                    float a = 0.0f;
+                    if (c < S)
+                        for (size_t d = 0; d < D; d++) a = fmaf(q[d], base[c * ld + H * D + d], a);
+                    sc[c] = a;
+                    if (c < S) m = fmaxf(m, a);
+                }
+                float part[16];
+                for (int t = 0; t < 16; t++) {
+                    float acc = 0.0f;
+                    for (int j = 0; j < 8; j++) {
+                        size_t c = (size_t)t + 16 * (size_t)j;
+                        float e = c < S ? tpto_exp_det(sc[c] - m) : 0.0f;
+                        sc[c] = e;
+                        acc = acc + e;
+                    }
+                    part[t] = acc;
+                }
+                for (int o = 8; o > 0; o >>= 1) {
+                    float tmp[16];
+                    for (int t = 0; t < 16; t++) tmp[t] = part[t] + part[t ^ o];
+                    memcpy(part, tmp, sizeof tmp);
+                }
+                const float inv = 1.0f / part[0];
+                for (size_t c = 0; c < 128; c++) p[c] = sc[c] * inv;
+                float *orow = out + (b * S + r) * H * D + h * D;
+                for (size_t d = 0; d < D; d++) {
+                    float a = 0.0f;
+                    for (size_t c = 0; c < 128; c++) a = fmaf(p[c], c < S ? base[c * ld + 2 * H * D + d] : 0.0f, a);
+                    orow[d] = a;
+                }
+            }
+        }
 }

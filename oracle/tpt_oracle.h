@@ -140,6 +140,18 @@ void tpto_transpose(const float *x, const size_t *xd, size_t rank, const size_t 
 void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_src, size_t inner, const float *src,
                           size_t src_len);
 
+/* deterministic exp / GELU of the device (det_math.cuh) */
+float tpto_exp_det(float x);
+float tpto_gelu_det(float x);
+void tpto_gelu_det_array(const float *a, size_t n, float *out);
+void tpto_exp_det_array(const float *a, size_t n, float *out);
+
+void tpto_layernorm_res(const float *x, const float *res, size_t rows, size_t cols, const float *gamma,
+                        const float *beta, float eps, float *y);
+
+void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
+                        size_t b1);
+
 #ifdef __cplusplus
 }
 #endif

@@ -424,3 +424,16 @@ def test_runtime_conv_bias_kat():
     y = g.add_node(L.Operator.conv2d([1, 1], [0, 0]), [x, w, b], [1, 1, 2, 2])
     g.mark_output(y)
     assert graph_exec.execute_graph(g, [np.ones(9, np.float32)])[0].ravel().tolist() == [1, 1, 1, 1]
+
+
+def test_deterministic_exp_and_gelu_accuracy():
+    # det_math.cuh restated: exp_det within 2 ulp of e^x on [-87, 88], 0 below,
+    # NaN kept; gelu_det within 1e-6 (1 + |y|) of the reference tanh formula
+    x = np.linspace(-87, 88, 400001).astype(np.float32)
+    e = O.exp_det(x)
+    ref = np.exp(x.astype(np.float64))
+    assert np.max(np.abs(e - ref) / ref) < 2 * 2.0 ** -24
+    assert O.exp_det([-87.5, -1000.0])[0] == 0.0 and np.isnan(O.exp_det([np.nan])[0])
+    g = O.normal(200001, 5, 0.0, 4.0)
+    assert np.max(np.abs(O.gelu_det(g) - O.gelu(g)) / (1 + np.abs(O.gelu(g)))) < 1e-6
+    assert O.gelu_det([0.0])[0] == 0.0 and np.isnan(O.gelu_det([np.nan])[0])

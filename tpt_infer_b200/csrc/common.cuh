@@ -8,6 +8,7 @@
 #include <string>
 
 #include "../../include/tpt_cuda.h"
+#include "det_math.cuh"
 
 // Device-side error words (one 32-bit word each), written by kernels whose
 // bounded waits ran out or whose own index checks failed. Read and cleared by
@@ -204,19 +205,12 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// GELU of crates/tpt-infer-ops/src/naive.rs:137-146, evaluated with explicit
-// round-to-nearest multiplies/adds in the reference's association order
-// (nvcc would otherwise contract them into FMAs).
-__device__ __forceinline__ float gelu_ref(float x) {
-    const float K = 0.7978846f, Cc = 0.044715f;
-    float cx = __fmul_rn(__fmul_rn(__fmul_rn(Cc, x), x), x);
-    float inner = __fmul_rn(K, __fadd_rn(x, cx));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-
+// GELU of crates/tpt-infer-ops/src/naive.rs:137-146 (tanh approximation),
+// evaluated by gelu_det (det_math.cuh): the same inner term, the tanh through
+// exp_det, so every GELU on the device has a bit-exact CPU restatement.
 __device__ __forceinline__ float apply_act(float y, int act) {
     if (act == TPT_ACT_RELU) return y > 0.0f ? y : 0.0f;
-    if (act == TPT_ACT_GELU) return gelu_ref(y);
+    if (act == TPT_ACT_GELU) return gelu_det(y);
     return y;
 }
 
@@ -242,7 +236,7 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 template <int ACT>
 __device__ __forceinline__ float act_t(float y) {
     if constexpr (ACT == TPT_ACT_RELU) return y > 0.0f ? y : 0.0f;
-    else if constexpr (ACT == TPT_ACT_GELU) return gelu_ref(y);
+    else if constexpr (ACT == TPT_ACT_GELU) return gelu_det(y);
     else return y;
 }
 
@@ -287,7 +281,7 @@ __device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, flo
 }
 // The activation of 32 values (f32 bits) in place, for epilogues that keep
 // their code small: ReLU as a select, GELU through an out-of-line call.
-static __device__ __noinline__ float gelu_outline(float y) { return gelu_ref(y); }
+static __device__ __noinline__ float gelu_outline(float y) { return gelu_det(y); }
 __device__ __forceinline__ void act32(uint32_t (&v)[32], int act) {
     if (act == TPT_ACT_RELU) {
 #pragma unroll

@@ -1,0 +1,72 @@
+// det_math.cuh -- exp, reciprocal and GELU built only from correctly rounded
+// IEEE operations (fmaf, multiply, add, rint, exact scaling by a power of two),
+// so a C restatement with the same operations in the same order gives the
+// same bits on the CPU. The model paths that must match a CPU replay bit for
+// bit use these instead of library transcendentals: the attention softmax and
+// every GELU epilogue.
+//
+// exp_det(x): Cody-Waite range reduction (W. J. Cody and W. Waite, "Software
+// Manual for the Elementary Functions", 1980): n = rint(x log2 e),
+// r = x - n ln2 with ln2 split into a 12-bit head (n * head is exact for
+// |n| < 2^12) and a tail, then the degree-7 Taylor polynomial of e^r on
+// |r| <= ln2/2 (truncation error < 6e-9 relative) by Horner's rule with fmaf,
+// scaled by 2^n through the exponent bits. Within 2 ulp of e^x for
+// x in [-87, 88]; 0 below -87 (the softmax terms there are < 2^-125 of the
+// row's largest), +inf above 88, NaN propagates.
+//
+// recip12_det(d): 1/d for d in [1, 2] by Newton-Raphson on h = d/2 in [0.5, 1]
+// from the linear start 48/17 - 32/17 h (maximum relative error 1/17), three
+// steps (error < 2e-10 before the last rounding), halved at the end. Not
+// correctly rounded, but deterministic.
+//
+// gelu_det(x): the tanh form of naive.rs:137-146, inner = K (x + C x x x) with
+// the same association, and 0.5 x (1 + tanh(inner)) written without tanh: with
+// t = exp(-2 |inner|), 1 + tanh(inner) = 2 / (1 + t) when inner >= 0 and
+// 2 t / (1 + t) otherwise, so gelu = (x w) / (1 + t) with w = 1 or t. This
+// avoids the cancellation in 1 + tanh for negative inputs and agrees with the
+// tanh form to within a few ulp of its largest term.
+#pragma once
+
+namespace tpt {
+
+constexpr float DET_LOG2E = 1.44269504f;
+constexpr float DET_LN2_HI = 0.693145751953125f;      // 12 significant bits
+constexpr float DET_LN2_LO = 1.42860676533018720e-06f;
+constexpr float DET_C2 = 0.5f, DET_C3 = 0.166666672f, DET_C4 = 0.0416666679f, DET_C5 = 0.00833333377f,
+                DET_C6 = 0.00138888892f, DET_C7 = 0.000198412701f;  // 1/k!
+
+__device__ __forceinline__ float exp_det(float x) {
+    if (!(x >= -87.0f)) return x != x ? x : 0.0f;
+    if (x > 88.0f) return __int_as_float(0x7f800000);
+    const float n = rintf(__fmul_rn(x, DET_LOG2E));
+    float r = __fmaf_rn(n, -DET_LN2_HI, x);
+    r = __fmaf_rn(n, -DET_LN2_LO, r);
+    float p = DET_C7;
+    p = __fmaf_rn(p, r, DET_C6);
+    p = __fmaf_rn(p, r, DET_C5);
+    p = __fmaf_rn(p, r, DET_C4);
+    p = __fmaf_rn(p, r, DET_C3);
+    p = __fmaf_rn(p, r, DET_C2);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+}
+
+__device__ __forceinline__ float recip12_det(float d) {
+    const float h = __fmul_rn(d, 0.5f);
+    float r = __fmaf_rn(h, -1.88235295f, 2.82352948f);  // 48/17 - 32/17 h
+#pragma unroll
+    for (int i = 0; i < 3; i++) r = __fmaf_rn(r, __fmaf_rn(-h, r, 1.0f), r);
+    return __fmul_rn(r, 0.5f);
+}
+
+__device__ __forceinline__ float gelu_det(float x) {
+    const float K = 0.7978846f, Cc = 0.044715f;
+    const float cx = __fmul_rn(__fmul_rn(__fmul_rn(Cc, x), x), x);
+    const float inner = __fmul_rn(K, __fadd_rn(x, cx));
+    const float t = exp_det(__fmul_rn(-2.0f, fabsf(inner)));
+    const float w = inner >= 0.0f ? 1.0f : t;
+    return __fmul_rn(__fmul_rn(x, w), recip12_det(__fadd_rn(1.0f, t)));
+}
+
+}  // namespace tpt

@@ -10,7 +10,7 @@ namespace {
 __device__ __forceinline__ float unary_op(int op, float x) {
     if (op == 1) return x > 0.0f ? x : 0.0f;                       // naive.rs:95-101
     if (op == 2) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));  // naive.rs:128-134
-    return gelu_ref(x);                                              // naive.rs:137-146
+    return gelu_det(x);                                              // naive.rs:137-146 (det_math.cuh)
 }
 
 __global__ void k_add_vec(const float4 *__restrict__ a, const float4 *__restrict__ b,

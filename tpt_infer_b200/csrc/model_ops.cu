@@ -20,7 +20,24 @@ namespace {
 // crates/tpt-infer-onnx/src/registry.rs:62 maps it to Custom): mean, biased
 // variance, y = (x - mean) / sqrt(var + eps) * gamma + beta. One warp per row,
 // the row held in registers (cols <= 32 * LN_MAX).
+//
+// The evaluation order is fixed, every operation explicitly rounded, so a CPU
+// restatement reproduces the bits:
+//   lane l holds columns c = l + 32 i (k_layernorm) or the float4 groups
+//   4 (l + 32 i) .. +3 (k_layernorm4, 768 columns); x = in (+ residual, one add);
+//   partial sum: s = s + x_c over its columns in increasing i (in k_layernorm4
+//   s = s + (((x0 + x1) + x2) + x3) per group); lanes combined by the xor
+//   butterfly s = s + s[l ^ o], o = 16, 8, 4, 2, 1; mean = s / cols;
+//   partial variance q = fmaf(d, d, q), d = x - mean, in the same order (a
+//   group's four in order), the same butterfly; var = q / cols;
+//   inv = 1 / sqrtf(var + eps); y = fmaf((x - mean) * inv, gamma, beta).
+// Columns past cols contribute +0 to both sums.
 constexpr int LN_MAX = 32;
+__device__ __forceinline__ float ln_butterfly(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
 __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ b,
                             float *__restrict__ y, int rows, int cols, float eps, int8_t *__restrict__ qout, float qs,
                             const float *__restrict__ res) {
@@ -36,24 +53,24 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
 #pragma unroll
         for (int i = 0; i < LN_MAX; i++) {
             const int c = lane + 32 * i;
-            v[i] = c < cols ? (res ? xr[c] + res[(size_t)r * cols + c] : xr[c]) : 0.0f;
-            s += v[i];
+            v[i] = c < cols ? (res ? __fadd_rn(xr[c], res[(size_t)r * cols + c]) : xr[c]) : 0.0f;
+            s = __fadd_rn(s, v[i]);
         }
-        const float mean = __fdiv_rn(warp_sum(s), (float)cols);
+        const float mean = __fdiv_rn(ln_butterfly(s), (float)cols);
         float q = 0.0f;
 #pragma unroll
         for (int i = 0; i < LN_MAX; i++) {
             const int c = lane + 32 * i;
-            const float d = c < cols ? v[i] - mean : 0.0f;
-            q += d * d;
+            const float d = c < cols ? __fsub_rn(v[i], mean) : 0.0f;
+            q = __fmaf_rn(d, d, q);
         }
-        const float var = __fdiv_rn(warp_sum(q), (float)cols);
-        const float inv = __fdiv_rn(1.0f, sqrtf(var + eps));
+        const float var = __fdiv_rn(ln_butterfly(q), (float)cols);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
         for (int i = 0; i < LN_MAX; i++) {
             const int c = lane + 32 * i;
             if (c < cols) {
-                const float o = (v[i] - mean) * inv * __ldg(g + c) + __ldg(b + c);
+                const float o = __fmaf_rn(__fmul_rn(__fsub_rn(v[i], mean), inv), __ldg(g + c), __ldg(b + c));
                 y[(size_t)r * cols + c] = o;
                 if (qout) qout[(size_t)r * cols + c] = requant_i8(o, qs);  // the next QUANTIZE, fused
             }
@@ -61,7 +78,7 @@ __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict
     }
 }
 
-// Same arithmetic, cols % 128 == 0 (each lane owns float4 groups c = 4 (lane + 32 i)):
+// Same definition, cols = 128 G (each lane owns float4 groups 4 (lane + 32 i)):
 // 16-byte loads and stores and a 4-byte store of the int8 copy.
 template <int G>
 __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restrict__ g, const float4 *__restrict__ b,
@@ -83,25 +100,32 @@ __global__ void k_layernorm4(const float4 *__restrict__ x, const float4 *__restr
             v[i] = xr[lane + 32 * i];
             if (res) {  // LayerNorm(x + res): the residual add of the ADD_ACT it replaces, same rounding
                 const float4 z = res[(size_t)r * cols4 + lane + 32 * i];
-                v[i] = make_float4(v[i].x + z.x, v[i].y + z.y, v[i].z + z.z, v[i].w + z.w);
+                v[i] = make_float4(__fadd_rn(v[i].x, z.x), __fadd_rn(v[i].y, z.y), __fadd_rn(v[i].z, z.z),
+                                   __fadd_rn(v[i].w, z.w));
             }
-            s += v[i].x + v[i].y + v[i].z + v[i].w;
+            s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fadd_rn(v[i].x, v[i].y), v[i].z), v[i].w));
         }
-        const float mean = __fdiv_rn(warp_sum(s), n);
+        const float mean = __fdiv_rn(ln_butterfly(s), n);
         float q = 0.0f;
 #pragma unroll
         for (int i = 0; i < G; i++) {
-            const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
-            q += dx * dx + dy * dy + dz * dz + dw * dw;
+            const float dx = __fsub_rn(v[i].x, mean), dy = __fsub_rn(v[i].y, mean), dz = __fsub_rn(v[i].z, mean),
+                        dw = __fsub_rn(v[i].w, mean);
+            q = __fmaf_rn(dx, dx, q);
+            q = __fmaf_rn(dy, dy, q);
+            q = __fmaf_rn(dz, dz, q);
+            q = __fmaf_rn(dw, dw, q);
         }
-        const float var = __fdiv_rn(warp_sum(q), n);
-        const float inv = __fdiv_rn(1.0f, sqrtf(var + eps));
+        const float var = __fdiv_rn(ln_butterfly(q), n);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
         for (int i = 0; i < G; i++) {
             const int c = lane + 32 * i;
             const float4 gg = __ldg(g + c), bb = __ldg(b + c);
-            const float4 o = make_float4((v[i].x - mean) * inv * gg.x + bb.x, (v[i].y - mean) * inv * gg.y + bb.y,
-                                         (v[i].z - mean) * inv * gg.z + bb.z, (v[i].w - mean) * inv * gg.w + bb.w);
+            const float4 o = make_float4(__fmaf_rn(__fmul_rn(__fsub_rn(v[i].x, mean), inv), gg.x, bb.x),
+                                         __fmaf_rn(__fmul_rn(__fsub_rn(v[i].y, mean), inv), gg.y, bb.y),
+                                         __fmaf_rn(__fmul_rn(__fsub_rn(v[i].z, mean), inv), gg.z, bb.z),
+                                         __fmaf_rn(__fmul_rn(__fsub_rn(v[i].w, mean), inv), gg.w, bb.w));
             y[(size_t)r * cols4 + c] = o;
             if (qout)
                 qout[(size_t)r * cols4 + c] = (uint32_t)(uint8_t)requant_i8(o.x, qs) |
@@ -388,12 +412,12 @@ int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const fl
     return after_launch(ctx, "layernorm");
 }
 
-int launch_attention_tc(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
-                        int8_t *q, float qs);
+int launch_attention_det(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                         int8_t *q, float qs);
 
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
                      int8_t *q, float qs) {
-    return launch_attention_tc(ctx, qkv, out, B, S, H, D, scale, q, qs);
+    return launch_attention_det(ctx, qkv, out, B, S, H, D, scale, q, qs);
 }
 
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act) {
