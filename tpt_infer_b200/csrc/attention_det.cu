@@ -62,30 +62,26 @@ __global__ void __launch_bounds__(AD_T, 2) k_attention_det(const float *__restri
     const size_t ld = (size_t)3 * H * AD_D;
     const float *base = qkv + (size_t)b * S * ld + (size_t)h * AD_D;
 
-    // stage Q (rows r0 .. r0+RQ-1, scaled), K and V (all 128 key slots); rows past S are zero
+    // stage Q (rows r0 .. r0+RQ-1), K and V (all 128 key slots) with 16-byte
+    // cp.async copies, all in flight at once; rows past S are zero-filled
     for (int e = tid; e < (RQ + 2 * AD_S) * 16; e += AD_T) {
         const int row = e >> 4, d4 = e & 15;
-        int src;
-        float *dst;
-        if (row < RQ) {
-            src = r0 + row;
-            dst = Qs + row * AD_LD;
-        } else if (row < RQ + AD_S) {
-            src = row - RQ;
-            dst = Ks + src * AD_LD;
-        } else {
-            src = row - RQ - AD_S;
-            dst = Vs + src * AD_LD;
-        }
         const int part = row < RQ ? 0 : (row < RQ + AD_S ? 1 : 2);
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (src < S) {
-            v = __ldg(reinterpret_cast<const float4 *>(base + (size_t)src * ld + (size_t)part * H * AD_D) + d4);
-            if (part == 0)
-                v = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
-                                __fmul_rn(v.w, scale));
-        }
-        *reinterpret_cast<float4 *>(dst + 4 * d4) = v;
+        const int src = part == 0 ? r0 + row : (part == 1 ? row - RQ : row - RQ - AD_S);
+        float *dst = (part == 0 ? Qs + row * AD_LD : (part == 1 ? Ks : Vs) + src * AD_LD) + 4 * d4;
+        const bool ok = src < S;
+        const float *g = ok ? base + (size_t)src * ld + (size_t)part * H * AD_D + 4 * d4 : base;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                     "l"(g), "r"(ok ? 16 : 0)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // q' = q * scale, in place
+    for (int e = tid; e < RQ * 16; e += AD_T) {
+        float4 *p = reinterpret_cast<float4 *>(Qs + (e >> 4) * AD_LD) + (e & 15);
+        const float4 v = *p;
+        *p = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale), __fmul_rn(v.w, scale));
     }
     __syncthreads();
 
@@ -95,7 +91,7 @@ __global__ void __launch_bounds__(AD_T, 2) k_attention_det(const float *__restri
     for (int i = 0; i < RT; i++)
 #pragma unroll
         for (int j = 0; j < 8; j++) s[i][j] = 0.0f;
-#pragma unroll 2
+#pragma unroll 1
     for (int d4 = 0; d4 < AD_D / 4; d4++) {
         float4 k[8];
 #pragma unroll
