@@ -348,6 +348,14 @@ int tpt_cuda_plan_add_tensor(tpt_cuda_plan *plan, int dtype, size_t numel, int *
 /* an f32 constant, uploaded now (weights of f32 MatMuls, biases, LN params) */
 int tpt_cuda_plan_add_const(tpt_cuda_plan *plan, const float *host, size_t numel, int *id);
 int tpt_cuda_plan_add_op(tpt_cuda_plan *plan, const tpt_plan_op *op);
+/* Before finalize: lay the arena out by liveness instead of one disjoint slot
+ * per tensor (the reference's assign_offsets, exec.rs:276-294, gives every
+ * node its own range). A tensor then occupies its bytes only from its first
+ * writer to its last reader, so tensors with disjoint lifetimes share memory;
+ * results are identical. Only the tensors listed here (kept to the end of a
+ * run) can be fetched by tpt_cuda_plan_run (another id -> TPT_INVALID);
+ * tpt_cuda_plan_tensor_ptr of any other tensor may alias a later tensor. */
+int tpt_cuda_plan_reuse_arena(tpt_cuda_plan *plan, const int *keep_ids, size_t n_keep);
 /* lays the arena out and allocates it (the only allocation of a run) */
 int tpt_cuda_plan_finalize(tpt_cuda_plan *plan);
 int tpt_cuda_plan_arena_bytes(tpt_cuda_plan *plan, size_t *bytes);
@@ -370,6 +378,14 @@ int tpt_cuda_plan_run_device(tpt_cuda_plan *plan);
 /* H2D of the inputs, the ops, D2H of the outputs, then synchronise */
 int tpt_cuda_plan_run(tpt_cuda_plan *plan, const int *in_ids, const float *const *inputs, size_t n_in,
                       const int *out_ids, float *const *outputs, size_t n_out);
+/* n_steps runs of tpt_cuda_plan_run over consecutive batches (a serving loop):
+ * step s reads inputs[s * n_in + i] and writes outputs[s * n_out + j]. The next
+ * batch's inputs are copied to the device (on a copy stream, into a staging
+ * buffer) while the current batch computes; with page-locked host buffers the
+ * copy hides behind the forward pass. Results are those of n_steps separate
+ * runs. Returns after the last outputs are in host memory. */
+int tpt_cuda_plan_run_batches(tpt_cuda_plan *plan, const int *in_ids, const float *const *inputs, size_t n_in,
+                              const int *out_ids, float *const *outputs, size_t n_out, size_t n_steps);
 
 /* ------------------------------------------------------------------ */
 /* Multi-GPU (one process per GPU on one node)                          */

@@ -273,3 +273,79 @@ def test_resnet18_plan_bit_exact_batch256(cuda):
         want = OM.resnet18(xin[b0 * IMG:(b0 + 64) * IMG], spec, 64, scales=cal.frozen())
         g = got[b0 * 1000:(b0 + 64) * 1000]
         assert np.array_equal(g, want), (b0, _relerr(g, want))
+
+
+def test_liveness_arena_same_results_smaller(cuda):
+    # arena offsets by liveness (tpt_cuda_plan_reuse_arena): the same logits and
+    # hidden states as the one-slot-per-tensor layout, in a fraction of the bytes
+    from tpt_infer_b200 import graphs, synth
+
+    spec = graphs.resnet18_weights(cuda)
+    outs, sizes = [], []
+    for reuse in (False, True):
+        p, x, logits = graphs.build_resnet18(cuda, 4, spec, reuse=reuse)
+        p.calibrate(True)
+        p.run({x: synth.normal(4 * 3 * 224 * 224, 31)}, [logits])
+        p.freeze()
+        outs.append(p.run({x: synth.normal(4 * 3 * 224 * 224, 32)}, [logits])[0])
+        sizes.append(p.arena_bytes())
+        p.close()
+    assert np.array_equal(outs[0], outs[1])
+    assert sizes[1] * 3 <= sizes[0], sizes
+    layers = graphs.bert_weights(cuda, layers=3)
+    outs, sizes = [], []
+    for reuse in (False, True):
+        p, x, h = graphs.build_bert(cuda, 2, 64, layers, reuse=reuse)
+        p.calibrate(True)
+        p.run({x: synth.normal(2 * 64 * 768, 41)}, [h])
+        p.freeze()
+        p.set_graph(True)
+        xin = synth.normal(2 * 64 * 768, 42)
+        outs.append(p.run({x: xin}, [h])[0])
+        outs.append(p.run({x: xin}, [h])[0])  # graph replay
+        sizes.append(p.arena_bytes())
+        p.close()
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    assert sizes[1] * 3 <= sizes[0], sizes
+
+
+def test_liveness_arena_rejects_fetch_of_dropped_tensor(cuda):
+    from tpt_infer_b200 import graphs
+    from tpt_infer_b200.backend import OpError
+
+    W = graphs.mlp_weights()
+    p = graphs.Plan(cuda)
+    x, h, y = p.tensor(graphs.F32, 2 * 784), p.tensor(graphs.F32, 2 * 512), p.tensor(graphs.F32, 2 * 10)
+    p.op(graphs.OP_MATMUL, x, h, in1=p.const(W.w1), act=graphs.ACT_RELU, dims=(2, 784, 512))
+    p.op(graphs.OP_MATMUL, h, y, in1=p.const(W.w2), dims=(2, 512, 10))
+    p.reuse([x, y])
+    p.finalize()
+    xin = np.ones(2 * 784, np.float32)
+    assert p.run({x: xin}, [y])[0].shape == (20,)
+    with pytest.raises(OpError):
+        p.run({x: xin}, [h])  # not kept: its bytes may hold a later tensor
+    p.close()
+
+
+def test_run_batches_equals_separate_runs(cuda):
+    # tpt_cuda_plan_run_batches: consecutive batches with the next batch's H2D
+    # overlapped (page-locked and pageable host buffers) give the outputs of
+    # separate tpt_cuda_plan_run calls, also when called twice in a row
+    import torch
+
+    from tpt_infer_b200 import graphs, synth
+
+    spec = graphs.resnet18_weights(cuda)
+    p, x, logits = graphs.build_resnet18(cuda, 2, spec)
+    p.calibrate(True)
+    p.run({x: synth.normal(2 * 3 * 224 * 224, 31)}, [logits])
+    p.freeze()
+    xs = [synth.normal(2 * 3 * 224 * 224, 50 + s) for s in range(5)]
+    want = [p.run({x: v}, [logits])[0] for v in xs]
+    pinned = [torch.from_numpy(v).pin_memory().numpy() for v in xs]
+    for src in (pinned, xs):
+        for _ in range(2):
+            got = p.run_batches([x], [[v] for v in src], [logits])
+            for g, w in zip(got, want):
+                assert np.array_equal(g[0], w)
+    p.close()

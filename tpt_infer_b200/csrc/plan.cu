@@ -16,6 +16,7 @@
 // max); tpt_cuda_plan_freeze_scales turns the maxima into static scales.
 #include <string.h>
 
+#include <algorithm>
 #include <new>
 #include <vector>
 
@@ -44,6 +45,7 @@ int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, in
                      int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
                      int act, float *y, bool *handled, Requant rq, Residual res = Residual());
 int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
+int ensure_copy_streams(tpt_cuda_ctx *ctx);
 int launch_binary(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, const size_t od[8], unsigned amask,
                   unsigned bmask, int op, size_t n);
 int launch_pool_nchw(tpt_cuda_ctx *ctx, const float *x, float *y, int avg, size_t NC, int H, int W, int KH, int KW,
@@ -88,6 +90,15 @@ struct tpt_cuda_plan {
     int n_cells = 0;
     bool finalized = false;
     bool calibrating = false;
+    // liveness-based arena (tpt_cuda_plan_reuse_arena): only `keep` tensors and
+    // graph inputs (before their last reader) may be fetched
+    bool reuse = false;
+    std::vector<char> keep;
+    // tpt_cuda_plan_run_batches: two device staging buffers for the inputs and the
+    // events that order them between the copy stream and the compute stream
+    char *stage = nullptr;
+    size_t stage_bytes = 0;
+    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
     // recorded replay of run_ops (tpt_cuda_plan_set_graph) and the output set it was recorded for
     bool use_graph = false;
     tpt_cuda_graph *graph = nullptr;
@@ -361,6 +372,11 @@ int tpt_cuda_plan_destroy(tpt_cuda_plan *p) {
     if (!p) return TPT_INVALID;
     cudaSetDevice(p->device);
     drop_graph(p);
+    if (p->stage) cudaFree(p->stage);
+    for (int i = 0; i < 2; i++) {
+        if (p->ev_in[i]) cudaEventDestroy(p->ev_in[i]);
+        if (p->ev_free[i]) cudaEventDestroy(p->ev_free[i]);
+    }
     if (p->arena) cudaFree(p->arena);
     if (p->cells) cudaFree(p->cells);
     for (auto &t : p->tensors)
@@ -438,14 +454,73 @@ int tpt_cuda_plan_add_op(tpt_cuda_plan *p, const tpt_plan_op *op) {
     return TPT_OK;
 }
 
+// Arena offsets by liveness. A tensor lives from its first writer (less the
+// span of the longest run-time fusion, 3 ops: a fused launch at op i writes
+// the outputs of ops i+1 .. i+3) to its last reader; graph inputs (no writer)
+// from before the first op; kept tensors to the end. Tensors whose lifetimes
+// are disjoint share bytes; every placement is the lowest 256-byte aligned
+// offset free over the tensor's whole lifetime.
+static size_t liveness_layout(tpt_cuda_plan *p) {
+    const int nt = (int)p->tensors.size(), no = (int)p->ops.size();
+    std::vector<int> first_w(nt, INT32_MAX), last_use(nt, -1);
+    for (int i = 0; i < no; i++) {
+        const tpt_plan_op &o = p->ops[i].op;
+        if (o.out >= 0) {
+            first_w[o.out] = std::min(first_w[o.out], i);
+            last_use[o.out] = std::max(last_use[o.out], i);
+        }
+        for (int id : {o.in0, o.in1, o.in2})
+            if (id >= 0) last_use[id] = std::max(last_use[id], i);
+    }
+    struct Iv {
+        int t, start, end;
+        size_t size, off;
+    };
+    std::vector<Iv> iv;
+    for (int t = 0; t < nt; t++) {
+        const PlanTensor &T = p->tensors[t];
+        if (T.is_const) continue;
+        Iv v;
+        v.t = t;
+        v.start = first_w[t] == INT32_MAX ? -4 : first_w[t] - 3;
+        v.end = p->keep[t] ? INT32_MAX : std::max(last_use[t], v.start);
+        v.size = (T.numel * dt_size(T.dtype) + 255) & ~size_t(255);
+        v.off = 0;
+        iv.push_back(v);
+    }
+    std::vector<Iv *> placed;
+    size_t top = 0;
+    for (auto &v : iv) {
+        std::vector<std::pair<size_t, size_t>> busy;  // [off, off + size) of overlapping lifetimes
+        for (Iv *u : placed)
+            if (!(u->end < v.start || v.end < u->start)) busy.push_back({u->off, u->off + u->size});
+        std::sort(busy.begin(), busy.end());
+        size_t off = 0;
+        for (auto &b : busy) {
+            if (off + v.size <= b.first) break;
+            off = std::max(off, b.second);
+        }
+        v.off = off;
+        top = std::max(top, off + v.size);
+        placed.push_back(&v);
+    }
+    for (auto &v : iv) p->tensors[v.t].offset = v.off;
+    return top;
+}
+
 int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
     CHECK_PLAN(p);
     if (p->finalized) return TPT_INVALID;
     size_t off = 0;
-    for (auto &t : p->tensors) {
-        if (t.is_const) continue;
-        t.offset = off;
-        off += (t.numel * dt_size(t.dtype) + 255) & ~size_t(255);
+    if (p->reuse) {
+        p->keep.resize(p->tensors.size(), 0);
+        off = liveness_layout(p);
+    } else {
+        for (auto &t : p->tensors) {
+            if (t.is_const) continue;
+            t.offset = off;
+            off += (t.numel * dt_size(t.dtype) + 255) & ~size_t(255);
+        }
     }
     p->arena_bytes = off;
     cudaError_t e = cudaMalloc(&p->arena, off ? off : 256);
@@ -464,6 +539,18 @@ int tpt_cuda_plan_finalize(tpt_cuda_plan *p) {
             if (id >= 0) p->tensors[id].readers++;
     }
     p->finalized = true;
+    return TPT_OK;
+}
+
+int tpt_cuda_plan_reuse_arena(tpt_cuda_plan *p, const int *keep_ids, size_t n_keep) {
+    CHECK_PLAN(p);
+    if (p->finalized || (n_keep && !keep_ids)) return TPT_INVALID;
+    p->keep.assign(p->tensors.size(), 0);
+    for (size_t i = 0; i < n_keep; i++) {
+        if (!valid_id(p, keep_ids[i])) return TPT_INVALID;
+        p->keep[keep_ids[i]] = 1;
+    }
+    p->reuse = true;
     return TPT_OK;
 }
 
@@ -754,6 +841,8 @@ int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *i
         int st = h2d(p->ctx, t.ptr, inputs[i], t.numel * dt_size(t.dtype));
         if (st) return st;
     }
+    for (size_t i = 0; i < n_out; i++)
+        if (!valid_id(p, out_ids[i]) || (p->reuse && !p->keep[out_ids[i]])) return TPT_INVALID;
     int st = run_plan(p, out_ids, n_out);
     if (st) return st;
     for (size_t i = 0; i < n_out; i++) {
@@ -763,6 +852,96 @@ int tpt_cuda_plan_run(tpt_cuda_plan *p, const int *in_ids, const float *const *i
         if (st) return st;
     }
     return sync_and_check(p->ctx);
+}
+
+// n_steps forward passes, step s reading inputs[s * n_in + i] and writing
+// outputs[s * n_out + j]. Step s + 1's inputs travel host -> device on the
+// context's copy stream into one of two staging buffers while step s computes;
+// at the start of its step the compute stream waits for them and moves them
+// into the input tensors (device to device); outputs return on the compute
+// stream. With page-locked host buffers the H2D of the next batch overlaps the
+// whole forward pass of the current one.
+int tpt_cuda_plan_run_batches(tpt_cuda_plan *p, const int *in_ids, const float *const *inputs, size_t n_in,
+                              const int *out_ids, float *const *outputs, size_t n_out, size_t n_steps) {
+    CHECK_PLAN(p);
+    if (!p->finalized || (n_in && (!in_ids || !inputs)) || (n_out && (!out_ids || !outputs))) return TPT_INVALID;
+    size_t in_bytes = 0;
+    std::vector<size_t> off(n_in);
+    for (size_t i = 0; i < n_in; i++) {
+        if (!valid_id(p, in_ids[i]) || p->tensors[in_ids[i]].is_const) return TPT_INVALID;
+        const PlanTensor &t = p->tensors[in_ids[i]];
+        off[i] = in_bytes;
+        in_bytes += (t.numel * dt_size(t.dtype) + 255) & ~size_t(255);
+    }
+    for (size_t i = 0; i < n_out; i++)
+        if (!valid_id(p, out_ids[i]) || (p->reuse && !p->keep[out_ids[i]])) return TPT_INVALID;
+    if (n_steps == 0) return TPT_OK;
+    tpt_cuda_ctx *ctx = p->ctx;
+    int st = ensure_copy_streams(ctx);
+    if (st) return st;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 2 && e == cudaSuccess; i++) {
+        if (!p->ev_in[i]) e = cudaEventCreateWithFlags(&p->ev_in[i], cudaEventDisableTiming);
+        if (e == cudaSuccess && !p->ev_free[i]) e = cudaEventCreateWithFlags(&p->ev_free[i], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess && p->stage_bytes < 2 * in_bytes) {
+        if (p->stage) cudaFree(p->stage);
+        p->stage = nullptr;
+        p->stage_bytes = 0;
+        e = cudaMalloc(&p->stage, 2 * in_bytes);
+        if (e == cudaSuccess) p->stage_bytes = 2 * in_bytes;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(ctx, e, "batch pipeline set-up");
+    }
+    // the staging buffers may still be read by an earlier call's last step
+    e = cudaStreamWaitEvent(ctx->copy_in, p->ev_free[0], 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->copy_in, p->ev_free[1], 0);
+    auto upload = [&](size_t s) -> cudaError_t {
+        char *dst = p->stage + (s & 1) * in_bytes;
+        for (size_t i = 0; i < n_in; i++) {
+            const PlanTensor &t = p->tensors[in_ids[i]];
+            cudaError_t r = cudaMemcpyAsync(dst + off[i], inputs[s * n_in + i], t.numel * dt_size(t.dtype),
+                                            cudaMemcpyHostToDevice, ctx->copy_in);
+            if (r != cudaSuccess) return r;
+        }
+        return cudaEventRecord(p->ev_in[s & 1], ctx->copy_in);
+    };
+    if (e == cudaSuccess) e = upload(0);
+    for (size_t s = 0; s < n_steps && e == cudaSuccess; s++) {
+        const int b = (int)(s & 1);
+        if (s + 1 < n_steps) {  // the next batch's inputs, once its buffer is free again
+            e = cudaStreamWaitEvent(ctx->copy_in, p->ev_free[b ^ 1], 0);
+            if (e == cudaSuccess) e = upload(s + 1);
+            if (e != cudaSuccess) break;
+        }
+        e = cudaStreamWaitEvent(ctx->stream, p->ev_in[b], 0);
+        for (size_t i = 0; i < n_in && e == cudaSuccess; i++) {
+            const PlanTensor &t = p->tensors[in_ids[i]];
+            e = cudaMemcpyAsync(t.ptr, p->stage + b * in_bytes + off[i], t.numel * dt_size(t.dtype),
+                                cudaMemcpyDeviceToDevice, ctx->stream);
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(p->ev_free[b], ctx->stream);
+        if (e != cudaSuccess) break;
+        st = run_plan(p, out_ids, n_out);
+        if (st) {
+            cudaStreamSynchronize(ctx->copy_in);
+            return st;
+        }
+        for (size_t j = 0; j < n_out && e == cudaSuccess; j++) {
+            const PlanTensor &t = p->tensors[out_ids[j]];
+            e = cudaMemcpyAsync(outputs[s * n_out + j], t.ptr, t.numel * dt_size(t.dtype), cudaMemcpyDeviceToHost,
+                                ctx->stream);
+        }
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        cudaStreamSynchronize(ctx->copy_in);
+        cudaStreamSynchronize(ctx->stream);
+        return cuda_fail(ctx, e, "batch pipeline");
+    }
+    return sync_and_check(ctx);
 }
 
 }  // extern "C"

@@ -77,6 +77,12 @@ class Plan:
         self.comm = comm
         self.be._check(lib.tpt_cuda_plan_set_comm(self.h, comm.h))
 
+    def reuse(self, keep):
+        """Before finalize: arena offsets by liveness; only ``keep`` can be fetched."""
+        ids = list(keep)
+        arr = (C.c_int * max(len(ids), 1))(*ids)
+        self.be._check(lib.tpt_cuda_plan_reuse_arena(self.h, arr, len(ids)))
+
     def finalize(self):
         self.be._check(lib.tpt_cuda_plan_finalize(self.h))
 
@@ -130,6 +136,26 @@ class Plan:
         out_p = (C.c_void_p * len(outputs))(*[a.ctypes.data for a in outs])
         self.be._check(lib.tpt_cuda_plan_run(self.h, in_ids, in_p, len(ids), out_ids, out_p, len(outputs)))
         return outs
+
+    def run_batches(self, in_ids, batches, out_ids, outputs=None):
+        """tpt_cuda_plan_run_batches: len(batches) runs, batches[s] = the host inputs
+        of step s (one array per id of ``in_ids``); the next step's inputs are
+        copied while the current one computes. ``outputs[s][j]`` (preallocated
+        f32 arrays, page-locked for overlap) receive the results."""
+        n, ni, no = len(batches), len(in_ids), len(out_ids)
+        if outputs is None:
+            outputs = [[np.empty(self.numel[o], np.float32) for o in out_ids] for _ in range(n)]
+        ins = []
+        for b in batches:
+            for i, a in zip(in_ids, b):
+                if a.dtype != np.float32 or not a.flags.c_contiguous or a.size != self.numel[i]:
+                    raise OpError(1, self.numel[i], a.size)
+                ins.append(a.ctypes.data)
+        outs = [o.ctypes.data for row in outputs for o in row]
+        self.be._check(lib.tpt_cuda_plan_run_batches(
+            self.h, (C.c_int * max(ni, 1))(*in_ids), (C.c_void_p * max(len(ins), 1))(*ins), ni,
+            (C.c_int * max(no, 1))(*out_ids), (C.c_void_p * max(len(outs), 1))(*outs), no, n))
+        return outputs
 
     def close(self):
         if self.h:
@@ -188,7 +214,7 @@ def mlp_weights(seed=10):
                       synth.normal(512 * 10, seed + 1, 0.0, 0.06).reshape(512, 10), np.zeros(10, np.float32))
 
 
-def build_mlp_f32(be, batch, W: MlpWeights):
+def build_mlp_f32(be, batch, W: MlpWeights, reuse=True):
     p = Plan(be)
     x = p.tensor(F32, batch * 784)
     h = p.tensor(F32, batch * 512)
@@ -198,11 +224,13 @@ def build_mlp_f32(be, batch, W: MlpWeights):
     p.op(OP_MATMUL, x, h, in1=w1, in2=b1, act=ACT_RELU, dims=(batch, 784, 512))
     p.op(OP_MATMUL, h, z, in1=w2, in2=b2, dims=(batch, 512, 10))
     p.op(OP_SOFTMAX, z, y, dims=(batch, 10))
+    if reuse:
+        p.reuse([x, y, z])
     p.finalize()
     return p, x, y, z
 
 
-def build_mlp_int8(be, batch, W: MlpWeights):
+def build_mlp_int8(be, batch, W: MlpWeights, reuse=True):
     """INT8 PTQ variant: W1, W2 per output channel (quantize W^T rows); activations
     per tensor with calibrated static scales."""
     p = Plan(be)
@@ -223,6 +251,8 @@ def build_mlp_int8(be, batch, W: MlpWeights):
     p.op(OP_QUANTIZE, h, hq, dims=(batch * 512,))
     p.op(OP_LINEAR, hq, z, in1=b2, w=wh2, dims=(batch,))
     p.op(OP_SOFTMAX, z, y, dims=(batch, 10))
+    if reuse:
+        p.reuse([x, y, z])
     p.finalize()
     return p, x, y, z, (q1, s1, q2, s2)
 
@@ -300,7 +330,7 @@ def _stem_s2d(cv, cp):
     return out.reshape(cv.cout, 4 * 4 * 4 * cp)
 
 
-def build_resnet18(be, batch, spec: ResNetSpec):
+def build_resnet18(be, batch, spec: ResNetSpec, reuse=True):
     """The stem input is held as 2x2 space-to-depth NHWC of the image padded to 4
     channels ([112, 112, 16]); the 7x7/2 stem runs as the equivalent 4x4/1 conv
     on it, so its gathers move 16-byte pixels. Outputs are unchanged (the same
@@ -363,6 +393,8 @@ def build_resnet18(be, batch, spec: ResNetSpec):
     p.op(OP_GAP, cur, g, dims=(batch, H * W, 512))
     logits = p.tensor(F32, batch * 1000)
     p.op(OP_MATMUL, g, logits, in1=p.const(spec.fc_w), in2=p.const(spec.fc_b), dims=(batch, 512, 1000))
+    if reuse:
+        p.reuse([x, logits])
     p.finalize()
     return p, x, logits
 
@@ -394,7 +426,7 @@ def bert_weights(be, layers=12, seed=5000, hidden=768, ffn=3072):
     return out
 
 
-def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-5, ffn_shard=None):
+def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-5, ffn_shard=None, reuse=True):
     """``ffn_shard`` = a sharding.Comm: FFN1 column-sharded over its ranks and
     reassembled by an all-gather inside the plan (see sharding.py)."""
     from . import sharding
@@ -453,5 +485,7 @@ def build_bert(be, batch, seq, layers_w, heads=12, hidden=768, ffn=3072, eps=1e-
         h2 = p.tensor(F32, T * hidden)
         p.op(OP_LAYERNORM, r2, h2, in1=p.const(lw.g2), in2=p.const(lw.b2), f0=eps, dims=(T, hidden))
         cur = h2
+    if reuse:
+        p.reuse([x, cur])
     p.finalize()
     return p, x, cur

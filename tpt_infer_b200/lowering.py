@@ -293,6 +293,7 @@ def lower(graph: ComputationGraph, be, quantized=None) -> LoweredGraph:
     try:
         for node in graph.nodes:
             _lower_node(graph, node, p, tid, in_ids, in_dims, const, port, is_init, out_tensor, be, quantized)
+        p.reuse(list(dict.fromkeys(in_ids + [tid[o] for o in graph.outputs])))
         p.finalize()
     except Exception:
         p.close()
