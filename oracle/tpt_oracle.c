@@ -296,7 +296,8 @@ static float gelu1(float x) {
 float tpto_exp_det(float x) {
     if (!(x >= -87.0f)) return x != x ? x : 0.0f;
     if (x > 88.0f) return INFINITY;
-    const float n = rintf(x * 1.44269504f);
+    const float t = fmaf(x, 1.44269504f, 12582912.0f);
+    const float n = t - 12582912.0f;
     float r = fmaf(n, -0.693145751953125f, x);
     r = fmaf(n, -1.42860676533018720e-06f, r);
     float p = 0.000198412701f;
@@ -307,7 +308,9 @@ float tpto_exp_det(float x) {
     p = fmaf(p, r, 0.5f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    uint32_t eb = (uint32_t)((int)n + 127) << 23;
+    int32_t tb;
+    memcpy(&tb, &t, 4);
+    uint32_t eb = (uint32_t)(tb - 0x4B400000 + 127) << 23;
     float sc;
     memcpy(&sc, &eb, 4);
     return p * sc;

@@ -1,12 +1,13 @@
 // det_math.cuh -- exp, reciprocal and GELU built only from correctly rounded
-// IEEE operations (fmaf, multiply, add, rint, exact scaling by a power of two),
+// IEEE operations (fmaf, multiply, add, exact scaling by a power of two),
 // so a C restatement with the same operations in the same order gives the
 // same bits on the CPU. The model paths that must match a CPU replay bit for
 // bit use these instead of library transcendentals: the attention softmax and
 // every GELU epilogue.
 //
 // exp_det(x): Cody-Waite range reduction (W. J. Cody and W. Waite, "Software
-// Manual for the Elementary Functions", 1980): n = rint(x log2 e),
+// Manual for the Elementary Functions", 1980): n = x log2 e rounded to the
+// nearest integer (by one fma with 1.5 * 2^23: no conversion instructions),
 // r = x - n ln2 with ln2 split into a 12-bit head (n * head is exact for
 // |n| < 2^12) and a tail, then the degree-7 Taylor polynomial of e^r on
 // |r| <= ln2/2 (truncation error < 6e-9 relative) by Horner's rule with fmaf,
@@ -38,7 +39,10 @@ constexpr float DET_C2 = 0.5f, DET_C3 = 0.166666672f, DET_C4 = 0.0416666679f, DE
 __device__ __forceinline__ float exp_det(float x) {
     if (!(x >= -87.0f)) return x != x ? x : 0.0f;
     if (x > 88.0f) return __int_as_float(0x7f800000);
-    const float n = rintf(__fmul_rn(x, DET_LOG2E));
+    // n = x log2 e rounded to an integer inside one fma: adding 1.5 * 2^23 leaves
+    // ulp 1, so the sum's low mantissa bits are n (two's complement offset)
+    const float t = __fmaf_rn(x, DET_LOG2E, 12582912.0f);
+    const float n = __fsub_rn(t, 12582912.0f);
     float r = __fmaf_rn(n, -DET_LN2_HI, x);
     r = __fmaf_rn(n, -DET_LN2_LO, r);
     float p = DET_C7;
@@ -49,7 +53,7 @@ __device__ __forceinline__ float exp_det(float x) {
     p = __fmaf_rn(p, r, DET_C2);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+    return __fmul_rn(p, __int_as_float((__float_as_int(t) - 0x4B400000 + 127) << 23));
 }
 
 __device__ __forceinline__ float recip12_det(float d) {
