@@ -175,7 +175,7 @@ def test_plan_add_layernorm_fusion(cuda, rows, cols):
     p.close()
 
 
-@pytest.mark.parametrize("B,S", [(2, 128), (1, 77), (3, 40), (1, 1)])
+@pytest.mark.parametrize("B,S", [(2, 128), (1, 77), (3, 40), (1, 1), (16, 128), (64, 100)])
 def test_attention_op(cuda, B, S):
     # the fused attention op alone against the oracle's MatMul / Softmax / MatMul
     from tpt_infer_b200 import graphs, synth

@@ -185,31 +185,29 @@ int launch_attention_det(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B,
     if (D != AD_D || S <= 0 || S > AD_S || B <= 0 || H <= 0 || B > 65535 || H > 65535 ||
         (((uintptr_t)qkv | (uintptr_t)out) & 15) || ((uintptr_t)q & 3))
         return TPT_UNSUPPORTED;
-    // one block of 128 query rows per head when that fills the GPU, else two of 64
-    const bool small = (size_t)B * H < (size_t)ctx->sm_count * 4;
-    const int rq = small ? 64 : 128;
-    const int zb = (S + rq - 1) / rq;
-    const dim3 grid((unsigned)H, (unsigned)B, (unsigned)zb);
-    static bool attr[64][2] = {};
-    if (small) {
-        const size_t smem = AdSmem<64>::FLOATS * sizeof(float);
-        if (!attr[ctx->device & 63][0]) {
-            cudaError_t e = cudaFuncSetAttribute(k_attention_det<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
-            if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
-            attr[ctx->device & 63][0] = true;
-        }
-        launch_pdl(k_attention_det<64>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
-    } else {
-        const size_t smem = AdSmem<128>::FLOATS * sizeof(float);
-        if (!attr[ctx->device & 63][1]) {
-            cudaError_t e = cudaFuncSetAttribute(k_attention_det<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
-            if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
-            attr[ctx->device & 63][1] = true;
-        }
-        launch_pdl(k_attention_det<128>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
+    // query rows per CTA: 128, or 64 / 32 when that many heads would leave SMs idle
+    // (two CTAs fit per SM); the arithmetic per output is the same for every split
+    const size_t heads = (size_t)B * H, slots = (size_t)ctx->sm_count * 2;
+    const int rq = heads >= slots ? 128 : (heads * 2 >= slots ? 64 : 32);
+    const dim3 grid((unsigned)H, (unsigned)B, (unsigned)((S + rq - 1) / rq));
+    static bool attr[64][3] = {};
+    const int ai = rq == 128 ? 0 : (rq == 64 ? 1 : 2);
+    const size_t smem = (rq == 128 ? AdSmem<128>::FLOATS : rq == 64 ? AdSmem<64>::FLOATS : AdSmem<32>::FLOATS) *
+                        sizeof(float);
+    const void *fn = rq == 128 ? (const void *)k_attention_det<128>
+                     : rq == 64 ? (const void *)k_attention_det<64>
+                                : (const void *)k_attention_det<32>;
+    if (!attr[ctx->device & 63][ai]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
+        attr[ctx->device & 63][ai] = true;
     }
+    if (rq == 128)
+        launch_pdl(k_attention_det<128>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
+    else if (rq == 64)
+        launch_pdl(k_attention_det<64>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
+    else
+        launch_pdl(k_attention_det<32>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
     return after_launch(ctx, "attention");
 }
 

@@ -615,8 +615,29 @@ template <int MODE>
 int launch_conv_bn(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
                    const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq,
                    const Residual &res) {
-    if (w->n <= 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
-    if (w->n <= 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
+    // tile N: the widest tile up to the channel count, unless a narrower one
+    // fills more SMs: rounds of tiles over the SMs x width x a per-width cost
+    // (the narrow tile's operand-bandwidth penalty, fading for short K)
+    const long long mt = ((long long)cs.N * cs.OH * cs.OW + CV_BM - 1) / CV_BM;
+    const long long sms = ctx->sm_count > 0 ? ctx->sm_count : 1;
+    const double kw = w->k < 4096 ? (double)w->k / 4096.0 : 1.0;
+    const int widths[3] = {256, 128, 64};
+    const double cost[3] = {1.0, 1.6, 2.6};
+    int bn = 64;
+    double best = 0.0;
+    bool first = true;
+    for (int i = 0; i < 3; i++) {
+        if (i < 2 && w->n <= (size_t)widths[i + 1]) continue;  // wider than the channels need
+        const long long tiles = mt * (((long long)w->n + widths[i] - 1) / widths[i]);
+        const double t = (double)((tiles + sms - 1) / sms) * widths[i] * (1.0 + (cost[i] - 1.0) * kw);
+        if (first || t < best) {
+            best = t;
+            bn = widths[i];
+            first = false;
+        }
+    }
+    if (bn == 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
+    if (bn == 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
     return launch_conv<256, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
 }
 

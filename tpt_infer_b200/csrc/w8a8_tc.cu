@@ -452,10 +452,11 @@ int build_weight_tmap(tpt_cuda_weights *w) {
 // Large-M shapes go to the tensor-core kernel: M >= 128, weights with a tensor
 // map (K % 16 == 0, 16-byte aligned), A 16-byte aligned.
 // M > 64 with the weight's tensor maps available and A 16-byte aligned.
-// Tile N is the largest of 256 / 128 / 64 whose tile count still covers the SM
-// pairs in one pass, weighing a narrower tile's lower shared-memory efficiency
-// (an M=256 x N=64 MMA reads 5 KB of operands per 64 tensor-core cycles per SM
-// against 4 KB at N=256) with a per-width cost factor.
+// Tile N (256 / 128 / 64) minimises rounds of tiles over the SM pairs x tile
+// width x a per-width cost factor: a narrower tile's lower shared-memory
+// efficiency (an M=256 x N=64 MMA reads 5 KB of operands per 64 tensor-core
+// cycles per SM against 4 KB at N=256), scaled down for short K, where the
+// epilogue's per-output work dominates.
 int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_weights *w, float a_scale,
                    const float *bias, int act, float *y, int32_t *acc, bool *handled, Requant rq) {
     *handled = false;
@@ -468,11 +469,14 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     const long long mt = (M + P_BM - 1) / P_BM;
     const int widths[3] = {256, 128, 64};
     const double cost[3] = {1.0, 1.6, 2.6};
+    // the narrow-tile penalty is an operand-bandwidth cost of the k loop: it
+    // fades for short K, where the epilogue (per output, any width) dominates
+    const double kw = K < 4096 ? (double)K / 4096.0 : 1.0;
     int bn = 256;
     double best = 0.0;
     for (int i = 0; i < 3; i++) {
         const long long tiles = mt * ((N + widths[i] - 1) / widths[i]);
-        const double t = (double)((tiles + pairs - 1) / pairs) * widths[i] * cost[i];
+        const double t = (double)((tiles + pairs - 1) / pairs) * widths[i] * (1.0 + (cost[i] - 1.0) * kw);
         if (i == 0 || t < best) {
             best = t;
             bn = widths[i];
