@@ -153,6 +153,7 @@ def cmd_bench(args):
             p.calibrate(True)
             p.run({x: synth.normal(B * IMG, 31)}, [y])
             p.freeze()
+            p.set_graph(True)  # the forward as one recorded launch sequence
             p.run({x: synth.normal(B * IMG, 32)}, [y])
             t = _time(p.run_device, be.sync, args.steps)
             res.update(batch=B, ms_per_batch=t * 1e3, images_per_s=B / t)
@@ -163,6 +164,7 @@ def cmd_bench(args):
             p.calibrate(True)
             p.run({x: synth.normal(B * S * H, 41)}, [y])
             p.freeze()
+            p.set_graph(True)
             p.run({x: synth.normal(B * S * H, 42)}, [y])
             t = _time(p.run_device, be.sync, args.steps)
             res.update(batch=B, seq=S, layers=args.layers, ms_per_batch=t * 1e3, sequences_per_s=B / t)
