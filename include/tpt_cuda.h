@@ -81,6 +81,15 @@ const char *tpt_cuda_last_error(tpt_cuda_ctx *ctx);
 void tpt_cuda_last_size_mismatch(tpt_cuda_ctx *ctx, size_t *expected, size_t *actual);
 /* Number of kernels this library launched on the context since creation. */
 uint64_t tpt_cuda_ctx_launch_count(tpt_cuda_ctx *ctx);
+/* Bound of the device-side waits in this context's kernels, in SM clock
+ * cycles (0 = the default of 2e9 cycles, about 1 s at the B200's boost clock).
+ * Every mbarrier wait in the tensor-core and TMA-ring kernels is bounded; a
+ * wait that runs out makes the kernel leave its loops, wait (with the default
+ * bound) for its own copies and MMAs still in flight, free its tensor memory
+ * and return, and the next synchronising call reports TPT_TIMEOUT. A short
+ * bound makes a normal launch run out, so the timeout path can be exercised
+ * without a stuck GPU. No counterpart in the reference (a CPU runtime). */
+int tpt_cuda_ctx_set_wait_limit(tpt_cuda_ctx *ctx, uint32_t cycles);
 
 /* CUDA graphs of device-pointer calls. The reference runtime walks the graph
  * node by node on every call (crates/tpt-infer-runtime/src/exec.rs:570-635);
@@ -404,6 +413,9 @@ typedef struct tpt_cuda_comm tpt_cuda_comm;
 int tpt_cuda_comm_unique_id(unsigned char *id, size_t id_bytes);
 int tpt_cuda_comm_create(tpt_cuda_ctx *ctx, const unsigned char *id, size_t id_bytes, int world, int rank,
                          tpt_cuda_comm **out);
+/* Deadline of communicator set-up and of each enqueue's completion report, in
+ * seconds (0 = the default of 120 s); process-wide. */
+int tpt_cuda_comm_set_timeout(double seconds);
 int tpt_cuda_comm_destroy(tpt_cuda_comm *comm);
 int tpt_cuda_comm_size(const tpt_cuda_comm *comm, int *world, int *rank);
 /* out [world * bytes_per_rank] = the ranks' in [bytes_per_rank], rank order (device pointers, async) */

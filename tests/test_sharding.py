@@ -114,3 +114,50 @@ def test_ffn_column_shard_gloo_bit_identical(world):
     want = _ffn_full()
     for r in range(world):
         assert np.array_equal(np.frombuffer(out[r], np.float32), want), r
+
+
+# ----------------------------------------------------------------- a rank that leaves
+def _leaver(rank, world, port, q):
+    # rank 1 leaves between steps (after the first collective, before the
+    # second); the others learn of it when their next collective ends with an
+    # error within the short process-group timeout, not by hanging
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    t = torch.ones(4)
+    dist.all_reduce(t)  # step 1: every rank
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()  # the message is out before the process vanishes
+        os._exit(0)  # gone without a word
+    t0 = time.time()
+    try:
+        dist.all_reduce(t)  # step 2: the peer never arrives
+        q.put((rank, "completed", time.time() - t0))
+    except Exception as e:  # noqa: BLE001  (gloo raises RuntimeError / DistBackendError)
+        q.put((rank, "error:" + type(e).__name__, time.time() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_is_detected_by_the_others():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (what, dt) for r, what, dt in (q.get(timeout=120) for _ in range(2))}
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][0] == "left"
+    assert res[0][0].startswith("error"), res
+    assert res[0][1] < 30

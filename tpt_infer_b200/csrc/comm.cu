@@ -16,6 +16,7 @@
 #include <nccl.h>
 #include <string.h>
 
+#include <atomic>
 #include <chrono>
 #include <mutex>
 #include <new>
@@ -72,6 +73,7 @@ const NcclApi &nccl() {
 }
 
 constexpr double COMM_TIMEOUT_S = 120.0;
+std::atomic<double> g_comm_timeout_s{COMM_TIMEOUT_S};  // tpt_cuda_comm_set_timeout
 
 int nccl_fail(tpt_cuda_ctx *ctx, ncclResult_t r, const char *what) {
     if (ctx) {
@@ -92,7 +94,7 @@ int settle(tpt_cuda_comm *c, ncclResult_t r, const char *what) {
         if (q != ncclSuccess) return nccl_fail(c->ctx, q, what);
         if (s == ncclSuccess) return TPT_OK;
         if (s != ncclInProgress) return nccl_fail(c->ctx, s, what);
-        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > COMM_TIMEOUT_S)
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > g_comm_timeout_s.load())
             return nccl_fail(c->ctx, ncclInProgress, what);
         std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
@@ -158,6 +160,12 @@ int tpt_cuda_comm_create(tpt_cuda_ctx *ctx, const unsigned char *id, size_t id_b
         return st;
     }
     *out = c;
+    return TPT_OK;
+}
+
+int tpt_cuda_comm_set_timeout(double seconds) {
+    if (!(seconds >= 0.0)) return TPT_INVALID;
+    g_comm_timeout_s.store(seconds > 0.0 ? seconds : COMM_TIMEOUT_S);
     return TPT_OK;
 }
 

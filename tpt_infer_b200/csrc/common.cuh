@@ -13,7 +13,7 @@
 // Device-side error words (one 32-bit word each), written by kernels whose
 // bounded waits ran out or whose own index checks failed. Read and cleared by
 // tpt_cuda_ctx_sync / the host-staged entry points.
-enum { TPT_FLAG_TIMEOUT = 0, TPT_FLAG_CHECK = 1, TPT_FLAG_WORDS = 4 };
+enum { TPT_FLAG_TIMEOUT = 0, TPT_FLAG_CHECK = 1, TPT_FLAG_WAIT_LIMIT = 2, TPT_FLAG_WORDS = 4 };
 
 struct tpt_cuda_ctx {
     int device = 0;

@@ -157,7 +157,7 @@ int sync_and_check(tpt_cuda_ctx *ctx) {
     if (e != cudaSuccess) return cuda_fail(ctx, e, "flag read");
     if (flags[TPT_FLAG_TIMEOUT] || flags[TPT_FLAG_CHECK]) {
         if (flags[TPT_FLAG_TIMEOUT]) ctx->sk_dirty = true;  // a stream-K launch may have stopped mid-tile
-        cudaMemsetAsync(ctx->d_flags, 0, sizeof flags, ctx->stream);
+        cudaMemsetAsync(ctx->d_flags, 0, 2 * sizeof(unsigned), ctx->stream);  // the error words, not the wait limit
         cudaStreamSynchronize(ctx->stream);
         char buf[160];
         snprintf(buf, sizeof buf, "device flags: timeout=0x%x check=0x%x", flags[TPT_FLAG_TIMEOUT],
@@ -598,3 +598,13 @@ int tpt_cuda_softmax_dev(tpt_cuda_ctx *ctx, const float *a, float *out, size_t n
 }
 
 }  // extern "C"
+
+extern "C" int tpt_cuda_ctx_set_wait_limit(tpt_cuda_ctx *ctx, uint32_t cycles) {
+    if (!ctx) return TPT_INVALID;
+    if (ctx->capturing) return refuse_in_capture(ctx, "setting the wait limit");
+    cudaSetDevice(ctx->device);
+    cudaError_t e = cudaMemcpyAsync(ctx->d_flags + TPT_FLAG_WAIT_LIMIT, &cycles, sizeof cycles, cudaMemcpyHostToDevice,
+                                    ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    return e == cudaSuccess ? TPT_OK : cuda_fail(ctx, e, "wait limit");
+}

@@ -71,16 +71,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait. Returns false when the CTA is aborting or the wait ran out
 // (then the abort is raised and the global timeout flag recorded). The abort
-// flag and the clock are checked every 16 polls.
+// flag and the clock are checked every 16 polls. Progress waits
+// (honour_abort) use the context's wait limit when one is set
+// (gflags[TPT_FLAG_WAIT_LIMIT], cycles; tpt_cuda_ctx_set_wait_limit), so a test
+// can make a normal launch run out of its waits; the drain waits of an
+// aborting CTA (its own copies and MMAs still in flight) always keep the full
+// bound, so no CTA exits while the hardware still writes its memory.
 static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
                                        bool honour_abort) {
     if (mbar_try_wait(bar, parity)) return true;
+    long long limit = TPT_WAIT_CYCLES;
+    if (honour_abort && gflags) {
+        const unsigned l = *reinterpret_cast<volatile unsigned *>(gflags + TPT_FLAG_WAIT_LIMIT);
+        if (l) limit = (long long)l;
+    }
     const long long t0 = clock64();
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 15u) == 0) {
             if (honour_abort && *abort_flag) return false;
-            if (clock64() - t0 > TPT_WAIT_CYCLES) {
+            if (clock64() - t0 > limit) {
                 *abort_flag = 1;
                 if (gflags) atomicOr(gflags + TPT_FLAG_TIMEOUT, 1u);
                 return false;
