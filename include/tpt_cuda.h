@@ -90,6 +90,12 @@ uint64_t tpt_cuda_ctx_launch_count(tpt_cuda_ctx *ctx);
  * bound makes a normal launch run out, so the timeout path can be exercised
  * without a stuck GPU. No counterpart in the reference (a CPU runtime). */
 int tpt_cuda_ctx_set_wait_limit(tpt_cuda_ctx *ctx, uint32_t cycles);
+/* Self-test of that mechanism: one CTA waits, through the same bounded wait,
+ * on a barrier nothing arrives on. *outcome receives bit 0 = the wait
+ * succeeded (never expected), bit 1 = the CTA's abort was raised. Returns
+ * TPT_TIMEOUT when the expiry was recorded and reported, as a real kernel's
+ * would be; the context stays usable. Takes the context's wait limit. */
+int tpt_cuda_selftest_bounded_wait(tpt_cuda_ctx *ctx, unsigned *outcome);
 
 /* CUDA graphs of device-pointer calls. The reference runtime walks the graph
  * node by node on every call (crates/tpt-infer-runtime/src/exec.rs:570-635);

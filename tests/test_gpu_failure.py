@@ -26,13 +26,34 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 TPT_TIMEOUT, TPT_NCCL_ERROR = 7, 8
 
 
+def test_bounded_wait_selftest(cuda):
+    # a barrier nothing arrives on: the bounded wait runs out (the default ~1 s
+    # bound, then a 1000-cycle limit), the host reads TPT_TIMEOUT, and the
+    # context keeps working
+    import ctypes as C
+
+    from tpt_infer_b200._capi import lib
+
+    out = C.c_uint(0)
+    for limit in (0, 1000):
+        assert lib.tpt_cuda_ctx_set_wait_limit(cuda.ctx, limit) == 0
+        t0 = time.time()
+        assert lib.tpt_cuda_selftest_bounded_wait(cuda.ctx, C.byref(out)) == TPT_TIMEOUT
+        assert out.value == 2  # not satisfied; the CTA's abort raised
+        assert time.time() - t0 < 10
+    assert lib.tpt_cuda_ctx_set_wait_limit(cuda.ctx, 0) == 0
+    x = O.normal(1000, 5)
+    q, s = cuda.quantize_i8_symmetric(x)
+    assert np.array_equal(q, O.quantize_i8_symmetric(x)[0])
+
+
 def test_wait_limit_timeout_then_recovers(cuda):
     import torch
 
     from tpt_infer_b200._capi import lib
     from tpt_infer_b200.backend import OpError
 
-    m, n, k = 16, 4096, 4096  # the TMA-ring small-batch kernel
+    m, n, k = 16, 32768, 4096  # the TMA-ring small-batch kernel, its ring cycling over HBM loads
     w = O.normal(n * k, 300, 0.0, 0.02)
     wq, ws = O.quantize_i8_symmetric_per_channel(w, n)
     aq, sa = O.quantize_i8_symmetric(O.normal(m * k, 301))
@@ -43,7 +64,7 @@ def test_wait_limit_timeout_then_recovers(cuda):
     y = torch.empty(m * n, dtype=torch.float32, device="cuda")
     want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, 0, threads=8)
     try:
-        assert lib.tpt_cuda_ctx_set_wait_limit(cuda.ctx, 300) == 0
+        assert lib.tpt_cuda_ctx_set_wait_limit(cuda.ctx, 100) == 0
         cuda.w8a8_gemm_dev(a, m, sa, wh, b, 0, y)
         with pytest.raises(OpError) as e:
             cuda.sync()

@@ -92,6 +92,7 @@ SIGNATURES = {
     "tpt_cuda_plan_finalize": (C.c_int, [vp]),
     "tpt_cuda_plan_reuse_arena": (C.c_int, [vp, C.POINTER(C.c_int), sz]),
     "tpt_cuda_ctx_set_wait_limit": (C.c_int, [ctxp, C.c_uint32]),
+    "tpt_cuda_selftest_bounded_wait": (C.c_int, [ctxp, C.POINTER(C.c_uint)]),
     "tpt_cuda_comm_set_timeout": (C.c_int, [C.c_double]),
     "tpt_cuda_plan_run_batches": (C.c_int, [vp, C.POINTER(C.c_int), C.POINTER(vp), sz, C.POINTER(C.c_int), C.POINTER(vp), sz, sz]),
     "tpt_cuda_plan_arena_bytes": (C.c_int, [vp, szp]),

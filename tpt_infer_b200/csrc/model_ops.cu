@@ -1,7 +1,7 @@
 // model_ops.cu -- device ops the model plans need besides the GEMMs:
 // LayerNorm, bias/residual adds, NHWC INT8 conv plumbing (layout change +
 // quantize, im2col), pooling, per-tensor max-abs. The fused attention is in
-// attention_tc.cu.
+// attention_det.cu.
 //
 // Layout inside a plan: activations are row-major [rows, channels] (NHWC for
 // images), so a conv's im2col rows and a GEMM's output rows are both

@@ -77,13 +77,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // can make a normal launch run out of its waits; the drain waits of an
 // aborting CTA (its own copies and MMAs still in flight) always keep the full
 // bound, so no CTA exits while the hardware still writes its memory.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
                                        bool honour_abort) {
     if (mbar_try_wait(bar, parity)) return true;
     long long limit = TPT_WAIT_CYCLES;
     if (honour_abort && gflags) {
         const unsigned l = *reinterpret_cast<volatile unsigned *>(gflags + TPT_FLAG_WAIT_LIMIT);
-        if (l) limit = (long long)l;
+        if (l) {  // a limit set by the context: poll without the hardware's suspend, check the clock each time
+            const long long t0 = clock64();
+            while (!mbar_test_wait(bar, parity)) {
+                if (*abort_flag) return false;
+                if (clock64() - t0 > (long long)l) {
+                    *abort_flag = 1;
+                    atomicOr(gflags + TPT_FLAG_TIMEOUT, 1u);
+                    return false;
+                }
+            }
+            return true;
+        }
     }
     const long long t0 = clock64();
     for (uint32_t i = 1;; i++) {
