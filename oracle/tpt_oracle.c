@@ -875,8 +875,7 @@ void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_
 
 /* The fused attention of the encoder plans as this backend defines it
  * (tpt_infer_b200/csrc/attention_det.cu; the reference has no attention
- * operator): per (batch, head), q' = q * scale; s_c = E + O with E (O) the
- * fmaf chain over the even (odd) d in increasing order;
+ * operator): per (batch, head), q' = q * scale; s_c = fmaf over d in order;
  * m = max over the S keys; e_c = exp_det(s_c - m) (0 for the padding slots
  * c >= S up to 128); the 128 slots summed per t = c mod 16 in increasing
  * c / 16, the 16 partials combined by the xor butterfly (o = 8, 4, 2, 1);
@@ -896,13 +895,9 @@ void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float sc
                 for (size_t d = 0; d < D; d++) q[d] = base[r * ld + d] * scale;
                 float m = -INFINITY;
                 for (size_t c = 0; c < 128; c++) {
-                    float ev = 0.0f, od = 0.0f;  /* the even-d and odd-d chains */
+                    float a = 0.0f;
                     if (c < S)
-                        for (size_t d = 0; d < D; d += 2) {
-                            ev = fmaf(q[d], base[c * ld + H * D + d], ev);
-                            od = fmaf(q[d + 1], base[c * ld + H * D + d + 1], od);
-                        }
-                    const float a = ev + od;
+                        for (size_t d = 0; d < D; d++) a = fmaf(q[d], base[c * ld + H * D + d], a);
                     sc[c] = a;
                     if (c < S) m = fmaxf(m, a);
                 }

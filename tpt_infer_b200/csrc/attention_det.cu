@@ -9,9 +9,7 @@
 // The reference has no attention operator (its runtime rejects rank-3/4
 // MatMul, exec.rs:360-362), so this backend defines the arithmetic:
 //   q'  = q * scale                                  (one rounding)
-//   s_c = E + O, E = fmaf over the even d = 0, 2, .., 62 in order of q'_d k_cd
-//         from 0, O the same over the odd d (two chains: one paired fma,
-//         fma.rn.f32x2, advances both)
+//   s_c = fmaf over d = 0 .. 63 in order of q'_d k_cd, from 0
 //   m   = max over the S keys of s_c
 //   e_c = exp_det(s_c - m) for c < S, 0 for the padding keys c >= S
 //         (exp_det: Cody-Waite + Taylor, det_math.cuh)
@@ -20,18 +18,17 @@
 //         p[t] + p[t ^ o], o = 8, 4, 2, 1
 //   p_c = e_c * (1 / sum)                            (the reciprocal correctly rounded)
 //   o_d = fmaf over the 128 key slots in order of p_c v_cd, from 0 (padding
-//         keys have p = 0 and v = 0; columns d, d+1 advance in one paired fma)
+//         keys have p = 0 and v = 0)
 //
-// Kernel: one CTA per (batch, head, block of RQ = 64 or 32 query rows), S <= 128,
-// D = 64, 256 threads as 16 x 16 (ty, tx). Q (scaled), K and V are staged
-// row-major in shared memory by cp.async (row stride 68 floats: 16-byte rows,
-// conflict-free 16-byte reads); thread (ty, tx) computes the scores of query
-// rows ty*RT + i (RT = RQ / 16) against keys tx + 16 j with paired fmas over
-// (even d, odd d), the softmax with half-warp shuffles, writes P row-major as
-// (p, p) pairs into the space of Q and K, and then the context rows ty*RT + i,
-// columns 4 tx .. 4 tx + 3 with paired fmas over column pairs, stored as
-// coalesced 16-byte (or 4-byte int8) row segments. FP32 pipe bound: 4 S^2 D
-// flops per head, all as f32x2 fma (half the FFMA instructions).
+// Kernel: one CTA per (batch, head, block of RQ query rows), S <= 128, D = 64,
+// 256 threads as 16 x 16 (ty, tx). Q (scaled), K and V are staged row-major in
+// shared memory (row stride 68 floats: 16-byte rows, conflict-free float4
+// reads); thread (ty, tx) computes the scores of query rows ty*RT + i
+// (RT = RQ / 16) against keys tx + 16 j in registers (float4 over d), the
+// softmax with half-warp shuffles, writes P row-major into the space of Q and
+// K, and then the context rows ty*RT + i, columns 4 tx .. 4 tx + 3 (float4
+// over keys), stored as coalesced 16-byte (or 4-byte int8) row segments.
+// FP32 pipe bound: 4 S^2 D flops per head, all FFMA.
 #include "common.cuh"
 
 namespace tpt {
@@ -39,27 +36,17 @@ namespace {
 
 constexpr int AD_D = 64, AD_S = 128, AD_T = 256;
 constexpr int AD_LD = AD_D + 4;     // Q/K/V row stride (floats)
-constexpr int AD_PLD2 = 2 * AD_S + 4;  // P row stride in floats, (p, p) pairs
+constexpr int AD_PLD = AD_S + 4;    // P row stride (floats)
 
 template <int RQ>
 struct AdSmem {
     static constexpr int Q = 0;                          // [RQ][AD_LD]
     static constexpr int K = RQ * AD_LD;                 // [AD_S][AD_LD]
-    static constexpr int P = 0;                          // [RQ][AD_PLD2] (p, p) pairs, over Q and K after the scores
-    static constexpr int QK_END = K + AD_S * AD_LD;
-    static constexpr int P_END = RQ * AD_PLD2;
-    static constexpr int V = QK_END > P_END ? QK_END : P_END;  // [AD_S][AD_LD]
+    static constexpr int V = K + AD_S * AD_LD;           // [AD_S][AD_LD]
+    static constexpr int P = 0;                          // [RQ][AD_PLD], over Q and K once the scores are done
     static constexpr int FLOATS = V + AD_S * AD_LD;
+    static_assert(RQ * AD_PLD <= K + AD_S * AD_LD, "P must fit in the space of Q and K");
 };
-
-// paired fma: (d0, d1) = (a0 b0 + c0, a1 b1 + c1), each correctly rounded
-__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ float lo32(unsigned long long v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float hi32(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
 template <int RQ>
 __global__ void __launch_bounds__(AD_T, 2) k_attention_det(const float *__restrict__ qkv, float *__restrict__ out,
@@ -98,23 +85,29 @@ __global__ void __launch_bounds__(AD_T, 2) k_attention_det(const float *__restri
     }
     __syncthreads();
 
-    // scores: rows ty*RT + i, keys tx + 16 j; lane 0 of each pair sums the even d,
-    // lane 1 the odd d, both in increasing d
-    unsigned long long s2[RT][8];
+    // scores: rows ty*RT + i, keys tx + 16 j, d in order
+    float s[RT][8];
 #pragma unroll
     for (int i = 0; i < RT; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) s2[i][j] = 0ull;
+        for (int j = 0; j < 8; j++) s[i][j] = 0.0f;
 #pragma unroll 1
     for (int d4 = 0; d4 < AD_D / 4; d4++) {
-        ulonglong2 k[8];
+        float4 k[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) k[j] = *reinterpret_cast<const ulonglong2 *>(Ks + (tx + 16 * j) * AD_LD + 4 * d4);
+        for (int j = 0; j < 8; j++) k[j] = *reinterpret_cast<const float4 *>(Ks + (tx + 16 * j) * AD_LD + 4 * d4);
 #pragma unroll
         for (int i = 0; i < RT; i++) {
-            const ulonglong2 q = *reinterpret_cast<const ulonglong2 *>(Qs + (ty * RT + i) * AD_LD + 4 * d4);
+            const float4 q = *reinterpret_cast<const float4 *>(Qs + (ty * RT + i) * AD_LD + 4 * d4);
 #pragma unroll
-            for (int j = 0; j < 8; j++) s2[i][j] = fma2(q.y, k[j].y, fma2(q.x, k[j].x, s2[i][j]));
+            for (int j = 0; j < 8; j++) {
+                float a = s[i][j];
+                a = __fmaf_rn(q.x, k[j].x, a);
+                a = __fmaf_rn(q.y, k[j].y, a);
+                a = __fmaf_rn(q.z, k[j].z, a);
+                a = __fmaf_rn(q.w, k[j].w, a);
+                s[i][j] = a;
+            }
         }
     }
     __syncthreads();  // Q and K are dead: P goes over them
@@ -122,62 +115,50 @@ __global__ void __launch_bounds__(AD_T, 2) k_attention_det(const float *__restri
     // softmax of each row over the S keys (half-warp = the 16 threads of one ty)
 #pragma unroll
     for (int i = 0; i < RT; i++) {
-        float sv[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) sv[j] = __fadd_rn(lo32(s2[i][j]), hi32(s2[i][j]));
         float m = -__int_as_float(0x7f800000);
 #pragma unroll
         for (int j = 0; j < 8; j++)
-            if (tx + 16 * j < S) m = fmaxf(m, sv[j]);
+            if (tx + 16 * j < S) m = fmaxf(m, s[i][j]);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float part = 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const float e = tx + 16 * j < S ? exp_det(__fsub_rn(sv[j], m)) : 0.0f;
-            sv[j] = e;
+            const float e = tx + 16 * j < S ? exp_det(__fsub_rn(s[i][j], m)) : 0.0f;
+            s[i][j] = e;
             part = __fadd_rn(part, e);
         }
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
         const float inv = __fdiv_rn(1.0f, part);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float pv = __fmul_rn(sv[j], inv);
-            *reinterpret_cast<float2 *>(Ps + (ty * RT + i) * AD_PLD2 + 2 * (tx + 16 * j)) = make_float2(pv, pv);
-        }
+        for (int j = 0; j < 8; j++) Ps[(ty * RT + i) * AD_PLD + tx + 16 * j] = __fmul_rn(s[i][j], inv);
     }
     __syncthreads();
 
-    // context: rows ty*RT + i, columns 4 tx .. 4 tx + 3 as two pairs, keys in order
-    unsigned long long o2[RT][2];
-#pragma unroll
-    for (int i = 0; i < RT; i++) o2[i][0] = o2[i][1] = 0ull;
-#pragma unroll 2
-    for (int c4 = 0; c4 < AD_S / 4; c4++) {
-        ulonglong2 v[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++)
-            v[jj] = *reinterpret_cast<const ulonglong2 *>(Vs + (4 * c4 + jj) * AD_LD + 4 * tx);
-#pragma unroll
-        for (int i = 0; i < RT; i++) {
-            const ulonglong2 pa = *reinterpret_cast<const ulonglong2 *>(Ps + (ty * RT + i) * AD_PLD2 + 8 * c4);
-            const ulonglong2 pb = *reinterpret_cast<const ulonglong2 *>(Ps + (ty * RT + i) * AD_PLD2 + 8 * c4 + 4);
-            const unsigned long long pp[4] = {pa.x, pa.y, pb.x, pb.y};
-#pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-                o2[i][0] = fma2(pp[jj], v[jj].x, o2[i][0]);
-                o2[i][1] = fma2(pp[jj], v[jj].y, o2[i][1]);
-            }
-        }
-    }
+    // context: rows ty*RT + i, columns 4 tx .. 4 tx + 3, keys in order
     float o[RT][4];
 #pragma unroll
-    for (int i = 0; i < RT; i++) {
-        o[i][0] = lo32(o2[i][0]);
-        o[i][1] = hi32(o2[i][0]);
-        o[i][2] = lo32(o2[i][1]);
-        o[i][3] = hi32(o2[i][1]);
+    for (int i = 0; i < RT; i++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[i][e] = 0.0f;
+#pragma unroll 2
+    for (int c4 = 0; c4 < AD_S / 4; c4++) {
+        float4 v[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) v[jj] = *reinterpret_cast<const float4 *>(Vs + (4 * c4 + jj) * AD_LD + 4 * tx);
+#pragma unroll
+        for (int i = 0; i < RT; i++) {
+            const float4 p = *reinterpret_cast<const float4 *>(Ps + (ty * RT + i) * AD_PLD + 4 * c4);
+            const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                o[i][0] = __fmaf_rn(pv[jj], v[jj].x, o[i][0]);
+                o[i][1] = __fmaf_rn(pv[jj], v[jj].y, o[i][1]);
+                o[i][2] = __fmaf_rn(pv[jj], v[jj].z, o[i][2]);
+                o[i][3] = __fmaf_rn(pv[jj], v[jj].w, o[i][3]);
+            }
+        }
     }
     const size_t ldo = (size_t)H * AD_D;
 #pragma unroll
@@ -204,21 +185,26 @@ int launch_attention_det(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B,
     if (D != AD_D || S <= 0 || S > AD_S || B <= 0 || H <= 0 || B > 65535 || H > 65535 ||
         (((uintptr_t)qkv | (uintptr_t)out) & 15) || ((uintptr_t)q & 3))
         return TPT_UNSUPPORTED;
-    // query rows per CTA: 64, or 32 when that many heads would leave SMs idle
+    // query rows per CTA: 128, or 64 / 32 when that many heads would leave SMs idle
     // (two CTAs fit per SM); the arithmetic per output is the same for every split
     const size_t heads = (size_t)B * H, slots = (size_t)ctx->sm_count * 2;
-    const int rq = heads * 2 >= slots ? 64 : 32;
+    const int rq = heads >= slots ? 128 : (heads * 2 >= slots ? 64 : 32);
     const dim3 grid((unsigned)H, (unsigned)B, (unsigned)((S + rq - 1) / rq));
-    static bool attr[64][2] = {};
-    const int ai = rq == 64 ? 0 : 1;
-    const size_t smem = (rq == 64 ? AdSmem<64>::FLOATS : AdSmem<32>::FLOATS) * sizeof(float);
-    const void *fn = rq == 64 ? (const void *)k_attention_det<64> : (const void *)k_attention_det<32>;
+    static bool attr[64][3] = {};
+    const int ai = rq == 128 ? 0 : (rq == 64 ? 1 : 2);
+    const size_t smem = (rq == 128 ? AdSmem<128>::FLOATS : rq == 64 ? AdSmem<64>::FLOATS : AdSmem<32>::FLOATS) *
+                        sizeof(float);
+    const void *fn = rq == 128 ? (const void *)k_attention_det<128>
+                     : rq == 64 ? (const void *)k_attention_det<64>
+                                : (const void *)k_attention_det<32>;
     if (!attr[ctx->device & 63][ai]) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
         attr[ctx->device & 63][ai] = true;
     }
-    if (rq == 64)
+    if (rq == 128)
+        launch_pdl(k_attention_det<128>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
+    else if (rq == 64)
         launch_pdl(k_attention_det<64>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
     else
         launch_pdl(k_attention_det<32>, grid, AD_T, smem, ctx->stream, qkv, out, S, H, scale, q, qs);
