@@ -138,10 +138,10 @@ def resnet18(x_nchw, spec, batch, scales=None, calib=None):
 
 # ------------------------------------------------------------------ BERT-shaped encoder
 def _attention(qkv, batch, seq, heads, d, scale):
-    """The plan's fused attention, in the device's evaluation order
-    (tpto_attention_det; D = 64)."""
+    """The plan's fused attention, the device's integer tensor-core arithmetic
+    (tpto_attention_i8; D = 64)."""
     assert d == 64
-    return O.attention_det(qkv, batch, seq, heads, scale).reshape(batch * seq, heads * d)
+    return O.attention_i8(qkv, batch, seq, heads, scale).reshape(batch * seq, heads * d)
 
 
 def bert(x, layers_w, batch, seq, scales=None, calib=None, heads=12, hidden=768, ffn=3072, eps=1e-5):

@@ -114,6 +114,7 @@ _sig("tpto_layernorm", None, _f32p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
 _sig("tpto_gelu_det_array", None, _f32p, _sz, _f32p)
 _sig("tpto_exp_det_array", None, _f32p, _sz, _f32p)
 _sig("tpto_attention_det", None, _f32p, _sz, _sz, _sz, C.c_float, _f32p, _sz, _sz)
+_sig("tpto_attention_i8", None, _f32p, _sz, _sz, _sz, C.c_float, _f32p, _sz, _sz)
 _sig("tpto_layernorm_res", None, _f32p, C.c_void_p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
 _sig("tpto_binary", None, C.c_int, _f32p, _szp, _sz, _f32p, _szp, _sz, _f32p, _szp, _sz)
 _sig("tpto_batch_norm", None, _f32p, _sz, _f32p, _f32p, _f32p, _f32p, _sz, _sz, C.c_float, _f32p)
@@ -543,3 +544,13 @@ def layernorm_res(x, res, rows, cols, gamma, beta, eps=1e-5):
     _lib.tpto_layernorm_res(x, r.ctypes.data_as(C.c_void_p), rows, cols, _f32(gamma).ravel(), _f32(beta).ravel(),
                             eps, y)
     return y
+
+
+def attention_i8(qkv, batch, seq, heads, scale, b0=0, b1=None):
+    """The device's integer tensor-core attention (attention_i8.cu), bit-exact;
+    rows of batches [b0, b1) are filled."""
+    qkv = _f32(qkv).ravel()
+    b1 = batch if b1 is None else b1
+    out = np.zeros(batch * seq * heads * 64, np.float32)
+    _lib.tpto_attention_i8(qkv, batch, seq, heads, scale, out, b0, b1)
+    return out

@@ -928,3 +928,122 @@ void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float sc
             }
         }
 }
+
+/* The fused attention of the encoder plans on the integer tensor cores
+ * (tpt_infer_b200/csrc/attention_i8.cu), restated: three 8-bit digits per
+ * value (row scale amax/127 for Q and K rows, column scale for V, 1/127 for P),
+ * exact integer sums of the digit products up to order 2, recombined in f32 in
+ * a fixed order; softmax with exp_det, quarters of 32 keys summed in order then
+ * ((q0 + q1) + q2) + q3. qkv [B*S, 3*H*64], out [B*S, H*64]; batches [b0, b1). */
+static void digits3(float x, float inv, int *d0, int *d1, int *d2) {
+    const float u = x * inv;
+    if (u != u) {
+        *d0 = *d1 = *d2 = 0;
+        return;
+    }
+    const float a = rintf(u);
+    const float r1 = (u - a) * 128.0f;
+    const float b = rintf(r1);
+    const float r2 = (r1 - b) * 128.0f;
+    *d0 = (int)a;
+    *d1 = (int)b;
+    *d2 = (int)rintf(r2);
+}
+
+static float combine3(int32_t t0, int32_t t1, int32_t t2) {
+    float t = (float)t2 * 0x1p-14f;
+    t = fmaf((float)t1, 0x1p-7f, t);
+    return (float)t0 + t;
+}
+
+void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
+                       size_t b1) {
+    (void)B;
+    const size_t D = 64, HD = H * D, ld = 3 * HD;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (size_t b = b0; b < b1; b++)
+        for (size_t h = 0; h < H; h++) {
+            const float *src = qkv + b * S * ld + h * D;
+            static _Thread_local int8_t qd[3][128][64], kd[3][128][64], vd[3][128][64], pd[3][128];
+            static _Thread_local float qsc[128], ksc[128], vps[64];
+            for (size_t r = 0; r < 128; r++)
+                for (int which = 0; which < 2; which++) {
+                    float x[64], amax = 0.0f;
+                    for (size_t d = 0; d < D; d++) {
+                        float v = r < S ? src[r * ld + (which ? HD : 0) + d] : 0.0f;
+                        x[d] = which ? v : v * scale;
+                        amax = fmaxf(amax, fabsf(x[d]));
+                    }
+                    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+                    for (size_t d = 0; d < D; d++) {
+                        int a0, a1, a2;
+                        digits3(x[d], inv, &a0, &a1, &a2);
+                        int8_t(*t)[128][64] = which ? kd : qd;
+                        t[0][r][d] = (int8_t)a0;
+                        t[1][r][d] = (int8_t)a1;
+                        t[2][r][d] = (int8_t)a2;
+                    }
+                    (which ? ksc : qsc)[r] = amax / 127.0f;
+                }
+            for (size_t d = 0; d < D; d++) {
+                float amax = 0.0f;
+                for (size_t c = 0; c < 128; c++) amax = fmaxf(amax, fabsf(c < S ? src[c * ld + 2 * HD + d] : 0.0f));
+                vps[d] = amax / 16129.0f;
+                const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+                for (size_t c = 0; c < 128; c++) {
+                    int e0, e1, e2;
+                    digits3(c < S ? src[c * ld + 2 * HD + d] : 0.0f, inv, &e0, &e1, &e2);
+                    vd[0][c][d] = (int8_t)e0;
+                    vd[1][c][d] = (int8_t)e1;
+                    vd[2][c][d] = (int8_t)e2;
+                }
+            }
+            for (size_t r = 0; r < S; r++) {
+                float sv[128];
+                for (size_t c = 0; c < 128; c++) {
+                    int32_t t0 = 0, t1 = 0, t2 = 0;
+                    for (size_t d = 0; d < D; d++) {
+                        const int a0 = qd[0][r][d], a1 = qd[1][r][d], a2 = qd[2][r][d];
+                        const int c0 = kd[0][c][d], c1 = kd[1][c][d], c2 = kd[2][c][d];
+                        t0 += a0 * c0;
+                        t1 += a0 * c1 + a1 * c0;
+                        t2 += a0 * c2 + a1 * c1 + a2 * c0;
+                    }
+                    sv[c] = combine3(t0, t1, t2) * (qsc[r] * ksc[c]);
+                }
+                float m = -INFINITY;
+                for (size_t c = 0; c < S; c++) m = fmaxf(m, sv[c]);
+                float part[4];
+                for (int q = 0; q < 4; q++) {
+                    float acc = 0.0f;
+                    for (int j = 0; j < 32; j++) {
+                        const size_t c = (size_t)(32 * q + j);
+                        const float e = c < S ? tpto_exp_det(sv[c] - m) : 0.0f;
+                        sv[c] = e;
+                        acc = acc + e;
+                    }
+                    part[q] = acc;
+                }
+                const float rs = 1.0f / (((part[0] + part[1]) + part[2]) + part[3]);
+                for (size_t c = 0; c < 128; c++) {
+                    int p0, p1, p2;
+                    digits3(sv[c] * rs, 127.0f, &p0, &p1, &p2);
+                    pd[0][c] = (int8_t)p0;
+                    pd[1][c] = (int8_t)p1;
+                    pd[2][c] = (int8_t)p2;
+                }
+                float *orow = out + (b * S + r) * HD + h * D;
+                for (size_t d = 0; d < D; d++) {
+                    int32_t u0 = 0, u1 = 0, u2 = 0;
+                    for (size_t c = 0; c < 128; c++) {
+                        const int p0 = pd[0][c], p1 = pd[1][c], p2 = pd[2][c];
+                        const int e0 = vd[0][c][d], e1 = vd[1][c][d], e2 = vd[2][c][d];
+                        u0 += p0 * e0;
+                        u1 += p0 * e1 + p1 * e0;
+                        u2 += p0 * e2 + p1 * e1 + p2 * e0;
+                    }
+                    orow[d] = combine3(u0, u1, u2) * vps[d];
+                }
+            }
+        }
+}

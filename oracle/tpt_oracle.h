@@ -152,6 +152,9 @@ void tpto_layernorm_res(const float *x, const float *res, size_t rows, size_t co
 void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
                         size_t b1);
 
+void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
+                       size_t b1);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,352 @@
+// attention_i8.cu -- fused attention softmax(scale * Q K^T) V per (batch, head)
+// with both products on the integer tensor cores (tcgen05.mma kind::i8, i32
+// accumulators in tensor memory), exact and therefore restatable on the CPU
+// bit for bit (oracle: tpto_attention_i8).
+//
+// Semantics: the composition MatMul -> Softmax -> MatMul of the encoder graph
+// (crates/tpt-infer-ops/src/naive.rs:13-33 and :104-125) on each head; qkv is
+// the packed projection output [B*S, 3*H*D] (Q | K | V along columns), the
+// context [B*S, H*D] (f32, or int8 at the next quantization point's scale).
+// The reference has no attention operator, so this backend defines the
+// arithmetic, with f32-class accuracy (about 2^-22 of each row's largest
+// value):
+//
+//   digits(x[0..n), amax): inv = 127 / amax (0 when amax is 0), for each x:
+//     u = x * inv; d0 = rint(u); r = (u - d0) * 128; d1 = rint(r);
+//     r = (r - d1) * 128; d2 = rint(r)      (NaN -> 0; every step but the
+//     first product exact), so x ~ (d0 + d1/128 + d2/16384) * amax / 127
+//   Q rows: x = q * scale, amax = max |x| over the row;  K rows likewise;
+//   V columns: amax = max |v| over the keys of a head dimension;
+//   T0 = sum_d a0 b0, T1 = sum_d (a0 b1 + a1 b0), T2 = sum_d (a0 b2 + a1 b1 + a2 b0)
+//     (exact integers; the terms of order 3 and 4, below 2^-21, are dropped)
+//   s = (T0 + (T1 * 2^-7 + T2 * 2^-14)) * ((amax_q / 127) * (amax_k / 127)),
+//     as  t = T2 * 2^-14;  t = fmaf(T1, 2^-7, t);  t = T0 + t;  s = t * (sq * sk)
+//   m = max over the S keys; e = exp_det(s - m) (0 for the padding keys);
+//   the 128 key slots summed per quarter of 32 in order, then ((q0 + q1) + q2) + q3;
+//   p = e * (1 / sum); P digits with amax = 1 (u = p * 127);
+//   U0, U1, U2 as T over the 128 key slots (P digits x V digits);
+//   o = (U0 + (U1 * 2^-7 + U2 * 2^-14)) * (amax_v / 16129)
+//
+// The three Q/K digit planes are packed two per 128-byte K-major row, so each
+// sum is one or two K = 128 MMA sequences: QA = [a0 | a1], QB = [a2 | 0],
+// KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]: T0 = QA.KA, T1 = QA.KB,
+// T2 = QA.KC + QB.KA. P and V^T (keys along K) give one 128-byte row per
+// plane: U0 = P0.V0, U1 = P0.V1 + P1.V0, U2 = P0.V2 + P1.V1 + P2.V0.
+//
+// One CTA per (batch, head), S <= 128, D = 64, 512 threads: every thread turns
+// its share of Q, K (a warp per row) and V (a thread per 16 keys of one head
+// dimension) into digit tiles (128B-swizzled, K-major); one thread issues the
+// 16 score MMAs (M = N = 128) into three TMEM accumulators, the softmax reads
+// them (thread = query row and a quarter of the keys) and writes the P digit
+// tiles over Q and K; one thread issues the 24 context MMAs (N = 64); the
+// context leaves through a shared staging tile as coalesced rows. Tensor
+// memory (512 columns) is allocated only after the digit tiles are written, so
+// a second CTA on the SM stages its head while the first one computes. Waits
+// on the MMA commits are bounded; after a timeout the MMAs issued are drained
+// (with the full bound) before tensor memory is freed.
+#include "tc_common.cuh"
+
+namespace tpt {
+namespace {
+using namespace tc;
+
+constexpr int AI_D = 64, AI_S = 128, AI_T = 512;
+constexpr uint32_t AI_TMEM_COLS = 512;                 // T0 [0,128), T1 [128,256), T2 [256,384); U0..U2 over [0,192)
+constexpr uint32_t OFF_QA = 0, OFF_QB = 16384, OFF_KA = 32768, OFF_KB = 49152, OFF_KC = 65536;
+constexpr uint32_t OFF_V0 = 81920, OFF_V1 = 90112, OFF_V2 = 98304;  // V^T digit tiles [64 rows x 128 keys]
+constexpr uint32_t OFF_P0 = 0, OFF_P1 = 16384, OFF_P2 = 32768;     // over QA, QB, KA once the scores are done
+constexpr int AI_OST = AI_D + 4;                                   // output staging row stride (floats)
+constexpr int AI_SMEM = 106496 + 1024;
+
+// byte (row, kb) of a 128B-swizzled K-major tile with 128-byte rows
+__device__ __forceinline__ uint32_t swz(int row, int kb) {
+    return (uint32_t)(row * 128 + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15)));
+}
+
+__host__ __device__ constexpr uint32_t ai_idesc(int m, int n) {  // D s32, A s8, B s8, K-major
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// the three digits of x (see the header); NaN gives 0
+__device__ __forceinline__ void digits3(float x, float inv, int &d0, int &d1, int &d2) {
+    const float u = __fmul_rn(x, inv);
+    if (u != u) {
+        d0 = d1 = d2 = 0;
+        return;
+    }
+    const float a = rintf(u);
+    const float r1 = __fmul_rn(__fsub_rn(u, a), 128.0f);
+    const float b = rintf(r1);
+    const float r2 = __fmul_rn(__fsub_rn(r1, b), 128.0f);
+    d0 = (int)a;
+    d1 = (int)b;
+    d2 = (int)rintf(r2);
+}
+
+__device__ __forceinline__ float combine3(uint32_t t0, uint32_t t1, uint32_t t2) {
+    float t = __fmul_rn((float)(int)t2, 0x1p-14f);
+    t = __fmaf_rn((float)(int)t1, 0x1p-7f, t);
+    return __fadd_rn((float)(int)t0, t);
+}
+
+__device__ __forceinline__ uint32_t pack2(int lo, int hi) { return (uint32_t)(uint8_t)lo | ((uint32_t)(uint8_t)hi << 8); }
+
+__global__ void __launch_bounds__(AI_T, 1)
+    k_attention_i8(const float *__restrict__ qkv, float *__restrict__ out, int S, int H, float scale,
+                   int8_t *__restrict__ qout, float qs, unsigned *gflags) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bars[3];  // scores done, context done, drain
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    __shared__ float red[2][4][AI_S];     // [max | sum][key quarter][row]
+    __shared__ float qsc[AI_S], ksc[AI_S];  // amax / 127 of each Q and K row
+    __shared__ float vmp[8][AI_D];          // per 16-key group column maxima of V
+    __shared__ float vps[AI_D];             // amax_v / 16129 of each head dimension
+
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *g = smem_raw + (base - raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.y, h = blockIdx.x;
+    const int HD = H * AI_D, ld = 3 * HD;
+    const float *src = qkv + (size_t)b * S * ld + h * AI_D;
+    const uint32_t s_bar = smem_u32(&bars[0]), o_bar = smem_u32(&bars[1]), d_bar = smem_u32(&bars[2]);
+    if (tid == 0) {
+        abort_flag = 0;
+        mbar_init(s_bar, 1);
+        mbar_init(o_bar, 1);
+        mbar_init(d_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    pdl_wait();  // the previous kernel's output (qkv) is complete from here on
+    pdl_trigger();
+
+    // ---- Q and K rows: a warp per row, lane = head dimensions 2 lane, 2 lane + 1
+    for (int rr = warp; rr < 2 * AI_S; rr += AI_T / 32) {
+        const bool isq = rr < AI_S;
+        const int r = isq ? rr : rr - AI_S;
+        float2 x = make_float2(0.0f, 0.0f);
+        if (r < S) x = __ldg(reinterpret_cast<const float2 *>(src + (size_t)r * ld + (isq ? 0 : HD)) + lane);
+        if (isq) x = make_float2(__fmul_rn(x.x, scale), __fmul_rn(x.y, scale));
+        const float amax = warp_max(fmaxf(fabsf(x.x), fabsf(x.y)));
+        const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        int a0, a1, a2, c0, c1, c2;
+        digits3(x.x, inv, a0, a1, a2);
+        digits3(x.y, inv, c0, c1, c2);
+        const uint32_t d0 = pack2(a0, c0), d1 = pack2(a1, c1), d2 = pack2(a2, c2);
+        const int kb = 2 * lane;
+        if (isq) {  // QA = [a0 | a1], QB = [a2 | 0]
+            *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, kb)) = (uint16_t)d0;
+            *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, 64 + kb)) = (uint16_t)d1;
+            *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, kb)) = (uint16_t)d2;
+            *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, 64 + kb)) = 0;
+            if (lane == 0) qsc[r] = __fdiv_rn(amax, 127.0f);
+        } else {    // KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]
+            *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, kb)) = (uint16_t)d0;
+            *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, 64 + kb)) = 0;
+            *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, kb)) = (uint16_t)d1;
+            *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, 64 + kb)) = (uint16_t)d0;
+            *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, kb)) = (uint16_t)d2;
+            *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, 64 + kb)) = (uint16_t)d1;
+            if (lane == 0) ksc[r] = __fdiv_rn(amax, 127.0f);
+        }
+    }
+    // ---- V: thread = head dimension d and 16 keys 16 kq .. 16 kq + 15
+    {
+        const int d = tid & (AI_D - 1), kq = tid >> 6;
+        float v[16];
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int c = 16 * kq + i;
+            v[i] = c < S ? __ldg(src + (size_t)c * ld + 2 * HD + d) : 0.0f;
+            m = fmaxf(m, fabsf(v[i]));
+        }
+        vmp[kq][d] = m;
+        __syncthreads();
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) amax = fmaxf(amax, vmp[j][d]);
+        if (kq == 0) vps[d] = __fdiv_rn(amax, 16129.0f);
+        const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            int e0, e1, e2;
+            digits3(v[i], inv, e0, e1, e2);
+            w0[i >> 2] |= (uint32_t)(uint8_t)e0 << (8 * (i & 3));
+            w1[i >> 2] |= (uint32_t)(uint8_t)e1 << (8 * (i & 3));
+            w2[i >> 2] |= (uint32_t)(uint8_t)e2 << (8 * (i & 3));
+        }
+        const uint32_t o = swz(d, 16 * kq);  // V^T row d, keys 16 kq .. 16 kq + 15: one 16-byte chunk
+        *reinterpret_cast<uint4 *>(g + OFF_V0 + o) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+        *reinterpret_cast<uint4 *>(g + OFF_V1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+        *reinterpret_cast<uint4 *>(g + OFF_V2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> the tensor core's reads
+    __syncthreads();
+    if (warp == 0) {  // tensor memory only now: a second CTA on this SM staged its head meanwhile
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(AI_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int *abort_p = &abort_flag;
+
+    if (tid == 0) {  // scores: T0 = QA.KA, T1 = QA.KB, T2 = QA.KC + QB.KA (K = 128 each: 4 MMAs of K = 32)
+        const uint32_t A[4] = {base + OFF_QA, base + OFF_QA, base + OFF_QA, base + OFF_QB};
+        const uint32_t Bm[4] = {base + OFF_KA, base + OFF_KB, base + OFF_KC, base + OFF_KA};
+        const uint32_t Dc[4] = {0u, 128u, 256u, 256u};
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+                tc_mma_i8(tmem + Dc[q], sw128_desc(A[q] + 32 * kk), sw128_desc(Bm[q] + 32 * kk), ai_idesc(128, 128),
+                          (q == 3 || kk > 0) ? 1u : 0u);
+        tc_commit(s_bar);
+    }
+    const int row = (warp & 3) * 32 + lane, qtr = warp >> 2;  // TMEM lane (query row); key / dimension quarter
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    bool ok = __syncthreads_and(mbar_wait(s_bar, 0, abort_p, gflags, true));
+    if (ok) {
+        tc_fence_after();
+        // ---- softmax over this thread's 32 keys qtr*32 .. +31, combined with the other quarters
+        float sv[32];
+        {
+            uint32_t t0[32], t1[32], t2[32];
+            tmem_ld32(lane_base + (uint32_t)(qtr * 32), t0);
+            tmem_ld32(lane_base + 128u + (uint32_t)(qtr * 32), t1);
+            tmem_ld32(lane_base + 256u + (uint32_t)(qtr * 32), t2);
+            tmem_wait_ld();
+            const float sq = qsc[row];
+#pragma unroll
+            for (int j = 0; j < 32; j++) sv[j] = __fmul_rn(combine3(t0[j], t1[j], t2[j]), __fmul_rn(sq, ksc[qtr * 32 + j]));
+        }
+        const int nvalid = S - qtr * 32;  // keys of this quarter below S
+        float m = -__int_as_float(0x7f800000);
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            if (j < nvalid) m = fmaxf(m, sv[j]);
+        red[0][qtr][row] = m;
+        __syncthreads();
+        m = fmaxf(fmaxf(red[0][0][row], red[0][1][row]), fmaxf(red[0][2][row], red[0][3][row]));
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float e = j < nvalid ? exp_det(__fsub_rn(sv[j], m)) : 0.0f;
+            sv[j] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        red[1][qtr][row] = sum;
+        __syncthreads();
+        sum = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0][row], red[1][1][row]), red[1][2][row]), red[1][3][row]);
+        const float rs = __fdiv_rn(1.0f, sum);
+        // P digits (amax 1: u = 127 p) into row `row`, keys qtr*32 .. +31 (two 16-byte chunks per plane)
+#pragma unroll
+        for (int hc = 0; hc < 2; hc++) {
+            uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                int c0, c1, c2;
+                digits3(__fmul_rn(sv[16 * hc + i], rs), 127.0f, c0, c1, c2);
+                w0[i >> 2] |= (uint32_t)(uint8_t)c0 << (8 * (i & 3));
+                w1[i >> 2] |= (uint32_t)(uint8_t)c1 << (8 * (i & 3));
+                w2[i >> 2] |= (uint32_t)(uint8_t)c2 << (8 * (i & 3));
+            }
+            const uint32_t o = swz(row, 32 * qtr + 16 * hc);
+            *reinterpret_cast<uint4 *>(g + OFF_P0 + o) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+            *reinterpret_cast<uint4 *>(g + OFF_P1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+            *reinterpret_cast<uint4 *>(g + OFF_P2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {  // context: U0 = P0.V0, U1 = P0.V1 + P1.V0, U2 = P0.V2 + P1.V1 + P2.V0 (N = 64)
+            const uint32_t A[6] = {base + OFF_P0, base + OFF_P0, base + OFF_P1, base + OFF_P0, base + OFF_P1,
+                                   base + OFF_P2};
+            const uint32_t Bm[6] = {base + OFF_V0, base + OFF_V1, base + OFF_V0, base + OFF_V2, base + OFF_V1,
+                                    base + OFF_V0};
+            const uint32_t Dc[6] = {0u, 64u, 64u, 128u, 128u, 128u};
+            const bool first[6] = {true, true, false, true, false, false};
+#pragma unroll
+            for (int q = 0; q < 6; q++)
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    tc_mma_i8(tmem + Dc[q], sw128_desc(A[q] + 32 * kk), sw128_desc(Bm[q] + 32 * kk),
+                              ai_idesc(128, 64), (!first[q] || kk > 0) ? 1u : 0u);
+            tc_commit(o_bar);
+        }
+        ok = __syncthreads_and(mbar_wait(o_bar, 0, abort_p, gflags, true));
+        if (ok) {
+            tc_fence_after();
+            // ---- context: thread (row, dims qtr*16 .. +15) -> staging [128][AI_OST] -> coalesced rows
+            uint32_t u0[16], u1[16], u2[16];
+            tmem_ld16(lane_base + (uint32_t)(qtr * 16), u0);
+            tmem_ld16(lane_base + 64u + (uint32_t)(qtr * 16), u1);
+            tmem_ld16(lane_base + 128u + (uint32_t)(qtr * 16), u2);
+            tmem_wait_ld();
+            float *st = reinterpret_cast<float *>(g);  // over P (its MMAs are done)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float ov[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int j = 4 * c + e;
+                    ov[e] = __fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[qtr * 16 + j]);
+                }
+                *reinterpret_cast<float4 *>(st + row * AI_OST + qtr * 16 + 4 * c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+            }
+            __syncthreads();
+            for (int i = tid; i < AI_S * (AI_D / 4); i += AI_T) {
+                const int r = i >> 4, c4 = i & 15;
+                if (r >= S) continue;
+                const float4 o = *reinterpret_cast<const float4 *>(st + r * AI_OST + 4 * c4);
+                const size_t off = ((size_t)b * S + r) * HD + h * AI_D + 4 * c4;
+                if (qout)  // the following QUANTIZE, fused: the f32 context is not written
+                    *reinterpret_cast<uint32_t *>(qout + off) =
+                        (uint32_t)(uint8_t)requant_i8(o.x, qs) | ((uint32_t)(uint8_t)requant_i8(o.y, qs) << 8) |
+                        ((uint32_t)(uint8_t)requant_i8(o.z, qs) << 16) | ((uint32_t)(uint8_t)requant_i8(o.w, qs) << 24);
+                else
+                    *reinterpret_cast<float4 *>(out + off) = o;
+            }
+        }
+    }
+    if (!ok && tid == 0) {  // a wait ran out: every MMA issued completes before tensor memory is freed
+        tc_commit(d_bar);
+        mbar_wait(d_bar, 0, abort_p, gflags, false);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AI_TMEM_COLS) : "memory");
+    }
+}
+}  // namespace
+}  // namespace tpt
+
+namespace tpt {
+
+// D = 64 and 0 < S <= 128 (the encoder's shapes); TPT_UNSUPPORTED otherwise.
+int launch_attention_i8(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                        int8_t *q, float qs) {
+    if (D != AI_D || S <= 0 || S > AI_S || B <= 0 || H <= 0 || B > 65535 || H > 65535 ||
+        (((uintptr_t)qkv | (uintptr_t)out) & 15) || ((uintptr_t)q & 3))
+        return TPT_UNSUPPORTED;
+    static bool attr[64] = {};
+    if (!attr[ctx->device & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, AI_SMEM);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
+        attr[ctx->device & 63] = true;
+    }
+    launch_pdl(k_attention_i8, dim3((unsigned)H, (unsigned)B), AI_T, AI_SMEM, ctx->stream, qkv, out, S, H, scale, q, qs,
+               ctx->d_flags);
+    return after_launch(ctx, "attention_i8");
+}
+
+}  // namespace tpt

@@ -1,7 +1,7 @@
 // model_ops.cu -- device ops the model plans need besides the GEMMs:
 // LayerNorm, bias/residual adds, NHWC INT8 conv plumbing (layout change +
 // quantize, im2col), pooling, per-tensor max-abs. The fused attention is in
-// attention_det.cu.
+// attention_i8.cu.
 //
 // Layout inside a plan: activations are row-major [rows, channels] (NHWC for
 // images), so a conv's im2col rows and a GEMM's output rows are both
@@ -412,12 +412,12 @@ int launch_layernorm(tpt_cuda_ctx *ctx, const float *x, const float *g, const fl
     return after_launch(ctx, "layernorm");
 }
 
-int launch_attention_det(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
-                         int8_t *q, float qs);
+int launch_attention_i8(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
+                        int8_t *q, float qs);
 
 int launch_attention(tpt_cuda_ctx *ctx, const float *qkv, float *out, int B, int S, int H, int D, float scale,
                      int8_t *q, float qs) {
-    return launch_attention_det(ctx, qkv, out, B, S, H, D, scale, q, qs);
+    return launch_attention_i8(ctx, qkv, out, B, S, H, D, scale, q, qs);
 }
 
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act) {
