@@ -931,7 +931,8 @@ void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float sc
 
 /* The fused attention of the encoder plans on the integer tensor cores
  * (tpt_infer_b200/csrc/attention_i8.cu), restated: three 8-bit digits per
- * value (row scale amax/127 for Q and K rows, column scale for V, 1/127 for P),
+ * value (scale sc = amax * r127 per Q and K row and per V column, r127 the f32
+ * nearest 1/127, digits of x * (1/sc); P with u = 127 p),
  * exact integer sums of the digit products up to order 2, recombined in f32 in
  * a fixed order; softmax with exp_det, quarters of 32 keys summed in order then
  * ((q0 + q1) + q2) + q3. qkv [B*S, 3*H*64], out [B*S, H*64]; batches [b0, b1). */
@@ -974,7 +975,8 @@ void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float sca
                         x[d] = which ? v : v * scale;
                         amax = fmaxf(amax, fabsf(x[d]));
                     }
-                    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+                    const float sc = amax * 0.00787401572f;
+                    const float inv = amax > 0.0f ? 1.0f / sc : 0.0f;
                     for (size_t d = 0; d < D; d++) {
                         int a0, a1, a2;
                         digits3(x[d], inv, &a0, &a1, &a2);
@@ -983,13 +985,14 @@ void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float sca
                         t[1][r][d] = (int8_t)a1;
                         t[2][r][d] = (int8_t)a2;
                     }
-                    (which ? ksc : qsc)[r] = amax / 127.0f;
+                    (which ? ksc : qsc)[r] = sc;
                 }
             for (size_t d = 0; d < D; d++) {
                 float amax = 0.0f;
                 for (size_t c = 0; c < 128; c++) amax = fmaxf(amax, fabsf(c < S ? src[c * ld + 2 * HD + d] : 0.0f));
-                vps[d] = amax / 16129.0f;
-                const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+                const float sc = amax * 0.00787401572f;
+                vps[d] = sc * 0.00787401572f;
+                const float inv = amax > 0.0f ? 1.0f / sc : 0.0f;
                 for (size_t c = 0; c < 128; c++) {
                     int e0, e1, e2;
                     digits3(c < S ? src[c * ld + 2 * HD + d] : 0.0f, inv, &e0, &e1, &e2);
@@ -1027,7 +1030,7 @@ void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float sca
                 const float rs = 1.0f / (((part[0] + part[1]) + part[2]) + part[3]);
                 for (size_t c = 0; c < 128; c++) {
                     int p0, p1, p2;
-                    digits3(sv[c] * rs, 127.0f, &p0, &p1, &p2);
+                    digits3(sv[c], 127.0f, &p0, &p1, &p2);  /* digits of e; 1 / sum on the context */
                     pd[0][c] = (int8_t)p0;
                     pd[1][c] = (int8_t)p1;
                     pd[2][c] = (int8_t)p2;
@@ -1042,7 +1045,7 @@ void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float sca
                         u1 += p0 * e1 + p1 * e0;
                         u2 += p0 * e2 + p1 * e1 + p2 * e0;
                     }
-                    orow[d] = combine3(u0, u1, u2) * vps[d];
+                    orow[d] = (combine3(u0, u1, u2) * vps[d]) * rs;
                 }
             }
         }

@@ -11,27 +11,28 @@
 // arithmetic, with f32-class accuracy (about 2^-22 of each row's largest
 // value):
 //
-//   digits(x[0..n), amax): inv = 127 / amax (0 when amax is 0), for each x:
+//   digits(x[0..n), amax): sc = amax * r127 (r127 = 1/127 rounded to f32),
+//     inv = 1 / sc (correctly rounded; 0 when amax is 0), for each x:
 //     u = x * inv; d0 = rint(u); r = (u - d0) * 128; d1 = rint(r);
 //     r = (r - d1) * 128; d2 = rint(r)      (NaN -> 0; every step but the
-//     first product exact), so x ~ (d0 + d1/128 + d2/16384) * amax / 127
+//     first product exact), so x ~ (d0 + d1/128 + d2/16384) * sc
 //   Q rows: x = q * scale, amax = max |x| over the row;  K rows likewise;
 //   V columns: amax = max |v| over the keys of a head dimension;
 //   T0 = sum_d a0 b0, T1 = sum_d (a0 b1 + a1 b0), T2 = sum_d (a0 b2 + a1 b1 + a2 b0)
 //     (exact integers; the terms of order 3 and 4, below 2^-21, are dropped)
-//   s = (T0 + (T1 * 2^-7 + T2 * 2^-14)) * ((amax_q / 127) * (amax_k / 127)),
+//   s = (T0 + (T1 * 2^-7 + T2 * 2^-14)) * (sc_q * sc_k),
 //     as  t = T2 * 2^-14;  t = fmaf(T1, 2^-7, t);  t = T0 + t;  s = t * (sq * sk)
 //   m = max over the S keys; e = exp_det(s - m) (0 for the padding keys);
 //   the 128 key slots summed per quarter of 32 in order, then ((q0 + q1) + q2) + q3;
-//   p = e * (1 / sum); P digits with amax = 1 (u = p * 127);
-//   U0, U1, U2 as T over the 128 key slots (P digits x V digits);
-//   o = (U0 + (U1 * 2^-7 + U2 * 2^-14)) * (amax_v / 16129)
+//   E digits with amax = 1 (u = 127 e: each row's largest e is exp(0) = 1);
+//   U0, U1, U2 as T over the 128 key slots (E digits x V digits);
+//   o = ((U0 + (U1 * 2^-7 + U2 * 2^-14)) * (sc_v * r127)) * (1 / sum)
 //
 // The three Q/K digit planes are packed two per 128-byte K-major row, so each
 // sum is one or two K = 128 MMA sequences: QA = [a0 | a1], QB = [a2 | 0],
 // KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]: T0 = QA.KA, T1 = QA.KB,
-// T2 = QA.KC + QB.KA. P and V^T (keys along K) give one 128-byte row per
-// plane: U0 = P0.V0, U1 = P0.V1 + P1.V0, U2 = P0.V2 + P1.V1 + P2.V0.
+// T2 = QA.KC + QB.KA. E and V^T (keys along K) give one 128-byte row per
+// plane: U0 = E0.V0, U1 = E0.V1 + E1.V0, U2 = E0.V2 + E1.V1 + E2.V0.
 //
 // One CTA per (batch, head), S <= 128, D = 64, 512 threads: every thread turns
 // its share of Q, K (a warp per row) and V (a thread per 16 keys of one head
@@ -56,6 +57,7 @@ constexpr uint32_t OFF_QA = 0, OFF_QB = 16384, OFF_KA = 32768, OFF_KB = 49152, O
 constexpr uint32_t OFF_V0 = 81920, OFF_V1 = 90112, OFF_V2 = 98304;  // V^T digit tiles [64 rows x 128 keys]
 constexpr uint32_t OFF_P0 = 0, OFF_P1 = 16384, OFF_P2 = 32768;     // over QA, QB, KA once the scores are done
 constexpr int AI_OST = AI_D + 4;                                   // output staging row stride (floats)
+constexpr float AI_R127 = 0.00787401572f;                          // 1/127 rounded to f32
 constexpr int AI_SMEM = 106496 + 1024;
 
 // byte (row, kb) of a 128B-swizzled K-major tile with 128-byte rows
@@ -99,9 +101,9 @@ __global__ void __launch_bounds__(AI_T, 1)
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     __shared__ float red[2][4][AI_S];     // [max | sum][key quarter][row]
-    __shared__ float qsc[AI_S], ksc[AI_S];  // amax / 127 of each Q and K row
+    __shared__ float qsc[AI_S], ksc[AI_S];  // amax * r127 of each Q and K row
     __shared__ float vmp[8][AI_D];          // per 16-key group column maxima of V
-    __shared__ float vps[AI_D];             // amax_v / 16129 of each head dimension
+    __shared__ float vps[AI_D];             // amax_v * r127 * r127 of each head dimension
 
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -121,34 +123,49 @@ __global__ void __launch_bounds__(AI_T, 1)
     pdl_wait();  // the previous kernel's output (qkv) is complete from here on
     pdl_trigger();
 
-    // ---- Q and K rows: a warp per row, lane = head dimensions 2 lane, 2 lane + 1
-    for (int rr = warp; rr < 2 * AI_S; rr += AI_T / 32) {
-        const bool isq = rr < AI_S;
-        const int r = isq ? rr : rr - AI_S;
-        float2 x = make_float2(0.0f, 0.0f);
-        if (r < S) x = __ldg(reinterpret_cast<const float2 *>(src + (size_t)r * ld + (isq ? 0 : HD)) + lane);
-        if (isq) x = make_float2(__fmul_rn(x.x, scale), __fmul_rn(x.y, scale));
-        const float amax = warp_max(fmaxf(fabsf(x.x), fabsf(x.y)));
-        const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        int a0, a1, a2, c0, c1, c2;
-        digits3(x.x, inv, a0, a1, a2);
-        digits3(x.y, inv, c0, c1, c2);
-        const uint32_t d0 = pack2(a0, c0), d1 = pack2(a1, c1), d2 = pack2(a2, c2);
-        const int kb = 2 * lane;
-        if (isq) {  // QA = [a0 | a1], QB = [a2 | 0]
-            *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, kb)) = (uint16_t)d0;
-            *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, 64 + kb)) = (uint16_t)d1;
-            *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, kb)) = (uint16_t)d2;
-            *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, 64 + kb)) = 0;
-            if (lane == 0) qsc[r] = __fdiv_rn(amax, 127.0f);
-        } else {    // KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]
-            *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, kb)) = (uint16_t)d0;
-            *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, 64 + kb)) = 0;
-            *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, kb)) = (uint16_t)d1;
-            *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, 64 + kb)) = (uint16_t)d0;
-            *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, kb)) = (uint16_t)d2;
-            *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, 64 + kb)) = (uint16_t)d1;
-            if (lane == 0) ksc[r] = __fdiv_rn(amax, 127.0f);
+    // ---- Q and K rows: a warp per row (rows warp + 16 i), lane = head dimensions
+    // 2 lane, 2 lane + 1; all 16 loads of a warp are in flight before the first use
+    {
+        constexpr int RPW = 2 * AI_S / (AI_T / 32);  // rows per warp: 16
+        float2 xs[RPW];
+#pragma unroll
+        for (int i = 0; i < RPW; i++) {
+            const int rr = warp + (AI_T / 32) * i;
+            const bool isq = rr < AI_S;
+            const int r = isq ? rr : rr - AI_S;
+            xs[i] = r < S ? __ldg(reinterpret_cast<const float2 *>(src + (size_t)r * ld + (isq ? 0 : HD)) + lane)
+                          : make_float2(0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int i = 0; i < RPW; i++) {
+            const int rr = warp + (AI_T / 32) * i;
+            const bool isq = rr < AI_S;
+            const int r = isq ? rr : rr - AI_S;
+            float2 x = xs[i];
+            if (isq) x = make_float2(__fmul_rn(x.x, scale), __fmul_rn(x.y, scale));
+            const float amax = warp_max(fmaxf(fabsf(x.x), fabsf(x.y)));
+            const float sc = __fmul_rn(amax, AI_R127);
+            const float inv = amax > 0.0f ? __frcp_rn(sc) : 0.0f;
+            int a0, a1, a2, c0, c1, c2;
+            digits3(x.x, inv, a0, a1, a2);
+            digits3(x.y, inv, c0, c1, c2);
+            const uint32_t d0 = pack2(a0, c0), d1 = pack2(a1, c1), d2 = pack2(a2, c2);
+            const int kb = 2 * lane;
+            if (isq) {  // QA = [a0 | a1], QB = [a2 | 0]
+                *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, kb)) = (uint16_t)d0;
+                *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, 64 + kb)) = (uint16_t)d1;
+                *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, kb)) = (uint16_t)d2;
+                *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, 64 + kb)) = 0;
+                if (lane == 0) qsc[r] = sc;
+            } else {    // KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]
+                *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, kb)) = (uint16_t)d0;
+                *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, 64 + kb)) = 0;
+                *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, kb)) = (uint16_t)d1;
+                *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, 64 + kb)) = (uint16_t)d0;
+                *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, kb)) = (uint16_t)d2;
+                *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, 64 + kb)) = (uint16_t)d1;
+                if (lane == 0) ksc[r] = sc;
+            }
         }
     }
     // ---- V: thread = head dimension d and 16 keys 16 kq .. 16 kq + 15
@@ -167,8 +184,9 @@ __global__ void __launch_bounds__(AI_T, 1)
         float amax = 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; j++) amax = fmaxf(amax, vmp[j][d]);
-        if (kq == 0) vps[d] = __fdiv_rn(amax, 16129.0f);
-        const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const float sc = __fmul_rn(amax, AI_R127);
+        if (kq == 0) vps[d] = __fmul_rn(sc, AI_R127);
+        const float inv = amax > 0.0f ? __frcp_rn(sc) : 0.0f;
         uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int i = 0; i < 16; i++) {
@@ -245,14 +263,15 @@ __global__ void __launch_bounds__(AI_T, 1)
         __syncthreads();
         sum = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0][row], red[1][1][row]), red[1][2][row]), red[1][3][row]);
         const float rs = __fdiv_rn(1.0f, sum);
-        // P digits (amax 1: u = 127 p) into row `row`, keys qtr*32 .. +31 (two 16-byte chunks per plane)
+        // digits of e (amax 1: the row's largest e is exp(0) = 1; u = 127 e) into row `row`,
+        // keys qtr*32 .. +31 (two 16-byte chunks per plane); 1 / sum is applied to the context
 #pragma unroll
         for (int hc = 0; hc < 2; hc++) {
             uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int i = 0; i < 16; i++) {
                 int c0, c1, c2;
-                digits3(__fmul_rn(sv[16 * hc + i], rs), 127.0f, c0, c1, c2);
+                digits3(sv[16 * hc + i], 127.0f, c0, c1, c2);
                 w0[i >> 2] |= (uint32_t)(uint8_t)c0 << (8 * (i & 3));
                 w1[i >> 2] |= (uint32_t)(uint8_t)c1 << (8 * (i & 3));
                 w2[i >> 2] |= (uint32_t)(uint8_t)c2 << (8 * (i & 3));
@@ -297,7 +316,7 @@ __global__ void __launch_bounds__(AI_T, 1)
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const int j = 4 * c + e;
-                    ov[e] = __fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[qtr * 16 + j]);
+                    ov[e] = __fmul_rn(__fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[qtr * 16 + j]), rs);
                 }
                 *reinterpret_cast<float4 *>(st + row * AI_OST + qtr * 16 + 4 * c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
             }
