@@ -91,9 +91,22 @@ __device__ __forceinline__ float combine3(uint32_t t0, uint32_t t1, uint32_t t2)
     return __fadd_rn((float)(int)t0, t);
 }
 
+// 32 lanes x 8 consecutive 32-bit TMEM columns, load and store
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t pack2(int lo, int hi) { return (uint32_t)(uint8_t)lo | ((uint32_t)(uint8_t)hi << 8); }
 
-__global__ void __launch_bounds__(AI_T, 1)
+__global__ void __launch_bounds__(AI_T, 2)
     k_attention_i8(const float *__restrict__ qkv, float *__restrict__ out, int S, int H, float scale,
                    int8_t *__restrict__ qout, float qs, unsigned *gflags) {
     extern __shared__ uint8_t smem_raw[];
@@ -232,55 +245,66 @@ __global__ void __launch_bounds__(AI_T, 1)
     bool ok = __syncthreads_and(mbar_wait(s_bar, 0, abort_p, gflags, true));
     if (ok) {
         tc_fence_after();
-        // ---- softmax over this thread's 32 keys qtr*32 .. +31, combined with the other quarters
-        float sv[32];
-        {
-            uint32_t t0[32], t1[32], t2[32];
-            tmem_ld32(lane_base + (uint32_t)(qtr * 32), t0);
-            tmem_ld32(lane_base + 128u + (uint32_t)(qtr * 32), t1);
-            tmem_ld32(lane_base + 256u + (uint32_t)(qtr * 32), t2);
-            tmem_wait_ld();
-            const float sq = qsc[row];
-#pragma unroll
-            for (int j = 0; j < 32; j++) sv[j] = __fmul_rn(combine3(t0[j], t1[j], t2[j]), __fmul_rn(sq, ksc[qtr * 32 + j]));
-        }
+        // ---- softmax over this thread's 32 keys qtr*32 .. +31, combined with the other quarters.
+        // Pass 1, 8 keys at a time: the scores from T0..T2, their max, the scores
+        // written back over T0 (tcgen05.st) so that few registers stay live.
+        const float sq = qsc[row];
         const int nvalid = S - qtr * 32;  // keys of this quarter below S
         float m = -__int_as_float(0x7f800000);
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (j < nvalid) m = fmaxf(m, sv[j]);
+        for (int ch = 0; ch < 4; ch++) {
+            const uint32_t col = (uint32_t)(qtr * 32 + ch * 8);
+            uint32_t t0[8], t1[8], t2[8];
+            tmem_ld8(lane_base + col, t0);
+            tmem_ld8(lane_base + 128u + col, t1);
+            tmem_ld8(lane_base + 256u + col, t2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float sv = __fmul_rn(combine3(t0[j], t1[j], t2[j]), __fmul_rn(sq, ksc[col + j]));
+                if (ch * 8 + j < nvalid) m = fmaxf(m, sv);
+                t0[j] = __float_as_uint(sv);
+            }
+            tmem_st8(lane_base + col, t0);
+        }
+        tmem_wait_st();
         red[0][qtr][row] = m;
         __syncthreads();
         m = fmaxf(fmaxf(red[0][0][row], red[0][1][row]), fmaxf(red[0][2][row], red[0][3][row]));
+        // Pass 2: e = exp_det(s - m) summed in key order; the digits of e (amax 1: the
+        // row's largest e is exp(0) = 1; u = 127 e) into row `row`, keys qtr*32 .. +31,
+        // two 16-byte chunks per plane; 1 / sum is applied to the context
         float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const float e = j < nvalid ? exp_det(__fsub_rn(sv[j], m)) : 0.0f;
-            sv[j] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        red[1][qtr][row] = sum;
-        __syncthreads();
-        sum = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0][row], red[1][1][row]), red[1][2][row]), red[1][3][row]);
-        const float rs = __fdiv_rn(1.0f, sum);
-        // digits of e (amax 1: the row's largest e is exp(0) = 1; u = 127 e) into row `row`,
-        // keys qtr*32 .. +31 (two 16-byte chunks per plane); 1 / sum is applied to the context
 #pragma unroll
         for (int hc = 0; hc < 2; hc++) {
             uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                int c0, c1, c2;
-                digits3(sv[16 * hc + i], 127.0f, c0, c1, c2);
-                w0[i >> 2] |= (uint32_t)(uint8_t)c0 << (8 * (i & 3));
-                w1[i >> 2] |= (uint32_t)(uint8_t)c1 << (8 * (i & 3));
-                w2[i >> 2] |= (uint32_t)(uint8_t)c2 << (8 * (i & 3));
+            for (int hh = 0; hh < 2; hh++) {
+                const int k0 = hc * 16 + hh * 8;
+                uint32_t sv8[8];
+                tmem_ld8(lane_base + (uint32_t)(qtr * 32 + k0), sv8);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float e = k0 + j < nvalid ? exp_det(__fsub_rn(__uint_as_float(sv8[j]), m)) : 0.0f;
+                    sum = __fadd_rn(sum, e);
+                    int c0, c1, c2;
+                    digits3(e, 127.0f, c0, c1, c2);
+                    const int i = hh * 8 + j;
+                    w0[i >> 2] |= (uint32_t)(uint8_t)c0 << (8 * (i & 3));
+                    w1[i >> 2] |= (uint32_t)(uint8_t)c1 << (8 * (i & 3));
+                    w2[i >> 2] |= (uint32_t)(uint8_t)c2 << (8 * (i & 3));
+                }
             }
             const uint32_t o = swz(row, 32 * qtr + 16 * hc);
             *reinterpret_cast<uint4 *>(g + OFF_P0 + o) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
             *reinterpret_cast<uint4 *>(g + OFF_P1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
             *reinterpret_cast<uint4 *>(g + OFF_P2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
         }
+        red[1][qtr][row] = sum;
+        __syncthreads();
+        sum = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0][row], red[1][1][row]), red[1][2][row]), red[1][3][row]);
+        const float rs = __fdiv_rn(1.0f, sum);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         __syncthreads();
@@ -304,21 +328,25 @@ __global__ void __launch_bounds__(AI_T, 1)
         if (ok) {
             tc_fence_after();
             // ---- context: thread (row, dims qtr*16 .. +15) -> staging [128][AI_OST] -> coalesced rows
-            uint32_t u0[16], u1[16], u2[16];
-            tmem_ld16(lane_base + (uint32_t)(qtr * 16), u0);
-            tmem_ld16(lane_base + 64u + (uint32_t)(qtr * 16), u1);
-            tmem_ld16(lane_base + 128u + (uint32_t)(qtr * 16), u2);
-            tmem_wait_ld();
-            float *st = reinterpret_cast<float *>(g);  // over P (its MMAs are done)
+            float *st = reinterpret_cast<float *>(g);  // over the E tiles (their MMAs are done)
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float ov[4];
+            for (int ch = 0; ch < 2; ch++) {
+                const uint32_t col = (uint32_t)(qtr * 16 + ch * 8);
+                uint32_t u0[8], u1[8], u2[8];
+                tmem_ld8(lane_base + col, u0);
+                tmem_ld8(lane_base + 64u + col, u1);
+                tmem_ld8(lane_base + 128u + col, u2);
+                tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int j = 4 * c + e;
-                    ov[e] = __fmul_rn(__fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[qtr * 16 + j]), rs);
+                for (int c = 0; c < 2; c++) {
+                    float ov[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int j = 4 * c + e;
+                        ov[e] = __fmul_rn(__fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[col + j]), rs);
+                    }
+                    *reinterpret_cast<float4 *>(st + row * AI_OST + col + 4 * c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
                 }
-                *reinterpret_cast<float4 *>(st + row * AI_OST + qtr * 16 + 4 * c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
             }
             __syncthreads();
             for (int i = tid; i < AI_S * (AI_D / 4); i += AI_T) {
