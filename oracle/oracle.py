@@ -113,7 +113,6 @@ _sig("tpto_add_bias_rows", None, _f32p, _sz, _sz, _f32p)
 _sig("tpto_layernorm", None, _f32p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
 _sig("tpto_gelu_det_array", None, _f32p, _sz, _f32p)
 _sig("tpto_exp_det_array", None, _f32p, _sz, _f32p)
-_sig("tpto_attention_det", None, _f32p, _sz, _sz, _sz, C.c_float, _f32p, _sz, _sz)
 _sig("tpto_attention_i8", None, _f32p, _sz, _sz, _sz, C.c_float, _f32p, _sz, _sz)
 _sig("tpto_layernorm_res", None, _f32p, C.c_void_p, _sz, _sz, _f32p, _f32p, C.c_float, _f32p)
 _sig("tpto_binary", None, C.c_int, _f32p, _szp, _sz, _f32p, _szp, _sz, _f32p, _szp, _sz)
@@ -523,16 +522,6 @@ def exp_det(a):
     a = _f32(a).ravel()
     out = np.empty(a.size, np.float32)
     _lib.tpto_exp_det_array(a, a.size, out)
-    return out
-
-
-def attention_det(qkv, batch, seq, heads, scale, b0=0, b1=None):
-    """The device's fused attention (attention_det.cu order), bit-exact; rows of
-    batches [b0, b1) are filled (the rest of the output stays zero)."""
-    qkv = _f32(qkv).ravel()
-    b1 = batch if b1 is None else b1
-    out = np.zeros(batch * seq * heads * 64, np.float32)
-    _lib.tpto_attention_det(qkv, batch, seq, heads, scale, out, b0, b1)
     return out
 
 

@@ -873,61 +873,6 @@ void tpto_concat_copy_one(float *out, size_t c_total, size_t c_offset, size_t c_
     for (size_t o = 0; o < outer; o++) memcpy(out + o * ob + c_offset * inner, src + o * sb, sb * 4);
 }
 
-/* The fused attention of the encoder plans as this backend defines it
- * (tpt_infer_b200/csrc/attention_det.cu; the reference has no attention
- * operator): per (batch, head), q' = q * scale; s_c = fmaf over d in order;
- * m = max over the S keys; e_c = exp_det(s_c - m) (0 for the padding slots
- * c >= S up to 128); the 128 slots summed per t = c mod 16 in increasing
- * c / 16, the 16 partials combined by the xor butterfly (o = 8, 4, 2, 1);
- * p_c = e_c * (1 / sum); o_d = fmaf over the 128 slots in order (padding
- * p = 0, v = 0). qkv [B*S, 3*H*D], out [B*S, H*D], D = 64, S <= 128. Rows of
- * the batch range [b0, b1) only. */
-void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
-                        size_t b1) {
-    (void)B;
-    const size_t D = 64, ld = 3 * H * D;
-    float q[64], sc[128], p[128];
-#pragma omp parallel for collapse(2) private(q, sc, p) schedule(static)
-    for (size_t b = b0; b < b1; b++)
-        for (size_t h = 0; h < H; h++) {
-            const float *base = qkv + b * S * ld + h * D;
-            for (size_t r = 0; r < S; r++) {
-                for (size_t d = 0; d < D; d++) q[d] = base[r * ld + d] * scale;
-                float m = -INFINITY;
-                for (size_t c = 0; c < 128; c++) {
-                    float a = 0.0f;
-                    if (c < S)
-                        for (size_t d = 0; d < D; d++) a = fmaf(q[d], base[c * ld + H * D + d], a);
-                    sc[c] = a;
-                    if (c < S) m = fmaxf(m, a);
-                }
-                float part[16];
-                for (int t = 0; t < 16; t++) {
-                    float acc = 0.0f;
-                    for (int j = 0; j < 8; j++) {
-                        size_t c = (size_t)t + 16 * (size_t)j;
-                        float e = c < S ? tpto_exp_det(sc[c] - m) : 0.0f;
-                        sc[c] = e;
-                        acc = acc + e;
-                    }
-                    part[t] = acc;
-                }
-                for (int o = 8; o > 0; o >>= 1) {
-                    float tmp[16];
-                    for (int t = 0; t < 16; t++) tmp[t] = part[t] + part[t ^ o];
-                    memcpy(part, tmp, sizeof tmp);
-                }
-                const float inv = 1.0f / part[0];
-                for (size_t c = 0; c < 128; c++) p[c] = sc[c] * inv;
-                float *orow = out + (b * S + r) * H * D + h * D;
-                for (size_t d = 0; d < D; d++) {
-                    float a = 0.0f;
-                    for (size_t c = 0; c < 128; c++) a = fmaf(p[c], c < S ? base[c * ld + 2 * H * D + d] : 0.0f, a);
-                    orow[d] = a;
-                }
-            }
-        }
-}
 
 /* The fused attention of the encoder plans on the integer tensor cores
  * (tpt_infer_b200/csrc/attention_i8.cu), restated: three 8-bit digits per

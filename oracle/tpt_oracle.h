@@ -149,8 +149,6 @@ void tpto_exp_det_array(const float *a, size_t n, float *out);
 void tpto_layernorm_res(const float *x, const float *res, size_t rows, size_t cols, const float *gamma,
                         const float *beta, float eps, float *y);
 
-void tpto_attention_det(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
-                        size_t b1);
 
 void tpto_attention_i8(const float *qkv, size_t B, size_t S, size_t H, float scale, float *out, size_t b0,
                        size_t b1);
