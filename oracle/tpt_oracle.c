@@ -290,7 +290,7 @@ static float gelu1(float x) {
 /* The device's deterministic exp / reciprocal / GELU (tpt_infer_b200/csrc/
  * det_math.cuh), restated with the same correctly rounded operations in the
  * same order: Cody-Waite reduction + degree-7 Taylor polynomial for exp,
- * three Newton steps from 48/17 - 32/17 h for 1/d on [1, 2], and
+ * three Newton steps from 24/17 - 8/17 d for 1/d on [1, 2], and
  * GELU = x w / (1 + t) with t = exp(-2 |inner|). Used by the W8A8 epilogue's
  * GELU and the attention softmax, which this backend defines. */
 float tpto_exp_det(float x) {
@@ -317,10 +317,9 @@ float tpto_exp_det(float x) {
 }
 
 static float recip12_det(float d) {
-    const float h = d * 0.5f;
-    float r = fmaf(h, -1.88235295f, 2.82352948f);
-    for (int i = 0; i < 3; i++) r = fmaf(r, fmaf(-h, r, 1.0f), r);
-    return r * 0.5f;
+    float r = fmaf(d, -0.470588237f, 1.41176474f);
+    for (int i = 0; i < 3; i++) r = fmaf(r, fmaf(-d, r, 1.0f), r);
+    return r;
 }
 
 float tpto_gelu_det(float x) {

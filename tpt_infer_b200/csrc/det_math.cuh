@@ -15,10 +15,9 @@
 // x in [-87, 88]; 0 below -87 (the softmax terms there are < 2^-125 of the
 // row's largest), +inf above 88, NaN propagates.
 //
-// recip12_det(d): 1/d for d in [1, 2] by Newton-Raphson on h = d/2 in [0.5, 1]
-// from the linear start 48/17 - 32/17 h (maximum relative error 1/17), three
-// steps (error < 2e-10 before the last rounding), halved at the end. Not
-// correctly rounded, but deterministic.
+// recip12_det(d): 1/d for d in [1, 2] by Newton-Raphson from the linear start
+// 24/17 - 8/17 d (maximum relative error 1/17), three steps (error < 2e-10
+// before the last rounding). Not correctly rounded, but deterministic.
 //
 // gelu_det(x): the tanh form of naive.rs:137-146, inner = K (x + C x x x) with
 // the same association, and 0.5 x (1 + tanh(inner)) written without tanh: with
@@ -37,13 +36,14 @@ constexpr float DET_C2 = 0.5f, DET_C3 = 0.166666672f, DET_C4 = 0.0416666679f, DE
                 DET_C6 = 0.00138888892f, DET_C7 = 0.000198412701f;  // 1/k!
 
 __device__ __forceinline__ float exp_det(float x) {
-    if (!(x >= -87.0f)) return x != x ? x : 0.0f;
-    if (x > 88.0f) return __int_as_float(0x7f800000);
+    // the range cases by selects, not branches: the polynomial runs on x clamped
+    // to [-87, 88] and the result is replaced below / above / for NaN
+    const float xc = fminf(fmaxf(x, -87.0f), 88.0f);
     // n = x log2 e rounded to an integer inside one fma: adding 1.5 * 2^23 leaves
     // ulp 1, so the sum's low mantissa bits are n (two's complement offset)
-    const float t = __fmaf_rn(x, DET_LOG2E, 12582912.0f);
+    const float t = __fmaf_rn(xc, DET_LOG2E, 12582912.0f);
     const float n = __fsub_rn(t, 12582912.0f);
-    float r = __fmaf_rn(n, -DET_LN2_HI, x);
+    float r = __fmaf_rn(n, -DET_LN2_HI, xc);
     r = __fmaf_rn(n, -DET_LN2_LO, r);
     float p = DET_C7;
     p = __fmaf_rn(p, r, DET_C6);
@@ -53,15 +53,19 @@ __device__ __forceinline__ float exp_det(float x) {
     p = __fmaf_rn(p, r, DET_C2);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    return __fmul_rn(p, __int_as_float((__float_as_int(t) - 0x4B400000 + 127) << 23));
+    float y = __fmul_rn(p, __int_as_float((__float_as_int(t) - 0x4B400000 + 127) << 23));
+    y = x < -87.0f ? 0.0f : y;
+    y = x > 88.0f ? __int_as_float(0x7f800000) : y;
+    return x != x ? x : y;
 }
 
+// 1/d for d in [1, 2]: Newton-Raphson r <- r + r (1 - d r) from the linear start
+// 24/17 - 8/17 d (relative error at most 1/17), three steps
 __device__ __forceinline__ float recip12_det(float d) {
-    const float h = __fmul_rn(d, 0.5f);
-    float r = __fmaf_rn(h, -1.88235295f, 2.82352948f);  // 48/17 - 32/17 h
+    float r = __fmaf_rn(d, -0.470588237f, 1.41176474f);
 #pragma unroll
-    for (int i = 0; i < 3; i++) r = __fmaf_rn(r, __fmaf_rn(-h, r, 1.0f), r);
-    return __fmul_rn(r, 0.5f);
+    for (int i = 0; i < 3; i++) r = __fmaf_rn(r, __fmaf_rn(-d, r, 1.0f), r);
+    return r;
 }
 
 __device__ __forceinline__ float gelu_det(float x) {
