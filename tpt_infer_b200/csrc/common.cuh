@@ -64,7 +64,7 @@ struct tpt_cuda_weights {
     // once: boxes of 128 / 64 / 32 rows x 128 bytes (the small-M kernel's
     // weight tile, and the SM-pair kernel's B half-tiles for tile N = 256 /
     // 128 / 64)
-    alignas(64) unsigned char tmaps[3][128];
+    alignas(64) unsigned char tmaps[4][128];  // int8 weights: TMA boxes of 128 / 64 / 32 / 96 rows x 128 B
     bool tmap_ok = false;
 };
 

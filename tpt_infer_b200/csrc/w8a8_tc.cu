@@ -63,7 +63,7 @@ constexpr int P_THREADS = (2 + P_EPI_WARPS) * 32;
 constexpr int P_A_BYTES = 128 * TC_BK;    // this CTA's 128 rows of A
 constexpr int P_OUT_BYTES = P_EPI_WARPS * 2 * 4096;
 
-// Tile N (the MMA's N) is a template parameter: 64, 128 or 256. Each CTA holds
+// Tile N (the MMA's N) is a template parameter: 64, 128, 192 or 256. Each CTA holds
 // BN/2 rows of B per stage; the ring is sized to ~160 KB.
 template <int BN>
 struct PairCfg {
@@ -71,10 +71,11 @@ struct PairCfg {
     static constexpr int STAGE_BYTES = P_A_BYTES + B_BYTES;
     static constexpr int STAGES_RAW = 163840 / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    // two accumulators of BN columns, rounded up to a power of two (the allocation unit)
+    static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + P_OUT_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "dynamic shared memory per CTA");
-    static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
+    static_assert(BN == 64 || BN == 128 || BN == 192 || BN == 256, "tile N");
 };
 
 // 2-SM TMA load: data into this CTA's shared memory, transaction bytes
@@ -442,8 +443,8 @@ bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uin
 
 int build_weight_tmap(tpt_cuda_weights *w) {
     bool ok = w->kind == 8 && w->n <= 0x7fffffff && w->k <= 0x7fffffff;
-    const uint32_t rows[3] = {128, 64, 32};
-    for (int i = 0; i < 3 && ok; i++)
+    const uint32_t rows[4] = {128, 64, 32, 96};
+    for (int i = 0; i < 4 && ok; i++)
         ok = make_tmap_i8(reinterpret_cast<CUtensorMap *>(w->tmaps[i]), w->data, w->n, w->k, rows[i]);
     w->tmap_ok = ok;
     return TPT_OK;
@@ -467,14 +468,14 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     const int M = (int)m, N = (int)w->n, K = (int)w->k;
     const long long pairs = ctx->sm_count / 2 > 0 ? ctx->sm_count / 2 : 1;
     const long long mt = (M + P_BM - 1) / P_BM;
-    const int widths[3] = {256, 128, 64};
-    const double cost[3] = {1.0, 1.6, 2.6};
+    const int widths[4] = {256, 192, 128, 64};
+    const double cost[4] = {1.0, 1.0, 1.6, 2.6};
     // the narrow-tile penalty is an operand-bandwidth cost of the k loop: it
     // fades for short K, where the epilogue (per output, any width) dominates
     const double kw = K < 4096 ? (double)K / 4096.0 : 1.0;
     int bn = 256;
     double best = 0.0;
-    for (int i = 0; i < 3; i++) {
+    for (int i = 0; i < 4; i++) {
         const long long tiles = mt * ((N + widths[i] - 1) / widths[i]);
         const double t = (double)((tiles + pairs - 1) / pairs) * widths[i] * (1.0 + (cost[i] - 1.0) * kw);
         if (i == 0 || t < best) {
@@ -482,8 +483,11 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
             bn = widths[i];
         }
     }
-    // each CTA's B box holds BN/2 rows: tmaps[0..2] are the 128 / 64 / 32-row boxes
+    // each CTA's B box holds BN/2 rows: tmaps[0..3] are the 128 / 64 / 32 / 96-row boxes
     const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(w->tmaps);
+    if (bn == 192)
+        return acc ? launch_tc2<192, true>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
+                   : launch_tc2<192, false>(ctx, ta, maps[3], M, N, K, a_scale, w->scales, bias, act, y, acc, rq);
     if (bn == 64)
         return acc ? launch_tc2<64, true>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc, rq)
                    : launch_tc2<64, false>(ctx, ta, maps[2], M, N, K, a_scale, w->scales, bias, act, y, acc, rq);
