@@ -469,7 +469,9 @@ int launch_w8a8_tc(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, const tpt_cuda_
     const long long pairs = ctx->sm_count / 2 > 0 ? ctx->sm_count / 2 : 1;
     const long long mt = (M + P_BM - 1) / P_BM;
     const int widths[4] = {256, 192, 128, 64};
-    const double cost[4] = {1.0, 1.0, 1.6, 2.6};
+    // per-column cost of a round at long K, from the operand bytes per MMA
+    // (measured for 192: 12.8 us per round against 14.6 for 256 at 4096^3)
+    const double cost[4] = {1.0, 1.17, 1.6, 2.6};
     // the narrow-tile penalty is an operand-bandwidth cost of the k loop: it
     // fades for short K, where the epilogue (per output, any width) dominates
     const double kw = K < 4096 ? (double)K / 4096.0 : 1.0;
