@@ -69,26 +69,41 @@ __host__ __device__ constexpr uint32_t ai_idesc(int m, int n) {  // D s32, A s8,
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// the three digits of x (see the header); NaN gives 0
+// round to the nearest integer (ties to even, as rintf) for |u| < 2^22 by one
+// add of 1.5 * 2^23, whose sum has ulp 1: the float result and the integer in
+// its low mantissa bits, on the FMA and integer pipes (no conversion unit)
+__device__ __forceinline__ float rint_magic(float u, int &i) {
+    const float t = __fadd_rn(u, 12582912.0f);
+    i = __float_as_int(t) - 0x4B400000;
+    return __fsub_rn(t, 12582912.0f);
+}
+// exact int -> float for |i| < 2^22, the same way back
+__device__ __forceinline__ float i2f_magic(uint32_t i) {
+    return __fsub_rn(__int_as_float((int)i + 0x4B400000), 12582912.0f);
+}
+
+// the three digits of x (see the header); NaN gives 0. |u| <= 127 and the two
+// residuals are in [-64, 64], so the rounding by addition equals rintf
 __device__ __forceinline__ void digits3(float x, float inv, int &d0, int &d1, int &d2) {
     const float u = __fmul_rn(x, inv);
     if (u != u) {
         d0 = d1 = d2 = 0;
         return;
     }
-    const float a = rintf(u);
+    const float a = rint_magic(u, d0);
     const float r1 = __fmul_rn(__fsub_rn(u, a), 128.0f);
-    const float b = rintf(r1);
+    const float b = rint_magic(r1, d1);
     const float r2 = __fmul_rn(__fsub_rn(r1, b), 128.0f);
-    d0 = (int)a;
-    d1 = (int)b;
-    d2 = (int)rintf(r2);
+    rint_magic(r2, d2);
 }
 
+// every accumulator is below 2^22 in magnitude (|T| <= 64 (2 * 127 * 64 + 64 * 64)
+// about 1.3e6, |U| <= 128 (2 * 127 * 64 + 64 * 64) about 2.6e6), so the
+// conversions are exact
 __device__ __forceinline__ float combine3(uint32_t t0, uint32_t t1, uint32_t t2) {
-    float t = __fmul_rn((float)(int)t2, 0x1p-14f);
-    t = __fmaf_rn((float)(int)t1, 0x1p-7f, t);
-    return __fadd_rn((float)(int)t0, t);
+    float t = __fmul_rn(i2f_magic(t2), 0x1p-14f);
+    t = __fmaf_rn(i2f_magic(t1), 0x1p-7f, t);
+    return __fadd_rn(i2f_magic(t0), t);
 }
 
 // 32 lanes x 8 consecutive 32-bit TMEM columns, load and store
