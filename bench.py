@@ -535,6 +535,33 @@ def profile_kernels(args):
     pa.run({tq: synth.normal(B * S * 3 * 768, 45)}, [to])
     out["attention_64x128x12_us"] = _time_device(stream, pa.run_device, args.steps, args.warmup, flush) * 1e6
     pa.close()
+    # BERT's FFN GEMMs over 64 x 128 tokens, each behind its input's QUANTIZE:
+    # FFN1 (768 -> 3072, GELU, int8 output at FFN2's frozen quantization point)
+    # and FFN2 (3072 -> 768, f32 output)
+    T = B * S
+    for name, n_, k_, act_, q_out in (("bert_ffn1_gelu_q8", 3072, 768, graphs.ACT_GELU, True),
+                                      ("bert_ffn2", 768, 3072, graphs.ACT_NONE, False)):
+        ql = graphs.make_qlinear(be, n_, k_, 5100 + n_, 0.02, 0.01)
+        pf = graphs.Plan(be)
+        wh = be.upload_i8(ql.q, ql.scales, ql.n, ql.k)
+        pf.weights.append(wh)
+        tx = pf.tensor(graphs.F32, T * k_)
+        txq = pf.tensor(graphs.I8, T * k_)
+        ty = pf.tensor(graphs.F32, T * n_)
+        pf.op(graphs.OP_QUANTIZE, tx, txq, dims=(T * k_,))
+        pf.op(graphs.OP_LINEAR, txq, ty, in1=pf.const(ql.bias), w=wh, act=act_, dims=(T,))
+        last = ty
+        if q_out:
+            tyq = pf.tensor(graphs.I8, T * n_)
+            pf.op(graphs.OP_QUANTIZE, ty, tyq, dims=(T * n_,))
+            last = tyq
+        pf.finalize()
+        pf.calibrate(True)
+        pf.run({tx: synth.normal(T * k_, 46)}, [last])
+        pf.freeze()
+        pf.run({tx: synth.normal(T * k_, 47)}, [last])
+        out[f"{name}_us_with_quantize"] = _time_device(stream, pf.run_device, args.steps, args.warmup, flush) * 1e6
+        pf.close()
     for name, shape, ohw in (("conv_stage1_b64", (64, 56, 56, 64, 64, 3, 1, 1), None),
                              ("conv_stem_b64", (64, 112, 112, 16, 64, 4, 1, 2), (112, 112))):
         pc = _conv_plan(be, *shape, seed=3100, out_hw=ohw)

@@ -322,23 +322,53 @@ __device__ __forceinline__ int8_t requant_i8(float y, float scale) {
 // which turns a faithful quotient into the correctly rounded one, the IEEE
 // quotient, whenever the residual is exact. The residual can be inexact only
 // when it underflows, for quotients far below 0.5 that round to 0 either way;
-// |y| > 2^80 clamps to +-127 whatever the quotient, and NaN gives 0. Rounding
-// is half away from zero (roundf) on the value clamped to [-128, 128], with no
-// branch, so the 32 values of an epilogue chunk interleave.
+// |y| > 2^80 clamps to +-127 whatever the quotient. Rounding half away from
+// zero (roundf): trunc(q + copysign(0.5 - 2^-25, q)) equals roundf(q) for every
+// float below 2^31 in magnitude (checked exhaustively), the truncating
+// conversion saturates above that and takes NaN to 0, and the integer clamp
+// gives [-127, 127]. No branch, so the 32 values of an epilogue chunk interleave.
 __device__ __forceinline__ bool requant_fast_ok(float s) { return s >= 0x1p-40f && s <= 0x1p40f; }
 __device__ __forceinline__ int8_t requant_i8_fast(float y, float s, float rs) {
     const float q1 = __fmul_rn(y, rs);
     const float q2 = __fmaf_rn(__fmaf_rn(-s, q1, y), rs, q1);
     float q = __fmaf_rn(__fmaf_rn(-s, q2, y), rs, q2);
     q = fabsf(y) <= 0x1p80f ? q : y;
-    const float f = __fsub_rn(q, truncf(q));  // exact, the sign of q; NaN for NaN and +-inf
-    // truncation saturates to the int32 range and takes NaN to 0 (cvt.rzi.s32.f32)
-    int n = __float2int_rz(q) + (f >= 0.5f ? 1 : 0) - (f <= -0.5f ? 1 : 0);
+    const float h = __fadd_rn(q, copysignf(0.49999997f, q));
+    int n = __float2int_rz(h);  // cvt.rzi.s32.f32: saturating, NaN -> 0
     n = n > 127 ? 127 : (n < -127 ? -127 : n);
     return (int8_t)n;
 }
 // out of line: the dividing path of the wide epilogues (scales outside the fast range)
 static __device__ __noinline__ int8_t requant_i8_outline(float y, float s) { return requant_i8(y, s); }
+
+// The W8A8 epilogue and the int8 requantization of one 32-column chunk of one
+// row, fused: qb[j/4] byte j%4 = requant_i8(act((float)acc[j] * cs[j] +
+// cs[32 + j]), qs), with cs[j] = a_scale * ws[n0 + j] and cs[32 + j] =
+// bias[n0 + j] staged in shared memory by the warp (each lane computes one
+// column's product once, instead of every lane all 32): the same operations in
+// the same order as w8a8_epi32 followed by requant_pack32. HAS_BIAS false
+// skips the add (adding 0 would turn -0 into +0). FAST: the division-free
+// requantization (requant_fast_ok(qs)), else the dividing one.
+template <int ACT, bool FAST>
+__device__ __forceinline__ void w8a8_epi_q32(const uint32_t (&v)[32], const float *cs, bool has_bias, float qs,
+                                             float rqs, uint32_t (&qb)[8]) {
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        const float4 s4 = reinterpret_cast<const float4 *>(cs)[g];
+        const float4 b4 = reinterpret_cast<const float4 *>(cs + 32)[g];
+        const float sc[4] = {s4.x, s4.y, s4.z, s4.w}, bi[4] = {b4.x, b4.y, b4.z, b4.w};
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float y = __fmul_rn(__int2float_rn((int)v[4 * g + i]), sc[i]);
+            if (has_bias) y = __fadd_rn(y, bi[i]);
+            y = act_t<ACT>(y);
+            const int8_t q8 = FAST ? requant_i8_fast(y, qs, rqs) : requant_i8_outline(y, qs);
+            word |= (uint32_t)(uint8_t)q8 << (8 * i);
+        }
+        qb[g] = word;
+    }
+}
 
 // requant_i8 of 32 values (f32 bits) packed 4 to a word, low byte first
 __device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s, float rs, bool fast,

@@ -59,6 +59,28 @@ __device__ __forceinline__ float exp_det(float x) {
     return x != x ? x : y;
 }
 
+// exp_det for x <= 0 (and NaN): the same operations and the same result for
+// every x <= 0, without the two selects that only x > 88 and NaN reach. A NaN
+// argument gives a finite value here, which the GELU below turns back into NaN
+// (its x is then NaN too).
+__device__ __forceinline__ float exp_det_nonpos(float x) {
+    const float xc = fmaxf(x, -87.0f);
+    const float t = __fmaf_rn(xc, DET_LOG2E, 12582912.0f);
+    const float n = __fsub_rn(t, 12582912.0f);
+    float r = __fmaf_rn(n, -DET_LN2_HI, xc);
+    r = __fmaf_rn(n, -DET_LN2_LO, r);
+    float p = DET_C7;
+    p = __fmaf_rn(p, r, DET_C6);
+    p = __fmaf_rn(p, r, DET_C5);
+    p = __fmaf_rn(p, r, DET_C4);
+    p = __fmaf_rn(p, r, DET_C3);
+    p = __fmaf_rn(p, r, DET_C2);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const float y = __fmul_rn(p, __int_as_float((__float_as_int(t) - 0x4B400000 + 127) << 23));
+    return x < -87.0f ? 0.0f : y;
+}
+
 // 1/d for d in [1, 2]: Newton-Raphson r <- r + r (1 - d r) from the linear start
 // 24/17 - 8/17 d (relative error at most 1/17), three steps
 __device__ __forceinline__ float recip12_det(float d) {
@@ -72,7 +94,7 @@ __device__ __forceinline__ float gelu_det(float x) {
     const float K = 0.7978846f, Cc = 0.044715f;
     const float cx = __fmul_rn(__fmul_rn(__fmul_rn(Cc, x), x), x);
     const float inner = __fmul_rn(K, __fadd_rn(x, cx));
-    const float t = exp_det(__fmul_rn(-2.0f, fabsf(inner)));
+    const float t = exp_det_nonpos(__fmul_rn(-2.0f, fabsf(inner)));
     const float w = inner >= 0.0f ? 1.0f : t;
     return __fmul_rn(__fmul_rn(x, w), recip12_det(__fadd_rn(1.0f, t)));
 }

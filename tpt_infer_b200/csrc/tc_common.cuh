@@ -42,6 +42,10 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// arrival on another CTA's mbarrier with the default CTA-scope release
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // 4-byte store into another CTA's shared memory (shared::cluster address) that
 // counts its bytes on that CTA's mbarrier `bar_cluster`
 __device__ __forceinline__ void st_async_b32(uint32_t addr_cluster, uint32_t v, uint32_t bar_cluster) {

@@ -261,15 +261,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             for (int c = 0; c < BN / 64; c++) {
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
-                tmem_wait_ld();
                 const int n0 = nt * BN + half * (BN / 2) + c * 32;
-                if (!ACC_OUT) w8a8_epi32<ACT>(v, n0, N, a_scale, wscale, bias);
                 if (!ACC_OUT && Q) {
                     // int8 output requantized with the next point's scale: this
-                    // lane's row gets 32 consecutive bytes
+                    // lane's row gets 32 consecutive bytes. The chunk's column
+                    // constants go through the warp's (otherwise unused) store
+                    // staging, loaded while the accumulators arrive.
+                    float *cs = reinterpret_cast<float *>(stage_g);
+                    const int nl = n0 + lane < N ? n0 + lane : N - 1;
+                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nl));
+                    const float bi = bias ? __ldg(bias + nl) : 0.0f;
+                    tmem_wait_ld();
+                    __syncwarp();  // the previous chunk's reads of cs are done
+                    cs[lane] = sc;
+                    cs[32 + lane] = bi;
+                    __syncwarp();
                     if (m < M) {
                         uint32_t b[8];
-                        requant_pack32(v, q_scale, __frcp_rn(q_scale), requant_fast_ok(q_scale), b);
+                        if (requant_fast_ok(q_scale))
+                            w8a8_epi_q32<ACT, true>(v, cs, bias != nullptr, q_scale, __frcp_rn(q_scale), b);
+                        else
+                            w8a8_epi_q32<ACT, false>(v, cs, bias != nullptr, q_scale, 0.0f, b);
                         int8_t *dst = Q + (size_t)m * N + n0;
                         if (n0 + 32 <= N && (N & 15) == 0) {
                             reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
@@ -280,7 +292,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                                 if (n0 + j < N) dst[j] = (int8_t)(b[j / 4] >> (8 * (j % 4)));
                         }
                     }
-                } else if (tma_store) {
+                    continue;
+                }
+                tmem_wait_ld();
+                if (!ACC_OUT) w8a8_epi32<ACT>(v, n0, N, a_scale, wscale, bias);
+                if (tma_store) {
                     if (mrow0 < M) {  // a block entirely below the last row is not stored
                         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                         __syncwarp();
@@ -313,7 +329,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc == 0 ? tempty_leader0 : tempty_leader1);
+            // CTA-scope release: the arrival publishes only that this warp's
+            // tensor-memory reads are complete (tcgen05.wait::ld, then the
+            // fence above); its global stores need no order against the MMA,
+            // and a cluster-scope release would wait for them to reach L2
+            if (lane == 0) mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
