@@ -240,16 +240,11 @@ __device__ __forceinline__ float act_t(float y) {
     else return y;
 }
 
-// The W8A8 epilogue of one 32-column chunk of one row, in place: i32
-// accumulators of columns n0 .. n0+31 become the f32 bits of
-// act((float)acc * (a_scale * ws[n]) + bias[n]) (the product of the scales
-// first, separately rounded multiply and add). Every lane of a warp passes the
-// same n0: the 32 channel scales and biases are broadcast loads, 128-bit when
-// aligned and in range.
-template <int ACT>
-__device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
-                                           const float *bias) {
-    float sc[32], bi[32];
+// The channel scales and biases of one 32-column chunk (columns n0 .. n0+31):
+// broadcast loads (every lane of a warp passes the same n0), 128-bit when
+// aligned and in range, clamped to column N-1 past the edge.
+__device__ __forceinline__ void w8a8_load_consts(int n0, int N, const float *ws, const float *bias, float (&sc)[32],
+                                                 float (&bi)[32]) {
     if (n0 + 32 <= N && ((reinterpret_cast<uintptr_t>(ws + n0) | reinterpret_cast<uintptr_t>(bias + n0)) & 15) == 0) {
 #pragma unroll
         for (int c = 0; c < 8; c++) {
@@ -272,12 +267,30 @@ __device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, flo
             bi[j] = bias ? __ldg(bias + n) : 0.0f;
         }
     }
+}
+
+// The W8A8 epilogue of one 32-column chunk of one row, in place: i32
+// accumulators become the f32 bits of act((float)acc * (a_scale * sc[j]) +
+// bi[j]) (the product of the scales first, separately rounded multiply and
+// add; no add without a bias, which keeps -0).
+template <int ACT>
+__device__ __forceinline__ void w8a8_apply32(uint32_t (&v)[32], float a_scale, const float (&sc)[32],
+                                             const float (&bi)[32], bool has_bias) {
 #pragma unroll
     for (int j = 0; j < 32; j++) {
         float y = __fmul_rn(__int2float_rn((int)v[j]), __fmul_rn(a_scale, sc[j]));
-        if (bias) y = __fadd_rn(y, bi[j]);
+        if (has_bias) y = __fadd_rn(y, bi[j]);
         v[j] = __float_as_uint(act_t<ACT>(y));
     }
+}
+
+// Both of the above for columns n0 .. n0+31
+template <int ACT>
+__device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
+                                           const float *bias) {
+    float sc[32], bi[32];
+    w8a8_load_consts(n0, N, ws, bias, sc, bi);
+    w8a8_apply32<ACT>(v, a_scale, sc, bi, bias != nullptr);
 }
 // The activation of 32 values (f32 bits) in place, for epilogues that keep
 // their code small: ReLU as a select, GELU through an out-of-line call.
@@ -340,35 +353,6 @@ __device__ __forceinline__ int8_t requant_i8_fast(float y, float s, float rs) {
 }
 // out of line: the dividing path of the wide epilogues (scales outside the fast range)
 static __device__ __noinline__ int8_t requant_i8_outline(float y, float s) { return requant_i8(y, s); }
-
-// The W8A8 epilogue and the int8 requantization of one 32-column chunk of one
-// row, fused: qb[j/4] byte j%4 = requant_i8(act((float)acc[j] * cs[j] +
-// cs[32 + j]), qs), with cs[j] = a_scale * ws[n0 + j] and cs[32 + j] =
-// bias[n0 + j] staged in shared memory by the warp (each lane computes one
-// column's product once, instead of every lane all 32): the same operations in
-// the same order as w8a8_epi32 followed by requant_pack32. HAS_BIAS false
-// skips the add (adding 0 would turn -0 into +0). FAST: the division-free
-// requantization (requant_fast_ok(qs)), else the dividing one.
-template <int ACT, bool FAST>
-__device__ __forceinline__ void w8a8_epi_q32(const uint32_t (&v)[32], const float *cs, bool has_bias, float qs,
-                                             float rqs, uint32_t (&qb)[8]) {
-#pragma unroll
-    for (int g = 0; g < 8; g++) {
-        const float4 s4 = reinterpret_cast<const float4 *>(cs)[g];
-        const float4 b4 = reinterpret_cast<const float4 *>(cs + 32)[g];
-        const float sc[4] = {s4.x, s4.y, s4.z, s4.w}, bi[4] = {b4.x, b4.y, b4.z, b4.w};
-        uint32_t word = 0;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float y = __fmul_rn(__int2float_rn((int)v[4 * g + i]), sc[i]);
-            if (has_bias) y = __fadd_rn(y, bi[i]);
-            y = act_t<ACT>(y);
-            const int8_t q8 = FAST ? requant_i8_fast(y, qs, rqs) : requant_i8_outline(y, qs);
-            word |= (uint32_t)(uint8_t)q8 << (8 * i);
-        }
-        qb[g] = word;
-    }
-}
 
 // requant_i8 of 32 values (f32 bits) packed 4 to a word, low byte first
 __device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s, float rs, bool fast,

@@ -247,6 +247,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
+        // The channel scales and biases of the next chunk are loaded as soon as
+        // the current chunk's arithmetic is done, so their latency (an L2 round
+        // trip behind the operand traffic) overlaps the current chunk's stores
+        float sc[32], bi[32];
+        auto chunk_n0 = [&](int tt, int c) {
+            return (tt - (tt / tiles_n) * tiles_n) * BN + half * (BN / 2) + c * 32;
+        };
+        if (!ACC_OUT && cluster < ntiles) w8a8_load_consts(chunk_n0(cluster, 0), N, wscale, bias, sc, bi);
         for (int t = cluster; t < ntiles; t += nclusters) {
             int okw = 0;
             if (lane == 0) okw = mbar_wait(tfull_bar(acc), acc_phase, abort_p, gflags, true) ? 1 : 0;
@@ -261,27 +269,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             for (int c = 0; c < BN / 64; c++) {
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(c * 32), v);
+                tmem_wait_ld();
                 const int n0 = nt * BN + half * (BN / 2) + c * 32;
+                if (!ACC_OUT) {
+                    w8a8_apply32<ACT>(v, a_scale, sc, bi, bias != nullptr);
+                    const bool last = c + 1 == BN / 64;
+                    if (!last || t + nclusters < ntiles)
+                        w8a8_load_consts(chunk_n0(last ? t + nclusters : t, last ? 0 : c + 1), N, wscale, bias, sc, bi);
+                }
                 if (!ACC_OUT && Q) {
                     // int8 output requantized with the next point's scale: this
-                    // lane's row gets 32 consecutive bytes. The chunk's column
-                    // constants go through the warp's (otherwise unused) store
-                    // staging, loaded while the accumulators arrive.
-                    float *cs = reinterpret_cast<float *>(stage_g);
-                    const int nl = n0 + lane < N ? n0 + lane : N - 1;
-                    const float sc = __fmul_rn(a_scale, __ldg(wscale + nl));
-                    const float bi = bias ? __ldg(bias + nl) : 0.0f;
-                    tmem_wait_ld();
-                    __syncwarp();  // the previous chunk's reads of cs are done
-                    cs[lane] = sc;
-                    cs[32 + lane] = bi;
-                    __syncwarp();
+                    // lane's row gets 32 consecutive bytes
                     if (m < M) {
                         uint32_t b[8];
-                        if (requant_fast_ok(q_scale))
-                            w8a8_epi_q32<ACT, true>(v, cs, bias != nullptr, q_scale, __frcp_rn(q_scale), b);
-                        else
-                            w8a8_epi_q32<ACT, false>(v, cs, bias != nullptr, q_scale, 0.0f, b);
+                        requant_pack32(v, q_scale, __frcp_rn(q_scale), requant_fast_ok(q_scale), b);
                         int8_t *dst = Q + (size_t)m * N + n0;
                         if (n0 + 32 <= N && (N & 15) == 0) {
                             reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
@@ -292,11 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                                 if (n0 + j < N) dst[j] = (int8_t)(b[j / 4] >> (8 * (j % 4)));
                         }
                     }
-                    continue;
-                }
-                tmem_wait_ld();
-                if (!ACC_OUT) w8a8_epi32<ACT>(v, n0, N, a_scale, wscale, bias);
-                if (tma_store) {
+                } else if (tma_store) {
                     if (mrow0 < M) {  // a block entirely below the last row is not stored
                         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                         __syncwarp();
