@@ -123,6 +123,43 @@ def test_w8a8_small_m_back_to_back(cuda):
         w.free()
 
 
+def test_small_m_and_w4_share_the_split_workspace(cuda):
+    # the split-K small-batch W8A8 kernel and the stream-K W4 kernel keep their
+    # partial sums in the same context workspace (counters zero between
+    # launches, slots overwritten): interleave them on the stream with no host
+    # sync in between and check every result
+    import torch
+
+    w8, w4 = [], []
+    for i, (m, n, k) in enumerate([(16, 4096, 4096), (5, 1000, 1024), (32, 768, 768)]):
+        aq, sa, wq, ws, bias = w8a8_case(m, n, k, seed=700 + 10 * i)
+        w = cuda.upload_i8(wq, ws, n, k)
+        y_dev = torch.empty(m * n, dtype=torch.float32, device="cuda")
+        w8.append((m, n, k, aq, sa, wq, ws, bias, w, torch.from_numpy(aq).cuda(), torch.from_numpy(bias).cuda(), y_dev))
+    for i, (m, n, k) in enumerate([(64, 11008, 4096), (24, 1000, 1024)]):
+        x, p, s = w4_case(m, n, k, seed=800 + 10 * i)
+        w = cuda.upload_i4(p, s, n, k)
+        w4.append((m, n, k, x, p, s, w, torch.from_numpy(x).cuda(), torch.empty(m * n, dtype=torch.float32,
+                                                                                  device="cuda")))
+    torch.cuda.synchronize()
+    for rep in range(2):
+        for j in range(3):
+            m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev = w8[j]
+            cuda.w8a8_gemm_dev(a_dev, m, sa, w, b_dev, 0, y_dev)
+            if j < 2:
+                m4, n4, k4, x, p, s, w4h, x_dev, y4 = w4[j]
+                cuda.w4_gemm_dev(x_dev, m4, w4h, None, 0, y4)
+    cuda.sync()
+    for m, n, k, aq, sa, wq, ws, bias, w, a_dev, b_dev, y_dev in w8:
+        want = O.w8a8_gemm(aq, wq, m, n, k, sa, ws, bias, 0, threads=8)
+        assert np.array_equal(y_dev.cpu().numpy(), want), (m, n, k)
+        w.free()
+    for m, n, k, x, p, s, w, x_dev, y4 in w4:
+        want = O.w4_gemm(x, p, s, m, n, k, threads=8)
+        assert np.max(np.abs(y4.cpu().numpy() - want)) <= w4_tol(want)
+        w.free()
+
+
 def test_w8a8_large_m_back_to_back(cuda):
     # SM-pair launches of several shapes and tile widths queued back to back
     # on the stream (twice) with no host sync in between, every result checked

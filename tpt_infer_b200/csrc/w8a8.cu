@@ -48,7 +48,9 @@ __device__ __forceinline__ int dot16(int4 a, int4 b, int acc) {
     return acc;
 }
 
-// One warp per output channel (grid-stride). Each lane owns 16-byte chunks
+// One warp per output channel: block b takes the channels [N b / G, N (b + 1) / G)
+// (G blocks; two per SM, so every SM streams the same number of rows to within
+// one), its warps in turn. Each lane owns 16-byte chunks
 // c = lane + 32 j of the row, j < 8, so a warp covers 4 KB of K per pass and
 // every load of the pass is issued before the first dp4a: a warp keeps 4 KB in
 // flight and the activations stay in registers (A_REG, M <= 2, K <= 4096) or in
@@ -62,13 +64,14 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
                                                    int8_t *__restrict__ Q, float q_scale) {
     const int lane = threadIdx.x & 31;
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int n_begin = (int)((long long)N * blockIdx.x / gridDim.x) + warp;
+    const int n_end = (int)((long long)N * (blockIdx.x + 1) / gridDim.x);
     const int chunks = K >> 4;  // 16-byte chunks per row
     // this warp's weight rows start streaming into L2 while the previous
     // kernel on the stream finishes (the grid is small enough to be resident
     // beside it); the loads below then hit L2
-    for (int n = warp + lane * nwarps; n < N; n += 32 * nwarps)
+    for (int n = n_begin + lane * nwarps; n < n_end; n += 32 * nwarps)
         for (int c = 0; c < K; c += 32768) prefetch_l2_bulk(Wt + (size_t)n * K + c, (uint32_t)min(K - c, 32768));
     pdl_wait();
     pdl_trigger();
@@ -83,7 +86,7 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                                                  : make_int4(0, 0, 0, 0);
             }
     }
-    for (int n = warp; n < N; n += nwarps) {
+    for (int n = n_begin; n < n_end; n += nwarps) {
         const int4 *wrow = reinterpret_cast<const int4 *>(Wt + (size_t)n * K);
         int acc[MM];
 #pragma unroll
