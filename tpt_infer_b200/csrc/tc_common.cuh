@@ -93,10 +93,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 
 static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, unsigned *gflags,
                                        bool honour_abort) {
+    // The context's limit is read through the read-only path, issued before the
+    // first poll: it changes only between launches (the host sets it), so after
+    // an SM's first read it is an L1 hit, and its latency overlaps the poll
+    // instead of adding to every wait that the first poll does not end (a
+    // producer waiting on each freed stage would otherwise pay an L2 round
+    // trip per stage)
+    const unsigned l = (honour_abort && gflags) ? __ldg(gflags + TPT_FLAG_WAIT_LIMIT) : 0u;
     if (mbar_try_wait(bar, parity)) return true;
     long long limit = TPT_WAIT_CYCLES;
     if (honour_abort && gflags) {
-        const unsigned l = *reinterpret_cast<volatile unsigned *>(gflags + TPT_FLAG_WAIT_LIMIT);
         if (l) {  // a limit set by the context: poll without the hardware's suspend, check the clock each time
             const long long t0 = clock64();
             while (!mbar_test_wait(bar, parity)) {
