@@ -158,3 +158,59 @@ def test_maxpool_op_bit_exact(cuda, N, H, W, C, k, s, pad):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     n = want.size
     assert np.array_equal(np.frombuffer(gq.tobytes()[:n], np.int8), O.quantize_i8_static(want, sq))
+
+
+@pytest.mark.parametrize("N,H,W,pad,oh,ow", [(2, 112, 112, 2, 112, 112), (3, 32, 48, 2, 33, 49), (1, 16, 16, 1, 15, 15),
+                                               (2, 20, 32, 3, 20, 30)])
+@pytest.mark.parametrize("quant", [False, True])
+def test_stem_pool_fused_bit_exact(cuda, N, H, W, pad, oh, ow, quant):
+    # IM2COL -> LINEAR (+bias, ReLU) -> MAXPOOL 3x3/2/1 [-> QUANTIZE] of a
+    # 16-channel 4x4 stride-1 conv with 64 outputs (the ResNet stem in its
+    # space-to-depth form; the output size may be cut below the full one, as the
+    # stem's is) runs as one fused stem + pool launch that never writes the conv
+    # output: the pooled f32 tensor and its int8 copy equal the oracle's conv,
+    # ReLU, max pool and quantizer bit for bit, at the stem's own shape and at
+    # odd / ragged ones
+    from tpt_infer_b200 import graphs
+
+    C, OC, k = 16, 64, 4
+    PH, PW = (oh - 1) // 2 + 1, (ow - 1) // 2 + 1
+    M, K = N * oh * ow, k * k * C
+    seed = 9300 + H + W + pad
+    x = O.normal(N * H * W * C, seed)
+    sx = np.float32(O.sym_scale(O.absmax(x)))
+    wq, ws = O.quantize_i8_symmetric_per_channel(O.normal(OC * K, seed + 1, 0.0, 0.05), OC)
+    bias = O.normal(OC, seed + 2, 0.0, 0.1)
+    p = graphs.Plan(cuda)
+    w = cuda.upload_i8(wq, ws, OC, K)
+    p.weights.append(w)
+    tx, txq = p.tensor(graphs.F32, x.size), p.tensor(graphs.I8, x.size)
+    col, ty = p.tensor(graphs.I8, M * K), p.tensor(graphs.F32, M * OC)
+    tp, tq = p.tensor(graphs.F32, N * PH * PW * OC), p.tensor(graphs.I8, N * PH * PW * OC)
+    p.op(graphs.OP_QUANTIZE, tx, txq, f0=float(sx), dims=(x.size,))
+    p.op(graphs.OP_IM2COL, txq, col, dims=(N, H, W, C, k, k, 1, 1, pad, pad, oh, ow, K))
+    p.op(graphs.OP_LINEAR, col, ty, in1=p.const(bias), w=w, act=graphs.ACT_RELU, dims=(M,))
+    p.op(graphs.OP_MAXPOOL, ty, tp, dims=(N, oh, ow, OC, 3, 3, 2, 2, 1, 1, PH, PW))
+    sq = np.float32(0.03)
+    if quant:
+        p.op(graphs.OP_QUANTIZE, tp, tq, f0=float(sq), dims=(N * PH * PW * OC,))
+    p.finalize()
+    outs = p.run({tx: x}, [tp, tq] if quant else [tp])
+    l0 = cuda.launch_count()
+    p.run_device()
+    cuda.sync()
+    assert cuda.launch_count() - l0 == 2  # the input's QUANTIZE and the fused stem + pool (+ its int8 copy)
+    p.close()
+
+    xq = O.quantize_i8_static(x, sx).reshape(N, H, W, C)
+    # the oracle's full conv output, cut to oh x ow like the op's dims
+    full_oh, full_ow = H + 2 * pad - k + 1, W + 2 * pad - k + 1
+    col_o, _, _ = OM._im2col(xq, k, 1, pad, K)
+    y = O.w8a8_gemm(col_o, wq, N * full_oh * full_ow, OC, K, sx, ws, bias, O.ACT_RELU, threads=8)
+    y = np.ascontiguousarray(y.reshape(N, full_oh, full_ow, OC)[:, :oh, :ow, :])
+    want = O.max_pool2d(np.ascontiguousarray(y.transpose(0, 3, 1, 2)), N, OC, oh, ow, (3, 3), (2, 2), (1, 1))
+    want = np.ascontiguousarray(want.reshape(N, OC, PH, PW).transpose(0, 2, 3, 1))
+    got = outs[0].reshape(N, PH, PW, OC)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    if quant:
+        assert np.array_equal(np.frombuffer(outs[1].tobytes()[:want.size], np.int8), O.quantize_i8_static(want, sq))

@@ -44,6 +44,9 @@ int comm_all_gather(tpt_cuda_comm *c, const void *in, void *out, size_t bytes_pe
 int launch_conv_w8a8(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
                      int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
                      int act, float *y, bool *handled, Requant rq, Residual res = Residual());
+int launch_stem_pool(tpt_cuda_ctx *ctx, const int8_t *x, int N, int H, int W, int C, int KH, int KW, int sh, int sw,
+                     int ph, int pw, int OH, int OW, const tpt_cuda_weights *w, float a_scale, const float *bias,
+                     int act, int PH, int PW, float *P, int8_t *Q, float q_scale, bool *handled);
 int comm_max_u32(tpt_cuda_comm *c, unsigned *words, size_t n);
 int ensure_copy_streams(tpt_cuda_ctx *ctx);
 int launch_binary(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, const size_t od[8], unsigned amask,
@@ -648,6 +651,48 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
         // folds in too: the epilogue adds the residual, applies the activation
         // and writes the sum (and, with a QUANTIZE of the sum after it, also
         // its int8 copy), so the conv output is neither written nor read back.
+        // IM2COL -> LINEAR_W8A8 (+ReLU) -> MAXPOOL 3x3/2/1 of the conv output (the
+        // conv rows and the conv output read by nothing else, neither fetched):
+        // the ResNet stem in its 16-channel 4x4 form runs fused with its pool, so
+        // the conv output is never written; a QUANTIZE of the pooled tensor folds
+        // in (its f32 copy is still written: a residual reads it).
+        if (o.kind == TPT_OP_IM2COL && i + 2 < p->ops.size()) {
+            const tpt_plan_op &l = p->ops[i + 1].op, &mp = p->ops[i + 2].op;
+            const PlanTensor &col = p->tensors[o.out], &yt = p->tensors[l.out];
+            const size_t *d = o.dims, *md = mp.dims;
+            if (l.kind == TPT_OP_LINEAR_W8A8 && l.in0 == o.out && col.readers == 1 &&
+                !is_output(out_ids, n_out, o.out) && mp.kind == TPT_OP_MAXPOOL_NHWC && mp.in0 == l.out &&
+                yt.readers == 1 && !is_output(out_ids, n_out, l.out) && md[0] == d[0] && md[1] == d[10] &&
+                md[2] == d[11] && md[3] == l.w->n && md[4] == 3 && md[5] == 3 && md[6] == 2 && md[7] == 2 &&
+                md[8] == 1 && md[9] == 1) {
+                const float sa = p->tensors[o.in0].scale;
+                p->tensors[o.out].scale = sa;
+                int8_t *qo = nullptr;
+                float qs = 0.0f;
+                size_t fused = 2;
+                if (!p->calibrating && i + 3 < p->ops.size()) {
+                    PlanOp &nq = p->ops[i + 3];
+                    const tpt_plan_op &q = nq.op;
+                    if (q.kind == TPT_OP_QUANTIZE && q.in0 == mp.out && q.dims[1] == 0 && nq.frozen > 0.0f &&
+                        q.dims[0] == p->tensors[mp.out].numel) {
+                        qo = Q(p, q.out);
+                        qs = nq.frozen;
+                        fused = 3;
+                    }
+                }
+                bool handled = false;
+                int st = launch_stem_pool(p->ctx, Q(p, o.in0), (int)d[0], (int)d[1], (int)d[2], (int)d[3], (int)d[4],
+                                          (int)d[5], (int)d[6], (int)d[7], (int)d[8], (int)d[9], (int)d[10],
+                                          (int)d[11], l.w, sa, F(p, l.in1), l.act, (int)md[10], (int)md[11],
+                                          F(p, mp.out), qo, qs, &handled);
+                if (st) return st;
+                if (handled) {
+                    if (qo) p->tensors[p->ops[i + 3].op.out].scale = qs;
+                    i += fused;
+                    continue;
+                }
+            }
+        }
         if (o.kind == TPT_OP_IM2COL && i + 1 < p->ops.size()) {
             const tpt_plan_op &l = p->ops[i + 1].op;
             const PlanTensor &col = p->tensors[o.out];
