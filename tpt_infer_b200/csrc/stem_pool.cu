@@ -23,12 +23,14 @@
 // 16 bytes further, i.e. the next pixel's bytes: the im2col rows are never
 // materialised. The weights ([64, 256], 128B-swizzled) stay in shared memory.
 //
-// Roles (192 threads, two CTAs per SM): warp 0 TMA (weights once, then the six
+// Roles (320 threads, two CTAs per SM): warp 0 TMA (weights once, then the six
 // rows of each unit into a double-buffered row set); warp 1 tensor memory
 // (192 columns: three 64-column accumulators) and the MMAs, 8 per conv row;
-// warps 2..5 epilogue, thread = conv pixel (TMEM lane): the conv rows' values,
-// their maximum over the three rows, through shared memory the maximum over
-// three pixels, the pooled f32 row and its int8 copy. Every wait is bounded.
+// warps 2..9 epilogue, two per TMEM lane quarter (one 32-channel half each),
+// thread = conv pixel: the conv rows' values (scale products and biases staged
+// once in shared memory), their maximum over the three rows, through shared
+// memory the maximum over three pixels, the pooled f32 row and its int8 copy.
+// Every wait is bounded.
 #include "tc_common.cuh"
 
 namespace tpt {
@@ -49,9 +51,10 @@ constexpr int SP_SET_BYTES = SP_ROWS * SP_ROW_STRIDE;
 constexpr int SP_W_BYTES = SP_OC * 256;      // weights: 2 k-blocks of [64 rows x 128 B]
 constexpr int SP_MAX_STRIDE = 68;            // floats per pixel in the row-max buffer (conflict-free float4)
 constexpr int SP_MAX_BYTES = 128 * SP_MAX_STRIDE * 4;
-constexpr int SP_THREADS = 192;
+constexpr int SP_EPI = 8;                   // epilogue warps
+constexpr int SP_THREADS = 64 + 32 * SP_EPI;
 constexpr int SP_TMEM_COLS = 256;            // three 64-column accumulators
-constexpr int SP_SMEM = 1024 + SP_W_BYTES + 2 * SP_SET_BYTES + SP_MAX_BYTES + 256;
+constexpr int SP_SMEM = 1024 + SP_W_BYTES + 2 * SP_SET_BYTES + SP_MAX_BYTES + 256 + 2 * SP_OC * 4;
 
 struct StemShape {
     int N, H, W;          // input [N, H, W, 16] int8
@@ -93,6 +96,7 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
     const uint32_t sets = wsm + SP_W_BYTES;
     const uint32_t maxs = sets + 2 * SP_SET_BYTES;
     const uint32_t bars = maxs + SP_MAX_BYTES;
+    float *cprod = reinterpret_cast<float *>(smem_raw + (bars + 256 - raw));  // a_scale * w_scale[n], then bias[n]
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (2 + s); };
     const uint32_t wbar = bars + 32, tfull = bars + 40, tempty = bars + 48, drain = bars + 56;
@@ -106,6 +110,10 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
     // zero the row buffers (their guards and tails stay zero: TMA writes only the data)
     for (int i = threadIdx.x; i < 2 * SP_SET_BYTES / 16; i += SP_THREADS)
         *reinterpret_cast<uint4 *>(smem_raw + (sets - raw) + 16 * i) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < SP_OC) {  // the epilogue's per-channel constants (the scale product first, as the GEMM's)
+        cprod[threadIdx.x] = __fmul_rn(a_scale, __ldg(wscale + threadIdx.x));
+        cprod[SP_OC + threadIdx.x] = bias ? __ldg(bias + threadIdx.x) : 0.0f;
+    }
     if (threadIdx.x == 0) {
         abort_flag = 0;
         for (int s = 0; s < 2; s++) {
@@ -114,7 +122,7 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
         }
         mbar_init(wbar, 1);
         mbar_init(tfull, 1);
-        mbar_init(tempty, 4);
+        mbar_init(tempty, SP_EPI);
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
@@ -198,39 +206,42 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
             mbar_wait(drain, 0, abort_p, gflags, false);
         }
     } else {
-        // ---------------- epilogue (warps 2..5): thread = conv pixel ----------------
-        const int q = warp & 3;  // TMEM lane quarter
+        // ---------------- epilogue (warps 2..9): thread = conv pixel ----------------
+        const int q = warp & 3;             // TMEM lane quarter
+        const int c = (warp - 2) >> 2;      // this warp's 32-channel half
         const int ox = q * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..127
+        const int et = threadIdx.x - 64;    // 0 .. 32 SP_EPI - 1
         const float qrs = Q ? __frcp_rn(q_scale) : 0.0f;
         const bool qfast = requant_fast_ok(q_scale);
+        const bool has_bias = bias != nullptr;
         uint32_t tphase = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             int okw = 0;
             if (lane == 0) okw = mbar_wait(tfull, tphase, abort_p, gflags, true) ? 1 : 0;
             okw = __shfl_sync(0xffffffffu, okw, 0);
-            if (!bar_and(1, 128, okw != 0)) break;
+            if (!bar_and(1, 32 * SP_EPI, okw != 0)) break;
             tphase ^= 1u;
             tc_fence_after();
             const int n = u / ss.PH, py = u - n * ss.PH;
             // the unit's three conv rows that exist: 2 py - 1 (not for py = 0) .. 2 py + 1 (below OH)
             const int r_lo = 2 * py - 1 < 0 ? 1 : 0, r_hi = 2 * py + 1 < ss.OH ? 3 : 2;
-#pragma unroll 1
-            for (int c = 0; c < 2; c++) {
-                float sc[32], bi[32];
-                w8a8_load_consts(c * 32, SP_OC, wscale, bias, sc, bi);
-                float mx[32];
+            float mx[32];
 #pragma unroll
-                for (int jj = 0; jj < 32; jj++) mx[jj] = 0.0f;  // every value is ReLU'd (>= +0)
+            for (int jj = 0; jj < 32; jj++) mx[jj] = 0.0f;  // every value is ReLU'd (>= +0)
 #pragma unroll 1
-                for (int ri = r_lo; ri < r_hi; ri++) {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ri * SP_OC + c * 32), v);
-                    tmem_wait_ld();
-                    w8a8_apply32<TPT_ACT_RELU>(v, a_scale, sc, bi, bias != nullptr);
+            for (int ri = r_lo; ri < r_hi; ri++) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ri * SP_OC + c * 32), v);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++) mx[jj] = fmaxf(mx[jj], __uint_as_float(v[jj]));
+                for (int jj = 0; jj < 32; jj++) {
+                    // y = (float)acc * (a_scale * w_scale[n]) + bias[n], ReLU (the W8A8 epilogue's operations)
+                    float y = __fmul_rn(__int2float_rn((int)v[jj]), cprod[c * 32 + jj]);
+                    if (has_bias) y = __fadd_rn(y, cprod[SP_OC + c * 32 + jj]);
+                    mx[jj] = fmaxf(mx[jj], y > 0.0f ? y : 0.0f);
                 }
+            }
+            {
                 float *dst = rowmax + ox * SP_MAX_STRIDE + c * 32;
 #pragma unroll
                 for (int c4 = 0; c4 < 8; c4++)
@@ -239,10 +250,10 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty);  // tensor memory is free for the next unit
-            bar_sync(1, 128);                   // every pixel's row maximum is in shared memory
+            bar_sync(1, 32 * SP_EPI);           // every pixel's row maximum is in shared memory
             // the pooled row: px over the conv pixels 2 px - 1 .. 2 px + 1 inside the image
             const size_t orow = ((size_t)n * ss.PH + py) * ss.PW;
-            for (int idx = et; idx < ss.PW * 16; idx += 128) {
+            for (int idx = et; idx < ss.PW * 16; idx += 32 * SP_EPI) {
                 const int px = idx >> 4, c4 = idx & 15;
                 const int x0 = 2 * px - 1 < 0 ? 0 : 2 * px - 1, x1 = 2 * px + 1 < ss.OW ? 2 * px + 1 : ss.OW - 1;
                 float4 m = reinterpret_cast<const float4 *>(rowmax + x0 * SP_MAX_STRIDE)[c4];
@@ -264,7 +275,7 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
                                                            ((uint32_t)(uint8_t)cq << 16) | ((uint32_t)(uint8_t)d << 24);
                 }
             }
-            bar_sync(1, 128);  // the row maxima are read before the next unit writes them
+            bar_sync(1, 32 * SP_EPI);  // the row maxima are read before the next unit writes them
         }
     }
 
