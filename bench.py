@@ -582,6 +582,36 @@ def profile_kernels(args):
     return 0
 
 
+def profile_plan(args):
+    """One model plan on one GPU, calibrated on a seeded batch and frozen, then
+    args.warmup + args.steps direct forwards (no CUDA graph, so a profiler sees
+    every launch in order): ResNet-18 (batch 256 by default) or the 12-layer
+    BERT-base encoder over 128 tokens (batch 64)."""
+    import torch
+
+    from tpt_infer_b200 import CudaBackend, graphs, synth
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    be = CudaBackend.new(0, stream)
+    if args.profile_plan == "resnet18":
+        B, numel = args.batch or 256, 3 * 224 * 224
+        p, x, out = graphs.build_resnet18(be, B, graphs.resnet18_weights(be))
+    else:
+        B, numel = args.batch or 64, 128 * 768
+        p, x, out = graphs.build_bert(be, B, 128, graphs.bert_weights(be, layers=12))
+    p.calibrate(True)
+    p.run({x: synth.normal(B * numel, 31)}, [out])
+    p.freeze()
+    p.run({x: synth.normal(B * numel, 32)}, [out])
+    t = _time_device(stream, p.run_device, args.steps, args.warmup)
+    p.close()
+    be.close()
+    print(json.dumps({"profile_plan": args.profile_plan, "batch": B, "forwards": args.warmup + args.steps,
+                      "ms_per_forward": t * 1e3}), flush=True)
+    return 0
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -631,12 +661,18 @@ def main():
     ap.add_argument("--profile-kernels", action="store_true",
                     help="each main kernel on one case, `--steps` launches each after warm-up: the ncu capture case "
                          "for the per-kernel summaries")
+    ap.add_argument("--profile-plan", choices=["resnet18", "bert"],
+                    help="one model plan (calibrated, frozen), `--warmup` + `--steps` forwards at `--batch`: the ncu "
+                         "capture case for the launch lists")
+    ap.add_argument("--batch", type=int, default=0, help="batch of --profile-plan (default 256 / 64)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
     if args.profile_kernels:
         return profile_kernels(args)
+    if args.profile_plan:
+        return profile_plan(args)
 
     import torch
     import torch.distributed as dist
