@@ -97,6 +97,30 @@ __device__ __forceinline__ void digits3(float x, float inv, int &d0, int &d1, in
     rint_magic(r2, d2);
 }
 
+// The same digits as their sums' float bits: rounding by adding 1.5 * 2^23
+// leaves the integer in the low mantissa bits, so the low byte of the bits is
+// the digit's two's-complement byte (0x4B400000 has a zero low byte); NaN
+// gives 0. For packing: pack4 takes the low bytes of four words.
+__device__ __forceinline__ void digits3_bits(float x, float inv, uint32_t &b0, uint32_t &b1, uint32_t &b2) {
+    const float u = __fmul_rn(x, inv);
+    if (u != u) {
+        b0 = b1 = b2 = 0;
+        return;
+    }
+    const float t0 = __fadd_rn(u, 12582912.0f);
+    const float a = __fsub_rn(t0, 12582912.0f);
+    const float r1 = __fmul_rn(__fsub_rn(u, a), 128.0f);
+    const float t1 = __fadd_rn(r1, 12582912.0f);
+    const float c = __fsub_rn(t1, 12582912.0f);
+    const float r2 = __fmul_rn(__fsub_rn(r1, c), 128.0f);
+    b0 = __float_as_uint(t0);
+    b1 = __float_as_uint(t1);
+    b2 = __float_as_uint(__fadd_rn(r2, 12582912.0f));
+}
+__device__ __forceinline__ uint32_t pack4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+    return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
+}
+
 // every accumulator is below 2^22 in magnitude (|T| <= 64 (2 * 127 * 64 + 64 * 64)
 // about 1.3e6, |U| <= 128 (2 * 127 * 64 + 64 * 64) about 2.6e6), so the
 // conversions are exact
@@ -215,14 +239,15 @@ __global__ void __launch_bounds__(AI_T, 2)
         const float sc = __fmul_rn(amax, AI_R127);
         if (kq == 0) vps[d] = __fmul_rn(sc, AI_R127);
         const float inv = amax > 0.0f ? __frcp_rn(sc) : 0.0f;
-        uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
+        uint32_t w0[4], w1[4], w2[4];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            int e0, e1, e2;
-            digits3(v[i], inv, e0, e1, e2);
-            w0[i >> 2] |= (uint32_t)(uint8_t)e0 << (8 * (i & 3));
-            w1[i >> 2] |= (uint32_t)(uint8_t)e1 << (8 * (i & 3));
-            w2[i >> 2] |= (uint32_t)(uint8_t)e2 << (8 * (i & 3));
+        for (int i4 = 0; i4 < 4; i4++) {
+            uint32_t x0[4], x1[4], x2[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) digits3_bits(v[4 * i4 + k], inv, x0[k], x1[k], x2[k]);
+            w0[i4] = pack4(x0[0], x0[1], x0[2], x0[3]);
+            w1[i4] = pack4(x1[0], x1[1], x1[2], x1[3]);
+            w2[i4] = pack4(x2[0], x2[1], x2[2], x2[3]);
         }
         const uint32_t o = swz(d, 16 * kq);  // V^T row d, keys 16 kq .. 16 kq + 15: one 16-byte chunk
         *reinterpret_cast<uint4 *>(g + OFF_V0 + o) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
@@ -292,23 +317,26 @@ __global__ void __launch_bounds__(AI_T, 2)
         float sum = 0.0f;
 #pragma unroll
         for (int hc = 0; hc < 2; hc++) {
-            uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0}, w2[4] = {0, 0, 0, 0};
+            uint32_t w0[4], w1[4], w2[4];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 const int k0 = hc * 16 + hh * 8;
                 uint32_t sv8[8];
                 tmem_ld8(lane_base + (uint32_t)(qtr * 32 + k0), sv8);
                 tmem_wait_ld();
+                uint32_t x0[8], x1[8], x2[8];
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    const float e = k0 + j < nvalid ? exp_det(__fsub_rn(__uint_as_float(sv8[j]), m)) : 0.0f;
+                    // s - m <= 0 (m is the row's maximum) or NaN: exp_det's result without its x > 88 case
+                    const float e = k0 + j < nvalid ? exp_det_le0(__fsub_rn(__uint_as_float(sv8[j]), m)) : 0.0f;
                     sum = __fadd_rn(sum, e);
-                    int c0, c1, c2;
-                    digits3(e, 127.0f, c0, c1, c2);
-                    const int i = hh * 8 + j;
-                    w0[i >> 2] |= (uint32_t)(uint8_t)c0 << (8 * (i & 3));
-                    w1[i >> 2] |= (uint32_t)(uint8_t)c1 << (8 * (i & 3));
-                    w2[i >> 2] |= (uint32_t)(uint8_t)c2 << (8 * (i & 3));
+                    digits3_bits(e, 127.0f, x0[j], x1[j], x2[j]);
+                }
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    w0[2 * hh + c] = pack4(x0[4 * c], x0[4 * c + 1], x0[4 * c + 2], x0[4 * c + 3]);
+                    w1[2 * hh + c] = pack4(x1[4 * c], x1[4 * c + 1], x1[4 * c + 2], x1[4 * c + 3]);
+                    w2[2 * hh + c] = pack4(x2[4 * c], x2[4 * c + 1], x2[4 * c + 2], x2[4 * c + 3]);
                 }
             }
             const uint32_t o = swz(row, 32 * qtr + 16 * hc);
@@ -369,10 +397,22 @@ __global__ void __launch_bounds__(AI_T, 2)
                 if (r >= S) continue;
                 const float4 o = *reinterpret_cast<const float4 *>(st + r * AI_OST + 4 * c4);
                 const size_t off = ((size_t)b * S + r) * HD + h * AI_D + 4 * c4;
-                if (qout)  // the following QUANTIZE, fused: the f32 context is not written
-                    *reinterpret_cast<uint32_t *>(qout + off) =
-                        (uint32_t)(uint8_t)requant_i8(o.x, qs) | ((uint32_t)(uint8_t)requant_i8(o.y, qs) << 8) |
-                        ((uint32_t)(uint8_t)requant_i8(o.z, qs) << 16) | ((uint32_t)(uint8_t)requant_i8(o.w, qs) << 24);
+                if (qout) {  // the following QUANTIZE, fused: the f32 context is not written
+                    int8_t q4[4];
+                    const float ov[4] = {o.x, o.y, o.z, o.w};
+                    if (requant_fast_ok(qs)) {
+                        const float qrs = __frcp_rn(qs);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) q4[e] = requant_i8_fast(ov[e], qs, qrs);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) q4[e] = requant_i8(ov[e], qs);
+                    }
+                    *reinterpret_cast<uint32_t *>(qout + off) = (uint32_t)(uint8_t)q4[0] |
+                                                                ((uint32_t)(uint8_t)q4[1] << 8) |
+                                                                ((uint32_t)(uint8_t)q4[2] << 16) |
+                                                                ((uint32_t)(uint8_t)q4[3] << 24);
+                }
                 else
                     *reinterpret_cast<float4 *>(out + off) = o;
             }

@@ -81,6 +81,28 @@ __device__ __forceinline__ float exp_det_nonpos(float x) {
     return x < -87.0f ? 0.0f : y;
 }
 
+// exp_det for x <= 0 or NaN (a softmax's s - max): the same operations and the
+// same result as exp_det there, NaN included, without the select that only
+// x > 88 reaches
+__device__ __forceinline__ float exp_det_le0(float x) {
+    const float xc = fmaxf(x, -87.0f);
+    const float t = __fmaf_rn(xc, DET_LOG2E, 12582912.0f);
+    const float n = __fsub_rn(t, 12582912.0f);
+    float r = __fmaf_rn(n, -DET_LN2_HI, xc);
+    r = __fmaf_rn(n, -DET_LN2_LO, r);
+    float p = DET_C7;
+    p = __fmaf_rn(p, r, DET_C6);
+    p = __fmaf_rn(p, r, DET_C5);
+    p = __fmaf_rn(p, r, DET_C4);
+    p = __fmaf_rn(p, r, DET_C3);
+    p = __fmaf_rn(p, r, DET_C2);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    float y = __fmul_rn(p, __int_as_float((__float_as_int(t) - 0x4B400000 + 127) << 23));
+    y = x < -87.0f ? 0.0f : y;
+    return x != x ? x : y;
+}
+
 // 1/d for d in [1, 2]: Newton-Raphson r <- r + r (1 - d r) from the linear start
 // 24/17 - 8/17 d (relative error at most 1/17), three steps
 __device__ __forceinline__ float recip12_det(float d) {
