@@ -75,18 +75,25 @@ struct ConvShape {
     int Kw; // the weight rows' length (>= K)
 };
 
-template <int BN, int MODE>
+// RB: the weights of the (single) output-channel tile stay resident in shared
+// memory for the whole launch (up to RES_MAX bytes), so a ring stage carries
+// only the activation rows: the tensor unit moves a third fewer box lines per
+// k-block (128 instead of 128 + BN), which bounds the 64-channel convs
+constexpr int CV_RES_MAX = 40 * 1024;
+template <int BN, int MODE, bool RB = false>
 struct ConvCfg {
     static constexpr int KB = cv_kb(MODE);  // k bytes per stage
     static constexpr int A_BYTES = CV_BM * KB;
     static constexpr int B_BYTES = BN * KB;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RES_BYTES = RB ? CV_RES_MAX : 0;
+    static constexpr int STAGE_BYTES = A_BYTES + (RB ? 0 : B_BYTES);
     static constexpr int EPI = cv_epi_warps(MODE, BN);
     static constexpr int OUT_BYTES = EPI * CV_WARP_OUT;
-    static constexpr int STAGES_FIT = (232448 - OUT_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
+    static constexpr int STAGES_FIT = (232448 - OUT_BYTES - RES_BYTES - 2048 - 3 * CV_BM * 4) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + (2 * STAGES + 5 + 3 * EPI) * 8 + 1024;
+    static constexpr int SMEM_BYTES =
+        STAGES * STAGE_BYTES + RES_BYTES + OUT_BYTES + (2 * STAGES + 6 + 3 * EPI) * 8 + 1024;
     static_assert(SMEM_BYTES + 3 * CV_BM * 4 + 16 <= 232448, "shared memory (dynamic + the static gather table)");
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile N");
     static_assert(STAGES >= 3, "stages");
@@ -145,7 +152,7 @@ __device__ __forceinline__ void cp_async_wait_upto(int n) {
     }
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool RB>
 __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
     k_conv_w8a8(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmQ,
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                 const int8_t *__restrict__ X, ConvShape cs, int OC, float a_scale, const float *__restrict__ wscale,
                 const float *__restrict__ bias, int act, float *__restrict__ Y, int8_t *__restrict__ Q,
                 float q_scale, const float *__restrict__ R, int ract, unsigned *gflags) {
-    using Cfg = ConvCfg<BN, MODE>;
+    using Cfg = ConvCfg<BN, MODE, RB>;
     constexpr int S = Cfg::STAGES;
     constexpr bool TMA_A = cv_tma(MODE);
     constexpr int KB = Cfg::KB;
@@ -169,15 +176,19 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
 
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t ring = (raw + 1023u) & ~1023u;
-    const uint32_t staging = ring + S * Cfg::STAGE_BYTES;
+    const uint32_t resw = ring + S * Cfg::STAGE_BYTES;  // resident weights (RB), 1 KB aligned
+    const uint32_t staging = resw + Cfg::RES_BYTES;
     const uint32_t bars = staging + Cfg::OUT_BYTES;
     auto a_s = [&](int s) { return ring + (uint32_t)(s * Cfg::STAGE_BYTES); };
+    // the weight tile of stage s (k-block kb): in the stage, or resident
     auto b_s = [&](int s) { return a_s(s) + (uint32_t)Cfg::A_BYTES; };
+    auto b_at = [&](int s, int kb) { return RB ? resw + (uint32_t)(kb * Cfg::B_BYTES) : b_s(s); };
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * S + b); };
     auto tempty_bar = [&](int b) { return bars + 8u * (2 * S + 2 + b); };
     const uint32_t drain_bar = bars + 8u * (2 * S + 4);
+    const uint32_t wres_bar = bars + 8u * (2 * S + 5 + 3 * EPI);  // the resident weights (RB)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = cs.N * cs.OH * cs.OW;
@@ -198,6 +209,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
         }
         mbar_init(drain_bar, 1);
         for (int b = 0; b < 3 * EPI; b++) mbar_init(bars + 8u * (2 * S + 5 + b), 1);  // residual tiles, 3 per epilogue warp
+        mbar_init(wres_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         if (TMA_A) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
@@ -223,6 +235,10 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
             uint32_t phase = 0, issued_mask = 0, last_phase = 0;
             bool ok = true;
             const int cblocks = TMA_A ? cs.C / KB : 1;  // k-blocks per tap
+            if (RB) {  // every k-block's weight tile once (one output-channel tile)
+                mbar_arrive_expect_tx(wres_bar, (uint32_t)(kblocks * Cfg::B_BYTES));
+                for (int kb = 0; kb < kblocks; kb++) tma_load_2d(b_at(0, kb), &tmW, wres_bar, kb * KB, 0);
+            }
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const int nt = t % tiles_n, m0 = (t / tiles_n) * CV_BM;
                 const int n0 = m0 / HWo, r0 = m0 - n0 * HWo, oy0 = r0 / cs.OW, ox0 = r0 - oy0 * cs.OW;
@@ -234,13 +250,13 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                     if (TMA_A) {
                         const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * KB;
                         const int ky = tap / cs.KW, kx = tap - ky * cs.KW;
-                        mbar_arrive_expect_tx(full_bar(stage), Cfg::A_BYTES + Cfg::B_BYTES);
+                        mbar_arrive_expect_tx(full_bar(stage), Cfg::A_BYTES + (RB ? 0 : Cfg::B_BYTES));
                         tma_load_im2col_4d(a_s(stage), &tmX, full_bar(stage), c0, ox0 * cs.sw - cs.pw,
                                            oy0 * cs.sh - cs.ph, n0, (uint16_t)kx, (uint16_t)ky);
                     } else {
                         mbar_arrive_expect_tx(full_bar(stage), Cfg::B_BYTES);
                     }
-                    tma_load_2d(b_s(stage), &tmW, full_bar(stage), kb * KB, nt * BN);
+                    if (!RB) tma_load_2d(b_s(stage), &tmW, full_bar(stage), kb * KB, nt * BN);
                     issued_mask |= 1u << stage;
                     last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -251,6 +267,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
             }
             // our own copies in flight land before the CTA can exit (the
             // stage's barrier also waits for the gather warps)
+            if (RB) mbar_wait(wres_bar, 0, abort_p, gflags, false);
             for (int s = 0; s < S; s++)
                 if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (last_phase >> s) & 1u, abort_p, gflags, false);
         }
@@ -261,7 +278,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                                        ((uint32_t)(CV_BM >> 4) << 24);
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            bool ok = true;
+            bool ok = !RB || mbar_wait(wres_bar, 0, abort_p, gflags, true);
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_p, gflags, true)) break;
                 tc_fence_after();
@@ -274,7 +291,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < KB / 32; kk++)
-                        tc_mma_i8(d_tmem, kmajor_desc<KB>(a_s(stage) + 32 * kk), kmajor_desc<KB>(b_s(stage) + 32 * kk),
+                        tc_mma_i8(d_tmem, kmajor_desc<KB>(a_s(stage) + 32 * kk), kmajor_desc<KB>(b_at(stage, kb) + 32 * kk),
                                   idesc, (kb | kk) != 0 ? 1u : 0u);
                     tc_commit(empty_bar(stage));
                     if (++stage == S) {
@@ -577,13 +594,13 @@ bool make_tmap_im2col(CUtensorMap *tm, const int8_t *x, const ConvShape &cs, int
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool RB = false>
 int launch_conv(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, const CUtensorMap *tx,
                 const tpt_cuda_weights *w, float a_scale, const float *bias, int act, float *y, Requant rq,
                 const Residual &res) {
-    using Cfg = ConvCfg<BN, MODE>;
+    using Cfg = ConvCfg<BN, MODE, RB>;
     static bool attr_done[64] = {};
-    auto kfn = k_conv_w8a8<BN, MODE>;
+    auto kfn = k_conv_w8a8<BN, MODE, RB>;
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
@@ -636,6 +653,9 @@ int launch_conv_bn(tpt_cuda_ctx *ctx, const int8_t *x, const ConvShape &cs, cons
             first = false;
         }
     }
+    // one output-channel tile whose weights fit in shared memory: resident weights
+    if (cv_tma(MODE) && bn == 64 && w->n <= 64 && ((w->k + cv_kb(MODE) - 1) / cv_kb(MODE)) * 64 * cv_kb(MODE) <= CV_RES_MAX)
+        return launch_conv<64, MODE, true>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
     if (bn == 64) return launch_conv<64, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
     if (bn == 128) return launch_conv<128, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
     return launch_conv<256, MODE>(ctx, x, cs, tx, w, a_scale, bias, act, y, rq, res);
