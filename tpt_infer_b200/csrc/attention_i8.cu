@@ -69,38 +69,18 @@ __host__ __device__ constexpr uint32_t ai_idesc(int m, int n) {  // D s32, A s8,
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// round to the nearest integer (ties to even, as rintf) for |u| < 2^22 by one
-// add of 1.5 * 2^23, whose sum has ulp 1: the float result and the integer in
-// its low mantissa bits, on the FMA and integer pipes (no conversion unit)
-__device__ __forceinline__ float rint_magic(float u, int &i) {
-    const float t = __fadd_rn(u, 12582912.0f);
-    i = __float_as_int(t) - 0x4B400000;
-    return __fsub_rn(t, 12582912.0f);
-}
-// exact int -> float for |i| < 2^22, the same way back
+// exact int -> float for |i| < 2^22 by the same 1.5 * 2^23 offset, on the
+// integer and FMA pipes (no conversion unit)
 __device__ __forceinline__ float i2f_magic(uint32_t i) {
     return __fsub_rn(__int_as_float((int)i + 0x4B400000), 12582912.0f);
 }
 
-// the three digits of x (see the header); NaN gives 0. |u| <= 127 and the two
-// residuals are in [-64, 64], so the rounding by addition equals rintf
-__device__ __forceinline__ void digits3(float x, float inv, int &d0, int &d1, int &d2) {
-    const float u = __fmul_rn(x, inv);
-    if (u != u) {
-        d0 = d1 = d2 = 0;
-        return;
-    }
-    const float a = rint_magic(u, d0);
-    const float r1 = __fmul_rn(__fsub_rn(u, a), 128.0f);
-    const float b = rint_magic(r1, d1);
-    const float r2 = __fmul_rn(__fsub_rn(r1, b), 128.0f);
-    rint_magic(r2, d2);
-}
-
-// The same digits as their sums' float bits: rounding by adding 1.5 * 2^23
-// leaves the integer in the low mantissa bits, so the low byte of the bits is
-// the digit's two's-complement byte (0x4B400000 has a zero low byte); NaN
-// gives 0. For packing: pack4 takes the low bytes of four words.
+// The three digits of x (see the header) as their rounding sums' float bits:
+// rounding by adding 1.5 * 2^23 (ties to even, as rintf, for |u| < 2^22; here
+// |u| <= 127 and the residuals are in [-64, 64]) leaves the integer in the low
+// mantissa bits, so the low byte of the bits is the digit's two's-complement
+// byte (0x4B400000 has a zero low byte); NaN gives 0. pack4 takes the low
+// bytes of four words.
 __device__ __forceinline__ void digits3_bits(float x, float inv, uint32_t &b0, uint32_t &b1, uint32_t &b2) {
     const float u = __fmul_rn(x, inv);
     if (u != u) {
@@ -143,7 +123,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ uint32_t pack2(int lo, int hi) { return (uint32_t)(uint8_t)lo | ((uint32_t)(uint8_t)hi << 8); }
 
 __global__ void __launch_bounds__(AI_T, 2)
     k_attention_i8(const float *__restrict__ qkv, float *__restrict__ out, int S, int H, float scale,
@@ -175,48 +154,56 @@ __global__ void __launch_bounds__(AI_T, 2)
     pdl_wait();  // the previous kernel's output (qkv) is complete from here on
     pdl_trigger();
 
-    // ---- Q and K rows: a warp per row (rows warp + 16 i), lane = head dimensions
-    // 2 lane, 2 lane + 1; all 16 loads of a warp are in flight before the first use
+    // ---- Q and K rows: half a warp per row (rows 2 warp + (lane >> 4) + 32 i), lane
+    // % 16 = head dimensions 4 l .. 4 l + 3; all 8 loads of a lane are in flight
+    // before the first use, and each plane's four digits leave as one word
     {
-        constexpr int RPW = 2 * AI_S / (AI_T / 32);  // rows per warp: 16
-        float2 xs[RPW];
+        constexpr int RPW = 2 * AI_S / (AI_T / 32) / 2;  // row pairs per warp: 8
+        const int l16 = lane & 15, half = lane >> 4;
+        float4 xs[RPW];
 #pragma unroll
         for (int i = 0; i < RPW; i++) {
-            const int rr = warp + (AI_T / 32) * i;
+            const int rr = 2 * warp + half + (AI_T / 16) * i;
             const bool isq = rr < AI_S;
             const int r = isq ? rr : rr - AI_S;
-            xs[i] = r < S ? __ldg(reinterpret_cast<const float2 *>(src + (size_t)r * ld + (isq ? 0 : HD)) + lane)
-                          : make_float2(0.0f, 0.0f);
+            xs[i] = r < S ? __ldg(reinterpret_cast<const float4 *>(src + (size_t)r * ld + (isq ? 0 : HD)) + l16)
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
         for (int i = 0; i < RPW; i++) {
-            const int rr = warp + (AI_T / 32) * i;
-            const bool isq = rr < AI_S;
+            const int rr = 2 * warp + half + (AI_T / 16) * i;
+            const bool isq = rr < AI_S;  // the same for both halves: 2 warp + half < 32 and the stride is 32
             const int r = isq ? rr : rr - AI_S;
-            float2 x = xs[i];
-            if (isq) x = make_float2(__fmul_rn(x.x, scale), __fmul_rn(x.y, scale));
-            const float amax = warp_max(fmaxf(fabsf(x.x), fabsf(x.y)));
-            const float sc = __fmul_rn(amax, AI_R127);
-            const float inv = amax > 0.0f ? __frcp_rn(sc) : 0.0f;
-            int a0, a1, a2, c0, c1, c2;
-            digits3(x.x, inv, a0, a1, a2);
-            digits3(x.y, inv, c0, c1, c2);
-            const uint32_t d0 = pack2(a0, c0), d1 = pack2(a1, c1), d2 = pack2(a2, c2);
-            const int kb = 2 * lane;
+            float4 x = xs[i];
+            if (isq) x = make_float4(__fmul_rn(x.x, scale), __fmul_rn(x.y, scale), __fmul_rn(x.z, scale),
+                                     __fmul_rn(x.w, scale));
+            float am = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));  // within the half
+            const float sc = __fmul_rn(am, AI_R127);
+            const float inv = am > 0.0f ? __frcp_rn(sc) : 0.0f;
+            uint32_t b0[4], b1[4], b2[4];
+            digits3_bits(x.x, inv, b0[0], b1[0], b2[0]);
+            digits3_bits(x.y, inv, b0[1], b1[1], b2[1]);
+            digits3_bits(x.z, inv, b0[2], b1[2], b2[2]);
+            digits3_bits(x.w, inv, b0[3], b1[3], b2[3]);
+            const uint32_t d0 = pack4(b0[0], b0[1], b0[2], b0[3]), d1 = pack4(b1[0], b1[1], b1[2], b1[3]),
+                           d2 = pack4(b2[0], b2[1], b2[2], b2[3]);
+            const int kb = 4 * l16;
             if (isq) {  // QA = [a0 | a1], QB = [a2 | 0]
-                *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, kb)) = (uint16_t)d0;
-                *reinterpret_cast<uint16_t *>(g + OFF_QA + swz(r, 64 + kb)) = (uint16_t)d1;
-                *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, kb)) = (uint16_t)d2;
-                *reinterpret_cast<uint16_t *>(g + OFF_QB + swz(r, 64 + kb)) = 0;
-                if (lane == 0) qsc[r] = sc;
+                *reinterpret_cast<uint32_t *>(g + OFF_QA + swz(r, kb)) = d0;
+                *reinterpret_cast<uint32_t *>(g + OFF_QA + swz(r, 64 + kb)) = d1;
+                *reinterpret_cast<uint32_t *>(g + OFF_QB + swz(r, kb)) = d2;
+                *reinterpret_cast<uint32_t *>(g + OFF_QB + swz(r, 64 + kb)) = 0;
+                if (l16 == 0) qsc[r] = sc;
             } else {    // KA = [b0 | 0], KB = [b1 | b0], KC = [b2 | b1]
-                *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, kb)) = (uint16_t)d0;
-                *reinterpret_cast<uint16_t *>(g + OFF_KA + swz(r, 64 + kb)) = 0;
-                *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, kb)) = (uint16_t)d1;
-                *reinterpret_cast<uint16_t *>(g + OFF_KB + swz(r, 64 + kb)) = (uint16_t)d0;
-                *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, kb)) = (uint16_t)d2;
-                *reinterpret_cast<uint16_t *>(g + OFF_KC + swz(r, 64 + kb)) = (uint16_t)d1;
-                if (lane == 0) ksc[r] = sc;
+                *reinterpret_cast<uint32_t *>(g + OFF_KA + swz(r, kb)) = d0;
+                *reinterpret_cast<uint32_t *>(g + OFF_KA + swz(r, 64 + kb)) = 0;
+                *reinterpret_cast<uint32_t *>(g + OFF_KB + swz(r, kb)) = d1;
+                *reinterpret_cast<uint32_t *>(g + OFF_KB + swz(r, 64 + kb)) = d0;
+                *reinterpret_cast<uint32_t *>(g + OFF_KC + swz(r, kb)) = d2;
+                *reinterpret_cast<uint32_t *>(g + OFF_KC + swz(r, 64 + kb)) = d1;
+                if (l16 == 0) ksc[r] = sc;
             }
         }
     }
