@@ -450,12 +450,14 @@ def run_configs(be, stream, flush, pk, local, world, rank, cpu=True, comm=None):
             p.calibrate(True)
             p.run({x: synth.normal(B * S * H, 41)}, [h])
             p.freeze()
+            p.set_graph(True)  # recorded with its all-gathers, replayed
             p.run({x: xall}, [h])
             t = _gmax(_time_device(stream, p.run_device, 5, 2), world, dev)
             bert["ffn_column_sharded"] = {
                 "ms_per_batch": t * 1e3, "sequences_per_s": B / t,
                 "parallelism": f"FFN1 split over {world} GPUs by output channel, int8 all-gather "
-                               f"({B * S * 3072 / 1e6:.0f} MB per layer) inside the plan; the rest replicated"}
+                               f"({B * S * 3072 / 1e6:.0f} MB per layer) inside the plan; the rest replicated",
+                "launch": "plan recorded as one CUDA graph with its NCCL all-gathers, replayed"}
             p.close()
         out["bert"] = bert
     except Exception as e:

@@ -47,6 +47,10 @@ def main():
     yr = ref.run({xr: xin}, [hr])[0]
     ys = shd.run({xs: xin}, [hs])[0]
     assert np.array_equal(yr, ys), f"ffn-sharded output differs: max {np.max(np.abs(yr - ys))}"
+    shd.set_graph(True)  # recorded with its NCCL all-gathers (first run), then replayed
+    for _ in range(2):
+        yg = shd.run({xs: xin}, [hs])[0]
+        assert np.array_equal(yr, yg), "graph-replayed ffn-sharded output differs"
 
     b0, bn = sharding.batch_shard(B, world, rank)
     part, xp, hp = graphs.build_bert(be, bn, S, layers)
@@ -58,7 +62,8 @@ def main():
     dist.all_reduce(ok)
     if rank == 0:
         print(json.dumps({"ok": True, "world": world, "ranks_ok": int(ok.item()),
-                          "ffn_shard": "bit-identical", "batch_shard": "bit-identical"}), flush=True)
+                          "ffn_shard": "bit-identical (direct and graph-replayed)",
+                          "batch_shard": "bit-identical"}), flush=True)
     for p in (part, shd, ref):
         p.close()
     comm.close()

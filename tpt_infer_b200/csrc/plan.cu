@@ -844,7 +844,10 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
 // (sizing every workspace the ops use), then the same sequence is recorded;
 // later runs launch the recording.
 int run_plan(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
-    if (!p->use_graph || p->calibrating || p->comm) return run_ops(p, out_ids, n_out);
+    // a plan with a communicator records its all-gathers too (NCCL collectives
+    // are captured as graph nodes); calibration, whose scales are agreed by an
+    // all-reduce read back on the host, always runs direct
+    if (!p->use_graph || p->calibrating) return run_ops(p, out_ids, n_out);
     tpt_cuda_ctx *ctx = p->ctx;
     const std::vector<int> key(out_ids, out_ids + n_out);
     if (p->graph && key == p->graph_out) {
