@@ -101,6 +101,89 @@ __device__ __forceinline__ uint32_t pack4(uint32_t w0, uint32_t w1, uint32_t w2,
     return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
 }
 
+// Pairs of f32 values in one 64-bit register and the paired IEEE operations
+// (fma / add / mul .rn.f32x2: two correctly rounded results per issue, the
+// same bits as the scalar operations)
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t splat2(float x) { return f2pack(x, x); }
+
+// exp_det_le0 of two values (x <= 0 or NaN): the same operations in the same
+// order on each half (a difference u - v as fma(v, -1, u): one rounding, as
+// the subtraction)
+__device__ __forceinline__ void exp_det_le0_x2(float x0, float x1, float &y0, float &y1) {
+    const uint64_t magic = splat2(12582912.0f);
+    const uint64_t xc = f2pack(fmaxf(x0, -87.0f), fmaxf(x1, -87.0f));
+    const uint64_t t = fma2(xc, splat2(DET_LOG2E), magic);
+    const uint64_t n = add2(t, splat2(-12582912.0f));
+    uint64_t r = fma2(n, splat2(-DET_LN2_HI), xc);
+    r = fma2(n, splat2(-DET_LN2_LO), r);
+    uint64_t p = splat2(DET_C7);
+    p = fma2(p, r, splat2(DET_C6));
+    p = fma2(p, r, splat2(DET_C5));
+    p = fma2(p, r, splat2(DET_C4));
+    p = fma2(p, r, splat2(DET_C3));
+    p = fma2(p, r, splat2(DET_C2));
+    p = fma2(p, r, splat2(1.0f));
+    p = fma2(p, r, splat2(1.0f));
+    float t0, t1;
+    f2unpack(t, t0, t1);
+    const uint64_t sc = f2pack(__int_as_float((__float_as_int(t0) - 0x4B400000 + 127) << 23),
+                               __int_as_float((__float_as_int(t1) - 0x4B400000 + 127) << 23));
+    float z0, z1;
+    f2unpack(mul2(p, sc), z0, z1);
+    z0 = x0 < -87.0f ? 0.0f : z0;
+    z1 = x1 < -87.0f ? 0.0f : z1;
+    y0 = x0 != x0 ? x0 : z0;
+    y1 = x1 != x1 ? x1 : z1;
+}
+
+// digits3_bits of two values (u = x * inv per half; NaN gives 0)
+__device__ __forceinline__ void digits3_bits_x2(float x0, float x1, float inv, uint32_t (&b0)[2], uint32_t (&b1)[2],
+                                                uint32_t (&b2)[2]) {
+    const uint64_t magic = splat2(12582912.0f), nmagic = splat2(-12582912.0f), neg1 = splat2(-1.0f),
+                   s128 = splat2(128.0f);
+    const uint64_t u = mul2(f2pack(x0, x1), splat2(inv));
+    const uint64_t t0 = add2(u, magic);
+    const uint64_t a = add2(t0, nmagic);
+    const uint64_t r1 = mul2(fma2(a, neg1, u), s128);  // (u - a) * 128
+    const uint64_t t1 = add2(r1, magic);
+    const uint64_t c = add2(t1, nmagic);
+    const uint64_t r2 = mul2(fma2(c, neg1, r1), s128);
+    const uint64_t t2 = add2(r2, magic);
+    float uu0, uu1, f0, f1;
+    f2unpack(u, uu0, uu1);
+    f2unpack(t0, f0, f1);
+    b0[0] = __float_as_uint(f0), b0[1] = __float_as_uint(f1);
+    f2unpack(t1, f0, f1);
+    b1[0] = __float_as_uint(f0), b1[1] = __float_as_uint(f1);
+    f2unpack(t2, f0, f1);
+    b2[0] = __float_as_uint(f0), b2[1] = __float_as_uint(f1);
+    if (uu0 != uu0) b0[0] = b1[0] = b2[0] = 0;
+    if (uu1 != uu1) b0[1] = b1[1] = b2[1] = 0;
+}
+
 // every accumulator is below 2^22 in magnitude (|T| <= 64 (2 * 127 * 64 + 64 * 64)
 // about 1.3e6, |U| <= 128 (2 * 127 * 64 + 64 * 64) about 2.6e6), so the
 // conversions are exact
@@ -313,11 +396,21 @@ __global__ void __launch_bounds__(AI_T, 2)
                 tmem_wait_ld();
                 uint32_t x0[8], x1[8], x2[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    // s - m <= 0 (m is the row's maximum) or NaN: exp_det's result without its x > 88 case
-                    const float e = k0 + j < nvalid ? exp_det_le0(__fsub_rn(__uint_as_float(sv8[j]), m)) : 0.0f;
-                    sum = __fadd_rn(sum, e);
-                    digits3_bits(e, 127.0f, x0[j], x1[j], x2[j]);
+                for (int j = 0; j < 8; j += 2) {
+                    // s - m <= 0 (m is the row's maximum) or NaN: exp_det's result without
+                    // its x > 88 case, two keys per paired operation
+                    float e0, e1;
+                    exp_det_le0_x2(__fsub_rn(__uint_as_float(sv8[j]), m), __fsub_rn(__uint_as_float(sv8[j + 1]), m), e0,
+                                   e1);
+                    e0 = k0 + j < nvalid ? e0 : 0.0f;
+                    e1 = k0 + j + 1 < nvalid ? e1 : 0.0f;
+                    sum = __fadd_rn(sum, e0);
+                    sum = __fadd_rn(sum, e1);
+                    uint32_t q0[2], q1[2], q2[2];
+                    digits3_bits_x2(e0, e1, 127.0f, q0, q1, q2);
+                    x0[j] = q0[0], x0[j + 1] = q0[1];
+                    x1[j] = q1[0], x1[j + 1] = q1[1];
+                    x2[j] = q2[0], x2[j + 1] = q2[1];
                 }
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
