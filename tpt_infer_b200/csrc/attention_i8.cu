@@ -69,34 +69,8 @@ __host__ __device__ constexpr uint32_t ai_idesc(int m, int n) {  // D s32, A s8,
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// exact int -> float for |i| < 2^22 by the same 1.5 * 2^23 offset, on the
-// integer and FMA pipes (no conversion unit)
-__device__ __forceinline__ float i2f_magic(uint32_t i) {
-    return __fsub_rn(__int_as_float((int)i + 0x4B400000), 12582912.0f);
-}
 
-// The three digits of x (see the header) as their rounding sums' float bits:
-// rounding by adding 1.5 * 2^23 (ties to even, as rintf, for |u| < 2^22; here
-// |u| <= 127 and the residuals are in [-64, 64]) leaves the integer in the low
-// mantissa bits, so the low byte of the bits is the digit's two's-complement
-// byte (0x4B400000 has a zero low byte); NaN gives 0. pack4 takes the low
-// bytes of four words.
-__device__ __forceinline__ void digits3_bits(float x, float inv, uint32_t &b0, uint32_t &b1, uint32_t &b2) {
-    const float u = __fmul_rn(x, inv);
-    if (u != u) {
-        b0 = b1 = b2 = 0;
-        return;
-    }
-    const float t0 = __fadd_rn(u, 12582912.0f);
-    const float a = __fsub_rn(t0, 12582912.0f);
-    const float r1 = __fmul_rn(__fsub_rn(u, a), 128.0f);
-    const float t1 = __fadd_rn(r1, 12582912.0f);
-    const float c = __fsub_rn(t1, 12582912.0f);
-    const float r2 = __fmul_rn(__fsub_rn(r1, c), 128.0f);
-    b0 = __float_as_uint(t0);
-    b1 = __float_as_uint(t1);
-    b2 = __float_as_uint(__fadd_rn(r2, 12582912.0f));
-}
+// pack4 takes the low bytes of four words
 __device__ __forceinline__ uint32_t pack4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
     return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
 }
@@ -159,7 +133,12 @@ __device__ __forceinline__ void exp_det_le0_x2(float x0, float x1, float &y0, fl
     y1 = x1 != x1 ? x1 : z1;
 }
 
-// digits3_bits of two values (u = x * inv per half; NaN gives 0)
+// The three digits of x (see the header) as their rounding sums' float bits:
+// rounding by adding 1.5 * 2^23 (ties to even, as rintf, for |u| < 2^22; here
+// |u| <= 127 and the residuals are in [-64, 64]) leaves the integer in the low
+// mantissa bits, so the low byte of the bits is the digit's two's-complement
+// byte (0x4B400000 has a zero low byte); NaN gives 0.
+// Two values at a time (u = x * inv per half).
 __device__ __forceinline__ void digits3_bits_x2(float x0, float x1, float inv, uint32_t (&b0)[2], uint32_t (&b1)[2],
                                                 uint32_t (&b2)[2]) {
     const uint64_t magic = splat2(12582912.0f), nmagic = splat2(-12582912.0f), neg1 = splat2(-1.0f),
@@ -184,13 +163,22 @@ __device__ __forceinline__ void digits3_bits_x2(float x0, float x1, float inv, u
     if (uu1 != uu1) b0[1] = b1[1] = b2[1] = 0;
 }
 
-// every accumulator is below 2^22 in magnitude (|T| <= 64 (2 * 127 * 64 + 64 * 64)
-// about 1.3e6, |U| <= 128 (2 * 127 * 64 + 64 * 64) about 2.6e6), so the
-// conversions are exact
-__device__ __forceinline__ float combine3(uint32_t t0, uint32_t t1, uint32_t t2) {
-    float t = __fmul_rn(i2f_magic(t2), 0x1p-14f);
-    t = __fmaf_rn(i2f_magic(t1), 0x1p-7f, t);
-    return __fadd_rn(i2f_magic(t0), t);
+
+// t = T2 * 2^-14; t = fmaf(T1, 2^-7, t); T0 + t for two accumulator triples on
+// paired operations. Each integer becomes a float by adding it to the bits of
+// 1.5 * 2^23 and subtracting 1.5 * 2^23 (integer and FMA pipes, no conversion
+// unit): exact, since every accumulator is below 2^22 in magnitude
+// (|T| <= 64 (2 * 127 * 64 + 64 * 64) about 1.3e6, |U| <= 128 (2 * 127 * 64 +
+// 64 * 64) about 2.6e6).
+__device__ __forceinline__ uint64_t combine3_x2(uint32_t a0, uint32_t b0, uint32_t a1, uint32_t b1, uint32_t a2,
+                                                uint32_t b2) {
+    const uint64_t nmagic = splat2(-12582912.0f);
+    auto i2f2 = [&](uint32_t x, uint32_t y) {
+        return add2(f2pack(__int_as_float((int)x + 0x4B400000), __int_as_float((int)y + 0x4B400000)), nmagic);
+    };
+    uint64_t t = mul2(i2f2(a2, b2), splat2(0x1p-14f));
+    t = fma2(i2f2(a1, b1), splat2(0x1p-7f), t);
+    return add2(i2f2(a0, b0), t);
 }
 
 // 32 lanes x 8 consecutive 32-bit TMEM columns, load and store
@@ -266,10 +254,13 @@ __global__ void __launch_bounds__(AI_T, 2)
             const float sc = __fmul_rn(am, AI_R127);
             const float inv = am > 0.0f ? __frcp_rn(sc) : 0.0f;
             uint32_t b0[4], b1[4], b2[4];
-            digits3_bits(x.x, inv, b0[0], b1[0], b2[0]);
-            digits3_bits(x.y, inv, b0[1], b1[1], b2[1]);
-            digits3_bits(x.z, inv, b0[2], b1[2], b2[2]);
-            digits3_bits(x.w, inv, b0[3], b1[3], b2[3]);
+            {
+                uint32_t p0[2], p1[2], p2[2];
+                digits3_bits_x2(x.x, x.y, inv, p0, p1, p2);
+                b0[0] = p0[0], b0[1] = p0[1], b1[0] = p1[0], b1[1] = p1[1], b2[0] = p2[0], b2[1] = p2[1];
+                digits3_bits_x2(x.z, x.w, inv, p0, p1, p2);
+                b0[2] = p0[0], b0[3] = p0[1], b1[2] = p1[0], b1[3] = p1[1], b2[2] = p2[0], b2[3] = p2[1];
+            }
             const uint32_t d0 = pack4(b0[0], b0[1], b0[2], b0[3]), d1 = pack4(b1[0], b1[1], b1[2], b1[3]),
                            d2 = pack4(b2[0], b2[1], b2[2], b2[3]);
             const int kb = 4 * l16;
@@ -314,7 +305,11 @@ __global__ void __launch_bounds__(AI_T, 2)
         for (int i4 = 0; i4 < 4; i4++) {
             uint32_t x0[4], x1[4], x2[4];
 #pragma unroll
-            for (int k = 0; k < 4; k++) digits3_bits(v[4 * i4 + k], inv, x0[k], x1[k], x2[k]);
+            for (int k = 0; k < 4; k += 2) {
+                uint32_t p0[2], p1[2], p2[2];
+                digits3_bits_x2(v[4 * i4 + k], v[4 * i4 + k + 1], inv, p0, p1, p2);
+                x0[k] = p0[0], x0[k + 1] = p0[1], x1[k] = p1[0], x1[k + 1] = p1[1], x2[k] = p2[0], x2[k + 1] = p2[1];
+            }
             w0[i4] = pack4(x0[0], x0[1], x0[2], x0[3]);
             w1[i4] = pack4(x1[0], x1[1], x1[2], x1[3]);
             w2[i4] = pack4(x2[0], x2[1], x2[2], x2[3]);
@@ -370,10 +365,15 @@ __global__ void __launch_bounds__(AI_T, 2)
             tmem_ld8(lane_base + 256u + col, t2);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float sv = __fmul_rn(combine3(t0[j], t1[j], t2[j]), __fmul_rn(sq, ksc[col + j]));
-                if (ch * 8 + j < nvalid) m = fmaxf(m, sv);
-                t0[j] = __float_as_uint(sv);
+            for (int j = 0; j < 8; j += 2) {
+                float sv0, sv1;
+                f2unpack(mul2(combine3_x2(t0[j], t0[j + 1], t1[j], t1[j + 1], t2[j], t2[j + 1]),
+                              mul2(splat2(sq), f2pack(ksc[col + j], ksc[col + j + 1]))),
+                         sv0, sv1);
+                if (ch * 8 + j < nvalid) m = fmaxf(m, sv0);
+                if (ch * 8 + j + 1 < nvalid) m = fmaxf(m, sv1);
+                t0[j] = __float_as_uint(sv0);
+                t0[j + 1] = __float_as_uint(sv1);
             }
             tmem_st8(lane_base + col, t0);
         }
@@ -464,9 +464,12 @@ __global__ void __launch_bounds__(AI_T, 2)
                 for (int c = 0; c < 2; c++) {
                     float ov[4];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
+                    for (int e = 0; e < 4; e += 2) {
                         const int j = 4 * c + e;
-                        ov[e] = __fmul_rn(__fmul_rn(combine3(u0[j], u1[j], u2[j]), vps[col + j]), rs);
+                        f2unpack(mul2(mul2(combine3_x2(u0[j], u0[j + 1], u1[j], u1[j + 1], u2[j], u2[j + 1]),
+                                           f2pack(vps[col + j], vps[col + j + 1])),
+                                      splat2(rs)),
+                                 ov[e], ov[e + 1]);
                     }
                     *reinterpret_cast<float4 *>(st + row * AI_OST + col + 4 * c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
                 }
