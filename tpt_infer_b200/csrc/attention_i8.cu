@@ -75,75 +75,18 @@ __device__ __forceinline__ uint32_t pack4(uint32_t w0, uint32_t w1, uint32_t w2,
     return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
 }
 
-// Pairs of f32 values in one 64-bit register and the paired IEEE operations
-// (fma / add / mul .rn.f32x2: two correctly rounded results per issue, the
-// same bits as the scalar operations)
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t splat2(float x) { return f2pack(x, x); }
-
-// exp_det_le0 of two values (x <= 0 or NaN): the same operations in the same
-// order on each half (a difference u - v as fma(v, -1, u): one rounding, as
-// the subtraction)
-__device__ __forceinline__ void exp_det_le0_x2(float x0, float x1, float &y0, float &y1) {
-    const uint64_t magic = splat2(12582912.0f);
-    const uint64_t xc = f2pack(fmaxf(x0, -87.0f), fmaxf(x1, -87.0f));
-    const uint64_t t = fma2(xc, splat2(DET_LOG2E), magic);
-    const uint64_t n = add2(t, splat2(-12582912.0f));
-    uint64_t r = fma2(n, splat2(-DET_LN2_HI), xc);
-    r = fma2(n, splat2(-DET_LN2_LO), r);
-    uint64_t p = splat2(DET_C7);
-    p = fma2(p, r, splat2(DET_C6));
-    p = fma2(p, r, splat2(DET_C5));
-    p = fma2(p, r, splat2(DET_C4));
-    p = fma2(p, r, splat2(DET_C3));
-    p = fma2(p, r, splat2(DET_C2));
-    p = fma2(p, r, splat2(1.0f));
-    p = fma2(p, r, splat2(1.0f));
-    float t0, t1;
-    f2unpack(t, t0, t1);
-    const uint64_t sc = f2pack(__int_as_float((__float_as_int(t0) - 0x4B400000 + 127) << 23),
-                               __int_as_float((__float_as_int(t1) - 0x4B400000 + 127) << 23));
-    float z0, z1;
-    f2unpack(mul2(p, sc), z0, z1);
-    z0 = x0 < -87.0f ? 0.0f : z0;
-    z1 = x1 < -87.0f ? 0.0f : z1;
-    y0 = x0 != x0 ? x0 : z0;
-    y1 = x1 != x1 ? x1 : z1;
-}
-
 // The three digits of x (see the header) as their rounding sums' float bits:
 // rounding by adding 1.5 * 2^23 (ties to even, as rintf, for |u| < 2^22; here
 // |u| <= 127 and the residuals are in [-64, 64]) leaves the integer in the low
 // mantissa bits, so the low byte of the bits is the digit's two's-complement
 // byte (0x4B400000 has a zero low byte); NaN gives 0.
-// Two values at a time (u = x * inv per half).
-__device__ __forceinline__ void digits3_bits_x2(float x0, float x1, float inv, uint32_t (&b0)[2], uint32_t (&b1)[2],
-                                                uint32_t (&b2)[2]) {
+// Two values at a time (u = x * inv per half; nz from opaque_nz2, since u
+// feeds adds).
+__device__ __forceinline__ void digits3_bits_x2(float x0, float x1, float inv, uint64_t nz, uint32_t (&b0)[2],
+                                                uint32_t (&b1)[2], uint32_t (&b2)[2]) {
     const uint64_t magic = splat2(12582912.0f), nmagic = splat2(-12582912.0f), neg1 = splat2(-1.0f),
                    s128 = splat2(128.0f);
-    const uint64_t u = mul2(f2pack(x0, x1), splat2(inv));
+    const uint64_t u = mulr2(f2pack(x0, x1), splat2(inv), nz);
     const uint64_t t0 = add2(u, magic);
     const uint64_t a = add2(t0, nmagic);
     const uint64_t r1 = mul2(fma2(a, neg1, u), s128);  // (u - a) * 128
@@ -215,6 +158,7 @@ __global__ void __launch_bounds__(AI_T, 2)
     const int HD = H * AI_D, ld = 3 * HD;
     const float *src = qkv + (size_t)b * S * ld + h * AI_D;
     const uint32_t s_bar = smem_u32(&bars[0]), o_bar = smem_u32(&bars[1]), d_bar = smem_u32(&bars[2]);
+    const uint64_t nz2 = opaque_nz2((uint32_t)S >> 31);  // S >= 0
     if (tid == 0) {
         abort_flag = 0;
         mbar_init(s_bar, 1);
@@ -256,9 +200,9 @@ __global__ void __launch_bounds__(AI_T, 2)
             uint32_t b0[4], b1[4], b2[4];
             {
                 uint32_t p0[2], p1[2], p2[2];
-                digits3_bits_x2(x.x, x.y, inv, p0, p1, p2);
+                digits3_bits_x2(x.x, x.y, inv, nz2, p0, p1, p2);
                 b0[0] = p0[0], b0[1] = p0[1], b1[0] = p1[0], b1[1] = p1[1], b2[0] = p2[0], b2[1] = p2[1];
-                digits3_bits_x2(x.z, x.w, inv, p0, p1, p2);
+                digits3_bits_x2(x.z, x.w, inv, nz2, p0, p1, p2);
                 b0[2] = p0[0], b0[3] = p0[1], b1[2] = p1[0], b1[3] = p1[1], b2[2] = p2[0], b2[3] = p2[1];
             }
             const uint32_t d0 = pack4(b0[0], b0[1], b0[2], b0[3]), d1 = pack4(b1[0], b1[1], b1[2], b1[3]),
@@ -307,7 +251,7 @@ __global__ void __launch_bounds__(AI_T, 2)
 #pragma unroll
             for (int k = 0; k < 4; k += 2) {
                 uint32_t p0[2], p1[2], p2[2];
-                digits3_bits_x2(v[4 * i4 + k], v[4 * i4 + k + 1], inv, p0, p1, p2);
+                digits3_bits_x2(v[4 * i4 + k], v[4 * i4 + k + 1], inv, nz2, p0, p1, p2);
                 x0[k] = p0[0], x0[k + 1] = p0[1], x1[k] = p1[0], x1[k + 1] = p1[1], x2[k] = p2[0], x2[k + 1] = p2[1];
             }
             w0[i4] = pack4(x0[0], x0[1], x0[2], x0[3]);
@@ -407,7 +351,7 @@ __global__ void __launch_bounds__(AI_T, 2)
                     sum = __fadd_rn(sum, e0);
                     sum = __fadd_rn(sum, e1);
                     uint32_t q0[2], q1[2], q2[2];
-                    digits3_bits_x2(e0, e1, 127.0f, q0, q1, q2);
+                    digits3_bits_x2(e0, e1, 127.0f, nz2, q0, q1, q2);
                     x0[j] = q0[0], x0[j + 1] = q0[1];
                     x1[j] = q1[0], x1[j + 1] = q1[1];
                     x2[j] = q2[0], x2[j + 1] = q2[1];

@@ -284,6 +284,31 @@ __device__ __forceinline__ void w8a8_apply32(uint32_t (&v)[32], float a_scale, c
     }
 }
 
+// w8a8_apply32 on paired f32 operations (two columns per issue; the int ->
+// float conversion stays scalar): the same operations in the same order on
+// each half, so the same bits. nz from opaque_nz2 (the dequantized product
+// feeds the bias add).
+template <int ACT>
+__device__ __forceinline__ void w8a8_apply32_x2(uint32_t (&v)[32], float a_scale, const float (&sc)[32],
+                                                const float (&bi)[32], bool has_bias, uint64_t nz) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        uint64_t y = mulr2(f2pack(__int2float_rn((int)v[j]), __int2float_rn((int)v[j + 1])),
+                           mul2(splat2(a_scale), f2pack(sc[j], sc[j + 1])), nz);
+        if (has_bias) y = add2(y, f2pack(bi[j], bi[j + 1]));
+        float y0, y1;
+        f2unpack(y, y0, y1);
+        if constexpr (ACT == TPT_ACT_GELU) {
+            gelu_det_x2(y0, y1, nz, y0, y1);
+        } else {
+            y0 = act_t<ACT>(y0);
+            y1 = act_t<ACT>(y1);
+        }
+        v[j] = __float_as_uint(y0);
+        v[j + 1] = __float_as_uint(y1);
+    }
+}
+
 // Both of the above for columns n0 .. n0+31
 template <int ACT>
 __device__ __forceinline__ void w8a8_epi32(uint32_t (&v)[32], int n0, int N, float a_scale, const float *ws,
@@ -351,8 +376,49 @@ __device__ __forceinline__ int8_t requant_i8_fast(float y, float s, float rs) {
     n = n > 127 ? 127 : (n < -127 ? -127 : n);
     return (int8_t)n;
 }
+// requant_i8_fast of two values, the quotient steps on paired operations
+// (nz from opaque_nz2)
+__device__ __forceinline__ void requant_i8_fast_x2(float y0, float y1, float s, float rs, uint64_t nz, int8_t &q0,
+                                                   int8_t &q1) {
+    const uint64_t Y = f2pack(y0, y1), RS = splat2(rs), NS = splat2(-s);
+    const uint64_t qa = mulr2(Y, RS, nz);
+    const uint64_t qb = fma2(fma2(NS, qa, Y), RS, qa);
+    float a0, a1;
+    f2unpack(fma2(fma2(NS, qb, Y), RS, qb), a0, a1);
+    a0 = fabsf(y0) <= 0x1p80f ? a0 : y0;
+    a1 = fabsf(y1) <= 0x1p80f ? a1 : y1;
+    float h0, h1;
+    f2unpack(add2(f2pack(a0, a1), f2pack(copysignf(0.49999997f, a0), copysignf(0.49999997f, a1))), h0, h1);
+    int n0 = __float2int_rz(h0), n1 = __float2int_rz(h1);  // saturating, NaN -> 0
+    n0 = n0 > 127 ? 127 : (n0 < -127 ? -127 : n0);
+    n1 = n1 > 127 ? 127 : (n1 < -127 ? -127 : n1);
+    q0 = (int8_t)n0;
+    q1 = (int8_t)n1;
+}
 // out of line: the dividing path of the wide epilogues (scales outside the fast range)
 static __device__ __noinline__ int8_t requant_i8_outline(float y, float s) { return requant_i8(y, s); }
+
+// requant_pack32 with the fast path on paired operations
+__device__ __forceinline__ void requant_pack32_x2(const uint32_t (&v)[32], float s, float rs, bool fast, uint64_t nz,
+                                                  uint32_t (&qb)[8]) {
+    if (fast) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            int8_t a, b, c, d;
+            requant_i8_fast_x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), s, rs, nz, a, b);
+            requant_i8_fast_x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]), s, rs, nz, c, d);
+            qb[j / 4] = (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
+                        ((uint32_t)(uint8_t)d << 24);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            qb[j / 4] = (uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j]), s) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 1]), s) << 8) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 2]), s) << 16) |
+                        ((uint32_t)(uint8_t)requant_i8_outline(__uint_as_float(v[j + 3]), s) << 24);
+    }
+}
 
 // requant_i8 of 32 values (f32 bits) packed 4 to a word, low byte first
 __device__ __forceinline__ void requant_pack32(const uint32_t (&v)[32], float s, float rs, bool fast,

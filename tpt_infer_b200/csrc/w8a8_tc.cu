@@ -251,6 +251,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         // the current chunk's arithmetic is done, so their latency (an L2 round
         // trip behind the operand traffic) overlaps the current chunk's stores
         float sc[32], bi[32];
+        const uint64_t nz2 = opaque_nz2((uint32_t)M >> 31);  // M >= 0
         auto chunk_n0 = [&](int tt, int c) {
             return (tt - (tt / tiles_n) * tiles_n) * BN + half * (BN / 2) + c * 32;
         };
@@ -272,7 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                 tmem_wait_ld();
                 const int n0 = nt * BN + half * (BN / 2) + c * 32;
                 if (!ACC_OUT) {
-                    w8a8_apply32<ACT>(v, a_scale, sc, bi, bias != nullptr);
+                    w8a8_apply32_x2<ACT>(v, a_scale, sc, bi, bias != nullptr, nz2);
                     const bool last = c + 1 == BN / 64;
                     if (!last || t + nclusters < ntiles)
                         w8a8_load_consts(chunk_n0(last ? t + nclusters : t, last ? 0 : c + 1), N, wscale, bias, sc, bi);
@@ -282,7 +283,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                     // lane's row gets 32 consecutive bytes
                     if (m < M) {
                         uint32_t b[8];
-                        requant_pack32(v, q_scale, __frcp_rn(q_scale), requant_fast_ok(q_scale), b);
+                        requant_pack32_x2(v, q_scale, __frcp_rn(q_scale), requant_fast_ok(q_scale), nz2, b);
                         int8_t *dst = Q + (size_t)m * N + n0;
                         if (n0 + 32 <= N && (N & 15) == 0) {
                             reinterpret_cast<uint4 *>(dst)[0] = make_uint4(b[0], b[1], b[2], b[3]);
