@@ -401,6 +401,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
         const bool bulk = (Y && tma_store) || (Q && tma_q);
         const float q_rs = __frcp_rn(q_scale);
         const bool q_fast = requant_fast_ok(q_scale);
+        const uint64_t nz2 = opaque_nz2((uint32_t)OC >> 31);  // OC > 0
         int acc = 0, k = 0;
         uint32_t acc_phase = 0, rphase = 0, rpend = 0;
         int pt = blockIdx.x, pcc = c0, pk = 0;  // residual prefetch cursor: tile, chunk, sequence number
@@ -449,7 +450,11 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                 uint32_t v[32];
                 tmem_ld32(t_base + (uint32_t)(cc * 32), v);
                 tmem_wait_ld();
-                w8a8_epi32<TPT_ACT_NONE>(v, n0, OC, a_scale, wscale, bias);
+                {
+                    float sc[32], bi[32];
+                    w8a8_load_consts(n0, OC, wscale, bias, sc, bi);
+                    w8a8_apply32_x2<TPT_ACT_NONE>(v, a_scale, sc, bi, bias != nullptr, nz2);
+                }
                 act32(v, act);
                 if (R && tma_r) {  // residual: y = ract(conv + r), the ADD_ACT op's f32 add
                     if (live) {
@@ -466,10 +471,17 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
 #pragma unroll
                         for (int c4 = 0; c4 < 8; c4++) {
                             const float4 r = *reinterpret_cast<const float4 *>(sb + ((c4 ^ (lane & 7)) << 4));
-                            v[4 * c4] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4]), r.x));
-                            v[4 * c4 + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 1]), r.y));
-                            v[4 * c4 + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 2]), r.z));
-                            v[4 * c4 + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[4 * c4 + 3]), r.w));
+                            float y0, y1, y2, y3;
+                            f2unpack(add2(f2pack(__uint_as_float(v[4 * c4]), __uint_as_float(v[4 * c4 + 1])),
+                                          f2pack(r.x, r.y)),
+                                     y0, y1);
+                            f2unpack(add2(f2pack(__uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3])),
+                                          f2pack(r.z, r.w)),
+                                     y2, y3);
+                            v[4 * c4] = __float_as_uint(y0);
+                            v[4 * c4 + 1] = __float_as_uint(y1);
+                            v[4 * c4 + 2] = __float_as_uint(y2);
+                            v[4 * c4 + 3] = __float_as_uint(y3);
                         }
                         act32(v, ract);
                     }
@@ -482,7 +494,7 @@ __global__ void __launch_bounds__(cv_threads(MODE, BN), 1)
                 }
                 if (Q && live) {
                     uint32_t qb[8];
-                    requant_pack32(v, q_scale, q_rs, q_fast, qb);
+                    requant_pack32_x2(v, q_scale, q_rs, q_fast, nz2, qb);
                     if (tma_q) {  // 32B swizzle: half h of row `lane` sits at h ^ bit 2 of the row
                         uint8_t *qrow = yg + 3 * 4096 + (k & 1) * 1024 + lane * 32;
                         const int sw = (lane >> 2) & 1;

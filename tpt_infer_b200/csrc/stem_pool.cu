@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
         const float qrs = Q ? __frcp_rn(q_scale) : 0.0f;
         const bool qfast = requant_fast_ok(q_scale);
         const bool has_bias = bias != nullptr;
+        const uint64_t nz2 = opaque_nz2((uint32_t)ss.PH >> 31);  // PH > 0
         uint32_t tphase = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             int okw = 0;
@@ -234,11 +235,20 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ri * SP_OC + c * 32), v);
                 tmem_wait_ld();
 #pragma unroll
-                for (int jj = 0; jj < 32; jj++) {
-                    // y = (float)acc * (a_scale * w_scale[n]) + bias[n], ReLU (the W8A8 epilogue's operations)
-                    float y = __fmul_rn(__int2float_rn((int)v[jj]), cprod[c * 32 + jj]);
-                    if (has_bias) y = __fadd_rn(y, cprod[SP_OC + c * 32 + jj]);
-                    mx[jj] = fmaxf(mx[jj], y > 0.0f ? y : 0.0f);
+                for (int jj = 0; jj < 32; jj += 2) {
+                    // y = (float)acc * (a_scale * w_scale[n]) + bias[n], ReLU (the W8A8 epilogue's
+                    // operations), two channels per paired operation
+                    const float2 cp = *reinterpret_cast<const float2 *>(cprod + c * 32 + jj);
+                    uint64_t y = mulr2(f2pack(__int2float_rn((int)v[jj]), __int2float_rn((int)v[jj + 1])),
+                                       f2pack(cp.x, cp.y), nz2);
+                    if (has_bias) {
+                        const float2 bb = *reinterpret_cast<const float2 *>(cprod + SP_OC + c * 32 + jj);
+                        y = add2(y, f2pack(bb.x, bb.y));
+                    }
+                    float y0, y1;
+                    f2unpack(y, y0, y1);
+                    mx[jj] = fmaxf(mx[jj], y0 > 0.0f ? y0 : 0.0f);
+                    mx[jj + 1] = fmaxf(mx[jj + 1], y1 > 0.0f ? y1 : 0.0f);
                 }
             }
             {
@@ -267,10 +277,16 @@ __global__ void __launch_bounds__(SP_THREADS, 2)
                 const size_t o = (orow + px) * SP_OC + 4 * c4;
                 if (P) *reinterpret_cast<float4 *>(P + o) = m;
                 if (Q) {
-                    const int8_t a = qfast ? requant_i8_fast(m.x, q_scale, qrs) : requant_i8(m.x, q_scale);
-                    const int8_t b = qfast ? requant_i8_fast(m.y, q_scale, qrs) : requant_i8(m.y, q_scale);
-                    const int8_t cq = qfast ? requant_i8_fast(m.z, q_scale, qrs) : requant_i8(m.z, q_scale);
-                    const int8_t d = qfast ? requant_i8_fast(m.w, q_scale, qrs) : requant_i8(m.w, q_scale);
+                    int8_t a, b, cq, d;
+                    if (qfast) {
+                        requant_i8_fast_x2(m.x, m.y, q_scale, qrs, nz2, a, b);
+                        requant_i8_fast_x2(m.z, m.w, q_scale, qrs, nz2, cq, d);
+                    } else {
+                        a = requant_i8(m.x, q_scale);
+                        b = requant_i8(m.y, q_scale);
+                        cq = requant_i8(m.z, q_scale);
+                        d = requant_i8(m.w, q_scale);
+                    }
                     *reinterpret_cast<uint32_t *>(Q + o) = (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) |
                                                            ((uint32_t)(uint8_t)cq << 16) | ((uint32_t)(uint8_t)d << 24);
                 }
