@@ -587,8 +587,9 @@ def profile_kernels(args):
 def profile_plan(args):
     """One model plan on one GPU, calibrated on a seeded batch and frozen, then
     args.warmup + args.steps direct forwards (no CUDA graph, so a profiler sees
-    every launch in order): ResNet-18 (batch 256 by default) or the 12-layer
-    BERT-base encoder over 128 tokens (batch 64)."""
+    every launch in order): ResNet-18 (batch 256 by default), the 12-layer
+    BERT-base encoder over 128 tokens (batch 64), or the 784-512-10 MLP in f32
+    or INT8 (batch 64)."""
     import torch
 
     from tpt_infer_b200 import CudaBackend, graphs, synth
@@ -599,6 +600,10 @@ def profile_plan(args):
     if args.profile_plan == "resnet18":
         B, numel = args.batch or 256, 3 * 224 * 224
         p, x, out = graphs.build_resnet18(be, B, graphs.resnet18_weights(be))
+    elif args.profile_plan in ("mlp", "mlp_int8"):
+        B, numel = args.batch or 64, 784
+        build = graphs.build_mlp_f32 if args.profile_plan == "mlp" else graphs.build_mlp_int8
+        p, x, out = build(be, B, graphs.mlp_weights())[:3]
     else:
         B, numel = args.batch or 64, 128 * 768
         p, x, out = graphs.build_bert(be, B, 128, graphs.bert_weights(be, layers=12))
@@ -663,7 +668,7 @@ def main():
     ap.add_argument("--profile-kernels", action="store_true",
                     help="each main kernel on one case, `--steps` launches each after warm-up: the ncu capture case "
                          "for the per-kernel summaries")
-    ap.add_argument("--profile-plan", choices=["resnet18", "bert"],
+    ap.add_argument("--profile-plan", choices=["resnet18", "bert", "mlp", "mlp_int8"],
                     help="one model plan (calibrated, frozen), `--warmup` + `--steps` forwards at `--batch`: the ncu "
                          "capture case for the launch lists")
     ap.add_argument("--batch", type=int, default=0, help="batch of --profile-plan (default 256 / 64)")
