@@ -31,6 +31,11 @@ def _close(got, want, rel=TOL_TRANSCENDENTAL):
     (32, 64, 48, 7, 8),     # dispatch.rs:501-511
     (64, 784, 512, 9, 10),  # MLP layer 1
     (257, 129, 300, 11, 12),
+    # the resident-K small-output kernel: K at its 1536 maximum (24 chunks), one
+    # past it (the tiled kernels), a ragged last chunk with 16-byte rows
+    (48, 1536, 40, 13, 14),
+    (20, 1537, 36, 15, 16),
+    (16, 100, 16, 17, 18),
 ])
 def test_matmul_bit_identical(cuda, m, k, n, sa, sb):
     a, b = O.lcg_sym(m * k, sa), O.lcg_sym(k * n, sb)

@@ -159,6 +159,9 @@ int launch_unary(tpt_cuda_ctx *ctx, int op, const float *a, float *out, size_t n
 int launch_softmax(tpt_cuda_ctx *ctx, const float *a, float *out, size_t rows, size_t row_len);
 int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m,
                       size_t k, size_t n);
+int launch_matmul_f32_epi(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act, float *out,
+                          size_t m, size_t k, size_t n);
+int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
 int launch_conv2d_f32(tpt_cuda_ctx *ctx, const float *in, const float *w, float *out, const size_t is[4],
                       const size_t ws[4], size_t oh, size_t ow, size_t sh, size_t sw, size_t ph,
                       size_t pw);

@@ -14,7 +14,7 @@
 //
 // Tiling: 128x128 output tile per 256-thread CTA, 8x8 outputs per thread,
 // k-slices of 8 staged through double-buffered shared memory.
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace tpt {
 namespace {
@@ -205,6 +205,128 @@ __global__ void __launch_bounds__(256) k_gemm_f32_small(const float *__restrict_
     if (m < M && n < N) Cout[(size_t)m * N + n] = acc;
 }
 
+// Small-output MatMul with all of K resident in shared memory (K <= MK_KMAX),
+// and the bias + activation of the plan's MatMul fused into its epilogue.
+// Each output is the same sequential chain as above (k ascending, RN multiply
+// then RN add), so it is latency-bound: the kernel's job is to have every
+// operand in shared memory before its chain needs it. A CTA (128 threads)
+// owns 16 rows x 16 columns; thread (ty, tx) computes row ty, columns 2 tx and
+// 2 tx + 1 as two interleaved chains. Right after
+// the dependency wait every thread issues its cp.async copies of all of K
+// (16-byte where rows are 16-byte aligned, else 4-byte), one mbarrier per
+// 64-k chunk, so the chains start on chunk 0 while the later chunks land.
+// Padding rows / columns / k are zero-filled; the chain stops at K.
+constexpr int MK_T = 128;
+constexpr int MK_KC = 64;
+constexpr int MK_KMAX = 1536;  // A and B tiles: 128 K bytes, 192 KB at most
+constexpr int MK_MAXC = MK_KMAX / MK_KC;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+
+__global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const float *__restrict__ A, const float *__restrict__ B,
+                                                          const float *__restrict__ bias, int act,
+                                                          float *__restrict__ Cout, int M, int N, int K, int vecA,
+                                                          int vecB, unsigned *gflags) {
+    using namespace tc;
+    extern __shared__ __align__(16) float mk_smem[];
+    __shared__ __align__(8) uint64_t bars[MK_MAXC];
+    __shared__ int abort_flag;
+    const int nch = (K + MK_KC - 1) / MK_KC, Kp = nch * MK_KC;
+    float *As = mk_smem;           // [16][Kp]
+    float *Bs = mk_smem + 16 * Kp;  // [Kp][16]
+    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+    const int m0 = blockIdx.y * 16, n0 = blockIdx.x * 16;
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int c = 0; c < nch; c++) mbar_init(smem_u32(&bars[c]), MK_T);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_wait();  // A and B may be the previous kernel's outputs
+    pdl_trigger();
+    const uint32_t as = smem_u32(As), bs = smem_u32(Bs);
+    for (int c = 0; c < nch; c++) {
+        const int kc = c * MK_KC;
+        if (vecA) {  // 16 rows x 16 four-float pieces
+            for (int e = tid; e < 256; e += MK_T) {
+                const int r = e >> 4, k = kc + 4 * (e & 15), m = m0 + r;
+                const bool v = m < M && k < K;  // K % 4 == 0
+                cp_async16(as + 4u * (uint32_t)(r * Kp + k), v ? A + (size_t)m * K + k : A, v);
+            }
+        } else {
+            for (int e = tid; e < 1024; e += MK_T) {
+                const int r = e >> 6, k = kc + (e & 63), m = m0 + r;
+                const bool v = m < M && k < K;
+                cp_async4(as + 4u * (uint32_t)(r * Kp + k), v ? A + (size_t)m * K + k : A, v);
+            }
+        }
+        if (vecB) {  // 64 k rows x 4 four-float pieces
+            for (int e = tid; e < 256; e += MK_T) {
+                const int k = kc + (e >> 2), j = 4 * (e & 3), n = n0 + j;
+                const bool v = k < K && n < N;  // N % 4 == 0
+                cp_async16(bs + 4u * (uint32_t)(k * 16 + j), v ? B + (size_t)k * N + n : B, v);
+            }
+        } else {
+            for (int e = tid; e < 1024; e += MK_T) {
+                const int k = kc + (e >> 4), j = e & 15, n = n0 + j;
+                const bool v = k < K && n < N;
+                cp_async4(bs + 4u * (uint32_t)(k * 16 + j), v ? B + (size_t)k * N + n : B, v);
+            }
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bars[c])) : "memory");
+    }
+    float acc0 = 0.0f, acc1 = 0.0f;  // columns 2 tx and 2 tx + 1: two independent chains
+    volatile int *abort_p = &abort_flag;
+    bool ok = true;
+    for (int c = 0; c < nch && ok; c++) {
+        ok = mbar_wait(smem_u32(&bars[c]), 0u, abort_p, gflags, true);
+        if (!ok) break;
+        const float *ar = As + ty * Kp + c * MK_KC;
+        const float *br = Bs + (size_t)c * MK_KC * 16 + 2 * tx;
+        const int kn = min(MK_KC, K - c * MK_KC);
+        if (kn == MK_KC) {
+            // the whole chunk unrolled: its loads can be issued well ahead of
+            // the chains (one warp per SMSP has nothing else to hide them behind)
+#pragma unroll
+            for (int kk = 0; kk < MK_KC; kk += 4) {
+                const float4 a4 = *reinterpret_cast<const float4 *>(ar + kk);
+                const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 b = *reinterpret_cast<const float2 *>(br + (kk + i) * 16);
+                    acc0 = __fadd_rn(acc0, __fmul_rn(av[i], b.x));
+                    acc1 = __fadd_rn(acc1, __fmul_rn(av[i], b.y));
+                }
+            }
+        } else {
+            for (int kk = 0; kk < kn; kk++) {
+                const float2 b = *reinterpret_cast<const float2 *>(br + kk * 16);
+                acc0 = __fadd_rn(acc0, __fmul_rn(ar[kk], b.x));
+                acc1 = __fadd_rn(acc1, __fmul_rn(ar[kk], b.y));
+            }
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort) no copy lands after the CTA exits
+    if (!ok) return;
+    const float v[2] = {acc0, acc1};
+    const int m = m0 + ty;
+    if (m < M) {
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int n = n0 + 2 * tx + j;
+            if (n >= N) continue;
+            float y = v[j];
+            if (bias) y = __fadd_rn(y, __ldg(bias + n));
+            Cout[(size_t)m * N + n] = apply_act(y, act);
+        }
+    }
+}
+
 // ONNX Gemm, Y = alpha * op(A) op(B) + beta * C (C: none, [N] broadcast, or
 // [M,N]): the small-tile structure above with transposable operands (each tile
 // load walks the operand's contiguous dimension with consecutive threads), the
@@ -278,8 +400,52 @@ int launch_gemm_onnx(tpt_cuda_ctx *ctx, const float *a, const float *b, const fl
     return after_launch(ctx, "gemm_onnx");
 }
 
+// The resident-K small-output kernel when it applies (the 128 x 128 tiling
+// would leave SMs idle and 1 <= K <= MK_KMAX); handled = false otherwise.
+static int launch_matmul_rows(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act,
+                              float *out, size_t m, size_t k, size_t n, bool *handled) {
+    *handled = false;
+    const size_t tiles128 = ((n + BN - 1) / BN) * ((m + BM - 1) / BM);
+    if (m == 0 || n == 0 || k == 0 || k > (size_t)MK_KMAX || tiles128 >= (size_t)ctx->sm_count || (m + 15) / 16 > 65535 ||
+        m > INT32_MAX || n > INT32_MAX || (((uintptr_t)a | (uintptr_t)b) & 3))
+        return TPT_OK;
+    static bool attr_done[64] = {};
+    const int dev = ctx->device & 63;
+    if (!attr_done[dev]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(k_matmul_f32_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * MK_KMAX);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "matmul_f32_rows smem attribute");
+        attr_done[dev] = true;
+    }
+    const size_t kp = (k + MK_KC - 1) / MK_KC * MK_KC;
+    const int vec_a = (k % 4 == 0 && ((uintptr_t)a & 15) == 0) ? 1 : 0;
+    const int vec_b = (n % 4 == 0 && ((uintptr_t)b & 15) == 0) ? 1 : 0;
+    dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16));
+    *handled = true;
+    launch_pdl(k_matmul_f32_rows, grid, MK_T, 128 * kp, ctx->stream, a, b, bias, act, out, (int)m, (int)n, (int)k,
+               vec_a, vec_b, ctx->d_flags);
+    return after_launch(ctx, "matmul_f32_rows");
+}
+
+// MatMul followed by the plan's bias + activation: one launch where the
+// resident-K kernel applies, else the MatMul and then k_bias_act
+int launch_matmul_f32_epi(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act, float *out,
+                          size_t m, size_t k, size_t n) {
+    bool handled = false;
+    int st = launch_matmul_rows(ctx, a, b, bias, act, out, m, k, n, &handled);
+    if (st || handled) return st;
+    st = launch_matmul_f32(ctx, a, b, out, m, k, n);
+    if (st || (!bias && act == 0)) return st;
+    return launch_bias_act(ctx, out, bias, out, m, n, act);
+}
+
 int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m, size_t k,
                       size_t n) {
+    {
+        bool handled = false;
+        int st = launch_matmul_rows(ctx, a, b, nullptr, 0, out, m, k, n, &handled);
+        if (st || handled) return st;
+    }
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return TPT_UNSUPPORTED;
     if (k == 0) {
         cudaError_t e = cudaMemsetAsync(out, 0, m * n * 4, ctx->stream);

@@ -185,9 +185,8 @@ int run_op(tpt_cuda_plan *p, PlanOp &po) {
             return launch_w8a8(ctx, Q(p, o.in0), d[0], o.w->k, o.w, sa, F(p, o.in1), o.act, F(p, o.out), nullptr);
         }
         case TPT_OP_MATMUL_F32: {  // [m,k] x [k,n] (+bias, act)
-            st = launch_matmul_f32(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], d[1], d[2]);
-            if (st || (o.in2 < 0 && o.act == 0)) return st;
-            return launch_bias_act(ctx, F(p, o.out), F(p, o.in2), F(p, o.out), d[0], d[2], o.act);
+            return launch_matmul_f32_epi(ctx, F(p, o.in0), F(p, o.in1), o.in2 < 0 ? nullptr : F(p, o.in2), o.act,
+                                         F(p, o.out), d[0], d[1], d[2]);
         }
         case TPT_OP_BIAS_ACT:
             return launch_bias_act(ctx, F(p, o.in0), F(p, o.in1), F(p, o.out), d[0], d[1], o.act);
