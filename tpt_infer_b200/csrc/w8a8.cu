@@ -58,7 +58,7 @@ __device__ __forceinline__ int dot16(int4 a, int4 b, int acc) {
 constexpr int GEMV_CH = 8;  // 16-byte chunks per lane per pass
 
 template <int MM, bool A_REG>
-__global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
+__global__ void __launch_bounds__(256, 2) k_w8a8_gemv(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
                                                    const float *__restrict__ wscale, const float *__restrict__ bias,
                                                    int M, int N, int K, float a_scale, int act,
                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
@@ -86,6 +86,54 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                                                  : make_int4(0, 0, 0, 0);
             }
     }
+    if constexpr (MM == 1 && A_REG) {
+        // one row of activations, one pass per row (K <= 4096): a warp's rows are
+        // taken two at a time with both rows' loads issued before the first
+        // dp4a, so the ~1.7 rows a warp holds at K = N = 4096 stream in one
+        // round trip instead of two (8 KB in flight per warp, 128 KB per SM)
+        for (int n = n_begin; n < n_end; n += 2 * nwarps) {
+            const int n2 = n + nwarps;
+            const bool two = n2 < n_end;
+            const int4 *w0 = reinterpret_cast<const int4 *>(Wt + (size_t)n * K);
+            const int4 *w1 = reinterpret_cast<const int4 *>(Wt + (size_t)(two ? n2 : n) * K);
+            int4 wa[GEMV_CH], wb[GEMV_CH];
+#pragma unroll
+            for (int j = 0; j < GEMV_CH; j++) {
+                const int c = lane + 32 * j;
+                wa[j] = c < chunks ? __ldcs(w0 + c) : make_int4(0, 0, 0, 0);
+                wb[j] = (two && c < chunks) ? __ldcs(w1 + c) : make_int4(0, 0, 0, 0);
+            }
+            int acc0 = 0, acc1 = 0;
+#pragma unroll
+            for (int j = 0; j < GEMV_CH; j++) {
+                acc0 = dot16(ar[0][j], wa[j], acc0);
+                acc1 = dot16(ar[0][j], wb[j], acc1);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, o);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, o);
+            }
+            if (lane == 0) {
+                const float ws0 = __ldg(wscale + n);
+                if (ACC)
+                    ACC[n] = acc0;
+                else if (Q)
+                    Q[n] = requant_i8(w8a8_epilogue(acc0, a_scale, ws0, bias, n, act), q_scale);
+                else
+                    Y[n] = w8a8_epilogue(acc0, a_scale, ws0, bias, n, act);
+                if (two) {
+                    const float ws1 = __ldg(wscale + n2);
+                    if (ACC)
+                        ACC[n2] = acc1;
+                    else if (Q)
+                        Q[n2] = requant_i8(w8a8_epilogue(acc1, a_scale, ws1, bias, n2, act), q_scale);
+                    else
+                        Y[n2] = w8a8_epilogue(acc1, a_scale, ws1, bias, n2, act);
+                }
+            }
+        }
+    } else {
     for (int n = n_begin; n < n_end; n += nwarps) {
         const int4 *wrow = reinterpret_cast<const int4 *>(Wt + (size_t)n * K);
         int acc[MM];
@@ -133,6 +181,7 @@ __global__ void __launch_bounds__(256) k_w8a8_gemv(const int8_t *__restrict__ A,
                 }
             }
         }
+    }
     }
 }
 
