@@ -37,7 +37,10 @@ def w8a8_case(m, n, k, seed=100, with_bias=True):
                                    (4, 257, 4160), (16, 1024, 4096), (64, 2048, 2048), (5, 200, 384),
                                    # the small-batch MMA kernel: 1, 2 and 4 activation tiles
                                    (3, 4096, 4096), (8, 1000, 1024), (12, 130, 512), (24, 500, 2048),
-                                   (32, 4096, 4096), (20, 17, 256)])
+                                   (32, 4096, 4096), (20, 17, 256),
+                                   # the resident-K kernel (M <= 64, K <= 1536): K at its maximum,
+                                   # a 10-channel head
+                                   (40, 1000, 1536), (64, 10, 512)])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_w8a8_bit_exact(cuda, m, n, k, act):
     if act and m * n * k > 1 << 26:

@@ -19,7 +19,7 @@
 
 #include <new>
 
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace tpt {
 
@@ -185,6 +185,93 @@ __global__ void __launch_bounds__(256, 2) k_w8a8_gemv(const int8_t *__restrict__
     }
 }
 
+// Small W8A8 (M <= 64, K <= 1536, K % 16 == 0, few output tiles): all of K
+// resident in shared memory, dp4a. A CTA (128 threads) owns 16 activation rows
+// x 16 output channels; thread (ty, tx) computes row ty, channels tx and tx + 8.
+// Right after the dependency wait every thread issues its 16-byte cp.async
+// copies of the 16 activation rows and 16 weight rows (rows padded by 16 bytes
+// so that the 8 channel rows a warp reads at one k fall in distinct banks),
+// one mbarrier per 64-k chunk, so the sums start on chunk 0 while the later
+// chunks land. Padding rows and k are zero-filled (zero products). Integer
+// sums are exact, then the same w8a8_epilogue as the other kernels. For the
+// short layers (an MLP's 64 x 784 x 512, a 10-way head) where the
+// tensor-core kernels' fixed cost (TMEM, clusters, rings) is most of their
+// time.
+constexpr int WR_T = 128;
+constexpr int WR_KC = 64;
+constexpr int WR_KMAX = 1536;
+constexpr int WR_MAXC = WR_KMAX / WR_KC;
+
+__global__ void __launch_bounds__(WR_T) k_w8a8_rows(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
+                                                    const float *__restrict__ wscale, const float *__restrict__ bias,
+                                                    int M, int N, int K, float a_scale, int act,
+                                                    float *__restrict__ Y, int32_t *__restrict__ ACC,
+                                                    int8_t *__restrict__ Q, float q_scale, unsigned *gflags) {
+    using namespace tc;
+    extern __shared__ __align__(16) uint8_t wr_smem[];
+    __shared__ __align__(8) uint64_t bars[WR_MAXC];
+    __shared__ int abort_flag;
+    const int nch = (K + WR_KC - 1) / WR_KC, rs = nch * WR_KC + 16;  // padded row stride
+    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+    const int m0 = blockIdx.y * 16, n0 = blockIdx.x * 16;
+    const uint8_t *As = wr_smem, *Ws = wr_smem + 16 * rs;
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int c = 0; c < nch; c++) mbar_init(smem_u32(&bars[c]), WR_T);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_wait();  // the activations are the previous kernel's output
+    pdl_trigger();
+    const uint32_t base = smem_u32(wr_smem);
+    for (int c = 0; c < nch; c++) {
+        // 32 rows (16 activation, 16 weight) x 4 sixteen-byte pieces: one per thread
+        const int r = tid >> 2, k = c * WR_KC + 16 * (tid & 3);
+        const bool is_w = r >= 16;
+        const int row = is_w ? n0 + r - 16 : m0 + r;
+        const bool v = (is_w ? row < N : row < M) && k < K;
+        const int8_t *src = v ? (is_w ? Wt : A) + (size_t)row * K + k : A;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(base + (uint32_t)(r * rs + k)), "l"(src),
+                     "r"(v ? 16 : 0)
+                     : "memory");
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bars[c])) : "memory");
+    }
+    volatile int *abort_p = &abort_flag;
+    int acc0 = 0, acc1 = 0;
+    bool ok = true;
+    const uint8_t *ar = As + ty * rs, *w0 = Ws + tx * rs, *w1 = Ws + (tx + 8) * rs;
+    for (int c = 0; c < nch && ok; c++) {
+        ok = mbar_wait(smem_u32(&bars[c]), 0u, abort_p, gflags, true);
+        if (!ok) break;
+#pragma unroll
+        for (int q = 0; q < WR_KC / 16; q++) {
+            const int k = c * WR_KC + 16 * q;
+            const int4 a = *reinterpret_cast<const int4 *>(ar + k);
+            acc0 = dot16(a, *reinterpret_cast<const int4 *>(w0 + k), acc0);
+            acc1 = dot16(a, *reinterpret_cast<const int4 *>(w1 + k), acc1);
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort) no copy lands after the CTA exits
+    if (!ok) return;
+    const int m = m0 + ty;
+    if (m >= M) return;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int n = n0 + tx + 8 * j;
+        if (n >= N) continue;
+        const int acc = j ? acc1 : acc0;
+        if (ACC)
+            ACC[(size_t)m * N + n] = acc;
+        else {
+            const float y = w8a8_epilogue(acc, a_scale, __ldg(wscale + n), bias, n, act);
+            if (Q)
+                Q[(size_t)m * N + n] = requant_i8(y, q_scale);
+            else
+                Y[(size_t)m * N + n] = y;
+        }
+    }
+}
+
 // General dp4a tile GEMM: 128x128 outputs per CTA, 8x8 per thread, K in
 // 32-byte slices (K % 16 == 0; a trailing 16-byte half is zero-filled).
 __global__ void __launch_bounds__(256) k_w8a8_simt(const int8_t *__restrict__ A, const int8_t *__restrict__ Wt,
@@ -315,6 +402,23 @@ int launch_w8a8(tpt_cuda_ctx *ctx, const int8_t *a, size_t m, size_t k, const tp
             TPT_GEMV(4, false);
 #undef TPT_GEMV
         return after_launch(ctx, "w8a8_gemv");
+    }
+    if (m <= 64 && k % 16 == 0 && k <= (size_t)WR_KMAX && ((((uintptr_t)a) | ((uintptr_t)wt)) & 15) == 0 &&
+        ((n + 15) / 16) * ((m + 15) / 16) <= (size_t)2 * ctx->sm_count) {
+        // short layers: the resident-K dp4a kernel
+        static bool attr_done[64] = {};
+        const int dev = ctx->device & 63;
+        if (!attr_done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(k_w8a8_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 32 * (WR_KMAX + 16));
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "w8a8_rows smem attribute");
+            attr_done[dev] = true;
+        }
+        const size_t nch = (k + WR_KC - 1) / WR_KC;
+        dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16));
+        launch_pdl(k_w8a8_rows, grid, WR_T, 32 * (nch * WR_KC + 16), ctx->stream, a, wt, w->scales, bias, (int)m,
+                   (int)n, (int)k, a_scale, act, y, acc, rq.q, rq.scale, ctx->d_flags);
+        return after_launch(ctx, "w8a8_rows");
     }
     bool handled = false;
     if (m <= 64) {
