@@ -17,6 +17,10 @@
 #include "tc_common.cuh"
 
 namespace tpt {
+
+bool make_tmap_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uint64_t rows, uint64_t cols,
+                  uint32_t elem_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
+
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 8, NT = 256;
@@ -228,7 +232,15 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool va
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
 }
 
-__global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const float *__restrict__ A, const float *__restrict__ B,
+// TMA: with 16-byte aligned rows the tiles come in as tensor boxes instead
+// (A: 16 rows x 64 floats = 256-byte lines, B: 64 k rows x 16 floats per
+// chunk), one thread issuing them: the TMA unit fills shared memory faster
+// than per-thread 16-byte copies here. A then sits chunk-major
+// ([chunk][16][64]); B keeps the [k][16] layout.
+template <bool TMA>
+__global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const __grid_constant__ CUtensorMap tmA,
+                                                          const __grid_constant__ CUtensorMap tmB,
+                                                          const float *__restrict__ A, const float *__restrict__ B,
                                                           const float *__restrict__ bias, int act,
                                                           float *__restrict__ Cout, int M, int N, int K, int vecA,
                                                           int vecB, unsigned *gflags) {
@@ -237,19 +249,29 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const float *__restric
     __shared__ __align__(8) uint64_t bars[MK_MAXC];
     __shared__ int abort_flag;
     const int nch = (K + MK_KC - 1) / MK_KC, Kp = nch * MK_KC;
-    float *As = mk_smem;           // [16][Kp]
-    float *Bs = mk_smem + 16 * Kp;  // [Kp][16]
+    const uint32_t raw = smem_u32(mk_smem), as = (raw + 127u) & ~127u, bs = as + 64u * (uint32_t)Kp;
+    float *As = mk_smem + (as - raw) / 4;  // [16][Kp], or [chunk][16][64] with TMA
+    float *Bs = As + 16 * Kp;              // [Kp][16]
     const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
     const int m0 = blockIdx.y * 16, n0 = blockIdx.x * 16;
     if (tid == 0) {
         abort_flag = 0;
-        for (int c = 0; c < nch; c++) mbar_init(smem_u32(&bars[c]), MK_T);
+        for (int c = 0; c < nch; c++) mbar_init(smem_u32(&bars[c]), TMA ? 1 : MK_T);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     pdl_wait();  // A and B may be the previous kernel's outputs
     pdl_trigger();
-    const uint32_t as = smem_u32(As), bs = smem_u32(Bs);
+    if constexpr (TMA) {
+        if (tid == 0) {
+            for (int c = 0; c < nch; c++) {
+                const uint32_t bar = smem_u32(&bars[c]);
+                mbar_arrive_expect_tx(bar, 2u * 16u * MK_KC * 4u);  // out-of-range rows / columns / k read as 0
+                tma_load_2d(as + (uint32_t)c * 16u * MK_KC * 4u, &tmA, bar, c * MK_KC, m0);
+                tma_load_2d(bs + (uint32_t)c * MK_KC * 16u * 4u, &tmB, bar, n0, c * MK_KC);
+            }
+        }
+    } else
     for (int c = 0; c < nch; c++) {
         const int kc = c * MK_KC;
         if (vecA) {  // 16 rows x 16 four-float pieces
@@ -286,7 +308,7 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const float *__restric
     for (int c = 0; c < nch && ok; c++) {
         ok = mbar_wait(smem_u32(&bars[c]), 0u, abort_p, gflags, true);
         if (!ok) break;
-        const float *ar = As + ty * Kp + c * MK_KC;
+        const float *ar = TMA ? As + (c * 16 + ty) * MK_KC : As + ty * Kp + c * MK_KC;
         const float *br = Bs + (size_t)c * MK_KC * 16 + 2 * tx;
         const int kn = min(MK_KC, K - c * MK_KC);
         if (kn == MK_KC) {
@@ -311,7 +333,12 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const float *__restric
             }
         }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort) no copy lands after the CTA exits
+    if (TMA) {
+        if (!ok && tid == 0)  // (after an abort) the boxes in flight land before the CTA exits
+            for (int c = 0; c < nch; c++) mbar_wait(smem_u32(&bars[c]), 0u, abort_p, gflags, false);
+    } else {
+        asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort) no copy lands after the CTA exits
+    }
     if (!ok) return;
     const float v[2] = {acc0, acc1};
     const int m = m0 + ty;
@@ -412,18 +439,30 @@ static int launch_matmul_rows(tpt_cuda_ctx *ctx, const float *a, const float *b,
     static bool attr_done[64] = {};
     const int dev = ctx->device & 63;
     if (!attr_done[dev]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(k_matmul_f32_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * MK_KMAX);
+        cudaError_t e = cudaFuncSetAttribute(k_matmul_f32_rows<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             128 * MK_KMAX + 128);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_matmul_f32_rows<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     128 * MK_KMAX + 128);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "matmul_f32_rows smem attribute");
         attr_done[dev] = true;
     }
     const size_t kp = (k + MK_KC - 1) / MK_KC * MK_KC;
     const int vec_a = (k % 4 == 0 && ((uintptr_t)a & 15) == 0) ? 1 : 0;
     const int vec_b = (n % 4 == 0 && ((uintptr_t)b & 15) == 0) ? 1 : 0;
+    CUtensorMap ta, tb;
+    const bool tma = vec_a && vec_b &&
+                     make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, m, k, 4, MK_KC, 16,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                     make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, b, k, n, 4, 16, MK_KC, CU_TENSOR_MAP_SWIZZLE_NONE);
     dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16));
     *handled = true;
-    launch_pdl(k_matmul_f32_rows, grid, MK_T, 128 * kp, ctx->stream, a, b, bias, act, out, (int)m, (int)n, (int)k,
-               vec_a, vec_b, ctx->d_flags);
+    if (tma)
+        launch_pdl(k_matmul_f32_rows<true>, grid, MK_T, 128 * kp + 128, ctx->stream, ta, tb, a, b, bias, act, out,
+                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags);
+    else
+        launch_pdl(k_matmul_f32_rows<false>, grid, MK_T, 128 * kp + 128, ctx->stream, ta, tb, a, b, bias, act, out,
+                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags);
     return after_launch(ctx, "matmul_f32_rows");
 }
 
