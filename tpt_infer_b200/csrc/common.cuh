@@ -161,6 +161,8 @@ int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *
                       size_t k, size_t n);
 int launch_matmul_f32_epi(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act, float *out,
                           size_t m, size_t k, size_t n);
+int launch_matmul_f32_softmax(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act,
+                              float *out, float *softmax_out, size_t m, size_t k, size_t n, bool *handled);
 int launch_bias_act(tpt_cuda_ctx *ctx, const float *x, const float *bias, float *y, size_t rows, size_t cols, int act);
 int launch_conv2d_f32(tpt_cuda_ctx *ctx, const float *in, const float *w, float *out, const size_t is[4],
                       const size_t ws[4], size_t oh, size_t ow, size_t sh, size_t sw, size_t ph,

@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const __grid_constant_
                                                           const float *__restrict__ A, const float *__restrict__ B,
                                                           const float *__restrict__ bias, int act,
                                                           float *__restrict__ Cout, int M, int N, int K, int vecA,
-                                                          int vecB, unsigned *gflags) {
+                                                          int vecB, unsigned *gflags, float *__restrict__ Ysm) {
     using namespace tc;
     extern __shared__ __align__(16) float mk_smem[];
     __shared__ __align__(8) uint64_t bars[MK_MAXC];
@@ -339,7 +339,8 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const __grid_constant_
     } else {
         asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort) no copy lands after the CTA exits
     }
-    if (!ok) return;
+    __shared__ float zt[16][17];  // the tile's outputs, for a fused softmax
+    if (!__syncthreads_and(ok)) return;
     const float v[2] = {acc0, acc1};
     const int m = m0 + ty;
     if (m < M) {
@@ -349,8 +350,30 @@ __global__ void __launch_bounds__(MK_T) k_matmul_f32_rows(const __grid_constant_
             if (n >= N) continue;
             float y = v[j];
             if (bias) y = __fadd_rn(y, __ldg(bias + n));
-            Cout[(size_t)m * N + n] = apply_act(y, act);
+            y = apply_act(y, act);
+            Cout[(size_t)m * N + n] = y;
+            zt[ty][2 * tx + j] = y;
         }
+    }
+    if (!Ysm) return;
+    // Softmax of each row (N <= 16: one tile holds whole rows), written to
+    // Ysm with k_softmax_warp's operations and order (a warp per row, lane j
+    // holding element j), so the result is that kernel's, bit for bit
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int r = warp; r < 16; r += MK_T / 32) {
+        const int mr = m0 + r;
+        if (mr >= M) break;
+        float mx = -INFINITY;
+        if (lane < N) mx = fmaxf(mx, zt[r][lane]);
+        mx = warp_max(mx);
+        float s = 0.0f, e = 0.0f;
+        if (lane < N) {
+            e = expf(zt[r][lane] - mx);
+            s += e;
+        }
+        s = warp_sum(s);
+        if (lane < N) Ysm[(size_t)mr * N + lane] = __fdiv_rn(e, s);
     }
 }
 
@@ -430,8 +453,9 @@ int launch_gemm_onnx(tpt_cuda_ctx *ctx, const float *a, const float *b, const fl
 // The resident-K small-output kernel when it applies (the 128 x 128 tiling
 // would leave SMs idle and 1 <= K <= MK_KMAX); handled = false otherwise.
 static int launch_matmul_rows(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act,
-                              float *out, size_t m, size_t k, size_t n, bool *handled) {
+                              float *out, size_t m, size_t k, size_t n, bool *handled, float *softmax_out = nullptr) {
     *handled = false;
+    if (softmax_out && n > 16) return TPT_OK;
     const size_t tiles128 = ((n + BN - 1) / BN) * ((m + BM - 1) / BM);
     if (m == 0 || n == 0 || k == 0 || k > (size_t)MK_KMAX || tiles128 >= (size_t)ctx->sm_count || (m + 15) / 16 > 65535 ||
         m > INT32_MAX || n > INT32_MAX || (((uintptr_t)a | (uintptr_t)b) & 3))
@@ -459,10 +483,10 @@ static int launch_matmul_rows(tpt_cuda_ctx *ctx, const float *a, const float *b,
     *handled = true;
     if (tma)
         launch_pdl(k_matmul_f32_rows<true>, grid, MK_T, 128 * kp + 128, ctx->stream, ta, tb, a, b, bias, act, out,
-                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags);
+                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags, softmax_out);
     else
         launch_pdl(k_matmul_f32_rows<false>, grid, MK_T, 128 * kp + 128, ctx->stream, ta, tb, a, b, bias, act, out,
-                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags);
+                   (int)m, (int)n, (int)k, vec_a, vec_b, ctx->d_flags, softmax_out);
     return after_launch(ctx, "matmul_f32_rows");
 }
 
@@ -476,6 +500,14 @@ int launch_matmul_f32_epi(tpt_cuda_ctx *ctx, const float *a, const float *b, con
     st = launch_matmul_f32(ctx, a, b, out, m, k, n);
     if (st || (!bias && act == 0)) return st;
     return launch_bias_act(ctx, out, bias, out, m, n, act);
+}
+
+// MatMul (+ bias, activation) followed by a Softmax over its rows (n <= 16)
+// in one launch, both outputs written; handled = false when the resident-K
+// kernel does not apply
+int launch_matmul_f32_softmax(tpt_cuda_ctx *ctx, const float *a, const float *b, const float *bias, int act,
+                              float *out, float *softmax_out, size_t m, size_t k, size_t n, bool *handled) {
+    return launch_matmul_rows(ctx, a, b, bias, act, out, m, k, n, handled, softmax_out);
 }
 
 int launch_matmul_f32(tpt_cuda_ctx *ctx, const float *a, const float *b, float *out, size_t m, size_t k,

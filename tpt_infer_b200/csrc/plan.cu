@@ -761,6 +761,23 @@ int run_ops(tpt_cuda_plan *p, const int *out_ids, size_t n_out) {
                 continue;
             }
         }
+        // MATMUL_F32 -> SOFTMAX of its rows (at most 16 wide): one launch writes
+        // both tensors (the matmul's output is still written, for its other
+        // readers or the caller); the softmax has k_softmax_warp's arithmetic
+        if (o.kind == TPT_OP_MATMUL_F32 && i + 1 < p->ops.size()) {
+            const tpt_plan_op &sm = p->ops[i + 1].op;
+            if (sm.kind == TPT_OP_SOFTMAX && sm.in0 == o.out && sm.dims[0] == o.dims[0] && sm.dims[1] == o.dims[2] &&
+                o.dims[2] <= 16) {
+                bool handled = false;
+                int st = launch_matmul_f32_softmax(p->ctx, F(p, o.in0), F(p, o.in1), F(p, o.in2), o.act, F(p, o.out),
+                                                   F(p, sm.out), o.dims[0], o.dims[1], o.dims[2], &handled);
+                if (st) return st;
+                if (handled) {
+                    i++;
+                    continue;
+                }
+            }
+        }
         // ATTENTION -> QUANTIZE of a context read by nothing else: int8 straight from the kernel
         if (!p->calibrating && o.kind == TPT_OP_ATTENTION && i + 1 < p->ops.size()) {
             PlanOp &nq = p->ops[i + 1];
