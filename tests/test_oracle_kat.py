@@ -374,14 +374,28 @@ def test_runtime_pool_batchnorm_transpose_concat_kats():
         [5, 7, 13, 15]
     g = O.average_pool2d([1, 2, 3, 6], 1, 1, 2, 2, (2, 2), (1, 1), (0, 0))
     assert abs(g[0] - 3.0) < 1e-6
-    # batch_norm_channel_mode (kernels.rs:676-695)
+    # batch_norm_channel_mode (kernels.rs:698-717)
     y = O.batch_norm([1, 2, 3, 4], [1, 2, 1, 2], [2, 1], [0, 10], [1, 3], [1, 1], 0.0)
     assert y.tolist() == [0, 2, 10, 11]
-    # transpose_swaps_axes (:706-711)
+    # transpose_swaps_axes (:729-735)
     assert O.transpose([1, 2, 3, 4, 5, 6], [2, 3], [1, 0]).tolist() == [1, 4, 2, 5, 3, 6]
-    # concat_streams_operands (:718-727): two [1,1,2] on axis 1
+    # concat_streams_operands (:745-755): two [1,1,2] on axis 1
     out, od = O.concat([[1, 2], [3, 4]], [[1, 1, 2], [1, 1, 2]], 1)
     assert out.tolist() == [1, 2, 3, 4] and od == [1, 2, 2]
+
+
+def test_runtime_sqrt_through_batch_norm():
+    # sqrt_f32_matches_known_values (kernels.rs:719-727), seen through the
+    # element mode of batch_norm (:468-473): x = 1, mean = 0, scale = 1,
+    # bias = 0, eps = 0 gives out = 1 / sqrt_f32(var)
+    var = np.array([0.0, 1.0, 4.0, 2.0, -1.0, np.inf], np.float32)
+    y = O.batch_norm(np.ones(6), [6], np.ones(6), np.zeros(6), np.zeros(6), var, 0.0)
+    assert y[0] == np.inf                      # sqrt_f32(0) == 0
+    assert abs(y[1] - 1.0) < 1e-6              # sqrt_f32(1) ~ 1
+    assert abs(y[2] - 0.5) < 1e-5 / 4          # sqrt_f32(4) ~ 2
+    assert abs(1.0 / y[3] - np.sqrt(2.0)) < 1e-5  # sqrt_f32(2) ~ SQRT_2
+    assert np.isnan(y[4])                      # sqrt_f32(-1) is NaN
+    assert y[5] == 0.0                         # sqrt_f32(inf) == inf
 
 
 def test_runtime_dispatch_coverage_graph_kats():
