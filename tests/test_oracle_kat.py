@@ -451,3 +451,20 @@ def test_deterministic_exp_and_gelu_accuracy():
     g = O.normal(200001, 5, 0.0, 4.0)
     assert np.max(np.abs(O.gelu_det(g) - O.gelu(g)) / (1 + np.abs(O.gelu(g)))) < 1e-6
     assert O.gelu_det([0.0])[0] == 0.0 and np.isnan(O.gelu_det([np.nan])[0])
+
+
+def test_dispatch_softmax_and_gelu_cases():
+    # softmax_matches_naive_and_rows_sum_to_one (dispatch.rs:450-467): lcg(14,
+    # seed 14) as 2 rows of 7, each row summing to 1 within 1e-5
+    sm = O.softmax(O.lcg_sym(14, 14), 7)
+    assert np.all(np.abs(sm.reshape(2, 7).sum(axis=1) - 1.0) < 1e-5)
+    # gelu_matches_scalar_reference (dispatch.rs:482-497): lcg(50, seed 16)
+    # against the tanh formula in f32, with assert_close's 1e-4 (1 + |want|)
+    # (dispatch.rs:284-295); the fused epilogues' deterministic GELU meets it too
+    x = O.lcg_sym(50, 16)
+    f = np.float32
+    inner = f(0.7978846) * (x + f(0.044715) * x * x * x)
+    want = f(0.5) * x * (f(1.0) + np.tanh(inner))
+    for got in (O.gelu(x), O.gelu_det(x)):
+        assert np.all(np.isfinite(got))
+        assert np.all(np.abs(got - want) <= 1e-4 * (1.0 + np.abs(want)))
