@@ -87,6 +87,10 @@ def execute_graph(graph, inputs, quantized=None, scales=None, calib=None):
             y = O.gelu(inp(0)[0])
         elif k == "Softmax":
             x, xd = inp(0)
+            ax = a.get("axis", -1)
+            if (ax + len(xd) if ax < 0 else ax) != len(xd) - 1:
+                # exec.rs:432-441: the HAL softmax normalizes rows of the last dim only
+                raise NotImplementedError("Softmax")
             y = O.softmax(x, xd[-1])
         elif k in ("Reshape", "Flatten"):
             y = np.array(inp(0)[0], np.float32, copy=True)

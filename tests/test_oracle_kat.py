@@ -468,3 +468,33 @@ def test_dispatch_softmax_and_gelu_cases():
     for got in (O.gelu(x), O.gelu_det(x)):
         assert np.all(np.isfinite(got))
         assert np.all(np.abs(got - want) <= 1e-4 * (1.0 + np.abs(want)))
+
+
+def test_runtime_batch_norm_softmax_graph_kats():
+    # crates/tpt-infer-runtime/src/tests.rs, replayed through the oracle's graph walk
+    from oracle import graph_exec
+    from tpt_infer_b200 import lowering as L
+
+    # batch_norm_dispatches (tests.rs:323-356): parameters as initializers
+    g = L.ComputationGraph()
+    x = g.add_input([1, 2, 1, 2], "x")
+    ps = [g.add_weight(nm, [2], v) for nm, v in (("scale", [2.0, 1.0]), ("bias", [0.0, 10.0]),
+                                                ("mean", [1.0, 3.0]), ("var", [1.0, 1.0]))]
+    y = g.add_node(L.Operator.batch_norm(0.0), [x] + ps, [1, 2, 1, 2])
+    g.mark_output(y)
+    assert graph_exec.execute_graph(g, [np.array([1, 2, 3, 4], np.float32)])[0].ravel().tolist() == [0, 2, 10, 11]
+    # softmax_non_last_axis_is_unsupported (tests.rs:358-370)
+    g = L.ComputationGraph()
+    x = g.add_input([2, 3], "x")
+    y = g.add_node(L.Operator.softmax(0), [x], [2, 3])
+    g.mark_output(y)
+    with pytest.raises(NotImplementedError):
+        graph_exec.execute_graph(g, [np.ones(6, np.float32)])
+    # selected_backend_executes (tests.rs:372-400): relu then softmax, sum 1, argmax 3
+    g = L.ComputationGraph()
+    x = g.add_input([1, 4], "x")
+    h = g.add_node(L.Operator.relu(), [x], [1, 4])
+    y = g.add_node(L.Operator.softmax(-1), [h], [1, 4])
+    g.mark_output(y)
+    out = graph_exec.execute_graph(g, [np.array([-1.0, 2.0, -3.0, 4.0], np.float32)])[0].ravel()
+    assert abs(out.sum() - 1.0) < 1e-4 and int(np.argmax(out)) == 3 and out[0] == out[2]
