@@ -111,3 +111,36 @@ def test_loader_rejects_malformed_bytes():
 
         good = onnx.save_bytes(_sample_graph(L))
         onnx.load_from_bytes(good[:-1] + bytes([99]))
+
+
+def test_shape_inference_reference_cases():
+    # crates/tpt-infer-onnx/src/shapes.rs:308-373: the shapes of MatMul, Conv,
+    # Flatten and a dynamic batch, and kernels that do not fit their input
+    from tpt_infer_b200 import onnx
+    from tpt_infer_b200.lowering import Operator as Op
+
+    assert onnx._infer(Op.matmul(), [[1, 784], [784, 10]]) == [1, 10]
+    assert onnx._infer(Op.conv2d((1, 1), (1, 1)), [[1, 3, 224, 224], [8, 3, 3, 3]]) == [1, 8, 224, 224]
+    assert onnx._infer(Op.flatten(1), [[1, 3, 32, 32]]) == [1, 3072]
+    assert onnx._infer(Op.relu(), [[0, 128]]) == [0, 128]
+    assert onnx._infer(Op.average_pool2d((0, 0), (1, 1), (0, 0)), [[2, 5, 7, 7]]) == [2, 5, 1, 1]
+    with pytest.raises(onnx.OnnxError):
+        onnx._infer(Op.conv2d((1, 1), (0, 0)), [[1, 3, 4, 4], [8, 3, 999, 999]])
+    with pytest.raises(onnx.OnnxError):
+        onnx._infer(Op.max_pool2d((999, 999), (1, 1), (0, 0)), [[1, 3, 4, 4]])
+
+
+def test_loader_rejects_kernel_larger_than_input():
+    # load.rs:1060-1105: a Conv whose 999 x 999 kernel exceeds its 4 x 4 input,
+    # with no declared output shape (so shape inference runs), is an invalid model
+    from tpt_infer_b200 import onnx as X
+
+    conv = (X._ld(1, "x") + X._ld(1, "w") + X._ld(2, "y") + X._ld(3, "conv") + X._ld(4, "Conv") +
+            X._attr_ints("strides", [1, 1]) + X._attr_ints("pads", [0, 0, 0, 0]) +
+            X._attr_ints("kernel_shape", [999, 999]))
+    body = (X._ld(1, conv) + X._ld(5, X._tensor_msg("w", [1, 1, 999, 999], np.zeros(999 * 999, np.float32))) +
+            X._vi(11, "x", [1, 1, 4, 4]) + X._ld(12, X._ld(1, "y")))
+    body = X._ld(2, "conv_bad") + body
+    model = X._key(1, 0) + X._enc_varint(8) + X._ld(7, body) + X._ld(8, X._ld(1, "") + X._key(2, 0) + X._enc_varint(17))
+    with pytest.raises(X.OnnxError, match="invalid model"):
+        X.load_from_bytes(model)

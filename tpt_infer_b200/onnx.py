@@ -303,6 +303,18 @@ def _bcast(a, b):
     return [max(x, y) if 1 in (x, y) else x for x, y in zip(a, b)]
 
 
+def _out_dim(inp, pad, kernel, stride):
+    """conv_out_dim (shapes.rs:199-217): (input + 2 pad - kernel) / stride + 1
+    with the stride taken as at least 1; a kernel that does not fit the padded
+    input is InvalidGeometry, which the loader reports as an invalid model
+    (load.rs:77-81)."""
+    num = inp + 2 * pad - kernel
+    if num < 0:
+        raise OnnxError("invalid model: shape inference failed: convolution/pooling kernel does not fit the "
+                        "(padded) input dimensions")
+    return num // max(stride, 1) + 1
+
+
 def _infer(op, ins):
     """Output dims of a node without a declared shape (the cases of
     crates/tpt-infer-onnx/src/shapes.rs the lowering supports); [1] otherwise."""
@@ -321,13 +333,18 @@ def _infer(op, ins):
         m = x[1] if a["trans_a"] else x[0]
         n = ins[1][0] if a["trans_b"] else ins[1][1]
         return [m, n]
-    if k == "Conv2d" and len(ins) > 1 and len(x) == 4:
+    if k == "Conv2d" and len(ins) > 1 and len(x) == 4 and len(ins[1]) == 4:
+        # conv_shape (shapes.rs:219-248): a dynamic (0) spatial dim stays 0
         w = ins[1]
         (sh, sw), (ph, pw) = a["strides"], a["padding"]
-        return [x[0], w[0], (x[2] + 2 * ph - w[2]) // sh + 1, (x[3] + 2 * pw - w[3]) // sw + 1]
+        return [x[0], w[0], 0 if x[2] == 0 else _out_dim(x[2], ph, w[2], sh),
+                0 if x[3] == 0 else _out_dim(x[3], pw, w[3], sw)]
     if k in ("MaxPool2d", "AveragePool2d") and len(x) == 4:
+        # pool_shape (shapes.rs:250-272): kernel 0 is the global pool
         (kh, kw), (sh, sw), (ph, pw) = a["kernel"], a["strides"], a["padding"]
-        return [x[0], x[1], (x[2] + 2 * ph - kh) // sh + 1, (x[3] + 2 * pw - kw) // sw + 1]
+        if kh == 0:
+            return [x[0], x[1], 1, 1]
+        return [x[0], x[1], _out_dim(x[2], ph, kh, sh), _out_dim(x[3], pw, kw, sw)]
     if k == "Flatten":
         ax = a["axis"] + len(x) if a["axis"] < 0 else a["axis"]
         return [int(np.prod(x[:ax], dtype=np.int64)), int(np.prod(x[ax:], dtype=np.int64))]
