@@ -498,3 +498,22 @@ def test_runtime_batch_norm_softmax_graph_kats():
     g.mark_output(y)
     out = graph_exec.execute_graph(g, [np.array([-1.0, 2.0, -3.0, 4.0], np.float32)])[0].ravel()
     assert abs(out.sum() - 1.0) < 1e-4 and int(np.argmax(out)) == 3 and out[0] == out[2]
+
+
+def test_lowering_graph_errors_before_device_work():
+    # exec.rs:833-846 (unmarked_graph_reports_no_outputs) and :848-864
+    # (custom_op_is_unsupported): both reported before the lowering touches a
+    # device, so no backend is needed here
+    from tpt_infer_b200 import lowering as L
+
+    g = L.ComputationGraph()
+    x = g.add_input([4], "x")
+    g.add_node(L.Operator.relu(), [x], [4])
+    with pytest.raises(L.NoOutputs):
+        L.lower(g, None)
+    g = L.ComputationGraph()
+    x = g.add_input([4], "x")
+    g.mark_output(g.add_node(L.Operator.custom("Erf"), [x], [4]))
+    with pytest.raises(L.UnsupportedOp) as e:
+        L.lower(g, None)
+    assert e.value.name == "Erf"

@@ -54,6 +54,14 @@ class UnsupportedOp(OpError):
         self.args = (f"unsupported operator {name!r} on the CUDA backend",)
 
 
+class NoOutputs(OpError):
+    """RuntimeError::NoOutputs (exec.rs:833-846): the graph marks no output."""
+
+    def __init__(self):
+        super().__init__(INVALID)
+        self.args = ("the graph has no marked output",)
+
+
 # ------------------------------------------------------------------ IR
 @dataclass
 class Operator:
@@ -267,6 +275,14 @@ def lower(graph: ComputationGraph, be, quantized=None) -> LoweredGraph:
     W^T, quant.rs:95-107), or a dict {initializer name: (q int8 [N, K], scales
     [N])} of already quantized weights in that layout.
     """
+    # graph-level errors before any device work: no marked output, and a node
+    # kind with no CUDA lowering (UnsupportedCustom for custom ops, as the
+    # reference's dispatch reports them, exec.rs:527-531)
+    if not graph.outputs:
+        raise NoOutputs()
+    for node in graph.nodes:
+        if node.op.kind not in SUPPORTED:
+            raise UnsupportedOp(node.op.name)
     p = G.Plan(be)
     tid = {}     # node id -> plan tensor id
     in_ids, in_dims = [], []
