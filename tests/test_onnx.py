@@ -144,3 +144,35 @@ def test_loader_rejects_kernel_larger_than_input():
     model = X._key(1, 0) + X._enc_varint(8) + X._ld(7, body) + X._ld(8, X._ld(1, "") + X._key(2, 0) + X._enc_varint(17))
     with pytest.raises(X.OnnxError, match="invalid model"):
         X.load_from_bytes(model)
+
+
+def _model_bytes(X, nodes, inits, ins, outs):
+    body = b"".join(X._ld(1, n) for n in nodes) + b"".join(X._ld(5, t) for t in inits)
+    body += b"".join(X._vi(11, n, d) for n, d in ins) + b"".join(X._vi(12, n, d) for n, d in outs)
+    body = X._ld(2, "g") + body
+    return X._key(1, 0) + X._enc_varint(8) + X._ld(7, body) + X._ld(8, X._ld(1, "") + X._key(2, 0) + X._enc_varint(17))
+
+
+def test_loader_limits_and_initializer_checks():
+    # load.rs tests: oversized_model_bytes_rejected, oversized_graph_item_count_rejected,
+    # negative_initializer_dim_rejected, mismatched_initializer_length_rejected
+    from tpt_infer_b200 import onnx as X
+
+    relu = X._ld(1, "x") + X._ld(2, "y") + X._ld(3, "relu0") + X._ld(4, "Relu")
+    b = _model_bytes(X, [relu], [], [("x", [1, 4])], [("y", [1, 4])])
+    assert [n.op.kind for n in X.load_from_bytes(b).nodes] == ["Input", "Relu"]
+    with pytest.raises(X.OnnxError, match="invalid model"):
+        X.load_from_bytes(b, max_bytes=len(b) - 1)
+    with pytest.raises(X.OnnxError, match="invalid model"):
+        X.load_from_bytes(b, max_graph_items=0)
+
+    def tensor(name, dims, data):  # dims as int64 varints (two's complement for negatives)
+        raw = np.ascontiguousarray(data, "<f4").tobytes()
+        return (X._ld(1, b"".join(X._enc_varint(d & (2 ** 64 - 1)) for d in dims)) + X._key(2, 0) +
+                X._enc_varint(1) + X._ld(8, name) + X._ld(9, raw))
+
+    mm = X._ld(1, "x") + X._ld(1, "w") + X._ld(2, "y") + X._ld(3, "mm0") + X._ld(4, "MatMul")
+    for dims, n in (([-4, 5], 20), ([4, 5], 3)):
+        b2 = _model_bytes(X, [mm], [tensor("w", dims, np.zeros(n, np.float32))], [("x", [1, 4])], [("y", [1, 5])])
+        with pytest.raises(X.OnnxError, match="invalid model"):
+            X.load_from_bytes(b2)
