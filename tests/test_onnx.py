@@ -176,3 +176,33 @@ def test_loader_limits_and_initializer_checks():
         b2 = _model_bytes(X, [mm], [tensor("w", dims, np.zeros(n, np.float32))], [("x", [1, 4])], [("y", [1, 5])])
         with pytest.raises(X.OnnxError, match="invalid model"):
             X.load_from_bytes(b2)
+
+
+def test_loader_same_padding_int64_reshape_and_dynamic_batch():
+    # load.rs tests: conv_auto_pad_same_upper_resolves_symmetric_padding,
+    # reshape_target_from_int64_initializer_input, dynamic_batch_zero
+    from tpt_infer_b200 import onnx as X
+
+    conv = (X._ld(1, "x") + X._ld(1, "conv_w") + X._ld(2, "c") + X._ld(3, "conv") + X._ld(4, "Conv") +
+            X._attr_ints("strides", [1, 1]) + X._attr_ints("kernel_shape", [5, 5]) +
+            X._ld(5, X._ld(1, "auto_pad") + X._ld(4, "SAME_UPPER") + X._key(20, 0) + X._enc_varint(3)))
+    g = X.load_from_bytes(_model_bytes(X, [conv], [X._tensor_msg("conv_w", [8, 1, 5, 5], np.zeros(200, np.float32))],
+                                       [("x", [1, 1, 28, 28])], [("c", [1, 8, 28, 28])]))
+    c = [n for n in g.nodes if n.op.kind == "Conv2d"][0]
+    assert tuple(c.op.attrs["padding"]) == (2, 2) and tuple(c.dims) == (1, 8, 28, 28)
+
+    rs = X._ld(1, "x") + X._ld(1, "target_shape") + X._ld(2, "y") + X._ld(3, "reshape0") + X._ld(4, "Reshape")
+    g = X.load_from_bytes(_model_bytes(X, [rs], [X._tensor_msg("target_shape", [2], np.array([1, 12], np.int64), 7)],
+                                       [("x", [1, 3, 4])], [("y", [1, 12])]))
+    r = [n for n in g.nodes if n.op.kind == "Reshape"][0]
+    assert tuple(r.op.attrs["shape"]) == (1, 12) and "target_shape" in g.initializers
+
+    def vi(f, name, dims):  # dim values as int64 varints, -1 included
+        dm = b"".join(X._ld(1, X._key(1, 0) + X._enc_varint(d & (2 ** 64 - 1))) for d in dims)
+        return X._ld(f, X._ld(1, name) + X._ld(2, X._ld(1, X._key(1, 0) + X._enc_varint(1) + X._ld(2, dm))))
+
+    relu = X._ld(1, "x") + X._ld(2, "y") + X._ld(3, "r") + X._ld(4, "Relu")
+    body = X._ld(2, "dyn") + X._ld(1, relu) + vi(11, "x", [-1, 4]) + vi(12, "y", [-1, 4])
+    model = X._key(1, 0) + X._enc_varint(8) + X._ld(7, body) + X._ld(8, X._ld(1, "") + X._key(2, 0) + X._enc_varint(17))
+    g = X.load_from_bytes(model)
+    assert [tuple(n.dims) for n in g.nodes] == [(0, 4), (0, 4)]

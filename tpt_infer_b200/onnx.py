@@ -168,7 +168,9 @@ def _node(b):
 
 
 def _value_info(b):
-    """(name, dims or None): dims of a tensor type whose every dim has a value."""
+    """(name, dims or None): the dims of a tensor type with a shape, a dim
+    without a positive value (symbolic, unset or <= 0: a dynamic dim) as 0,
+    as vi_dims does (load.rs:562-579); None without a tensor shape."""
     name, dims = "", None
     for f, _, v in _fields(b):
         if f == 1:
@@ -188,7 +190,7 @@ def _value_info(b):
                                 if f5 == 1:
                                     val = _sint64(v5)
                             ds.append(val)
-                    dims = None if any(d is None or d < 0 for d in ds) else [int(d) for d in ds]
+                    dims = [int(d) if d is not None and d > 0 else 0 for d in ds]
     return name, dims
 
 
