@@ -517,3 +517,23 @@ def test_lowering_graph_errors_before_device_work():
     with pytest.raises(L.UnsupportedOp) as e:
         L.lower(g, None)
     assert e.value.name == "Erf"
+
+
+def test_graph_rank_limit_and_idempotent_outputs():
+    # crates/tpt-infer-graph/src/graph.rs:538-542 (node_rank_too_large) and
+    # :630-636 (mark_output_idempotent); unknown nodes are rejected
+    from tpt_infer_b200 import lowering as L
+    from tpt_infer_b200.backend import OpError
+
+    g = L.ComputationGraph()
+    with pytest.raises(OpError):
+        g.add_input([1] * 9, "x")
+    x = g.add_input([1] * 8, "x")
+    r = g.add_node(L.Operator.relu(), [x], [1] * 8)
+    g.mark_output(r)
+    g.mark_output(r)
+    assert g.outputs == [r]
+    with pytest.raises(OpError):
+        g.mark_output(5)
+    with pytest.raises(OpError):
+        g.add_node(L.Operator.relu(), [7], [1])

@@ -169,6 +169,8 @@ class ComputationGraph:
 
     def add_node(self, op, inputs, dims, name=""):
         nid = len(self.nodes)
+        if len(dims) > MAX_RANK:
+            raise OpError(INVALID)  # GraphError::RankTooLarge (graph.rs:538-542)
         for i in inputs:
             if not 0 <= i < nid:
                 raise OpError(INVALID)  # GraphError: inputs must precede the node
@@ -191,9 +193,12 @@ class ComputationGraph:
         return nid
 
     def mark_output(self, nid):
+        """Marks a graph output; marking a node twice keeps one entry
+        (graph.rs:392-400)."""
         if not 0 <= nid < len(self.nodes):
             raise OpError(INVALID)
-        self.outputs.append(nid)
+        if nid not in self.outputs:
+            self.outputs.append(nid)
 
     def inputs(self):
         """Input nodes not bound to an initializer, in node order (execute_graph's binding order)."""
